@@ -1,0 +1,266 @@
+/*
+ * veda_cuda.h — the C ABI of libveda_cuda.so: hand-written sm_100a kernels for the backward path
+ * of Veda's training step (forward kernels included where the backward needs their saved state).
+ *
+ * Conventions
+ *   - Every entry point returns an int status: VEDA_OK (0) or a negative VEDA_ERR_* code; the
+ *     message of the last failure on the calling thread is veda_last_error().
+ *   - Pointers are device pointers unless stated otherwise; sizes and leading dimensions are in
+ *     ELEMENTS; matrices are row-major. `dtype` is VEDA_F32 or VEDA_BF16 and applies to every
+ *     activation-like operand of the call; parameter gradients are always fp32.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Nothing is synchronised: every
+ *     call is an asynchronous launch on `stream`.
+ *   - Token-major activations: element (b, t, h, d) of a [B, T, H, Dh] tensor lives at
+ *     ptr[(b*T + t) * ld + h*Dh + d]; `ld` lets q, k and v be column slices of one fused buffer.
+ *
+ * The reference (pictaile/veda) has no C ABI: its boundary is the C++ autograd API of
+ * src/libs/autograd/Variable.h:69-119. Each entry point names the reference function whose
+ * arithmetic it carries. The C++ host library (include/veda/*.hpp) calls these and turns status
+ * codes into the reference's exception types.
+ */
+#ifndef VEDA_CUDA_H
+#define VEDA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* veda_stream_t;
+
+enum veda_status {
+    VEDA_OK = 0,
+    VEDA_ERR_INVALID_ARGUMENT = -1, /* reference: std::invalid_argument */
+    VEDA_ERR_CUDA = -2,             /* a CUDA launch or runtime failure   */
+    VEDA_ERR_TIMEOUT = -3,          /* a bounded device wait gave up      */
+    VEDA_ERR_UNSUPPORTED = -4,      /* shape/alignment this build does not handle */
+    VEDA_ERR_OUT_OF_RANGE = -5      /* reference: std::out_of_range (ids) */
+};
+
+enum veda_dtype { VEDA_F32 = 0, VEDA_BF16 = 1 };
+
+/* ---------------------------------------------------------------------------------------- */
+/* Library                                                                                    */
+/* ---------------------------------------------------------------------------------------- */
+const char* veda_last_error(void);
+/* Number of SMs and compute capability of the current device. */
+int veda_device_info(int* sm_count, int* cc_major, int* cc_minor);
+/* Kernel launches issued by this library since load (all threads); a diagnostic counter. */
+uint64_t veda_launch_count(void);
+/* The current device's status word: 0, or VEDA_ERR_TIMEOUT if a kernel's bounded device-side
+ * wait gave up since the last reset. Synchronises with the device; reset = 1 clears it. */
+int veda_kernel_status(int reset);
+
+/* ---------------------------------------------------------------------------------------- */
+/* GEMM — the Linear / LM-head matmuls and both of their backward products.                  */
+/*   bf16 operands: tcgen05.mma (TMEM accumulator, TMA-fed shared memory), fp32 accumulate.   */
+/*   fp32 operands: fp32 FFMA kernel (exact-precision path for fp32 parity).                 */
+/* C[M,N] = alpha * op(A) op(B) + beta * C   (beta = 0: C is not read)                        */
+/* ---------------------------------------------------------------------------------------- */
+/* NT: A[M,K] (lda), B[N,K] (ldb). Linear forward y = x W^T: ops::matmul_nt
+ *     (src/libs/ops/Matmul.cpp:259-262) via autograd::matmul_nt (src/libs/autograd/Variable.cpp:325-327). */
+int veda_gemm_nt(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* B,
+                 int64_t ldb, void* C, int64_t ldc, int dtype_ab, int dtype_c, float alpha,
+                 float beta, veda_stream_t stream);
+/* NN: A[M,K] (lda), B[K,N] (ldb). Input gradient dX = dY W: ops::matmul(g, W)
+ *     (src/libs/autograd/Variable.cpp:338). */
+int veda_gemm_nn(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* B,
+                 int64_t ldb, void* C, int64_t ldc, int dtype_ab, int dtype_c, float alpha,
+                 float beta, veda_stream_t stream);
+/* TN: A[K,M] (lda), B[K,N] (ldb). Weight gradient dW = dY^T X summed over every token:
+ *     ops::matmul(transpose(g), x) + unbroadcast (src/libs/autograd/Variable.cpp:342-343, 48-87). */
+int veda_gemm_tn(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* B,
+                 int64_t ldb, void* C, int64_t ldc, int dtype_ab, int dtype_c, float alpha,
+                 float beta, veda_stream_t stream);
+/* Batched form of the three products above (op = 0 NT, 1 NN, 2 TN) with element strides between
+ * batch entries; a stride of 0 broadcasts that operand (ops::matmul's batch broadcast,
+ * src/libs/ops/Matmul.cpp:169-250). */
+int veda_gemm_batched(int op, int64_t batch, int64_t M, int64_t N, int64_t K, const void* A,
+                      int64_t lda, int64_t stride_a, const void* B, int64_t ldb, int64_t stride_b,
+                      void* C, int64_t ldc, int64_t stride_c, int dtype_ab, int dtype_c,
+                      float alpha, float beta, veda_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------- */
+/* RMSNorm with gain: y = gamma * x / sqrt(mean(x^2) + eps) over rows of n.                   */
+/*   ops::rms_normalize (src/libs/ops/Normalize.cpp:18-70) + mul by gamma (Model.cpp:242-243).*/
+/*   gamma == NULL means gain 1 (plain rms_normalize).                                       */
+/* ---------------------------------------------------------------------------------------- */
+int veda_rmsnorm_fwd(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
+                     int64_t rows, int64_t n, float eps, int dtype, veda_stream_t stream);
+/* Backward (src/libs/autograd/NonLinear.cpp:153-201 and the gain's mul/unbroadcast,
+ * Variable.cpp:218-239): dx = dresid + (G/r - x * sum(G x)/(n r^3)), G = dy * gamma;
+ * dgamma (fp32 [n], may be NULL) += sum over rows of dy * x / r. dresid may be NULL.
+ * workspace: veda_rmsnorm_bwd_workspace(rows, n) bytes of device scratch (NULL if dgamma NULL). */
+int veda_rmsnorm_bwd(const void* x, int64_t ldx, const void* gamma, const void* dy, int64_t lddy,
+                     const void* dresid, int64_t ldr, void* dx, int64_t lddx, float* dgamma,
+                     void* workspace, size_t workspace_bytes, int64_t rows, int64_t n, float eps,
+                     int dtype, veda_stream_t stream);
+size_t veda_rmsnorm_bwd_workspace(int64_t rows, int64_t n);
+
+/* ---------------------------------------------------------------------------------------- */
+/* QK-norm + RoPE, per head over head_dim (Model.cpp:171-178): y = rope(gamma * x / r).       */
+/*   x: tokens x heads x head_dim token-major (ld per token); token n sits at position        */
+/*   n % seq_len. cos/sin: fp32 [seq_len, head_dim] tables of model::rope_tables              */
+/*   (src/libs/model/Rope.cpp:17-63); rotation of autograd::rope (Views.cpp:78-134).           */
+/* ---------------------------------------------------------------------------------------- */
+int veda_qknorm_rope_fwd(const void* x, int64_t ldx, const void* gamma, const float* cos,
+                         const float* sin, void* y, int64_t ldy, int64_t tokens, int64_t heads,
+                         int64_t seq_len, int64_t head_dim, float eps, int dtype,
+                         veda_stream_t stream);
+/* Backward: rotate dy by -theta (Views.cpp:136-171), then the gain and norm backward as above.
+ * dgamma (fp32 [head_dim]) += sum over tokens and heads. */
+int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamma, const float* cos,
+                         const float* sin, const void* dy, int64_t lddy, void* dx, int64_t lddx,
+                         float* dgamma, void* workspace, size_t workspace_bytes, int64_t tokens,
+                         int64_t heads, int64_t seq_len, int64_t head_dim, float eps, int dtype,
+                         veda_stream_t stream);
+size_t veda_qknorm_rope_bwd_workspace(int64_t tokens, int64_t heads, int64_t head_dim);
+
+/* Plain RoPE on a contiguous [lanes, seq_len, head_dim] tensor (autograd::rope,
+ * src/libs/autograd/Views.cpp:78-171); inverse = 1 rotates by -theta (the backward). */
+int veda_rope(const void* x, void* y, const float* cos, const float* sin, int64_t lanes,
+              int64_t seq_len, int64_t head_dim, int inverse, int dtype, veda_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------- */
+/* SwiGLU: h = silu(gate) * up (Model.cpp:198-204; silu of Activations.cpp:13-16).            */
+/* ---------------------------------------------------------------------------------------- */
+int veda_swiglu_fwd(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* h,
+                    int64_t ldh, int64_t rows, int64_t n, int dtype, veda_stream_t stream);
+/* dgate = dh * up * s(1 + g(1 - s)), dup = dh * silu(g)   (NonLinear.cpp:47-63, Variable.cpp:218-239) */
+int veda_swiglu_bwd(const void* gate, int64_t ldg, const void* up, int64_t ldu, const void* dh,
+                    int64_t lddh, void* dgate, int64_t lddg, void* dup, int64_t lddu,
+                    int64_t rows, int64_t n, int dtype, veda_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Fused softmax cross-entropy (autograd::cross_entropy, src/libs/autograd/Loss.cpp:18-103).  */
+/*   row_loss[r] = -(x_t - max - log sum exp(x - max)) in fp32;                                */
+/*   dlogits = (softmax(x) - onehot(t)) * grad_scale (grad_scale = upstream / lanes), written  */
+/*   in dtype; dlogits may alias logits (in place). dlogits == NULL: forward only.            */
+/*   status (device int, may be NULL) receives VEDA_ERR_OUT_OF_RANGE if a target is outside  */
+/*   [0, vocab); such a row is skipped.                                                        */
+/* ---------------------------------------------------------------------------------------- */
+int veda_cross_entropy(const void* logits, int64_t ldl, const int64_t* targets, float* row_loss,
+                       void* dlogits, int64_t ldd, int64_t rows, int64_t vocab, float grad_scale,
+                       int* status, int dtype, veda_stream_t stream);
+/* out[0] = (float)(sum_i v[i] / n) with the sum in double, in a fixed order (Loss.cpp:52-60). */
+int veda_mean_f64(const float* v, int64_t n, float* out, double* out_f64, veda_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Embedding (autograd::embedding, src/libs/autograd/NonLinear.cpp:203-254).                  */
+/* ---------------------------------------------------------------------------------------- */
+/* out[p] = table[ids[p]], bit-exact. An id outside [0, vocab) writes zeros and sets *status
+ * (device int, may be NULL) to VEDA_ERR_OUT_OF_RANGE. */
+int veda_embedding_fwd(const int64_t* ids, int64_t count, const void* table, int64_t vocab,
+                       int64_t dim, void* out, int64_t ldo, int* status, int dtype,
+                       veda_stream_t stream);
+/* dtable (fp32 [vocab, dim]) += scatter of dout rows. deterministic = 1: each id's rows are
+ * added in ascending position order onto the existing value, the loop order of
+ * NonLinear.cpp:245-252, so the result equals the CPU's bit for bit given equal inputs.
+ * deterministic = 0: fp32 atomics (order unspecified). */
+int veda_embedding_bwd(const int64_t* ids, int64_t count, const void* dout, int64_t ldd,
+                       int64_t vocab, int64_t dim, float* dtable, int deterministic,
+                       void* workspace, size_t workspace_bytes, int dtype, veda_stream_t stream);
+size_t veda_embedding_bwd_workspace(int64_t count);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Global-norm clip + AdamW (optim::clip_gradient_norm, src/libs/optim/Clip.cpp:12-61;        */
+/* optim::AdamW::step, src/libs/optim/AdamW.cpp:38-93).                                        */
+/* ---------------------------------------------------------------------------------------- */
+/* *sumsq (device double) = sum of g^2 over n floats, in double, deterministic order.
+ * accumulate = 1 adds to the existing *sumsq (several tensors, one norm). */
+int veda_sumsq(const float* g, int64_t n, double* sumsq, int accumulate, void* workspace,
+               size_t workspace_bytes, veda_stream_t stream);
+size_t veda_sumsq_workspace(int64_t n);
+/* In place g *= clip scale, where total = sqrt(*sumsq) and the scale is float(max_norm/total)
+ * only when total is finite and > max_norm (otherwise nothing is written). */
+int veda_clip_apply(float* g, int64_t n, const double* sumsq, float max_norm,
+                    veda_stream_t stream);
+/* One AdamW step on fp32 master weights:
+ *   g' = g * grad_scale (skipped when grad_scale == 1) * clip (as veda_clip_apply; sumsq NULL =
+ *   no clip; sumsq is of g * grad_scale when grad_scale != 1 is folded by the caller)
+ *   m = b1 m + (1-b1) g';  v = b2 v + (1-b2) g'^2  (fp32, unfused roundings as the reference)
+ *   w -= lr*wd*w;  w -= lr * float((m/bias1) / (sqrt(v/bias2) + eps))  (m_hat, v_hat in double)
+ * bias1 = 1 - beta1^t, bias2 = 1 - beta2^t computed by the caller in double.
+ * lowp (bf16 [n], may be NULL) receives the rounded copy the forward reads.
+ * write_grad = 1 stores g' back into g (the clipped gradient, as Clip.cpp:52-58 leaves it). */
+int veda_adamw_step(float* master, float* m, float* v, float* g, void* lowp, int64_t n, float lr,
+                    float beta1, float beta2, float eps, float weight_decay, double bias1,
+                    double bias2, const double* sumsq, float max_norm, float grad_scale,
+                    int write_grad, veda_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Element-wise and per-lane ops of the fine-grained autograd API.                           */
+/* ---------------------------------------------------------------------------------------- */
+/* out = a (+|*) b with numpy broadcasting expressed by strides (0 = broadcast axis), rank <= 8.
+ * op: 0 add (ops::add, src/libs/ops/Elementwise.cpp:24-49), 1 mul (ops::mul). */
+int veda_binary(int op, const void* a, const int64_t* a_strides, const void* b,
+                const int64_t* b_strides, void* out, const int64_t* shape, int rank, int dtype,
+                veda_stream_t stream);
+/* out = x * s (ops::mul by a scalar). */
+int veda_scale(const void* x, float s, void* out, int64_t n, int dtype, veda_stream_t stream);
+/* dst += src, element-wise over n (detail accumulate, Variable.cpp:27-38); dst in dtype_dst. */
+int veda_accumulate(void* dst, int dtype_dst, const void* src, int dtype_src, int64_t n,
+                    veda_stream_t stream);
+/* Copy a strided view of rank <= 8 into a contiguous tensor (core::contiguous,
+ * src/libs/tensor/Tensor.cpp:157-191); dtype conversion allowed. */
+int veda_copy_strided(const void* src, int dtype_src, const int64_t* src_strides, int64_t offset,
+                      void* dst, int dtype_dst, const int64_t* shape, int rank,
+                      veda_stream_t stream);
+/* Sum a contiguous gradient over broadcast axes down to `target` (detail::unbroadcast,
+ * Variable.cpp:48-87). shape/target are aligned to `rank` (target axes of extent 1 or
+ * leading axes absent from the target collapse). out is contiguous fp32 or dtype. */
+int veda_unbroadcast(const void* g, const int64_t* shape, const int64_t* target, int rank,
+                     void* out, int dtype, veda_stream_t stream);
+/* out[0] = sum of x (autograd::sum, Variable.cpp:260-287), fp32 result, double accumulation. */
+int veda_sum(const void* x, int64_t n, float* out, int dtype, veda_stream_t stream);
+/* Fill n elements with a value. */
+int veda_fill(void* x, float value, int64_t n, int dtype, veda_stream_t stream);
+/* softmax over the last dim of [lanes, length] (ops::softmax, src/libs/ops/Softmax.cpp:20-80)
+ * and its backward y * (g - sum(g y)) (NonLinear.cpp:89-151). */
+int veda_softmax_fwd(const void* x, void* y, int64_t lanes, int64_t length, int dtype,
+                     veda_stream_t stream);
+int veda_softmax_bwd(const void* y, const void* g, void* dx, int64_t lanes, int64_t length,
+                     int dtype, veda_stream_t stream);
+/* silu and its backward on n elements (Activations.cpp:13-16, NonLinear.cpp:47-63). */
+int veda_silu_fwd(const void* x, void* y, int64_t n, int dtype, veda_stream_t stream);
+int veda_silu_bwd(const void* x, const void* g, void* dx, int64_t n, int dtype,
+                  veda_stream_t stream);
+/* Row argmax over [rows, n], ties to the lower index, NaN -> *status = VEDA_ERR_INVALID_ARGUMENT
+ * (generate::greedy_of, src/libs/generate/Sampling.cpp:97-113). */
+int veda_argmax(const void* x, int64_t ld, int64_t rows, int64_t n, int64_t* out, int* status,
+                int dtype, veda_stream_t stream);
+/* Seeded N(0, std) fill (counter-based hash + Box-Muller) for synthetic weights. */
+int veda_randn(void* x, int64_t n, float std, uint64_t seed, int dtype, veda_stream_t stream);
+/* fp32 -> bf16 rounding copy (round to nearest even). */
+int veda_f32_to_bf16(const float* src, void* dst, int64_t n, veda_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Causal GQA attention (the composition of src/libs/train/Model.cpp:182-189:                 */
+/* softmax(q k^T * scale + mask) v, KV head of query head h = h / (H/Hkv),                    */
+/* src/libs/model/Attention.cpp:191).                                                          */
+/*   q, o: [B, T, H, Dh] token-major; k, v: [B, T, Hkv, Dh]; lse: fp32 [B, H, T] saved for    */
+/*   the backward (log-sum-exp of the scaled, masked scores).                                 */
+/* ---------------------------------------------------------------------------------------- */
+int veda_attention_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                       int64_t ldv, void* o, int64_t ldo, float* lse, int64_t batch,
+                       int64_t seq_len, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                       float scale, int causal, int dtype, veda_stream_t stream);
+/* Recomputes P from lse; dq, dk, dv written (not accumulated) in dtype; dk/dv are summed over
+ * the H/Hkv query heads of each group (the unbroadcast of the KV expansion).
+ * workspace: veda_attention_bwd_workspace() bytes. */
+int veda_attention_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                       int64_t ldv, const void* o, int64_t ldo, const void* dout, int64_t lddo,
+                       const float* lse, void* dq, int64_t lddq, void* dk, int64_t lddk, void* dv,
+                       int64_t lddv, void* workspace, size_t workspace_bytes, int64_t batch,
+                       int64_t seq_len, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                       float scale, int causal, int dtype, veda_stream_t stream);
+size_t veda_attention_bwd_workspace(int64_t batch, int64_t seq_len, int64_t heads,
+                                    int64_t kv_heads, int64_t head_dim, int dtype);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VEDA_CUDA_H */

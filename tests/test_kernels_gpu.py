@@ -1,0 +1,525 @@
+"""Parity of every kernel behind include/veda_cuda.h with the oracle, through the C ABI.
+
+Tolerances (max-abs-relative error per tensor): 1e-4 for fp32, 2e-2 for bf16; integer and index
+work (gathers, deterministic scatter, argmax) and the AdamW update on equal gradients are
+compared bit for bit."""
+import math
+
+import numpy as np
+import pytest
+
+import veda_b200 as V
+from oracle import veda_oracle as O
+from tests.gpu_util import (bf, call, dev, empty, host, ptr, rel, stream, sync, workspace,
+                            zeros)
+
+pytestmark = pytest.mark.gpu
+F32 = np.float32
+TOL = {V.F32: 1e-4, V.BF16: 2e-2}
+
+
+@pytest.fixture(autouse=True)
+def _lib(cuda):
+    yield
+
+
+def rng(seed):
+    return np.random.default_rng(seed)
+
+
+# ---------------------------------------------------------------------------------------------
+# RMSNorm
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype,rows,n", [(V.F32, 128, 64), (V.F32, 37, 100), (V.BF16, 8192, 1024),
+                                          (V.BF16, 33, 2048), (V.F32, 8192, 1024)])
+def test_rmsnorm_fwd_bwd(dtype, rows, n):
+    r = rng(rows + n)
+    x = r.standard_normal((rows, n)).astype(F32)
+    gam = (1 + 0.1 * r.standard_normal(n)).astype(F32)
+    g = r.standard_normal((rows, n)).astype(F32)
+    res = r.standard_normal((rows, n)).astype(F32)
+    if dtype == V.BF16:
+        x, gam, g, res = bf(x), bf(gam), bf(g), bf(res)
+    y_ref, _, _ = O.rms_norm_gamma(x, gam, 1e-6)
+    dx_ref, dgam_ref = O.rms_norm_gamma_backward(x, gam, g, 1e-6)
+    dx_ref = dx_ref + res
+    dx_, gam_, g_, res_ = dev(x, dtype), dev(gam, dtype), dev(g, dtype), dev(res, dtype)
+    y = empty((rows, n), dtype)
+    call("veda_rmsnorm_fwd", ptr(dx_), n, ptr(gam_), ptr(y), n, rows, n, 1e-6, dtype, stream())
+    dx = empty((rows, n), dtype)
+    dgam = dev(np.full(n, 0.5, F32))   # accumulates onto an existing gradient
+    ws = workspace(V.lib().veda_rmsnorm_bwd_workspace(rows, n))
+    call("veda_rmsnorm_bwd", ptr(dx_), n, ptr(gam_), ptr(g_), n, ptr(res_), n, ptr(dx), n,
+         ptr(dgam), ptr(ws), ws.numel(), rows, n, 1e-6, dtype, stream())
+    sync()
+    assert rel(host(y), y_ref) <= TOL[dtype]
+    assert rel(host(dx), dx_ref) <= TOL[dtype]
+    assert rel(host(dgam), dgam_ref + 0.5) <= (1e-4 if dtype == V.F32 else 1e-3)
+
+
+def test_rmsnorm_plain_matches_golden():
+    from pathlib import Path
+    ops = np.load(Path(__file__).parent / "golden" / "ops_small.npz")
+    x, gam, g = ops["rms_x"], ops["rms_gamma"], ops["rms_g"]
+    rows, n = x.shape
+    y = empty((rows, n))
+    dx = empty((rows, n))
+    dgam = zeros(n)
+    xd, gd, gg = dev(x), dev(gam), dev(g)
+    call("veda_rmsnorm_fwd", ptr(xd), n, ptr(gd), ptr(y), n, rows, n, 1e-6, V.F32, stream())
+    ws = workspace(V.lib().veda_rmsnorm_bwd_workspace(rows, n))
+    call("veda_rmsnorm_bwd", ptr(xd), n, ptr(gd), ptr(gg), n, None, 0, ptr(dx), n, ptr(dgam),
+         ptr(ws), ws.numel(), rows, n, 1e-6, V.F32, stream())
+    sync()
+    assert rel(host(y), ops["rms_y"]) <= 1e-6
+    assert rel(host(dx), ops["rms_dx"]) <= 1e-5
+    assert rel(host(dgam), ops["rms_dgamma"]) <= 1e-5
+
+
+# ---------------------------------------------------------------------------------------------
+# QK-norm + RoPE
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype,B,T,H,Dh,theta", [(V.F32, 4, 32, 4, 16, 1e4),
+                                                 (V.BF16, 2, 256, 16, 128, 1e6),
+                                                 (V.F32, 1, 64, 8, 128, 1e6)])
+def test_qknorm_rope(dtype, B, T, H, Dh, theta):
+    r = rng(T + H)
+    N = B * T
+    ld = H * Dh + 8 * 3  # a column slice of a wider fused buffer
+    buf = r.standard_normal((N, ld)).astype(F32)
+    if dtype == V.BF16:
+        buf = bf(buf)
+    gam = (1 + 0.1 * r.standard_normal(Dh)).astype(F32)
+    if dtype == V.BF16:
+        gam = bf(gam)
+    g = r.standard_normal((N, H * Dh)).astype(F32)
+    if dtype == V.BF16:
+        g = bf(g)
+    x = buf[:, 8:8 + H * Dh]
+    cos, sin = O.rope_tables(T, Dh, theta)
+    xh = x.reshape(B, T, H, Dh).transpose(0, 2, 1, 3)
+    gh = g.reshape(B, T, H, Dh).transpose(0, 2, 1, 3)
+    yn, _, _ = O.rms_norm_gamma(xh, gam, 1e-6)
+    y_ref = O.rope(yn, cos, sin).transpose(0, 2, 1, 3).reshape(N, H * Dh)
+    dyn = O.rope_backward(gh, cos, sin)
+    dx_ref, dgam_ref = O.rms_norm_gamma_backward(xh, gam, dyn, 1e-6)
+    dx_ref = dx_ref.transpose(0, 2, 1, 3).reshape(N, H * Dh)
+    bufd = dev(buf, dtype)
+    base = bufd.data_ptr() + 8 * (2 if dtype == V.BF16 else 4)
+    gamd, gd = dev(gam, dtype), dev(g, dtype)
+    cd, sd = dev(cos), dev(sin)
+    y = empty((N, H * Dh), dtype)
+    call("veda_qknorm_rope_fwd", base, ld, ptr(gamd), ptr(cd), ptr(sd), ptr(y), H * Dh, N, H, T,
+         Dh, 1e-6, dtype, stream())
+    dx = empty((N, H * Dh), dtype)
+    dgam = zeros(Dh)
+    ws = workspace(V.lib().veda_qknorm_rope_bwd_workspace(N, H, Dh))
+    call("veda_qknorm_rope_bwd", base, ld, ptr(gamd), ptr(cd), ptr(sd), ptr(gd), H * Dh, ptr(dx),
+         H * Dh, ptr(dgam), ptr(ws), ws.numel(), N, H, T, Dh, 1e-6, dtype, stream())
+    sync()
+    assert rel(host(y), y_ref) <= TOL[dtype]
+    assert rel(host(dx), dx_ref) <= TOL[dtype]
+    assert rel(host(dgam), dgam_ref) <= (1e-4 if dtype == V.F32 else 1e-3)
+
+
+def test_rope_plain_matches_golden():
+    from pathlib import Path
+    ops = np.load(Path(__file__).parent / "golden" / "ops_small.npz")
+    x, g = ops["rope_x"], ops["rope_g"]
+    lanes, T, Dh = x.shape
+    cd, sd = dev(ops["rope_cos"]), dev(ops["rope_sin"])
+    y, dx = empty(x.shape), empty(x.shape)
+    call("veda_rope", ptr(dev(x)), ptr(y), ptr(cd), ptr(sd), lanes, T, Dh, 0, V.F32, stream())
+    call("veda_rope", ptr(dev(g)), ptr(dx), ptr(cd), ptr(sd), lanes, T, Dh, 1, V.F32, stream())
+    sync()
+    assert rel(host(y), ops["rope_y"]) <= 1e-6
+    assert rel(host(dx), ops["rope_dx"]) <= 1e-6
+
+
+# ---------------------------------------------------------------------------------------------
+# SwiGLU
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype,rows,F", [(V.F32, 128, 192), (V.BF16, 4096, 3072), (V.F32, 7, 13)])
+def test_swiglu(dtype, rows, F):
+    r = rng(F)
+    gu = (2 * r.standard_normal((rows, 2 * F))).astype(F32)
+    dh = r.standard_normal((rows, F)).astype(F32)
+    if dtype == V.BF16:
+        gu, dh = bf(gu), bf(dh)
+    gate, up = gu[:, :F], gu[:, F:]
+    h_ref = O.swiglu(gate, up)
+    dg_ref, du_ref = O.swiglu_backward(gate, up, dh)
+    gud, dhd = dev(gu, dtype), dev(dh, dtype)
+    es = 2 if dtype == V.BF16 else 4
+    h = empty((rows, F), dtype)
+    call("veda_swiglu_fwd", ptr(gud), 2 * F, gud.data_ptr() + F * es, 2 * F, ptr(h), F, rows, F,
+         dtype, stream())
+    dgu = empty((rows, 2 * F), dtype)
+    call("veda_swiglu_bwd", ptr(gud), 2 * F, gud.data_ptr() + F * es, 2 * F, ptr(dhd), F,
+         ptr(dgu), 2 * F, dgu.data_ptr() + F * es, 2 * F, rows, F, dtype, stream())
+    sync()
+    out = host(dgu)
+    assert rel(host(h), h_ref) <= TOL[dtype]
+    assert rel(out[:, :F], dg_ref) <= TOL[dtype]
+    assert rel(out[:, F:], du_ref) <= TOL[dtype]
+
+
+# ---------------------------------------------------------------------------------------------
+# Cross-entropy
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype,rows,Vv", [(V.F32, 128, 512), (V.F32, 9, 77), (V.BF16, 64, 151936),
+                                           (V.F32, 16, 151936)])
+def test_cross_entropy(dtype, rows, Vv):
+    r = rng(rows * 7 + Vv)
+    lg = (3 * r.standard_normal((rows, Vv))).astype(F32)
+    if dtype == V.BF16:
+        lg = bf(lg)
+    t = r.integers(0, Vv, rows).astype(np.int64)
+    loss_ref, d_ref = O.cross_entropy(lg, t)
+    rows_ref = O.cross_entropy_rows(lg, t)
+    lgd, td = dev(lg, dtype), dev(t)
+    row_loss = empty(rows)
+    d = lgd.clone()   # in place over a copy of the logits
+    status = zeros(1).int()
+    call("veda_cross_entropy", ptr(lgd), Vv, ptr(td), ptr(row_loss), ptr(d), Vv, rows, Vv,
+         1.0 / rows, ptr(status), dtype, stream())
+    mean = empty(1)
+    call("veda_mean_f64", ptr(row_loss), rows, ptr(mean), None, stream())
+    sync()
+    assert int(host(status)[0]) == 0
+    assert rel(host(row_loss), rows_ref) <= 1e-5
+    assert abs(float(host(mean)[0]) - loss_ref) <= 1e-5 * abs(loss_ref)
+    assert rel(host(d), d_ref) <= TOL[dtype]
+
+
+def test_cross_entropy_golden_and_out_of_range():
+    from pathlib import Path
+    ops = np.load(Path(__file__).parent / "golden" / "ops_small.npz")
+    lg, t = ops["ce_logits"], ops["ce_targets"]
+    rows, Vv = lg.shape
+    lgd, td = dev(lg), dev(t)
+    row_loss, d, mean = empty(rows), empty((rows, Vv)), empty(1)
+    status = zeros(1).int()
+    call("veda_cross_entropy", ptr(lgd), Vv, ptr(td), ptr(row_loss), ptr(d), Vv, rows, Vv,
+         1.0 / rows, ptr(status), V.F32, stream())
+    call("veda_mean_f64", ptr(row_loss), rows, ptr(mean), None, stream())
+    sync()
+    assert abs(float(host(mean)[0]) - float(ops["ce_loss"][0])) <= 1e-6
+    assert rel(host(d), ops["ce_dlogits"]) <= 1e-6
+    bad = t.copy()
+    bad[3] = Vv
+    call("veda_cross_entropy", ptr(lgd), Vv, ptr(dev(bad)), ptr(row_loss), ptr(d), Vv, rows, Vv,
+         1.0, ptr(status), V.F32, stream())
+    sync()
+    assert int(host(status)[0]) == V.ERR_OUT_OF_RANGE
+
+
+# ---------------------------------------------------------------------------------------------
+# Embedding
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype,count,Vv,D", [(V.F32, 128, 512, 64), (V.BF16, 8192, 151936, 1024),
+                                              (V.F32, 20000, 300, 24)])
+def test_embedding(dtype, count, Vv, D):
+    r = rng(count + D)
+    table = r.standard_normal((Vv, D)).astype(F32)
+    if dtype == V.BF16:
+        table = bf(table)
+    ids = r.integers(0, min(Vv, max(8, count // 4)), count).astype(np.int64)  # many repeats
+    g = r.standard_normal((count, D)).astype(F32)
+    if dtype == V.BF16:
+        g = bf(g)
+    start = r.standard_normal((Vv, D)).astype(F32)   # e.g. the tied LM-head contribution
+    out_ref = O.embedding(table, ids)
+    dt_ref = O.embedding_backward(start.copy(), ids, g)
+    tabd, idd, gd = dev(table, dtype), dev(ids), dev(g, dtype)
+    out = empty((count, D), dtype)
+    status = zeros(1).int()
+    call("veda_embedding_fwd", ptr(idd), count, ptr(tabd), Vv, D, ptr(out), D, ptr(status), dtype,
+         stream())
+    dt = dev(start)
+    ws = workspace(V.lib().veda_embedding_bwd_workspace(count))
+    call("veda_embedding_bwd", ptr(idd), count, ptr(gd), D, Vv, D, ptr(dt), 1, ptr(ws), ws.numel(),
+         dtype, stream())
+    dta = dev(start)
+    call("veda_embedding_bwd", ptr(idd), count, ptr(gd), D, Vv, D, ptr(dta), 0, None, 0, dtype,
+         stream())
+    sync()
+    assert np.array_equal(host(out), out_ref), "gather must be bit-exact"
+    assert np.array_equal(host(dt), dt_ref), "deterministic scatter must be bit-exact"
+    assert rel(host(dta), dt_ref) <= 1e-5
+    assert int(host(status)[0]) == 0
+    call("veda_embedding_fwd", ptr(dev(np.array([0, Vv], np.int64))), 2, ptr(tabd), Vv, D,
+         ptr(out), D, ptr(status), dtype, stream())
+    sync()
+    assert int(host(status)[0]) == V.ERR_OUT_OF_RANGE
+
+
+# ---------------------------------------------------------------------------------------------
+# Clip + AdamW
+# ---------------------------------------------------------------------------------------------
+def test_clip_kat_thirteen():
+    g = dev(np.array([3.0, 4.0, 12.0], F32))
+    ss = zeros(1).double()
+    ws = workspace(V.lib().veda_sumsq_workspace(3))
+    call("veda_sumsq", ptr(g), 3, ptr(ss), 0, ptr(ws), ws.numel(), stream())
+    call("veda_clip_apply", ptr(g), 3, ptr(ss), 6.5, stream())
+    sync()
+    assert abs(math.sqrt(float(host(ss)[0])) - 13.0) < 1e-9
+    np.testing.assert_allclose(host(g), [1.5, 2.0, 6.0], atol=1e-6)
+    g2 = dev(np.array([3.0, 4.0, 12.0], F32))
+    call("veda_sumsq", ptr(g2), 3, ptr(ss), 0, ptr(ws), ws.numel(), stream())
+    call("veda_clip_apply", ptr(g2), 3, ptr(ss), 13.0, stream())
+    sync()
+    assert np.array_equal(host(g2), np.array([3.0, 4.0, 12.0], F32)), "no-op must be bitwise"
+
+
+@pytest.mark.parametrize("n,clip", [(1000003, 1.0), (4096, 1e9)])
+def test_adamw_bit_exact_with_clip(n, clip):
+    r = rng(n)
+    w = r.standard_normal(n).astype(F32)
+    grads = [(r.standard_normal(n) * 0.01).astype(F32) for _ in range(3)]
+    cfg = O.AdamWConfig(1e-3, 0.9, 0.95, 1e-8, 0.1)
+    ref_w = w.copy()
+    opt = O.AdamW([ref_w], cfg)
+    wd, md, vd = dev(w), zeros(n), zeros(n)
+    lowp = empty(n, V.BF16)
+    ss = zeros(1).double()
+    ws = workspace(V.lib().veda_sumsq_workspace(n))
+    for s, g in enumerate(grads, start=1):
+        gc = [g.copy()]
+        O.clip_gradient_norm(gc, clip)
+        opt.step(gc)
+        gd = dev(g)
+        call("veda_sumsq", ptr(gd), n, ptr(ss), 0, ptr(ws), ws.numel(), stream())
+        b1 = 1.0 - math.pow(float(F32(0.9)), s)
+        b2 = 1.0 - math.pow(float(F32(0.95)), s)
+        call("veda_adamw_step", ptr(wd), ptr(md), ptr(vd), ptr(gd), ptr(lowp), n, 1e-3, 0.9, 0.95,
+             1e-8, 0.1, b1, b2, ptr(ss), clip, 1.0, 1, stream())
+        sync()
+        assert np.array_equal(host(gd), gc[0]), "clipped gradient must equal the CPU's"
+    assert np.array_equal(host(wd), ref_w), "AdamW on equal gradients must be bit-exact"
+    assert np.array_equal(host(lowp), bf(ref_w))
+
+
+def test_adamw_kat_point_nine():
+    w, m, v, g = dev(np.array([1.0], F32)), zeros(1), zeros(1), dev(np.array([2.0], F32))
+    call("veda_adamw_step", ptr(w), ptr(m), ptr(v), ptr(g), None, 1, 0.1, 0.9, 0.999, 1e-8, 0.0,
+         1 - 0.9, 1 - 0.999, None, 1.0, 1.0, 0, stream())
+    sync()
+    assert abs(float(host(w)[0]) - 0.9) < 1e-5
+
+
+# ---------------------------------------------------------------------------------------------
+# GEMM
+# ---------------------------------------------------------------------------------------------
+def _gemm_case(op, M, N, K, dtype_c, seed, beta=0.0):
+    r = rng(seed)
+    a = bf(r.standard_normal((K, M) if op == "tn" else (M, K)).astype(F32) / math.sqrt(K))
+    b = bf(r.standard_normal((N, K) if op == "nt" else (K, N)).astype(F32))
+    c0 = r.standard_normal((M, N)).astype(F32)
+    am = a.T if op == "tn" else a
+    bm = b.T if op == "nt" else b
+    ref = (am.astype(np.float64) @ bm.astype(np.float64)).astype(F32)
+    if beta != 0.0:
+        ref = ref + beta * (bf(c0) if dtype_c == V.BF16 else c0)
+    ad, bd = dev(a, V.BF16), dev(b, V.BF16)
+    c = dev(c0, dtype_c)
+    lda = a.shape[1]
+    ldb = b.shape[1]
+    call(f"veda_gemm_{op}", M, N, K, ptr(ad), lda, ptr(bd), ldb, ptr(c), N, V.BF16, dtype_c, 1.0,
+         beta, stream())
+    sync()
+    return host(c), ref
+
+
+@pytest.mark.parametrize("op", ["nt", "nn", "tn"])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 1024), (300, 200, 136),
+                                   (4096, 1024, 1024), (128, 128, 8192)])
+def test_gemm_bf16_fp32_out(op, M, N, K):
+    c, ref = _gemm_case(op, M, N, K, V.F32, M + N + K)
+    assert rel(c, ref) <= 1e-5, rel(c, ref)
+
+
+@pytest.mark.parametrize("op", ["nt", "nn", "tn"])
+def test_gemm_bf16_out_and_accumulate(op):
+    c, ref = _gemm_case(op, 512, 768, 320, V.BF16, 5)
+    assert rel(c, ref) <= 1e-2
+    c, ref = _gemm_case(op, 1024, 1024, 4096, V.F32, 6, beta=1.0)   # split-K path + accumulate
+    assert rel(c, ref) <= 1e-5
+
+
+def test_gemm_fp32_is_bit_exact_with_reference_loop(ref_lib):
+    r = rng(9)
+    a = r.standard_normal((70, 45)).astype(F32)
+    b = r.standard_normal((33, 45)).astype(F32)
+    want = ref_lib.gemm_nt(a, b)
+    c = empty((70, 33))
+    call("veda_gemm_nt", 70, 33, 45, ptr(dev(a)), 45, ptr(dev(b)), 45, ptr(c), 33, V.F32, V.F32,
+         1.0, 0.0, stream())
+    sync()
+    assert np.array_equal(host(c), want)
+
+
+@pytest.mark.parametrize("op", ["nt", "nn", "tn"])
+def test_gemm_fp32_small_shapes(op):
+    r = rng(3)
+    M, N, K = 96, 40, 17
+    a = r.standard_normal((K, M) if op == "tn" else (M, K)).astype(F32)
+    b = r.standard_normal((N, K) if op == "nt" else (K, N)).astype(F32)
+    am = a.T if op == "tn" else a
+    bm = b.T if op == "nt" else b
+    c = empty((M, N))
+    call(f"veda_gemm_{op}", M, N, K, ptr(dev(a)), a.shape[1], ptr(dev(b)), b.shape[1], ptr(c), N,
+         V.F32, V.F32, 1.0, 0.0, stream())
+    sync()
+    assert rel(host(c), am @ bm) <= 1e-6
+
+
+# ---------------------------------------------------------------------------------------------
+# Attention
+# ---------------------------------------------------------------------------------------------
+def _attention_case(dtype, B, T, H, Hk, Dh, seed):
+    r = rng(seed)
+    q = r.standard_normal((B, H, T, Dh)).astype(F32)
+    k = r.standard_normal((B, Hk, T, Dh)).astype(F32)
+    v = r.standard_normal((B, Hk, T, Dh)).astype(F32)
+    do = r.standard_normal((B, H, T, Dh)).astype(F32)
+    if dtype == V.BF16:
+        q, k, v, do = bf(q), bf(k), bf(v), bf(do)
+    o_ref, lse_ref, p = O.attention(q, k, v)
+    dq_ref, dk_ref, dv_ref = O.attention_backward(q, k, v, p, do)
+    tok = lambda a: np.ascontiguousarray(a.transpose(0, 2, 1, 3)).reshape(B * T, -1)  # noqa: E731
+    qd, kd, vd, dod = dev(tok(q), dtype), dev(tok(k), dtype), dev(tok(v), dtype), dev(tok(do), dtype)
+    o = empty((B * T, H * Dh), dtype)
+    lse = empty(B * H * T)
+    scale = 1.0 / math.sqrt(Dh)
+    call("veda_attention_fwd", ptr(qd), H * Dh, ptr(kd), Hk * Dh, ptr(vd), Hk * Dh, ptr(o), H * Dh,
+         ptr(lse), B, T, H, Hk, Dh, scale, 1, dtype, stream())
+    # the backward runs on the reference's O (rounded like ours would be) to isolate its error
+    od = dev(tok(o_ref), dtype)
+    dq, dk, dv = empty((B * T, H * Dh), dtype), empty((B * T, Hk * Dh), dtype), empty((B * T, Hk * Dh), dtype)
+    ws = workspace(V.lib().veda_attention_bwd_workspace(B, T, H, Hk, Dh, dtype))
+    call("veda_attention_bwd", ptr(qd), H * Dh, ptr(kd), Hk * Dh, ptr(vd), Hk * Dh, ptr(od), H * Dh,
+         ptr(dod), H * Dh, ptr(lse), ptr(dq), H * Dh, ptr(dk), Hk * Dh, ptr(dv), Hk * Dh, ptr(ws),
+         ws.numel(), B, T, H, Hk, Dh, scale, 1, dtype, stream())
+    sync()
+    return (host(o), tok(o_ref), host(lse).reshape(B, H, T), lse_ref, host(dq), tok(dq_ref),
+            host(dk), tok(dk_ref), host(dv), tok(dv_ref))
+
+
+@pytest.mark.parametrize("dtype,B,T,H,Hk,Dh", [(V.F32, 4, 32, 4, 2, 16), (V.F32, 2, 70, 4, 1, 64),
+                                              (V.BF16, 2, 256, 16, 8, 128),
+                                              (V.BF16, 1, 200, 4, 2, 128)])
+def test_attention(dtype, B, T, H, Hk, Dh):
+    o, o_ref, lse, lse_ref, dq, dq_ref, dk, dk_ref, dv, dv_ref = _attention_case(
+        dtype, B, T, H, Hk, Dh, T + Dh)
+    tol = TOL[dtype]
+    assert rel(o, o_ref) <= tol
+    assert rel(lse, lse_ref) <= (1e-5 if dtype == V.F32 else 1e-3)
+    assert rel(dq, dq_ref) <= tol
+    assert rel(dk, dk_ref) <= tol
+    assert rel(dv, dv_ref) <= tol
+
+
+def test_attention_golden():
+    from pathlib import Path
+    ops = np.load(Path(__file__).parent / "golden" / "ops_small.npz")
+    q, k, v, g = ops["att_q"], ops["att_k"], ops["att_v"], ops["att_g"]
+    B, H, T, Dh = q.shape
+    Hk = k.shape[1]
+    tok = lambda a: np.ascontiguousarray(a.transpose(0, 2, 1, 3)).reshape(B * T, -1)  # noqa: E731
+    qd, kd, vd, gd = dev(tok(q)), dev(tok(k)), dev(tok(v)), dev(tok(g))
+    o, lse = empty((B * T, H * Dh)), empty(B * H * T)
+    call("veda_attention_fwd", ptr(qd), H * Dh, ptr(kd), Hk * Dh, ptr(vd), Hk * Dh, ptr(o), H * Dh,
+         ptr(lse), B, T, H, Hk, Dh, 0.25, 1, V.F32, stream())
+    dq, dk, dv = empty((B * T, H * Dh)), empty((B * T, Hk * Dh)), empty((B * T, Hk * Dh))
+    ws = workspace(V.lib().veda_attention_bwd_workspace(B, T, H, Hk, Dh, V.F32))
+    call("veda_attention_bwd", ptr(qd), H * Dh, ptr(kd), Hk * Dh, ptr(vd), Hk * Dh, ptr(o), H * Dh,
+         ptr(gd), H * Dh, ptr(lse), ptr(dq), H * Dh, ptr(dk), Hk * Dh, ptr(dv), Hk * Dh, ptr(ws),
+         ws.numel(), B, T, H, Hk, Dh, 0.25, 1, V.F32, stream())
+    sync()
+    assert rel(host(o), tok(ops["att_o"])) <= 1e-5
+    assert rel(host(dq), tok(ops["att_dq"])) <= 1e-5
+    assert rel(host(dk), tok(ops["att_dk"])) <= 1e-5
+    assert rel(host(dv), tok(ops["att_dv"])) <= 1e-5
+
+
+# ---------------------------------------------------------------------------------------------
+# Element-wise ops of the fine-grained API
+# ---------------------------------------------------------------------------------------------
+def test_binary_broadcast_and_unbroadcast():
+    r = rng(21)
+    a = r.standard_normal((3, 4, 5)).astype(F32)
+    b = r.standard_normal((5,)).astype(F32)
+    shape = np.array([3, 4, 5], np.int64)
+    sa = np.array([20, 5, 1], np.int64)
+    sb = np.array([0, 0, 1], np.int64)
+    out = empty((3, 4, 5))
+    for op, ref in ((0, a + b), (1, a * b)):
+        call("veda_binary", op, ptr(dev(a)), sa.ctypes.data, ptr(dev(b)), sb.ctypes.data, ptr(out),
+             shape.ctypes.data, 3, V.F32, stream())
+        sync()
+        assert np.array_equal(host(out), ref.astype(F32))
+    g = r.standard_normal((3, 4, 5)).astype(F32)
+    red = empty((1, 4, 1))
+    tgt = np.array([1, 4, 1], np.int64)
+    call("veda_unbroadcast", ptr(dev(g)), shape.ctypes.data, tgt.ctypes.data, 3, ptr(red), V.F32,
+         stream())
+    sync()
+    assert rel(host(red).ravel(), g.sum(axis=(0, 2))) <= 1e-6
+
+
+def test_softmax_silu_sum_copy():
+    from pathlib import Path
+    ops = np.load(Path(__file__).parent / "golden" / "ops_small.npz")
+    x, g = ops["softmax_x"], ops["softmax_g"]
+    lanes, n = x.shape
+    y, dx = empty(x.shape), empty(x.shape)
+    yd = dev(x)
+    call("veda_softmax_fwd", ptr(yd), ptr(y), lanes, n, V.F32, stream())
+    call("veda_softmax_bwd", ptr(y), ptr(dev(g)), ptr(dx), lanes, n, V.F32, stream())
+    sync()
+    assert rel(host(y), ops["softmax_y"]) <= 1e-6
+    assert rel(host(dx), ops["softmax_dx"]) <= 1e-5
+    xs = np.array([0.0, 1.0, -1.0], F32)
+    d = empty(3)
+    call("veda_silu_bwd", ptr(dev(xs)), ptr(dev(np.ones(3, F32))), ptr(d), 3, V.F32, stream())
+    s = empty(1)
+    call("veda_sum", ptr(dev(np.arange(10, dtype=F32))), 10, ptr(s), V.F32, stream())
+    m = np.arange(12, dtype=F32).reshape(3, 4)
+    t = empty((4, 3))
+    shape = np.array([4, 3], np.int64)
+    strides = np.array([1, 4], np.int64)
+    call("veda_copy_strided", ptr(dev(m)), V.F32, strides.ctypes.data, 0, ptr(t), V.F32,
+         shape.ctypes.data, 2, stream())
+    sync()
+    np.testing.assert_allclose(host(d), [0.5, 0.9277, 0.0723], atol=1e-3)
+    assert float(host(s)[0]) == 45.0
+    assert np.array_equal(host(t), m.T)
+
+
+def test_argmax_ties_and_nan():
+    x = np.array([[1.0, 3.0, 3.0, 2.0], [5.0, 5.0, 5.0, 5.0], [0.0, np.nan, 1.0, 2.0]], F32)
+    out = torch_long(3)
+    status = zeros(1).int()
+    call("veda_argmax", ptr(dev(x[:2])), 4, 2, 4, ptr(out), ptr(status), V.F32, stream())
+    sync()
+    assert list(host(out)[:2]) == [1, 0] and int(host(status)[0]) == 0
+    call("veda_argmax", ptr(dev(x)), 4, 3, 4, ptr(out), ptr(status), V.F32, stream())
+    sync()
+    assert int(host(status)[0]) == V.ERR_INVALID_ARGUMENT
+
+
+def torch_long(n):
+    from tests.gpu_util import torch
+    t = torch()
+    return t.zeros(n, dtype=t.int64, device="cuda")
+
+
+def test_randn_statistics():
+    n = 1 << 20
+    x = empty(n)
+    call("veda_randn", ptr(x), n, 0.02, 3, V.F32, stream())
+    sync()
+    h = host(x)
+    assert abs(h.mean()) < 1e-4 and abs(h.std() - 0.02) < 2e-4

@@ -1,0 +1,257 @@
+// Fused softmax cross-entropy: loss rows and dlogits in one streaming pass over the logits.
+//
+// The reference (src/libs/autograd/Loss.cpp:18-103 with ops::log_softmax,
+// src/libs/ops/Softmax.cpp:82-151) materialises fp32 log-probabilities and probabilities for the
+// whole [lanes, V] block. Here one CTA owns a row: pass 1 reads it once keeping a running
+// (max, sum of exp) per thread (online normaliser), reduced across the CTA; pass 2 re-reads it
+// (an L2 hit: 148 SMs x one 300 KB row in flight fits the 126 MB L2) and writes
+//   dlogits = grad_scale * exp(x - max - log(sum))   minus grad_scale at the target,
+// the (p - onehot) * g/lanes of Loss.cpp:80-99 with p = exp(log_softmax) as the reference forms
+// it. row_loss = -(x_t - max - log(sum)) in fp32; the mean over rows is taken in double by
+// veda_mean_f64, as Loss.cpp:52-60 does.
+#include "common.cuh"
+
+#include <cfloat>
+
+namespace veda::cuda
+{
+namespace
+{
+
+constexpr int kThreads = 512;
+
+__device__ __forceinline__ void online_merge(float& m, float& s, float om, float os)
+{
+    if (om == -INFINITY)
+    {
+        return;
+    }
+    if (m == -INFINITY)
+    {
+        m = om;
+        s = os;
+        return;
+    }
+    if (om > m)
+    {
+        s = s * expf(m - om) + os;
+        m = om;
+    }
+    else
+    {
+        s = s + os * expf(om - m);
+    }
+}
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__ targets,
+          float* __restrict__ row_loss, T* dlogits, int64_t ldd, int64_t rows, int64_t vocab,
+          float grad_scale, int* status)
+{
+    constexpr int V = VEC ? Vec16<T>::N : 1;
+    __shared__ float red_m[kThreads / 32];
+    __shared__ float red_s[kThreads / 32];
+    __shared__ float final_m, final_log;
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x)
+    {
+        const T* x = logits + row * ldl;
+        float m = -INFINITY, s = 0.0f;
+        for (int64_t i = static_cast<int64_t>(threadIdx.x) * V; i < vocab;
+             i += static_cast<int64_t>(kThreads) * V)
+        {
+            float v[V];
+            if constexpr (VEC)
+            {
+                load16(x + i, v);
+            }
+            else
+            {
+                v[0] = to_f32(x[i]);
+            }
+#pragma unroll
+            for (int j = 0; j < V; ++j)
+            {
+                if (v[j] > m)
+                {
+                    s = (m == -INFINITY ? 0.0f : s * expf(m - v[j])) + 1.0f;
+                    m = v[j];
+                }
+                else if (v[j] != -INFINITY || m != -INFINITY)
+                {
+                    s += expf(v[j] - m);
+                }
+            }
+        }
+        // warp then block merge of (m, s)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+        {
+            const float om = __shfl_xor_sync(0xFFFFFFFFu, m, o);
+            const float os = __shfl_xor_sync(0xFFFFFFFFu, s, o);
+            online_merge(m, s, om, os);
+        }
+        const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+        if (lane == 0)
+        {
+            red_m[wid] = m;
+            red_s[wid] = s;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0)
+        {
+            float bm = red_m[0], bs = red_s[0];
+            for (int w = 1; w < kThreads / 32; ++w)
+            {
+                online_merge(bm, bs, red_m[w], red_s[w]);
+            }
+            final_m = bm;
+            final_log = logf(bs);
+        }
+        __syncthreads();
+        const float mx = final_m, lg = final_log;
+        const int64_t t = targets[row];
+        const bool valid = t >= 0 && t < vocab;
+        if (threadIdx.x == 0)
+        {
+            if (!valid)
+            {
+                if (status != nullptr)
+                {
+                    *status = VEDA_ERR_OUT_OF_RANGE;
+                }
+                if (row_loss != nullptr)
+                {
+                    row_loss[row] = NAN;
+                }
+            }
+            else if (row_loss != nullptr)
+            {
+                row_loss[row] = -((to_f32(x[t]) - mx) - lg);
+            }
+        }
+        if (dlogits != nullptr && valid)
+        {
+            T* d = dlogits + row * ldd;
+            for (int64_t i = static_cast<int64_t>(threadIdx.x) * V; i < vocab;
+                 i += static_cast<int64_t>(kThreads) * V)
+            {
+                float v[V];
+                if constexpr (VEC)
+                {
+                    load16(x + i, v);
+                }
+                else
+                {
+                    v[0] = to_f32(x[i]);
+                }
+#pragma unroll
+                for (int j = 0; j < V; ++j)
+                {
+                    const float p = expf((v[j] - mx) - lg);
+                    float g = grad_scale * p;
+                    if (i + j == t)
+                    {
+                        g -= grad_scale;
+                    }
+                    v[j] = g;
+                }
+                if constexpr (VEC)
+                {
+                    store16(d + i, v);
+                }
+                else
+                {
+                    d[i] = from_f32<T>(v[0]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// Deterministic double-precision mean: one CTA, fixed order of partial sums.
+__global__ void mean_f64_kernel(const float* __restrict__ v, int64_t n, float* out,
+                                double* out_f64)
+{
+    __shared__ double part[1024 / 32];
+    double s = 0.0;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
+    {
+        s += static_cast<double>(v[i]);
+    }
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0)
+    {
+        part[threadIdx.x >> 5] = s;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+    {
+        double total = 0.0;
+        for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w)
+        {
+            total += part[w];
+        }
+        const double mean = total / static_cast<double>(n);
+        if (out != nullptr)
+        {
+            *out = static_cast<float>(mean);
+        }
+        if (out_f64 != nullptr)
+        {
+            *out_f64 = mean;
+        }
+    }
+}
+
+} // namespace
+} // namespace veda::cuda
+
+using namespace veda::cuda;
+
+extern "C" int veda_cross_entropy(const void* logits, int64_t ldl, const int64_t* targets,
+                                  float* row_loss, void* dlogits, int64_t ldd, int64_t rows,
+                                  int64_t vocab, float grad_scale, int* status, int dtype,
+                                  veda_stream_t stream)
+{
+    VEDA_REQUIRE(valid_dtype(dtype), "unknown dtype");
+    VEDA_REQUIRE(rows >= 0 && vocab > 0 && ldl >= vocab, "bad shape");
+    VEDA_REQUIRE(dlogits == nullptr || ldd >= vocab, "bad dlogits leading dimension");
+    if (rows == 0)
+    {
+        return VEDA_OK;
+    }
+    VEDA_REQUIRE(logits != nullptr && targets != nullptr, "null pointer");
+    const size_t es = dtype_size(dtype);
+    const int64_t v = 16 / static_cast<int64_t>(es);
+    const bool vec = aligned16(logits) && ldl % v == 0 && vocab % v == 0 &&
+                     (dlogits == nullptr || (aligned16(dlogits) && ldd % v == 0));
+    const unsigned grid = static_cast<unsigned>(
+        rows < static_cast<int64_t>(sm_count()) * 4 ? rows : static_cast<int64_t>(sm_count()) * 4);
+#define VEDA_CE(T, VEC)                                                                           \
+    ce_kernel<T, VEC><<<grid, kThreads, 0, stream>>>(static_cast<const T*>(logits), ldl, targets, \
+                                                     row_loss, static_cast<T*>(dlogits), ldd,    \
+                                                     rows, vocab, grad_scale, status)
+    if (dtype == VEDA_BF16)
+    {
+        if (vec) VEDA_CE(bf16, true); else VEDA_CE(bf16, false);
+    }
+    else
+    {
+        if (vec) VEDA_CE(float, true); else VEDA_CE(float, false);
+    }
+#undef VEDA_CE
+    count_launch();
+    return check_launch("veda_cross_entropy");
+}
+
+extern "C" int veda_mean_f64(const float* v, int64_t n, float* out, double* out_f64,
+                             veda_stream_t stream)
+{
+    VEDA_REQUIRE(n > 0, "nothing to average over");
+    VEDA_REQUIRE(v != nullptr, "null pointer");
+    mean_f64_kernel<<<1, 1024, 0, stream>>>(v, n, out, out_f64);
+    count_launch();
+    return check_launch("veda_mean_f64");
+}

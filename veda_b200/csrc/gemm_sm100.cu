@@ -1,0 +1,775 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05.mma, accumulators in TMEM), fed by TMA.
+//
+// The Linear/LM-head products of the training step: forward y = x W^T (NT), input gradient
+// dX = dY W (NN) and weight gradient dW = dY^T X (TN) — ops::matmul / ops::matmul_nt as used by
+// autograd::matmul_nt's forward and backward (src/libs/autograd/Variable.cpp:325-346). The
+// reference runs a scalar fp32 i-j-k loop (src/libs/ops/Matmul.cpp:47-74); here operands are bf16,
+// products accumulate in fp32 in TMEM, and the epilogue writes bf16 or fp32 (fp32 with beta = 1
+// accumulates into a gradient, the leaf accumulation of Variable.cpp:27-38).
+//
+// Kernel structure (one CTA per SM, persistent over output tiles of 128 x BN):
+//   warp 0     TMA producer: one thread streams 128x64 A and BNx64 B bf16 tiles into a
+//              STAGES-deep ring of 128-byte-swizzled shared-memory buffers (no multicast);
+//   warp 1     MMA issuer: allocates 2*BN TMEM columns (two accumulators), one thread issues
+//              tcgen05.mma (M=128, N=BN, K=16) and signals stage release / tile completion with
+//              tcgen05.commit onto mbarriers;
+//   warps 2-5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, alpha/beta, convert, store;
+//              the other accumulator is being filled meanwhile.
+// Operand layouts: A and B are each either K-major (the reduction dim contiguous) or MN-major; the
+// shared-memory descriptors and the instruction descriptor's major bits say which, so NT, NN and
+// TN all run without a transpose pass. Split-K (fp32 output only) adds partial tiles with fp32
+// vector atomics, so small weight-gradient GEMMs still fill all 148 SMs.
+// Every mbarrier wait is bounded; a wait that gives up records VEDA_ERR_TIMEOUT in the library's
+// device status word (veda_kernel_status) and the kernel runs to completion.
+#include "gemm.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+namespace veda::cuda
+{
+int* device_status_ptr();
+
+namespace
+{
+
+constexpr int BM = 128;
+constexpr int BK = 64;               // 64 bf16 = 128 bytes: one swizzle row
+constexpr int kThreads = 192;        // 6 warps
+
+template <int BN>
+struct Cfg
+{
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+struct Params
+{
+    int M, N, K;
+    int num_m, num_n, kblocks, splits, kb_per_split;
+    void* C;
+    int64_t ldc;
+    float alpha, beta;
+    int out_f32;      // 1: fp32 C, 0: bf16 C
+    int atomic;       // 1: split-K partial tiles are added with fp32 atomics
+    int vec_ok;       // C base and ldc allow 16-byte stores
+    int* status;
+};
+
+// ---- PTX wrappers ------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t phase)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: about two seconds of spinning, then the status word records a timeout, the CTA's
+// shared abort flag is raised so every later wait returns at once, and the caller proceeds
+// (results are then garbage, but the kernel ends promptly and the context survives).
+__device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t phase, int* status,
+                                          volatile int* abort)
+{
+    const uint32_t addr = smem_u32(bar);
+    if (mbar_try_wait(addr, phase))
+    {
+        return;
+    }
+    const long long start = clock64();
+    while (!mbar_try_wait(addr, phase))
+    {
+        if (*abort != 0)
+        {
+            return;
+        }
+        if (clock64() - start > (1ll << 32))
+        {
+            *abort = 1;
+            if (status != nullptr)
+            {
+                atomicExch(status, VEDA_ERR_TIMEOUT);
+            }
+            return;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
+                                            int y)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch(const CUtensorMap* map)
+{
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before()
+{
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after()
+{
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: 128-byte swizzle, descriptor version 1 (sm_100).
+//   K-major operand: rows of 128 bytes, 8-row core groups SBO = 1024 bytes apart (LBO unused).
+//   MN-major operand: 64-element MN chunks LBO bytes apart, 8-row K groups SBO = 1024 apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo)
+{
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= 1ull << 46;   // version
+    d |= 2ull << 61;   // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor, kind::f16: D fp32, A and B bf16, majors, N >> 3, M >> 4.
+__host__ __device__ constexpr uint32_t instr_desc(int n, bool a_mn, bool b_mn)
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) |
+           ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(BM >> 4) << 24);
+}
+
+// Output tile order: groups of 16 M-tiles sweep all N-tiles, so an A row-panel stays in L2.
+__device__ __forceinline__ void unit_coords(int u, const Params& p, int& mb, int& nb, int& split)
+{
+    const int tiles = p.num_m * p.num_n;
+    split = u / tiles;
+    const int t = u - split * tiles;
+    constexpr int G = 16;
+    const int group = t / (G * p.num_n);
+    const int first = group * G;
+    const int gm = min(p.num_m - first, G);
+    const int in = t - group * G * p.num_n;
+    mb = first + in % gm;
+    nb = in / gm;
+}
+
+template <int BN>
+__device__ __forceinline__ void store_chunk(const Params& p, int row, int col0, const uint32_t (&r)[32])
+{
+    if (row >= p.M)
+    {
+        return;
+    }
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+    {
+        v[j] = __uint_as_float(r[j]);
+        if (p.alpha != 1.0f)
+        {
+            v[j] *= p.alpha;
+        }
+    }
+    const bool full = col0 + 32 <= p.N && p.vec_ok;
+    if (p.out_f32)
+    {
+        float* c = static_cast<float*>(p.C) + static_cast<int64_t>(row) * p.ldc + col0;
+        if (full)
+        {
+            if (p.atomic)
+            {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                {
+                    atomicAdd(reinterpret_cast<float4*>(c + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+                }
+                return;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+            {
+                float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                if (p.beta != 0.0f)
+                {
+                    const float4 old = *reinterpret_cast<const float4*>(c + j);
+                    o.x += p.beta * old.x;
+                    o.y += p.beta * old.y;
+                    o.z += p.beta * old.z;
+                    o.w += p.beta * old.w;
+                }
+                *reinterpret_cast<float4*>(c + j) = o;
+            }
+            return;
+        }
+        for (int j = 0; j < 32; ++j)
+        {
+            if (col0 + j < p.N)
+            {
+                if (p.atomic)
+                {
+                    atomicAdd(c + j, v[j]);
+                }
+                else
+                {
+                    c[j] = p.beta != 0.0f ? v[j] + p.beta * c[j] : v[j];
+                }
+            }
+        }
+        return;
+    }
+    bf16* c = static_cast<bf16*>(p.C) + static_cast<int64_t>(row) * p.ldc + col0;
+    if (full)
+    {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8)
+        {
+            float o[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+            {
+                o[q] = v[j + q];
+            }
+            if (p.beta != 0.0f)
+            {
+                float old[8];
+                load16(c + j, old);
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                {
+                    o[q] += p.beta * old[q];
+                }
+            }
+            store16(c + j, o);
+        }
+        return;
+    }
+    for (int j = 0; j < 32; ++j)
+    {
+        if (col0 + j < p.N)
+        {
+            const float o = p.beta != 0.0f ? v[j] + p.beta * __bfloat162float(c[j]) : v[j];
+            c[j] = __float2bfloat16_rn(o);
+        }
+    }
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+               const Params p)
+{
+    using C_ = Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* sa = smem;
+    uint8_t* sb = smem + C_::STAGES * C_::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sb + C_::STAGES * C_::B_BYTES);
+    uint64_t* empty = full + C_::STAGES;
+    uint64_t* tfull = empty + C_::STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0)
+    {
+        *abort = 0;
+        for (int s = 0; s < C_::STAGES; ++s)
+        {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b)
+        {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1)
+    {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(C_::TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int units = p.num_m * p.num_n * p.splits;
+
+    if (warp == 0 && lane == 0)
+    {
+        tma_prefetch(&tma_a);
+        tma_prefetch(&tma_b);
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x)
+        {
+            int mb, nb, split;
+            unit_coords(u, p, mb, nb, split);
+            const int kb0 = split * p.kb_per_split;
+            const int kb1 = min(p.kblocks, kb0 + p.kb_per_split);
+            for (int kb = kb0; kb < kb1; ++kb)
+            {
+                mbar_wait(&empty[stage], phase ^ 1, p.status, abort);
+                mbar_expect_tx(&full[stage], C_::STAGE_BYTES);
+                uint8_t* a_dst = sa + stage * C_::A_BYTES;
+                uint8_t* b_dst = sb + stage * C_::B_BYTES;
+                if constexpr (!A_MN)
+                {
+                    tma_load_2d(a_dst, &tma_a, &full[stage], kb * BK, mb * BM);
+                }
+                else
+                {
+#pragma unroll
+                    for (int j = 0; j < BM / 64; ++j)
+                    {
+                        tma_load_2d(a_dst + j * (BK * 128), &tma_a, &full[stage], mb * BM + j * 64,
+                                    kb * BK);
+                    }
+                }
+                if constexpr (!B_MN)
+                {
+                    tma_load_2d(b_dst, &tma_b, &full[stage], kb * BK, nb * BN);
+                }
+                else
+                {
+#pragma unroll
+                    for (int j = 0; j < BN / 64; ++j)
+                    {
+                        tma_load_2d(b_dst + j * (BK * 128), &tma_b, &full[stage], nb * BN + j * 64,
+                                    kb * BK);
+                    }
+                }
+                if (++stage == C_::STAGES)
+                {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+    }
+    else if (warp == 1 && lane == 0)
+    {
+        constexpr uint32_t idesc = instr_desc(BN, A_MN, B_MN);
+        int stage = 0;
+        uint32_t phase = 0;
+        int it = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++it)
+        {
+            int mb, nb, split;
+            unit_coords(u, p, mb, nb, split);
+            const int kb0 = split * p.kb_per_split;
+            const int kb1 = min(p.kblocks, kb0 + p.kb_per_split);
+            const int buf = it & 1;
+            const uint32_t tphase = (it >> 1) & 1;
+            mbar_wait(&tempty[buf], tphase ^ 1, p.status, abort);
+            tc_fence_after();
+            const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
+            for (int kb = kb0; kb < kb1; ++kb)
+            {
+                mbar_wait(&full[stage], phase, p.status, abort);
+                tc_fence_after();
+                const uint32_t a_base = smem_u32(sa + stage * C_::A_BYTES);
+                const uint32_t b_base = smem_u32(sb + stage * C_::B_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk)
+                {
+                    const uint64_t ad = A_MN ? smem_desc(a_base + kk * 2048, BK * 128, 1024)
+                                             : smem_desc(a_base + kk * 32, 16, 1024);
+                    const uint64_t bd = B_MN ? smem_desc(b_base + kk * 2048, BK * 128, 1024)
+                                             : smem_desc(b_base + kk * 32, 16, 1024);
+                    tc_mma(d, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+                }
+                tc_commit(&empty[stage]);
+                if (++stage == C_::STAGES)
+                {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            tc_commit(&tfull[buf]);
+        }
+    }
+    else if (warp >= 2)
+    {
+        const int quarter = warp & 3;
+        int it = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++it)
+        {
+            int mb, nb, split;
+            unit_coords(u, p, mb, nb, split);
+            const int buf = it & 1;
+            const uint32_t tphase = (it >> 1) & 1;
+            mbar_wait(&tfull[buf], tphase, p.status, abort);
+            tc_fence_after();
+            const int row = mb * BM + quarter * 32 + lane;
+            const uint32_t base = tmem + static_cast<uint32_t>(buf * BN) +
+                                  (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32)
+            {
+                uint32_t r[32];
+                tmem_ld32(base + static_cast<uint32_t>(c), r);
+                store_chunk<BN>(p, row, nb * BN + c, r);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+            {
+                mbar_arrive(&tempty[buf]);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1)
+    {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(C_::TMEM_COLS));
+    }
+}
+
+// ---- host ------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                             &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+        {
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        }
+    });
+    return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix with `inner` contiguous elements per row.
+bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t ld,
+              uint32_t box_inner, uint32_t box_outer)
+{
+    auto fn = encode_fn();
+    if (fn == nullptr)
+    {
+        return false;
+    }
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int grid,
+              cudaStream_t s)
+{
+    auto kernel = tc_gemm_kernel<BN, A_MN, B_MN>;
+    static int configured_device = -1;
+    int device = 0;
+    cudaGetDevice(&device);
+    if (configured_device != device)
+    {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
+        configured_device = device;
+    }
+    kernel<<<grid, kThreads, Cfg<BN>::SMEM, s>>>(ma, mb, p);
+    count_launch();
+    return check_launch("veda_gemm (tcgen05)");
+}
+
+// Picks a split-K factor (fp32 output only) that best fills whole waves of SMs.
+int choose_splits(int tiles, int kblocks, bool allowed)
+{
+    const int sms = sm_count();
+    if (!allowed || tiles >= sms)
+    {
+        return 1;
+    }
+    int best = 1;
+    double best_score = -1.0;
+    for (int s = 1; s <= 8; ++s)
+    {
+        const int per = (kblocks + s - 1) / s;
+        if (per < 4 || (s - 1) * per >= kblocks)
+        {
+            break;
+        }
+        const int units = tiles * s;
+        const int waves = (units + sms - 1) / sms;
+        const double score = static_cast<double>(units) / (waves * sms) - 0.03 * (s - 1);
+        if (score > best_score)
+        {
+            best_score = score;
+            best = s;
+        }
+    }
+    return best;
+}
+
+int tc_gemm(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* B,
+            int64_t ldb, void* C, int64_t ldc, int dtype_c, float alpha, float beta, cudaStream_t s)
+{
+    const bool a_mn = op == kTN;
+    const bool b_mn = op != kNT;
+    const int BN = N >= 256 ? 256 : 128;
+    CUtensorMap ma, mb;
+    bool ok = a_mn ? make_map(&ma, A, M, K, lda, 64, 64) : make_map(&ma, A, K, M, lda, 64, BM);
+    ok = ok && (b_mn ? make_map(&mb, B, N, K, ldb, 64, 64)
+                     : make_map(&mb, B, K, N, ldb, 64, static_cast<uint32_t>(BN)));
+    if (!ok)
+    {
+        return -1;   // caller falls back
+    }
+    Params p{};
+    p.M = static_cast<int>(M);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.num_m = static_cast<int>((M + BM - 1) / BM);
+    p.num_n = static_cast<int>((N + BN - 1) / BN);
+    p.kblocks = static_cast<int>((K + BK - 1) / BK);
+    p.C = C;
+    p.ldc = ldc;
+    p.alpha = alpha;
+    p.beta = beta;
+    p.out_f32 = dtype_c == VEDA_F32;
+    p.vec_ok = aligned16(C) && (ldc % (dtype_c == VEDA_F32 ? 4 : 8)) == 0;
+    p.status = device_status_ptr();
+    const int tiles = p.num_m * p.num_n;
+    p.splits = choose_splits(tiles, p.kblocks, p.out_f32 != 0);
+    p.kb_per_split = (p.kblocks + p.splits - 1) / p.splits;
+    p.atomic = p.splits > 1;
+    if (p.atomic)
+    {
+        // partial tiles are added onto C: first bring C to beta * C
+        if (beta == 0.0f)
+        {
+            if (cudaMemset2DAsync(C, ldc * 4, 0, N * 4, M, s) != cudaSuccess)
+            {
+                return fail(VEDA_ERR_CUDA, "veda_gemm: clearing C for split-K failed");
+            }
+        }
+        else if (beta != 1.0f)
+        {
+            return -1;   // general beta with split-K: let the caller use one split
+        }
+        p.beta = 0.0f;
+    }
+    const int units = tiles * p.splits;
+    const int grid = std::min(units, sm_count());
+    const bool big = BN == 256;
+    if (op == kNT)
+        return big ? launch_tc<256, false, false>(ma, mb, p, grid, s)
+                   : launch_tc<128, false, false>(ma, mb, p, grid, s);
+    if (op == kNN)
+        return big ? launch_tc<256, false, true>(ma, mb, p, grid, s)
+                   : launch_tc<128, false, true>(ma, mb, p, grid, s);
+    return big ? launch_tc<256, true, true>(ma, mb, p, grid, s)
+               : launch_tc<128, true, true>(ma, mb, p, grid, s);
+}
+
+bool tc_eligible(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                 const void* B, int64_t ldb)
+{
+    (void)op;
+    return M >= 1 && N >= 16 && K >= 16 && M < (1ll << 31) && N < (1ll << 31) &&
+           K < (1ll << 31) && aligned16(A) && aligned16(B) && lda % 8 == 0 && ldb % 8 == 0;
+}
+
+int gemm_dispatch(int op, int64_t batch, int64_t M, int64_t N, int64_t K, const void* A,
+                  int64_t lda, int64_t sa, const void* B, int64_t ldb, int64_t sb, void* C,
+                  int64_t ldc, int64_t sc, int dtype_ab, int dtype_c, float alpha, float beta,
+                  cudaStream_t s)
+{
+    VEDA_REQUIRE(valid_dtype(dtype_ab) && valid_dtype(dtype_c), "unknown dtype");
+    VEDA_REQUIRE(op >= 0 && op <= 2, "unknown op");
+    VEDA_REQUIRE(batch >= 0 && M >= 0 && N >= 0 && K >= 0, "negative extent");
+    const int64_t a_rows = op == kTN ? K : M, a_cols = op == kTN ? M : K;
+    const int64_t b_rows = op == kNT ? N : K, b_cols = op == kNT ? K : N;
+    VEDA_REQUIRE(a_rows == 0 || lda >= a_cols, "lda smaller than the row length of A");
+    VEDA_REQUIRE(b_rows == 0 || ldb >= b_cols, "ldb smaller than the row length of B");
+    VEDA_REQUIRE(M == 0 || ldc >= N, "ldc smaller than N");
+    (void)b_rows;
+    if (batch == 0 || M == 0 || N == 0)
+    {
+        return VEDA_OK;
+    }
+    VEDA_REQUIRE(A != nullptr && B != nullptr && C != nullptr, "null pointer");
+    if (K == 0)
+    {
+        // the empty sum is 0 (Matmul.cpp:63): C = beta * C
+        for (int64_t z = 0; z < batch; ++z)
+        {
+            char* c = static_cast<char*>(C) + z * sc * static_cast<int64_t>(dtype_size(dtype_c));
+            for (int64_t r = 0; r < M; ++r)
+            {
+                const int rc = veda_scale(c + r * ldc * static_cast<int64_t>(dtype_size(dtype_c)),
+                                          beta, c + r * ldc * static_cast<int64_t>(dtype_size(dtype_c)),
+                                          N, dtype_c, s);
+                if (rc != VEDA_OK) return rc;
+            }
+        }
+        return VEDA_OK;
+    }
+    if (dtype_ab == VEDA_BF16 && tc_eligible(op, M, N, K, A, lda, B, ldb))
+    {
+        const size_t es = 2, ec = dtype_size(dtype_c);
+        bool all = true;
+        for (int64_t z = 0; z < batch && all; ++z)
+        {
+            const char* a = static_cast<const char*>(A) + z * sa * static_cast<int64_t>(es);
+            const char* b = static_cast<const char*>(B) + z * sb * static_cast<int64_t>(es);
+            char* c = static_cast<char*>(C) + z * sc * static_cast<int64_t>(ec);
+            if (!aligned16(a) || !aligned16(b))
+            {
+                all = false;
+                break;
+            }
+            const int rc = tc_gemm(op, M, N, K, a, lda, b, ldb, c, ldc, dtype_c, alpha, beta, s);
+            if (rc == -1)
+            {
+                if (z != 0)
+                {
+                    return fail(VEDA_ERR_CUDA, "veda_gemm: tensor-map creation failed mid-batch");
+                }
+                all = false;
+                break;
+            }
+            if (rc != VEDA_OK)
+            {
+                return rc;
+            }
+        }
+        if (all)
+        {
+            return VEDA_OK;
+        }
+    }
+    return simt_gemm(op, batch, M, N, K, A, lda, sa, B, ldb, sb, C, ldc, sc, dtype_ab, dtype_c,
+                     alpha, beta, s);
+}
+
+} // namespace
+} // namespace veda::cuda
+
+using namespace veda::cuda;
+
+extern "C" int veda_gemm_nt(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                            const void* B, int64_t ldb, void* C, int64_t ldc, int dtype_ab,
+                            int dtype_c, float alpha, float beta, veda_stream_t stream)
+{
+    return gemm_dispatch(kNT, 1, M, N, K, A, lda, 0, B, ldb, 0, C, ldc, 0, dtype_ab, dtype_c,
+                         alpha, beta, stream);
+}
+
+extern "C" int veda_gemm_nn(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                            const void* B, int64_t ldb, void* C, int64_t ldc, int dtype_ab,
+                            int dtype_c, float alpha, float beta, veda_stream_t stream)
+{
+    return gemm_dispatch(kNN, 1, M, N, K, A, lda, 0, B, ldb, 0, C, ldc, 0, dtype_ab, dtype_c,
+                         alpha, beta, stream);
+}
+
+extern "C" int veda_gemm_tn(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                            const void* B, int64_t ldb, void* C, int64_t ldc, int dtype_ab,
+                            int dtype_c, float alpha, float beta, veda_stream_t stream)
+{
+    return gemm_dispatch(kTN, 1, M, N, K, A, lda, 0, B, ldb, 0, C, ldc, 0, dtype_ab, dtype_c,
+                         alpha, beta, stream);
+}
+
+extern "C" int veda_gemm_batched(int op, int64_t batch, int64_t M, int64_t N, int64_t K,
+                                 const void* A, int64_t lda, int64_t stride_a, const void* B,
+                                 int64_t ldb, int64_t stride_b, void* C, int64_t ldc,
+                                 int64_t stride_c, int dtype_ab, int dtype_c, float alpha,
+                                 float beta, veda_stream_t stream)
+{
+    return gemm_dispatch(op, batch, M, N, K, A, lda, stride_a, B, ldb, stride_b, C, ldc, stride_c,
+                         dtype_ab, dtype_c, alpha, beta, stream);
+}

@@ -1,0 +1,131 @@
+// Library-wide state of libveda_cuda.so: the per-thread error message, the launch counter and
+// the cached device properties.
+#include "common.cuh"
+
+#include <mutex>
+
+
+
+namespace veda::cuda
+{
+
+namespace
+{
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+int g_sm_count[64] = {0};
+} // namespace
+
+void set_error(const std::string& message) { g_last_error = message; }
+
+int fail(int code, const std::string& message)
+{
+    g_last_error = message;
+    return code;
+}
+
+int check_launch(const char* what)
+{
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess)
+    {
+        return fail(VEDA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+    }
+    return VEDA_OK;
+}
+
+void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+uint64_t g_launches_value() { return g_launches.load(std::memory_order_relaxed); }
+
+int sm_count()
+{
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
+    {
+        return 148;
+    }
+    if (g_sm_count[device] == 0)
+    {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+        g_sm_count[device] = n > 0 ? n : 148;
+    }
+    return g_sm_count[device];
+}
+
+const char* last_error_cstr() { return g_last_error.c_str(); }
+
+// One int per device, allocated on first use: kernels whose bounded waits give up write
+// VEDA_ERR_TIMEOUT here instead of spinning forever.
+int* device_status_ptr()
+{
+    static int* ptrs[64] = {nullptr};
+    static std::mutex mu;
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
+    {
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (ptrs[device] == nullptr)
+    {
+        int* p = nullptr;
+        if (cudaMalloc(&p, sizeof(int)) == cudaSuccess)
+        {
+            cudaMemset(p, 0, sizeof(int));
+            ptrs[device] = p;
+        }
+    }
+    return ptrs[device];
+}
+
+} // namespace veda::cuda
+
+extern "C" int veda_kernel_status(int reset)
+{
+    int* p = veda::cuda::device_status_ptr();
+    if (p == nullptr)
+    {
+        return veda::cuda::fail(VEDA_ERR_CUDA, "veda_kernel_status: no device status word");
+    }
+    int value = 0;
+    if (cudaMemcpy(&value, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    {
+        return veda::cuda::fail(VEDA_ERR_CUDA, "veda_kernel_status: read failed");
+    }
+    if (reset)
+    {
+        cudaMemset(p, 0, sizeof(int));
+    }
+    if (value != 0)
+    {
+        veda::cuda::set_error("a kernel's bounded wait gave up (device status word)");
+    }
+    return value;
+}
+
+extern "C" const char* veda_last_error(void) { return veda::cuda::last_error_cstr(); }
+
+extern "C" uint64_t veda_launch_count(void)
+{
+    return veda::cuda::g_launches_value();
+}
+
+extern "C" int veda_device_info(int* sm, int* major, int* minor)
+{
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess)
+    {
+        return veda::cuda::fail(VEDA_ERR_CUDA, "veda_device_info: no CUDA device");
+    }
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
+    {
+        return veda::cuda::fail(VEDA_ERR_CUDA, "veda_device_info: cudaGetDeviceProperties failed");
+    }
+    if (sm) *sm = prop.multiProcessorCount;
+    if (major) *major = prop.major;
+    if (minor) *minor = prop.minor;
+    return VEDA_OK;
+}
