@@ -337,7 +337,8 @@ def _gemm_case(op, M, N, K, dtype_c, seed, beta=0.0):
                                    (4096, 1024, 1024), (128, 128, 8192)])
 def test_gemm_bf16_fp32_out(op, M, N, K):
     c, ref = _gemm_case(op, M, N, K, V.F32, M + N + K)
-    assert rel(c, ref) <= 1e-5, rel(c, ref)
+    # fp32 accumulation of bf16 products against a float64 product of the same bf16 values
+    assert rel(c, ref) <= 3e-5, rel(c, ref)
 
 
 @pytest.mark.parametrize("op", ["nt", "nn", "tn"])
@@ -354,7 +355,8 @@ def test_gemm_fp32_is_bit_exact_with_reference_loop(ref_lib):
     b = r.standard_normal((33, 45)).astype(F32)
     want = ref_lib.gemm_nt(a, b)
     c = empty((70, 33))
-    call("veda_gemm_nt", 70, 33, 45, ptr(dev(a)), 45, ptr(dev(b)), 45, ptr(c), 33, V.F32, V.F32,
+    ad, bd = dev(a), dev(b)
+    call("veda_gemm_nt", 70, 33, 45, ptr(ad), 45, ptr(bd), 45, ptr(c), 33, V.F32, V.F32,
          1.0, 0.0, stream())
     sync()
     assert np.array_equal(host(c), want)
@@ -369,7 +371,8 @@ def test_gemm_fp32_small_shapes(op):
     am = a.T if op == "tn" else a
     bm = b.T if op == "nt" else b
     c = empty((M, N))
-    call(f"veda_gemm_{op}", M, N, K, ptr(dev(a)), a.shape[1], ptr(dev(b)), b.shape[1], ptr(c), N,
+    ad, bd = dev(a), dev(b)
+    call(f"veda_gemm_{op}", M, N, K, ptr(ad), a.shape[1], ptr(bd), b.shape[1], ptr(c), N,
          V.F32, V.F32, 1.0, 0.0, stream())
     sync()
     assert rel(host(c), am @ bm) <= 1e-6
@@ -455,15 +458,17 @@ def test_binary_broadcast_and_unbroadcast():
     sa = np.array([20, 5, 1], np.int64)
     sb = np.array([0, 0, 1], np.int64)
     out = empty((3, 4, 5))
+    ad, bd = dev(a), dev(b)   # held: a freed temporary could be reused before the launch runs
     for op, ref in ((0, a + b), (1, a * b)):
-        call("veda_binary", op, ptr(dev(a)), sa.ctypes.data, ptr(dev(b)), sb.ctypes.data, ptr(out),
+        call("veda_binary", op, ptr(ad), sa.ctypes.data, ptr(bd), sb.ctypes.data, ptr(out),
              shape.ctypes.data, 3, V.F32, stream())
         sync()
         assert np.array_equal(host(out), ref.astype(F32))
     g = r.standard_normal((3, 4, 5)).astype(F32)
     red = empty((1, 4, 1))
     tgt = np.array([1, 4, 1], np.int64)
-    call("veda_unbroadcast", ptr(dev(g)), shape.ctypes.data, tgt.ctypes.data, 3, ptr(red), V.F32,
+    gd = dev(g)
+    call("veda_unbroadcast", ptr(gd), shape.ctypes.data, tgt.ctypes.data, 3, ptr(red), V.F32,
          stream())
     sync()
     assert rel(host(red).ravel(), g.sum(axis=(0, 2))) <= 1e-6
@@ -475,22 +480,25 @@ def test_softmax_silu_sum_copy():
     x, g = ops["softmax_x"], ops["softmax_g"]
     lanes, n = x.shape
     y, dx = empty(x.shape), empty(x.shape)
-    yd = dev(x)
+    yd, gd = dev(x), dev(g)
     call("veda_softmax_fwd", ptr(yd), ptr(y), lanes, n, V.F32, stream())
-    call("veda_softmax_bwd", ptr(y), ptr(dev(g)), ptr(dx), lanes, n, V.F32, stream())
+    call("veda_softmax_bwd", ptr(y), ptr(gd), ptr(dx), lanes, n, V.F32, stream())
     sync()
     assert rel(host(y), ops["softmax_y"]) <= 1e-6
     assert rel(host(dx), ops["softmax_dx"]) <= 1e-5
-    xs = np.array([0.0, 1.0, -1.0], F32)
+    xs = dev(np.array([0.0, 1.0, -1.0], F32))
+    ones = dev(np.ones(3, F32))
     d = empty(3)
-    call("veda_silu_bwd", ptr(dev(xs)), ptr(dev(np.ones(3, F32))), ptr(d), 3, V.F32, stream())
+    call("veda_silu_bwd", ptr(xs), ptr(ones), ptr(d), 3, V.F32, stream())
     s = empty(1)
-    call("veda_sum", ptr(dev(np.arange(10, dtype=F32))), 10, ptr(s), V.F32, stream())
+    ar = dev(np.arange(10, dtype=F32))
+    call("veda_sum", ptr(ar), 10, ptr(s), V.F32, stream())
     m = np.arange(12, dtype=F32).reshape(3, 4)
     t = empty((4, 3))
     shape = np.array([4, 3], np.int64)
     strides = np.array([1, 4], np.int64)
-    call("veda_copy_strided", ptr(dev(m)), V.F32, strides.ctypes.data, 0, ptr(t), V.F32,
+    md = dev(m)
+    call("veda_copy_strided", ptr(md), V.F32, strides.ctypes.data, 0, ptr(t), V.F32,
          shape.ctypes.data, 2, stream())
     sync()
     np.testing.assert_allclose(host(d), [0.5, 0.9277, 0.0723], atol=1e-3)
