@@ -1,0 +1,130 @@
+// veda::autograd — the reference's reverse-mode tape (src/libs/autograd/Variable.h:31-119,
+// Loss.h:43) over device tensors, plus fused training modules.
+//
+// Kept from the reference (same names, argument meaning and exception types):
+//   Variable::leaf, backward() (starts at a scalar, reverse topological order, intermediate
+//   gradients reset each pass, leaf gradients accumulate across passes), zero_grad(); the ops
+//   add, mul, mul(scalar), sum, matmul, matmul_nt, silu, gelu, softmax, rms_normalize,
+//   embedding, reshape, transpose, rope, cross_entropy; detail::unbroadcast.
+// Changed for the device:
+//   * an intermediate gradient is allocated on first contribution, and the first contribution is
+//     aliased rather than copied (a node whose gradient is an alias copies before mutating), so
+//     residual fan-out costs nothing;
+//   * producers that can add in place (GEMM epilogues with beta = 1, the norm backward's
+//     residual input, the embedding scatter) write straight into the destination gradient;
+//   * a parameter's gradient may be a view into one flat fp32 arena (Variable::parameter), which
+//     is what lets the optimiser and the data-parallel all-reduce work on whole buckets.
+// Fused modules (one node each, B200 kernels): rms_norm (norm + gain), linear (x W^T over
+// flattened tokens), attention (QK-norm + RoPE + causal GQA attention on a fused q|k|v buffer),
+// swiglu (on a fused gate|up buffer), cross_entropy (streaming softmax-CE with the gradient
+// formed in the same pass).
+#pragma once
+
+#include "veda/tensor.hpp"
+
+#include <cstdint>
+#include <functional>
+#include <memory>
+#include <vector>
+
+namespace veda::autograd
+{
+
+struct Node
+{
+    core::Tensor value;
+    core::Tensor grad;   // undefined until the first contribution (intermediates)
+    std::vector<std::shared_ptr<Node>> parents;
+    std::function<void(const core::Tensor& out_grad)> backward;
+    bool requires_grad = false;
+    bool grad_owned = true;    // false: grad aliases another tensor; copy before mutating
+    bool grad_zero = false;    // leaf gradient buffer currently holds zeros
+    bool is_leaf = false;
+
+    explicit Node(core::Tensor v);
+};
+
+struct BackwardOptions
+{
+    // Keep intermediate gradients after the pass (the reference does); false frees each one as
+    // soon as its node has propagated it.
+    bool retain_intermediate_grads = true;
+    // Called once per leaf when its gradient is final for this pass (every consumer has run).
+    std::function<void(Node*)> on_leaf_ready;
+};
+
+class Variable
+{
+public:
+    static Variable leaf(core::Tensor value, bool requires_grad = true);
+    // A trainable leaf whose gradient is the given fp32 buffer (e.g. a view into a gradient
+    // arena); the buffer is taken to hold zeros.
+    static Variable parameter(core::Tensor value, core::Tensor grad);
+    Variable() = default;
+    explicit Variable(std::shared_ptr<Node> node) : node_(std::move(node)) {}
+
+    const core::Tensor& value() const noexcept { return node_->value; }
+    // The gradient (a zero tensor if nothing has been accumulated yet).
+    const core::Tensor& grad() const;
+    bool requires_grad() const noexcept { return node_->requires_grad; }
+    const std::shared_ptr<Node>& node() const noexcept { return node_; }
+
+    void backward();
+    void backward(const BackwardOptions& options);
+    void zero_grad();
+
+private:
+    std::shared_ptr<Node> node_;
+};
+
+Variable add(const Variable& a, const Variable& b);
+Variable mul(const Variable& a, const Variable& b);
+Variable mul(const Variable& a, float scalar);
+Variable sum(const Variable& x);
+Variable matmul(const Variable& a, const Variable& b);
+Variable matmul_nt(const Variable& a, const Variable& b);
+Variable silu(const Variable& x);
+Variable gelu(const Variable& x);
+Variable softmax(const Variable& x, size_t dim);
+Variable rms_normalize(const Variable& x, float eps);
+Variable embedding(const Variable& table, const std::vector<int64_t>& ids,
+                   const core::Shape& id_shape);
+Variable reshape(const Variable& x, const core::Shape& shape);
+Variable transpose(const Variable& x, size_t a, size_t b);
+Variable rope(const Variable& x, const core::Tensor& cosines, const core::Tensor& sines);
+// Mean cross-entropy over lanes; targets on the host, validated like Loss.cpp:21-47.
+Variable cross_entropy(const Variable& logits, const std::vector<int64_t>& targets);
+
+// ---- fused modules --------------------------------------------------------------------------
+// mul(rms_normalize(x, eps), gamma) over the last dim.
+Variable rms_norm(const Variable& x, const Variable& gamma, float eps);
+// matmul_nt(x, w) with x [.., in] flattened to rows and w [out, in].
+Variable linear(const Variable& x, const Variable& w);
+// Qwen3 attention core on a fused projection qkv [B*T, (H + 2 Hkv) * Dh] (q | k | v columns):
+// rope(mul(rms_normalize(q_h), q_norm)) and the same for k, causal softmax(q k^T / sqrt(Dh)) v
+// with GQA; returns the context [B*T, H*Dh] (src/libs/train/Model.cpp:154-194).
+Variable attention(const Variable& qkv, const Variable& q_norm, const Variable& k_norm,
+                   const core::Tensor& cosines, const core::Tensor& sines, size_t batch,
+                   size_t length, size_t heads, size_t kv_heads, size_t head_dim, float eps);
+// mul(silu(gate), up) on a fused gate|up buffer [rows, 2F] -> [rows, F].
+Variable swiglu(const Variable& gate_up);
+// Token ids already on the device (int64 [count]); ids are checked on the device and an
+// out-of-range id raises std::out_of_range at the next synchronisation point.
+Variable embedding_device(const Variable& table, const core::Tensor& ids);
+// Mean cross-entropy with device targets (int64 [lanes]).
+Variable cross_entropy_device(const Variable& logits, const core::Tensor& targets);
+
+namespace detail
+{
+core::Tensor unbroadcast(const core::Tensor& gradient, const core::Shape& target);
+// The node's gradient made private and ready to be written: *fresh is true when the buffer
+// holds no contribution yet (an overwrite is then correct), false when it must be added to.
+core::Tensor& grad_target(Node& node, bool* fresh, core::DType dtype);
+// node.grad += g (the first contribution is aliased).
+void accumulate(Node& node, const core::Tensor& g);
+// Device error flag checked after launches that validate indices on the device.
+int* device_flag();
+void raise_device_flag();
+} // namespace detail
+
+} // namespace veda::autograd

@@ -1,0 +1,146 @@
+// veda::train — the reference's trainable Qwen3-architecture decoder
+// (src/libs/train/Model.h:34-72, Model.cpp:72-255) on the device, and the training step driver.
+//
+// TinyTransformer keeps the reference's parameter names, shapes and order
+// (model.embed_tokens.weight, then per layer input_layernorm, q/k/v/o_proj, q/k_norm,
+// post_attention_layernorm, gate/up/down_proj, then model.norm.weight; tied LM head) and its
+// forward (pre-norm residual blocks, QK-norm before RoPE, causal softmax attention, SwiGLU). It
+// differs where the B200 build needs it to:
+//   * GQA is allowed (Hkv < H; k/v_proj are [Hkv*Dh, D]); the reference refuses it in training;
+//   * weights live in one flat value arena (fp32 or bf16) and gradients in one flat fp32 arena,
+//     in parameter order, so q|k|v and gate|up are single [.., D] matrices and the optimiser and
+//     the all-reduce see whole buckets;
+//   * the forward uses the fused modules of veda::autograd (rms_norm, linear, attention,
+//     swiglu, cross_entropy) — one tape node each.
+// Trainer runs one step (zero_grad, forward, cross-entropy, backward, data-parallel gradient
+// all-reduce overlapped with the backward, fused clip + AdamW) on one GPU of a data-parallel job.
+#pragma once
+
+#include "veda/autograd.hpp"
+#include "veda/optim.hpp"
+
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <string>
+#include <utility>
+#include <vector>
+
+namespace veda::train
+{
+
+struct ModelConfig
+{
+    size_t hidden_size = 0;              // D
+    size_t intermediate_size = 0;        // F
+    size_t num_layers = 0;
+    size_t num_heads = 0;                // H
+    size_t num_kv_heads = 0;             // Hkv
+    size_t head_dim = 0;                 // Dh
+    size_t vocab_size = 0;               // V
+    size_t max_position_embeddings = 0;
+    float rms_norm_eps = 1e-6f;
+    float rope_theta = 10000.0f;
+    bool tie_word_embeddings = true;
+
+    size_t queries_per_kv_head() const { return num_heads / num_kv_heads; }
+};
+
+// The reference's tiny_config() (src/libs/train/Model.cpp:72-89).
+ModelConfig tiny_config();
+
+// RoPE tables [T, Dh] in fp32 from angles computed in double (src/libs/model/Rope.cpp:17-63).
+std::pair<core::Tensor, core::Tensor> rope_tables(size_t positions, size_t head_dim, float theta);
+
+class TinyTransformer
+{
+public:
+    // Weights ~ N(0, 0.02) from `seed` (device hash generator), norm gains 1.
+    TinyTransformer(ModelConfig config, uint64_t seed, core::DType dtype = core::DType::F32);
+
+    // ids are B*T token ids; the result is logits [B*T, V] on the tape.
+    autograd::Variable forward(const std::vector<int64_t>& ids, size_t batch, size_t length);
+    // ids already on the device (int64 [B*T]).
+    autograd::Variable forward_device(const core::Tensor& ids, size_t batch, size_t length);
+
+    // Every trainable leaf, once each, in the reference's order (views into the arenas).
+    const std::vector<autograd::Variable>& parameters() const noexcept { return parameters_; }
+    std::vector<std::pair<std::string, core::Tensor>> named_parameters() const;
+    const ModelConfig& config() const noexcept { return config_; }
+    core::DType dtype() const noexcept { return dtype_; }
+
+    // The leaves the forward graph consumes (q|k|v and gate|up fused), with their arena ranges.
+    struct GraphLeaf
+    {
+        autograd::Variable var;
+        size_t offset, count;   // in elements of the arenas
+    };
+    const std::vector<GraphLeaf>& graph_leaves() const noexcept { return graph_leaves_; }
+    const core::Tensor& value_arena() const noexcept { return values_; }
+    const core::Tensor& grad_arena() const noexcept { return grads_; }
+    size_t parameter_count() const noexcept { return total_; }
+    // Clears the whole gradient arena in one memset and marks every leaf's gradient as zero.
+    void zero_grad();
+
+private:
+    autograd::Variable forward_from(const autograd::Variable& x, size_t batch, size_t length);
+
+    ModelConfig config_;
+    core::DType dtype_;
+    core::Tensor values_, grads_;
+    size_t total_ = 0;
+    std::vector<autograd::Variable> parameters_;
+    std::vector<std::string> names_;
+    std::vector<GraphLeaf> graph_leaves_;
+    struct Layer
+    {
+        autograd::Variable in_norm, qkv, o, q_norm, k_norm, post_norm, gate_up, down;
+    };
+    autograd::Variable embed_, final_norm_;
+    std::vector<Layer> layers_;
+    std::map<size_t, std::pair<core::Tensor, core::Tensor>> rope_cache_;
+};
+
+class DataParallel;
+
+struct StepStats
+{
+    float loss = 0.0f;
+    float grad_norm = 0.0f;
+};
+
+class Trainer
+{
+public:
+    Trainer(ModelConfig config, optim::AdamWConfig adam, float max_norm, core::DType dtype,
+            size_t batch, size_t length, uint64_t seed);
+    ~Trainer();
+
+    // One process per GPU: NCCL communicator from a unique id shared by the caller; gradients
+    // are all-reduced in buckets of `bucket_bytes` as soon as the backward finishes them.
+    void init_data_parallel(const void* nccl_unique_id, int rank, int world, size_t bucket_bytes);
+    int world() const noexcept;
+
+    // One training step on device-resident ids/targets (int64 [B*T]); asynchronous.
+    void step(const core::Tensor& ids, const core::Tensor& targets);
+    // One step from host buffers: copies in, steps, reads loss and grad norm back (synchronous).
+    StepStats step_host(const int64_t* ids, const int64_t* targets);
+    // Loss and pre-clip grad norm of the last step (synchronises).
+    StepStats last_stats();
+
+    TinyTransformer& model() noexcept { return *model_; }
+    optim::AdamW& optimizer() noexcept { return *opt_; }
+    size_t batch() const noexcept { return batch_; }
+    size_t length() const noexcept { return length_; }
+
+private:
+    std::unique_ptr<TinyTransformer> model_;
+    std::unique_ptr<optim::AdamW> opt_;
+    std::unique_ptr<DataParallel> dp_;
+    float max_norm_;
+    size_t batch_, length_;
+    core::Tensor ids_, targets_, loss_;
+    core::Tensor pinned_;   // host-side staging is done by the caller; kept for symmetry
+};
+
+} // namespace veda::train

@@ -178,8 +178,9 @@ size_t veda_sumsq_workspace(int64_t n);
 int veda_clip_apply(float* g, int64_t n, const double* sumsq, float max_norm,
                     veda_stream_t stream);
 /* One AdamW step on fp32 master weights:
- *   g' = g * grad_scale (skipped when grad_scale == 1) * clip (as veda_clip_apply; sumsq NULL =
- *   no clip; sumsq is of g * grad_scale when grad_scale != 1 is folded by the caller)
+ *   g' = g * grad_scale (skipped when grad_scale == 1) * clip, where clip is computed as in
+ *   veda_clip_apply from total = sqrt(*sumsq) * grad_scale (sumsq of the unscaled g; NULL = no
+ *   clip) — grad_scale carries the 1/world average of data-parallel training
  *   m = b1 m + (1-b1) g';  v = b2 v + (1-b2) g'^2  (fp32, unfused roundings as the reference)
  *   w -= lr*wd*w;  w -= lr * float((m/bias1) / (sqrt(v/bias2) + eps))  (m_hat, v_hat in double)
  * bias1 = 1 - beta1^t, bias2 = 1 - beta2^t computed by the caller in double.
@@ -226,6 +227,11 @@ int veda_softmax_bwd(const void* y, const void* g, void* dx, int64_t lanes, int6
 /* silu and its backward on n elements (Activations.cpp:13-16, NonLinear.cpp:47-63). */
 int veda_silu_fwd(const void* x, void* y, int64_t n, int dtype, veda_stream_t stream);
 int veda_silu_bwd(const void* x, const void* g, void* dx, int64_t n, int dtype,
+                  veda_stream_t stream);
+/* tanh-GELU and its backward on n elements (src/libs/ops/Activations.cpp:18-26,
+ * src/libs/autograd/NonLinear.cpp:65-87). */
+int veda_gelu_fwd(const void* x, void* y, int64_t n, int dtype, veda_stream_t stream);
+int veda_gelu_bwd(const void* x, const void* g, void* dx, int64_t n, int dtype,
                   veda_stream_t stream);
 /* Row argmax over [rows, n], ties to the lower index, NaN -> *status = VEDA_ERR_INVALID_ARGUMENT
  * (generate::greedy_of, src/libs/generate/Sampling.cpp:97-113). */

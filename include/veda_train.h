@@ -1,0 +1,79 @@
+/*
+ * veda_train.h — C ABI of libveda.so (the C++23 host library) for callers that are not C++:
+ * the Python tests and bench.py bind it with ctypes. It drives veda::train::Trainer — the
+ * reference's training loop (zero_grad, TinyTransformer::forward, cross_entropy, backward,
+ * clip_gradient_norm, AdamW::step; tests/TinyModelTest.cpp:290-299) on one GPU of a
+ * data-parallel job — and exposes the flat parameter / gradient vectors in the reference's
+ * parameter order (src/libs/train/Model.cpp:120-140, GQA k/v shapes [Hkv*Dh, D]).
+ * Every entry point returns 0 or a negative status; veda_train_last_error() has the message
+ * (the C++ exception's what()).
+ */
+#ifndef VEDA_TRAIN_H
+#define VEDA_TRAIN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* veda_stream_t;
+typedef struct veda_trainer veda_trainer;
+
+/* io::ModelConfig's fields (src/libs/io/ModelConfig.h) used by training. */
+typedef struct
+{
+    int64_t vocab, hidden, intermediate, layers, heads, kv_heads, head_dim;
+    float eps, theta;
+} veda_model_config;
+
+/* optim::AdamWConfig (src/libs/optim/AdamW.h:23-30) plus the clip threshold. */
+typedef struct
+{
+    float lr, beta1, beta2, eps, weight_decay, max_norm;
+} veda_optim_config;
+
+const char* veda_train_last_error(void);
+/* Sets the stream every subsequent call of this thread launches on (NULL = default stream). */
+int veda_train_set_stream(veda_stream_t stream);
+
+/* dtype: 0 fp32 (weights, activations, GEMMs in fp32), 1 bf16 (bf16 weights and activations,
+ * fp32 master weights, moments and gradients). Weights ~ N(0, 0.02) from seed, gains 1. */
+int veda_trainer_create(const veda_model_config* model, const veda_optim_config* optim, int dtype,
+                        int64_t batch, int64_t seq_len, uint64_t seed, veda_trainer** out);
+int veda_trainer_destroy(veda_trainer* t);
+int64_t veda_trainer_param_count(const veda_trainer* t);
+/* Host fp32 flat vectors in parameter order. set_params writes the master weights (and their
+ * bf16 rounding into the model in bf16 mode); get_params reads the master weights; get_grads
+ * reads the last step's averaged pre-clip gradients. */
+int veda_trainer_set_params(veda_trainer* t, const float* host);
+int veda_trainer_get_params(veda_trainer* t, float* host);
+int veda_trainer_get_grads(veda_trainer* t, float* host);
+
+/* Data parallel: 128-byte NCCL unique id (made by rank 0, shared by the caller). */
+int veda_nccl_unique_id(void* out128);
+int veda_trainer_init_dp(veda_trainer* t, const void* unique_id128, int rank, int world,
+                         size_t bucket_bytes);
+
+/* One step from host ids/targets (int64 [batch*seq_len], targets = next ids); copies them in,
+ * steps and reads back loss and pre-clip grad norm (synchronous). */
+int veda_trainer_step_host(veda_trainer* t, const int64_t* ids, const int64_t* targets,
+                           float* loss, float* grad_norm);
+/* One step on device-resident ids/targets; asynchronous on the current stream. */
+int veda_trainer_step_device(veda_trainer* t, const int64_t* ids, const int64_t* targets);
+/* Loss and grad norm of the last step (synchronises). */
+int veda_trainer_last_stats(veda_trainer* t, float* loss, float* grad_norm);
+
+/* Device-time profile of kernel classes (gemm_fwd, gemm_dx, gemm_dw, attn_fwd, attn_bwd,
+ * cross_entropy, rmsnorm_bwd, swiglu_bwd, adamw), recorded with CUDA events while enabled. */
+int veda_profile_enable(int on);
+/* Writes up to `cap` entries; returns the number of classes (synchronises; resets the totals). */
+int veda_profile_collect(char (*names)[32], double* ms, double* flops, double* bytes,
+                         uint64_t* launches, int cap);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VEDA_TRAIN_H */

@@ -1,0 +1,122 @@
+"""Parity of the full training step (forward, cross-entropy, backward, clip, AdamW) run by the
+C++ trainer (libveda.so, include/veda_train.h) against the reference.
+
+* fp32, the tiny decoder config: against tests/golden/tiny_step.npz, produced by the reference
+  compiled from its sources (tolerance 1e-4 max-abs-relative per tensor);
+* bf16, Qwen3-shaped (head_dim 128, GQA 2:1, QK-norm, RoPE theta 1e6), reduced width and depth:
+  against the oracle's fp32 step on the same bf16-rounded weights (tolerance 2e-2).
+"""
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import veda_oracle as O
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+ADAM = O.AdamWConfig(1e-3, 0.9, 0.95, 1e-8, 0.1)
+
+
+@pytest.fixture(autouse=True)
+def _gpu(cuda):
+    yield
+
+
+def make_trainer(cfg, dtype, batch, seq_len, seed=0):
+    from veda_b200.train_abi import Trainer
+    return Trainer(cfg, lr=ADAM.learning_rate, betas=(ADAM.beta1, ADAM.beta2), eps=ADAM.eps,
+                   weight_decay=ADAM.weight_decay, max_norm=1.0, dtype=dtype, batch=batch,
+                   seq_len=seq_len, seed=seed)
+
+
+def split(cfg, flat):
+    out, at = [], 0
+    for _, shape in O.param_specs(cfg):
+        n = int(np.prod(shape))
+        out.append(flat[at:at + n].reshape(shape))
+        at += n
+    return out
+
+
+def test_tiny_fp32_step_matches_reference_golden():
+    g = dict(np.load(GOLDEN / "tiny_step.npz"))
+    cfg = O.TINY
+    n = len(O.param_specs(cfg))
+    w0 = np.concatenate([g[f"w0_{i:03d}"].ravel() for i in range(n)])
+    t = make_trainer(cfg, 0, 4, 32)
+    t.set_params(w0)
+    assert np.array_equal(t.get_params(), w0)
+    loss, norm = t.step_host(g["ids"], g["targets"])
+    assert abs(loss - g["loss"][0]) <= 1e-5 * abs(g["loss"][0]), (loss, g["loss"][0])
+    assert abs(norm - g["norm"][0]) <= 1e-4 * g["norm"][0], (norm, g["norm"][0])
+    grads = split(cfg, t.get_grads())
+    w1 = split(cfg, t.get_params())
+    specs = O.param_specs(cfg)
+    worst_g = max((O.max_abs_rel(grads[i], g[f"g_{i:03d}"]), specs[i][0]) for i in range(n))
+    worst_w = max((O.max_abs_rel(w1[i], g[f"w1_{i:03d}"]), specs[i][0]) for i in range(n))
+    assert worst_g[0] <= 1e-4, worst_g
+    # AdamW's g / (|g| + eps) amplifies last-bit gradient differences where |g| ~ eps; the
+    # reference compiled twice with different summation orders differs by the same amount
+    assert worst_w[0] <= 2e-4, worst_w
+    t.close()
+
+
+def test_tiny_fp32_loss_decreases_and_is_log_v_at_init():
+    cfg = O.TINY
+    ids, tg = O.synthetic_batch(cfg, 4, 32, 0)
+    t = make_trainer(cfg, 0, 4, 32)
+    t.set_params(np.concatenate([p.ravel() for p in O.init_params(cfg, 0)]))
+    first, _ = t.step_host(ids, tg)
+    assert abs(first - math.log(cfg.vocab)) < 0.3
+    last = first
+    for _ in range(10):
+        last, norm = t.step_host(ids, tg)
+        assert math.isfinite(norm)
+    assert last < first - 0.05
+    t.close()
+
+
+QWEN_SMALL = O.ModelConfig(vocab=2048, hidden=256, intermediate=512, layers=2, heads=4,
+                           kv_heads=2, head_dim=128, eps=1e-6, theta=1e6)
+
+
+def test_qwen_shaped_bf16_step_matches_oracle():
+    cfg = QWEN_SMALL
+    B, T = 2, 128
+    params = O.init_params(cfg, 3, bf16=True)
+    ids, tg = O.synthetic_batch(cfg, B, T, 3)
+    t = make_trainer(cfg, 1, B, T)
+    t.set_params(np.concatenate([p.ravel() for p in params]))
+    loss, norm = t.step_host(ids, tg)
+    ref = [p.copy() for p in params]
+    opt = O.AdamW(ref, ADAM)
+    rloss, rnorm, rgrads = O.train_step(cfg, ref, ids, tg, 1.0, opt)
+    assert abs(loss - rloss) <= 2e-2 * abs(rloss)
+    assert abs(norm - rnorm) <= 2e-2 * rnorm
+    grads = split(cfg, t.get_grads())
+    w1 = split(cfg, t.get_params())
+    specs = O.param_specs(cfg)
+    errs = sorted(((O.max_abs_rel(grads[i], rgrads[i]), specs[i][0]) for i in range(len(specs))),
+                  reverse=True)
+    assert errs[0][0] <= 2e-2, errs[:4]
+    werrs = max(O.max_abs_rel(w1[i], ref[i]) for i in range(len(specs)))
+    assert werrs <= 2e-2
+    t.close()
+
+
+def test_qwen_06b_full_shape_step_properties():
+    """The Qwen3-0.6B-shaped step at its full size (28 layers, B 4 x T 2048): the CPU oracle
+    cannot run it, so check size-independent properties: initial loss ~ log V, finite grad norm,
+    and a second step on the same batch lowering the loss."""
+    cfg = O.QWEN3_06B
+    B, T = 4, 2048
+    ids, tg = O.synthetic_batch(cfg, B, T, 3)
+    t = make_trainer(cfg, 1, B, T, seed=3)
+    l1, n1 = t.step_host(ids, tg)
+    l2, n2 = t.step_host(ids, tg)
+    assert abs(l1 - math.log(cfg.vocab)) < 0.5, l1
+    assert math.isfinite(n1) and math.isfinite(n2) and n1 > 0
+    assert l2 < l1
+    t.close()

@@ -266,6 +266,37 @@ __global__ void silu_bwd_kernel(const T* __restrict__ x, const T* __restrict__ g
     }
 }
 
+// tanh-GELU: 0.5 x (1 + tanh(c (x + 0.044715 x^3))), c = sqrt(2/pi).
+constexpr float kGeluC = 0.7978845608028654f;
+constexpr float kGeluCubic = 0.044715f;
+
+template <typename T>
+__global__ void gelu_fwd_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t n)
+{
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    {
+        const float v = to_f32(x[i]);
+        y[i] = from_f32<T>(0.5f * v * (1.0f + tanhf(kGeluC * (v + kGeluCubic * v * v * v))));
+    }
+}
+
+template <typename T>
+__global__ void gelu_bwd_kernel(const T* __restrict__ x, const T* __restrict__ g,
+                                T* __restrict__ dx, int64_t n)
+{
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    {
+        const float v = to_f32(x[i]);
+        const float u = kGeluC * (v + kGeluCubic * v * v * v);
+        const float t = tanhf(u);
+        const float d = 0.5f * (1.0f + t) +
+                        0.5f * v * (1.0f - t * t) * kGeluC * (1.0f + 3.0f * kGeluCubic * v * v);
+        dx[i] = from_f32<T>(to_f32(g[i]) * d);
+    }
+}
+
 // Row argmax, ties to the lower index; NaN anywhere in the row flags the status.
 template <typename T>
 __global__ void argmax_kernel(const T* __restrict__ x, int64_t ld, int64_t rows, int64_t n,
@@ -593,6 +624,31 @@ extern "C" int veda_silu_bwd(const void* x, const void* g, void* dx, int64_t n, 
                       static_cast<const T*>(x), static_cast<const T*>(g), static_cast<T*>(dx), n));
     count_launch();
     return check_launch("veda_silu_bwd");
+}
+
+extern "C" int veda_gelu_fwd(const void* x, void* y, int64_t n, int dtype, veda_stream_t stream)
+{
+    VEDA_REQUIRE(valid_dtype(dtype) && n >= 0, "bad arguments");
+    if (n == 0) return VEDA_OK;
+    VEDA_REQUIRE(x && y, "null pointer");
+    VEDA_DISPATCH(dtype, T,
+                  gelu_fwd_kernel<T><<<grid_for(n, 256), 256, 0, stream>>>(
+                      static_cast<const T*>(x), static_cast<T*>(y), n));
+    count_launch();
+    return check_launch("veda_gelu_fwd");
+}
+
+extern "C" int veda_gelu_bwd(const void* x, const void* g, void* dx, int64_t n, int dtype,
+                             veda_stream_t stream)
+{
+    VEDA_REQUIRE(valid_dtype(dtype) && n >= 0, "bad arguments");
+    if (n == 0) return VEDA_OK;
+    VEDA_REQUIRE(x && g && dx, "null pointer");
+    VEDA_DISPATCH(dtype, T,
+                  gelu_bwd_kernel<T><<<grid_for(n, 256), 256, 0, stream>>>(
+                      static_cast<const T*>(x), static_cast<const T*>(g), static_cast<T*>(dx), n));
+    count_launch();
+    return check_launch("veda_gelu_bwd");
 }
 
 extern "C" int veda_argmax(const void* x, int64_t ld, int64_t rows, int64_t n, int64_t* out,

@@ -1,0 +1,252 @@
+// C ABI of libveda.so (include/veda_train.h): exceptions become status codes.
+#include "veda_train.h"
+
+#include "veda/profile.hpp"
+#include "veda/train.hpp"
+
+#include "veda_cuda.h"
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+struct veda_trainer
+{
+    std::unique_ptr<veda::train::Trainer> impl;
+};
+
+namespace
+{
+thread_local std::string g_error;
+
+template <class F>
+int guarded(F&& body)
+{
+    try
+    {
+        body();
+        return VEDA_OK;
+    }
+    catch (const std::out_of_range& e)
+    {
+        g_error = e.what();
+        return VEDA_ERR_OUT_OF_RANGE;
+    }
+    catch (const std::invalid_argument& e)
+    {
+        g_error = e.what();
+        return VEDA_ERR_INVALID_ARGUMENT;
+    }
+    catch (const std::exception& e)
+    {
+        g_error = e.what();
+        return VEDA_ERR_CUDA;
+    }
+}
+
+void cuda_check(cudaError_t e, const char* what)
+{
+    if (e != cudaSuccess)
+    {
+        throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+    }
+}
+
+cudaStream_t cs() { return reinterpret_cast<cudaStream_t>(veda::current_stream()); }
+
+// The fp32 flat vector of master weights: the model's values in fp32 mode, AdamW's master arena
+// in bf16 mode (both contiguous in parameter order).
+void* master_base(veda::train::Trainer& t)
+{
+    return t.model().dtype() == veda::core::DType::F32 ? t.model().value_arena().data_ptr()
+                                                       : t.optimizer().master(0).data_ptr();
+}
+} // namespace
+
+extern "C" {
+
+const char* veda_train_last_error(void) { return g_error.c_str(); }
+
+int veda_train_set_stream(veda_stream_t stream)
+{
+    veda::set_current_stream(stream);
+    return VEDA_OK;
+}
+
+int veda_trainer_create(const veda_model_config* m, const veda_optim_config* o, int dtype,
+                        int64_t batch, int64_t seq_len, uint64_t seed, veda_trainer** out)
+{
+    return guarded([&] {
+        if (m == nullptr || o == nullptr || out == nullptr)
+        {
+            throw std::invalid_argument("veda_trainer_create: null argument");
+        }
+        if (dtype != 0 && dtype != 1)
+        {
+            throw std::invalid_argument("veda_trainer_create: dtype must be 0 (fp32) or 1 (bf16)");
+        }
+        veda::train::ModelConfig c;
+        c.vocab_size = static_cast<size_t>(m->vocab);
+        c.hidden_size = static_cast<size_t>(m->hidden);
+        c.intermediate_size = static_cast<size_t>(m->intermediate);
+        c.num_layers = static_cast<size_t>(m->layers);
+        c.num_heads = static_cast<size_t>(m->heads);
+        c.num_kv_heads = static_cast<size_t>(m->kv_heads);
+        c.head_dim = static_cast<size_t>(m->head_dim);
+        c.max_position_embeddings = 0;   // no context limit for synthetic training
+        c.rms_norm_eps = m->eps;
+        c.rope_theta = m->theta;
+        veda::optim::AdamWConfig a{o->lr, o->beta1, o->beta2, o->eps, o->weight_decay};
+        auto t = std::make_unique<veda_trainer>();
+        t->impl = std::make_unique<veda::train::Trainer>(
+            c, a, o->max_norm, dtype == 1 ? veda::core::DType::BF16 : veda::core::DType::F32,
+            static_cast<size_t>(batch), static_cast<size_t>(seq_len), seed);
+        *out = t.release();
+    });
+}
+
+int veda_trainer_destroy(veda_trainer* t)
+{
+    return guarded([&] {
+        if (t != nullptr)
+        {
+            cuda_check(cudaStreamSynchronize(cs()), "veda_trainer_destroy");
+            delete t;
+        }
+    });
+}
+
+int64_t veda_trainer_param_count(const veda_trainer* t)
+{
+    return t ? static_cast<int64_t>(t->impl->model().parameter_count()) : -1;
+}
+
+int veda_trainer_set_params(veda_trainer* t, const float* host)
+{
+    return guarded([&] {
+        auto& tr = *t->impl;
+        const size_t n = tr.model().parameter_count();
+        void* master = master_base(tr);
+        cuda_check(cudaMemcpyAsync(master, host, n * sizeof(float), cudaMemcpyHostToDevice, cs()),
+                   "veda_trainer_set_params");
+        if (tr.model().dtype() == veda::core::DType::BF16)
+        {
+            veda::check(veda_f32_to_bf16(static_cast<const float*>(master),
+                                         tr.model().value_arena().data_ptr(),
+                                         static_cast<int64_t>(n), veda::current_stream()),
+                        "veda_trainer_set_params");
+        }
+        cuda_check(cudaStreamSynchronize(cs()), "veda_trainer_set_params");
+    });
+}
+
+int veda_trainer_get_params(veda_trainer* t, float* host)
+{
+    return guarded([&] {
+        auto& tr = *t->impl;
+        cuda_check(cudaMemcpyAsync(host, master_base(tr),
+                                   tr.model().parameter_count() * sizeof(float),
+                                   cudaMemcpyDeviceToHost, cs()),
+                   "veda_trainer_get_params");
+        cuda_check(cudaStreamSynchronize(cs()), "veda_trainer_get_params");
+    });
+}
+
+int veda_trainer_get_grads(veda_trainer* t, float* host)
+{
+    return guarded([&] {
+        auto& tr = *t->impl;
+        cuda_check(cudaMemcpyAsync(host, tr.model().grad_arena().data_ptr(),
+                                   tr.model().parameter_count() * sizeof(float),
+                                   cudaMemcpyDeviceToHost, cs()),
+                   "veda_trainer_get_grads");
+        cuda_check(cudaStreamSynchronize(cs()), "veda_trainer_get_grads");
+    });
+}
+
+int veda_nccl_unique_id(void* out128)
+{
+    return guarded([&] {
+        ncclUniqueId id;
+        if (ncclGetUniqueId(&id) != ncclSuccess)
+        {
+            throw std::runtime_error("ncclGetUniqueId failed");
+        }
+        static_assert(sizeof(id) == 128, "NCCL unique id is 128 bytes");
+        std::memcpy(out128, &id, sizeof(id));
+    });
+}
+
+int veda_trainer_init_dp(veda_trainer* t, const void* unique_id128, int rank, int world,
+                         size_t bucket_bytes)
+{
+    return guarded([&] { t->impl->init_data_parallel(unique_id128, rank, world, bucket_bytes); });
+}
+
+int veda_trainer_step_host(veda_trainer* t, const int64_t* ids, const int64_t* targets,
+                           float* loss, float* grad_norm)
+{
+    return guarded([&] {
+        const auto s = t->impl->step_host(ids, targets);
+        if (loss) *loss = s.loss;
+        if (grad_norm) *grad_norm = s.grad_norm;
+    });
+}
+
+int veda_trainer_step_device(veda_trainer* t, const int64_t* ids, const int64_t* targets)
+{
+    return guarded([&] {
+        auto& tr = *t->impl;
+        const size_t n = tr.batch() * tr.length();
+        auto wrap = [&](const int64_t* p) {
+            auto storage = std::make_shared<veda::core::Storage>(const_cast<int64_t*>(p),
+                                                                 n * sizeof(int64_t));
+            return veda::core::Tensor::view(storage, 0, veda::core::Shape({2 * n}),
+                                            veda::core::DType::F32);
+        };
+        tr.step(wrap(ids), wrap(targets));
+    });
+}
+
+int veda_trainer_last_stats(veda_trainer* t, float* loss, float* grad_norm)
+{
+    return guarded([&] {
+        const auto s = t->impl->last_stats();
+        if (loss) *loss = s.loss;
+        if (grad_norm) *grad_norm = s.grad_norm;
+    });
+}
+
+int veda_profile_enable(int on)
+{
+    veda::profile::enable(on != 0);
+    return VEDA_OK;
+}
+
+int veda_profile_collect(char (*names)[32], double* ms, double* flops, double* bytes,
+                         uint64_t* launches, int cap)
+{
+    int count = 0;
+    const int rc = guarded([&] {
+        const auto totals = veda::profile::collect(true);
+        for (const auto& [name, t] : totals)
+        {
+            if (count < cap)
+            {
+                std::strncpy(names[count], name.c_str(), 31);
+                names[count][31] = '\0';
+                ms[count] = t.ms;
+                flops[count] = t.flops;
+                bytes[count] = t.bytes;
+                launches[count] = t.launches;
+            }
+            ++count;
+        }
+    });
+    return rc == VEDA_OK ? count : rc;
+}
+
+} // extern "C"

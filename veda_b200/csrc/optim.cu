@@ -81,13 +81,20 @@ __global__ void sumsq_final_kernel(const double* __restrict__ partials, int coun
     }
 }
 
-__device__ __forceinline__ float clip_scale(const double* sumsq, float max_norm)
+// total = sqrt(sumsq) * grad_scale: the norm of the gradient after the grad_scale factor (the
+// 1/world average of data-parallel training) has been applied.
+__device__ __forceinline__ float clip_scale(const double* sumsq, float max_norm,
+                                            float grad_scale = 1.0f)
 {
     if (sumsq == nullptr)
     {
         return 1.0f;
     }
-    const double total = sqrt(*sumsq);
+    double total = sqrt(*sumsq);
+    if (grad_scale != 1.0f)
+    {
+        total *= fabs(static_cast<double>(grad_scale));
+    }
     if (!isfinite(total) || total <= static_cast<double>(max_norm))
     {
         return 1.0f;
@@ -135,7 +142,7 @@ adamw_kernel(float* __restrict__ master, float* __restrict__ m, float* __restric
              float* __restrict__ g, bf16* __restrict__ lowp, int64_t n,
              const double* __restrict__ sumsq, AdamArgs a, bool vec)
 {
-    const float clip = clip_scale(sumsq, a.max_norm);
+    const float clip = clip_scale(sumsq, a.max_norm, a.grad_scale);
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     const int64_t n4 = vec ? n / 4 : 0;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;

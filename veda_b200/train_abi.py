@@ -1,0 +1,157 @@
+"""ctypes binding of include/veda_train.h (libveda.so) and a thin Python handle around it, used
+by the tests and bench.py. The training step itself runs in the C++ library."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+_p, _i, _i64, _f, _sz, _u64 = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t, C.c_uint64
+
+
+class ModelConfig(C.Structure):
+    _fields_ = [("vocab", _i64), ("hidden", _i64), ("intermediate", _i64), ("layers", _i64),
+                ("heads", _i64), ("kv_heads", _i64), ("head_dim", _i64), ("eps", _f),
+                ("theta", _f)]
+
+
+class OptimConfig(C.Structure):
+    _fields_ = [("lr", _f), ("beta1", _f), ("beta2", _f), ("eps", _f), ("weight_decay", _f),
+                ("max_norm", _f)]
+
+
+SIGNATURES = {
+    "veda_train_last_error": (C.c_char_p, []),
+    "veda_train_set_stream": (_i, [_p]),
+    "veda_trainer_create": (_i, [C.POINTER(ModelConfig), C.POINTER(OptimConfig), _i, _i64, _i64,
+                                 _u64, C.POINTER(_p)]),
+    "veda_trainer_destroy": (_i, [_p]),
+    "veda_trainer_param_count": (_i64, [_p]),
+    "veda_trainer_set_params": (_i, [_p, _p]),
+    "veda_trainer_get_params": (_i, [_p, _p]),
+    "veda_trainer_get_grads": (_i, [_p, _p]),
+    "veda_nccl_unique_id": (_i, [_p]),
+    "veda_trainer_init_dp": (_i, [_p, _p, _i, _i, _sz]),
+    "veda_trainer_step_host": (_i, [_p, _p, _p, _p, _p]),
+    "veda_trainer_step_device": (_i, [_p, _p, _p]),
+    "veda_trainer_last_stats": (_i, [_p, _p, _p]),
+    "veda_profile_enable": (_i, [_i]),
+    "veda_profile_collect": (_i, [_p, _p, _p, _p, _p, _i]),
+}
+
+
+def load(path):
+    L = C.CDLL(str(path))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    return L
+
+
+class TrainError(RuntimeError):
+    pass
+
+
+def _check(L, rc):
+    if rc < 0:
+        msg = L.veda_train_last_error().decode(errors="replace")
+        if rc == -5:
+            raise IndexError(msg)
+        if rc == -1:
+            raise ValueError(msg)
+        raise TrainError(f"[{rc}] {msg}")
+    return rc
+
+
+class Trainer:
+    """A veda::train::Trainer on the current CUDA device (C++ object behind the C ABI)."""
+
+    def __init__(self, cfg, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, max_norm=1.0,
+                 dtype=1, batch=1, seq_len=1, seed=0, stream=None):
+        from . import host_lib
+        self.L = host_lib()
+        if stream is not None:
+            _check(self.L, self.L.veda_train_set_stream(stream))
+        m = ModelConfig(cfg.vocab, cfg.hidden, cfg.intermediate, cfg.layers, cfg.heads,
+                        cfg.kv_heads, cfg.head_dim, cfg.eps, cfg.theta)
+        o = OptimConfig(lr, betas[0], betas[1], eps, weight_decay, max_norm)
+        h = _p()
+        _check(self.L, self.L.veda_trainer_create(C.byref(m), C.byref(o), dtype, batch, seq_len,
+                                                  seed, C.byref(h)))
+        self.h = h
+        self.batch, self.seq_len = batch, seq_len
+        self.n = int(self.L.veda_trainer_param_count(h))
+
+    def close(self):
+        if self.h:
+            _check(self.L, self.L.veda_trainer_destroy(self.h))
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_params(self, flat: np.ndarray):
+        flat = np.ascontiguousarray(flat, dtype=np.float32)
+        assert flat.size == self.n
+        _check(self.L, self.L.veda_trainer_set_params(self.h, flat.ctypes.data))
+
+    def get_params(self) -> np.ndarray:
+        out = np.empty(self.n, np.float32)
+        _check(self.L, self.L.veda_trainer_get_params(self.h, out.ctypes.data))
+        return out
+
+    def get_grads(self) -> np.ndarray:
+        out = np.empty(self.n, np.float32)
+        _check(self.L, self.L.veda_trainer_get_grads(self.h, out.ctypes.data))
+        return out
+
+    def init_dp(self, unique_id: bytes, rank: int, world: int, bucket_bytes=25 << 20):
+        buf = C.create_string_buffer(bytes(unique_id), 128)
+        _check(self.L, self.L.veda_trainer_init_dp(self.h, buf, rank, world, bucket_bytes))
+
+    def step_host(self, ids: np.ndarray, targets: np.ndarray):
+        ids = np.ascontiguousarray(ids, dtype=np.int64)
+        targets = np.ascontiguousarray(targets, dtype=np.int64)
+        loss, norm = C.c_float(0), C.c_float(0)
+        _check(self.L, self.L.veda_trainer_step_host(self.h, ids.ctypes.data, targets.ctypes.data,
+                                                     C.byref(loss), C.byref(norm)))
+        return float(loss.value), float(norm.value)
+
+    def step_device(self, ids_ptr: int, targets_ptr: int):
+        _check(self.L, self.L.veda_trainer_step_device(self.h, ids_ptr, targets_ptr))
+
+    def last_stats(self):
+        loss, norm = C.c_float(0), C.c_float(0)
+        _check(self.L, self.L.veda_trainer_last_stats(self.h, C.byref(loss), C.byref(norm)))
+        return float(loss.value), float(norm.value)
+
+
+def nccl_unique_id() -> bytes:
+    from . import host_lib
+    L = host_lib()
+    buf = C.create_string_buffer(128)
+    _check(L, L.veda_nccl_unique_id(buf))
+    return buf.raw
+
+
+def profile_enable(on: bool):
+    from . import host_lib
+    host_lib().veda_profile_enable(1 if on else 0)
+
+
+def profile_collect():
+    """{class: (ms, flops, bytes, launches)} since the last collect (synchronises)."""
+    from . import host_lib
+    L = host_lib()
+    cap = 64
+    names = (C.c_char * 32 * cap)()
+    ms = (C.c_double * cap)()
+    fl = (C.c_double * cap)()
+    by = (C.c_double * cap)()
+    la = (C.c_uint64 * cap)()
+    n = _check(L, L.veda_profile_collect(names, ms, fl, by, la, cap))
+    return {names[i].value.decode(): (ms[i], fl[i], by[i], int(la[i])) for i in range(min(n, cap))}
