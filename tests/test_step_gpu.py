@@ -101,8 +101,21 @@ def test_qwen_shaped_bf16_step_matches_oracle():
     errs = sorted(((O.max_abs_rel(grads[i], rgrads[i]), specs[i][0]) for i in range(len(specs))),
                   reverse=True)
     assert errs[0][0] <= 2e-2, errs[:4]
-    werrs = max(O.max_abs_rel(w1[i], ref[i]) for i in range(len(specs)))
-    assert werrs <= 2e-2
+    # Updated weights. AdamW's first step moves every element by about lr * sign(g), so an
+    # element whose gradient is below bf16 resolution can take the opposite sign on the GPU and
+    # land 2*lr away from the fp32 reference (measured: 0.2-0.8% of elements per tensor, which
+    # puts the per-tensor max-abs-relative error at up to 2.4e-2 for matrices with |w| ~ 0.09).
+    # Checked: the difference never exceeds those flips, flips are rare, and apart from them the
+    # weights agree to 2e-2.
+    lr = ADAM.learning_rate
+    for i in range(len(specs)):
+        dw_gpu, dw_ref = w1[i] - params[i], ref[i] - params[i]
+        flips = np.sign(dw_gpu) != np.sign(dw_ref)
+        assert np.max(np.abs(dw_gpu - dw_ref)) <= 2.02 * lr, specs[i][0]
+        assert flips.mean() <= 0.01, (specs[i][0], flips.mean())
+        keep = ~flips
+        den = np.abs(ref[i]).max()
+        assert np.max(np.abs(w1[i] - ref[i])[keep], initial=0.0) <= 2e-2 * den, specs[i][0]
     t.close()
 
 

@@ -54,6 +54,25 @@ void cuda_check(cudaError_t err, const char* what)
 }
 
 cudaStream_t cs() { return reinterpret_cast<cudaStream_t>(current_stream()); }
+
+// The stream-ordered pool gives memory back to the system at every synchronisation unless told
+// to keep it; a training step allocates the same working set every time, so keep all of it.
+void configure_pool_once()
+{
+    static bool done[64] = {false};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64 || done[device])
+    {
+        return;
+    }
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess)
+    {
+        uint64_t threshold = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
+    }
+    done[device] = true;
+}
 } // namespace
 
 size_t dtype_size(DType d) { return d == DType::BF16 ? 2 : 4; }
@@ -108,6 +127,7 @@ Storage::Storage(size_t bytes, bool zero) : bytes_(bytes)
     {
         return;
     }
+    configure_pool_once();
     cuda_check(cudaMallocAsync(&data_, bytes, cs()), "Storage: cudaMallocAsync");
     if (zero)
     {
