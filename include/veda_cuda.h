@@ -98,6 +98,22 @@ int veda_rmsnorm_bwd(const void* x, int64_t ldx, const void* gamma, const void* 
                      void* workspace, size_t workspace_bytes, int64_t rows, int64_t n, float eps,
                      int dtype, veda_stream_t stream);
 size_t veda_rmsnorm_bwd_workspace(int64_t rows, int64_t n);
+/* veda_rmsnorm_bwd for callers that cannot allocate device memory. No counterpart in the
+ * reference (its CPU loop needs no scratch); it exists because a workspace costs a cudaMalloc,
+ * which synchronises the device and can fail under an engine that reserves its memory up front,
+ * and because a caller binding this library through a plain C ABI may have no device allocator.
+ * Its scratch (the per-block partial sums of dgamma) is a fixed 4 MiB array compiled into the
+ * library: every GPU that loads the library holds it until the process exits. Limit: the
+ * scratch needed, veda_rmsnorm_bwd_workspace(rows, n) bytes, must be at most 4 MiB (rows of up
+ * to 3542 elements on a 148-SM B200); larger sizes are rejected with VEDA_ERR_INVALID_ARGUMENT.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture. All calls share the one array, so calls that
+ * overlap on the GPU (on different streams without ordering) race; calls ordered on one stream
+ * do not (each call overwrites the partials it reads). Allocates nothing. */
+int veda_rmsnorm_bwd_noalloc(const void* x, int64_t ldx, const void* gamma, const void* dy,
+                             int64_t lddy, const void* dresid, int64_t ldr, void* dx,
+                             int64_t lddx, float* dgamma, int64_t rows, int64_t n, float eps,
+                             int dtype, veda_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------- */
 /* QK-norm + RoPE, per head over head_dim (Model.cpp:171-178): y = rope(gamma * x / r).       */

@@ -44,6 +44,8 @@ SIGNATURES = {
     "veda_rmsnorm_bwd": (_i, [_p, _i64, _p, _p, _i64, _p, _i64, _p, _i64, _p, _p, _sz, _i64,
                               _i64, _f, _i, _p]),
     "veda_rmsnorm_bwd_workspace": (_sz, [_i64, _i64]),
+    "veda_rmsnorm_bwd_noalloc": (_i, [_p, _i64, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i64,
+                                      _f, _i, _p]),
     "veda_qknorm_rope_fwd": (_i, [_p, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f,
                                   _i, _p]),
     "veda_qknorm_rope_bwd": (_i, [_p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _p, _sz, _i64,

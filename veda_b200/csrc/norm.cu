@@ -14,6 +14,7 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace veda::cuda
 {
@@ -708,4 +709,83 @@ extern "C" int veda_rope(const void* x, void* y, const float* cosv, const float*
     }
     count_launch();
     return check_launch("veda_rope");
+}
+
+// ---- RMSNorm backward without allocation --------------------------------------------------
+// Some callers cannot hand veda_rmsnorm_bwd a workspace: cudaMalloc synchronises the whole device
+// (a stall in the middle of a pipelined training step) and fails or fragments memory under an
+// engine that reserves its device memory up front, and a caller binding this library through a
+// plain C ABI (Go via cgo, Java via JNI) may have no allocator of its own on the device.
+// veda_rmsnorm_bwd_noalloc takes its scratch — the per-block partial sums of the gain gradient —
+// from a fixed array compiled into this library instead.
+namespace
+{
+// 1 Mi floats = 4 MiB, reserved on every GPU that loads the library, until the process exits.
+constexpr size_t kNoAllocScratchFloats = size_t{1} << 20;
+static __device__ __align__(256) float g_rmsnorm_bwd_scratch[kNoAllocScratchFloats];
+
+// Device address of the array for the current device, looked up on the first call made on
+// that device. Host code cannot use the array's name as a device pointer (on the host it names a
+// host-side shadow), so the address is obtained with cudaGetSymbolAddress while the device is
+// current and cached per device.
+float* rmsnorm_scratch_for_current_device(int* status)
+{
+    static std::mutex mu;
+    static float* cached[64] = {nullptr};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
+    {
+        *status = fail(VEDA_ERR_CUDA, "veda_rmsnorm_bwd_noalloc: no current CUDA device");
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached[device] == nullptr)
+    {
+        void* p = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&p, g_rmsnorm_bwd_scratch);
+        if (err != cudaSuccess || p == nullptr)
+        {
+            *status = fail(VEDA_ERR_CUDA, std::string("veda_rmsnorm_bwd_noalloc: "
+                                                      "cudaGetSymbolAddress failed: ") +
+                                              cudaGetErrorString(err));
+            return nullptr;
+        }
+        cached[device] = static_cast<float*>(p);
+    }
+    return cached[device];
+}
+} // namespace
+
+extern "C" int veda_rmsnorm_bwd_noalloc(const void* x, int64_t ldx, const void* gamma,
+                                        const void* dy, int64_t lddy, const void* dresid,
+                                        int64_t ldr, void* dx, int64_t lddx, float* dgamma,
+                                        int64_t rows, int64_t n, float eps, int dtype,
+                                        veda_stream_t stream)
+{
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+    if (dgamma != nullptr && rows > 0 && n > 0)
+    {
+        const size_t need = veda_rmsnorm_bwd_workspace(rows, n);
+        const size_t have = kNoAllocScratchFloats * sizeof(float);
+        if (need > have)
+        {
+            return fail(VEDA_ERR_INVALID_ARGUMENT,
+                        "veda_rmsnorm_bwd_noalloc: rows of " + std::to_string(n) +
+                            " need " + std::to_string(need) +
+                            " bytes of gain-gradient scratch, above the fixed " +
+                            std::to_string(have) + " (use veda_rmsnorm_bwd with a workspace)");
+        }
+        int status = VEDA_OK;
+        scratch = rmsnorm_scratch_for_current_device(&status);
+        if (scratch == nullptr)
+        {
+            return status;
+        }
+        scratch_bytes = have;
+    }
+    // Each block writes its own partial sums in full before the reduction reads them, so the
+    // scratch needs no clearing between calls.
+    return veda_rmsnorm_bwd(x, ldx, gamma, dy, lddy, dresid, ldr, dx, lddx, dgamma, scratch,
+                            scratch_bytes, rows, n, eps, dtype, stream);
 }
