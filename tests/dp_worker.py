@@ -1,0 +1,67 @@
+"""One rank of the 2-GPU data-parallel parity check (launched by tests/test_dp.py under torchrun).
+
+Each rank trains the Qwen3-shaped bf16 decoder through the C++ trainer on its own micro-batch
+(B 2 x T 128) with the library's NCCL bucketed all-reduce (small 1 MB buckets, so many are in
+flight during the backward). Rank 0 compares the averaged gradient with the oracle's gradient of
+the full batch (both micro-batches, B 4) and every rank checks that the updated weights are the
+same on both ranks."""
+import datetime
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+
+
+def main():
+    import torch
+    import torch.distributed as dist
+    from oracle import veda_oracle as O
+    from veda_b200 import train_abi as TA
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    cfg = O.ModelConfig(vocab=2048, hidden=256, intermediate=512, layers=2, heads=4, kv_heads=2,
+                        head_dim=128, eps=1e-6, theta=1e6)
+    B, T = 2, 128
+    params = O.init_params(cfg, 3, bf16=True)
+    ids, tg = O.synthetic_batch(cfg, B * world, T, 7)
+    mine = slice(B * rank, B * rank + B)
+    t = TA.Trainer(cfg, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, max_norm=1.0,
+                   dtype=1, batch=B, seq_len=T, seed=3)
+    t.set_params(np.concatenate([p.ravel() for p in params]))
+    uid = [TA.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    t.init_dp(uid[0], rank, world, 1 << 20)
+    loss, norm = t.step_host(ids[mine], tg[mine])
+    grads_sum = t.get_grads()
+    w = t.get_params()
+    # identical weights on every rank
+    wt = torch.from_numpy(w.astype(np.float64))
+    w0 = wt.clone()
+    dist.broadcast(w0, src=0)
+    assert torch.equal(wt, w0), "ranks diverged"
+    if rank == 0:
+        ref = [p.copy() for p in params]
+        _, rnorm, rgrads = O.train_step(cfg, ref, ids, tg, 1.0,
+                                        O.AdamW(ref, O.AdamWConfig(1e-3, 0.9, 0.95, 1e-8, 0.1)))
+        avg = grads_sum / world
+        at, worst = 0, 0.0
+        for g in rgrads:
+            worst = max(worst, O.max_abs_rel(avg[at:at + g.size].reshape(g.shape), g))
+            at += g.size
+        assert worst <= 2e-2, worst
+        assert abs(norm - rnorm) <= 2e-2 * rnorm, (norm, rnorm)
+        print(f"DP OK worst grad err {worst:.2e} norm {norm:.4f} vs {rnorm:.4f}", flush=True)
+    dist.barrier()
+    t.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
