@@ -169,7 +169,7 @@ def run_reference(args):
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -317,14 +317,28 @@ def run_veda(args):
             line["cpu_baseline"] = {"value": None, "unit": "tokens/s", "cores": 0,
                                     "kind": "reference", "sample": f"unavailable: {e}"}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     tr.close()
     if world > 1:
         dist.destroy_process_group()
     return 0
 
 
+_JSON_OUT = None
+
+
+def emit(line: dict):
+    """Writes the one JSON line to the real stdout (everything else goes to stderr)."""
+    os.write(_JSON_OUT if _JSON_OUT is not None else 1, (json.dumps(line) + "\n").encode())
+
+
 def main():
+    global _JSON_OUT
+    # Libraries (NCCL, torch.distributed) may print to stdout from native code; keep stdout for
+    # the JSON line alone by pointing fd 1 at stderr and keeping a private copy of the original.
+    sys.stdout.flush()
+    _JSON_OUT = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
