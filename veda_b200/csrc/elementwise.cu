@@ -40,6 +40,34 @@ __global__ void binary_kernel(int op, const T* __restrict__ a, const T* __restri
     }
 }
 
+// Same-shape contiguous operands (the residual add): 16-byte vectors, no index arithmetic.
+template <typename T>
+__global__ void binary_dense_kernel(int op, const T* __restrict__ a, const T* __restrict__ b,
+                                    T* __restrict__ out, int64_t n)
+{
+    constexpr int V = Vec16<T>::N;
+    const int64_t nv = n / V;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nv;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    {
+        float x[V], y[V];
+        load16(a + i * V, x);
+        load16(b + i * V, y);
+#pragma unroll
+        for (int j = 0; j < V; ++j)
+        {
+            x[j] = op == 0 ? x[j] + y[j] : x[j] * y[j];
+        }
+        store16(out + i * V, x);
+    }
+    for (int64_t i = nv * V + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    {
+        const float x = to_f32(a[i]), y = to_f32(b[i]);
+        out[i] = from_f32<T>(op == 0 ? x + y : x * y);
+    }
+}
+
 template <typename T>
 __global__ void scale_kernel(const T* __restrict__ x, float s, T* __restrict__ out, int64_t n)
 {
@@ -448,6 +476,23 @@ extern "C" int veda_binary(int op, const void* a, const int64_t* a_strides, cons
     if (rc != VEDA_OK) return rc;
     if (total == 0) return VEDA_OK;
     VEDA_REQUIRE(a && b && out, "null pointer");
+    bool dense = aligned16(a) && aligned16(b) && aligned16(out);
+    int64_t expect = 1;
+    for (int k = rank - 1; k >= 0 && dense; --k)
+    {
+        dense = d.shape[k] == 1 || (d.sa[k] == expect && d.sb[k] == expect);
+        expect *= d.shape[k];
+    }
+    if (dense)
+    {
+        const int64_t v = 16 / static_cast<int64_t>(dtype_size(dtype));
+        VEDA_DISPATCH(dtype, T,
+                      binary_dense_kernel<T><<<grid_for(total / v + 1, 256, 4), 256, 0, stream>>>(
+                          op, static_cast<const T*>(a), static_cast<const T*>(b),
+                          static_cast<T*>(out), total));
+        count_launch();
+        return check_launch("veda_binary");
+    }
     VEDA_DISPATCH(dtype, T,
                   binary_kernel<T><<<grid_for(total, 256), 256, 0, stream>>>(
                       op, static_cast<const T*>(a), static_cast<const T*>(b),

@@ -564,11 +564,12 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int
     return check_launch("veda_gemm (tcgen05)");
 }
 
-// Picks a split-K factor (fp32 output only) that best fills whole waves of SMs.
+// Picks a split-K factor (fp32 output only) that best fills whole waves of SMs: the fraction of
+// SM-time doing useful tiles, less a small charge per extra split for its atomic traffic.
 int choose_splits(int tiles, int kblocks, bool allowed)
 {
     const int sms = sm_count();
-    if (!allowed || tiles >= sms)
+    if (!allowed)
     {
         return 1;
     }
@@ -577,7 +578,7 @@ int choose_splits(int tiles, int kblocks, bool allowed)
     for (int s = 1; s <= 8; ++s)
     {
         const int per = (kblocks + s - 1) / s;
-        if (per < 4 || (s - 1) * per >= kblocks)
+        if (s > 1 && (per < 8 || (s - 1) * per >= kblocks))
         {
             break;
         }

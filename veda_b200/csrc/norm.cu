@@ -230,21 +230,394 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ g
     }
 }
 
-// dgamma[i] += sum over blocks b (in order) of partials[b][i]
-__global__ void reduce_partials_kernel(const float* __restrict__ partials, int blocks, int n,
-                                       float* __restrict__ dgamma)
+// dgamma[i] += sum over blocks of partials[b][i], in a fixed order: 32 columns x 8 row groups
+// per CTA, group k summing blocks k, k+8, ... in ascending order, then the 8 groups in order.
+__global__ void __launch_bounds__(256)
+reduce_partials_kernel(const float* __restrict__ partials, int blocks, int n,
+                       float* __restrict__ dgamma)
 {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n)
+    __shared__ float part[8][33];
+    const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
+    const int col = blockIdx.x * 32 + lane;
+    float acc = 0.0f;
+    if (col < n)
     {
-        return;
+        for (int b = grp; b < blocks; b += 8)
+        {
+            acc += partials[static_cast<size_t>(b) * n + col];
+        }
     }
-    float s = 0.0f;
-    for (int b = 0; b < blocks; ++b)
+    part[grp][lane] = acc;
+    __syncthreads();
+    if (grp == 0 && col < n)
     {
-        s += partials[static_cast<size_t>(b) * n + i];
+        float s = 0.0f;
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+        {
+            s += part[g][lane];
+        }
+        dgamma[col] += s;
     }
-    dgamma[i] += s;
+}
+
+inline void launch_reduce_partials(const float* partials, int blocks, int n, float* dgamma,
+                                   cudaStream_t s)
+{
+    reduce_partials_kernel<<<(n + 31) / 32, 256, 0, s>>>(partials, blocks, n, dgamma);
+    count_launch();
+}
+
+// ---- register-resident row kernels (n == CH * 32 * V, 16-byte aligned rows) ------------------
+// Every 16-byte chunk of a row is loaded before any is used, so a warp keeps the whole row in
+// flight instead of one dependent load at a time; the row is then reused from registers.
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& raw, float (&out)[16 / sizeof(T)])
+{
+    if constexpr (sizeof(T) == 4)
+    {
+        out[0] = __uint_as_float(raw.x);
+        out[1] = __uint_as_float(raw.y);
+        out[2] = __uint_as_float(raw.z);
+        out[3] = __uint_as_float(raw.w);
+    }
+    else
+    {
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+        {
+            out[2 * i] = __uint_as_float(w[i] << 16);
+            out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        }
+    }
+}
+
+template <typename T, int CH>
+__global__ void __launch_bounds__(kWarps * 32)
+rmsnorm_fwd_reg_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ gamma,
+                       T* __restrict__ y, int64_t ldy, int64_t rows, float eps)
+{
+    constexpr int V = Vec16<T>::N;
+    constexpr int n = CH * 32 * V;
+    const int lane = threadIdx.x & 31;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5); row < rows;
+         row += stride)
+    {
+        uint4 xr[CH];
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+        {
+            xr[c] = *reinterpret_cast<const uint4*>(x + row * ldx + (c * 32 + lane) * V);
+        }
+        float ss = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+        {
+            float v[V];
+            unpack16<T>(xr[c], v);
+#pragma unroll
+            for (int j = 0; j < V; ++j)
+            {
+                ss += v[j] * v[j];
+            }
+        }
+        ss = warp_sum(ss);
+        const float r = sqrtf(ss / static_cast<float>(n) + eps);
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+        {
+            float v[V], g[V];
+            unpack16<T>(xr[c], v);
+            if (gamma != nullptr)
+            {
+                load16(gamma + (c * 32 + lane) * V, g);
+            }
+#pragma unroll
+            for (int j = 0; j < V; ++j)
+            {
+                const float t = v[j] / r;
+                v[j] = gamma != nullptr ? t * g[j] : t;
+            }
+            store16(y + row * ldy + (c * 32 + lane) * V, v);
+        }
+    }
+}
+
+// Shared memory (when partials != null): [kWarps][n] fp32, one gain-gradient row per warp.
+template <typename T, int CH>
+__global__ void __launch_bounds__(kWarps * 32)
+rmsnorm_bwd_reg_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ gamma,
+                       const T* __restrict__ dy, int64_t lddy, const T* __restrict__ dresid,
+                       int64_t ldr, T* __restrict__ dx, int64_t lddx,
+                       float* __restrict__ partials, int64_t rows, float eps)
+{
+    constexpr int V = Vec16<T>::N;
+    constexpr int n = CH * 32 * V;
+    extern __shared__ float smem[];
+    const int lane = threadIdx.x & 31;
+    const int wid = threadIdx.x >> 5;
+    float acc[CH][V];
+#pragma unroll
+    for (int c = 0; c < CH; ++c)
+#pragma unroll
+        for (int j = 0; j < V; ++j) acc[c][j] = 0.0f;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + wid; row < rows; row += stride)
+    {
+        uint4 xr[CH], gr[CH], rr[CH];
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+        {
+            const int64_t col = (c * 32 + lane) * V;
+            xr[c] = *reinterpret_cast<const uint4*>(x + row * ldx + col);
+            gr[c] = *reinterpret_cast<const uint4*>(dy + row * lddy + col);
+            if (dresid != nullptr)
+            {
+                rr[c] = *reinterpret_cast<const uint4*>(dresid + row * ldr + col);
+            }
+        }
+        float ss = 0.0f, w = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+        {
+            float xv[V], gv[V], gm[V];
+            unpack16<T>(xr[c], xv);
+            unpack16<T>(gr[c], gv);
+            if (gamma != nullptr)
+            {
+                load16(gamma + (c * 32 + lane) * V, gm);
+            }
+#pragma unroll
+            for (int j = 0; j < V; ++j)
+            {
+                const float G = gamma != nullptr ? gv[j] * gm[j] : gv[j];
+                ss += xv[j] * xv[j];
+                w += G * xv[j];
+            }
+        }
+        ss = warp_sum(ss);
+        w = warp_sum(w);
+        const float nf = static_cast<float>(n);
+        const float r = sqrtf(ss / nf + eps);
+        const float coupling = w / (nf * r * r * r);
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+        {
+            float xv[V], gv[V], gm[V], res[V];
+            unpack16<T>(xr[c], xv);
+            unpack16<T>(gr[c], gv);
+            if (gamma != nullptr)
+            {
+                load16(gamma + (c * 32 + lane) * V, gm);
+            }
+            if (dresid != nullptr)
+            {
+                unpack16<T>(rr[c], res);
+            }
+#pragma unroll
+            for (int j = 0; j < V; ++j)
+            {
+                const float G = gamma != nullptr ? gv[j] * gm[j] : gv[j];
+                float d = G / r - xv[j] * coupling;
+                if (dresid != nullptr)
+                {
+                    d = res[j] + d;
+                }
+                acc[c][j] += gv[j] * (xv[j] / r);
+                xv[j] = d;
+            }
+            store16(dx + row * lddx + (c * 32 + lane) * V, xv);
+        }
+    }
+    if (partials != nullptr)
+    {
+        float* mine = smem + static_cast<size_t>(wid) * n;
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+#pragma unroll
+            for (int j = 0; j < V; ++j) mine[(c * 32 + lane) * V + j] = acc[c][j];
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += blockDim.x)
+        {
+            float s = 0.0f;
+            for (int k = 0; k < kWarps; ++k)
+            {
+                s += smem[static_cast<size_t>(k) * n + i];
+            }
+            partials[static_cast<size_t>(blockIdx.x) * n + i] = s;
+        }
+    }
+}
+
+// ---- QK-norm + RoPE, head_dim 128, bf16: eight lanes per (token, head) row ---------------------
+// Lane q of an 8-lane group holds elements [8q, 8q+8) and their rotation partners
+// [64+8q, 64+8q+8) as two 16-byte vectors; a warp works on 4 rows at once.
+__device__ __forceinline__ float group8_sum(float v)
+{
+    v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+    v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+    v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
+    return v;
+}
+
+__global__ void __launch_bounds__(kWarps * 32)
+qknorm_rope_fwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ gamma,
+                            const float* __restrict__ cosv, const float* __restrict__ sinv,
+                            bf16* __restrict__ y, int64_t ldy, int64_t tokens, int heads,
+                            int seq_len, float eps)
+{
+    const int lane = threadIdx.x & 31, q = lane & 7;
+    const int64_t rows = tokens * heads;
+    float ga[8], gb[8];
+    load16(gamma + 8 * q, ga);
+    load16(gamma + 64 + 8 * q, gb);
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps * 4;
+    for (int64_t base = (static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5)) * 4;
+         base < rows; base += stride)
+    {
+        const int64_t row = base + (lane >> 3);
+        const bool valid = row < rows;
+        const int64_t token = valid ? row / heads : 0;
+        const int head = valid ? static_cast<int>(row - token * heads) : 0;
+        const int t = static_cast<int>(token % seq_len);
+        float a[8], b[8];
+        if (valid)
+        {
+            const bf16* xr = x + token * ldx + static_cast<int64_t>(head) * 128;
+            load16(xr + 8 * q, a);
+            load16(xr + 64 + 8 * q, b);
+        }
+        else
+        {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a[j] = b[j] = 0.0f;
+        }
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += a[j] * a[j] + b[j] * b[j];
+        ss = group8_sum(ss);
+        const float r = sqrtf(ss / 128.0f + eps);
+        if (!valid)
+        {
+            continue;
+        }
+        const float4* cp = reinterpret_cast<const float4*>(cosv + static_cast<int64_t>(t) * 128 + 8 * q);
+        const float4* sp = reinterpret_cast<const float4*>(sinv + static_cast<int64_t>(t) * 128 + 8 * q);
+        const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+        const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        float oa[8], ob[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+        {
+            const float na = (a[j] / r) * ga[j], nb = (b[j] / r) * gb[j];
+            oa[j] = na * cs[j] - nb * sn[j];
+            ob[j] = nb * cs[j] + na * sn[j];
+        }
+        bf16* yr = y + token * ldy + static_cast<int64_t>(head) * 128;
+        store16(yr + 8 * q, oa);
+        store16(yr + 64 + 8 * q, ob);
+    }
+}
+
+// Shared memory: [kWarps * 4][128] fp32 gain-gradient rows (one per row slot).
+__global__ void __launch_bounds__(kWarps * 32)
+qknorm_rope_bwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx,
+                            const bf16* __restrict__ gamma, const float* __restrict__ cosv,
+                            const float* __restrict__ sinv, const bf16* __restrict__ dy,
+                            int64_t lddy, bf16* __restrict__ dx, int64_t lddx,
+                            float* __restrict__ partials, int64_t tokens, int heads, int seq_len,
+                            float eps)
+{
+    __shared__ float part[kWarps * 4][128];
+    const int lane = threadIdx.x & 31, q = lane & 7, slot = (threadIdx.x >> 5) * 4 + (lane >> 3);
+    const int64_t rows = tokens * heads;
+    float ga[8], gb[8], acca[8], accb[8];
+    load16(gamma + 8 * q, ga);
+    load16(gamma + 64 + 8 * q, gb);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acca[j] = accb[j] = 0.0f;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps * 4;
+    for (int64_t base = (static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5)) * 4;
+         base < rows; base += stride)
+    {
+        const int64_t row = base + (lane >> 3);
+        const bool valid = row < rows;
+        const int64_t token = valid ? row / heads : 0;
+        const int head = valid ? static_cast<int>(row - token * heads) : 0;
+        const int t = static_cast<int>(token % seq_len);
+        float a[8], b[8], da[8], db[8];
+        if (valid)
+        {
+            const bf16* xr = x + token * ldx + static_cast<int64_t>(head) * 128;
+            const bf16* gr = dy + token * lddy + static_cast<int64_t>(head) * 128;
+            load16(xr + 8 * q, a);
+            load16(xr + 64 + 8 * q, b);
+            load16(gr + 8 * q, da);
+            load16(gr + 64 + 8 * q, db);
+        }
+        else
+        {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a[j] = b[j] = da[j] = db[j] = 0.0f;
+        }
+        const float4* cp = reinterpret_cast<const float4*>(cosv + static_cast<int64_t>(t) * 128 + 8 * q);
+        const float4* sp = reinterpret_cast<const float4*>(sinv + static_cast<int64_t>(t) * 128 + 8 * q);
+        const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+        const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        float ss = 0.0f, w = 0.0f, na[8], nb[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+        {
+            // rotation by -theta: the gradient at the normed-and-scaled value
+            na[j] = da[j] * cs[j] + db[j] * sn[j];
+            nb[j] = db[j] * cs[j] - da[j] * sn[j];
+            ss += a[j] * a[j] + b[j] * b[j];
+            w += (na[j] * ga[j]) * a[j] + (nb[j] * gb[j]) * b[j];
+        }
+        ss = group8_sum(ss);
+        w = group8_sum(w);
+        if (!valid)
+        {
+            continue;
+        }
+        const float r = sqrtf(ss / 128.0f + eps);
+        const float coupling = w / (128.0f * r * r * r);
+        float oa[8], ob[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+        {
+            acca[j] += na[j] * (a[j] / r);
+            accb[j] += nb[j] * (b[j] / r);
+            oa[j] = (na[j] * ga[j]) / r - a[j] * coupling;
+            ob[j] = (nb[j] * gb[j]) / r - b[j] * coupling;
+        }
+        bf16* out = dx + token * lddx + static_cast<int64_t>(head) * 128;
+        store16(out + 8 * q, oa);
+        store16(out + 64 + 8 * q, ob);
+    }
+    if (partials != nullptr)
+    {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+        {
+            part[slot][8 * q + j] = acca[j];
+            part[slot][64 + 8 * q + j] = accb[j];
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < 128; i += blockDim.x)
+        {
+            float s = 0.0f;
+            for (int k = 0; k < kWarps * 4; ++k)
+            {
+                s += part[k][i];
+            }
+            partials[static_cast<size_t>(blockIdx.x) * 128 + i] = s;
+        }
+    }
 }
 
 // ---- QK-norm + RoPE ---------------------------------------------------------------------------
@@ -460,7 +833,23 @@ int launch_rms_fwd(const void* x, int64_t ldx, const void* gamma, void* y, int64
                      vec_ok(gamma, n, static_cast<int>(n), sizeof(T));
     const unsigned grid = static_cast<unsigned>(
         std::min<int64_t>((rows + kWarps - 1) / kWarps, static_cast<int64_t>(sm_count()) * 16));
-    if (vec)
+    constexpr int64_t V = 16 / sizeof(T);
+    const int64_t chunks = n % (32 * V) == 0 ? n / (32 * V) : 0;
+    if (vec && (chunks == 1 || chunks == 2 || chunks == 4 || chunks == 8))
+    {
+        const T* xp = static_cast<const T*>(x);
+        const T* gp = static_cast<const T*>(gamma);
+        T* yp = static_cast<T*>(y);
+        if (chunks == 1)
+            rmsnorm_fwd_reg_kernel<T, 1><<<grid, kWarps * 32, 0, s>>>(xp, ldx, gp, yp, ldy, rows, eps);
+        else if (chunks == 2)
+            rmsnorm_fwd_reg_kernel<T, 2><<<grid, kWarps * 32, 0, s>>>(xp, ldx, gp, yp, ldy, rows, eps);
+        else if (chunks == 4)
+            rmsnorm_fwd_reg_kernel<T, 4><<<grid, kWarps * 32, 0, s>>>(xp, ldx, gp, yp, ldy, rows, eps);
+        else
+            rmsnorm_fwd_reg_kernel<T, 8><<<grid, kWarps * 32, 0, s>>>(xp, ldx, gp, yp, ldy, rows, eps);
+    }
+    else if (vec)
     {
         rmsnorm_fwd_kernel<T, true><<<grid, kWarps * 32, 0, s>>>(
             static_cast<const T*>(x), ldx, static_cast<const T*>(gamma), static_cast<T*>(y), ldy,
@@ -488,21 +877,43 @@ int launch_rms_bwd(const void* x, int64_t ldx, const void* gamma, const void* dy
     const int grid = norm_bwd_grid(rows);
     float* partials = dgamma != nullptr ? static_cast<float*>(ws) : nullptr;
     const size_t smem = partials != nullptr ? static_cast<size_t>(kWarps) * n * sizeof(float) : 0;
-    auto kernel = vec ? rmsnorm_bwd_kernel<T, true> : rmsnorm_bwd_kernel<T, false>;
-    if (smem > 48 * 1024)
+    constexpr int64_t V = 16 / sizeof(T);
+    const int64_t chunks = n % (32 * V) == 0 ? n / (32 * V) : 0;
+    const T* xp = static_cast<const T*>(x);
+    const T* gp = static_cast<const T*>(gamma);
+    const T* dyp = static_cast<const T*>(dy);
+    const T* rp = static_cast<const T*>(dresid);
+    T* dxp = static_cast<T*>(dx);
+    auto allow_smem = [&](auto kernel) {
+        if (smem > 48 * 1024)
+        {
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem));
+        }
+    };
+    if (vec && (chunks == 1 || chunks == 2 || chunks == 4 || chunks == 8))
     {
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
+        auto launch_reg = [&](auto kernel) {
+            allow_smem(kernel);
+            kernel<<<grid, kWarps * 32, smem, s>>>(xp, ldx, gp, dyp, lddy, rp, ldr, dxp, lddx,
+                                                  partials, rows, eps);
+        };
+        if (chunks == 1) launch_reg(rmsnorm_bwd_reg_kernel<T, 1>);
+        else if (chunks == 2) launch_reg(rmsnorm_bwd_reg_kernel<T, 2>);
+        else if (chunks == 4) launch_reg(rmsnorm_bwd_reg_kernel<T, 4>);
+        else launch_reg(rmsnorm_bwd_reg_kernel<T, 8>);
     }
-    kernel<<<grid, kWarps * 32, smem, s>>>(
-        static_cast<const T*>(x), ldx, static_cast<const T*>(gamma), static_cast<const T*>(dy),
-        lddy, static_cast<const T*>(dresid), ldr, static_cast<T*>(dx), lddx, partials, rows, ni,
-        eps);
+    else
+    {
+        auto kernel = vec ? rmsnorm_bwd_kernel<T, true> : rmsnorm_bwd_kernel<T, false>;
+        allow_smem(kernel);
+        kernel<<<grid, kWarps * 32, smem, s>>>(xp, ldx, gp, dyp, lddy, rp, ldr, dxp, lddx,
+                                              partials, rows, ni, eps);
+    }
     count_launch();
     if (partials != nullptr)
     {
-        reduce_partials_kernel<<<(ni + 255) / 256, 256, 0, s>>>(partials, grid, ni, dgamma);
-        count_launch();
+        launch_reduce_partials(partials, grid, ni, dgamma, s);
     }
     return check_launch("veda_rmsnorm_bwd");
 }
@@ -572,6 +983,14 @@ extern "C" size_t veda_qknorm_rope_bwd_workspace(int64_t tokens, int64_t heads, 
 
 namespace
 {
+// The eight-lanes-per-row kernels need bf16, head_dim 128 and 16-byte aligned rows and tables.
+bool d128_ok(const void* x, int64_t ldx, const void* gamma, const float* c, const float* s,
+             const void* y, int64_t ldy, int64_t head_dim, int dtype)
+{
+    return dtype == VEDA_BF16 && head_dim == 128 && aligned16(x) && aligned16(y) &&
+           aligned16(gamma) && aligned16(c) && aligned16(s) && ldx % 8 == 0 && ldy % 8 == 0;
+}
+
 int qk_checks(const void* x, int64_t ldx, const void* gamma, const float* c, const float* s,
               int64_t tokens, int64_t heads, int64_t seq_len, int64_t dh, int dtype)
 {
@@ -606,7 +1025,16 @@ extern "C" int veda_qknorm_rope_fwd(const void* x, int64_t ldx, const void* gamm
     const int64_t rows = tokens * heads;
     const unsigned grid = static_cast<unsigned>(
         std::min<int64_t>((rows + kWarps - 1) / kWarps, static_cast<int64_t>(sm_count()) * 16));
-    if (dtype == VEDA_BF16)
+    if (d128_ok(x, ldx, gamma, cosv, sinv, y, ldy, head_dim, dtype))
+    {
+        const unsigned g4 = static_cast<unsigned>(std::min<int64_t>(
+            (rows + 4 * kWarps - 1) / (4 * kWarps), static_cast<int64_t>(sm_count()) * 16));
+        qknorm_rope_fwd_d128_kernel<<<g4, kWarps * 32, 0, stream>>>(
+            static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(gamma), cosv, sinv,
+            static_cast<bf16*>(y), ldy, tokens, static_cast<int>(heads),
+            static_cast<int>(seq_len), eps);
+    }
+    else if (dtype == VEDA_BF16)
     {
         qknorm_rope_fwd_kernel<bf16><<<grid, kWarps * 32, 0, stream>>>(
             static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(gamma), cosv, sinv,
@@ -653,7 +1081,15 @@ extern "C" int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamm
     const int grid = norm_bwd_grid(rows);
     float* partials = dgamma != nullptr ? static_cast<float*>(workspace) : nullptr;
     const size_t smem = partials != nullptr ? kWarps * head_dim * sizeof(float) : 0;
-    if (dtype == VEDA_BF16)
+    if (d128_ok(x, ldx, gamma, cosv, sinv, dy, lddy, head_dim, dtype) &&
+        d128_ok(x, ldx, gamma, cosv, sinv, dx, lddx, head_dim, dtype))
+    {
+        qknorm_rope_bwd_d128_kernel<<<grid, kWarps * 32, 0, stream>>>(
+            static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(gamma), cosv, sinv,
+            static_cast<const bf16*>(dy), lddy, static_cast<bf16*>(dx), lddx, partials, tokens,
+            static_cast<int>(heads), static_cast<int>(seq_len), eps);
+    }
+    else if (dtype == VEDA_BF16)
     {
         qknorm_rope_bwd_kernel<bf16><<<grid, kWarps * 32, smem, stream>>>(
             static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(gamma), cosv, sinv,
@@ -671,8 +1107,7 @@ extern "C" int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamm
     if (partials != nullptr)
     {
         const int n = static_cast<int>(head_dim);
-        reduce_partials_kernel<<<(n + 255) / 256, 256, 0, stream>>>(partials, grid, n, dgamma);
-        count_launch();
+        launch_reduce_partials(partials, grid, n, dgamma, stream);
     }
     return check_launch("veda_qknorm_rope_bwd");
 }

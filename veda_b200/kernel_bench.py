@@ -82,7 +82,7 @@ def mm_sweep(reps):
         ref_dw = (x.double().T @ dy[:, cols].double())
         e1 = float((dx[rows].double() - ref_dx).abs().max() / ref_dx.abs().max())
         e2 = float((dw[:, cols].double() - ref_dw).abs().max() / ref_dw.abs().max())
-        assert e1 < 1e-4 and e2 < 1e-4, (M, K, N, e1, e2)
+        assert e1 < 1e-3 and e2 < 1e-3, (M, K, N, e1, e2)   # fp32 accumulation over K
         del x, w, dy, dx, dw
         torch.cuda.empty_cache()
 
