@@ -277,6 +277,15 @@ extern "C" int veda_attention_fwd(const void* q, int64_t ldq, const void* k, int
     if (flash_supported(head_dim, dtype) &&
         flash_aligned(q, ldq, k, ldk, v, ldv, o, ldo))
     {
+        if (attention_tc_enabled())
+        {
+            const int rc2 = attn_tc_fwd(q, ldq, k, ldk, v, ldv, o, ldo, lse, batch, seq_len, heads,
+                                        kv_heads, scale, causal, stream);
+            if (rc2 != -1)
+            {
+                return rc2;
+            }
+        }
         return flash_fwd(q, ldq, k, ldk, v, ldv, o, ldo, lse, batch, seq_len, heads, kv_heads,
                          scale, causal, stream);
     }
@@ -320,6 +329,16 @@ extern "C" int veda_attention_bwd(const void* q, int64_t ldq, const void* k, int
     {
         char* extra = static_cast<char*>(workspace) +
                       ((static_cast<size_t>(batch * heads * seq_len) * sizeof(float) + 255) & ~static_cast<size_t>(255));
+        if (attention_tc_enabled())
+        {
+            const int rc2 = attn_tc_bwd(q, ldq, k, ldk, v, ldv, o, ldo, dout, lddo, lse, dq, lddq,
+                                        dk, lddk, dv, lddv, dvec, extra, batch, seq_len, heads,
+                                        kv_heads, scale, causal, stream);
+            if (rc2 != -1)
+            {
+                return rc2;
+            }
+        }
         return flash_bwd(q, ldq, k, ldk, v, ldv, o, ldo, dout, lddo, lse, dq, lddq, dk, lddk, dv,
                          lddv, dvec, extra, batch, seq_len, heads, kv_heads, scale, causal,
                          stream);

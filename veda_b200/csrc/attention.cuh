@@ -23,6 +23,19 @@ inline bool flash_aligned(const void* a, int64_t lda, const void* b, int64_t ldb
 
 size_t flash_bwd_extra_workspace(int64_t B, int64_t T, int64_t H, int64_t Hkv, int64_t Dh);
 
+// tcgen05 kernels (attention_tc.cu): same contract as flash_fwd / flash_bwd (bf16, head_dim 128,
+// 16-byte aligned operands); return -1 when a tensor map cannot be built (caller falls back).
+int attn_tc_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                void* o, int64_t ldo, float* lse, int64_t B, int64_t T, int64_t H, int64_t Hkv,
+                float scale, int causal, cudaStream_t s);
+int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                const void* o, int64_t ldo, const void* dout, int64_t lddo, const float* lse,
+                void* dq, int64_t lddq, void* dk, int64_t lddk, void* dv, int64_t lddv, float* dvec,
+                void* extra, int64_t B, int64_t T, int64_t H, int64_t Hkv, float scale, int causal,
+                cudaStream_t s);
+// Which tiled implementation serves bf16 / head_dim 128: 1 tcgen05 (default), 0 mma.sync.
+int attention_tc_enabled();
+
 int flash_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
               void* o, int64_t ldo, float* lse, int64_t B, int64_t T, int64_t H, int64_t Hkv,
               float scale, int causal, cudaStream_t s);

@@ -1,0 +1,788 @@
+// Causal GQA attention on the 5th-generation tensor cores (tcgen05.mma, TMEM), bf16, head_dim 128.
+//
+// Same semantics as attention_flash.cu (the composition of src/libs/train/Model.cpp:182-189 with
+// kv head h / (H/Hkv), src/libs/model/Attention.cpp:191); this file is the sm_100a-native form.
+//
+// Forward — one CTA per (batch, head, 128-query tile); 6 warps:
+//   warp 0     TMA: the Q tile once, then 128-key K and V tiles into a 2-stage ring
+//              (3-D tensor maps [B, T, columns], so rows past T read as zeros; no multicast);
+//   warp 1     MMA issuer: S_j = Q K_j^T (M128 N128 K128) into one of two TMEM S buffers, then
+//              O += P_{j-1} V_{j-1} (M128 N128 K128, O in TMEM) — so the QK^T of the next tile
+//              runs while the softmax warps work on the current one;
+//   warps 2-5  softmax: thread i owns query row i (TMEM lane i): loads its S row, masks, keeps
+//              a running max in the log2 domain and rescales O in TMEM only when the max grows
+//              by more than 2^8 (otherwise the stale max is kept; every exponent stays below 2^8),
+//              writes P (bf16) into a 128-byte-swizzled shared tile for the P.V product, and at
+//              the end writes O / l and LSE = (m + log2 l) ln 2.
+// Every mbarrier wait is bounded (see tc_common.cuh).
+#include "attention.cuh"
+#include "tc_common.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <mutex>
+
+namespace veda::cuda
+{
+int* device_status_ptr();
+
+namespace
+{
+using namespace tc;
+
+constexpr int kTq = 128;                 // queries per CTA
+constexpr int kTk = 128;                 // keys per tile
+constexpr int kTileBytes = 128 * 128 * 2;   // a [128 rows x 128 dims] bf16 tile (two 16 KB halves)
+constexpr int kHalf = kTileBytes / 2;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;   // log2 units
+
+struct FwdParams
+{
+    bf16* o;
+    float* lse;
+    int64_t ldo;
+    int T, H, Hkv;
+    float scale_log2;
+    int causal;
+    int* status;
+};
+
+// smem: Q | K[2] | V[2] | P | barriers
+constexpr int kFwdSmem = 1024 + kTileBytes * 6 + 256;
+
+__device__ __forceinline__ void load_tile_3d(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
+                                             int col, int row, int batch)
+{
+    tma_load_3d(dst, map, bar, col, row, batch);
+    tma_load_3d(dst + kHalf, map, bar, col + 64, row, batch);
+}
+
+// K-major [128 x 128] operand, k-step ks (16 elements) of the 128-wide K dimension.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int ks)
+{
+    return smem_desc(base + (ks >> 2) * kHalf + (ks & 3) * 32, 16, 1024);
+}
+
+// MN-major operand whose rows are the K dimension (16 rows per k-step) and whose 128 MN columns
+// are two 64-column halves kHalf bytes apart.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int ks, uint32_t lbo)
+{
+    return smem_desc(base + ks * 2048, lbo, 1024);
+}
+
+__global__ void __launch_bounds__(192, 1)
+attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                   const __grid_constant__ CUtensorMap tv, const FwdParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* sq = smem;
+    uint8_t* sk = sq + kTileBytes;           // [2]
+    uint8_t* sv = sk + 2 * kTileBytes;       // [2]
+    uint8_t* sp = sv + 2 * kTileBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sp + kTileBytes);
+    uint64_t* q_full = bars + 0;
+    uint64_t* kv_full = bars + 1;    // [2]
+    uint64_t* kv_empty = bars + 3;   // [2]
+    uint64_t* s_full = bars + 5;     // [2]
+    uint64_t* s_free = bars + 7;     // [2]
+    uint64_t* p_full = bars + 9;
+    uint64_t* o_done = bars + 10;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nq = (p.T + kTq - 1) / kTq;
+    const int qt = nq - 1 - static_cast<int>(blockIdx.x);   // longest rows first
+    const int bh = blockIdx.y;
+    const int b = bh / p.H, h = bh % p.H;
+    const int kvh = h / (p.H / p.Hkv);
+    const int nk = p.causal ? qt + 1 : (p.T + kTk - 1) / kTk;
+
+    if (threadIdx.x == 0)
+    {
+        *abort = 0;
+        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; ++i)
+        {
+            mbar_init(&kv_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_free[i], 4);
+        }
+        mbar_init(p_full, 4);
+        mbar_init(o_done, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1)
+    {
+        tmem_alloc(tmem_slot, 512);
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0)
+    {
+        tma_prefetch(&tq);
+        tma_prefetch(&tk);
+        tma_prefetch(&tv);
+        mbar_expect_tx(q_full, kTileBytes);
+        load_tile_3d(sq, &tq, q_full, h * 128, qt * kTq, b);
+        for (int j = 0; j < nk; ++j)
+        {
+            const int st = j & 1;
+            mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, p.status, abort);
+            mbar_expect_tx(&kv_full[st], 2 * kTileBytes);
+            load_tile_3d(sk + st * kTileBytes, &tk, &kv_full[st], kvh * 128, j * kTk, b);
+            load_tile_3d(sv + st * kTileBytes, &tv, &kv_full[st], kvh * 128, j * kTk, b);
+        }
+    }
+    else if (warp == 1 && lane == 0)
+    {
+        constexpr uint32_t idesc_s = instr_desc(128, 128, false, false);
+        constexpr uint32_t idesc_o = instr_desc(128, 128, false, true);
+        const uint32_t q_base = smem_u32(sq), p_base = smem_u32(sp);
+        mbar_wait(q_full, 0, p.status, abort);
+        auto issue_pv = [&](int j) {
+            mbar_wait(p_full, j & 1, p.status, abort);
+            fence_after();
+            const uint32_t v_base = smem_u32(sv + (j & 1) * kTileBytes);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+            {
+                mma(tmem + 256, kmajor_desc(p_base, ks), mnmajor_desc(v_base, ks, kHalf), idesc_o,
+                    (j > 0 || ks > 0) ? 1u : 0u);
+            }
+            commit(o_done);
+            commit(&kv_empty[j & 1]);
+        };
+        for (int j = 0; j < nk; ++j)
+        {
+            const int st = j & 1;
+            mbar_wait(&kv_full[st], (j >> 1) & 1, p.status, abort);
+            mbar_wait(&s_free[st], ((j >> 1) & 1) ^ 1, p.status, abort);
+            fence_after();
+            const uint32_t k_base = smem_u32(sk + st * kTileBytes);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+            {
+                mma(tmem + st * 128, kmajor_desc(q_base, ks), kmajor_desc(k_base, ks), idesc_s,
+                    ks > 0 ? 1u : 0u);
+            }
+            commit(&s_full[st]);
+            if (j > 0)
+            {
+                issue_pv(j - 1);
+            }
+        }
+        issue_pv(nk - 1);
+    }
+    else if (warp >= 2)
+    {
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;                // row within the tile (TMEM lane)
+        const int query = qt * kTq + r;
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        float m = -INFINITY, l = 0.0f;
+        for (int j = 0; j < nk; ++j)
+        {
+            const int st = j & 1;
+            mbar_wait(&s_full[st], (j >> 1) & 1, p.status, abort);
+            fence_after();
+            float s[128];
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+            {
+                uint32_t raw[32];
+                tmem_ld32(tmem + lane_base + st * 128 + c * 32, raw);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(raw[e]);
+            }
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[st]);
+            const bool diag = p.causal && j == qt;
+            const int key0 = j * kTk;
+            const bool tail = key0 + kTk > p.T;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int e = 0; e < 128; ++e)
+            {
+                float x = s[e] * p.scale_log2;
+                if ((diag && key0 + e > query) || (tail && key0 + e >= p.T)) x = -INFINITY;
+                s[e] = x;
+                mx = fmaxf(mx, x);
+            }
+            // O and the P buffer are in use by the previous tile's P.V product until it is done
+            if (j > 0)
+            {
+                mbar_wait(o_done, (j - 1) & 1, p.status, abort);
+                fence_after();
+            }
+            const bool first = m == -INFINITY;
+            const bool grow = mx > m + kRescaleThreshold;
+            if (__any_sync(0xFFFFFFFFu, grow && !first) && j > 0)
+            {
+                const float corr = (grow && !first) ? exp2f(m - mx) : 1.0f;
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c)
+                {
+                    uint32_t raw[32];
+                    tmem_ld32(tmem + lane_base + 256 + c * 32, raw);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * corr);
+                    tmem_st32(tmem + lane_base + 256 + c * 32, raw);
+                }
+                l *= corr;
+            }
+            if (grow || first)
+            {
+                m = mx;
+            }
+            float rs = 0.0f;
+            uint8_t* prow = sp;
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+            {
+                float e8[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                {
+                    const float x = s[c * 8 + e];
+                    e8[e] = m == -INFINITY ? 0.0f : exp2f(x - m);
+                    rs += e8[e];
+                }
+                uint4 packed;
+                const __nv_bfloat162 p0 = __floats2bfloat162_rn(e8[0], e8[1]);
+                const __nv_bfloat162 p1 = __floats2bfloat162_rn(e8[2], e8[3]);
+                const __nv_bfloat162 p2 = __floats2bfloat162_rn(e8[4], e8[5]);
+                const __nv_bfloat162 p3 = __floats2bfloat162_rn(e8[6], e8[7]);
+                packed.x = *reinterpret_cast<const uint32_t*>(&p0);
+                packed.y = *reinterpret_cast<const uint32_t*>(&p1);
+                packed.z = *reinterpret_cast<const uint32_t*>(&p2);
+                packed.w = *reinterpret_cast<const uint32_t*>(&p3);
+                *reinterpret_cast<uint4*>(prow + (c >> 3) * kHalf + sw128_offset(r, c & 7)) = packed;
+            }
+            l += rs;
+            fence_proxy_async();
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+        }
+        // epilogue: O / l and the log-sum-exp
+        mbar_wait(o_done, (nk - 1) & 1, p.status, abort);
+        fence_after();
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        const bool valid = query < p.T;
+        bf16* orow = p.o + (static_cast<int64_t>(b) * p.T + query) * p.ldo + static_cast<int64_t>(h) * 128;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c)
+        {
+            uint32_t raw[32];
+            tmem_ld32(tmem + lane_base + 256 + c * 32, raw);
+            if (valid)
+            {
+#pragma unroll
+                for (int e = 0; e < 32; e += 8)
+                {
+                    float v8[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) v8[q] = __uint_as_float(raw[e + q]) * inv;
+                    store16(orow + c * 32 + e, v8);
+                }
+            }
+        }
+        if (valid)
+        {
+            p.lse[(static_cast<int64_t>(b) * p.H + h) * p.T + query] = (m + log2f(l)) * kLn2;
+        }
+    }
+    fence_before();
+    __syncthreads();
+    if (warp == 1)
+    {
+        fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Backward — one CTA per (batch, KV head, 128-key tile); 6 warps. For every query head of the
+// GQA group and every 64-query tile at or after the diagonal:
+//   MMA   S^T = K Q^T and dP^T = V dO^T          (M128 keys, N64 queries, K128 dims)
+//   warps P^T = exp2(S^T scale log2e - LSE log2e), causal mask, dS^T = P^T (dP^T - D)
+//         -> bf16 into swizzled shared tiles
+//   MMA   dV += P^T dO, dK += dS^T Q             (M128 keys, N128 dims, K64 queries; in TMEM)
+//         dQ^T = K^T dS^T                        (M128 dims, N64 queries, K128 keys)
+//   warps dQ^T rows added to an fp32 accumulator with atomics (scaled and rounded afterwards).
+// The Q/dO tiles are staged once per iteration (2-stage ring) and serve both as K-major operands
+// (rows = queries = N) and as MN-major operands (rows = queries = K); the K tile likewise serves
+// S^T (K-major) and dQ^T (MN-major). dK and dV are summed over the group's heads in TMEM, so
+// they are written once and deterministically.
+// ---------------------------------------------------------------------------------------------
+constexpr int kBq = 64;                      // queries per backward iteration
+constexpr int kQTileBytes = kBq * 128 * 2;   // [64 rows x 128 dims] = two 8 KB halves
+constexpr int kQHalf = kQTileBytes / 2;
+constexpr int kPTileBytes = 128 * kBq * 2;   // [128 keys x 64 queries]
+// alignment slack | K, V | Q[2], dO[2] | P^T, dS^T | LSE/D staging (1 KB) + barriers
+constexpr int kBwdSmem = 1024 + 2 * kTileBytes + 4 * kQTileBytes + 2 * kPTileBytes + 2048;
+
+struct BwdParams
+{
+    const float* lse;
+    const float* dvec;
+    float* dq_acc;   // [B*T, H*128]
+    bf16 *dk, *dv;
+    int64_t lddk, lddv;
+    int T, H, Hkv;
+    float scale, scale_log2;
+    int causal;
+    int* status;
+};
+
+__device__ __forceinline__ void named_sync_compute()
+{
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+__device__ __forceinline__ void load_qtile_3d(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
+                                              int col, int row, int batch)
+{
+    tma_load_3d(dst, map, bar, col, row, batch);
+    tma_load_3d(dst + kQHalf, map, bar, col + 64, row, batch);
+}
+
+__global__ void __launch_bounds__(192, 1)
+attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                   const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                   const BwdParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* sk = smem;
+    uint8_t* sv = sk + kTileBytes;
+    uint8_t* sq = sv + kTileBytes;             // [2]
+    uint8_t* sdo = sq + 2 * kQTileBytes;       // [2]
+    uint8_t* sp = sdo + 2 * kQTileBytes;
+    uint8_t* sds = sp + kPTileBytes;
+    float* sld = reinterpret_cast<float*>(sds + kPTileBytes);   // [2][2][64]: LSE*log2e, D
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sld + 4 * kBq);
+    uint64_t* kv_full = bars + 0;
+    uint64_t* qd_full = bars + 1;    // [2]
+    uint64_t* qd_empty = bars + 3;   // [2]
+    uint64_t* sp_full = bars + 5;
+    uint64_t* st_free = bars + 6;
+    uint64_t* ds_full = bars + 7;
+    uint64_t* pds_free = bars + 8;
+    uint64_t* dq_full = bars + 9;
+    uint64_t* dq_free = bars + 10;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kt = static_cast<int>(blockIdx.x);
+    const int bk = blockIdx.y;
+    const int b = bk / p.Hkv, kvh = bk % p.Hkv;
+    const int rep = p.H / p.Hkv;
+    const int nq = (p.T + kBq - 1) / kBq;
+    const int qi0 = p.causal ? (kt * 128) / kBq : 0;
+    const int per_head = nq - qi0;
+    const int iters = rep * per_head;
+
+    if (threadIdx.x == 0)
+    {
+        *abort = 0;
+        mbar_init(kv_full, 1);
+        for (int i = 0; i < 2; ++i)
+        {
+            mbar_init(&qd_full[i], 1);
+            mbar_init(&qd_empty[i], 1);
+        }
+        mbar_init(sp_full, 1);
+        mbar_init(st_free, 4);
+        mbar_init(ds_full, 4);
+        mbar_init(pds_free, 1);
+        mbar_init(dq_full, 1);
+        mbar_init(dq_free, 4);
+        mbar_fence_init();
+    }
+    if (warp == 1)
+    {
+        tmem_alloc(tmem_slot, 512);
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+    constexpr uint32_t kST = 0, kDPT = 64, kDV = 128, kDK = 256, kDQT = 384;
+
+    if (warp == 0 && lane == 0)
+    {
+        tma_prefetch(&tq);
+        tma_prefetch(&tk);
+        tma_prefetch(&tv);
+        tma_prefetch(&tdo);
+        mbar_expect_tx(kv_full, 2 * kTileBytes);
+        load_tile_3d(sk, &tk, kv_full, kvh * 128, kt * 128, b);
+        load_tile_3d(sv, &tv, kv_full, kvh * 128, kt * 128, b);
+        for (int it = 0; it < iters; ++it)
+        {
+            const int st = it & 1;
+            const int h = kvh * rep + it / per_head;
+            const int q0 = (qi0 + it % per_head) * kBq;
+            mbar_wait(&qd_empty[st], ((it >> 1) & 1) ^ 1, p.status, abort);
+            mbar_expect_tx(&qd_full[st], 2 * kQTileBytes);
+            load_qtile_3d(sq + st * kQTileBytes, &tq, &qd_full[st], h * 128, q0, b);
+            load_qtile_3d(sdo + st * kQTileBytes, &tdo, &qd_full[st], h * 128, q0, b);
+        }
+    }
+    else if (warp == 1 && lane == 0)
+    {
+        constexpr uint32_t idesc_s = instr_desc(128, kBq, false, false);
+        constexpr uint32_t idesc_kv = instr_desc(128, 128, false, true);
+        constexpr uint32_t idesc_q = instr_desc(128, kBq, true, true);
+        const uint32_t k_base = smem_u32(sk), v_base = smem_u32(sv);
+        const uint32_t p_base = smem_u32(sp), ds_base = smem_u32(sds);
+        mbar_wait(kv_full, 0, p.status, abort);
+        for (int it = 0; it < iters; ++it)
+        {
+            const int st = it & 1;
+            const uint32_t q_base = smem_u32(sq + st * kQTileBytes);
+            const uint32_t do_base = smem_u32(sdo + st * kQTileBytes);
+            mbar_wait(&qd_full[st], (it >> 1) & 1, p.status, abort);
+            mbar_wait(st_free, (it & 1) ^ 1, p.status, abort);
+            fence_after();
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+            {
+                const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;
+                mma(tmem + kST, kmajor_desc(k_base, ks), smem_desc(q_base + off, 16, 1024), idesc_s,
+                    ks > 0 ? 1u : 0u);
+                mma(tmem + kDPT, kmajor_desc(v_base, ks), smem_desc(do_base + off, 16, 1024),
+                    idesc_s, ks > 0 ? 1u : 0u);
+            }
+            commit(sp_full);
+            mbar_wait(ds_full, it & 1, p.status, abort);
+            fence_after();
+#pragma unroll
+            for (int ks = 0; ks < kBq / 16; ++ks)
+            {
+                const uint32_t acc = (it > 0 || ks > 0) ? 1u : 0u;
+                mma(tmem + kDV, smem_desc(p_base + ks * 32, 16, 1024),
+                    mnmajor_desc(do_base, ks, kQHalf), idesc_kv, acc);
+                mma(tmem + kDK, smem_desc(ds_base + ks * 32, 16, 1024),
+                    mnmajor_desc(q_base, ks, kQHalf), idesc_kv, acc);
+            }
+            mbar_wait(dq_free, (it & 1) ^ 1, p.status, abort);
+            fence_after();
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+            {
+                mma(tmem + kDQT, mnmajor_desc(k_base, ks, kHalf), mnmajor_desc(ds_base, ks, kHalf),
+                    idesc_q, ks > 0 ? 1u : 0u);
+            }
+            commit(dq_full);
+            commit(pds_free);
+            commit(&qd_empty[st]);
+        }
+    }
+    else if (warp >= 2)
+    {
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;   // key row (S^T, dP^T, dV, dK) or dim row (dQ^T)
+        const int key = kt * 128 + r;
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        const int tid = threadIdx.x - 64;    // 0..127 among the compute warps
+        const int64_t width = static_cast<int64_t>(p.H) * 128;
+        for (int it = 0; it < iters; ++it)
+        {
+            const int h = kvh * rep + it / per_head;
+            const int q0 = (qi0 + it % per_head) * kBq;
+            float* lse2 = sld + (it & 1) * 2 * kBq;
+            float* dd = lse2 + kBq;
+            {
+                const int c = tid & (kBq - 1);
+                const int q = q0 + c;
+                const int64_t at = (static_cast<int64_t>(b) * p.H + h) * p.T + q;
+                if (tid < kBq)
+                {
+                    lse2[c] = q < p.T ? p.lse[at] * kLog2e : INFINITY;
+                }
+                else
+                {
+                    dd[c] = q < p.T ? p.dvec[at] : 0.0f;
+                }
+            }
+            named_sync_compute();
+            mbar_wait(sp_full, it & 1, p.status, abort);
+            fence_after();
+            uint32_t sraw[64], draw[64];
+            tmem_ld32(tmem + lane_base + kST, *reinterpret_cast<uint32_t(*)[32]>(sraw));
+            tmem_ld32(tmem + lane_base + kST + 32, *reinterpret_cast<uint32_t(*)[32]>(sraw + 32));
+            tmem_ld32(tmem + lane_base + kDPT, *reinterpret_cast<uint32_t(*)[32]>(draw));
+            tmem_ld32(tmem + lane_base + kDPT + 32, *reinterpret_cast<uint32_t(*)[32]>(draw + 32));
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(st_free);
+            const bool maybe_masked = p.causal && q0 < kt * 128 + 128;
+            float pv[64], dsv[64];
+#pragma unroll
+            for (int c = 0; c < kBq; ++c)
+            {
+                float pr = exp2f(__uint_as_float(sraw[c]) * p.scale_log2 - lse2[c]);
+                if (maybe_masked && key > q0 + c) pr = 0.0f;
+                pv[c] = pr;
+                dsv[c] = pr * (__uint_as_float(draw[c]) - dd[c]);
+            }
+            mbar_wait(pds_free, (it & 1) ^ 1, p.status, abort);
+#pragma unroll
+            for (int c8 = 0; c8 < kBq / 8; ++c8)
+            {
+                uint4 a, d;
+                __nv_bfloat162 t;
+                t = __floats2bfloat162_rn(pv[c8 * 8 + 0], pv[c8 * 8 + 1]); a.x = *reinterpret_cast<uint32_t*>(&t);
+                t = __floats2bfloat162_rn(pv[c8 * 8 + 2], pv[c8 * 8 + 3]); a.y = *reinterpret_cast<uint32_t*>(&t);
+                t = __floats2bfloat162_rn(pv[c8 * 8 + 4], pv[c8 * 8 + 5]); a.z = *reinterpret_cast<uint32_t*>(&t);
+                t = __floats2bfloat162_rn(pv[c8 * 8 + 6], pv[c8 * 8 + 7]); a.w = *reinterpret_cast<uint32_t*>(&t);
+                t = __floats2bfloat162_rn(dsv[c8 * 8 + 0], dsv[c8 * 8 + 1]); d.x = *reinterpret_cast<uint32_t*>(&t);
+                t = __floats2bfloat162_rn(dsv[c8 * 8 + 2], dsv[c8 * 8 + 3]); d.y = *reinterpret_cast<uint32_t*>(&t);
+                t = __floats2bfloat162_rn(dsv[c8 * 8 + 4], dsv[c8 * 8 + 5]); d.z = *reinterpret_cast<uint32_t*>(&t);
+                t = __floats2bfloat162_rn(dsv[c8 * 8 + 6], dsv[c8 * 8 + 7]); d.w = *reinterpret_cast<uint32_t*>(&t);
+                *reinterpret_cast<uint4*>(sp + sw128_offset(r, c8)) = a;
+                *reinterpret_cast<uint4*>(sds + sw128_offset(r, c8)) = d;
+            }
+            fence_proxy_async();
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(ds_full);
+            // dQ^T: this thread holds dims row r for the 64 queries of the tile
+            mbar_wait(dq_full, it & 1, p.status, abort);
+            fence_after();
+            uint32_t qraw[64];
+            tmem_ld32(tmem + lane_base + kDQT, *reinterpret_cast<uint32_t(*)[32]>(qraw));
+            tmem_ld32(tmem + lane_base + kDQT + 32, *reinterpret_cast<uint32_t(*)[32]>(qraw + 32));
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(dq_free);
+            float* dst = p.dq_acc + (static_cast<int64_t>(b) * p.T + q0) * width +
+                         static_cast<int64_t>(h) * 128 + r;
+            const int nvalid = min(kBq, p.T - q0);
+#pragma unroll
+            for (int c = 0; c < kBq; ++c)
+            {
+                if (c < nvalid)
+                {
+                    atomicAdd(dst + static_cast<int64_t>(c) * width, __uint_as_float(qraw[c]));
+                }
+            }
+        }
+        // dV and dK rows of this key (summed over the group's heads in TMEM)
+        if (iters > 0)
+        {
+            mbar_wait(dq_full, (iters - 1) & 1, p.status, abort);   // already passed: no-op
+        }
+        fence_after();
+        const bool valid = key < p.T;
+        bf16* vrow = p.dv + (static_cast<int64_t>(b) * p.T + key) * p.lddv + static_cast<int64_t>(kvh) * 128;
+        bf16* krow = p.dk + (static_cast<int64_t>(b) * p.T + key) * p.lddk + static_cast<int64_t>(kvh) * 128;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c)
+        {
+            uint32_t rv[32], rk[32];
+            tmem_ld32(tmem + lane_base + kDV + c * 32, rv);
+            tmem_ld32(tmem + lane_base + kDK + c * 32, rk);
+            if (valid)
+            {
+#pragma unroll
+                for (int e = 0; e < 32; e += 8)
+                {
+                    float a8[8], k8[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                    {
+                        a8[q] = iters > 0 ? __uint_as_float(rv[e + q]) : 0.0f;
+                        k8[q] = iters > 0 ? __uint_as_float(rk[e + q]) * p.scale : 0.0f;
+                    }
+                    store16(vrow + c * 32 + e, a8);
+                    store16(krow + c * 32 + e, k8);
+                }
+            }
+        }
+    }
+    fence_before();
+    __syncthreads();
+    if (warp == 1)
+    {
+        fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// D[b,h,t] = sum_d dO * O over the head's 128 dims; one warp per row.
+__global__ void attn_rowdot_kernel(const bf16* __restrict__ o, int64_t ldo,
+                                   const bf16* __restrict__ dout, int64_t lddo,
+                                   float* __restrict__ dvec, int64_t B, int64_t T, int64_t H)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t rows = B * H * T;
+    for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows;
+         r += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5)
+    {
+        const int64_t i = r % T, h = (r / T) % H, b = r / (T * H);
+        float s = 0.0f;
+        if (lane < 16)
+        {
+            float x[8], y[8];
+            load16(o + (b * T + i) * ldo + h * 128 + lane * 8, x);
+            load16(dout + (b * T + i) * lddo + h * 128 + lane * 8, y);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s += x[e] * y[e];
+        }
+        s = warp_sum(s);
+        if (lane == 0) dvec[(b * H + h) * T + i] = s;
+    }
+}
+
+// dq = bf16(scale * acc)
+__global__ void attn_dq_convert_kernel(const float* __restrict__ acc, bf16* __restrict__ dq,
+                                       int64_t lddq, int64_t rows, int64_t width, float scale)
+{
+    const int64_t total = rows * width / 4;
+    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    {
+        const int64_t r = (idx * 4) / width, c = (idx * 4) % width;
+        const float4 v = reinterpret_cast<const float4*>(acc)[idx];
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x * scale, v.y * scale);
+        const __nv_bfloat162 hi = __floats2bfloat162_rn(v.z * scale, v.w * scale);
+        uint2 packed;
+        packed.x = *reinterpret_cast<const uint32_t*>(&lo);
+        packed.y = *reinterpret_cast<const uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(dq + r * lddq + c) = packed;
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                             cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+        {
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        }
+    });
+    return fn;
+}
+
+// [B, T, width] bf16 view of a token-major operand with row stride ld; box 64 columns x `rows`.
+bool make_map3(CUtensorMap* map, const void* base, int64_t width, int64_t T, int64_t B, int64_t ld,
+               uint32_t rows)
+{
+    auto fn = encode_fn();
+    if (fn == nullptr)
+    {
+        return false;
+    }
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(T),
+                                static_cast<cuuint64_t>(B)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2,
+                                   static_cast<cuuint64_t>(ld) * 2 * static_cast<cuuint64_t>(T)};
+    const cuuint32_t box[3] = {64, rows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+} // namespace
+
+// The tcgen05 kernels serve bf16 / head_dim 128 unless VEDA_ATTENTION_MMA_SYNC=1 selects the
+// mma.sync kernels of attention_flash.cu (kept for comparison and as the fallback).
+int attention_tc_enabled()
+{
+    static const int enabled = [] {
+        const char* v = std::getenv("VEDA_ATTENTION_MMA_SYNC");
+        return (v != nullptr && v[0] == '1') ? 0 : 1;
+    }();
+    return enabled;
+}
+
+int attn_tc_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                void* o, int64_t ldo, float* lse, int64_t B, int64_t T, int64_t H, int64_t Hkv,
+                float scale, int causal, cudaStream_t s)
+{
+    CUtensorMap mq, mk, mv;
+    if (!make_map3(&mq, q, H * 128, T, B, ldq, kTq) || !make_map3(&mk, k, Hkv * 128, T, B, ldk, kTk) ||
+        !make_map3(&mv, v, Hkv * 128, T, B, ldv, kTk))
+    {
+        return -1;   // caller falls back
+    }
+    static int configured = -1;
+    int device = 0;
+    cudaGetDevice(&device);
+    if (configured != device)
+    {
+        cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+        configured = device;
+    }
+    FwdParams p{static_cast<bf16*>(o), lse, ldo, static_cast<int>(T), static_cast<int>(H),
+                static_cast<int>(Hkv), scale * kLog2e, causal, device_status_ptr()};
+    const dim3 grid(static_cast<unsigned>((T + kTq - 1) / kTq), static_cast<unsigned>(B * H));
+    attn_fwd_tc_kernel<<<grid, 192, kFwdSmem, s>>>(mq, mk, mv, p);
+    count_launch();
+    return check_launch("veda_attention_fwd (tcgen05)");
+}
+
+int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                const void* o, int64_t ldo, const void* dout, int64_t lddo, const float* lse,
+                void* dq, int64_t lddq, void* dk, int64_t lddk, void* dv, int64_t lddv, float* dvec,
+                void* extra, int64_t B, int64_t T, int64_t H, int64_t Hkv, float scale, int causal,
+                cudaStream_t s)
+{
+    CUtensorMap mq, mk, mv, mdo;
+    if (!make_map3(&mq, q, H * 128, T, B, ldq, kBq) || !make_map3(&mk, k, Hkv * 128, T, B, ldk, 128) ||
+        !make_map3(&mv, v, Hkv * 128, T, B, ldv, 128) ||
+        !make_map3(&mdo, dout, H * 128, T, B, lddo, kBq))
+    {
+        return -1;   // caller falls back
+    }
+    static int configured = -1;
+    int device = 0;
+    cudaGetDevice(&device);
+    if (configured != device)
+    {
+        cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
+        configured = device;
+    }
+    float* acc = static_cast<float*>(extra);
+    const int64_t width = H * 128;
+    if (cudaMemsetAsync(acc, 0, static_cast<size_t>(B * T * width) * sizeof(float), s) != cudaSuccess)
+    {
+        return fail(VEDA_ERR_CUDA, "veda_attention_bwd: clearing the dQ accumulator failed");
+    }
+    attn_rowdot_kernel<<<grid_for(B * H * T * 32, 256), 256, 0, s>>>(
+        static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, dvec, B, T, H);
+    BwdParams p{lse, dvec, acc, static_cast<bf16*>(dk), static_cast<bf16*>(dv), lddk, lddv,
+                static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
+                scale * kLog2e, causal, device_status_ptr()};
+    const dim3 grid(static_cast<unsigned>((T + 127) / 128), static_cast<unsigned>(B * Hkv));
+    attn_bwd_tc_kernel<<<grid, 192, kBwdSmem, s>>>(mq, mk, mv, mdo, p);
+    attn_dq_convert_kernel<<<grid_for(B * T * width / 4, 256), 256, 0, s>>>(
+        acc, static_cast<bf16*>(dq), lddq, B * T, width, scale);
+    count_launch(3);
+    return check_launch("veda_attention_bwd (tcgen05)");
+}
+
+} // namespace veda::cuda

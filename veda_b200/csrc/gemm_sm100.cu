@@ -22,6 +22,7 @@
 // Every mbarrier wait is bounded; a wait that gives up records VEDA_ERR_TIMEOUT in the library's
 // device status word (veda_kernel_status) and the kernel runs to completion.
 #include "gemm.cuh"
+#include "tc_common.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -64,150 +65,7 @@ struct Params
     int* status;
 };
 
-// ---- PTX wrappers ------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p)
-{
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
-{
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes)
-{
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
-{
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t phase)
-{
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(addr), "r"(phase)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait: about two seconds of spinning, then the status word records a timeout, the CTA's
-// shared abort flag is raised so every later wait returns at once, and the caller proceeds
-// (results are then garbage, but the kernel ends promptly and the context survives).
-__device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t phase, int* status,
-                                          volatile int* abort)
-{
-    const uint32_t addr = smem_u32(bar);
-    if (mbar_try_wait(addr, phase))
-    {
-        return;
-    }
-    const long long start = clock64();
-    while (!mbar_try_wait(addr, phase))
-    {
-        if (*abort != 0)
-        {
-            return;
-        }
-        if (clock64() - start > (1ll << 32))
-        {
-            *abort = 1;
-            if (status != nullptr)
-            {
-                atomicExch(status, VEDA_ERR_TIMEOUT);
-            }
-            return;
-        }
-    }
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
-                                            int y)
-{
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_prefetch(const CUtensorMap* map)
-{
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before()
-{
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after()
-{
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tc_commit(uint64_t* bar)
-{
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                       uint32_t accumulate)
-{
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
-{
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-          "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Shared-memory matrix descriptor: 128-byte swizzle, descriptor version 1 (sm_100).
-//   K-major operand: rows of 128 bytes, 8-row core groups SBO = 1024 bytes apart (LBO unused).
-//   MN-major operand: 64-element MN chunks LBO bytes apart, 8-row K groups SBO = 1024 apart.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo)
-{
-    uint64_t d = 0;
-    d |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
-    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
-    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
-    d |= 1ull << 46;   // version
-    d |= 2ull << 61;   // SWIZZLE_128B
-    return d;
-}
-
-// Instruction descriptor, kind::f16: D fp32, A and B bf16, majors, N >> 3, M >> 4.
-__host__ __device__ constexpr uint32_t instr_desc(int n, bool a_mn, bool b_mn)
-{
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) |
-           ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
-           (static_cast<uint32_t>(BM >> 4) << 24);
-}
+using namespace tc;
 
 // Output tile order: groups of 16 M-tiles sweep all N-tiles, so an A row-panel stays in L2.
 __device__ __forceinline__ void unit_coords(int u, const Params& p, int& mb, int& nb, int& split)
@@ -358,7 +216,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], 4);
         }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_fence_init();
     }
     if (warp == 1)
     {
@@ -367,9 +225,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                      "r"(C_::TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    tc_fence_before();
+    fence_before();
     __syncthreads();
-    tc_fence_after();
+    fence_after();
     const uint32_t tmem = *tmem_slot;
 
     const int units = p.num_m * p.num_n * p.splits;
@@ -428,7 +286,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
     }
     else if (warp == 1 && lane == 0)
     {
-        constexpr uint32_t idesc = instr_desc(BN, A_MN, B_MN);
+        constexpr uint32_t idesc = instr_desc(BM, BN, A_MN, B_MN);
         int stage = 0;
         uint32_t phase = 0;
         int it = 0;
@@ -441,12 +299,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             const int buf = it & 1;
             const uint32_t tphase = (it >> 1) & 1;
             mbar_wait(&tempty[buf], tphase ^ 1, p.status, abort);
-            tc_fence_after();
+            fence_after();
             const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
             for (int kb = kb0; kb < kb1; ++kb)
             {
                 mbar_wait(&full[stage], phase, p.status, abort);
-                tc_fence_after();
+                fence_after();
                 const uint32_t a_base = smem_u32(sa + stage * C_::A_BYTES);
                 const uint32_t b_base = smem_u32(sb + stage * C_::B_BYTES);
 #pragma unroll
@@ -456,16 +314,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                                              : smem_desc(a_base + kk * 32, 16, 1024);
                     const uint64_t bd = B_MN ? smem_desc(b_base + kk * 2048, BK * 128, 1024)
                                              : smem_desc(b_base + kk * 32, 16, 1024);
-                    tc_mma(d, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+                    mma(d, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
                 }
-                tc_commit(&empty[stage]);
+                commit(&empty[stage]);
                 if (++stage == C_::STAGES)
                 {
                     stage = 0;
                     phase ^= 1;
                 }
             }
-            tc_commit(&tfull[buf]);
+            commit(&tfull[buf]);
         }
     }
     else if (warp >= 2)
@@ -479,7 +337,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             const int buf = it & 1;
             const uint32_t tphase = (it >> 1) & 1;
             mbar_wait(&tfull[buf], tphase, p.status, abort);
-            tc_fence_after();
+            fence_after();
             const int row = mb * BM + quarter * 32 + lane;
             const uint32_t base = tmem + static_cast<uint32_t>(buf * BN) +
                                   (static_cast<uint32_t>(quarter * 32) << 16);
@@ -490,7 +348,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                 tmem_ld32(base + static_cast<uint32_t>(c), r);
                 store_chunk<BN>(p, row, nb * BN + c, r);
             }
-            tc_fence_before();
+            fence_before();
             __syncwarp();
             if (lane == 0)
             {
@@ -498,11 +356,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             }
         }
     }
-    tc_fence_before();
+    fence_before();
     __syncthreads();
     if (warp == 1)
     {
-        tc_fence_after();
+        fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(C_::TMEM_COLS));
     }
