@@ -412,7 +412,9 @@ def _attention_case(dtype, B, T, H, Hk, Dh, seed):
 
 @pytest.mark.parametrize("dtype,B,T,H,Hk,Dh", [(V.F32, 4, 32, 4, 2, 16), (V.F32, 2, 70, 4, 1, 64),
                                               (V.BF16, 2, 256, 16, 8, 128),
-                                              (V.BF16, 1, 200, 4, 2, 128)])
+                                              (V.BF16, 1, 200, 4, 2, 128),
+                                              (V.BF16, 1, 136, 4, 1, 128),
+                                              (V.BF16, 1, 100, 2, 2, 128)])
 def test_attention(dtype, B, T, H, Hk, Dh):
     o, o_ref, lse, lse_ref, dq, dq_ref, dk, dk_ref, dv, dv_ref = _attention_case(
         dtype, B, T, H, Hk, Dh, T + Dh)

@@ -14,6 +14,8 @@
 //     fp32 parity and the fallback for shapes the tiled kernels do not cover.
 #include "attention.cuh"
 
+#include <algorithm>
+
 namespace veda::cuda
 {
 namespace
@@ -255,11 +257,19 @@ using namespace veda::cuda;
 extern "C" size_t veda_attention_bwd_workspace(int64_t batch, int64_t seq_len, int64_t heads,
                                                int64_t kv_heads, int64_t head_dim, int dtype)
 {
-    // D = rowsum(dO * O) [B, H, T] fp32, plus the fp32 dQ accumulator of the tiled kernel.
-    size_t bytes = static_cast<size_t>(batch * heads * seq_len) * sizeof(float);
+    // D = rowsum(dO * O) [B, H, T] fp32, plus what the tiled kernels keep between launches: the
+    // fp32 dQ accumulator (mma.sync) or dS^T (tcgen05); sized for either, since the tcgen05 path
+    // falls back to the mma.sync one for shapes its tensor maps cannot describe.
+    size_t bytes = (static_cast<size_t>(batch * heads * seq_len) * sizeof(float) + 255) &
+                   ~static_cast<size_t>(255);
     if (flash_supported(head_dim, dtype))
     {
-        bytes += flash_bwd_extra_workspace(batch, seq_len, heads, kv_heads, head_dim);
+        size_t extra = flash_bwd_extra_workspace(batch, seq_len, heads, kv_heads, head_dim);
+        if (attention_tc_enabled())
+        {
+            extra = std::max(extra, tc_bwd_extra_workspace(batch, seq_len, heads));
+        }
+        bytes += extra;
     }
     return (bytes + 255) & ~static_cast<size_t>(255);
 }

@@ -22,6 +22,8 @@ inline bool flash_aligned(const void* a, int64_t lda, const void* b, int64_t ldb
 }
 
 size_t flash_bwd_extra_workspace(int64_t B, int64_t T, int64_t H, int64_t Hkv, int64_t Dh);
+// The tcgen05 backward keeps dS^T for every (batch, head) as bf16 [T x T] between its two kernels.
+size_t tc_bwd_extra_workspace(int64_t B, int64_t T, int64_t H);
 
 // tcgen05 kernels (attention_tc.cu): same contract as flash_fwd / flash_bwd (bf16, head_dim 128,
 // 16-byte aligned operands); return -1 when a tensor map cannot be built (caller falls back).

@@ -4,7 +4,8 @@
 // kv head h / (H/Hkv), src/libs/model/Attention.cpp:191); this file is the sm_100a-native form.
 //
 // Forward — one CTA per (batch, head, 128-query tile); 6 warps:
-//   warp 0     TMA: the Q tile once, then 128-key K and V tiles into a 2-stage ring
+//   warp 0     TMA (lane 0: the Q tile, then 128-key K tiles; lane 1: the V tiles), each into
+//              its own 2-stage ring so a K stage is refilled as soon as its QK^T has completed
 //              (3-D tensor maps [B, T, columns], so rows past T read as zeros; no multicast);
 //   warp 1     MMA issuer: S_j = Q K_j^T (M128 N128 K128) into one of two TMEM S buffers, then
 //              O += P_{j-1} V_{j-1} (M128 N128 K128, O in TMEM) — so the QK^T of the next tile
@@ -86,13 +87,15 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     uint8_t* sp = sv + 2 * kTileBytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sp + kTileBytes);
     uint64_t* q_full = bars + 0;
-    uint64_t* kv_full = bars + 1;    // [2]
-    uint64_t* kv_empty = bars + 3;   // [2]
-    uint64_t* s_full = bars + 5;     // [2]
-    uint64_t* s_free = bars + 7;     // [2]
-    uint64_t* p_full = bars + 9;
-    uint64_t* o_done = bars + 10;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    uint64_t* k_full = bars + 1;     // [2]
+    uint64_t* k_empty = bars + 3;    // [2]
+    uint64_t* v_full = bars + 5;     // [2]
+    uint64_t* v_empty = bars + 7;    // [2]
+    uint64_t* s_full = bars + 9;     // [2]
+    uint64_t* s_free = bars + 11;    // [2]
+    uint64_t* p_full = bars + 13;
+    uint64_t* o_done = bars + 14;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -109,8 +112,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
         mbar_init(q_full, 1);
         for (int i = 0; i < 2; ++i)
         {
-            mbar_init(&kv_full[i], 1);
-            mbar_init(&kv_empty[i], 1);
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
             mbar_init(&s_free[i], 4);
         }
@@ -129,18 +134,29 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
 
     if (warp == 0 && lane == 0)
     {
+        // Q, then the K ring: a K stage is free as soon as its QK^T product has completed
         tma_prefetch(&tq);
         tma_prefetch(&tk);
-        tma_prefetch(&tv);
         mbar_expect_tx(q_full, kTileBytes);
         load_tile_3d(sq, &tq, q_full, h * 128, qt * kTq, b);
         for (int j = 0; j < nk; ++j)
         {
             const int st = j & 1;
-            mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, p.status, abort);
-            mbar_expect_tx(&kv_full[st], 2 * kTileBytes);
-            load_tile_3d(sk + st * kTileBytes, &tk, &kv_full[st], kvh * 128, j * kTk, b);
-            load_tile_3d(sv + st * kTileBytes, &tv, &kv_full[st], kvh * 128, j * kTk, b);
+            mbar_wait(&k_empty[st], ((j >> 1) & 1) ^ 1, p.status, abort);
+            mbar_expect_tx(&k_full[st], kTileBytes);
+            load_tile_3d(sk + st * kTileBytes, &tk, &k_full[st], kvh * 128, j * kTk, b);
+        }
+    }
+    else if (warp == 0 && lane == 1)
+    {
+        // the V ring: a V stage is free once its P.V product has completed
+        tma_prefetch(&tv);
+        for (int j = 0; j < nk; ++j)
+        {
+            const int st = j & 1;
+            mbar_wait(&v_empty[st], ((j >> 1) & 1) ^ 1, p.status, abort);
+            mbar_expect_tx(&v_full[st], kTileBytes);
+            load_tile_3d(sv + st * kTileBytes, &tv, &v_full[st], kvh * 128, j * kTk, b);
         }
     }
     else if (warp == 1 && lane == 0)
@@ -150,6 +166,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
         const uint32_t q_base = smem_u32(sq), p_base = smem_u32(sp);
         mbar_wait(q_full, 0, p.status, abort);
         auto issue_pv = [&](int j) {
+            mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.status, abort);
             mbar_wait(p_full, j & 1, p.status, abort);
             fence_after();
             const uint32_t v_base = smem_u32(sv + (j & 1) * kTileBytes);
@@ -160,12 +177,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
                     (j > 0 || ks > 0) ? 1u : 0u);
             }
             commit(o_done);
-            commit(&kv_empty[j & 1]);
+            commit(&v_empty[j & 1]);
         };
         for (int j = 0; j < nk; ++j)
         {
             const int st = j & 1;
-            mbar_wait(&kv_full[st], (j >> 1) & 1, p.status, abort);
+            mbar_wait(&k_full[st], (j >> 1) & 1, p.status, abort);
             mbar_wait(&s_free[st], ((j >> 1) & 1) ^ 1, p.status, abort);
             fence_after();
             const uint32_t k_base = smem_u32(sk + st * kTileBytes);
@@ -176,6 +193,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
                     ks > 0 ? 1u : 0u);
             }
             commit(&s_full[st]);
+            commit(&k_empty[st]);
             if (j > 0)
             {
                 issue_pv(j - 1);
@@ -313,31 +331,34 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
 }
 
 // ---------------------------------------------------------------------------------------------
-// Backward — one CTA per (batch, KV head, 128-key tile); 6 warps. For every query head of the
-// GQA group and every 64-query tile at or after the diagonal:
-//   MMA   S^T = K Q^T and dP^T = V dO^T          (M128 keys, N64 queries, K128 dims)
-//   warps P^T = exp2(S^T scale log2e - LSE log2e), causal mask, dS^T = P^T (dP^T - D)
-//         -> bf16 into swizzled shared tiles
-//   MMA   dV += P^T dO, dK += dS^T Q             (M128 keys, N128 dims, K64 queries; in TMEM)
-//         dQ^T = K^T dS^T                        (M128 dims, N64 queries, K128 keys)
-//   warps dQ^T rows added to an fp32 accumulator with atomics (scaled and rounded afterwards).
-// The Q/dO tiles are staged once per iteration (2-stage ring) and serve both as K-major operands
-// (rows = queries = N) and as MN-major operands (rows = queries = K); the K tile likewise serves
-// S^T (K-major) and dQ^T (MN-major). dK and dV are summed over the group's heads in TMEM, so
-// they are written once and deterministically.
+// Backward, in two kernels.
+// (1) attn_bwd_tc_kernel — one CTA per (batch, KV head, 128-key tile); 10 warps. For every query
+//     head of the GQA group and every 64-query tile at or after the diagonal:
+//       MMA    S^T = K Q^T and dP^T = V dO^T    (M128 keys, N64 queries, K128 dims) into one of
+//              two TMEM buffers, so the products of tile i+1 run while tile i is elementwise;
+//       warps  (8, two per TMEM lane quarter, 32 query columns each)
+//              P^T = exp2(S^T scale log2e - LSE log2e), causal mask, dS^T = P^T (dP^T - D),
+//              bf16 into double-buffered swizzled shared tiles; dS^T also goes to HBM by TMA;
+//       MMA    dV += P^T dO, dK += dS^T Q        (M128 keys, N128 dims, K64 queries; TMEM).
+//     dK and dV are summed over the group's heads in TMEM: written once, deterministically.
+// (2) attn_dq_tc_kernel — one CTA per (batch, head, 128-query tile): dQ = sum over key tiles of
+//     dS K (M128 queries, N128 dims, K128 keys) from the stored dS^T, accumulated in TMEM — no
+//     atomics, so dQ is deterministic too.
+// The Q/dO tiles are staged once per tile and serve both as K-major operands (rows = queries = N)
+// and as MN-major operands (rows = queries = K); likewise K for S^T and the dQ product.
 // ---------------------------------------------------------------------------------------------
 constexpr int kBq = 64;                      // queries per backward iteration
 constexpr int kQTileBytes = kBq * 128 * 2;   // [64 rows x 128 dims] = two 8 KB halves
 constexpr int kQHalf = kQTileBytes / 2;
 constexpr int kPTileBytes = 128 * kBq * 2;   // [128 keys x 64 queries]
-// alignment slack | K, V | Q[2], dO[2] | P^T, dS^T | LSE/D staging (1 KB) + barriers
-constexpr int kBwdSmem = 1024 + 2 * kTileBytes + 4 * kQTileBytes + 2 * kPTileBytes + 2048;
+constexpr int kComputeThreads = 256;
+// alignment slack | K, V | Q[2], dO[2] | P^T[2], dS^T[2] | LSE/D staging (1 KB) + barriers
+constexpr int kBwdSmem = 1024 + 2 * kTileBytes + 4 * kQTileBytes + 4 * kPTileBytes + 2048;
 
 struct BwdParams
 {
     const float* lse;
     const float* dvec;
-    float* dq_acc;   // [B*T, H*128]
     bf16 *dk, *dv;
     int64_t lddk, lddv;
     int T, H, Hkv;
@@ -346,9 +367,9 @@ struct BwdParams
     int* status;
 };
 
-__device__ __forceinline__ void named_sync_compute()
+__device__ __forceinline__ void named_sync(int id, int count)
 {
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 __device__ __forceinline__ void load_qtile_3d(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
@@ -358,10 +379,16 @@ __device__ __forceinline__ void load_qtile_3d(uint8_t* dst, const CUtensorMap* m
     tma_load_3d(dst + kQHalf, map, bar, col + 64, row, batch);
 }
 
-__global__ void __launch_bounds__(192, 1)
+__device__ __forceinline__ uint32_t pack2(float a, float b)
+{
+    const __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&t);
+}
+
+__global__ void __launch_bounds__(320, 1)
 attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                   const BwdParams p)
+                   const __grid_constant__ CUtensorMap tds, const BwdParams p)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -370,20 +397,19 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     uint8_t* sv = sk + kTileBytes;
     uint8_t* sq = sv + kTileBytes;             // [2]
     uint8_t* sdo = sq + 2 * kQTileBytes;       // [2]
-    uint8_t* sp = sdo + 2 * kQTileBytes;
-    uint8_t* sds = sp + kPTileBytes;
-    float* sld = reinterpret_cast<float*>(sds + kPTileBytes);   // [2][2][64]: LSE*log2e, D
+    uint8_t* sp = sdo + 2 * kQTileBytes;       // [2]
+    uint8_t* sds = sp + 2 * kPTileBytes;       // [2]
+    float* sld = reinterpret_cast<float*>(sds + 2 * kPTileBytes);   // [2][2][64]: LSE*log2e, D
     uint64_t* bars = reinterpret_cast<uint64_t*>(sld + 4 * kBq);
     uint64_t* kv_full = bars + 0;
     uint64_t* qd_full = bars + 1;    // [2]
     uint64_t* qd_empty = bars + 3;   // [2]
-    uint64_t* sp_full = bars + 5;
-    uint64_t* st_free = bars + 6;
-    uint64_t* ds_full = bars + 7;
-    uint64_t* pds_free = bars + 8;
-    uint64_t* dq_full = bars + 9;
-    uint64_t* dq_free = bars + 10;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    uint64_t* sp_full = bars + 5;    // [2]
+    uint64_t* st_free = bars + 7;    // [2]
+    uint64_t* ds_full = bars + 9;    // [2]
+    uint64_t* pds_free = bars + 11;  // [2]
+    uint64_t* done = bars + 13;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -404,13 +430,12 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
         {
             mbar_init(&qd_full[i], 1);
             mbar_init(&qd_empty[i], 1);
+            mbar_init(&sp_full[i], 1);
+            mbar_init(&st_free[i], 8);
+            mbar_init(&ds_full[i], 8);
+            mbar_init(&pds_free[i], 1);
         }
-        mbar_init(sp_full, 1);
-        mbar_init(st_free, 4);
-        mbar_init(ds_full, 4);
-        mbar_init(pds_free, 1);
-        mbar_init(dq_full, 1);
-        mbar_init(dq_free, 4);
+        mbar_init(done, 1);
         mbar_fence_init();
     }
     if (warp == 1)
@@ -421,7 +446,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
-    constexpr uint32_t kST = 0, kDPT = 64, kDV = 128, kDK = 256, kDQT = 384;
+    constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 384;   // S^T, dP^T: 2 x 64 each
 
     if (warp == 0 && lane == 0)
     {
@@ -447,66 +472,79 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     {
         constexpr uint32_t idesc_s = instr_desc(128, kBq, false, false);
         constexpr uint32_t idesc_kv = instr_desc(128, 128, false, true);
-        constexpr uint32_t idesc_q = instr_desc(128, kBq, true, true);
         const uint32_t k_base = smem_u32(sk), v_base = smem_u32(sv);
-        const uint32_t p_base = smem_u32(sp), ds_base = smem_u32(sds);
         mbar_wait(kv_full, 0, p.status, abort);
+        auto issue_dvdk = [&](int i) {
+            const int s = i & 1;
+            mbar_wait(&ds_full[s], (i >> 1) & 1, p.status, abort);
+            fence_after();
+            const uint32_t q_base = smem_u32(sq + s * kQTileBytes);
+            const uint32_t do_base = smem_u32(sdo + s * kQTileBytes);
+            const uint32_t p_base = smem_u32(sp + s * kPTileBytes);
+            const uint32_t ds_base = smem_u32(sds + s * kPTileBytes);
+#pragma unroll
+            for (int ks = 0; ks < kBq / 16; ++ks)
+            {
+                const uint32_t acc = (i > 0 || ks > 0) ? 1u : 0u;
+                mma(tmem + kDV, smem_desc(p_base + ks * 32, 16, 1024),
+                    mnmajor_desc(do_base, ks, kQHalf), idesc_kv, acc);
+                mma(tmem + kDK, smem_desc(ds_base + ks * 32, 16, 1024),
+                    mnmajor_desc(q_base, ks, kQHalf), idesc_kv, acc);
+            }
+            commit(&pds_free[s]);
+            commit(&qd_empty[s]);
+        };
         for (int it = 0; it < iters; ++it)
         {
             const int st = it & 1;
             const uint32_t q_base = smem_u32(sq + st * kQTileBytes);
             const uint32_t do_base = smem_u32(sdo + st * kQTileBytes);
             mbar_wait(&qd_full[st], (it >> 1) & 1, p.status, abort);
-            mbar_wait(st_free, (it & 1) ^ 1, p.status, abort);
+            mbar_wait(&st_free[st], ((it >> 1) & 1) ^ 1, p.status, abort);
             fence_after();
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks)
             {
                 const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;
-                mma(tmem + kST, kmajor_desc(k_base, ks), smem_desc(q_base + off, 16, 1024), idesc_s,
-                    ks > 0 ? 1u : 0u);
-                mma(tmem + kDPT, kmajor_desc(v_base, ks), smem_desc(do_base + off, 16, 1024),
+                mma(tmem + kST + st * kBq, kmajor_desc(k_base, ks), smem_desc(q_base + off, 16, 1024),
                     idesc_s, ks > 0 ? 1u : 0u);
+                mma(tmem + kDPT + st * kBq, kmajor_desc(v_base, ks),
+                    smem_desc(do_base + off, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
             }
-            commit(sp_full);
-            mbar_wait(ds_full, it & 1, p.status, abort);
-            fence_after();
-#pragma unroll
-            for (int ks = 0; ks < kBq / 16; ++ks)
+            commit(&sp_full[st]);
+            if (it > 0)
             {
-                const uint32_t acc = (it > 0 || ks > 0) ? 1u : 0u;
-                mma(tmem + kDV, smem_desc(p_base + ks * 32, 16, 1024),
-                    mnmajor_desc(do_base, ks, kQHalf), idesc_kv, acc);
-                mma(tmem + kDK, smem_desc(ds_base + ks * 32, 16, 1024),
-                    mnmajor_desc(q_base, ks, kQHalf), idesc_kv, acc);
+                issue_dvdk(it - 1);
             }
-            mbar_wait(dq_free, (it & 1) ^ 1, p.status, abort);
-            fence_after();
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks)
-            {
-                mma(tmem + kDQT, mnmajor_desc(k_base, ks, kHalf), mnmajor_desc(ds_base, ks, kHalf),
-                    idesc_q, ks > 0 ? 1u : 0u);
-            }
-            commit(dq_full);
-            commit(pds_free);
-            commit(&qd_empty[st]);
         }
+        if (iters > 0)
+        {
+            issue_dvdk(iters - 1);
+        }
+        commit(done);
     }
     else if (warp >= 2)
     {
+        const int cw = warp - 2;                // 0..7
         const int quarter = warp & 3;
-        const int r = quarter * 32 + lane;   // key row (S^T, dP^T, dV, dK) or dim row (dQ^T)
+        const int half = cw >> 2;               // query columns [32 half, 32 half + 32)
+        const int r = quarter * 32 + lane;      // key row
         const int key = kt * 128 + r;
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-        const int tid = threadIdx.x - 64;    // 0..127 among the compute warps
-        const int64_t width = static_cast<int64_t>(p.H) * 128;
+        const int tid = threadIdx.x - 64;       // 0..255
+        const bool issuer = tid == 0;           // issues the dS^T stores
         for (int it = 0; it < iters; ++it)
         {
+            const int st = it & 1;
             const int h = kvh * rep + it / per_head;
             const int q0 = (qi0 + it % per_head) * kBq;
-            float* lse2 = sld + (it & 1) * 2 * kBq;
+            if (issuer && it >= 2)
+            {
+                bulk_wait_group_read<1>();      // the store of tile it-2 has read its dS^T buffer
+            }
+            float* lse2 = sld + st * 2 * kBq;
             float* dd = lse2 + kBq;
+            if (tid < 2 * kBq)
             {
                 const int c = tid & (kBq - 1);
                 const int q = q0 + c;
@@ -520,80 +558,68 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
                     dd[c] = q < p.T ? p.dvec[at] : 0.0f;
                 }
             }
-            named_sync_compute();
-            mbar_wait(sp_full, it & 1, p.status, abort);
+            named_sync(1, kComputeThreads);
+            mbar_wait(&sp_full[st], (it >> 1) & 1, p.status, abort);
             fence_after();
-            uint32_t sraw[64], draw[64];
-            tmem_ld32(tmem + lane_base + kST, *reinterpret_cast<uint32_t(*)[32]>(sraw));
-            tmem_ld32(tmem + lane_base + kST + 32, *reinterpret_cast<uint32_t(*)[32]>(sraw + 32));
-            tmem_ld32(tmem + lane_base + kDPT, *reinterpret_cast<uint32_t(*)[32]>(draw));
-            tmem_ld32(tmem + lane_base + kDPT + 32, *reinterpret_cast<uint32_t(*)[32]>(draw + 32));
+            uint32_t sraw[32], draw[32];
+            tmem_ld32(tmem + lane_base + kST + st * kBq + half * 32, sraw);
+            tmem_ld32(tmem + lane_base + kDPT + st * kBq + half * 32, draw);
             fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(st_free);
+            if (lane == 0) mbar_arrive(&st_free[st]);
             const bool maybe_masked = p.causal && q0 < kt * 128 + 128;
-            float pv[64], dsv[64];
+            float pv[32], dsv[32];
 #pragma unroll
-            for (int c = 0; c < kBq; ++c)
+            for (int c = 0; c < 32; ++c)
             {
-                float pr = exp2f(__uint_as_float(sraw[c]) * p.scale_log2 - lse2[c]);
-                if (maybe_masked && key > q0 + c) pr = 0.0f;
+                const int col = half * 32 + c;
+                float pr = exp2f(__uint_as_float(sraw[c]) * p.scale_log2 - lse2[col]);
+                if (maybe_masked && key > q0 + col) pr = 0.0f;
                 pv[c] = pr;
-                dsv[c] = pr * (__uint_as_float(draw[c]) - dd[c]);
+                dsv[c] = pr * (__uint_as_float(draw[c]) - dd[col]);
             }
-            mbar_wait(pds_free, (it & 1) ^ 1, p.status, abort);
+            mbar_wait(&pds_free[st], ((it >> 1) & 1) ^ 1, p.status, abort);
+            uint8_t* pt = sp + st * kPTileBytes;
+            uint8_t* dt = sds + st * kPTileBytes;
 #pragma unroll
-            for (int c8 = 0; c8 < kBq / 8; ++c8)
+            for (int c8 = 0; c8 < 4; ++c8)
             {
+                const int chunk = half * 4 + c8;
                 uint4 a, d;
-                __nv_bfloat162 t;
-                t = __floats2bfloat162_rn(pv[c8 * 8 + 0], pv[c8 * 8 + 1]); a.x = *reinterpret_cast<uint32_t*>(&t);
-                t = __floats2bfloat162_rn(pv[c8 * 8 + 2], pv[c8 * 8 + 3]); a.y = *reinterpret_cast<uint32_t*>(&t);
-                t = __floats2bfloat162_rn(pv[c8 * 8 + 4], pv[c8 * 8 + 5]); a.z = *reinterpret_cast<uint32_t*>(&t);
-                t = __floats2bfloat162_rn(pv[c8 * 8 + 6], pv[c8 * 8 + 7]); a.w = *reinterpret_cast<uint32_t*>(&t);
-                t = __floats2bfloat162_rn(dsv[c8 * 8 + 0], dsv[c8 * 8 + 1]); d.x = *reinterpret_cast<uint32_t*>(&t);
-                t = __floats2bfloat162_rn(dsv[c8 * 8 + 2], dsv[c8 * 8 + 3]); d.y = *reinterpret_cast<uint32_t*>(&t);
-                t = __floats2bfloat162_rn(dsv[c8 * 8 + 4], dsv[c8 * 8 + 5]); d.z = *reinterpret_cast<uint32_t*>(&t);
-                t = __floats2bfloat162_rn(dsv[c8 * 8 + 6], dsv[c8 * 8 + 7]); d.w = *reinterpret_cast<uint32_t*>(&t);
-                *reinterpret_cast<uint4*>(sp + sw128_offset(r, c8)) = a;
-                *reinterpret_cast<uint4*>(sds + sw128_offset(r, c8)) = d;
+                a.x = pack2(pv[c8 * 8 + 0], pv[c8 * 8 + 1]);
+                a.y = pack2(pv[c8 * 8 + 2], pv[c8 * 8 + 3]);
+                a.z = pack2(pv[c8 * 8 + 4], pv[c8 * 8 + 5]);
+                a.w = pack2(pv[c8 * 8 + 6], pv[c8 * 8 + 7]);
+                d.x = pack2(dsv[c8 * 8 + 0], dsv[c8 * 8 + 1]);
+                d.y = pack2(dsv[c8 * 8 + 2], dsv[c8 * 8 + 3]);
+                d.z = pack2(dsv[c8 * 8 + 4], dsv[c8 * 8 + 5]);
+                d.w = pack2(dsv[c8 * 8 + 6], dsv[c8 * 8 + 7]);
+                *reinterpret_cast<uint4*>(pt + sw128_offset(r, chunk)) = a;
+                *reinterpret_cast<uint4*>(dt + sw128_offset(r, chunk)) = d;
             }
             fence_proxy_async();
             fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(ds_full);
-            // dQ^T: this thread holds dims row r for the 64 queries of the tile
-            mbar_wait(dq_full, it & 1, p.status, abort);
-            fence_after();
-            uint32_t qraw[64];
-            tmem_ld32(tmem + lane_base + kDQT, *reinterpret_cast<uint32_t(*)[32]>(qraw));
-            tmem_ld32(tmem + lane_base + kDQT + 32, *reinterpret_cast<uint32_t(*)[32]>(qraw + 32));
-            fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(dq_free);
-            float* dst = p.dq_acc + (static_cast<int64_t>(b) * p.T + q0) * width +
-                         static_cast<int64_t>(h) * 128 + r;
-            const int nvalid = min(kBq, p.T - q0);
-#pragma unroll
-            for (int c = 0; c < kBq; ++c)
+            if (lane == 0) mbar_arrive(&ds_full[st]);
+            named_sync(2, kComputeThreads);     // every row of dS^T is in shared memory
+            if (issuer)
             {
-                if (c < nvalid)
-                {
-                    atomicAdd(dst + static_cast<int64_t>(c) * width, __uint_as_float(qraw[c]));
-                }
+                tma_store_3d(&tds, dt, q0, kt * 128, b * p.H + h);
+                bulk_commit_group();
             }
         }
-        // dV and dK rows of this key (summed over the group's heads in TMEM)
-        if (iters > 0)
+        if (issuer)
         {
-            mbar_wait(dq_full, (iters - 1) & 1, p.status, abort);   // already passed: no-op
+            bulk_wait_group<0>();
         }
+        // dV and dK rows of this key (summed over the group's heads in TMEM): 64 dims per warp
+        mbar_wait(done, 0, p.status, abort);
         fence_after();
         const bool valid = key < p.T;
         bf16* vrow = p.dv + (static_cast<int64_t>(b) * p.T + key) * p.lddv + static_cast<int64_t>(kvh) * 128;
         bf16* krow = p.dk + (static_cast<int64_t>(b) * p.T + key) * p.lddk + static_cast<int64_t>(kvh) * 128;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c)
+        for (int c = half * 2; c < half * 2 + 2; ++c)
         {
             uint32_t rv[32], rk[32];
             tmem_ld32(tmem + lane_base + kDV + c * 32, rv);
@@ -625,6 +651,136 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     }
 }
 
+// dQ[q-tile] = sum over key tiles of dS K, from dS^T stored as [B*H][keys][queries].
+// One CTA per (batch, head, 128-query tile); warp 0 TMA (3-stage ring of a dS^T tile and a K tile),
+// warp 1 MMA (M128 queries, N128 dims, K128 keys; both operands MN-major), warps 2-5 epilogue.
+constexpr int kDqStages = 3;
+constexpr int kDqSmem = 1024 + kDqStages * 2 * kTileBytes + 256;
+
+struct DqParams
+{
+    bf16* dq;
+    int64_t lddq;
+    int T, H, Hkv;
+    float scale;
+    int causal;
+    int* status;
+};
+
+__global__ void __launch_bounds__(192, 1)
+attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tds, const __grid_constant__ CUtensorMap tk,
+                  const DqParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* sds = smem;                                   // [stages]
+    uint8_t* sk = sds + kDqStages * kTileBytes;            // [stages]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sk + kDqStages * kTileBytes);
+    uint64_t* full = bars;                  // [stages]
+    uint64_t* empty = bars + kDqStages;     // [stages]
+    uint64_t* done = bars + 2 * kDqStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nq = (p.T + 127) / 128;
+    const int qt = nq - 1 - static_cast<int>(blockIdx.x);
+    const int bh = blockIdx.y;
+    const int b = bh / p.H, h = bh % p.H;
+    const int kvh = h / (p.H / p.Hkv);
+    const int nk = p.causal ? qt + 1 : nq;
+
+    if (threadIdx.x == 0)
+    {
+        *abort = 0;
+        for (int s = 0; s < kDqStages; ++s)
+        {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1)
+    {
+        tmem_alloc(tmem_slot, 128);
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0)
+    {
+        tma_prefetch(&tds);
+        tma_prefetch(&tk);
+        for (int j = 0; j < nk; ++j)
+        {
+            const int s = j % kDqStages;
+            mbar_wait(&empty[s], ((j / kDqStages) & 1) ^ 1, p.status, abort);
+            mbar_expect_tx(&full[s], 2 * kTileBytes);
+            // dS^T tile: rows = keys j*128.., columns = this tile's 128 queries
+            load_tile_3d(sds + s * kTileBytes, &tds, &full[s], qt * 128, j * 128, bh);
+            load_tile_3d(sk + s * kTileBytes, &tk, &full[s], kvh * 128, j * 128, b);
+        }
+    }
+    else if (warp == 1 && lane == 0)
+    {
+        constexpr uint32_t idesc = instr_desc(128, 128, true, true);
+        for (int j = 0; j < nk; ++j)
+        {
+            const int s = j % kDqStages;
+            mbar_wait(&full[s], (j / kDqStages) & 1, p.status, abort);
+            fence_after();
+            const uint32_t a_base = smem_u32(sds + s * kTileBytes);
+            const uint32_t b_base = smem_u32(sk + s * kTileBytes);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+            {
+                mma(tmem, mnmajor_desc(a_base, ks, kHalf), mnmajor_desc(b_base, ks, kHalf), idesc,
+                    (j > 0 || ks > 0) ? 1u : 0u);
+            }
+            commit(&empty[s]);
+        }
+        commit(done);
+    }
+    else if (warp >= 2)
+    {
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const int query = qt * 128 + r;
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        mbar_wait(done, 0, p.status, abort);
+        fence_after();
+        bf16* row = p.dq + (static_cast<int64_t>(b) * p.T + query) * p.lddq + static_cast<int64_t>(h) * 128;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c)
+        {
+            uint32_t raw[32];
+            tmem_ld32(tmem + lane_base + c * 32, raw);
+            if (query < p.T)
+            {
+#pragma unroll
+                for (int e = 0; e < 32; e += 8)
+                {
+                    float v8[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) v8[q] = nk > 0 ? __uint_as_float(raw[e + q]) * p.scale : 0.0f;
+                    store16(row + c * 32 + e, v8);
+                }
+            }
+        }
+    }
+    fence_before();
+    __syncthreads();
+    if (warp == 1)
+    {
+        fence_after();
+        tmem_dealloc(tmem, 128);
+    }
+}
+
 // D[b,h,t] = sum_d dO * O over the head's 128 dims; one warp per row.
 __global__ void attn_rowdot_kernel(const bf16* __restrict__ o, int64_t ldo,
                                    const bf16* __restrict__ dout, int64_t lddo,
@@ -647,25 +803,6 @@ __global__ void attn_rowdot_kernel(const bf16* __restrict__ o, int64_t ldo,
         }
         s = warp_sum(s);
         if (lane == 0) dvec[(b * H + h) * T + i] = s;
-    }
-}
-
-// dq = bf16(scale * acc)
-__global__ void attn_dq_convert_kernel(const float* __restrict__ acc, bf16* __restrict__ dq,
-                                       int64_t lddq, int64_t rows, int64_t width, float scale)
-{
-    const int64_t total = rows * width / 4;
-    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    {
-        const int64_t r = (idx * 4) / width, c = (idx * 4) % width;
-        const float4 v = reinterpret_cast<const float4*>(acc)[idx];
-        const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x * scale, v.y * scale);
-        const __nv_bfloat162 hi = __floats2bfloat162_rn(v.z * scale, v.w * scale);
-        uint2 packed;
-        packed.x = *reinterpret_cast<const uint32_t*>(&lo);
-        packed.y = *reinterpret_cast<const uint32_t*>(&hi);
-        *reinterpret_cast<uint2*>(dq + r * lddq + c) = packed;
     }
 }
 
@@ -745,16 +882,27 @@ int attn_tc_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     return check_launch("veda_attention_fwd (tcgen05)");
 }
 
+size_t tc_bwd_extra_workspace(int64_t B, int64_t T, int64_t H)
+{
+    return static_cast<size_t>(B * H) * static_cast<size_t>(T) * static_cast<size_t>(T) * sizeof(bf16);
+}
+
 int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
                 const void* o, int64_t ldo, const void* dout, int64_t lddo, const float* lse,
                 void* dq, int64_t lddq, void* dk, int64_t lddk, void* dv, int64_t lddv, float* dvec,
                 void* extra, int64_t B, int64_t T, int64_t H, int64_t Hkv, float scale, int causal,
                 cudaStream_t s)
 {
-    CUtensorMap mq, mk, mv, mdo;
+    // dS^T rows are T bf16 wide: the tensor map needs their byte stride to be a multiple of 16.
+    if (T % 8 != 0 || B * H > 65535)
+    {
+        return -1;
+    }
+    CUtensorMap mq, mk, mv, mdo, mds;
     if (!make_map3(&mq, q, H * 128, T, B, ldq, kBq) || !make_map3(&mk, k, Hkv * 128, T, B, ldk, 128) ||
         !make_map3(&mv, v, Hkv * 128, T, B, ldv, 128) ||
-        !make_map3(&mdo, dout, H * 128, T, B, lddo, kBq))
+        !make_map3(&mdo, dout, H * 128, T, B, lddo, kBq) ||
+        !make_map3(&mds, extra, T, T, B * H, T, 128))
     {
         return -1;   // caller falls back
     }
@@ -764,23 +912,20 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     if (configured != device)
     {
         cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
+        cudaFuncSetAttribute(attn_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDqSmem);
         configured = device;
-    }
-    float* acc = static_cast<float*>(extra);
-    const int64_t width = H * 128;
-    if (cudaMemsetAsync(acc, 0, static_cast<size_t>(B * T * width) * sizeof(float), s) != cudaSuccess)
-    {
-        return fail(VEDA_ERR_CUDA, "veda_attention_bwd: clearing the dQ accumulator failed");
     }
     attn_rowdot_kernel<<<grid_for(B * H * T * 32, 256), 256, 0, s>>>(
         static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, dvec, B, T, H);
-    BwdParams p{lse, dvec, acc, static_cast<bf16*>(dk), static_cast<bf16*>(dv), lddk, lddv,
+    BwdParams p{lse, dvec, static_cast<bf16*>(dk), static_cast<bf16*>(dv), lddk, lddv,
                 static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
                 scale * kLog2e, causal, device_status_ptr()};
     const dim3 grid(static_cast<unsigned>((T + 127) / 128), static_cast<unsigned>(B * Hkv));
-    attn_bwd_tc_kernel<<<grid, 192, kBwdSmem, s>>>(mq, mk, mv, mdo, p);
-    attn_dq_convert_kernel<<<grid_for(B * T * width / 4, 256), 256, 0, s>>>(
-        acc, static_cast<bf16*>(dq), lddq, B * T, width, scale);
+    attn_bwd_tc_kernel<<<grid, 64 + kComputeThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, mds, p);
+    DqParams pq{static_cast<bf16*>(dq), lddq, static_cast<int>(T), static_cast<int>(H),
+                static_cast<int>(Hkv), scale, causal, device_status_ptr()};
+    const dim3 gq(static_cast<unsigned>((T + 127) / 128), static_cast<unsigned>(B * H));
+    attn_dq_tc_kernel<<<gq, 192, kDqSmem, s>>>(mds, mk, pq);
     count_launch(3);
     return check_launch("veda_attention_bwd (tcgen05)");
 }
