@@ -3,18 +3,20 @@
 // Same semantics as attention_flash.cu (the composition of src/libs/train/Model.cpp:182-189 with
 // kv head h / (H/Hkv), src/libs/model/Attention.cpp:191); this file is the sm_100a-native form.
 //
-// Forward — one CTA per (batch, head, 128-query tile); 6 warps:
-//   warp 0     TMA (lane 0: the Q tile, then 128-key K tiles; lane 1: the V tiles), each into
-//              its own 2-stage ring so a K stage is refilled as soon as its QK^T has completed
-//              (3-D tensor maps [B, T, columns], so rows past T read as zeros; no multicast);
-//   warp 1     MMA issuer: S_j = Q K_j^T (M128 N128 K128) into one of two TMEM S buffers, then
-//              O += P_{j-1} V_{j-1} (M128 N128 K128, O in TMEM) — so the QK^T of the next tile
-//              runs while the softmax warps work on the current one;
-//   warps 2-5  softmax: thread i owns query row i (TMEM lane i): loads its S row, masks, keeps
-//              a running max in the log2 domain and rescales O in TMEM only when the max grows
-//              by more than 2^8 (otherwise the stale max is kept; every exponent stays below 2^8),
-//              writes P (bf16) into a 128-byte-swizzled shared tile for the P.V product, and at
-//              the end writes O / l and LSE = (m + log2 l) ln 2.
+// Forward — one CTA per (batch, head, pair of 128-query tiles A and B); 10 warps:
+//   warp 0     TMA (lane 0: both Q tiles, then 128-key K tiles; lane 1: the V tiles), each into
+//              its own 2-stage ring shared by the two query tiles (3-D tensor maps [B, T, columns],
+//              so rows past T read as zeros; no multicast);
+//   warp 1     MMA issuer, ping-pong between the query tiles: per key tile j it issues
+//              O_A += P_A V_j, S_A = Q_A K_{j+1}^T, O_B += P_B V_j, S_B = Q_B K_{j+1}^T
+//              (M128 N128 K128 each; S, P and O all in TMEM, P read by the MMA straight from
+//              tensor memory), so the tensor core computes one tile's products while the softmax
+//              warps of the other work;
+//   warps 2-5  softmax of tile A, warps 6-9 of tile B: thread i owns query row i (TMEM lane i):
+//              loads its S row, masks, keeps a running max in the log2 domain and rescales O in
+//              TMEM only when the max grows by more than 2^8 (otherwise the stale max is kept;
+//              every exponent stays below 2^8), writes P (bf16 pairs) over the first half of its
+//              S columns, and at the end writes O / l and LSE = (m + log2 l) ln 2.
 // Every mbarrier wait is bounded (see tc_common.cuh).
 #include "attention.cuh"
 #include "tc_common.cuh"
@@ -51,9 +53,6 @@ struct FwdParams
     int* status;
 };
 
-// smem: Q | K[2] | V[2] | P | barriers
-constexpr int kFwdSmem = 1024 + kTileBytes * 6 + 256;
-
 __device__ __forceinline__ void load_tile_3d(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
                                              int col, int row, int batch)
 {
@@ -74,37 +73,80 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int ks, uint32_t
     return smem_desc(base + ks * 2048, lbo, 1024);
 }
 
-__global__ void __launch_bounds__(192, 1)
+// smem: Q[2] | K[2] | V[2] | barriers
+constexpr int kFwdThreads = 320;
+constexpr int kFwdSmem = 1024 + kTileBytes * 6 + 256;
+
+__device__ __forceinline__ uint64_t f2_pack(float a, float b)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b)
+{
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// 2^x with the hardware approximation (relative error far below bf16 rounding; -inf -> 0)
+__device__ __forceinline__ float ex2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float max3(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, const FwdParams p)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t* sq = smem;
-    uint8_t* sk = sq + kTileBytes;           // [2]
+    uint8_t* sq = smem;                      // [2]: the pair's two query tiles
+    uint8_t* sk = sq + 2 * kTileBytes;       // [2]
     uint8_t* sv = sk + 2 * kTileBytes;       // [2]
-    uint8_t* sp = sv + 2 * kTileBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sp + kTileBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sv + 2 * kTileBytes);
     uint64_t* q_full = bars + 0;
-    uint64_t* k_full = bars + 1;     // [2]
+    uint64_t* k_full = bars + 1;     // [2] ring stages
     uint64_t* k_empty = bars + 3;    // [2]
     uint64_t* v_full = bars + 5;     // [2]
     uint64_t* v_empty = bars + 7;    // [2]
-    uint64_t* s_full = bars + 9;     // [2]
-    uint64_t* s_free = bars + 11;    // [2]
-    uint64_t* p_full = bars + 13;
-    uint64_t* o_done = bars + 14;
+    uint64_t* s_full = bars + 9;     // [2] per query tile
+    uint64_t* p_full = bars + 11;    // [2] per query tile
+    uint64_t* o_done = bars + 13;    // [2] per query tile
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nq = (p.T + kTq - 1) / kTq;
-    const int qt = nq - 1 - static_cast<int>(blockIdx.x);   // longest rows first
+    const int nkt = (p.T + kTk - 1) / kTk;
+    const int npairs = (nq + 1) / 2;
+    const int qt0 = 2 * (npairs - 1 - static_cast<int>(blockIdx.x));   // longest rows first
+    const bool has_b = qt0 + 1 < nq;
     const int bh = blockIdx.y;
     const int b = bh / p.H, h = bh % p.H;
     const int kvh = h / (p.H / p.Hkv);
-    const int nk = p.causal ? qt + 1 : (p.T + kTk - 1) / kTk;
+    const int n_a = p.causal ? qt0 + 1 : nkt;
+    const int n_b = has_b ? (p.causal ? qt0 + 2 : nkt) : 0;
+    const int nmax = n_a > n_b ? n_a : n_b;
 
     if (threadIdx.x == 0)
     {
@@ -117,10 +159,9 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 4);
+            mbar_init(&p_full[i], 4);
+            mbar_init(&o_done[i], 1);
         }
-        mbar_init(p_full, 4);
-        mbar_init(o_done, 1);
         mbar_fence_init();
     }
     if (warp == 1)
@@ -131,15 +172,19 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    // TMEM columns: S_A | S_B | O_A | O_B (128 each); P_x (bf16 pairs) overwrites S_x's first 64
 
     if (warp == 0 && lane == 0)
     {
-        // Q, then the K ring: a K stage is free as soon as its QK^T product has completed
         tma_prefetch(&tq);
         tma_prefetch(&tk);
-        mbar_expect_tx(q_full, kTileBytes);
-        load_tile_3d(sq, &tq, q_full, h * 128, qt * kTq, b);
-        for (int j = 0; j < nk; ++j)
+        mbar_expect_tx(q_full, (has_b ? 2 : 1) * kTileBytes);
+        load_tile_3d(sq, &tq, q_full, h * 128, qt0 * kTq, b);
+        if (has_b)
+        {
+            load_tile_3d(sq + kTileBytes, &tq, q_full, h * 128, (qt0 + 1) * kTq, b);
+        }
+        for (int j = 0; j < nmax; ++j)
         {
             const int st = j & 1;
             mbar_wait(&k_empty[st], ((j >> 1) & 1) ^ 1, p.status, abort);
@@ -149,9 +194,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     }
     else if (warp == 0 && lane == 1)
     {
-        // the V ring: a V stage is free once its P.V product has completed
         tma_prefetch(&tv);
-        for (int j = 0; j < nk; ++j)
+        for (int j = 0; j < nmax; ++j)
         {
             const int st = j & 1;
             mbar_wait(&v_empty[st], ((j >> 1) & 1) ^ 1, p.status, abort);
@@ -161,101 +205,140 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     }
     else if (warp == 1 && lane == 0)
     {
+        // Order per key tile j: P_A V_j, S_A(j+1), P_B V_j, S_B(j+1) — so the tensor core works
+        // on one query tile while the softmax warps of the other compute its probabilities.
+        // An S_x(j+1) issued after P_x V_j overwrites P_x only once that product has read it
+        // (the MMAs of one thread execute in issue order).
         constexpr uint32_t idesc_s = instr_desc(128, 128, false, false);
         constexpr uint32_t idesc_o = instr_desc(128, 128, false, true);
-        const uint32_t q_base = smem_u32(sq), p_base = smem_u32(sp);
-        mbar_wait(q_full, 0, p.status, abort);
-        auto issue_pv = [&](int j) {
-            mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.status, abort);
-            mbar_wait(p_full, j & 1, p.status, abort);
+        const uint32_t q_base = smem_u32(sq);
+        auto issue_s = [&](int x, int j) {
+            const uint32_t k_base = smem_u32(sk + (j & 1) * kTileBytes);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+            {
+                mma(tmem + x * 128, kmajor_desc(q_base + x * kTileBytes, ks), kmajor_desc(k_base, ks),
+                    idesc_s, ks > 0 ? 1u : 0u);
+            }
+            commit(&s_full[x]);
+        };
+        auto issue_pv = [&](int x, int j, int n) {
+            mbar_wait(&p_full[x], j & 1, p.status, abort);
             fence_after();
             const uint32_t v_base = smem_u32(sv + (j & 1) * kTileBytes);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks)
             {
-                mma(tmem + 256, kmajor_desc(p_base, ks), mnmajor_desc(v_base, ks, kHalf), idesc_o,
-                    (j > 0 || ks > 0) ? 1u : 0u);
+                mma_ts(tmem + 256 + x * 128, tmem + x * 128 + ks * 8, mnmajor_desc(v_base, ks, kHalf),
+                       idesc_o, (j > 0 || ks > 0) ? 1u : 0u);
             }
-            commit(o_done);
-            commit(&v_empty[j & 1]);
+            if (j == n - 1)
+            {
+                commit(&o_done[x]);
+            }
         };
-        for (int j = 0; j < nk; ++j)
+        mbar_wait(q_full, 0, p.status, abort);
+        mbar_wait(&k_full[0], 0, p.status, abort);
+        fence_after();
+        issue_s(0, 0);
+        if (n_b > 0)
         {
-            const int st = j & 1;
-            mbar_wait(&k_full[st], (j >> 1) & 1, p.status, abort);
-            mbar_wait(&s_free[st], ((j >> 1) & 1) ^ 1, p.status, abort);
+            issue_s(1, 0);
+        }
+        commit(&k_empty[0]);
+        for (int j = 0; j < nmax; ++j)
+        {
+            const int st = j & 1, jn = j + 1;
+            mbar_wait(&v_full[st], (j >> 1) & 1, p.status, abort);
             fence_after();
-            const uint32_t k_base = smem_u32(sk + st * kTileBytes);
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks)
+            if (j < n_a)
             {
-                mma(tmem + st * 128, kmajor_desc(q_base, ks), kmajor_desc(k_base, ks), idesc_s,
-                    ks > 0 ? 1u : 0u);
+                issue_pv(0, j, n_a);
             }
-            commit(&s_full[st]);
-            commit(&k_empty[st]);
-            if (j > 0)
+            if (jn < nmax)
             {
-                issue_pv(j - 1);
+                mbar_wait(&k_full[jn & 1], (jn >> 1) & 1, p.status, abort);
+                fence_after();
+                if (jn < n_a)
+                {
+                    issue_s(0, jn);
+                }
+            }
+            if (j < n_b)
+            {
+                issue_pv(1, j, n_b);
+            }
+            commit(&v_empty[st]);
+            if (jn < nmax)
+            {
+                if (jn < n_b)
+                {
+                    issue_s(1, jn);
+                }
+                commit(&k_empty[jn & 1]);
             }
         }
-        issue_pv(nk - 1);
     }
     else if (warp >= 2)
     {
+        const int x = warp >= 6 ? 1 : 0;                  // query tile of this warpgroup
+        const int n = x ? n_b : n_a;
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;                // row within the tile (TMEM lane)
-        const int query = qt * kTq + r;
+        const int qtile = qt0 + x;
+        const int query = qtile * kTq + r;
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-        float m = -INFINITY, l = 0.0f;
-        for (int j = 0; j < nk; ++j)
+        const uint32_t s_addr = tmem + lane_base + x * 128;
+        const uint32_t o_addr = tmem + lane_base + 256 + x * 128;
+        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
+        float m = -INFINITY, l = 0.0f;   // running max (scaled, log2 units) and row sum
+        for (int j = 0; j < n; ++j)
         {
-            const int st = j & 1;
-            mbar_wait(&s_full[st], (j >> 1) & 1, p.status, abort);
+            mbar_wait(&s_full[x], j & 1, p.status, abort);
             fence_after();
-            float s[128];
+            uint32_t s[4][32];
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-            {
-                uint32_t raw[32];
-                tmem_ld32(tmem + lane_base + st * 128 + c * 32, raw);
+            for (int c = 0; c < 4; ++c) tmem_ld32_async(s_addr + c * 32, s[c]);
+            tmem_wait_ld();
 #pragma unroll
-                for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(raw[e]);
-            }
-            fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[st]);
-            const bool diag = p.causal && j == qt;
+            for (int c = 0; c < 4; ++c) reg_fence(s[c]);
             const int key0 = j * kTk;
-            const bool tail = key0 + kTk > p.T;
-            float mx = -INFINITY;
+            if ((p.causal && j == qtile) || key0 + kTk > p.T)
+            {
+                int limit = p.T - key0 - 1;               // last visible column of this row
+                if (p.causal && j == qtile && r < limit) limit = r;
 #pragma unroll
-            for (int e = 0; e < 128; ++e)
-            {
-                float x = s[e] * p.scale_log2;
-                if ((diag && key0 + e > query) || (tail && key0 + e >= p.T)) x = -INFINITY;
-                s[e] = x;
-                mx = fmaxf(mx, x);
+                for (int e = 0; e < 128; ++e)
+                {
+                    if (e > limit) s[e >> 5][e & 31] = 0xFF800000u;   // -inf
+                }
             }
-            // O and the P buffer are in use by the previous tile's P.V product until it is done
-            if (j > 0)
+            float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+#pragma unroll
+            for (int e = 0; e < 128; e += 8)
             {
-                mbar_wait(o_done, (j - 1) & 1, p.status, abort);
-                fence_after();
+                const uint32_t* v = &s[e >> 5][e & 31];
+                m0 = max3(m0, __uint_as_float(v[0]), __uint_as_float(v[1]));
+                m1 = max3(m1, __uint_as_float(v[2]), __uint_as_float(v[3]));
+                m2 = max3(m2, __uint_as_float(v[4]), __uint_as_float(v[5]));
+                m3 = max3(m3, __uint_as_float(v[6]), __uint_as_float(v[7]));
             }
+            const float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * p.scale_log2;
+            // O_x holds the products of tiles < j; they have completed (S_x(j) was issued after
+            // them and has completed), so O_x may be rescaled here.
             const bool first = m == -INFINITY;
             const bool grow = mx > m + kRescaleThreshold;
-            if (__any_sync(0xFFFFFFFFu, grow && !first) && j > 0)
+            if (__any_sync(0xFFFFFFFFu, grow && !first))
             {
-                const float corr = (grow && !first) ? exp2f(m - mx) : 1.0f;
+                const float corr = (grow && !first) ? ex2(m - mx) : 1.0f;
 #pragma unroll 1
                 for (int c = 0; c < 4; ++c)
                 {
                     uint32_t raw[32];
-                    tmem_ld32(tmem + lane_base + 256 + c * 32, raw);
+                    tmem_ld32(o_addr + c * 32, raw);
 #pragma unroll
                     for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * corr);
-                    tmem_st32(tmem + lane_base + 256 + c * 32, raw);
+                    tmem_st32(o_addr + c * 32, raw);
                 }
                 l *= corr;
             }
@@ -263,62 +346,65 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
             {
                 m = mx;
             }
-            float rs = 0.0f;
-            uint8_t* prow = sp;
+            const float mu = m == -INFINITY ? 0.0f : m;
+            const uint64_t neg = f2_pack(-mu, -mu);
+            uint64_t acc0 = 0, acc1 = 0;   // two packed partial sums (+0.0f pairs)
+            uint32_t pk[4][16];
 #pragma unroll
-            for (int c = 0; c < 16; ++c)
+            for (int c = 0; c < 64; ++c)
             {
-                float e8[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-                {
-                    const float x = s[c * 8 + e];
-                    e8[e] = m == -INFINITY ? 0.0f : exp2f(x - m);
-                    rs += e8[e];
-                }
-                uint4 packed;
-                const __nv_bfloat162 p0 = __floats2bfloat162_rn(e8[0], e8[1]);
-                const __nv_bfloat162 p1 = __floats2bfloat162_rn(e8[2], e8[3]);
-                const __nv_bfloat162 p2 = __floats2bfloat162_rn(e8[4], e8[5]);
-                const __nv_bfloat162 p3 = __floats2bfloat162_rn(e8[6], e8[7]);
-                packed.x = *reinterpret_cast<const uint32_t*>(&p0);
-                packed.y = *reinterpret_cast<const uint32_t*>(&p1);
-                packed.z = *reinterpret_cast<const uint32_t*>(&p2);
-                packed.w = *reinterpret_cast<const uint32_t*>(&p3);
-                *reinterpret_cast<uint4*>(prow + (c >> 3) * kHalf + sw128_offset(r, c & 7)) = packed;
+                const uint32_t* v = &s[c >> 4][(c & 15) * 2];
+                float a, bb;
+                f2_unpack(f2_fma(f2_pack(__uint_as_float(v[0]), __uint_as_float(v[1])), sc2, neg), a, bb);
+                a = ex2(a);
+                bb = ex2(bb);
+                if (c & 1)
+                    acc1 = f2_add(acc1, f2_pack(a, bb));
+                else
+                    acc0 = f2_add(acc0, f2_pack(a, bb));
+                const __nv_bfloat162 t = __floats2bfloat162_rn(a, bb);
+                pk[c >> 4][c & 15] = *reinterpret_cast<const uint32_t*>(&t);
             }
-            l += rs;
-            fence_proxy_async();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_st16_async(s_addr + c * 16, pk[c]);
+            float a0, a1, b0, b1;
+            f2_unpack(acc0, a0, a1);
+            f2_unpack(acc1, b0, b1);
+            l += (a0 + a1) + (b0 + b1);
+            tmem_wait_st();
             fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&p_full[x]);
         }
-        // epilogue: O / l and the log-sum-exp
-        mbar_wait(o_done, (nk - 1) & 1, p.status, abort);
-        fence_after();
-        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-        const bool valid = query < p.T;
-        bf16* orow = p.o + (static_cast<int64_t>(b) * p.T + query) * p.ldo + static_cast<int64_t>(h) * 128;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c)
+        if (n > 0)
         {
-            uint32_t raw[32];
-            tmem_ld32(tmem + lane_base + 256 + c * 32, raw);
-            if (valid)
+            // epilogue: O / l and the log-sum-exp
+            mbar_wait(&o_done[x], 0, p.status, abort);
+            fence_after();
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            const bool valid = query < p.T;
+            bf16* orow = p.o + (static_cast<int64_t>(b) * p.T + query) * p.ldo + static_cast<int64_t>(h) * 128;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c)
             {
-#pragma unroll
-                for (int e = 0; e < 32; e += 8)
+                uint32_t raw[32];
+                tmem_ld32(o_addr + c * 32, raw);
+                if (valid)
                 {
-                    float v8[8];
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) v8[q] = __uint_as_float(raw[e + q]) * inv;
-                    store16(orow + c * 32 + e, v8);
+                    for (int e = 0; e < 32; e += 8)
+                    {
+                        float v8[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) v8[q] = __uint_as_float(raw[e + q]) * inv;
+                        store16(orow + c * 32 + e, v8);
+                    }
                 }
             }
-        }
-        if (valid)
-        {
-            p.lse[(static_cast<int64_t>(b) * p.H + h) * p.T + query] = (m + log2f(l)) * kLn2;
+            if (valid)
+            {
+                p.lse[(static_cast<int64_t>(b) * p.H + h) * p.T + query] = (m + log2f(l)) * kLn2;
+            }
         }
     }
     fence_before();
@@ -876,8 +962,9 @@ int attn_tc_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     }
     FwdParams p{static_cast<bf16*>(o), lse, ldo, static_cast<int>(T), static_cast<int>(H),
                 static_cast<int>(Hkv), scale * kLog2e, causal, device_status_ptr()};
-    const dim3 grid(static_cast<unsigned>((T + kTq - 1) / kTq), static_cast<unsigned>(B * H));
-    attn_fwd_tc_kernel<<<grid, 192, kFwdSmem, s>>>(mq, mk, mv, p);
+    const int64_t pairs = ((T + kTq - 1) / kTq + 1) / 2;
+    const dim3 grid(static_cast<unsigned>(pairs), static_cast<unsigned>(B * H));
+    attn_fwd_tc_kernel<<<grid, kFwdThreads, kFwdSmem, s>>>(mq, mk, mv, p);
     count_launch();
     return check_launch("veda_attention_fwd (tcgen05)");
 }
