@@ -417,15 +417,19 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
 }
 
 // ---------------------------------------------------------------------------------------------
-// Backward, in two kernels.
+// Backward, in three launches.
+// (0) attn_rowdot_kernel — D = rowsum(dO * O) and -LSE log2(e) per (batch, head, query).
 // (1) attn_bwd_tc_kernel — one CTA per (batch, KV head, 128-key tile); 10 warps. For every query
 //     head of the GQA group and every 64-query tile at or after the diagonal:
-//       MMA    S^T = K Q^T and dP^T = V dO^T    (M128 keys, N64 queries, K128 dims) into one of
-//              two TMEM buffers, so the products of tile i+1 run while tile i is elementwise;
+//       TMA    Q, dO (64 x 128 each) and that tile's -LSE log2(e) and D into a 4-stage ring;
+//       MMA    S^T = K Q^T and dP^T = V dO^T (M128 keys, N64 queries, K128 dims) into one of two
+//              TMEM buffer pairs, so the products of tile i+1 run while tile i is elementwise;
 //       warps  (8, two per TMEM lane quarter, 32 query columns each)
-//              P^T = exp2(S^T scale log2e - LSE log2e), causal mask, dS^T = P^T (dP^T - D),
-//              bf16 into double-buffered swizzled shared tiles; dS^T also goes to HBM by TMA;
-//       MMA    dV += P^T dO, dK += dS^T Q        (M128 keys, N128 dims, K64 queries; TMEM).
+//              P^T = exp2(S^T scale log2e - LSE log2e), causal mask, dS^T = P^T (dP^T - D);
+//              P^T and dS^T (bf16 pairs) overwrite their S^T and dP^T columns in TMEM, and dS^T
+//              also goes straight to HBM for the dQ kernel;
+//       MMA    dV += P^T dO, dK += dS^T Q (M128 keys, N128 dims, K64 queries; P^T and dS^T read
+//              by the MMA from tensor memory, accumulators in TMEM).
 //     dK and dV are summed over the group's heads in TMEM: written once, deterministically.
 // (2) attn_dq_tc_kernel — one CTA per (batch, head, 128-query tile): dQ = sum over key tiles of
 //     dS K (M128 queries, N128 dims, K128 keys) from the stored dS^T, accumulated in TMEM — no
@@ -436,27 +440,22 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
 constexpr int kBq = 64;                      // queries per backward iteration
 constexpr int kQTileBytes = kBq * 128 * 2;   // [64 rows x 128 dims] = two 8 KB halves
 constexpr int kQHalf = kQTileBytes / 2;
-constexpr int kPTileBytes = 128 * kBq * 2;   // [128 keys x 64 queries]
-constexpr int kComputeThreads = 256;
-// alignment slack | K, V | Q[2], dO[2] | P^T[2], dS^T[2] | LSE/D staging (1 KB) + barriers
-constexpr int kBwdSmem = 1024 + 2 * kTileBytes + 4 * kQTileBytes + 4 * kPTileBytes + 2048;
+constexpr int kQStages = 4;
+constexpr int kBwdThreads = 320;
+// alignment slack | K, V | (Q, dO)[4] | (-LSE log2e, D)[4] | barriers
+constexpr int kBwdSmem = 1024 + 2 * kTileBytes + 2 * kQStages * kQTileBytes + kQStages * 2 * kBq * 4 + 256;
 
 struct BwdParams
 {
-    const float* lse;
-    const float* dvec;
-    bf16 *dk, *dv;
+    const float* nlse2;   // -LSE log2(e) [B, H, T]
+    const float* dvec;    // D [B, H, T]
+    bf16 *dk, *dv, *ds;   // ds: dS^T [B*H][T keys][T queries]
     int64_t lddk, lddv;
     int T, H, Hkv;
     float scale, scale_log2;
     int causal;
     int* status;
 };
-
-__device__ __forceinline__ void named_sync(int id, int count)
-{
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
 
 __device__ __forceinline__ void load_qtile_3d(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
                                               int col, int row, int batch)
@@ -471,31 +470,34 @@ __device__ __forceinline__ uint32_t pack2(float a, float b)
     return *reinterpret_cast<const uint32_t*>(&t);
 }
 
-__global__ void __launch_bounds__(320, 1)
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
 attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                   const __grid_constant__ CUtensorMap tds, const BwdParams p)
+                   const BwdParams p)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* sk = smem;
     uint8_t* sv = sk + kTileBytes;
-    uint8_t* sq = sv + kTileBytes;             // [2]
-    uint8_t* sdo = sq + 2 * kQTileBytes;       // [2]
-    uint8_t* sp = sdo + 2 * kQTileBytes;       // [2]
-    uint8_t* sds = sp + 2 * kPTileBytes;       // [2]
-    float* sld = reinterpret_cast<float*>(sds + 2 * kPTileBytes);   // [2][2][64]: LSE*log2e, D
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sld + 4 * kBq);
+    uint8_t* sq = sv + kTileBytes;                          // [stages]
+    uint8_t* sdo = sq + kQStages * kQTileBytes;             // [stages]
+    float* srow = reinterpret_cast<float*>(sdo + kQStages * kQTileBytes);   // [stages][2][64]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(srow + kQStages * 2 * kBq);
     uint64_t* kv_full = bars + 0;
-    uint64_t* qd_full = bars + 1;    // [2]
-    uint64_t* qd_empty = bars + 3;   // [2]
-    uint64_t* sp_full = bars + 5;    // [2]
-    uint64_t* st_free = bars + 7;    // [2]
-    uint64_t* ds_full = bars + 9;    // [2]
-    uint64_t* pds_free = bars + 11;  // [2]
-    uint64_t* done = bars + 13;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+    uint64_t* qd_full = bars + 1;                  // [stages]
+    uint64_t* qd_empty = bars + 1 + kQStages;      // [stages]
+    uint64_t* sp_full = bars + 1 + 2 * kQStages;   // [2]
+    uint64_t* ds_full = bars + 3 + 2 * kQStages;   // [2]
+    uint64_t* done = bars + 5 + 2 * kQStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6 + 2 * kQStages);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -512,14 +514,15 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     {
         *abort = 0;
         mbar_init(kv_full, 1);
-        for (int i = 0; i < 2; ++i)
+        for (int i = 0; i < kQStages; ++i)
         {
             mbar_init(&qd_full[i], 1);
             mbar_init(&qd_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i)
+        {
             mbar_init(&sp_full[i], 1);
-            mbar_init(&st_free[i], 8);
             mbar_init(&ds_full[i], 8);
-            mbar_init(&pds_free[i], 1);
         }
         mbar_init(done, 1);
         mbar_fence_init();
@@ -532,7 +535,9 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
-    constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 384;   // S^T, dP^T: 2 x 64 each
+    // TMEM columns: S^T[2] (64 each) | dP^T[2] (64 each) | dV (128) | dK (128). P^T and dS^T
+    // (bf16 pairs) overwrite columns [32 g, 32 g + 16) of their buffer, g = the query half.
+    constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 384;
 
     if (warp == 0 && lane == 0)
     {
@@ -545,13 +550,18 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
         load_tile_3d(sv, &tv, kv_full, kvh * 128, kt * 128, b);
         for (int it = 0; it < iters; ++it)
         {
-            const int st = it & 1;
+            const int sq_i = it % kQStages;
             const int h = kvh * rep + it / per_head;
             const int q0 = (qi0 + it % per_head) * kBq;
-            mbar_wait(&qd_empty[st], ((it >> 1) & 1) ^ 1, p.status, abort);
-            mbar_expect_tx(&qd_full[st], 2 * kQTileBytes);
-            load_qtile_3d(sq + st * kQTileBytes, &tq, &qd_full[st], h * 128, q0, b);
-            load_qtile_3d(sdo + st * kQTileBytes, &tdo, &qd_full[st], h * 128, q0, b);
+            const int nrow = p.T - q0 < kBq ? p.T - q0 : kBq;   // a multiple of 8 (T % 8 == 0)
+            const uint32_t rbytes = static_cast<uint32_t>(nrow) * 4;
+            const int64_t at = (static_cast<int64_t>(b) * p.H + h) * p.T + q0;
+            mbar_wait(&qd_empty[sq_i], ((it / kQStages) & 1) ^ 1, p.status, abort);
+            mbar_expect_tx(&qd_full[sq_i], 2 * kQTileBytes + 2 * rbytes);
+            load_qtile_3d(sq + sq_i * kQTileBytes, &tq, &qd_full[sq_i], h * 128, q0, b);
+            load_qtile_3d(sdo + sq_i * kQTileBytes, &tdo, &qd_full[sq_i], h * 128, q0, b);
+            bulk_load(srow + sq_i * 2 * kBq, p.nlse2 + at, rbytes, &qd_full[sq_i]);
+            bulk_load(srow + sq_i * 2 * kBq + kBq, p.dvec + at, rbytes, &qd_full[sq_i]);
         }
     }
     else if (warp == 1 && lane == 0)
@@ -561,40 +571,37 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
         const uint32_t k_base = smem_u32(sk), v_base = smem_u32(sv);
         mbar_wait(kv_full, 0, p.status, abort);
         auto issue_dvdk = [&](int i) {
-            const int s = i & 1;
+            const int s = i & 1, sq_i = i % kQStages;
             mbar_wait(&ds_full[s], (i >> 1) & 1, p.status, abort);
             fence_after();
-            const uint32_t q_base = smem_u32(sq + s * kQTileBytes);
-            const uint32_t do_base = smem_u32(sdo + s * kQTileBytes);
-            const uint32_t p_base = smem_u32(sp + s * kPTileBytes);
-            const uint32_t ds_base = smem_u32(sds + s * kPTileBytes);
+            const uint32_t q_base = smem_u32(sq + sq_i * kQTileBytes);
+            const uint32_t do_base = smem_u32(sdo + sq_i * kQTileBytes);
 #pragma unroll
             for (int ks = 0; ks < kBq / 16; ++ks)
             {
                 const uint32_t acc = (i > 0 || ks > 0) ? 1u : 0u;
-                mma(tmem + kDV, smem_desc(p_base + ks * 32, 16, 1024),
-                    mnmajor_desc(do_base, ks, kQHalf), idesc_kv, acc);
-                mma(tmem + kDK, smem_desc(ds_base + ks * 32, 16, 1024),
-                    mnmajor_desc(q_base, ks, kQHalf), idesc_kv, acc);
+                const uint32_t col = s * 64 + (ks >> 1) * 32 + (ks & 1) * 8;
+                mma_ts(tmem + kDV, tmem + kST + col, mnmajor_desc(do_base, ks, kQHalf), idesc_kv, acc);
+                mma_ts(tmem + kDK, tmem + kDPT + col, mnmajor_desc(q_base, ks, kQHalf), idesc_kv, acc);
             }
-            commit(&pds_free[s]);
-            commit(&qd_empty[s]);
+            commit(&qd_empty[sq_i]);
         };
         for (int it = 0; it < iters; ++it)
         {
-            const int st = it & 1;
-            const uint32_t q_base = smem_u32(sq + st * kQTileBytes);
-            const uint32_t do_base = smem_u32(sdo + st * kQTileBytes);
-            mbar_wait(&qd_full[st], (it >> 1) & 1, p.status, abort);
-            mbar_wait(&st_free[st], ((it >> 1) & 1) ^ 1, p.status, abort);
+            const int st = it & 1, sq_i = it % kQStages;
+            const uint32_t q_base = smem_u32(sq + sq_i * kQTileBytes);
+            const uint32_t do_base = smem_u32(sdo + sq_i * kQTileBytes);
+            mbar_wait(&qd_full[sq_i], (it / kQStages) & 1, p.status, abort);
             fence_after();
+            // S^T / dP^T of buffer st were last read (as P^T / dS^T) by the dV/dK products of
+            // tile it-2, issued before these: the MMAs of one thread execute in issue order.
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks)
             {
                 const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;
-                mma(tmem + kST + st * kBq, kmajor_desc(k_base, ks), smem_desc(q_base + off, 16, 1024),
+                mma(tmem + kST + st * 64, kmajor_desc(k_base, ks), smem_desc(q_base + off, 16, 1024),
                     idesc_s, ks > 0 ? 1u : 0u);
-                mma(tmem + kDPT + st * kBq, kmajor_desc(v_base, ks),
+                mma(tmem + kDPT + st * 64, kmajor_desc(v_base, ks),
                     smem_desc(do_base + off, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
             }
             commit(&sp_full[st]);
@@ -611,92 +618,78 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     }
     else if (warp >= 2)
     {
-        const int cw = warp - 2;                // 0..7
         const int quarter = warp & 3;
-        const int half = cw >> 2;               // query columns [32 half, 32 half + 32)
+        const int half = (warp - 2) >> 2;       // query columns [32 half, 32 half + 32)
         const int r = quarter * 32 + lane;      // key row
         const int key = kt * 128 + r;
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-        const int tid = threadIdx.x - 64;       // 0..255
-        const bool issuer = tid == 0;           // issues the dS^T stores
+        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
+        const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
         for (int it = 0; it < iters; ++it)
         {
-            const int st = it & 1;
+            const int st = it & 1, sq_i = it % kQStages;
             const int h = kvh * rep + it / per_head;
             const int q0 = (qi0 + it % per_head) * kBq;
-            if (issuer && it >= 2)
-            {
-                bulk_wait_group_read<1>();      // the store of tile it-2 has read its dS^T buffer
-            }
-            float* lse2 = sld + st * 2 * kBq;
-            float* dd = lse2 + kBq;
-            if (tid < 2 * kBq)
-            {
-                const int c = tid & (kBq - 1);
-                const int q = q0 + c;
-                const int64_t at = (static_cast<int64_t>(b) * p.H + h) * p.T + q;
-                if (tid < kBq)
-                {
-                    lse2[c] = q < p.T ? p.lse[at] * kLog2e : INFINITY;
-                }
-                else
-                {
-                    dd[c] = q < p.T ? p.dvec[at] : 0.0f;
-                }
-            }
-            named_sync(1, kComputeThreads);
+            const int qc = q0 + half * 32;      // first query of this thread's columns
             mbar_wait(&sp_full[st], (it >> 1) & 1, p.status, abort);
+            // the stage's -LSE log2e / D rows arrived with its Q / dO (phase already complete)
+            mbar_wait(&qd_full[sq_i], (it / kQStages) & 1, p.status, abort);
             fence_after();
             uint32_t sraw[32], draw[32];
-            tmem_ld32(tmem + lane_base + kST + st * kBq + half * 32, sraw);
-            tmem_ld32(tmem + lane_base + kDPT + st * kBq + half * 32, draw);
-            fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&st_free[st]);
-            const bool maybe_masked = p.causal && q0 < kt * 128 + 128;
-            float pv[32], dsv[32];
+            const uint32_t col = st * 64 + half * 32;
+            tmem_ld32_async(tmem + lane_base + kST + col, sraw);
+            tmem_ld32_async(tmem + lane_base + kDPT + col, draw);
+            tmem_wait_ld();
+            reg_fence(sraw);
+            reg_fence(draw);
+            const float* nl = srow + sq_i * 2 * kBq + half * 32;
+            const float* dd = nl + kBq;
+            // masked columns: queries at or past T, and (causal) queries before this key
+            int first_masked = 32;
+            if (qc + 32 > p.T) first_masked = p.T - qc > 0 ? p.T - qc : 0;
+            const bool causal_tile = p.causal && qc < kt * 128 + 128;   // some key > query
+            uint32_t pk[16], dk[16];
 #pragma unroll
-            for (int c = 0; c < 32; ++c)
+            for (int c = 0; c < 32; c += 2)
             {
-                const int col = half * 32 + c;
-                float pr = exp2f(__uint_as_float(sraw[c]) * p.scale_log2 - lse2[col]);
-                if (maybe_masked && key > q0 + col) pr = 0.0f;
-                pv[c] = pr;
-                dsv[c] = pr * (__uint_as_float(draw[c]) - dd[col]);
+                const float2 nl2 = *reinterpret_cast<const float2*>(nl + c);
+                const float2 d2 = *reinterpret_cast<const float2*>(dd + c);
+                float p0, p1;
+                f2_unpack(f2_fma(f2_pack(__uint_as_float(sraw[c]), __uint_as_float(sraw[c + 1])), sc2,
+                                 f2_pack(nl2.x, nl2.y)),
+                          p0, p1);
+                const bool v0 = c < first_masked && !(causal_tile && key > qc + c);
+                const bool v1 = c + 1 < first_masked && !(causal_tile && key > qc + c + 1);
+                p0 = v0 ? ex2(p0) : 0.0f;
+                p1 = v1 ? ex2(p1) : 0.0f;
+                const uint64_t t = f2_fma(f2_pack(d2.x, d2.y), neg1,
+                                          f2_pack(__uint_as_float(draw[c]), __uint_as_float(draw[c + 1])));
+                float d0, d1;
+                f2_unpack(f2_mul(f2_pack(p0, p1), t), d0, d1);
+                d0 = v0 ? d0 : 0.0f;   // masked columns may hold stale -LSE / D values
+                d1 = v1 ? d1 : 0.0f;
+                pk[c >> 1] = pack2(p0, p1);
+                dk[c >> 1] = pack2(d0, d1);
             }
-            mbar_wait(&pds_free[st], ((it >> 1) & 1) ^ 1, p.status, abort);
-            uint8_t* pt = sp + st * kPTileBytes;
-            uint8_t* dt = sds + st * kPTileBytes;
+            tmem_st16_async(tmem + lane_base + kST + col, pk);
+            tmem_st16_async(tmem + lane_base + kDPT + col, dk);
+            if (key < p.T)
+            {
+                bf16* drow = p.ds + ((static_cast<int64_t>(b) * p.H + h) * p.T + key) * p.T + qc;
 #pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8)
-            {
-                const int chunk = half * 4 + c8;
-                uint4 a, d;
-                a.x = pack2(pv[c8 * 8 + 0], pv[c8 * 8 + 1]);
-                a.y = pack2(pv[c8 * 8 + 2], pv[c8 * 8 + 3]);
-                a.z = pack2(pv[c8 * 8 + 4], pv[c8 * 8 + 5]);
-                a.w = pack2(pv[c8 * 8 + 6], pv[c8 * 8 + 7]);
-                d.x = pack2(dsv[c8 * 8 + 0], dsv[c8 * 8 + 1]);
-                d.y = pack2(dsv[c8 * 8 + 2], dsv[c8 * 8 + 3]);
-                d.z = pack2(dsv[c8 * 8 + 4], dsv[c8 * 8 + 5]);
-                d.w = pack2(dsv[c8 * 8 + 6], dsv[c8 * 8 + 7]);
-                *reinterpret_cast<uint4*>(pt + sw128_offset(r, chunk)) = a;
-                *reinterpret_cast<uint4*>(dt + sw128_offset(r, chunk)) = d;
+                for (int c8 = 0; c8 < 4; ++c8)
+                {
+                    if (qc + c8 * 8 < p.T)   // T % 8 == 0: whole 8-query chunks
+                    {
+                        *reinterpret_cast<uint4*>(drow + c8 * 8) =
+                            make_uint4(dk[c8 * 4], dk[c8 * 4 + 1], dk[c8 * 4 + 2], dk[c8 * 4 + 3]);
+                    }
+                }
             }
-            fence_proxy_async();
+            tmem_wait_st();
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&ds_full[st]);
-            named_sync(2, kComputeThreads);     // every row of dS^T is in shared memory
-            if (issuer)
-            {
-                tma_store_3d(&tds, dt, q0, kt * 128, b * p.H + h);
-                bulk_commit_group();
-            }
-        }
-        if (issuer)
-        {
-            bulk_wait_group<0>();
         }
         // dV and dK rows of this key (summed over the group's heads in TMEM): 64 dims per warp
         mbar_wait(done, 0, p.status, abort);
@@ -719,8 +712,8 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
 #pragma unroll
                     for (int q = 0; q < 8; ++q)
                     {
-                        a8[q] = iters > 0 ? __uint_as_float(rv[e + q]) : 0.0f;
-                        k8[q] = iters > 0 ? __uint_as_float(rk[e + q]) * p.scale : 0.0f;
+                        a8[q] = __uint_as_float(rv[e + q]);
+                        k8[q] = __uint_as_float(rk[e + q]) * p.scale;
                     }
                     store16(vrow + c * 32 + e, a8);
                     store16(krow + c * 32 + e, k8);
@@ -736,6 +729,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
         tmem_dealloc(tmem, 512);
     }
 }
+
 
 // dQ[q-tile] = sum over key tiles of dS K, from dS^T stored as [B*H][keys][queries].
 // One CTA per (batch, head, 128-query tile); warp 0 TMA (3-stage ring of a dS^T tile and a K tile),
@@ -867,28 +861,34 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tds, const __grid_constant
     }
 }
 
-// D[b,h,t] = sum_d dO * O over the head's 128 dims; one warp per row.
+// D = rowsum(dO * O) and -LSE log2(e) for every (batch, head, query); 16 threads per (token, head)
+// row, rows in token-major order so a warp reads two contiguous 256-byte rows of O and dO.
 __global__ void attn_rowdot_kernel(const bf16* __restrict__ o, int64_t ldo,
                                    const bf16* __restrict__ dout, int64_t lddo,
-                                   float* __restrict__ dvec, int64_t B, int64_t T, int64_t H)
+                                   const float* __restrict__ lse, float* __restrict__ dvec,
+                                   float* __restrict__ nlse2, int64_t B, int64_t T, int64_t H)
 {
-    const int lane = threadIdx.x & 31;
-    const int64_t rows = B * H * T;
-    for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows;
-         r += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5)
+    const int sub = threadIdx.x & 15;
+    const int64_t rows = B * T * H;
+    const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 4;
+    for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4; r < rows; r += stride)
     {
-        const int64_t i = r % T, h = (r / T) % H, b = r / (T * H);
+        const int64_t h = r % H, bt = r / H;
+        float x[8], y[8];
+        load16(o + bt * ldo + h * 128 + sub * 8, x);
+        load16(dout + bt * lddo + h * 128 + sub * 8, y);
         float s = 0.0f;
-        if (lane < 16)
-        {
-            float x[8], y[8];
-            load16(o + (b * T + i) * ldo + h * 128 + lane * 8, x);
-            load16(dout + (b * T + i) * lddo + h * 128 + lane * 8, y);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) s += x[e] * y[e];
+        for (int e = 0; e < 8; ++e) s += x[e] * y[e];
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, off);
+        if (sub == 0)
+        {
+            const int64_t b = bt / T, t = bt % T;
+            const int64_t at = (b * H + h) * T + t;
+            dvec[at] = s;
+            nlse2[at] = -lse[at] * kLog2e;
         }
-        s = warp_sum(s);
-        if (lane == 0) dvec[(b * H + h) * T + i] = s;
     }
 }
 
@@ -969,9 +969,16 @@ int attn_tc_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     return check_launch("veda_attention_fwd (tcgen05)");
 }
 
+// Workspace of the tcgen05 backward: dS^T [B*H][T][T] bf16, then -LSE log2(e) [B, H, T] fp32.
+size_t tc_bwd_ds_bytes(int64_t B, int64_t T, int64_t H)
+{
+    const size_t bytes = static_cast<size_t>(B * H) * static_cast<size_t>(T) * static_cast<size_t>(T) * sizeof(bf16);
+    return (bytes + 255) & ~static_cast<size_t>(255);
+}
+
 size_t tc_bwd_extra_workspace(int64_t B, int64_t T, int64_t H)
 {
-    return static_cast<size_t>(B * H) * static_cast<size_t>(T) * static_cast<size_t>(T) * sizeof(bf16);
+    return tc_bwd_ds_bytes(B, T, H) + static_cast<size_t>(B * H * T) * sizeof(float);
 }
 
 int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
@@ -980,7 +987,8 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
                 void* extra, int64_t B, int64_t T, int64_t H, int64_t Hkv, float scale, int causal,
                 cudaStream_t s)
 {
-    // dS^T rows are T bf16 wide: the tensor map needs their byte stride to be a multiple of 16.
+    // dS^T rows are T bf16 wide: the tensor map needs their byte stride to be a multiple of 16,
+    // and the per-tile -LSE / D bulk copies whole 32-byte pieces.
     if (T % 8 != 0 || B * H > 65535)
     {
         return -1;
@@ -989,7 +997,7 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     if (!make_map3(&mq, q, H * 128, T, B, ldq, kBq) || !make_map3(&mk, k, Hkv * 128, T, B, ldk, 128) ||
         !make_map3(&mv, v, Hkv * 128, T, B, ldv, 128) ||
         !make_map3(&mdo, dout, H * 128, T, B, lddo, kBq) ||
-        !make_map3(&mds, extra, T, T, B * H, T, 128))
+        !make_map3(&mds, extra, T, T, B * H, T, 128) || !aligned16(dvec))
     {
         return -1;   // caller falls back
     }
@@ -1002,13 +1010,15 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
         cudaFuncSetAttribute(attn_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDqSmem);
         configured = device;
     }
-    attn_rowdot_kernel<<<grid_for(B * H * T * 32, 256), 256, 0, s>>>(
-        static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, dvec, B, T, H);
-    BwdParams p{lse, dvec, static_cast<bf16*>(dk), static_cast<bf16*>(dv), lddk, lddv,
+    bf16* ds = static_cast<bf16*>(extra);
+    float* nlse2 = reinterpret_cast<float*>(static_cast<char*>(extra) + tc_bwd_ds_bytes(B, T, H));
+    attn_rowdot_kernel<<<grid_for(B * H * T * 16, 256), 256, 0, s>>>(
+        static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, lse, dvec, nlse2, B, T, H);
+    BwdParams p{nlse2, dvec, static_cast<bf16*>(dk), static_cast<bf16*>(dv), ds, lddk, lddv,
                 static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
                 scale * kLog2e, causal, device_status_ptr()};
     const dim3 grid(static_cast<unsigned>((T + 127) / 128), static_cast<unsigned>(B * Hkv));
-    attn_bwd_tc_kernel<<<grid, 64 + kComputeThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, mds, p);
+    attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, p);
     DqParams pq{static_cast<bf16*>(dq), lddq, static_cast<int>(T), static_cast<int>(H),
                 static_cast<int>(Hkv), scale, causal, device_status_ptr()};
     const dim3 gq(static_cast<unsigned>((T + 127) / 128), static_cast<unsigned>(B * H));
