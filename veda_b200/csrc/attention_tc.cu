@@ -324,13 +324,47 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
                 m3 = max3(m3, __uint_as_float(v[6]), __uint_as_float(v[7]));
             }
             const float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * p.scale_log2;
-            // O_x holds the products of tiles < j; they have completed (S_x(j) was issued after
-            // them and has completed), so O_x may be rescaled here.
             const bool first = m == -INFINITY;
             const bool grow = mx > m + kRescaleThreshold;
-            if (__any_sync(0xFFFFFFFFu, grow && !first))
+            // O_x is rescaled after P is written (fewer live registers); corr = 1 for rows whose
+            // max is kept
+            const bool rescale = __any_sync(0xFFFFFFFFu, grow && !first);
+            const float corr = (grow && !first) ? ex2(m - mx) : 1.0f;
+            if (grow || first)
             {
-                const float corr = (grow && !first) ? ex2(m - mx) : 1.0f;
+                m = mx;
+            }
+            const float mu = m == -INFINITY ? 0.0f : m;
+            const uint64_t neg = f2_pack(-mu, -mu);
+            uint64_t acc0 = 0, acc1 = 0;   // two packed partial sums (+0.0f pairs)
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+            {
+                uint32_t pk[16];   // 32 probabilities as bf16 pairs, stored as soon as computed
+#pragma unroll
+                for (int c = 0; c < 16; ++c)
+                {
+                    const uint32_t* v = &s[g][c * 2];
+                    float a, bb;
+                    f2_unpack(f2_fma(f2_pack(__uint_as_float(v[0]), __uint_as_float(v[1])), sc2, neg), a, bb);
+                    a = ex2(a);
+                    bb = ex2(bb);
+                    if (c & 1)
+                        acc1 = f2_add(acc1, f2_pack(a, bb));
+                    else
+                        acc0 = f2_add(acc0, f2_pack(a, bb));
+                    const __nv_bfloat162 t = __floats2bfloat162_rn(a, bb);
+                    pk[c] = *reinterpret_cast<const uint32_t*>(&t);
+                }
+                tmem_st16_async(s_addr + g * 16, pk);
+            }
+            float a0, a1, b0, b1;
+            f2_unpack(acc0, a0, a1);
+            f2_unpack(acc1, b0, b1);
+            if (rescale)
+            {
+                // the products of tiles < j have completed (S_x(j), issued after them, has), and
+                // P_x V_j is not issued before this warp arrives on p_full
 #pragma unroll 1
                 for (int c = 0; c < 4; ++c)
                 {
@@ -340,37 +374,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
                     for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * corr);
                     tmem_st32(o_addr + c * 32, raw);
                 }
-                l *= corr;
             }
-            if (grow || first)
-            {
-                m = mx;
-            }
-            const float mu = m == -INFINITY ? 0.0f : m;
-            const uint64_t neg = f2_pack(-mu, -mu);
-            uint64_t acc0 = 0, acc1 = 0;   // two packed partial sums (+0.0f pairs)
-            uint32_t pk[4][16];
-#pragma unroll
-            for (int c = 0; c < 64; ++c)
-            {
-                const uint32_t* v = &s[c >> 4][(c & 15) * 2];
-                float a, bb;
-                f2_unpack(f2_fma(f2_pack(__uint_as_float(v[0]), __uint_as_float(v[1])), sc2, neg), a, bb);
-                a = ex2(a);
-                bb = ex2(bb);
-                if (c & 1)
-                    acc1 = f2_add(acc1, f2_pack(a, bb));
-                else
-                    acc0 = f2_add(acc0, f2_pack(a, bb));
-                const __nv_bfloat162 t = __floats2bfloat162_rn(a, bb);
-                pk[c >> 4][c & 15] = *reinterpret_cast<const uint32_t*>(&t);
-            }
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_st16_async(s_addr + c * 16, pk[c]);
-            float a0, a1, b0, b1;
-            f2_unpack(acc0, a0, a1);
-            f2_unpack(acc1, b0, b1);
-            l += (a0 + a1) + (b0 + b1);
+            l = l * corr + ((a0 + a1) + (b0 + b1));
             tmem_wait_st();
             fence_before();
             __syncwarp();
@@ -644,32 +649,61 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
             reg_fence(draw);
             const float* nl = srow + sq_i * 2 * kBq + half * 32;
             const float* dd = nl + kBq;
-            // masked columns: queries at or past T, and (causal) queries before this key
-            int first_masked = 32;
-            if (qc + 32 > p.T) first_masked = p.T - qc > 0 ? p.T - qc : 0;
-            const bool causal_tile = p.causal && qc < kt * 128 + 128;   // some key > query
+            // visible columns c: lo <= c < hi (queries before T and, causal, not before this key)
+            const int hi = qc + 32 > p.T ? (p.T - qc > 0 ? p.T - qc : 0) : 32;
+            const bool causal_tile = p.causal && qc < kt * 128 + 127;   // some key > query here
+            const int lo = causal_tile ? (key - qc > 0 ? key - qc : 0) : 0;
             uint32_t pk[16], dk[16];
-#pragma unroll
-            for (int c = 0; c < 32; c += 2)
+            if (!causal_tile && hi == 32)
             {
-                const float2 nl2 = *reinterpret_cast<const float2*>(nl + c);
-                const float2 d2 = *reinterpret_cast<const float2*>(dd + c);
-                float p0, p1;
-                f2_unpack(f2_fma(f2_pack(__uint_as_float(sraw[c]), __uint_as_float(sraw[c + 1])), sc2,
-                                 f2_pack(nl2.x, nl2.y)),
-                          p0, p1);
-                const bool v0 = c < first_masked && !(causal_tile && key > qc + c);
-                const bool v1 = c + 1 < first_masked && !(causal_tile && key > qc + c + 1);
-                p0 = v0 ? ex2(p0) : 0.0f;
-                p1 = v1 ? ex2(p1) : 0.0f;
-                const uint64_t t = f2_fma(f2_pack(d2.x, d2.y), neg1,
-                                          f2_pack(__uint_as_float(draw[c]), __uint_as_float(draw[c + 1])));
-                float d0, d1;
-                f2_unpack(f2_mul(f2_pack(p0, p1), t), d0, d1);
-                d0 = v0 ? d0 : 0.0f;   // masked columns may hold stale -LSE / D values
-                d1 = v1 ? d1 : 0.0f;
-                pk[c >> 1] = pack2(p0, p1);
-                dk[c >> 1] = pack2(d0, d1);
+#pragma unroll
+                for (int c = 0; c < 32; c += 4)
+                {
+                    const float4 nl4 = *reinterpret_cast<const float4*>(nl + c);
+                    const float4 d4 = *reinterpret_cast<const float4*>(dd + c);
+#pragma unroll
+                    for (int u = 0; u < 4; u += 2)
+                    {
+                        const int e = c + u;
+                        float p0, p1;
+                        f2_unpack(f2_fma(f2_pack(__uint_as_float(sraw[e]), __uint_as_float(sraw[e + 1])), sc2,
+                                         u == 0 ? f2_pack(nl4.x, nl4.y) : f2_pack(nl4.z, nl4.w)),
+                                  p0, p1);
+                        p0 = ex2(p0);
+                        p1 = ex2(p1);
+                        const uint64_t t = f2_fma(u == 0 ? f2_pack(d4.x, d4.y) : f2_pack(d4.z, d4.w), neg1,
+                                                  f2_pack(__uint_as_float(draw[e]), __uint_as_float(draw[e + 1])));
+                        float d0, d1;
+                        f2_unpack(f2_mul(f2_pack(p0, p1), t), d0, d1);
+                        pk[e >> 1] = pack2(p0, p1);
+                        dk[e >> 1] = pack2(d0, d1);
+                    }
+                }
+            }
+            else
+            {
+#pragma unroll
+                for (int c = 0; c < 32; c += 2)
+                {
+                    const float2 nl2 = *reinterpret_cast<const float2*>(nl + c);
+                    const float2 d2 = *reinterpret_cast<const float2*>(dd + c);
+                    float p0, p1;
+                    f2_unpack(f2_fma(f2_pack(__uint_as_float(sraw[c]), __uint_as_float(sraw[c + 1])), sc2,
+                                     f2_pack(nl2.x, nl2.y)),
+                              p0, p1);
+                    const bool v0 = c >= lo && c < hi;
+                    const bool v1 = c + 1 >= lo && c + 1 < hi;
+                    p0 = v0 ? ex2(p0) : 0.0f;
+                    p1 = v1 ? ex2(p1) : 0.0f;
+                    const uint64_t t = f2_fma(f2_pack(d2.x, d2.y), neg1,
+                                              f2_pack(__uint_as_float(draw[c]), __uint_as_float(draw[c + 1])));
+                    float d0, d1;
+                    f2_unpack(f2_mul(f2_pack(p0, p1), t), d0, d1);
+                    d0 = v0 ? d0 : 0.0f;   // masked columns may hold stale -LSE / D values
+                    d1 = v1 ? d1 : 0.0f;
+                    pk[c >> 1] = pack2(p0, p1);
+                    dk[c >> 1] = pack2(d0, d1);
+                }
             }
             tmem_st16_async(tmem + lane_base + kST + col, pk);
             tmem_st16_async(tmem + lane_base + kDPT + col, dk);
