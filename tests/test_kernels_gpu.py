@@ -342,6 +342,18 @@ def test_gemm_bf16_fp32_out(op, M, N, K):
 
 
 @pytest.mark.parametrize("op", ["nt", "nn", "tn"])
+@pytest.mark.parametrize("M,N,K", [(300, 520, 200), (520, 776, 72), (256, 256, 8192),
+                                   (1000, 1000, 1000)])
+def test_gemm_cta_pair_tiles(op, M, N, K):
+    """M, N >= 256 run as 256 x 256 tiles on CTA pairs: ragged edges in M, N and K, a split-K
+    case (one tile, K = 8192), and the bf16 output of the same tiles."""
+    c, ref = _gemm_case(op, M, N, K, V.F32, M * 7 + N + K)
+    assert rel(c, ref) <= 3e-5, rel(c, ref)
+    c, ref = _gemm_case(op, M, N, K, V.BF16, M * 7 + N + K + 1)
+    assert rel(c, ref) <= 1e-2, rel(c, ref)
+
+
+@pytest.mark.parametrize("op", ["nt", "nn", "tn"])
 def test_gemm_bf16_out_and_accumulate(op):
     c, ref = _gemm_case(op, 512, 768, 320, V.BF16, 5)
     assert rel(c, ref) <= 1e-2

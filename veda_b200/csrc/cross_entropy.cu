@@ -4,7 +4,8 @@
 // src/libs/ops/Softmax.cpp:82-151) materialises fp32 log-probabilities and probabilities for the
 // whole [lanes, V] block. Here one CTA owns a row: pass 1 reads it once keeping a running
 // (max, sum of exp) per thread (online normaliser), reduced across the CTA; pass 2 re-reads it
-// (an L2 hit: 148 SMs x one 300 KB row in flight fits the 126 MB L2) and writes
+// (an L2 hit: 2 CTAs on each of 148 SMs keep 296 rows of 300 KB in flight, inside the 126 MB L2)
+// and writes
 //   dlogits = grad_scale * exp(x - max - log(sum))   minus grad_scale at the target,
 // the (p - onehot) * g/lanes of Loss.cpp:80-99 with p = exp(log_softmax) as the reference forms
 // it. row_loss = -(x_t - max - log(sum)) in fp32; the mean over rows is taken in double by
@@ -19,7 +20,18 @@ namespace
 {
 
 constexpr int kThreads = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
 
+// 2^x with the hardware approximation (relative error ~2^-22; -inf -> 0)
+__device__ __forceinline__ float ex2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// (m, s): running max of x log2(e) and sum of 2^(x log2(e) - m)
 __device__ __forceinline__ void online_merge(float& m, float& s, float om, float os)
 {
     if (om == -INFINITY)
@@ -34,54 +46,95 @@ __device__ __forceinline__ void online_merge(float& m, float& s, float om, float
     }
     if (om > m)
     {
-        s = s * expf(m - om) + os;
+        s = s * ex2(m - om) + os;
         m = om;
     }
     else
     {
-        s = s + os * expf(om - m);
+        s = s + os * ex2(om - m);
     }
 }
 
+// Adds a group of N values (already scaled by log2 e) to (m, s): one max over the group, a
+// rescale only when the group raises the running max, then N exponentials.
+template <int N>
+__device__ __forceinline__ void online_add(float& m, float& s, const float (&y)[N])
+{
+    float gm = y[0];
+#pragma unroll
+    for (int j = 1; j < N; ++j) gm = fmaxf(gm, y[j]);
+    if (gm > m)
+    {
+        s = (m == -INFINITY) ? 0.0f : s * ex2(m - gm);
+        m = gm;
+    }
+    if (m == -INFINITY)
+    {
+        return;   // every value so far is -inf
+    }
+    float a = 0.0f, b = 0.0f;
+#pragma unroll
+    for (int j = 0; j < N; j += 2)
+    {
+        a += ex2(y[j] - m);
+        if (j + 1 < N) b += ex2(y[j + 1] - m);
+    }
+    s += a + b;
+}
+
+// One CTA per row (grid-stride). Pass 1 streams the row from HBM; pass 2 re-reads it from L2
+// (at most 2 CTAs per SM: 296 rows of 304 KB in flight stay well inside the 126 MB L2) and writes
+// the gradient. Exponentials run in the log2 domain on the MUFU unit.
 template <typename T, bool VEC>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 2)
 ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__ targets,
           float* __restrict__ row_loss, T* dlogits, int64_t ldd, int64_t rows, int64_t vocab,
           float grad_scale, int* status)
 {
     constexpr int V = VEC ? Vec16<T>::N : 1;
+    constexpr int U = VEC ? 2 : 1;   // vectors in flight per thread
     __shared__ float red_m[kThreads / 32];
     __shared__ float red_s[kThreads / 32];
-    __shared__ float final_m, final_log;
+    __shared__ float final_m, final_log2;
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x)
     {
         const T* x = logits + row * ldl;
+        const int64_t t = targets[row];
+        const bool valid = t >= 0 && t < vocab;
+        // the target logit is read before the block barrier: with dlogits aliasing logits, pass 2
+        // of other threads may overwrite it afterwards
+        const float xt = (threadIdx.x == 0 && valid) ? to_f32(x[t]) : 0.0f;
         float m = -INFINITY, s = 0.0f;
-        for (int64_t i = static_cast<int64_t>(threadIdx.x) * V; i < vocab;
-             i += static_cast<int64_t>(kThreads) * V)
+        int64_t i = static_cast<int64_t>(threadIdx.x) * V;
+        for (; i + static_cast<int64_t>(kThreads) * V * (U - 1) < vocab; i += static_cast<int64_t>(kThreads) * V * U)
+        {
+            float v[U][V];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+            {
+                if constexpr (VEC)
+                    load16(x + i + static_cast<int64_t>(u) * kThreads * V, v[u]);
+                else
+                    v[u][0] = to_f32(x[i]);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+            {
+#pragma unroll
+                for (int j = 0; j < V; ++j) v[u][j] *= kLog2e;
+                online_add<V>(m, s, v[u]);
+            }
+        }
+        for (; i < vocab; i += static_cast<int64_t>(kThreads) * V)
         {
             float v[V];
             if constexpr (VEC)
-            {
                 load16(x + i, v);
-            }
             else
-            {
                 v[0] = to_f32(x[i]);
-            }
 #pragma unroll
-            for (int j = 0; j < V; ++j)
-            {
-                if (v[j] > m)
-                {
-                    s = (m == -INFINITY ? 0.0f : s * expf(m - v[j])) + 1.0f;
-                    m = v[j];
-                }
-                else if (v[j] != -INFINITY || m != -INFINITY)
-                {
-                    s += expf(v[j] - m);
-                }
-            }
+            for (int j = 0; j < V; ++j) v[j] *= kLog2e;
+            online_add<V>(m, s, v);
         }
         // warp then block merge of (m, s)
 #pragma unroll
@@ -106,12 +159,10 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
                 online_merge(bm, bs, red_m[w], red_s[w]);
             }
             final_m = bm;
-            final_log = logf(bs);
+            final_log2 = log2f(bs);
         }
         __syncthreads();
-        const float mx = final_m, lg = final_log;
-        const int64_t t = targets[row];
-        const bool valid = t >= 0 && t < vocab;
+        const float shift = final_m + final_log2;   // log2 of the normaliser, in log2 units
         if (threadIdx.x == 0)
         {
             if (!valid)
@@ -127,30 +178,30 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
             }
             else if (row_loss != nullptr)
             {
-                row_loss[row] = -((to_f32(x[t]) - mx) - lg);
+                // -log softmax at the target = ln 2 * (shift - x_t log2 e)
+                row_loss[row] = (shift - xt * kLog2e) * kLn2;
             }
         }
         if (dlogits != nullptr && valid)
         {
             T* d = dlogits + row * ldd;
-            for (int64_t i = static_cast<int64_t>(threadIdx.x) * V; i < vocab;
-                 i += static_cast<int64_t>(kThreads) * V)
+            for (int64_t k = static_cast<int64_t>(threadIdx.x) * V; k < vocab;
+                 k += static_cast<int64_t>(kThreads) * V)
             {
                 float v[V];
                 if constexpr (VEC)
                 {
-                    load16(x + i, v);
+                    load16(x + k, v);
                 }
                 else
                 {
-                    v[0] = to_f32(x[i]);
+                    v[0] = to_f32(x[k]);
                 }
 #pragma unroll
                 for (int j = 0; j < V; ++j)
                 {
-                    const float p = expf((v[j] - mx) - lg);
-                    float g = grad_scale * p;
-                    if (i + j == t)
+                    float g = grad_scale * ex2(fmaf(v[j], kLog2e, -shift));
+                    if (k + j == t)
                     {
                         g -= grad_scale;
                     }
@@ -158,11 +209,11 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
                 }
                 if constexpr (VEC)
                 {
-                    store16(d + i, v);
+                    store16(d + k, v);
                 }
                 else
                 {
-                    d[i] = from_f32<T>(v[0]);
+                    d[k] = from_f32<T>(v[0]);
                 }
             }
         }
@@ -228,7 +279,7 @@ extern "C" int veda_cross_entropy(const void* logits, int64_t ldl, const int64_t
     const bool vec = aligned16(logits) && ldl % v == 0 && vocab % v == 0 &&
                      (dlogits == nullptr || (aligned16(dlogits) && ldd % v == 0));
     const unsigned grid = static_cast<unsigned>(
-        rows < static_cast<int64_t>(sm_count()) * 4 ? rows : static_cast<int64_t>(sm_count()) * 4);
+        rows < static_cast<int64_t>(sm_count()) * 2 ? rows : static_cast<int64_t>(sm_count()) * 2);
 #define VEDA_CE(T, VEC)                                                                           \
     ce_kernel<T, VEC><<<grid, kThreads, 0, stream>>>(static_cast<const T*>(logits), ldl, targets, \
                                                      row_loss, static_cast<T*>(dlogits), ldd,    \

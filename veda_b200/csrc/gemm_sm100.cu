@@ -28,6 +28,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 namespace veda::cuda
@@ -366,6 +367,274 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
     }
 }
 
+// ---- paired-CTA kernel ------------------------------------------------------------------------
+// A cluster of two CTAs on one TPC computes a 256 x 256 output tile with tcgen05.mma.cta_group::2
+// (M = 256, N = 256, K = 16) issued by the even CTA: each CTA stages its own 128 rows of A and its
+// own 128 columns of B (a 128 x 128 layout per CTA, exactly the single-CTA operand layout), and the
+// tensor cores of the pair read both halves. Per k-block each SM then streams 32 KB instead of the
+// 48 KB a 128 x 256 tile needs, and six stages fit in shared memory. Each CTA's TMEM receives its
+// 128 rows of the tile (two 256-column accumulators); each CTA's epilogue stores its rows.
+// Loads carry no multicast: each CTA loads only its own operand halves. The odd CTA's loads
+// complete on the even CTA's stage barrier (the .cta_group::2 form of the TMA load, which may
+// signal the peer's barrier); tcgen05.commit signals stage release and tile completion to the
+// barriers of both CTAs; the odd CTA's epilogue releases an accumulator on the even CTA's barrier.
+struct Cfg2
+{
+    static constexpr int STAGES = 6;
+    static constexpr int A_BYTES = 128 * BK * 2;   // this CTA's 128 rows of A
+    static constexpr int B_BYTES = 128 * BK * 2;   // this CTA's 128 columns of B
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared::cluster address of the same shared variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync()
+{
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// TMA tile load whose completion may be signalled on the peer CTA's barrier (no multicast).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                                 int x, int y)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrives (once the issuing thread's MMAs complete) on the barrier at this offset in both CTAs.
+__device__ __forceinline__ void commit_pair(uint64_t* bar)
+{
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;" ::"r"(smem_u32(bar)),
+        "h"(static_cast<uint16_t>(3))
+        : "memory");
+}
+
+template <bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                const Params p)
+{
+    using C_ = Cfg2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* sa = smem;
+    uint8_t* sb = smem + C_::STAGES * C_::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sb + C_::STAGES * C_::B_BYTES);
+    uint64_t* empty = full + C_::STAGES;
+    uint64_t* tfull = empty + C_::STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();     // 0: issues the MMAs; 1: its peer
+    const int cid = static_cast<int>(blockIdx.x >> 1);
+    const int nclusters = static_cast<int>(gridDim.x >> 1);
+
+    if (threadIdx.x == 0)
+    {
+        *abort = 0;
+        for (int s = 0; s < C_::STAGES; ++s)
+        {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b)
+        {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 8);   // 4 epilogue warps in each CTA
+        }
+        mbar_fence_init();
+    }
+    if (warp == 1)
+    {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(C_::TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    fence_before();
+    __syncthreads();
+    cluster_sync();   // both CTAs' barriers are initialised before any cross-CTA signal
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int units = p.num_m * p.num_n * p.splits;
+
+    if (warp == 0 && lane == 0)
+    {
+        tma_prefetch(&tma_a);
+        tma_prefetch(&tma_b);
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int u = cid; u < units; u += nclusters)
+        {
+            int mb, nb, split;
+            unit_coords(u, p, mb, nb, split);
+            const int kb0 = split * p.kb_per_split;
+            const int kb1 = min(p.kblocks, kb0 + p.kb_per_split);
+            const int row0 = mb * 256 + static_cast<int>(rank) * 128;
+            const int col0 = nb * 256 + static_cast<int>(rank) * 128;
+            for (int kb = kb0; kb < kb1; ++kb)
+            {
+                mbar_wait(&empty[stage], phase ^ 1, p.status, abort);
+                if (rank == 0)
+                {
+                    mbar_expect_tx(&full[stage], 2 * C_::STAGE_BYTES);   // both CTAs' halves
+                }
+                const uint32_t bar = peer_addr(&full[stage], 0);
+                uint8_t* a_dst = sa + stage * C_::A_BYTES;
+                uint8_t* b_dst = sb + stage * C_::B_BYTES;
+                if constexpr (!A_MN)
+                {
+                    tma_load_2d_pair(a_dst, &tma_a, bar, kb * BK, row0);
+                }
+                else
+                {
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                    {
+                        tma_load_2d_pair(a_dst + j * (BK * 128), &tma_a, bar, row0 + j * 64, kb * BK);
+                    }
+                }
+                if constexpr (!B_MN)
+                {
+                    tma_load_2d_pair(b_dst, &tma_b, bar, kb * BK, col0);
+                }
+                else
+                {
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                    {
+                        tma_load_2d_pair(b_dst + j * (BK * 128), &tma_b, bar, col0 + j * 64, kb * BK);
+                    }
+                }
+                if (++stage == C_::STAGES)
+                {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+    }
+    else if (warp == 1 && lane == 0 && rank == 0)
+    {
+        constexpr uint32_t idesc = instr_desc(256, 256, A_MN, B_MN);
+        int stage = 0;
+        uint32_t phase = 0;
+        int it = 0;
+        for (int u = cid; u < units; u += nclusters, ++it)
+        {
+            int mb, nb, split;
+            unit_coords(u, p, mb, nb, split);
+            const int kb0 = split * p.kb_per_split;
+            const int kb1 = min(p.kblocks, kb0 + p.kb_per_split);
+            const int buf = it & 1;
+            const uint32_t tphase = (it >> 1) & 1;
+            mbar_wait(&tempty[buf], tphase ^ 1, p.status, abort);
+            fence_after();
+            const uint32_t d = tmem + static_cast<uint32_t>(buf * 256);
+            for (int kb = kb0; kb < kb1; ++kb)
+            {
+                mbar_wait(&full[stage], phase, p.status, abort);
+                fence_after();
+                const uint32_t a_base = smem_u32(sa + stage * C_::A_BYTES);
+                const uint32_t b_base = smem_u32(sb + stage * C_::B_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk)
+                {
+                    const uint64_t ad = A_MN ? smem_desc(a_base + kk * 2048, BK * 128, 1024)
+                                             : smem_desc(a_base + kk * 32, 16, 1024);
+                    const uint64_t bd = B_MN ? smem_desc(b_base + kk * 2048, BK * 128, 1024)
+                                             : smem_desc(b_base + kk * 32, 16, 1024);
+                    mma_pair(d, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+                }
+                commit_pair(&empty[stage]);
+                if (++stage == C_::STAGES)
+                {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            commit_pair(&tfull[buf]);
+        }
+    }
+    else if (warp >= 2)
+    {
+        const int quarter = warp & 3;
+        const uint32_t release = peer_addr(&tempty[0], 0);   // the even CTA's tempty[0]
+        int it = 0;
+        for (int u = cid; u < units; u += nclusters, ++it)
+        {
+            int mb, nb, split;
+            unit_coords(u, p, mb, nb, split);
+            const int buf = it & 1;
+            const uint32_t tphase = (it >> 1) & 1;
+            mbar_wait(&tfull[buf], tphase, p.status, abort);
+            fence_after();
+            const int row = mb * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
+            const uint32_t base = tmem + static_cast<uint32_t>(buf * 256) +
+                                  (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < 256; c += 32)
+            {
+                uint32_t r[32];
+                tmem_ld32(base + static_cast<uint32_t>(c), r);
+                store_chunk<256>(p, row, nb * 256 + c, r);
+            }
+            fence_before();
+            __syncwarp();
+            if (lane == 0)
+            {
+                asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                                 release + static_cast<uint32_t>(buf * 8))
+                             : "memory");
+            }
+        }
+    }
+    fence_before();
+    __syncthreads();
+    cluster_sync();   // no CTA leaves while its peer may still read its operands or barriers
+    if (warp == 1)
+    {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(C_::TMEM_COLS));
+    }
+}
+
 // ---- host ------------------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
 {
@@ -422,11 +691,71 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int
     return check_launch("veda_gemm (tcgen05)");
 }
 
-// Picks a split-K factor (fp32 output only) that best fills whole waves of SMs: the fraction of
-// SM-time doing useful tiles, less a small charge per extra split for its atomic traffic.
-int choose_splits(int tiles, int kblocks, bool allowed)
+// Launches the paired-CTA kernel on `clusters` clusters of two; -1 if clusters cannot be
+// scheduled (the caller then uses the single-CTA kernel).
+template <bool A_MN, bool B_MN>
+int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int clusters,
+               cudaStream_t s)
 {
-    const int sms = sm_count();
+    auto kernel = tc_gemm2_kernel<A_MN, B_MN>;
+    kernel<<<2 * clusters, kThreads, Cfg2::SMEM, s>>>(ma, mb, p);
+    count_launch();
+    return check_launch("veda_gemm (tcgen05, CTA pair)");
+}
+
+// How many two-CTA clusters of the paired kernel fit on the device at once (0: none).
+template <bool A_MN, bool B_MN>
+int pair_clusters()
+{
+    static int cached_device = -1, cached = 0;
+    int device = 0;
+    cudaGetDevice(&device);
+    if (cached_device != device)
+    {
+        auto kernel = tc_gemm2_kernel<A_MN, B_MN>;
+        cached = 0;
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2::SMEM) ==
+            cudaSuccess)
+        {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(2 * (sm_count() / 2));
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = Cfg2::SMEM;
+            cudaLaunchAttribute attr{};
+            attr.id = cudaLaunchAttributeClusterDimension;
+            attr.val.clusterDim.x = 2;
+            attr.val.clusterDim.y = 1;
+            attr.val.clusterDim.z = 1;
+            cfg.attrs = &attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) == cudaSuccess)
+            {
+                cached = n;
+            }
+            cudaGetLastError();
+        }
+        cached_device = device;
+    }
+    return cached;
+}
+
+// The paired kernel serves M, N >= 256 unless VEDA_GEMM_SINGLE_CTA=1.
+bool pair_enabled()
+{
+    static const bool enabled = [] {
+        const char* v = std::getenv("VEDA_GEMM_SINGLE_CTA");
+        return !(v != nullptr && v[0] == '1');
+    }();
+    return enabled;
+}
+
+// Picks a split-K factor (fp32 output only) that best fills whole waves of `slots` workers (SMs,
+// or CTA pairs): the fraction of worker-time doing useful tiles, less a small charge per extra
+// split for its atomic traffic.
+int choose_splits(int tiles, int kblocks, bool allowed, int slots)
+{
+    const int sms = slots;
     if (!allowed)
     {
         return 1;
@@ -452,11 +781,78 @@ int choose_splits(int tiles, int kblocks, bool allowed)
     return best;
 }
 
+// 256 x 256 tiles on CTA pairs; -1 when the pair kernel cannot run (tensor maps, clusters, or a
+// split-K that needs a general beta), so the caller uses the single-CTA kernel.
+int tc_gemm_pair(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* B,
+                 int64_t ldb, void* C, int64_t ldc, int dtype_c, float alpha, float beta,
+                 cudaStream_t s)
+{
+    const bool a_mn = op == kTN;
+    const bool b_mn = op != kNT;
+    const int clusters_max = op == kNT ? pair_clusters<false, false>()
+                           : op == kNN ? pair_clusters<false, true>()
+                                       : pair_clusters<true, true>();
+    if (clusters_max < 1)
+    {
+        return -1;
+    }
+    CUtensorMap ma, mb;
+    // each CTA loads a 128-row (or, MN-major, 2 x 64-column) piece of its own half
+    bool ok = a_mn ? make_map(&ma, A, M, K, lda, 64, 64) : make_map(&ma, A, K, M, lda, 64, 128);
+    ok = ok && (b_mn ? make_map(&mb, B, N, K, ldb, 64, 64) : make_map(&mb, B, K, N, ldb, 64, 128));
+    if (!ok)
+    {
+        return -1;
+    }
+    Params p{};
+    p.M = static_cast<int>(M);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.num_m = static_cast<int>((M + 255) / 256);
+    p.num_n = static_cast<int>((N + 255) / 256);
+    p.kblocks = static_cast<int>((K + BK - 1) / BK);
+    p.C = C;
+    p.ldc = ldc;
+    p.alpha = alpha;
+    p.beta = beta;
+    p.out_f32 = dtype_c == VEDA_F32;
+    p.vec_ok = aligned16(C) && (ldc % (dtype_c == VEDA_F32 ? 4 : 8)) == 0;
+    p.status = device_status_ptr();
+    const int tiles = p.num_m * p.num_n;
+    p.splits = choose_splits(tiles, p.kblocks, p.out_f32 != 0, clusters_max);
+    p.kb_per_split = (p.kblocks + p.splits - 1) / p.splits;
+    p.atomic = p.splits > 1;
+    if (p.atomic)
+    {
+        if (beta != 0.0f && beta != 1.0f)
+        {
+            return -1;
+        }
+        if (beta == 0.0f && cudaMemset2DAsync(C, ldc * 4, 0, N * 4, M, s) != cudaSuccess)
+        {
+            return fail(VEDA_ERR_CUDA, "veda_gemm: clearing C for split-K failed");
+        }
+        p.beta = 0.0f;
+    }
+    const int clusters = std::min(tiles * p.splits, clusters_max);
+    if (op == kNT) return launch_tc2<false, false>(ma, mb, p, clusters, s);
+    if (op == kNN) return launch_tc2<false, true>(ma, mb, p, clusters, s);
+    return launch_tc2<true, true>(ma, mb, p, clusters, s);
+}
+
 int tc_gemm(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* B,
             int64_t ldb, void* C, int64_t ldc, int dtype_c, float alpha, float beta, cudaStream_t s)
 {
     const bool a_mn = op == kTN;
     const bool b_mn = op != kNT;
+    if (M >= 256 && N >= 256 && pair_enabled())
+    {
+        const int rc = tc_gemm_pair(op, M, N, K, A, lda, B, ldb, C, ldc, dtype_c, alpha, beta, s);
+        if (rc != -1)
+        {
+            return rc;
+        }
+    }
     const int BN = N >= 256 ? 256 : 128;
     CUtensorMap ma, mb;
     bool ok = a_mn ? make_map(&ma, A, M, K, lda, 64, 64) : make_map(&ma, A, K, M, lda, 64, BM);
@@ -481,7 +877,7 @@ int tc_gemm(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
     p.vec_ok = aligned16(C) && (ldc % (dtype_c == VEDA_F32 ? 4 : 8)) == 0;
     p.status = device_status_ptr();
     const int tiles = p.num_m * p.num_n;
-    p.splits = choose_splits(tiles, p.kblocks, p.out_f32 != 0);
+    p.splits = choose_splits(tiles, p.kblocks, p.out_f32 != 0, sm_count());
     p.kb_per_split = (p.kblocks + p.splits - 1) / p.splits;
     p.atomic = p.splits > 1;
     if (p.atomic)

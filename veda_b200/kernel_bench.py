@@ -8,6 +8,12 @@
         causal GQA attention backward, B 8, H 16, Hkv 8, Dh 128, bf16, seed 2; 5*B*H*T^2*Dh FLOP.
     python -m veda_b200.kernel_bench gemm --op nt --m 8192 --n 151936 --k 1024 [--reps 3]
         one GEMM shape (used for the ncu captures).
+    python -m veda_b200.kernel_bench bw [--tokens 8192] [--reps 20]
+        the bandwidth-bound kernels of one Qwen3-0.6B layer at `tokens` tokens (hidden 1024,
+        16 query / 8 KV heads of 128, FFN 3072, vocab 151936 for the cross-entropy): RMSNorm
+        forward / backward (with residual gradient and dgamma), QK-norm+RoPE forward / backward,
+        SwiGLU forward / backward, cross-entropy; GB/s from the algorithmic bytes (each tensor
+        read or written once).
 Prints one JSON line per measurement.
 """
 from __future__ import annotations
@@ -134,6 +140,81 @@ def attn_bwd(seqs, reps):
         torch.cuda.empty_cache()
 
 
+def bandwidth_kernels(tokens, reps):
+    import torch
+    import veda_b200 as V
+    L = V.lib()
+    s = torch.cuda.current_stream()
+    _, hbm, kind = _peaks()
+    g = torch.Generator(device="cuda").manual_seed(3)
+    T, D, H, Hk, F, Vv = 2048, 1024, 16, 8, 3072, 151936
+    bf = torch.bfloat16
+    rn = lambda *shape: torch.randn(*shape, device="cuda", generator=g).to(bf)  # noqa: E731
+    x, dy, dr = rn(tokens, D), rn(tokens, D), rn(tokens, D)
+    gam = rn(D)
+    y, dx = torch.empty_like(x), torch.empty_like(x)
+    dg = torch.zeros(D, dtype=torch.float32, device="cuda")
+    ws = torch.empty(L.veda_rmsnorm_bwd_workspace(tokens, D), dtype=torch.uint8, device="cuda")
+    qkv = rn(tokens, (H + 2 * Hk) * 128)
+    dqkv = rn(tokens, (H + 2 * Hk) * 128)
+    qo = torch.empty(tokens, H * 128, dtype=bf, device="cuda")
+    gq = rn(128)
+    cos = torch.randn(T, 128, device="cuda", generator=g)
+    sin = torch.randn(T, 128, device="cuda", generator=g)
+    dgq = torch.zeros(128, dtype=torch.float32, device="cuda")
+    wsq = torch.empty(L.veda_qknorm_rope_bwd_workspace(tokens, H, 128), dtype=torch.uint8, device="cuda")
+    gu = rn(tokens, 2 * F)
+    hh = torch.empty(tokens, F, dtype=bf, device="cuda")
+    dh = rn(tokens, F)
+    dgu = torch.empty_like(gu)
+    logits = rn(tokens, Vv)
+    tgt = torch.randint(0, Vv, (tokens,), device="cuda", generator=g)
+    rl = torch.empty(tokens, dtype=torch.float32, device="cuda")
+    dl = torch.empty_like(logits)
+    st = s.cuda_stream
+    B2 = 2
+    cases = {
+        "rmsnorm_fwd": (lambda: V.check(L.veda_rmsnorm_fwd(x.data_ptr(), D, gam.data_ptr(), y.data_ptr(), D,
+                                                           tokens, D, 1e-6, V.BF16, st)),
+                        2 * tokens * D * B2),
+        "rmsnorm_bwd": (lambda: V.check(L.veda_rmsnorm_bwd(x.data_ptr(), D, gam.data_ptr(), dy.data_ptr(), D,
+                                                           dr.data_ptr(), D, dx.data_ptr(), D, dg.data_ptr(),
+                                                           ws.data_ptr(), ws.numel(), tokens, D, 1e-6, V.BF16,
+                                                           st)),
+                        4 * tokens * D * B2),
+        "qknorm_rope_fwd_q": (lambda: V.check(L.veda_qknorm_rope_fwd(qkv.data_ptr(), qkv.shape[1], gq.data_ptr(),
+                                                                     cos.data_ptr(), sin.data_ptr(), qo.data_ptr(),
+                                                                     H * 128, tokens, H, T, 128, 1e-6, V.BF16,
+                                                                     st)),
+                              2 * tokens * H * 128 * B2),
+        "qknorm_rope_bwd_q": (lambda: V.check(L.veda_qknorm_rope_bwd(qkv.data_ptr(), qkv.shape[1], gq.data_ptr(),
+                                                                     cos.data_ptr(), sin.data_ptr(),
+                                                                     dqkv.data_ptr(), dqkv.shape[1],
+                                                                     qo.data_ptr(), H * 128, dgq.data_ptr(),
+                                                                     wsq.data_ptr(), wsq.numel(), tokens, H, T,
+                                                                     128, 1e-6, V.BF16, st)),
+                              3 * tokens * H * 128 * B2),
+        "swiglu_fwd": (lambda: V.check(L.veda_swiglu_fwd(gu.data_ptr(), 2 * F, gu.data_ptr() + F * B2, 2 * F,
+                                                         hh.data_ptr(), F, tokens, F, V.BF16, st)),
+                       3 * tokens * F * B2),
+        "swiglu_bwd": (lambda: V.check(L.veda_swiglu_bwd(gu.data_ptr(), 2 * F, gu.data_ptr() + F * B2, 2 * F,
+                                                         dh.data_ptr(), F, dgu.data_ptr(), 2 * F,
+                                                         dgu.data_ptr() + F * B2, 2 * F, tokens, F, V.BF16,
+                                                         st)),
+                       5 * tokens * F * B2),
+        "cross_entropy": (lambda: V.check(L.veda_cross_entropy(logits.data_ptr(), Vv, tgt.data_ptr(), rl.data_ptr(),
+                                                               dl.data_ptr(), Vv, tokens, Vv, 1.0 / tokens, 0,
+                                                               V.BF16, st)),
+                          2 * tokens * Vv * B2),
+    }
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for name, (fn, nbytes) in cases.items():
+        ms = _time(fn, reps, s, flush)
+        print(json.dumps({"bench": "bw", "kernel": name, "tokens": tokens, "ms": ms,
+                          "gbs": nbytes / (ms / 1e3) / 1e9, "peak_gbs": hbm, "peak_kind": kind,
+                          "frac": nbytes / (ms / 1e3) / 1e9 / hbm}), flush=True)
+
+
 def one_gemm(op, M, N, K, reps):
     import torch
     import veda_b200 as V
@@ -168,11 +249,16 @@ def main():
     c.add_argument("--n", type=int, default=151936)
     c.add_argument("--k", type=int, default=1024)
     c.add_argument("--reps", type=int, default=3)
+    d = sub.add_parser("bw")
+    d.add_argument("--tokens", type=int, default=8192)
+    d.add_argument("--reps", type=int, default=20)
     args = ap.parse_args()
     if args.cmd == "mm-sweep":
         mm_sweep(args.reps)
     elif args.cmd == "attn-bwd":
         attn_bwd(args.seq, args.reps)
+    elif args.cmd == "bw":
+        bandwidth_kernels(args.tokens, args.reps)
     else:
         one_gemm(args.op, args.m, args.n, args.k, args.reps)
 
