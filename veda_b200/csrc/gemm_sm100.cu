@@ -50,7 +50,7 @@ struct Cfg
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 4 * 2 * 32 * 128;
 };
 
 struct Params
@@ -63,8 +63,32 @@ struct Params
     int out_f32;      // 1: fp32 C, 0: bf16 C
     int atomic;       // 1: split-K partial tiles are added with fp32 atomics
     int vec_ok;       // C base and ldc allow 16-byte stores
+    int out_mode;     // 0: stores from registers; 1: TMA store; 2: TMA reduce-add (fp32 C)
     int* status;
 };
+
+// Per-warp output staging: two 4 KB tiles of 32 rows x 128 bytes (128-byte swizzle), so the
+// epilogue writes C with coalesced TMA stores instead of one 16-byte store per row and thread.
+constexpr int kStageTile = 32 * 128;
+constexpr int kOutStaging = 4 * 2 * kStageTile;   // 4 epilogue warps, double-buffered
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(tc::smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
+// Element-wise atomic add of a shared tile onto global memory (fp32).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y)
+{
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(tc::smem_u32(src)), "r"(x), "r"(y)
+        : "memory");
+}
 
 using namespace tc;
 
@@ -183,10 +207,101 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int col0, 
     }
 }
 
+// TMA epilogue of one warp: its 32 accumulator rows (TMEM lanes) x NCOLS columns, from TMEM
+// through a swizzled staging tile to C (store, or fp32 reduce-add for split-K / beta = 1).
+// `row0`, `col0`: C coordinates of the warp's first row and the tile's first column; `nstore`
+// counts this warp's bulk groups (staging buffers alternate; one group may stay in flight).
+template <int NCOLS>
+__device__ __forceinline__ void epilogue_tma(const Params& p, const CUtensorMap* mc, uint32_t taddr,
+                                             int row0, int col0, uint8_t* staging, uint32_t& nstore,
+                                             int lane)
+{
+    if (row0 >= p.M)
+    {
+        return;
+    }
+    const int chunk = p.out_f32 ? 32 : 64;   // columns per 128-byte staging row
+    for (int c = 0; c < NCOLS; c += chunk)
+    {
+        if (col0 + c >= p.N)
+        {
+            break;
+        }
+        uint8_t* buf = staging + (nstore & 1) * kStageTile;
+        if (nstore >= 2)
+        {
+            if (lane == 0)
+            {
+                bulk_wait_group_read<1>();   // the group that last used `buf` has read it
+            }
+            __syncwarp();
+        }
+        uint32_t r0[32];
+        tmem_ld32(taddr + static_cast<uint32_t>(c), r0);
+        uint8_t* row = buf + lane * 128;
+        if (p.out_f32)
+        {
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+            {
+                float4 o = make_float4(__uint_as_float(r0[4 * k]), __uint_as_float(r0[4 * k + 1]),
+                                       __uint_as_float(r0[4 * k + 2]), __uint_as_float(r0[4 * k + 3]));
+                if (p.alpha != 1.0f)
+                {
+                    o.x *= p.alpha;
+                    o.y *= p.alpha;
+                    o.z *= p.alpha;
+                    o.w *= p.alpha;
+                }
+                *reinterpret_cast<float4*>(row + ((k ^ (lane & 7)) << 4)) = o;
+            }
+        }
+        else
+        {
+            uint32_t r1[32];
+            tmem_ld32(taddr + static_cast<uint32_t>(c + 32), r1);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+            {
+                const uint32_t* src = k < 4 ? &r0[8 * k] : &r1[8 * (k - 4)];
+                uint32_t w[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                {
+                    float a = __uint_as_float(src[2 * q]), b = __uint_as_float(src[2 * q + 1]);
+                    if (p.alpha != 1.0f)
+                    {
+                        a *= p.alpha;
+                        b *= p.alpha;
+                    }
+                    const __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+                    w[q] = *reinterpret_cast<const uint32_t*>(&t);
+                }
+                *reinterpret_cast<uint4*>(row + ((k ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0)
+        {
+            if (p.out_mode == 2)
+            {
+                tma_reduce_add_2d(mc, buf, col0 + c, row0);
+            }
+            else
+            {
+                tma_store_2d(mc, buf, col0 + c, row0);
+            }
+            bulk_commit_group();
+        }
+        ++nstore;
+    }
+}
+
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-               const Params p)
+               const __grid_constant__ CUtensorMap tma_c, const Params p)
 {
     using C_ = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
@@ -194,7 +309,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* sa = smem;
     uint8_t* sb = smem + C_::STAGES * C_::A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sb + C_::STAGES * C_::B_BYTES);
+    uint8_t* staging = sb + C_::STAGES * C_::B_BYTES;   // epilogue staging tiles
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + kOutStaging);
     uint64_t* empty = full + C_::STAGES;
     uint64_t* tfull = empty + C_::STAGES;
     uint64_t* tempty = tfull + 2;
@@ -330,6 +446,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
     else if (warp >= 2)
     {
         const int quarter = warp & 3;
+        uint32_t nstore = 0;
         int it = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++it)
         {
@@ -342,12 +459,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             const int row = mb * BM + quarter * 32 + lane;
             const uint32_t base = tmem + static_cast<uint32_t>(buf * BN) +
                                   (static_cast<uint32_t>(quarter * 32) << 16);
-#pragma unroll 1
-            for (int c = 0; c < BN; c += 32)
+            if (p.out_mode != 0)
             {
-                uint32_t r[32];
-                tmem_ld32(base + static_cast<uint32_t>(c), r);
-                store_chunk<BN>(p, row, nb * BN + c, r);
+                epilogue_tma<BN>(p, &tma_c, base, mb * BM + quarter * 32, nb * BN,
+                                 staging + (warp - 2) * 2 * kStageTile, nstore, lane);
+            }
+            else
+            {
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32)
+                {
+                    uint32_t r[32];
+                    tmem_ld32(base + static_cast<uint32_t>(c), r);
+                    store_chunk<BN>(p, row, nb * BN + c, r);
+                }
             }
             fence_before();
             __syncwarp();
@@ -356,6 +481,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                 mbar_arrive(&tempty[buf]);
             }
         }
+    }
+    if (warp >= 2 && lane == 0)
+    {
+        bulk_wait_group<0>();   // staged output fully written before the CTA's memory goes
     }
     fence_before();
     __syncthreads();
@@ -385,7 +514,7 @@ struct Cfg2
     static constexpr int B_BYTES = 128 * BK * 2;   // this CTA's 128 columns of B
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 512;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + kOutStaging + 1024 + 256;
 };
 
 __device__ __forceinline__ uint32_t cluster_rank()
@@ -442,7 +571,7 @@ __device__ __forceinline__ void commit_pair(uint64_t* bar)
 template <bool A_MN, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                const Params p)
+                const __grid_constant__ CUtensorMap tma_c, const Params p)
 {
     using C_ = Cfg2;
     extern __shared__ uint8_t smem_raw[];
@@ -450,7 +579,8 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* sa = smem;
     uint8_t* sb = smem + C_::STAGES * C_::A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sb + C_::STAGES * C_::B_BYTES);
+    uint8_t* staging = sb + C_::STAGES * C_::B_BYTES;   // epilogue staging tiles
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + kOutStaging);
     uint64_t* empty = full + C_::STAGES;
     uint64_t* tfull = empty + C_::STAGES;
     uint64_t* tempty = tfull + 2;
@@ -595,6 +725,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
     {
         const int quarter = warp & 3;
         const uint32_t release = peer_addr(&tempty[0], 0);   // the even CTA's tempty[0]
+        uint32_t nstore = 0;
         int it = 0;
         for (int u = cid; u < units; u += nclusters, ++it)
         {
@@ -607,12 +738,20 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
             const int row = mb * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
             const uint32_t base = tmem + static_cast<uint32_t>(buf * 256) +
                                   (static_cast<uint32_t>(quarter * 32) << 16);
-#pragma unroll 1
-            for (int c = 0; c < 256; c += 32)
+            if (p.out_mode != 0)
             {
-                uint32_t r[32];
-                tmem_ld32(base + static_cast<uint32_t>(c), r);
-                store_chunk<256>(p, row, nb * 256 + c, r);
+                epilogue_tma<256>(p, &tma_c, base, row - lane, nb * 256,
+                                  staging + (warp - 2) * 2 * kStageTile, nstore, lane);
+            }
+            else
+            {
+#pragma unroll 1
+                for (int c = 0; c < 256; c += 32)
+                {
+                    uint32_t r[32];
+                    tmem_ld32(base + static_cast<uint32_t>(c), r);
+                    store_chunk<256>(p, row, nb * 256 + c, r);
+                }
             }
             fence_before();
             __syncwarp();
@@ -623,6 +762,10 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
                              : "memory");
             }
         }
+    }
+    if (warp >= 2 && lane == 0)
+    {
+        bulk_wait_group<0>();   // staged output fully written before the CTA's memory goes
     }
     fence_before();
     __syncthreads();
@@ -674,8 +817,8 @@ bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, 
 }
 
 template <int BN, bool A_MN, bool B_MN>
-int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int grid,
-              cudaStream_t s)
+int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const Params& p,
+              int grid, cudaStream_t s)
 {
     auto kernel = tc_gemm_kernel<BN, A_MN, B_MN>;
     static int configured_device = -1;
@@ -686,7 +829,7 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
         configured_device = device;
     }
-    kernel<<<grid, kThreads, Cfg<BN>::SMEM, s>>>(ma, mb, p);
+    kernel<<<grid, kThreads, Cfg<BN>::SMEM, s>>>(ma, mb, mc, p);
     count_launch();
     return check_launch("veda_gemm (tcgen05)");
 }
@@ -694,11 +837,11 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int
 // Launches the paired-CTA kernel on `clusters` clusters of two; -1 if clusters cannot be
 // scheduled (the caller then uses the single-CTA kernel).
 template <bool A_MN, bool B_MN>
-int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int clusters,
-               cudaStream_t s)
+int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const Params& p,
+               int clusters, cudaStream_t s)
 {
     auto kernel = tc_gemm2_kernel<A_MN, B_MN>;
-    kernel<<<2 * clusters, kThreads, Cfg2::SMEM, s>>>(ma, mb, p);
+    kernel<<<2 * clusters, kThreads, Cfg2::SMEM, s>>>(ma, mb, mc, p);
     count_launch();
     return check_launch("veda_gemm (tcgen05, CTA pair)");
 }
@@ -748,6 +891,53 @@ bool pair_enabled()
         return !(v != nullptr && v[0] == '1');
     }();
     return enabled;
+}
+
+// How the epilogue writes C: TMA store (beta = 0), TMA fp32 reduce-add (split-K partial tiles, or
+// beta = 1 accumulation into fp32), else per-thread stores from registers (general beta, bf16
+// accumulation, or a C whose base / row pitch a tensor map cannot describe). Builds the C map.
+int output_mode(Params& p, CUtensorMap* mc, void* C, int64_t M, int64_t N, int64_t ldc, float beta)
+{
+    p.out_mode = 0;
+    if (!p.vec_ok)
+    {
+        return 0;
+    }
+    int mode = 0;
+    if (p.atomic)
+    {
+        mode = p.out_f32 ? 2 : 0;
+    }
+    else if (beta == 0.0f)
+    {
+        mode = 1;
+    }
+    else if (beta == 1.0f && p.out_f32)
+    {
+        mode = 2;
+    }
+    if (mode == 0)
+    {
+        return 0;
+    }
+    auto fn = encode_fn();
+    if (fn == nullptr)
+    {
+        return 0;
+    }
+    const size_t es = p.out_f32 ? 4 : 2;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldc) * es};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / es), 32};
+    const cuuint32_t estr[2] = {1, 1};
+    if (fn(mc, p.out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, C,
+           dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    {
+        return 0;
+    }
+    p.out_mode = mode;
+    return mode;
 }
 
 // Picks a split-K factor (fp32 output only) that best fills whole waves of `slots` workers (SMs,
@@ -834,10 +1024,12 @@ int tc_gemm_pair(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t
         }
         p.beta = 0.0f;
     }
+    CUtensorMap mc{};
+    output_mode(p, &mc, C, M, N, ldc, beta);
     const int clusters = std::min(tiles * p.splits, clusters_max);
-    if (op == kNT) return launch_tc2<false, false>(ma, mb, p, clusters, s);
-    if (op == kNN) return launch_tc2<false, true>(ma, mb, p, clusters, s);
-    return launch_tc2<true, true>(ma, mb, p, clusters, s);
+    if (op == kNT) return launch_tc2<false, false>(ma, mb, mc, p, clusters, s);
+    if (op == kNN) return launch_tc2<false, true>(ma, mb, mc, p, clusters, s);
+    return launch_tc2<true, true>(ma, mb, mc, p, clusters, s);
 }
 
 int tc_gemm(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* B,
@@ -896,17 +1088,19 @@ int tc_gemm(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
         }
         p.beta = 0.0f;
     }
+    CUtensorMap mc{};
+    output_mode(p, &mc, C, M, N, ldc, beta);
     const int units = tiles * p.splits;
     const int grid = std::min(units, sm_count());
     const bool big = BN == 256;
     if (op == kNT)
-        return big ? launch_tc<256, false, false>(ma, mb, p, grid, s)
-                   : launch_tc<128, false, false>(ma, mb, p, grid, s);
+        return big ? launch_tc<256, false, false>(ma, mb, mc, p, grid, s)
+                   : launch_tc<128, false, false>(ma, mb, mc, p, grid, s);
     if (op == kNN)
-        return big ? launch_tc<256, false, true>(ma, mb, p, grid, s)
-                   : launch_tc<128, false, true>(ma, mb, p, grid, s);
-    return big ? launch_tc<256, true, true>(ma, mb, p, grid, s)
-               : launch_tc<128, true, true>(ma, mb, p, grid, s);
+        return big ? launch_tc<256, false, true>(ma, mb, mc, p, grid, s)
+                   : launch_tc<128, false, true>(ma, mb, mc, p, grid, s);
+    return big ? launch_tc<256, true, true>(ma, mb, mc, p, grid, s)
+               : launch_tc<128, true, true>(ma, mb, mc, p, grid, s);
 }
 
 bool tc_eligible(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,

@@ -13,7 +13,7 @@
         16 query / 8 KV heads of 128, FFN 3072, vocab 151936 for the cross-entropy): RMSNorm
         forward / backward (with residual gradient and dgamma), QK-norm+RoPE forward / backward,
         SwiGLU forward / backward, cross-entropy; GB/s from the algorithmic bytes (each tensor
-        read or written once).
+        read or written once). --kernels NAME... runs a subset (names as printed).
 Prints one JSON line per measurement.
 """
 from __future__ import annotations
@@ -140,7 +140,7 @@ def attn_bwd(seqs, reps):
         torch.cuda.empty_cache()
 
 
-def bandwidth_kernels(tokens, reps):
+def bandwidth_kernels(tokens, reps, only=None):
     import torch
     import veda_b200 as V
     L = V.lib()
@@ -167,10 +167,11 @@ def bandwidth_kernels(tokens, reps):
     hh = torch.empty(tokens, F, dtype=bf, device="cuda")
     dh = rn(tokens, F)
     dgu = torch.empty_like(gu)
-    logits = rn(tokens, Vv)
+    want_ce = only is None or "cross_entropy" in only
+    logits = rn(tokens, Vv) if want_ce else None
     tgt = torch.randint(0, Vv, (tokens,), device="cuda", generator=g)
     rl = torch.empty(tokens, dtype=torch.float32, device="cuda")
-    dl = torch.empty_like(logits)
+    dl = torch.empty_like(logits) if want_ce else None
     st = s.cuda_stream
     B2 = 2
     cases = {
@@ -209,6 +210,8 @@ def bandwidth_kernels(tokens, reps):
     }
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     for name, (fn, nbytes) in cases.items():
+        if only is not None and name not in only:
+            continue
         ms = _time(fn, reps, s, flush)
         print(json.dumps({"bench": "bw", "kernel": name, "tokens": tokens, "ms": ms,
                           "gbs": nbytes / (ms / 1e3) / 1e9, "peak_gbs": hbm, "peak_kind": kind,
@@ -252,13 +255,14 @@ def main():
     d = sub.add_parser("bw")
     d.add_argument("--tokens", type=int, default=8192)
     d.add_argument("--reps", type=int, default=20)
+    d.add_argument("--kernels", nargs="+", default=None)
     args = ap.parse_args()
     if args.cmd == "mm-sweep":
         mm_sweep(args.reps)
     elif args.cmd == "attn-bwd":
         attn_bwd(args.seq, args.reps)
     elif args.cmd == "bw":
-        bandwidth_kernels(args.tokens, args.reps)
+        bandwidth_kernels(args.tokens, args.reps, args.kernels)
     else:
         one_gemm(args.op, args.m, args.n, args.k, args.reps)
 
