@@ -31,7 +31,8 @@ def rng(seed):
 # RMSNorm
 # ---------------------------------------------------------------------------------------------
 @pytest.mark.parametrize("dtype,rows,n", [(V.F32, 128, 64), (V.F32, 37, 100), (V.BF16, 8192, 1024),
-                                          (V.BF16, 33, 2048), (V.F32, 8192, 1024)])
+                                          (V.BF16, 33, 2048), (V.F32, 8192, 1024),
+                                          (V.BF16, 1001, 512), (V.F32, 77, 2048)])
 def test_rmsnorm_fwd_bwd(dtype, rows, n):
     r = rng(rows + n)
     x = r.standard_normal((rows, n)).astype(F32)
@@ -81,6 +82,7 @@ def test_rmsnorm_plain_matches_golden():
 # ---------------------------------------------------------------------------------------------
 @pytest.mark.parametrize("dtype,B,T,H,Dh,theta", [(V.F32, 4, 32, 4, 16, 1e4),
                                                  (V.BF16, 2, 256, 16, 128, 1e6),
+                                                 (V.BF16, 3, 100, 3, 128, 1e6),
                                                  (V.F32, 1, 64, 8, 128, 1e6)])
 def test_qknorm_rope(dtype, B, T, H, Dh, theta):
     r = rng(T + H)

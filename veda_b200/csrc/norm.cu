@@ -23,6 +23,15 @@ namespace
 
 constexpr int kWarps = 8;   // warps per block for the row kernels
 
+// QK-norm backward: two resident blocks per SM, each writing one 128-float partial row of the
+// gain gradient.
+inline int qk_bwd_grid(int64_t rows)
+{
+    int64_t blocks = (rows + 4 * kWarps - 1) / (4 * kWarps);
+    const int64_t cap = 2LL * sm_count();
+    return static_cast<int>(blocks < cap ? (blocks < 1 ? 1 : blocks) : cap);
+}
+
 inline int norm_bwd_grid(int64_t rows)
 {
     int64_t blocks = (rows + kWarps - 1) / kWarps;
@@ -230,32 +239,34 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ g
     }
 }
 
-// dgamma[i] += sum over blocks of partials[b][i], in a fixed order: 32 columns x 8 row groups
-// per CTA, group k summing blocks k, k+8, ... in ascending order, then the 8 groups in order.
+// dgamma[i] += sum over blocks of partials[b][i], in a fixed order.
 __global__ void __launch_bounds__(256)
 reduce_partials_kernel(const float* __restrict__ partials, int blocks, int n,
                        float* __restrict__ dgamma)
 {
-    __shared__ float part[8][33];
-    const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
-    const int col = blockIdx.x * 32 + lane;
+    // 8 columns x 32 row groups per block: group g sums partial rows g, g + 32, ... of its column
+    // in that order, then the 32 group sums are added in group order (deterministic).
+    __shared__ float part[32][9];
+    const int c = threadIdx.x & 7, grp = threadIdx.x >> 3;
+    const int col = blockIdx.x * 8 + c;
     float acc = 0.0f;
     if (col < n)
     {
-        for (int b = grp; b < blocks; b += 8)
+#pragma unroll 4
+        for (int b = grp; b < blocks; b += 32)
         {
             acc += partials[static_cast<size_t>(b) * n + col];
         }
     }
-    part[grp][lane] = acc;
+    part[grp][c] = acc;
     __syncthreads();
     if (grp == 0 && col < n)
     {
         float s = 0.0f;
 #pragma unroll
-        for (int g = 0; g < 8; ++g)
+        for (int g = 0; g < 32; ++g)
         {
-            s += part[g][lane];
+            s += part[g][c];
         }
         dgamma[col] += s;
     }
@@ -264,7 +275,7 @@ reduce_partials_kernel(const float* __restrict__ partials, int blocks, int n,
 inline void launch_reduce_partials(const float* partials, int blocks, int n, float* dgamma,
                                    cudaStream_t s)
 {
-    reduce_partials_kernel<<<(n + 31) / 32, 256, 0, s>>>(partials, blocks, n, dgamma);
+    reduce_partials_kernel<<<(n + 7) / 8, 256, 0, s>>>(partials, blocks, n, dgamma);
     count_launch();
 }
 
@@ -289,6 +300,201 @@ __device__ __forceinline__ void unpack16(const uint4& raw, float (&out)[16 / siz
         {
             out[2 * i] = __uint_as_float(w[i] << 16);
             out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        }
+    }
+}
+
+// ---- row-group kernels: TPR threads per row, each owning V consecutive columns ----------------
+// A 512-thread block works on 512 / TPR rows at a time; the next row of each group is loaded
+// before the current one is reduced, so loads stay in flight across the block-wide reduction.
+// Each thread's columns are fixed, so gamma stays in registers and (backward) the gain gradient
+// accumulates per thread without a shared-memory pass per row.
+constexpr int kRowThreads = 512;
+
+template <typename T, int TPR>
+__global__ void __launch_bounds__(kRowThreads)
+rmsnorm_fwd_rows_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ gamma,
+                        T* __restrict__ y, int64_t ldy, int64_t rows, float eps)
+{
+    constexpr int V = Vec16<T>::N;
+    constexpr int G = kRowThreads / TPR;     // rows per block step
+    constexpr int W = TPR / 32;              // warps per row
+    constexpr int n = TPR * V;
+    __shared__ float red[2][G][W];
+    const int g = threadIdx.x / TPR, t = threadIdx.x % TPR;
+    const int wr = t >> 5, lane = threadIdx.x & 31;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * G;
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * G;
+    const int64_t iters = first < rows ? (rows - first + step - 1) / step : 0;
+    float gm[V];
+    if (gamma != nullptr)
+    {
+        load16(gamma + t * V, gm);
+    }
+    int64_t row = first + g;
+    uint4 cur = make_uint4(0, 0, 0, 0);
+    if (row < rows)
+    {
+        cur = *reinterpret_cast<const uint4*>(x + row * ldx + t * V);
+    }
+    for (int64_t k = 0; k < iters; ++k)
+    {
+        const int64_t nrow = row + step;
+        uint4 nxt = make_uint4(0, 0, 0, 0);
+        if (nrow < rows)
+        {
+            nxt = *reinterpret_cast<const uint4*>(x + nrow * ldx + t * V);
+        }
+        float v[V];
+        unpack16<T>(cur, v);
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < V; ++j) ss += v[j] * v[j];
+        ss = warp_sum(ss);
+        const int b = static_cast<int>(k & 1);
+        if (lane == 0) red[b][g][wr] = ss;
+        __syncthreads();
+        float tot = 0.0f;
+#pragma unroll
+        for (int w = 0; w < W; ++w) tot += red[b][g][w];
+        const float inv = 1.0f / sqrtf(tot / static_cast<float>(n) + eps);
+        if (row < rows)
+        {
+#pragma unroll
+            for (int j = 0; j < V; ++j)
+            {
+                const float tn = v[j] * inv;
+                v[j] = gamma != nullptr ? tn * gm[j] : tn;
+            }
+            store16(y + row * ldy + t * V, v);
+        }
+        cur = nxt;
+        row = nrow;
+    }
+}
+
+// Shared memory: [G][n] fp32 for the final cross-group sum of the gain gradient.
+// Two blocks per SM (64 registers a thread) keep 32 warps and 64 rows of loads in flight per SM.
+template <typename T, int TPR>
+__global__ void __launch_bounds__(kRowThreads, 2)
+rmsnorm_bwd_rows_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ gamma,
+                        const T* __restrict__ dy, int64_t lddy, const T* __restrict__ dresid,
+                        int64_t ldr, T* __restrict__ dx, int64_t lddx, float* __restrict__ partials,
+                        int64_t rows, float eps)
+{
+    constexpr int V = Vec16<T>::N;
+    constexpr int G = kRowThreads / TPR;
+    constexpr int W = TPR / 32;
+    constexpr int n = TPR * V;
+    __shared__ float2 red[2][G][W];
+    extern __shared__ float part[];
+    const int g = threadIdx.x / TPR, t = threadIdx.x % TPR;
+    const int wr = t >> 5, lane = threadIdx.x & 31;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * G;
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * G;
+    const int64_t iters = first < rows ? (rows - first + step - 1) / step : 0;
+    const int64_t col = static_cast<int64_t>(t) * V;
+    float acc[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) acc[j] = 0.0f;
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    int64_t row = first + g;
+    uint4 cx = zero, cg = zero, cr = zero;
+    if (row < rows)
+    {
+        cx = *reinterpret_cast<const uint4*>(x + row * ldx + col);
+        cg = *reinterpret_cast<const uint4*>(dy + row * lddy + col);
+        if (dresid != nullptr) cr = *reinterpret_cast<const uint4*>(dresid + row * ldr + col);
+    }
+    for (int64_t k = 0; k < iters; ++k)
+    {
+        const int64_t nrow = row + step;
+        uint4 nx = zero, ng = zero, nr = zero;
+        if (nrow < rows)
+        {
+            nx = *reinterpret_cast<const uint4*>(x + nrow * ldx + col);
+            ng = *reinterpret_cast<const uint4*>(dy + nrow * lddy + col);
+            if (dresid != nullptr) nr = *reinterpret_cast<const uint4*>(dresid + nrow * ldr + col);
+        }
+        float ss = 0.0f, w = 0.0f;
+        {
+            float xv[V], gv[V], gm[V];
+            unpack16<T>(cx, xv);
+            unpack16<T>(cg, gv);
+            if (gamma != nullptr)
+            {
+                load16(gamma + col, gm);   // an L1 hit after the first row
+            }
+            else
+            {
+#pragma unroll
+                for (int j = 0; j < V; ++j) gm[j] = 1.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < V; ++j)
+            {
+                ss += xv[j] * xv[j];
+                w += (gv[j] * gm[j]) * xv[j];
+            }
+        }
+        ss = warp_sum(ss);
+        w = warp_sum(w);
+        const int b = static_cast<int>(k & 1);
+        if (lane == 0) red[b][g][wr] = make_float2(ss, w);
+        __syncthreads();
+        float tss = 0.0f, tw = 0.0f;
+#pragma unroll
+        for (int q = 0; q < W; ++q)
+        {
+            tss += red[b][g][q].x;
+            tw += red[b][g][q].y;
+        }
+        if (row < rows)
+        {
+            // the row is unpacked again from its packed registers (fewer live values across the
+            // barrier)
+            float xv[V], gv[V], gm[V];
+            unpack16<T>(cx, xv);
+            unpack16<T>(cg, gv);
+            if (gamma != nullptr)
+            {
+                load16(gamma + col, gm);
+            }
+            else
+            {
+#pragma unroll
+                for (int j = 0; j < V; ++j) gm[j] = 1.0f;
+            }
+            const float inv = 1.0f / sqrtf(tss / static_cast<float>(n) + eps);
+            const float coupling = tw * inv * inv * inv / static_cast<float>(n);
+            float res[V];
+            if (dresid != nullptr) unpack16<T>(cr, res);
+#pragma unroll
+            for (int j = 0; j < V; ++j)
+            {
+                float d = (gv[j] * gm[j]) * inv - xv[j] * coupling;
+                if (dresid != nullptr) d = res[j] + d;
+                acc[j] += gv[j] * (xv[j] * inv);
+                xv[j] = d;
+            }
+            store16(dx + row * lddx + col, xv);
+        }
+        cx = nx;
+        cg = ng;
+        cr = nr;
+        row = nrow;
+    }
+    if (partials != nullptr)
+    {
+#pragma unroll
+        for (int j = 0; j < V; ++j) part[g * n + col + j] = acc[j];
+        __syncthreads();
+        for (int c = threadIdx.x; c < n; c += kRowThreads)
+        {
+            float s = 0.0f;
+#pragma unroll
+            for (int q = 0; q < G; ++q) s += part[q * n + c];
+            partials[static_cast<size_t>(blockIdx.x) * n + c] = s;
         }
     }
 }
@@ -453,13 +659,37 @@ rmsnorm_bwd_reg_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict
 
 // ---- QK-norm + RoPE, head_dim 128, bf16: eight lanes per (token, head) row ---------------------
 // Lane q of an 8-lane group holds elements [8q, 8q+8) and their rotation partners
-// [64+8q, 64+8q+8) as two 16-byte vectors; a warp works on 4 rows at once.
+// [64+8q, 64+8q+8) as two 16-byte vectors; a warp works on 4 rows at once and loads its next 4
+// rows (kept packed as bf16) before working on the current ones.
 __device__ __forceinline__ float group8_sum(float v)
 {
     v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
     v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
     v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
     return v;
+}
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& raw, float (&out)[8])
+{
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        out[2 * i] = __uint_as_float(w[i] << 16);
+        out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+}
+
+__device__ __forceinline__ void rope_row(const float* cosv, const float* sinv, int t, int q,
+                                         float (&cs)[8], float (&sn)[8])
+{
+    const float4* cp = reinterpret_cast<const float4*>(cosv + static_cast<int64_t>(t) * 128 + 8 * q);
+    const float4* sp = reinterpret_cast<const float4*>(sinv + static_cast<int64_t>(t) * 128 + 8 * q);
+    const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+    cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
+    cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+    sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
+    sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
 }
 
 __global__ void __launch_bounds__(kWarps * 32)
@@ -470,60 +700,68 @@ qknorm_rope_fwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16*
 {
     const int lane = threadIdx.x & 31, q = lane & 7;
     const int64_t rows = tokens * heads;
-    float ga[8], gb[8];
-    load16(gamma + 8 * q, ga);
-    load16(gamma + 64 + 8 * q, gb);
     const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps * 4;
-    for (int64_t base = (static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5)) * 4;
-         base < rows; base += stride)
-    {
-        const int64_t row = base + (lane >> 3);
-        const bool valid = row < rows;
-        const int64_t token = valid ? row / heads : 0;
-        const int head = valid ? static_cast<int>(row - token * heads) : 0;
-        const int t = static_cast<int>(token % seq_len);
-        float a[8], b[8];
-        if (valid)
+    int64_t row = (static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5)) * 4 + (lane >> 3);
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    auto load_row = [&](int64_t r, uint4& a, uint4& b) {
+        if (r < rows)
         {
-            const bf16* xr = x + token * ldx + static_cast<int64_t>(head) * 128;
-            load16(xr + 8 * q, a);
-            load16(xr + 64 + 8 * q, b);
+            const int64_t token = r / heads;
+            const bf16* xr = x + token * ldx + (r - token * heads) * 128;
+            a = *reinterpret_cast<const uint4*>(xr + 8 * q);
+            b = *reinterpret_cast<const uint4*>(xr + 64 + 8 * q);
         }
         else
         {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) a[j] = b[j] = 0.0f;
+            a = zero;
+            b = zero;
         }
+    };
+    uint4 ca, cb;
+    load_row(row, ca, cb);
+    // every lane of a warp runs the same number of steps (the group sums shuffle across rows)
+    const int64_t wfirst = row - (lane >> 3);
+    const int64_t iters = wfirst < rows ? (rows - wfirst + stride - 1) / stride : 0;
+    for (int64_t k = 0; k < iters; ++k)
+    {
+        uint4 na, nb;
+        load_row(row + stride, na, nb);
+        float a[8], b[8];
+        bf16x8_to_f32(ca, a);
+        bf16x8_to_f32(cb, b);
         float ss = 0.0f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) ss += a[j] * a[j] + b[j] * b[j];
         ss = group8_sum(ss);
-        const float r = sqrtf(ss / 128.0f + eps);
-        if (!valid)
+        if (row < rows)
         {
-            continue;
-        }
-        const float4* cp = reinterpret_cast<const float4*>(cosv + static_cast<int64_t>(t) * 128 + 8 * q);
-        const float4* sp = reinterpret_cast<const float4*>(sinv + static_cast<int64_t>(t) * 128 + 8 * q);
-        const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
-        const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-        const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-        float oa[8], ob[8];
+            const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
+            const int64_t token = row / heads;
+            const int t = static_cast<int>(token % seq_len);
+            float ga[8], gb[8], cs[8], sn[8];
+            load16(gamma + 8 * q, ga);
+            load16(gamma + 64 + 8 * q, gb);
+            rope_row(cosv, sinv, t, q, cs, sn);
+            float oa[8], ob[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-        {
-            const float na = (a[j] / r) * ga[j], nb = (b[j] / r) * gb[j];
-            oa[j] = na * cs[j] - nb * sn[j];
-            ob[j] = nb * cs[j] + na * sn[j];
+            for (int j = 0; j < 8; ++j)
+            {
+                const float na2 = (a[j] * inv) * ga[j], nb2 = (b[j] * inv) * gb[j];
+                oa[j] = na2 * cs[j] - nb2 * sn[j];
+                ob[j] = nb2 * cs[j] + na2 * sn[j];
+            }
+            bf16* yr = y + token * ldy + (row - token * heads) * 128;
+            store16(yr + 8 * q, oa);
+            store16(yr + 64 + 8 * q, ob);
         }
-        bf16* yr = y + token * ldy + static_cast<int64_t>(head) * 128;
-        store16(yr + 8 * q, oa);
-        store16(yr + 64 + 8 * q, ob);
+        ca = na;
+        cb = nb;
+        row += stride;
     }
 }
 
 // Shared memory: [kWarps * 4][128] fp32 gain-gradient rows (one per row slot).
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, 2)
 qknorm_rope_bwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx,
                             const bf16* __restrict__ gamma, const float* __restrict__ cosv,
                             const float* __restrict__ sinv, const bf16* __restrict__ dy,
@@ -534,70 +772,90 @@ qknorm_rope_bwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx,
     __shared__ float part[kWarps * 4][128];
     const int lane = threadIdx.x & 31, q = lane & 7, slot = (threadIdx.x >> 5) * 4 + (lane >> 3);
     const int64_t rows = tokens * heads;
-    float ga[8], gb[8], acca[8], accb[8];
-    load16(gamma + 8 * q, ga);
-    load16(gamma + 64 + 8 * q, gb);
+    float acca[8], accb[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acca[j] = accb[j] = 0.0f;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps * 4;
-    for (int64_t base = (static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5)) * 4;
-         base < rows; base += stride)
-    {
-        const int64_t row = base + (lane >> 3);
-        const bool valid = row < rows;
-        const int64_t token = valid ? row / heads : 0;
-        const int head = valid ? static_cast<int>(row - token * heads) : 0;
-        const int t = static_cast<int>(token % seq_len);
-        float a[8], b[8], da[8], db[8];
-        if (valid)
+    int64_t row = (static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5)) * 4 + (lane >> 3);
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    auto load_row = [&](int64_t r, uint4& a, uint4& b, uint4& da, uint4& db) {
+        if (r < rows)
         {
-            const bf16* xr = x + token * ldx + static_cast<int64_t>(head) * 128;
-            const bf16* gr = dy + token * lddy + static_cast<int64_t>(head) * 128;
-            load16(xr + 8 * q, a);
-            load16(xr + 64 + 8 * q, b);
-            load16(gr + 8 * q, da);
-            load16(gr + 64 + 8 * q, db);
+            const int64_t token = r / heads;
+            const int64_t h = r - token * heads;
+            const bf16* xr = x + token * ldx + h * 128;
+            const bf16* gr = dy + token * lddy + h * 128;
+            a = *reinterpret_cast<const uint4*>(xr + 8 * q);
+            b = *reinterpret_cast<const uint4*>(xr + 64 + 8 * q);
+            da = *reinterpret_cast<const uint4*>(gr + 8 * q);
+            db = *reinterpret_cast<const uint4*>(gr + 64 + 8 * q);
         }
         else
         {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) a[j] = b[j] = da[j] = db[j] = 0.0f;
+            a = b = da = db = zero;
         }
-        const float4* cp = reinterpret_cast<const float4*>(cosv + static_cast<int64_t>(t) * 128 + 8 * q);
-        const float4* sp = reinterpret_cast<const float4*>(sinv + static_cast<int64_t>(t) * 128 + 8 * q);
-        const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
-        const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-        const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-        float ss = 0.0f, w = 0.0f, na[8], nb[8];
+    };
+    uint4 ca, cb, cda, cdb;
+    load_row(row, ca, cb, cda, cdb);
+    const int64_t wfirst = row - (lane >> 3);
+    const int64_t iters = wfirst < rows ? (rows - wfirst + stride - 1) / stride : 0;
+    for (int64_t k = 0; k < iters; ++k)
+    {
+        uint4 na, nb, nda, ndb;
+        load_row(row + stride, na, nb, nda, ndb);
+        const bool valid = row < rows;
+        const int64_t token = valid ? row / heads : 0;
+        const int t = static_cast<int>(token % seq_len);
+        float cs[8], sn[8], ga[8], gb[8];
+        rope_row(cosv, sinv, t, q, cs, sn);
+        load16(gamma + 8 * q, ga);
+        load16(gamma + 64 + 8 * q, gb);
+        float a[8], b[8], na2[8], nb2[8];
+        {
+            float da[8], db[8];
+            bf16x8_to_f32(cda, da);
+            bf16x8_to_f32(cdb, db);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+            {
+                // rotation by -theta: the gradient at the normed-and-scaled value
+                na2[j] = da[j] * cs[j] + db[j] * sn[j];
+                nb2[j] = db[j] * cs[j] - da[j] * sn[j];
+            }
+        }
+        bf16x8_to_f32(ca, a);
+        bf16x8_to_f32(cb, b);
+        float ss = 0.0f, w = 0.0f;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
         {
-            // rotation by -theta: the gradient at the normed-and-scaled value
-            na[j] = da[j] * cs[j] + db[j] * sn[j];
-            nb[j] = db[j] * cs[j] - da[j] * sn[j];
             ss += a[j] * a[j] + b[j] * b[j];
-            w += (na[j] * ga[j]) * a[j] + (nb[j] * gb[j]) * b[j];
+            w += (na2[j] * ga[j]) * a[j] + (nb2[j] * gb[j]) * b[j];
         }
         ss = group8_sum(ss);
         w = group8_sum(w);
-        if (!valid)
+        if (valid)
         {
-            continue;
-        }
-        const float r = sqrtf(ss / 128.0f + eps);
-        const float coupling = w / (128.0f * r * r * r);
-        float oa[8], ob[8];
+            const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
+            const float coupling = w * inv * inv * inv / 128.0f;
+            float oa[8], ob[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-        {
-            acca[j] += na[j] * (a[j] / r);
-            accb[j] += nb[j] * (b[j] / r);
-            oa[j] = (na[j] * ga[j]) / r - a[j] * coupling;
-            ob[j] = (nb[j] * gb[j]) / r - b[j] * coupling;
+            for (int j = 0; j < 8; ++j)
+            {
+                acca[j] += na2[j] * (a[j] * inv);
+                accb[j] += nb2[j] * (b[j] * inv);
+                oa[j] = (na2[j] * ga[j]) * inv - a[j] * coupling;
+                ob[j] = (nb2[j] * gb[j]) * inv - b[j] * coupling;
+            }
+            bf16* out = dx + token * lddx + (row - token * heads) * 128;
+            store16(out + 8 * q, oa);
+            store16(out + 64 + 8 * q, ob);
         }
-        bf16* out = dx + token * lddx + static_cast<int64_t>(head) * 128;
-        store16(out + 8 * q, oa);
-        store16(out + 64 + 8 * q, ob);
+        ca = na;
+        cb = nb;
+        cda = nda;
+        cdb = ndb;
+        row += stride;
     }
     if (partials != nullptr)
     {
@@ -611,9 +869,9 @@ qknorm_rope_bwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx,
         for (int i = threadIdx.x; i < 128; i += blockDim.x)
         {
             float s = 0.0f;
-            for (int k = 0; k < kWarps * 4; ++k)
+            for (int k2 = 0; k2 < kWarps * 4; ++k2)
             {
-                s += part[k][i];
+                s += part[k2][i];
             }
             partials[static_cast<size_t>(blockIdx.x) * 128 + i] = s;
         }
@@ -835,7 +1093,26 @@ int launch_rms_fwd(const void* x, int64_t ldx, const void* gamma, void* y, int64
         std::min<int64_t>((rows + kWarps - 1) / kWarps, static_cast<int64_t>(sm_count()) * 16));
     constexpr int64_t V = 16 / sizeof(T);
     const int64_t chunks = n % (32 * V) == 0 ? n / (32 * V) : 0;
-    if (vec && (chunks == 1 || chunks == 2 || chunks == 4 || chunks == 8))
+    const int64_t tpr = n % V == 0 ? n / V : 0;
+    if (vec && (tpr == 64 || tpr == 128 || tpr == 256 || tpr == 512))
+    {
+        // 512 / tpr rows per block step; enough blocks for four per SM
+        const int64_t per = kRowThreads / tpr;
+        const unsigned g2 = static_cast<unsigned>(
+            std::max<int64_t>(1, std::min<int64_t>((rows + per - 1) / per, static_cast<int64_t>(sm_count()) * 4)));
+        const T* xp = static_cast<const T*>(x);
+        const T* gp = static_cast<const T*>(gamma);
+        T* yp = static_cast<T*>(y);
+        if (tpr == 64)
+            rmsnorm_fwd_rows_kernel<T, 64><<<g2, kRowThreads, 0, s>>>(xp, ldx, gp, yp, ldy, rows, eps);
+        else if (tpr == 128)
+            rmsnorm_fwd_rows_kernel<T, 128><<<g2, kRowThreads, 0, s>>>(xp, ldx, gp, yp, ldy, rows, eps);
+        else if (tpr == 256)
+            rmsnorm_fwd_rows_kernel<T, 256><<<g2, kRowThreads, 0, s>>>(xp, ldx, gp, yp, ldy, rows, eps);
+        else
+            rmsnorm_fwd_rows_kernel<T, 512><<<g2, kRowThreads, 0, s>>>(xp, ldx, gp, yp, ldy, rows, eps);
+    }
+    else if (vec && (chunks == 1 || chunks == 2 || chunks == 4 || chunks == 8))
     {
         const T* xp = static_cast<const T*>(x);
         const T* gp = static_cast<const T*>(gamma);
@@ -891,7 +1168,21 @@ int launch_rms_bwd(const void* x, int64_t ldx, const void* gamma, const void* dy
                                  static_cast<int>(smem));
         }
     };
-    if (vec && (chunks == 1 || chunks == 2 || chunks == 4 || chunks == 8))
+    const int64_t tpr = n % V == 0 ? n / V : 0;
+    if (vec && (tpr == 64 || tpr == 128 || tpr == 256 || tpr == 512))
+    {
+        // same grid (and partials layout) as the other backward kernels: one partial row per block
+        const size_t psmem = partials != nullptr ? static_cast<size_t>(kRowThreads) * V * sizeof(float) : 0;
+        auto launch_rows = [&](auto kernel) {
+            kernel<<<grid, kRowThreads, psmem, s>>>(xp, ldx, gp, dyp, lddy, rp, ldr, dxp, lddx,
+                                                   partials, rows, eps);
+        };
+        if (tpr == 64) launch_rows(rmsnorm_bwd_rows_kernel<T, 64>);
+        else if (tpr == 128) launch_rows(rmsnorm_bwd_rows_kernel<T, 128>);
+        else if (tpr == 256) launch_rows(rmsnorm_bwd_rows_kernel<T, 256>);
+        else launch_rows(rmsnorm_bwd_rows_kernel<T, 512>);
+    }
+    else if (vec && (chunks == 1 || chunks == 2 || chunks == 4 || chunks == 8))
     {
         auto launch_reg = [&](auto kernel) {
             allow_smem(kernel);
@@ -977,7 +1268,7 @@ extern "C" int veda_rmsnorm_bwd(const void* x, int64_t ldx, const void* gamma, c
 
 extern "C" size_t veda_qknorm_rope_bwd_workspace(int64_t tokens, int64_t heads, int64_t head_dim)
 {
-    return static_cast<size_t>(norm_bwd_grid(tokens * heads)) * static_cast<size_t>(head_dim) *
+    return static_cast<size_t>(qk_bwd_grid(tokens * heads)) * static_cast<size_t>(head_dim) *
            sizeof(float);
 }
 
@@ -1028,7 +1319,7 @@ extern "C" int veda_qknorm_rope_fwd(const void* x, int64_t ldx, const void* gamm
     if (d128_ok(x, ldx, gamma, cosv, sinv, y, ldy, head_dim, dtype))
     {
         const unsigned g4 = static_cast<unsigned>(std::min<int64_t>(
-            (rows + 4 * kWarps - 1) / (4 * kWarps), static_cast<int64_t>(sm_count()) * 16));
+            (rows + 4 * kWarps - 1) / (4 * kWarps), static_cast<int64_t>(sm_count()) * 4));
         qknorm_rope_fwd_d128_kernel<<<g4, kWarps * 32, 0, stream>>>(
             static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(gamma), cosv, sinv,
             static_cast<bf16*>(y), ldy, tokens, static_cast<int>(heads),
@@ -1078,7 +1369,7 @@ extern "C" int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamm
                      "workspace too small (see veda_qknorm_rope_bwd_workspace)");
     }
     const int64_t rows = tokens * heads;
-    const int grid = norm_bwd_grid(rows);
+    const int grid = qk_bwd_grid(rows);
     float* partials = dgamma != nullptr ? static_cast<float*>(workspace) : nullptr;
     const size_t smem = partials != nullptr ? kWarps * head_dim * sizeof(float) : 0;
     if (d128_ok(x, ldx, gamma, cosv, sinv, dy, lddy, head_dim, dtype) &&
