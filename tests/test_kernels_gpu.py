@@ -58,6 +58,28 @@ def test_rmsnorm_fwd_bwd(dtype, rows, n):
     assert rel(host(dgam), dgam_ref + 0.5) <= (1e-4 if dtype == V.F32 else 1e-3)
 
 
+@pytest.mark.parametrize("with_dgamma", [True, False])
+def test_rmsnorm_bwd_without_residual(with_dgamma):
+    """The backward without a residual gradient, with and without the gain gradient."""
+    rows, n = 515, 1024
+    r = rng(71)
+    x = bf(r.standard_normal((rows, n)).astype(F32))
+    gam = bf((1 + 0.1 * r.standard_normal(n)).astype(F32))
+    g = bf(r.standard_normal((rows, n)).astype(F32))
+    dx_ref, dgam_ref = O.rms_norm_gamma_backward(x, gam, g, 1e-6)
+    xd, gamd, gd = dev(x, V.BF16), dev(gam, V.BF16), dev(g, V.BF16)
+    dx = empty((rows, n), V.BF16)
+    dgam = zeros(n) if with_dgamma else None
+    ws = workspace(V.lib().veda_rmsnorm_bwd_workspace(rows, n)) if with_dgamma else None
+    call("veda_rmsnorm_bwd", ptr(xd), n, ptr(gamd), ptr(gd), n, None, 0, ptr(dx), n,
+         ptr(dgam) if with_dgamma else None, ptr(ws) if with_dgamma else None,
+         ws.numel() if with_dgamma else 0, rows, n, 1e-6, V.BF16, stream())
+    sync()
+    assert rel(host(dx), dx_ref) <= TOL[V.BF16]
+    if with_dgamma:
+        assert rel(host(dgam), dgam_ref) <= 1e-3
+
+
 def test_rmsnorm_plain_matches_golden():
     from pathlib import Path
     ops = np.load(Path(__file__).parent / "golden" / "ops_small.npz")

@@ -105,14 +105,18 @@ def test_qwen_shaped_bf16_step_matches_oracle():
     # element whose gradient is below bf16 resolution can take the opposite sign on the GPU and
     # land 2*lr away from the fp32 reference (measured: 0.2-0.8% of elements per tensor, which
     # puts the per-tensor max-abs-relative error at up to 2.4e-2 for matrices with |w| ~ 0.09).
-    # Checked: the difference never exceeds those flips, flips are rare, and apart from them the
-    # weights agree to 2e-2.
+    # Checked: the difference never exceeds those flips; a flip happens only where the reference
+    # gradient is within the gradient tolerance (2e-2 of the tensor's largest gradient) of zero,
+    # so its sign is not resolved at the stated precision; flips stay rare; and apart from them
+    # the weights agree to 2e-2.
     lr = ADAM.learning_rate
     for i in range(len(specs)):
         dw_gpu, dw_ref = w1[i] - params[i], ref[i] - params[i]
         flips = np.sign(dw_gpu) != np.sign(dw_ref)
         assert np.max(np.abs(dw_gpu - dw_ref)) <= 2.02 * lr, specs[i][0]
-        assert flips.mean() <= 0.01, (specs[i][0], flips.mean())
+        g_scale = np.abs(rgrads[i]).max()
+        assert np.all(np.abs(rgrads[i])[flips] <= 2e-2 * g_scale), specs[i][0]
+        assert flips.mean() <= 0.05, (specs[i][0], flips.mean())
         keep = ~flips
         den = np.abs(ref[i]).max()
         assert np.max(np.abs(w1[i] - ref[i])[keep], initial=0.0) <= 2e-2 * den, specs[i][0]

@@ -12,6 +12,7 @@
 // summed in a fixed order into one partial per block, and a second kernel sums the block
 // partials in a fixed order and adds the result into dgamma.
 #include "common.cuh"
+#include "norm_stream.cuh"
 
 #include <algorithm>
 #include <mutex>
@@ -1086,6 +1087,15 @@ template <typename T>
 int launch_rms_fwd(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
                    int64_t rows, int64_t n, float eps, cudaStream_t s)
 {
+    if constexpr (sizeof(T) == 2)
+    {
+        const int rc = rms_fwd_stream(static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(gamma),
+                                      static_cast<bf16*>(y), ldy, rows, n, eps, s);
+        if (rc != -1)
+        {
+            return rc;
+        }
+    }
     const bool vec = vec_ok(x, ldx, static_cast<int>(n), sizeof(T)) &&
                      vec_ok(y, ldy, static_cast<int>(n), sizeof(T)) &&
                      vec_ok(gamma, n, static_cast<int>(n), sizeof(T));
@@ -1153,6 +1163,23 @@ int launch_rms_bwd(const void* x, int64_t ldx, const void* gamma, const void* dy
                      vec_ok(gamma, n, ni, sizeof(T));
     const int grid = norm_bwd_grid(rows);
     float* partials = dgamma != nullptr ? static_cast<float*>(ws) : nullptr;
+    if constexpr (sizeof(T) == 2)
+    {
+        int blocks = 0;
+        const int rc = rms_bwd_stream(static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(gamma),
+                                      static_cast<const bf16*>(dy), lddy, static_cast<const bf16*>(dresid),
+                                      ldr, static_cast<bf16*>(dx), lddx, partials, grid, rows, n, eps, s,
+                                      &blocks);
+        if (rc != -1)
+        {
+            if (rc == VEDA_OK && partials != nullptr)
+            {
+                launch_reduce_partials(partials, blocks, ni, dgamma, s);
+                return check_launch("veda_rmsnorm_bwd");
+            }
+            return rc;
+        }
+    }
     const size_t smem = partials != nullptr ? static_cast<size_t>(kWarps) * n * sizeof(float) : 0;
     constexpr int64_t V = 16 / sizeof(T);
     const int64_t chunks = n % (32 * V) == 0 ? n / (32 * V) : 0;

@@ -1,0 +1,398 @@
+// Streaming RMSNorm forward and backward (bf16 rows of 256..2048 elements).
+//
+// Same arithmetic as the row kernels of norm.cu (src/libs/ops/Normalize.cpp:50-63,
+// src/libs/autograd/NonLinear.cpp:171-196; the gain through Variable.cpp:218-239): fp32 sums,
+// r = sqrt(sum x^2 / n + eps), y = x / r * gamma; dx = G / r - x * sum(G x) / (n r^3) (+ the
+// residual gradient), G = dy * gamma, dgamma = sum over rows of dy * x / r.
+//
+// Structure: one block per SM, 1 producer warp + 8 consumer warps. The producer's lane 0 streams
+// whole rows (x; for the backward also dy and the residual gradient) into a ring of shared-memory
+// stages with bulk asynchronous copies (cp.async.bulk, no tensor map, no multicast) completing on
+// the stage's mbarrier; a stage holds 8 rows, one per consumer warp. Consumers wait for their
+// stage, reduce their row with warp shuffles only (no block barrier), write the output row with
+// coalesced 16-byte stores and release the stage. With 128-192 KB of rows in flight per SM the
+// loads no longer wait on the arithmetic, which is what the register-resident kernels could not
+// reach. Every mbarrier wait is bounded (tc_common.cuh).
+//
+// The gain gradient: each consumer warp accumulates its lanes' columns over the rows it processed;
+// at the end the 8 warps' rows are summed in warp order into one partial row per block (the
+// caller then sums the block partials in block order) — deterministic.
+#include "norm_stream.cuh"
+#include "tc_common.cuh"
+
+namespace veda::cuda
+{
+int* device_status_ptr();
+
+namespace
+{
+using namespace tc;
+
+constexpr int kRows = 8;                       // rows per stage = consumer warps
+constexpr int kThreadsStream = 32 * (1 + kRows);
+constexpr int kRingBytes = 192 * 1024;         // shared-memory ring per block
+
+template <int CH, int NIN>
+struct Ring
+{
+    static constexpr int N = CH * 256;                 // elements per row
+    static constexpr int ROW = N * 2;                  // bytes per bf16 row
+    static constexpr int STAGE = kRows * NIN * ROW;    // bytes per stage
+    static constexpr int STAGES = kRingBytes / STAGE < 8 ? kRingBytes / STAGE : 8;
+    // ring | gamma as fp32 [N] | barriers | abort flag, plus alignment slack
+    static constexpr int SMEM = STAGES * STAGE + N * 4 + 2 * STAGES * 8 + 16 + 128;
+    static_assert(STAGES >= 2, "ring too small");
+};
+
+__device__ __forceinline__ void unpack8(const uint4& raw, float (&o)[8])
+{
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        o[2 * i] = __uint_as_float(w[i] << 16);
+        o[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+}
+
+// Producer: streams NIN input rows per row of each of this block's chunks of kRows rows.
+template <int CH, int NIN>
+__device__ __forceinline__ void produce(uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                        const bf16* const (&src)[3], const int64_t (&ld)[3],
+                                        int64_t rows, int* status, volatile int* abort)
+{
+    using R = Ring<CH, NIN>;
+    const int64_t chunks = (rows + kRows - 1) / kRows;
+    int i = 0;
+    for (int64_t q = blockIdx.x; q < chunks; q += gridDim.x, ++i)
+    {
+        const int st = i % R::STAGES;
+        mbar_wait(&empty[st], ((i / R::STAGES) & 1) ^ 1, status, abort);
+        const int64_t r0 = q * kRows;
+        const int nr = static_cast<int>(rows - r0 < kRows ? rows - r0 : kRows);
+        mbar_expect_tx(&full[st], static_cast<uint32_t>(nr * NIN * R::ROW));
+        uint8_t* dst = ring + st * R::STAGE;
+        for (int r = 0; r < nr; ++r)
+        {
+#pragma unroll
+            for (int k = 0; k < NIN; ++k)
+            {
+                bulk_load(dst + (r * NIN + k) * R::ROW, src[k] + (r0 + r) * ld[k], R::ROW, &full[st]);
+            }
+        }
+    }
+}
+
+template <int CH>
+__global__ void __launch_bounds__(kThreadsStream, 1)
+rms_fwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ gamma,
+                      bf16* __restrict__ y, int64_t ldy, int64_t rows, float eps, int* status)
+{
+    using R = Ring<CH, 1>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
+    float* gsm = reinterpret_cast<float*>(ring + R::STAGES * R::STAGE);   // gamma, fp32
+    uint64_t* full = reinterpret_cast<uint64_t*>(gsm + R::N);
+    uint64_t* empty = full + R::STAGES;
+    volatile int* abort = reinterpret_cast<volatile int*>(empty + R::STAGES);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0)
+    {
+        *abort = 0;
+        for (int s = 0; s < R::STAGES; ++s)
+        {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kRows);
+        }
+        mbar_fence_init();
+    }
+    for (int c = threadIdx.x; c < R::N; c += blockDim.x)
+    {
+        gsm[c] = gamma != nullptr ? __bfloat162float(gamma[c]) : 1.0f;
+    }
+    __syncthreads();
+    if (warp == 0)
+    {
+        if (lane == 0)
+        {
+            const bf16* const src[3] = {x, nullptr, nullptr};
+            const int64_t ld[3] = {ldx, 0, 0};
+            produce<CH, 1>(ring, full, empty, src, ld, rows, status, abort);
+        }
+        return;
+    }
+    const int w = warp - 1;
+    const int64_t chunks = (rows + kRows - 1) / kRows;
+    int i = 0;
+    for (int64_t q = blockIdx.x; q < chunks; q += gridDim.x, ++i)
+    {
+        const int st = i % R::STAGES;
+        mbar_wait(&full[st], (i / R::STAGES) & 1, status, abort);
+        const int64_t row = q * kRows + w;
+        if (row < rows)
+        {
+            const uint8_t* src = ring + st * R::STAGE + w * R::ROW;
+            uint4 xr[CH];
+#pragma unroll
+            for (int c = 0; c < CH; ++c) xr[c] = *reinterpret_cast<const uint4*>(src + (c * 32 + lane) * 16);
+            float ss = 0.0f;
+#pragma unroll
+            for (int c = 0; c < CH; ++c)
+            {
+                float v[8];
+                unpack8(xr[c], v);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+            }
+            ss = warp_sum(ss);
+            const float inv = 1.0f / sqrtf(ss / static_cast<float>(R::N) + eps);
+#pragma unroll
+            for (int c = 0; c < CH; ++c)
+            {
+                float v[8];
+                unpack8(xr[c], v);
+                const float4 g0 = *reinterpret_cast<const float4*>(gsm + (c * 32 + lane) * 8);
+                const float4 g1 = *reinterpret_cast<const float4*>(gsm + (c * 32 + lane) * 8 + 4);
+                const float gm[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = (v[j] * inv) * gm[j];
+                store16(y + row * ldy + (c * 32 + lane) * 8, v);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+}
+
+template <int CH, int NIN>
+__global__ void __launch_bounds__(kThreadsStream, 1)
+rms_bwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ gamma,
+                      const bf16* __restrict__ dy, int64_t lddy, const bf16* __restrict__ dresid,
+                      int64_t ldr, bf16* __restrict__ dx, int64_t lddx, float* __restrict__ partials,
+                      int64_t rows, float eps, int* status)
+{
+    using R = Ring<CH, NIN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
+    float* gsm = reinterpret_cast<float*>(ring + R::STAGES * R::STAGE);   // gamma, fp32
+    uint64_t* full = reinterpret_cast<uint64_t*>(gsm + R::N);
+    uint64_t* empty = full + R::STAGES;
+    volatile int* abort = reinterpret_cast<volatile int*>(empty + R::STAGES);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0)
+    {
+        *abort = 0;
+        for (int s = 0; s < R::STAGES; ++s)
+        {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kRows);
+        }
+        mbar_fence_init();
+    }
+    for (int c = threadIdx.x; c < R::N; c += blockDim.x)
+    {
+        gsm[c] = gamma != nullptr ? __bfloat162float(gamma[c]) : 1.0f;
+    }
+    __syncthreads();
+    float acc[CH][8];
+#pragma unroll
+    for (int c = 0; c < CH; ++c)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[c][j] = 0.0f;
+    if (warp == 0)
+    {
+        if (lane == 0)
+        {
+            const bf16* const src[3] = {x, dy, dresid};
+            const int64_t ld[3] = {ldx, lddy, ldr};
+            produce<CH, NIN>(ring, full, empty, src, ld, rows, status, abort);
+        }
+    }
+    else
+    {
+        const int w = warp - 1;
+        auto gain = [&](int c, float (&gm)[8]) {
+            const float4 g0 = *reinterpret_cast<const float4*>(gsm + (c * 32 + lane) * 8);
+            const float4 g1 = *reinterpret_cast<const float4*>(gsm + (c * 32 + lane) * 8 + 4);
+            gm[0] = g0.x; gm[1] = g0.y; gm[2] = g0.z; gm[3] = g0.w;
+            gm[4] = g1.x; gm[5] = g1.y; gm[6] = g1.z; gm[7] = g1.w;
+        };
+        const int64_t chunks = (rows + kRows - 1) / kRows;
+        int i = 0;
+        for (int64_t q = blockIdx.x; q < chunks; q += gridDim.x, ++i)
+        {
+            const int st = i % R::STAGES;
+            mbar_wait(&full[st], (i / R::STAGES) & 1, status, abort);
+            const int64_t row = q * kRows + w;
+            if (row < rows)
+            {
+                const uint8_t* xs = ring + st * R::STAGE + (w * NIN) * R::ROW;
+                const uint8_t* gs = xs + R::ROW;
+                float ss = 0.0f, wsum = 0.0f;
+#pragma unroll
+                for (int c = 0; c < CH; ++c)
+                {
+                    float xv[8], gv[8], gm[8];
+                    unpack8(*reinterpret_cast<const uint4*>(xs + (c * 32 + lane) * 16), xv);
+                    unpack8(*reinterpret_cast<const uint4*>(gs + (c * 32 + lane) * 16), gv);
+                    gain(c, gm);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                    {
+                        ss += xv[j] * xv[j];
+                        wsum += (gv[j] * gm[j]) * xv[j];
+                    }
+                }
+                ss = warp_sum(ss);
+                wsum = warp_sum(wsum);
+                const float inv = 1.0f / sqrtf(ss / static_cast<float>(R::N) + eps);
+                const float coupling = wsum * inv * inv * inv / static_cast<float>(R::N);
+#pragma unroll
+                for (int c = 0; c < CH; ++c)
+                {
+                    float xv[8], gv[8], res[8], gm[8];
+                    unpack8(*reinterpret_cast<const uint4*>(xs + (c * 32 + lane) * 16), xv);
+                    unpack8(*reinterpret_cast<const uint4*>(gs + (c * 32 + lane) * 16), gv);
+                    gain(c, gm);
+                    if constexpr (NIN == 3)
+                    {
+                        unpack8(*reinterpret_cast<const uint4*>(xs + 2 * R::ROW + (c * 32 + lane) * 16), res);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                    {
+                        float d = (gv[j] * gm[j]) * inv - xv[j] * coupling;
+                        if constexpr (NIN == 3)
+                        {
+                            d = res[j] + d;
+                        }
+                        acc[c][j] += gv[j] * (xv[j] * inv);
+                        xv[j] = d;
+                    }
+                    store16(dx + row * lddx + (c * 32 + lane) * 8, xv);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+    }
+    if (partials != nullptr)
+    {
+        // every stage has been consumed and no copy is in flight: reuse the ring for the sums
+        __syncthreads();
+        float* part = reinterpret_cast<float*>(ring);   // [kRows][N]
+        if (warp > 0)
+        {
+#pragma unroll
+            for (int c = 0; c < CH; ++c)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) part[(warp - 1) * R::N + (c * 32 + lane) * 8 + j] = acc[c][j];
+        }
+        __syncthreads();
+        for (int col = threadIdx.x; col < R::N; col += blockDim.x)
+        {
+            float s = 0.0f;
+#pragma unroll
+            for (int k = 0; k < kRows; ++k) s += part[k * R::N + col];
+            partials[static_cast<size_t>(blockIdx.x) * R::N + col] = s;
+        }
+    }
+}
+
+bool rows_aligned(const void* p, int64_t ld) { return aligned16(p) && ld % 8 == 0; }
+
+template <int CH>
+int launch_fwd(const bf16* x, int64_t ldx, const bf16* gamma, bf16* y, int64_t ldy, int64_t rows,
+               float eps, cudaStream_t s)
+{
+    using R = Ring<CH, 1>;
+    static int configured = -1;
+    int device = 0;
+    cudaGetDevice(&device);
+    if (configured != device)
+    {
+        cudaFuncSetAttribute(rms_fwd_stream_kernel<CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, R::SMEM);
+        configured = device;
+    }
+    const int64_t chunks = (rows + kRows - 1) / kRows;
+    const unsigned grid = static_cast<unsigned>(chunks < sm_count() ? chunks : sm_count());
+    rms_fwd_stream_kernel<CH><<<grid, kThreadsStream, R::SMEM, s>>>(x, ldx, gamma, y, ldy, rows, eps,
+                                                                    device_status_ptr());
+    count_launch();
+    return check_launch("veda_rmsnorm_fwd (streaming)");
+}
+
+template <int CH, int NIN>
+int launch_bwd(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* dy, int64_t lddy,
+               const bf16* dresid, int64_t ldr, bf16* dx, int64_t lddx, float* partials, int max_blocks,
+               int64_t rows, float eps, cudaStream_t s, int* blocks)
+{
+    using R = Ring<CH, NIN>;
+    static int configured = -1;
+    int device = 0;
+    cudaGetDevice(&device);
+    if (configured != device)
+    {
+        cudaFuncSetAttribute(rms_bwd_stream_kernel<CH, NIN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             R::SMEM);
+        configured = device;
+    }
+    const int64_t chunks = (rows + kRows - 1) / kRows;
+    int64_t g = chunks < sm_count() ? chunks : sm_count();
+    if (g > max_blocks) g = max_blocks;
+    if (g < 1) g = 1;
+    *blocks = static_cast<int>(g);
+    rms_bwd_stream_kernel<CH, NIN><<<static_cast<unsigned>(g), kThreadsStream, R::SMEM, s>>>(
+        x, ldx, gamma, dy, lddy, dresid, ldr, dx, lddx, partials, rows, eps, device_status_ptr());
+    count_launch();
+    return check_launch("veda_rmsnorm_bwd (streaming)");
+}
+
+} // namespace
+
+int rms_fwd_stream(const bf16* x, int64_t ldx, const bf16* gamma, bf16* y, int64_t ldy,
+                   int64_t rows, int64_t n, float eps, cudaStream_t s)
+{
+    if (!rows_aligned(x, ldx) || !rows_aligned(y, ldy) || (gamma != nullptr && !aligned16(gamma)))
+    {
+        return -1;
+    }
+    switch (n)
+    {
+    case 256: return launch_fwd<1>(x, ldx, gamma, y, ldy, rows, eps, s);
+    case 512: return launch_fwd<2>(x, ldx, gamma, y, ldy, rows, eps, s);
+    case 1024: return launch_fwd<4>(x, ldx, gamma, y, ldy, rows, eps, s);
+    case 2048: return launch_fwd<8>(x, ldx, gamma, y, ldy, rows, eps, s);
+    default: return -1;
+    }
+}
+
+int rms_bwd_stream(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* dy, int64_t lddy,
+                   const bf16* dresid, int64_t ldr, bf16* dx, int64_t lddx, float* partials,
+                   int max_blocks, int64_t rows, int64_t n, float eps, cudaStream_t s, int* blocks)
+{
+    if (!rows_aligned(x, ldx) || !rows_aligned(dy, lddy) || !rows_aligned(dx, lddx) ||
+        (dresid != nullptr && !rows_aligned(dresid, ldr)) || (gamma != nullptr && !aligned16(gamma)))
+    {
+        return -1;
+    }
+#define VEDA_BWD(CH)                                                                              \
+    return dresid != nullptr                                                                      \
+               ? launch_bwd<CH, 3>(x, ldx, gamma, dy, lddy, dresid, ldr, dx, lddx, partials,       \
+                                   max_blocks, rows, eps, s, blocks)                              \
+               : launch_bwd<CH, 2>(x, ldx, gamma, dy, lddy, dresid, ldr, dx, lddx, partials,       \
+                                   max_blocks, rows, eps, s, blocks)
+    switch (n)
+    {
+    case 256: VEDA_BWD(1);
+    case 512: VEDA_BWD(2);
+    case 1024: VEDA_BWD(4);
+    default: return -1;   // 2048: the 64 per-lane gain sums would not fit in registers
+
+    }
+#undef VEDA_BWD
+}
+
+} // namespace veda::cuda

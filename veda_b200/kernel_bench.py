@@ -13,7 +13,9 @@
         16 query / 8 KV heads of 128, FFN 3072, vocab 151936 for the cross-entropy): RMSNorm
         forward / backward (with residual gradient and dgamma), QK-norm+RoPE forward / backward,
         SwiGLU forward / backward, cross-entropy; GB/s from the algorithmic bytes (each tensor
-        read or written once). --kernels NAME... runs a subset (names as printed).
+        read or written once). --kernels NAME... runs a subset (names as printed). Each kernel is
+        timed as a CUDA graph of 24 calls over 6 rotating input sets (so launch latency is not
+        counted and every call reads HBM).
 Prints one JSON line per measurement.
 """
 from __future__ import annotations
@@ -38,13 +40,16 @@ def _peaks():
 
 
 def _time(fn, reps, stream, flush=None):
+    """Mean CUDA-event time of fn over reps. With `flush` (a device tensor larger than L2), each
+    rep first reads it (a sum), so L2 holds clean lines of no use to fn: fn's reads come from
+    HBM without also paying write-backs of dirty lines a writing flush would leave behind."""
     import torch
     fn()
     torch.cuda.synchronize()
     total = 0.0
     for _ in range(reps):
         if flush is not None:
-            flush.zero_()
+            flush.sum()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         fn()
@@ -60,7 +65,7 @@ def mm_sweep(reps):
     L = V.lib()
     s = torch.cuda.current_stream()
     peak, _, kind = _peaks()
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")   # > L2, cleared per rep
+    flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")   # 256 MB > L2, read per rep
     g = torch.Generator(device="cuda").manual_seed(1)
     for (M, K, N) in SWEEP:
         x = (torch.randn(M, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
@@ -141,79 +146,124 @@ def attn_bwd(seqs, reps):
 
 
 def bandwidth_kernels(tokens, reps, only=None):
+    """Each kernel is captured in a CUDA graph of 24 calls rotating over 6 input sets (together far
+    larger than L2, so every call reads HBM), replayed `reps` times; per-call time = graph time /
+    24. Timing a single call between two events would measure the host's launch latency for
+    these ~10-50 us kernels. The cross-entropy (~1.4 ms a call) is timed directly."""
     import torch
     import veda_b200 as V
     L = V.lib()
-    s = torch.cuda.current_stream()
+    s = torch.cuda.Stream()     # graphs are captured on a non-default stream
+    torch.cuda.set_stream(s)
     _, hbm, kind = _peaks()
     g = torch.Generator(device="cuda").manual_seed(3)
     T, D, H, Hk, F, Vv = 2048, 1024, 16, 8, 3072, 151936
     bf = torch.bfloat16
+    B2 = 2
+    SETS, CALLS = 6, 24
     rn = lambda *shape: torch.randn(*shape, device="cuda", generator=g).to(bf)  # noqa: E731
-    x, dy, dr = rn(tokens, D), rn(tokens, D), rn(tokens, D)
-    gam = rn(D)
-    y, dx = torch.empty_like(x), torch.empty_like(x)
-    dg = torch.zeros(D, dtype=torch.float32, device="cuda")
-    ws = torch.empty(L.veda_rmsnorm_bwd_workspace(tokens, D), dtype=torch.uint8, device="cuda")
-    qkv = rn(tokens, (H + 2 * Hk) * 128)
-    dqkv = rn(tokens, (H + 2 * Hk) * 128)
-    qo = torch.empty(tokens, H * 128, dtype=bf, device="cuda")
-    gq = rn(128)
+    st = s.cuda_stream
+    gam, gq = rn(D), rn(128)
     cos = torch.randn(T, 128, device="cuda", generator=g)
     sin = torch.randn(T, 128, device="cuda", generator=g)
+    dg = torch.zeros(D, dtype=torch.float32, device="cuda")
     dgq = torch.zeros(128, dtype=torch.float32, device="cuda")
-    wsq = torch.empty(L.veda_qknorm_rope_bwd_workspace(tokens, H, 128), dtype=torch.uint8, device="cuda")
-    gu = rn(tokens, 2 * F)
-    hh = torch.empty(tokens, F, dtype=bf, device="cuda")
-    dh = rn(tokens, F)
-    dgu = torch.empty_like(gu)
-    want_ce = only is None or "cross_entropy" in only
-    logits = rn(tokens, Vv) if want_ce else None
-    tgt = torch.randint(0, Vv, (tokens,), device="cuda", generator=g)
-    rl = torch.empty(tokens, dtype=torch.float32, device="cuda")
-    dl = torch.empty_like(logits) if want_ce else None
-    st = s.cuda_stream
-    B2 = 2
+    ws = torch.empty(L.veda_rmsnorm_bwd_workspace(tokens, D), dtype=torch.uint8, device="cuda")
+    wsq = torch.empty(L.veda_qknorm_rope_bwd_workspace(tokens, H, 128), dtype=torch.uint8,
+                      device="cuda")
+
+    def want(name):
+        return only is None or name in only
+
+    sets = []
+    for _ in range(SETS):
+        d = {}
+        if want("rmsnorm_fwd") or want("rmsnorm_bwd"):
+            d.update(x=rn(tokens, D), dy=rn(tokens, D), dr=rn(tokens, D),
+                     y=torch.empty(tokens, D, dtype=bf, device="cuda"),
+                     dx=torch.empty(tokens, D, dtype=bf, device="cuda"))
+        if want("qknorm_rope_fwd_q") or want("qknorm_rope_bwd_q"):
+            d.update(qkv=rn(tokens, (H + 2 * Hk) * 128), dqkv=rn(tokens, H * 128),
+                     qo=torch.empty(tokens, H * 128, dtype=bf, device="cuda"))
+        if want("swiglu_fwd") or want("swiglu_bwd"):
+            d.update(gu=rn(tokens, 2 * F), dh=rn(tokens, F),
+                     hh=torch.empty(tokens, F, dtype=bf, device="cuda"),
+                     dgu=torch.empty(tokens, 2 * F, dtype=bf, device="cuda"))
+        sets.append(d)
+
+    def rms_fwd(d):
+        V.check(L.veda_rmsnorm_fwd(d["x"].data_ptr(), D, gam.data_ptr(), d["y"].data_ptr(), D, tokens, D,
+                                   1e-6, V.BF16, st))
+
+    def rms_bwd(d):
+        V.check(L.veda_rmsnorm_bwd(d["x"].data_ptr(), D, gam.data_ptr(), d["dy"].data_ptr(), D,
+                                   d["dr"].data_ptr(), D, d["dx"].data_ptr(), D, dg.data_ptr(),
+                                   ws.data_ptr(), ws.numel(), tokens, D, 1e-6, V.BF16, st))
+
+    def qk_fwd(d):
+        q = d["qkv"]
+        V.check(L.veda_qknorm_rope_fwd(q.data_ptr(), q.shape[1], gq.data_ptr(), cos.data_ptr(),
+                                       sin.data_ptr(), d["qo"].data_ptr(), H * 128, tokens, H, T, 128,
+                                       1e-6, V.BF16, st))
+
+    def qk_bwd(d):
+        q = d["qkv"]
+        V.check(L.veda_qknorm_rope_bwd(q.data_ptr(), q.shape[1], gq.data_ptr(), cos.data_ptr(),
+                                       sin.data_ptr(), d["dqkv"].data_ptr(), H * 128, d["qo"].data_ptr(),
+                                       H * 128, dgq.data_ptr(), wsq.data_ptr(), wsq.numel(), tokens, H, T,
+                                       128, 1e-6, V.BF16, st))
+
+    def sw_fwd(d):
+        gu = d["gu"]
+        V.check(L.veda_swiglu_fwd(gu.data_ptr(), 2 * F, gu.data_ptr() + F * B2, 2 * F, d["hh"].data_ptr(),
+                                  F, tokens, F, V.BF16, st))
+
+    def sw_bwd(d):
+        gu, dgu = d["gu"], d["dgu"]
+        V.check(L.veda_swiglu_bwd(gu.data_ptr(), 2 * F, gu.data_ptr() + F * B2, 2 * F, d["dh"].data_ptr(), F,
+                                  dgu.data_ptr(), 2 * F, dgu.data_ptr() + F * B2, 2 * F, tokens, F, V.BF16,
+                                  st))
+
     cases = {
-        "rmsnorm_fwd": (lambda: V.check(L.veda_rmsnorm_fwd(x.data_ptr(), D, gam.data_ptr(), y.data_ptr(), D,
-                                                           tokens, D, 1e-6, V.BF16, st)),
-                        2 * tokens * D * B2),
-        "rmsnorm_bwd": (lambda: V.check(L.veda_rmsnorm_bwd(x.data_ptr(), D, gam.data_ptr(), dy.data_ptr(), D,
-                                                           dr.data_ptr(), D, dx.data_ptr(), D, dg.data_ptr(),
-                                                           ws.data_ptr(), ws.numel(), tokens, D, 1e-6, V.BF16,
-                                                           st)),
-                        4 * tokens * D * B2),
-        "qknorm_rope_fwd_q": (lambda: V.check(L.veda_qknorm_rope_fwd(qkv.data_ptr(), qkv.shape[1], gq.data_ptr(),
-                                                                     cos.data_ptr(), sin.data_ptr(), qo.data_ptr(),
-                                                                     H * 128, tokens, H, T, 128, 1e-6, V.BF16,
-                                                                     st)),
-                              2 * tokens * H * 128 * B2),
-        "qknorm_rope_bwd_q": (lambda: V.check(L.veda_qknorm_rope_bwd(qkv.data_ptr(), qkv.shape[1], gq.data_ptr(),
-                                                                     cos.data_ptr(), sin.data_ptr(),
-                                                                     dqkv.data_ptr(), dqkv.shape[1],
-                                                                     qo.data_ptr(), H * 128, dgq.data_ptr(),
-                                                                     wsq.data_ptr(), wsq.numel(), tokens, H, T,
-                                                                     128, 1e-6, V.BF16, st)),
-                              3 * tokens * H * 128 * B2),
-        "swiglu_fwd": (lambda: V.check(L.veda_swiglu_fwd(gu.data_ptr(), 2 * F, gu.data_ptr() + F * B2, 2 * F,
-                                                         hh.data_ptr(), F, tokens, F, V.BF16, st)),
-                       3 * tokens * F * B2),
-        "swiglu_bwd": (lambda: V.check(L.veda_swiglu_bwd(gu.data_ptr(), 2 * F, gu.data_ptr() + F * B2, 2 * F,
-                                                         dh.data_ptr(), F, dgu.data_ptr(), 2 * F,
-                                                         dgu.data_ptr() + F * B2, 2 * F, tokens, F, V.BF16,
-                                                         st)),
-                       5 * tokens * F * B2),
-        "cross_entropy": (lambda: V.check(L.veda_cross_entropy(logits.data_ptr(), Vv, tgt.data_ptr(), rl.data_ptr(),
-                                                               dl.data_ptr(), Vv, tokens, Vv, 1.0 / tokens, 0,
-                                                               V.BF16, st)),
-                          2 * tokens * Vv * B2),
+        "rmsnorm_fwd": (rms_fwd, 2 * tokens * D * B2),
+        "rmsnorm_bwd": (rms_bwd, 4 * tokens * D * B2),
+        "qknorm_rope_fwd_q": (qk_fwd, 2 * tokens * H * 128 * B2),
+        "qknorm_rope_bwd_q": (qk_bwd, 3 * tokens * H * 128 * B2),
+        "swiglu_fwd": (sw_fwd, 3 * tokens * F * B2),
+        "swiglu_bwd": (sw_bwd, 5 * tokens * F * B2),
     }
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     for name, (fn, nbytes) in cases.items():
-        if only is not None and name not in only:
+        if not want(name):
             continue
-        ms = _time(fn, reps, s, flush)
+        for d in sets:          # warm-up outside the capture (first-call set-up, attributes)
+            fn(d)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for k in range(CALLS):
+                fn(sets[k % SETS])
+        graph.replay()
+        torch.cuda.synchronize()
+        ms = _time(graph.replay, reps, s) / CALLS
         print(json.dumps({"bench": "bw", "kernel": name, "tokens": tokens, "ms": ms,
+                          "gbs": nbytes / (ms / 1e3) / 1e9, "peak_gbs": hbm, "peak_kind": kind,
+                          "frac": nbytes / (ms / 1e3) / 1e9 / hbm}), flush=True)
+        del graph
+    del sets
+    torch.cuda.empty_cache()
+    if want("cross_entropy"):
+        logits = rn(tokens, Vv)
+        tgt = torch.randint(0, Vv, (tokens,), device="cuda", generator=g)
+        rl = torch.empty(tokens, dtype=torch.float32, device="cuda")
+        dl = torch.empty_like(logits)
+        flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")   # 256 MB > L2, read per rep
+
+        def ce():
+            V.check(L.veda_cross_entropy(logits.data_ptr(), Vv, tgt.data_ptr(), rl.data_ptr(), dl.data_ptr(),
+                                         Vv, tokens, Vv, 1.0 / tokens, 0, V.BF16, st))
+        ms = _time(ce, reps, s, flush)
+        nbytes = 2 * tokens * Vv * B2
+        print(json.dumps({"bench": "bw", "kernel": "cross_entropy", "tokens": tokens, "ms": ms,
                           "gbs": nbytes / (ms / 1e3) / 1e9, "peak_gbs": hbm, "peak_kind": kind,
                           "frac": nbytes / (ms / 1e3) / 1e9 / hbm}), flush=True)
 
