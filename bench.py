@@ -278,13 +278,9 @@ def run_veda(args):
                    "tflops": (v[1] / (v[0] / 1000.0) / 1e12) if v[1] and v[0] else None,
                    "gbs": (v[2] / (v[0] / 1000.0) / 1e9) if v[2] and v[0] else None}
                for k, v in sorted(prof.items())}
-    traffic = None
-    tpath = ROOT / "profiles" / "gemm_traffic.json"
-    if tpath.exists():
-        try:
-            traffic = json.loads(tpath.read_text()).get(args.workload)
-        except Exception:
-            traffic = None
+    # DRAM bytes (read + write) per GEMM launch, averaged over the 339 GEMM launches of one step,
+    # from one ncu capture: profiles/gemm_dram_traffic_qwen3_0.6b_b4t2048.md
+    traffic = GEMM_DRAM_BYTES_PER_LAUNCH.get(args.workload)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -325,6 +321,7 @@ def run_veda(args):
 
 
 _JSON_OUT = None
+GEMM_DRAM_BYTES_PER_LAUNCH = {"qwen3-0.6b": 116.57e6}
 
 
 def emit(line: dict):

@@ -2,8 +2,8 @@
 
     python -m veda_b200.kernel_bench mm-sweep [--reps 10]
         the matmul-backward sweep: for X[M,K], W[K,N], dY[M,N] (bf16, ~N(0,1)/sqrt(K), seed 1)
-        time dX = dY W^T and dW = X^T dY (fp32 out) for (M,K,N) in the five sweep shapes;
-        4*M*K*N FLOP per shape.
+        time dX = dY W^T and dW = X^T dY (fp32 out) for (M,K,N) in the five sweep shapes, the
+        pair as one CUDA graph replayed after an L2-clearing read; 4*M*K*N FLOP per shape.
     python -m veda_b200.kernel_bench attn-bwd [--seq 1024 4096] [--reps 5]
         causal GQA attention backward, B 8, H 16, Hkv 8, Dh 128, bf16, seed 2; 5*B*H*T^2*Dh FLOP.
     python -m veda_b200.kernel_bench gemm --op nt --m 8192 --n 151936 --k 1024 [--reps 3]
@@ -60,10 +60,13 @@ def _time(fn, reps, stream, flush=None):
 
 
 def mm_sweep(reps):
+    """dX and dW of each shape as one CUDA graph (so the host's launch latency is not timed),
+    replayed after an L2-clearing read; parity spot-checked against fp64."""
     import torch
     import veda_b200 as V
     L = V.lib()
-    s = torch.cuda.current_stream()
+    s = torch.cuda.Stream()     # graphs are captured on a non-default stream
+    torch.cuda.set_stream(s)
     peak, _, kind = _peaks()
     flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")   # 256 MB > L2, read per rep
     g = torch.Generator(device="cuda").manual_seed(1)
@@ -80,7 +83,13 @@ def mm_sweep(reps):
                                    V.BF16, V.F32, 1.0, 0.0, s.cuda_stream))
             V.check(L.veda_gemm_tn(K, N, M, x.data_ptr(), K, dy.data_ptr(), N, dw.data_ptr(), N,
                                    V.BF16, V.F32, 1.0, 0.0, s.cuda_stream))
-        ms = _time(run, reps, s, flush)
+        run()                   # first calls (attributes, cluster occupancy) outside the capture
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            run()
+        ms = _time(graph.replay, reps, s, flush)
+        del graph
         flops = 4.0 * M * K * N
         tf = flops / (ms / 1e3) / 1e12
         print(json.dumps({"bench": "mm-sweep", "M": M, "K": K, "N": N, "ms": ms,
