@@ -5,6 +5,9 @@
 
 #include <cuda_runtime.h>
 
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <vector>
@@ -23,6 +26,32 @@ struct Record
 
 std::mutex g_mu;
 bool g_enabled = false;
+
+// VEDA_HOST_PROFILE=1: every scope also sums the host (wall-clock) time spent inside it, and the
+// totals per name are printed to stderr when the process exits — where the host's issue time
+// goes, independent of the device timers.
+struct HostTotals
+{
+    std::map<std::string, std::pair<double, uint64_t>> by_name;   // ms, count
+    ~HostTotals()
+    {
+        if (by_name.empty())
+        {
+            return;
+        }
+        std::fprintf(stderr, "veda host profile (ms total, scopes):\n");
+        for (const auto& [name, v] : by_name)
+        {
+            std::fprintf(stderr, "  %-20s %12.3f %10llu\n", name.c_str(), v.first,
+                         static_cast<unsigned long long>(v.second));
+        }
+    }
+};
+HostTotals g_host;
+const bool g_host_enabled = [] {
+    const char* v = std::getenv("VEDA_HOST_PROFILE");
+    return v != nullptr && v[0] == '1';
+}();
 std::vector<Record> g_records;     // recorded since the last collect
 std::vector<cudaEvent_t> g_free;   // pooled events
 std::map<std::string, Totals> g_totals;
@@ -54,6 +83,13 @@ bool enabled() { return g_enabled; }
 
 Scope::Scope(const char* name, double flops, double bytes)
 {
+    if (g_host_enabled)
+    {
+        name_ = name;
+        host_start_ = std::chrono::duration<double, std::milli>(
+                          std::chrono::steady_clock::now().time_since_epoch())
+                          .count();
+    }
     if (!g_enabled)
     {
         return;
@@ -67,6 +103,16 @@ Scope::Scope(const char* name, double flops, double bytes)
 
 Scope::~Scope()
 {
+    if (name_ != nullptr)
+    {
+        const double now = std::chrono::duration<double, std::milli>(
+                               std::chrono::steady_clock::now().time_since_epoch())
+                               .count();
+        std::lock_guard<std::mutex> lock(g_mu);
+        auto& v = g_host.by_name[name_];
+        v.first += now - host_start_;
+        v.second += 1;
+    }
     if (slot_ < 0)
     {
         return;
@@ -75,6 +121,39 @@ Scope::~Scope()
     if (slot_ < static_cast<int>(g_records.size()))
     {
         cudaEventRecord(g_records[slot_].stop, reinterpret_cast<cudaStream_t>(current_stream()));
+    }
+}
+
+namespace
+{
+double now_ms()
+{
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+void add_host(const char* name, double ms)
+{
+    std::lock_guard<std::mutex> lock(g_mu);
+    auto& v = g_host.by_name[name];
+    v.first += ms;
+    v.second += 1;
+}
+} // namespace
+
+HostScope::HostScope(const char* name)
+{
+    if (g_host_enabled)
+    {
+        name_ = name;
+        start_ = now_ms();
+    }
+}
+
+HostScope::~HostScope()
+{
+    if (name_ != nullptr)
+    {
+        add_host(name_, now_ms() - start_);
     }
 }
 

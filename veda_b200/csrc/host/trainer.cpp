@@ -215,8 +215,15 @@ int Trainer::world() const noexcept { return dp_ ? dp_->world() : 1; }
 
 void Trainer::step(const Tensor& ids, const Tensor& targets)
 {
-    model_->zero_grad();
-    Variable logits = model_->forward_device(ids, batch_, length_);
+    profile::HostScope whole("host:step");
+    {
+        profile::HostScope scope("host:zero_grad");
+        model_->zero_grad();
+    }
+    Variable logits = [&] {
+        profile::HostScope scope("host:forward");
+        return model_->forward_device(ids, batch_, length_);
+    }();
     Variable loss = autograd::cross_entropy_device(logits, targets);
     autograd::BackwardOptions options;
     options.retain_intermediate_grads = false;
@@ -225,7 +232,10 @@ void Trainer::step(const Tensor& ids, const Tensor& targets)
         dp_->begin_step();
         options.on_leaf_ready = [this](autograd::Node* node) { dp_->leaf_ready(node); };
     }
-    loss.backward(options);
+    {
+        profile::HostScope scope("host:backward");
+        loss.backward(options);
+    }
     if (dp_)
     {
         dp_->finish();
