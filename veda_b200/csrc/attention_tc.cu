@@ -139,9 +139,9 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     const int nq = (p.T + kTq - 1) / kTq;
     const int nkt = (p.T + kTk - 1) / kTk;
     const int npairs = (nq + 1) / 2;
-    const int qt0 = 2 * (npairs - 1 - static_cast<int>(blockIdx.x));   // longest rows first
+    const int qt0 = 2 * (npairs - 1 - static_cast<int>(blockIdx.y));   // longest rows first
     const bool has_b = qt0 + 1 < nq;
-    const int bh = blockIdx.y;
+    const int bh = blockIdx.x;
     const int b = bh / p.H, h = bh % p.H;
     const int kvh = h / (p.H / p.Hkv);
     const int n_a = p.causal ? qt0 + 1 : nkt;
@@ -506,8 +506,8 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kt = static_cast<int>(blockIdx.x);
-    const int bk = blockIdx.y;
+    const int kt = static_cast<int>(blockIdx.y);   // launch order: all heads' key tile 0 (the
+    const int bk = blockIdx.x;                      // longest under the causal mask) first
     const int b = bk / p.Hkv, kvh = bk % p.Hkv;
     const int rep = p.H / p.Hkv;
     const int nq = (p.T + kBq - 1) / kBq;
@@ -799,8 +799,8 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tds, const __grid_constant
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nq = (p.T + 127) / 128;
-    const int qt = nq - 1 - static_cast<int>(blockIdx.x);
-    const int bh = blockIdx.y;
+    const int qt = nq - 1 - static_cast<int>(blockIdx.y);   // longest rows first
+    const int bh = blockIdx.x;
     const int b = bh / p.H, h = bh % p.H;
     const int kvh = h / (p.H / p.Hkv);
     const int nk = p.causal ? qt + 1 : nq;
@@ -997,7 +997,7 @@ int attn_tc_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     FwdParams p{static_cast<bf16*>(o), lse, ldo, static_cast<int>(T), static_cast<int>(H),
                 static_cast<int>(Hkv), scale * kLog2e, causal, device_status_ptr()};
     const int64_t pairs = ((T + kTq - 1) / kTq + 1) / 2;
-    const dim3 grid(static_cast<unsigned>(pairs), static_cast<unsigned>(B * H));
+    const dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>(pairs));
     attn_fwd_tc_kernel<<<grid, kFwdThreads, kFwdSmem, s>>>(mq, mk, mv, p);
     count_launch();
     return check_launch("veda_attention_fwd (tcgen05)");
@@ -1051,11 +1051,11 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     BwdParams p{nlse2, dvec, static_cast<bf16*>(dk), static_cast<bf16*>(dv), ds, lddk, lddv,
                 static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
                 scale * kLog2e, causal, device_status_ptr()};
-    const dim3 grid(static_cast<unsigned>((T + 127) / 128), static_cast<unsigned>(B * Hkv));
+    const dim3 grid(static_cast<unsigned>(B * Hkv), static_cast<unsigned>((T + 127) / 128));
     attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, p);
     DqParams pq{static_cast<bf16*>(dq), lddq, static_cast<int>(T), static_cast<int>(H),
                 static_cast<int>(Hkv), scale, causal, device_status_ptr()};
-    const dim3 gq(static_cast<unsigned>((T + 127) / 128), static_cast<unsigned>(B * H));
+    const dim3 gq(static_cast<unsigned>(B * H), static_cast<unsigned>((T + 127) / 128));
     attn_dq_tc_kernel<<<gq, 192, kDqSmem, s>>>(mds, mk, pq);
     count_launch(3);
     return check_launch("veda_attention_bwd (tcgen05)");
