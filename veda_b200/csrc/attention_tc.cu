@@ -445,10 +445,13 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
 constexpr int kBq = 64;                      // queries per backward iteration
 constexpr int kQTileBytes = kBq * 128 * 2;   // [64 rows x 128 dims] = two 8 KB halves
 constexpr int kQHalf = kQTileBytes / 2;
-constexpr int kQStages = 4;
-constexpr int kBwdThreads = 320;
-// alignment slack | K, V | (Q, dO)[4] | (-LSE log2e, D)[4] | barriers
-constexpr int kBwdSmem = 1024 + 2 * kTileBytes + 2 * kQStages * kQTileBytes + kQStages * 2 * kBq * 4 + 256;
+constexpr int kQStages = 3;
+constexpr int kComputeWarps = 16;            // four per TMEM lane quarter, 16 query columns each
+constexpr int kBwdThreads = 64 + 32 * kComputeWarps;
+constexpr int kDsTileBytes = 128 * kBq * 2;  // dS^T [128 keys x 64 queries] staging for the store
+// alignment slack | K, V | (Q, dO)[3] | dS^T staging [2] | (-LSE log2e, D)[3] | barriers
+constexpr int kBwdSmem = 1024 + 2 * kTileBytes + 2 * kQStages * kQTileBytes + 2 * kDsTileBytes +
+                         kQStages * 2 * kBq * 4 + 256;
 
 struct BwdParams
 {
@@ -469,6 +472,11 @@ __device__ __forceinline__ void load_qtile_3d(uint8_t* dst, const CUtensorMap* m
     tma_load_3d(dst + kQHalf, map, bar, col + 64, row, batch);
 }
 
+__device__ __forceinline__ void named_sync(int id, int count)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b)
 {
     const __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
@@ -485,7 +493,7 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b)
 __global__ void __launch_bounds__(kBwdThreads, 1)
 attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                   const BwdParams p)
+                   const __grid_constant__ CUtensorMap tds, const BwdParams p)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -494,7 +502,8 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     uint8_t* sv = sk + kTileBytes;
     uint8_t* sq = sv + kTileBytes;                          // [stages]
     uint8_t* sdo = sq + kQStages * kQTileBytes;             // [stages]
-    float* srow = reinterpret_cast<float*>(sdo + kQStages * kQTileBytes);   // [stages][2][64]
+    uint8_t* sdst = sdo + kQStages * kQTileBytes;            // [2] dS^T staging
+    float* srow = reinterpret_cast<float*>(sdst + 2 * kDsTileBytes);   // [stages][2][64]
     uint64_t* bars = reinterpret_cast<uint64_t*>(srow + kQStages * 2 * kBq);
     uint64_t* kv_full = bars + 0;
     uint64_t* qd_full = bars + 1;                  // [stages]
@@ -527,7 +536,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
         for (int i = 0; i < 2; ++i)
         {
             mbar_init(&sp_full[i], 1);
-            mbar_init(&ds_full[i], 8);
+            mbar_init(&ds_full[i], kComputeWarps);
         }
         mbar_init(done, 1);
         mbar_fence_init();
@@ -541,7 +550,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     fence_after();
     const uint32_t tmem = *tmem_slot;
     // TMEM columns: S^T[2] (64 each) | dP^T[2] (64 each) | dV (128) | dK (128). P^T and dS^T
-    // (bf16 pairs) overwrite columns [32 g, 32 g + 16) of their buffer, g = the query half.
+    // (bf16 pairs) overwrite columns [16 g, 16 g + 8) of their buffer, g = the 16-query group.
     constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 384;
 
     if (warp == 0 && lane == 0)
@@ -585,7 +594,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
             for (int ks = 0; ks < kBq / 16; ++ks)
             {
                 const uint32_t acc = (i > 0 || ks > 0) ? 1u : 0u;
-                const uint32_t col = s * 64 + (ks >> 1) * 32 + (ks & 1) * 8;
+                const uint32_t col = s * 64 + ks * 16;   // queries [16 ks, 16 ks + 16), packed
                 mma_ts(tmem + kDV, tmem + kST + col, mnmajor_desc(do_base, ks, kQHalf), idesc_kv, acc);
                 mma_ts(tmem + kDK, tmem + kDPT + col, mnmajor_desc(q_base, ks, kQHalf), idesc_kv, acc);
             }
@@ -624,40 +633,41 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     else if (warp >= 2)
     {
         const int quarter = warp & 3;
-        const int half = (warp - 2) >> 2;       // query columns [32 half, 32 half + 32)
+        const int grp = (warp - 2) >> 2;        // query columns [16 grp, 16 grp + 16)
         const int r = quarter * 32 + lane;      // key row
         const int key = kt * 128 + r;
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
         const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
         const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
+        const bool issuer = warp == 2 && lane == 0;   // issues the dS^T tile stores
         for (int it = 0; it < iters; ++it)
         {
             const int st = it & 1, sq_i = it % kQStages;
             const int h = kvh * rep + it / per_head;
             const int q0 = (qi0 + it % per_head) * kBq;
-            const int qc = q0 + half * 32;      // first query of this thread's columns
+            const int qc = q0 + grp * 16;       // first query of this thread's columns
             mbar_wait(&sp_full[st], (it >> 1) & 1, p.status, abort);
             // the stage's -LSE log2e / D rows arrived with its Q / dO (phase already complete)
             mbar_wait(&qd_full[sq_i], (it / kQStages) & 1, p.status, abort);
             fence_after();
-            uint32_t sraw[32], draw[32];
-            const uint32_t col = st * 64 + half * 32;
-            tmem_ld32_async(tmem + lane_base + kST + col, sraw);
-            tmem_ld32_async(tmem + lane_base + kDPT + col, draw);
+            uint32_t sraw[16], draw[16];
+            const uint32_t col = st * 64 + grp * 16;
+            tmem_ld16_async(tmem + lane_base + kST + col, sraw);
+            tmem_ld16_async(tmem + lane_base + kDPT + col, draw);
             tmem_wait_ld();
             reg_fence(sraw);
             reg_fence(draw);
-            const float* nl = srow + sq_i * 2 * kBq + half * 32;
+            const float* nl = srow + sq_i * 2 * kBq + grp * 16;
             const float* dd = nl + kBq;
             // visible columns c: lo <= c < hi (queries before T and, causal, not before this key)
-            const int hi = qc + 32 > p.T ? (p.T - qc > 0 ? p.T - qc : 0) : 32;
+            const int hi = qc + 16 > p.T ? (p.T - qc > 0 ? p.T - qc : 0) : 16;
             const bool causal_tile = p.causal && qc < kt * 128 + 127;   // some key > query here
             const int lo = causal_tile ? (key - qc > 0 ? key - qc : 0) : 0;
-            uint32_t pk[16], dk[16];
-            if (!causal_tile && hi == 32)
+            uint32_t pk[8], dk[8];
+            if (!causal_tile && hi == 16)
             {
 #pragma unroll
-                for (int c = 0; c < 32; c += 4)
+                for (int c = 0; c < 16; c += 4)
                 {
                     const float4 nl4 = *reinterpret_cast<const float4*>(nl + c);
                     const float4 d4 = *reinterpret_cast<const float4*>(dd + c);
@@ -683,7 +693,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
             else
             {
 #pragma unroll
-                for (int c = 0; c < 32; c += 2)
+                for (int c = 0; c < 16; c += 2)
                 {
                     const float2 nl2 = *reinterpret_cast<const float2*>(nl + c);
                     const float2 d2 = *reinterpret_cast<const float2*>(dd + c);
@@ -705,35 +715,42 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
                     dk[c >> 1] = pack2(d0, d1);
                 }
             }
-            tmem_st16_async(tmem + lane_base + kST + col, pk);
-            tmem_st16_async(tmem + lane_base + kDPT + col, dk);
-            if (key < p.T)
-            {
-                bf16* drow = p.ds + ((static_cast<int64_t>(b) * p.H + h) * p.T + key) * p.T + qc;
-#pragma unroll
-                for (int c8 = 0; c8 < 4; ++c8)
-                {
-                    if (qc + c8 * 8 < p.T)   // T % 8 == 0: whole 8-query chunks
-                    {
-                        *reinterpret_cast<uint4*>(drow + c8 * 8) =
-                            make_uint4(dk[c8 * 4], dk[c8 * 4 + 1], dk[c8 * 4 + 2], dk[c8 * 4 + 3]);
-                    }
-                }
-            }
+            tmem_st8_async(tmem + lane_base + kST + col, pk);
+            tmem_st8_async(tmem + lane_base + kDPT + col, dk);
+            // dS^T row piece into the swizzled staging tile (two 16-byte chunks of the 128-byte row)
+            uint8_t* stile = sdst + st * kDsTileBytes;
+            *reinterpret_cast<uint4*>(stile + sw128_offset(r, grp * 2)) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
+            *reinterpret_cast<uint4*>(stile + sw128_offset(r, grp * 2 + 1)) = make_uint4(dk[4], dk[5], dk[6], dk[7]);
+            fence_proxy_async();
             tmem_wait_st();
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&ds_full[st]);
+            if (issuer)
+            {
+                // the previous tile's store has read its staging buffer, which the next
+                // iteration rewrites (every thread passes the barrier below before that)
+                bulk_wait_group_read<0>();
+            }
+            named_sync(1, 32 * kComputeWarps);   // every row of this dS^T tile is staged
+            if (issuer)
+            {
+                tma_store_3d(&tds, stile, q0, kt * 128, b * p.H + h);
+                bulk_commit_group();
+            }
         }
-        // dV and dK rows of this key (summed over the group's heads in TMEM): 64 dims per warp
+        if (issuer)
+        {
+            bulk_wait_group<0>();
+        }
+        // dV and dK rows of this key (summed over the group's heads in TMEM): 32 dims per warp
         mbar_wait(done, 0, p.status, abort);
         fence_after();
         const bool valid = key < p.T;
         bf16* vrow = p.dv + (static_cast<int64_t>(b) * p.T + key) * p.lddv + static_cast<int64_t>(kvh) * 128;
         bf16* krow = p.dk + (static_cast<int64_t>(b) * p.T + key) * p.lddk + static_cast<int64_t>(kvh) * 128;
-#pragma unroll 1
-        for (int c = half * 2; c < half * 2 + 2; ++c)
         {
+            const int c = grp;
             uint32_t rv[32], rk[32];
             tmem_ld32(tmem + lane_base + kDV + c * 32, rv);
             tmem_ld32(tmem + lane_base + kDK + c * 32, rk);
@@ -1052,7 +1069,7 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
                 static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
                 scale * kLog2e, causal, device_status_ptr()};
     const dim3 grid(static_cast<unsigned>(B * Hkv), static_cast<unsigned>((T + 127) / 128));
-    attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, p);
+    attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, mds, p);
     DqParams pq{static_cast<bf16*>(dq), lddq, static_cast<int>(T), static_cast<int>(H),
                 static_cast<int>(Hkv), scale, causal, device_status_ptr()};
     const dim3 gq(static_cast<unsigned>(B * H), static_cast<unsigned>((T + 127) / 128));
