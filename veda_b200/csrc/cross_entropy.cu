@@ -92,7 +92,7 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
           float grad_scale, int* status)
 {
     constexpr int V = VEC ? Vec16<T>::N : 1;
-    constexpr int U = VEC ? 2 : 1;   // vectors in flight per thread
+    constexpr int U = VEC ? 4 : 1;   // vectors in flight per thread (64 KB a block)
     __shared__ float red_m[kThreads / 32];
     __shared__ float red_s[kThreads / 32];
     __shared__ float final_m, final_log2;
@@ -185,18 +185,8 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
         if (dlogits != nullptr && valid)
         {
             T* d = dlogits + row * ldd;
-            for (int64_t k = static_cast<int64_t>(threadIdx.x) * V; k < vocab;
-                 k += static_cast<int64_t>(kThreads) * V)
-            {
-                float v[V];
-                if constexpr (VEC)
-                {
-                    load16(x + k, v);
-                }
-                else
-                {
-                    v[0] = to_f32(x[k]);
-                }
+            constexpr int U2 = VEC ? 2 : 1;   // vectors in flight per thread in the L2 pass
+            auto grad = [&](int64_t k, float (&v)[V]) {
 #pragma unroll
                 for (int j = 0; j < V; ++j)
                 {
@@ -207,14 +197,43 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
                     }
                     v[j] = g;
                 }
+            };
+            int64_t k = static_cast<int64_t>(threadIdx.x) * V;
+            for (; k + static_cast<int64_t>(kThreads) * V * (U2 - 1) < vocab;
+                 k += static_cast<int64_t>(kThreads) * V * U2)
+            {
+                float v[U2][V];
+#pragma unroll
+                for (int u = 0; u < U2; ++u)
+                {
+                    if constexpr (VEC)
+                        load16(x + k + static_cast<int64_t>(u) * kThreads * V, v[u]);
+                    else
+                        v[u][0] = to_f32(x[k]);
+                }
+#pragma unroll
+                for (int u = 0; u < U2; ++u)
+                {
+                    const int64_t ku = k + static_cast<int64_t>(u) * kThreads * V;
+                    grad(ku, v[u]);
+                    if constexpr (VEC)
+                        store16(d + ku, v[u]);
+                    else
+                        d[ku] = from_f32<T>(v[u][0]);
+                }
+            }
+            for (; k < vocab; k += static_cast<int64_t>(kThreads) * V)
+            {
+                float v[V];
                 if constexpr (VEC)
-                {
-                    store16(d + k, v);
-                }
+                    load16(x + k, v);
                 else
-                {
+                    v[0] = to_f32(x[k]);
+                grad(k, v);
+                if constexpr (VEC)
+                    store16(d + k, v);
+                else
                     d[k] = from_f32<T>(v[0]);
-                }
             }
         }
         __syncthreads();
