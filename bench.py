@@ -275,10 +275,10 @@ def run_veda(args):
     e2e = tokens / (e2e_ms / 1000.0)
     hbm, tf_burst, tf_sus, peak_kind = load_peaks()
 
-    gemm = [prof[k] for k in ("gemm_fwd", "gemm_dx", "gemm_dw") if k in prof]
-    g_ms = sum(p[0] for p in gemm)
-    g_fl = sum(p[1] for p in gemm)
-    g_n = sum(p[3] for p in gemm)
+    gemm = [(k, prof[k]) for k in ("gemm_fwd", "gemm_dx", "gemm_dw", "gemm_bwd") if k in prof]
+    g_ms = sum(p[0] for _, p in gemm)
+    g_fl = sum(p[1] for _, p in gemm)
+    g_n = sum(p[3] * (2 if k == "gemm_bwd" else 1) for k, p in gemm)   # a gemm_bwd scope = 2 GEMMs
     achieved = g_fl / (g_ms / 1000.0) / 1e12 if g_ms > 0 else None
     kernels = {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[3] / args.steps,
                    "tflops": (v[1] / (v[0] / 1000.0) / 1e12) if v[1] and v[0] else None,
@@ -298,7 +298,7 @@ def run_veda(args):
                    "params": tr.n, "l2": "inputs and the step's working set exceed L2",
                    "buckets_mb": 25},
         "mfu_model_tflops": model_flops_per_token(c, T) * value / 1e12,
-        "roofline": {"bound": "tensor", "kernel": "tcgen05 GEMM (gemm_fwd+gemm_dx+gemm_dw)",
+        "roofline": {"bound": "tensor", "kernel": "tcgen05 GEMM (gemm_fwd + gemm_bwd: dX beside dW)",
                      "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s",
                      "peak_kind": f"{peak_kind} bf16 sustained",
                      "frac": (achieved / tf_sus) if achieved else None,

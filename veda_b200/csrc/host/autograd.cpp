@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <limits>
 #include <mutex>
 #include <stdexcept>
@@ -40,6 +41,41 @@ void cuda_check(cudaError_t e, const char* what)
 }
 
 Tensor make_contiguous(const Tensor& t) { return t.is_contiguous() ? t : core::contiguous(t); }
+
+// A second stream per device for work that may run beside the current stream (a Linear's weight
+// gradient beside its input gradient), with the two events that fork it off and join it back.
+struct SideStream
+{
+    cudaStream_t stream = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+SideStream& side_stream()
+{
+    thread_local SideStream sides[64];
+    int device = 0;
+    cuda_check(cudaGetDevice(&device), "side stream: device");
+    SideStream& f = sides[device & 63];
+    if (f.stream == nullptr)
+    {
+        cuda_check(cudaStreamCreateWithFlags(&f.stream, cudaStreamNonBlocking), "side stream");
+        cuda_check(cudaEventCreateWithFlags(&f.fork, cudaEventDisableTiming), "fork event");
+        cuda_check(cudaEventCreateWithFlags(&f.join, cudaEventDisableTiming), "join event");
+    }
+    return f;
+}
+
+// The input- and weight-gradient GEMMs of a Linear run concurrently (VEDA_GEMM_OVERLAP=0 runs
+// them one after the other): both are persistent kernels, so the second one's tiles fill the SMs
+// the first one's last partial wave leaves idle.
+bool gemm_overlap_enabled()
+{
+    static const bool on = [] {
+        const char* v = std::getenv("VEDA_GEMM_OVERLAP");
+        return !(v != nullptr && v[0] == '0');
+    }();
+    return on;
+}
 
 Tensor as_dtype(const Tensor& t, DType d)
 {
@@ -1167,6 +1203,45 @@ Variable linear(const Variable& x, const Variable& w)
     return make({x, w}, std::move(value), [xin, win, xs, ldx, wc, rows, in, out](const Tensor& g) {
         const Tensor gc = as_dtype(g, xs.dtype());
         const double es = static_cast<double>(core::dtype_size(xs.dtype()));
+        if (xin->requires_grad && win->requires_grad && gemm_overlap_enabled())
+        {
+            // dW (+)= G^T X on the side stream, dX = G W on this one, then join: everything
+            // after this (including the release of G and X) is ordered after both.
+            bool fresh = false;
+            Tensor& gw = grad_target(*win, &fresh, DType::F32);
+            profile::Scope scope("gemm_bwd", 4.0 * rows * in * out,
+                                 es * (2.0 * static_cast<double>(rows) * out +
+                                       static_cast<double>(out) * in +
+                                       2.0 * static_cast<double>(rows) * in) +
+                                     4.0 * static_cast<double>(out) * in * (fresh ? 1.0 : 2.0));
+            SideStream& side = side_stream();
+            const cudaStream_t main = reinterpret_cast<cudaStream_t>(S());
+            cuda_check(cudaEventRecord(side.fork, main), "gemm fork");
+            cuda_check(cudaStreamWaitEvent(side.stream, side.fork, 0), "gemm fork wait");
+            check(veda_gemm_tn(out, in, rows, gc.data_ptr(), out, xs.data_ptr(), ldx,
+                               gw.data_ptr(), in, dt(xs.dtype()), dt(gw.dtype()), 1.0f,
+                               fresh ? 0.0f : 1.0f, side.stream),
+                  "linear backward (weight)");
+            if (!xin->grad.defined() || xin->is_leaf || xin->grad_zero || !xin->grad_owned)
+            {
+                Tensor d = Tensor::empty(xin->value.shape(), xs.dtype());
+                check(veda_gemm_nn(rows, in, out, gc.data_ptr(), out, wc.data_ptr(), in,
+                                   d.data_ptr(), in, dt(xs.dtype()), dt(xs.dtype()), 1.0f, 0.0f,
+                                   S()),
+                      "linear backward (input)");
+                accumulate(*xin, d);
+            }
+            else
+            {
+                check(veda_gemm_nn(rows, in, out, gc.data_ptr(), out, wc.data_ptr(), in,
+                                   xin->grad.data_ptr(), in, dt(xs.dtype()),
+                                   dt(xin->grad.dtype()), 1.0f, 1.0f, S()),
+                      "linear backward (input)");
+            }
+            cuda_check(cudaEventRecord(side.join, side.stream), "gemm join");
+            cuda_check(cudaStreamWaitEvent(main, side.join, 0), "gemm join wait");
+            return;
+        }
         if (xin->requires_grad)
         {
             // dX = G W  (NN)
