@@ -52,6 +52,11 @@ uint64_t veda_launch_count(void);
 /* The current device's status word: 0, or VEDA_ERR_TIMEOUT if a kernel's bounded device-side
  * wait gave up since the last reset. Synchronises with the device; reset = 1 clears it. */
 int veda_kernel_status(int reset);
+/* Number of SMs the persistent kernels (tensor-core GEMMs, streaming RMSNorm) leave free for
+ * work running beside them, such as NCCL all-reduce blocks during a data-parallel backward;
+ * 0 (the default) uses every SM. Process-wide; returns the previous value. No counterpart in
+ * the reference (its kernels are CPU loops). */
+int veda_set_reserved_sms(int n);
 
 /* ---------------------------------------------------------------------------------------- */
 /* GEMM — the Linear / LM-head matmuls and both of their backward products.                  */

@@ -22,6 +22,8 @@ int fail(int code, const std::string& message);
 int check_launch(const char* what);
 void count_launch(uint64_t n = 1);
 int sm_count();
+// SMs a persistent kernel may use: sm_count() less those reserved by veda_set_reserved_sms.
+int compute_sms();
 uint64_t g_launches_value();
 const char* last_error_cstr();
 

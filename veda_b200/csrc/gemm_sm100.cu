@@ -979,9 +979,10 @@ int tc_gemm_pair(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t
 {
     const bool a_mn = op == kTN;
     const bool b_mn = op != kNT;
-    const int clusters_max = op == kNT ? pair_clusters<false, false>()
-                           : op == kNN ? pair_clusters<false, true>()
-                                       : pair_clusters<true, true>();
+    const int clusters_max = std::min(op == kNT ? pair_clusters<false, false>()
+                                      : op == kNN ? pair_clusters<false, true>()
+                                                  : pair_clusters<true, true>(),
+                                      compute_sms() / 2);
     if (clusters_max < 1)
     {
         return -1;
@@ -1069,7 +1070,7 @@ int tc_gemm(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
     p.vec_ok = aligned16(C) && (ldc % (dtype_c == VEDA_F32 ? 4 : 8)) == 0;
     p.status = device_status_ptr();
     const int tiles = p.num_m * p.num_n;
-    p.splits = choose_splits(tiles, p.kblocks, p.out_f32 != 0, sm_count());
+    p.splits = choose_splits(tiles, p.kblocks, p.out_f32 != 0, compute_sms());
     p.kb_per_split = (p.kblocks + p.splits - 1) / p.splits;
     p.atomic = p.splits > 1;
     if (p.atomic)
@@ -1091,7 +1092,7 @@ int tc_gemm(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
     CUtensorMap mc{};
     output_mode(p, &mc, C, M, N, ldc, beta);
     const int units = tiles * p.splits;
-    const int grid = std::min(units, sm_count());
+    const int grid = std::min(units, compute_sms());
     const bool big = BN == 256;
     if (op == kNT)
         return big ? launch_tc<256, false, false>(ma, mb, mc, p, grid, s)

@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <unordered_map>
@@ -56,7 +57,12 @@ public:
         ncclUniqueId id;
         std::memcpy(&id, unique_id, sizeof(id));
         nccl_check(ncclCommInitRank(&comm_, world, id, rank), "ncclCommInitRank");
-        cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "comm stream");
+        // Highest priority: the compute kernels hold every SM (one large block per SM), so the
+        // all-reduce blocks must win each SM slot that frees up to overlap with the backward.
+        int least = 0, greatest = 0;
+        cuda_check(cudaDeviceGetStreamPriorityRange(&least, &greatest), "stream priorities");
+        cuda_check(cudaStreamCreateWithPriority(&stream_, cudaStreamNonBlocking, greatest),
+                   "comm stream");
         cuda_check(cudaEventCreateWithFlags(&done_, cudaEventDisableTiming), "comm event");
     }
 
@@ -104,6 +110,9 @@ public:
         }
     }
 
+    // From the start of the backward until every bucket is queued, the persistent kernels leave
+    // reserved_sms_ SMs free so the all-reduce blocks run beside them instead of only in the gaps
+    // between kernels (each compute block holds a whole SM).
     void begin_step()
     {
         for (Bucket& b : buckets_)
@@ -111,6 +120,7 @@ public:
             b.pending = b.waiting;
             b.launched = false;
         }
+        veda_set_reserved_sms(reserved_sms_);
     }
 
     void leaf_ready(autograd::Node* node)
@@ -140,6 +150,7 @@ public:
         }
         cuda_check(cudaEventRecord(done_, stream_), "comm done");
         cuda_check(cudaStreamWaitEvent(cs(), done_, 0), "comm wait");
+        veda_set_reserved_sms(0);
     }
 
     int world() const noexcept { return world_; }
@@ -164,6 +175,11 @@ private:
                    "ncclAllReduce");
     }
 
+    // SMs left to NCCL during the backward (VEDA_DP_RESERVED_SMS, default 16)
+    int reserved_sms_ = [] {
+        const char* v = std::getenv("VEDA_DP_RESERVED_SMS");
+        return v != nullptr ? std::atoi(v) : 16;
+    }();
     ncclComm_t comm_ = nullptr;
     cudaStream_t stream_ = nullptr;
     cudaEvent_t done_ = nullptr;

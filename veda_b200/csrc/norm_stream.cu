@@ -317,7 +317,7 @@ int launch_fwd(const bf16* x, int64_t ldx, const bf16* gamma, bf16* y, int64_t l
         configured = device;
     }
     const int64_t chunks = (rows + kRows - 1) / kRows;
-    const unsigned grid = static_cast<unsigned>(chunks < sm_count() ? chunks : sm_count());
+    const unsigned grid = static_cast<unsigned>(chunks < compute_sms() ? chunks : compute_sms());
     rms_fwd_stream_kernel<CH><<<grid, kThreadsStream, R::SMEM, s>>>(x, ldx, gamma, y, ldy, rows, eps,
                                                                     device_status_ptr());
     count_launch();
@@ -340,7 +340,7 @@ int launch_bwd(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* dy, in
         configured = device;
     }
     const int64_t chunks = (rows + kRows - 1) / kRows;
-    int64_t g = chunks < sm_count() ? chunks : sm_count();
+    int64_t g = chunks < compute_sms() ? chunks : compute_sms();
     if (g > max_blocks) g = max_blocks;
     if (g < 1) g = 1;
     *blocks = static_cast<int>(g);

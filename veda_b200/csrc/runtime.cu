@@ -54,6 +54,15 @@ int sm_count()
     return g_sm_count[device];
 }
 
+// SMs the persistent kernels leave free (veda_set_reserved_sms).
+std::atomic<int> g_reserved_sms{0};
+
+int compute_sms()
+{
+    const int n = sm_count() - g_reserved_sms.load(std::memory_order_relaxed);
+    return n < 2 ? 2 : n;
+}
+
 const char* last_error_cstr() { return g_last_error.c_str(); }
 
 // One int per device, allocated on first use: kernels whose bounded waits give up write
@@ -128,4 +137,9 @@ extern "C" int veda_device_info(int* sm, int* major, int* minor)
     if (major) *major = prop.major;
     if (minor) *minor = prop.minor;
     return VEDA_OK;
+}
+
+extern "C" int veda_set_reserved_sms(int n)
+{
+    return veda::cuda::g_reserved_sms.exchange(n < 0 ? 0 : n);
 }
