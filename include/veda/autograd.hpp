@@ -98,6 +98,10 @@ Variable cross_entropy(const Variable& logits, const std::vector<int64_t>& targe
 // ---- fused modules --------------------------------------------------------------------------
 // mul(rms_normalize(x, eps), gamma) over the last dim.
 Variable rms_norm(const Variable& x, const Variable& gamma, float eps);
+// rms_norm(add(x, r), gamma, eps) with the sum formed in the same pass; *sum receives the
+// add(x, r) node (the residual stream), which the result's node takes as its input.
+Variable add_rms_norm(const Variable& x, const Variable& r, const Variable& gamma, float eps,
+                      Variable* sum);
 // matmul_nt(x, w) with x [.., in] flattened to rows and w [out, in].
 Variable linear(const Variable& x, const Variable& w);
 // Qwen3 attention core on a fused projection qkv [B*T, (H + 2 Hkv) * Dh] (q | k | v columns):

@@ -81,6 +81,12 @@ public:
     size_t parameter_count() const noexcept { return total_; }
     // Clears the whole gradient arena in one memset and marks every leaf's gradient as zero.
     void zero_grad();
+    // zero_grad without the memset: every leaf is only marked as holding zeros, so the backward's
+    // first write to it overwrites (a GEMM with beta 0, a copy, a kernel that clears its target
+    // first). clear_untouched_grads() then clears the leaves the backward never reached; between
+    // the two calls the arena holds the previous step's values.
+    void mark_grads_zero();
+    void clear_untouched_grads();
 
 private:
     autograd::Variable forward_from(const autograd::Variable& x, size_t batch, size_t length);

@@ -94,6 +94,12 @@ int veda_gemm_batched(int op, int64_t batch, int64_t M, int64_t N, int64_t K, co
 /* ---------------------------------------------------------------------------------------- */
 int veda_rmsnorm_fwd(const void* x, int64_t ldx, const void* gamma, void* y, int64_t ldy,
                      int64_t rows, int64_t n, float eps, int dtype, veda_stream_t stream);
+/* The residual add followed by the next norm (Model.cpp:244-249, the add of Variable.cpp:195-216
+ * then the RMSNorm above), in one pass for bf16 rows of 256/512/1024/2048: sum = x + r (rounded
+ * to the dtype, as the add stores it) and y = RMSNorm(sum) * gamma. */
+int veda_add_rmsnorm_fwd(const void* x, int64_t ldx, const void* r, int64_t ldr,
+                         const void* gamma, void* sum, int64_t lds, void* y, int64_t ldy,
+                         int64_t rows, int64_t n, float eps, int dtype, veda_stream_t stream);
 /* Backward (src/libs/autograd/NonLinear.cpp:153-201 and the gain's mul/unbroadcast,
  * Variable.cpp:218-239): dx = dresid + (G/r - x * sum(G x)/(n r^3)), G = dy * gamma;
  * dgamma (fp32 [n], may be NULL) += sum over rows of dy * x / r. dresid may be NULL.
@@ -206,7 +212,8 @@ int veda_clip_apply(float* g, int64_t n, const double* sumsq, float max_norm,
  *   w -= lr*wd*w;  w -= lr * float((m/bias1) / (sqrt(v/bias2) + eps))  (m_hat, v_hat in double)
  * bias1 = 1 - beta1^t, bias2 = 1 - beta2^t computed by the caller in double.
  * lowp (bf16 [n], may be NULL) receives the rounded copy the forward reads.
- * write_grad = 1 stores g' back into g (the clipped gradient, as Clip.cpp:52-58 leaves it). */
+ * write_grad = 1 leaves g' in g (the clipped gradient, as Clip.cpp:52-58 leaves it); the store
+ * is skipped when g' == g (no clip and grad_scale 1). */
 int veda_adamw_step(float* master, float* m, float* v, float* g, void* lowp, int64_t n, float lr,
                     float beta1, float beta2, float eps, float weight_decay, double bias1,
                     double bias2, const double* sumsq, float max_norm, float grad_scale,

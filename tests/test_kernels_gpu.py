@@ -58,6 +58,30 @@ def test_rmsnorm_fwd_bwd(dtype, rows, n):
     assert rel(host(dgam), dgam_ref + 0.5) <= (1e-4 if dtype == V.F32 else 1e-3)
 
 
+@pytest.mark.parametrize("dtype,rows,n", [(V.BF16, 1001, 1024), (V.BF16, 77, 2048),
+                                          (V.BF16, 9, 256), (V.BF16, 5, 300), (V.F32, 33, 512)])
+def test_add_rmsnorm_fwd(dtype, rows, n):
+    """The residual add fused with the next norm: the sum is the add's result exactly (fp32 add
+    rounded to the dtype, Variable.cpp:195-216) and the output is the norm of that sum."""
+    r = rng(rows * 3 + n)
+    x = r.standard_normal((rows, n)).astype(F32)
+    res = r.standard_normal((rows, n)).astype(F32)
+    gam = (1 + 0.1 * r.standard_normal(n)).astype(F32)
+    if dtype == V.BF16:
+        x, res, gam = bf(x), bf(res), bf(gam)
+    s_ref = x + res
+    if dtype == V.BF16:
+        s_ref = bf(s_ref)
+    y_ref, _, _ = O.rms_norm_gamma(s_ref, gam, 1e-6)
+    xd, rd, gd = dev(x, dtype), dev(res, dtype), dev(gam, dtype)
+    total, y = empty((rows, n), dtype), empty((rows, n), dtype)
+    call("veda_add_rmsnorm_fwd", ptr(xd), n, ptr(rd), n, ptr(gd), ptr(total), n, ptr(y), n, rows,
+         n, 1e-6, dtype, stream())
+    sync()
+    assert np.array_equal(host(total), s_ref)
+    assert rel(host(y), y_ref) <= TOL[dtype]
+
+
 @pytest.mark.parametrize("with_dgamma", [True, False])
 def test_rmsnorm_bwd_without_residual(with_dgamma):
     """The backward without a residual gradient, with and without the gain gradient."""
@@ -191,9 +215,16 @@ def test_swiglu(dtype, rows, F):
 # ---------------------------------------------------------------------------------------------
 # Cross-entropy
 # ---------------------------------------------------------------------------------------------
-@pytest.mark.parametrize("dtype,rows,Vv", [(V.F32, 128, 512), (V.F32, 9, 77), (V.BF16, 64, 151936),
-                                           (V.F32, 16, 151936)])
-def test_cross_entropy(dtype, rows, Vv):
+# rows of >= 128 KB take the cluster form (a row split over 8 CTAs); (BF16, 37, 65544) leaves the
+# last CTA a shorter slice, (BF16, 3, 70001) is not a whole number of 16-byte vectors (one-CTA
+# form), and 1000 rows make every cluster loop over several rows
+@pytest.mark.parametrize("dtype,rows,Vv,inplace", [(V.F32, 128, 512, False), (V.F32, 9, 77, False),
+                                                   (V.BF16, 64, 151936, False),
+                                                   (V.F32, 16, 151936, False),
+                                                   (V.BF16, 1000, 151936, True),
+                                                   (V.BF16, 37, 65544, True),
+                                                   (V.BF16, 3, 70001, False)])
+def test_cross_entropy(dtype, rows, Vv, inplace):
     r = rng(rows * 7 + Vv)
     lg = (3 * r.standard_normal((rows, Vv))).astype(F32)
     if dtype == V.BF16:
@@ -203,7 +234,7 @@ def test_cross_entropy(dtype, rows, Vv):
     rows_ref = O.cross_entropy_rows(lg, t)
     lgd, td = dev(lg, dtype), dev(t)
     row_loss = empty(rows)
-    d = lgd.clone()   # in place over a copy of the logits
+    d = lgd if inplace else lgd.clone()
     status = zeros(1).int()
     call("veda_cross_entropy", ptr(lgd), Vv, ptr(td), ptr(row_loss), ptr(d), Vv, rows, Vv,
          1.0 / rows, ptr(status), dtype, stream())
@@ -236,6 +267,26 @@ def test_cross_entropy_golden_and_out_of_range():
          1.0, ptr(status), V.F32, stream())
     sync()
     assert int(host(status)[0]) == V.ERR_OUT_OF_RANGE
+
+
+def test_cross_entropy_cluster_out_of_range_target():
+    rows, Vv = 6, 151936
+    r = rng(11)
+    lg = bf((3 * r.standard_normal((rows, Vv))).astype(F32))
+    t = r.integers(0, Vv, rows).astype(np.int64)
+    t[2] = -1
+    ok = np.arange(rows) != 2
+    rows_ref = O.cross_entropy_rows(lg[ok], t[ok])
+    lgd, td = dev(lg, V.BF16), dev(t)
+    row_loss, status = empty(rows), zeros(1).int()
+    d = lgd.clone()
+    call("veda_cross_entropy", ptr(lgd), Vv, ptr(td), ptr(row_loss), ptr(d), Vv, rows, Vv,
+         1.0 / rows, ptr(status), V.BF16, stream())
+    sync()
+    assert int(host(status)[0]) == V.ERR_OUT_OF_RANGE
+    got = host(row_loss)
+    assert np.isnan(got[2])
+    assert rel(got[ok], rows_ref) <= 1e-5
 
 
 # ---------------------------------------------------------------------------------------------

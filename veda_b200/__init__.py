@@ -42,6 +42,8 @@ SIGNATURES = {
     "veda_gemm_batched": (_i, [_i, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p,
                                _i64, _i64, _i, _i, _f, _f, _p]),
     "veda_rmsnorm_fwd": (_i, [_p, _i64, _p, _p, _i64, _i64, _i64, _f, _i, _p]),
+    "veda_add_rmsnorm_fwd": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _i64, _i64, _f, _i,
+                                  _p]),
     "veda_rmsnorm_bwd": (_i, [_p, _i64, _p, _p, _i64, _p, _i64, _p, _i64, _p, _p, _sz, _i64,
                               _i64, _f, _i, _p]),
     "veda_rmsnorm_bwd_workspace": (_sz, [_i64, _i64]),

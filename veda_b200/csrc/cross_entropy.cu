@@ -4,8 +4,8 @@
 // src/libs/ops/Softmax.cpp:82-151) materialises fp32 log-probabilities and probabilities for the
 // whole [lanes, V] block. Here one CTA owns a row: pass 1 reads it once keeping a running
 // (max, sum of exp) per thread (online normaliser), reduced across the CTA; pass 2 re-reads it
-// (an L2 hit: 2 CTAs on each of 148 SMs keep 296 rows of 300 KB in flight, inside the 126 MB L2)
-// and writes
+// (from L2: 2 CTAs on each of 148 SMs keep 296 rows of 300 KB in flight, held there by L2
+// eviction priorities) and writes
 //   dlogits = grad_scale * exp(x - max - log(sum))   minus grad_scale at the target,
 // the (p - onehot) * g/lanes of Loss.cpp:80-99 with p = exp(log_softmax) as the reference forms
 // it. row_loss = -(x_t - max - log(sum)) in fp32; the mean over rows is taken in double by
@@ -55,14 +55,16 @@ __device__ __forceinline__ void online_merge(float& m, float& s, float om, float
     }
 }
 
-// Adds a group of N values (already scaled by log2 e) to (m, s): one max over the group, a
-// rescale only when the group raises the running max, then N exponentials.
+// Adds a group of N logits to (m, s), m in log2 units: one max over the group (max(x) log2 e =
+// max(x log2 e), the scaling being monotone), a rescale only when the group raises the running
+// max, then N exponentials 2^(x log2 e - m), each argument formed by one fused multiply-add.
 template <int N>
-__device__ __forceinline__ void online_add(float& m, float& s, const float (&y)[N])
+__device__ __forceinline__ void online_add(float& m, float& s, const float (&x)[N])
 {
-    float gm = y[0];
+    float gx = x[0];
 #pragma unroll
-    for (int j = 1; j < N; ++j) gm = fmaxf(gm, y[j]);
+    for (int j = 1; j < N; ++j) gx = fmaxf(gx, x[j]);
+    const float gm = gx * kLog2e;
     if (gm > m)
     {
         s = (m == -INFINITY) ? 0.0f : s * ex2(m - gm);
@@ -76,15 +78,52 @@ __device__ __forceinline__ void online_add(float& m, float& s, const float (&y)[
 #pragma unroll
     for (int j = 0; j < N; j += 2)
     {
-        a += ex2(y[j] - m);
-        if (j + 1 < N) b += ex2(y[j + 1] - m);
+        a += ex2(fmaf(x[j], kLog2e, -m));
+        if (j + 1 < N) b += ex2(fmaf(x[j + 1], kLog2e, -m));
     }
     s += a + b;
 }
 
+// L2 eviction policies: the row's first read marks its lines to be kept for the second pass,
+// which reads them for the last time and writes the gradient as first to be evicted, so the
+// 2 x 148 rows in flight (90 MB of logits, as much again of gradient) stay in the 126 MB L2.
+__device__ __forceinline__ uint64_t l2_policy_keep()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_drop()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+template <typename T>
+__device__ __forceinline__ void load16_hint(const T* p, float (&out)[16 / sizeof(T)], uint64_t pol)
+{
+    uint4 r;
+    asm volatile("ld.global.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p), "l"(pol));
+    load16(reinterpret_cast<const T*>(&r), out);
+}
+
+template <typename T>
+__device__ __forceinline__ void store16_hint(T* p, const float (&in)[16 / sizeof(T)], uint64_t pol)
+{
+    uint4 r;
+    store16(reinterpret_cast<T*>(&r), in);
+    asm volatile("st.global.L2::cache_hint.v4.u32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "r"(r.x),
+                 "r"(r.y), "r"(r.z), "r"(r.w), "l"(pol)
+                 : "memory");
+}
+
 // One CTA per row (grid-stride). Pass 1 streams the row from HBM; pass 2 re-reads it from L2
-// (at most 2 CTAs per SM: 296 rows of 304 KB in flight stay well inside the 126 MB L2) and writes
-// the gradient. Exponentials run in the log2 domain on the MUFU unit.
+// (at most 2 CTAs per SM; the eviction policies above keep the 296 rows in flight resident) and
+// writes the gradient. Exponentials run in the log2 domain on the MUFU unit.
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(kThreads, 2)
 ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__ targets,
@@ -96,6 +135,14 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
     __shared__ float red_m[kThreads / 32];
     __shared__ float red_s[kThreads / 32];
     __shared__ float final_m, final_log2;
+    const uint64_t keep = l2_policy_keep(), drop = l2_policy_drop();
+    // a power-of-two grad_scale (1 / lanes for a power-of-two lane count) folds into the exponent
+    // exactly: grad_scale 2^a = 2^(a + log2 grad_scale)
+    const bool pow2 = grad_scale > 0.0f && (__float_as_uint(grad_scale) & 0x7FFFFFu) == 0 &&
+                      (__float_as_uint(grad_scale) >> 23) != 0;
+    const float log2_scale =
+        pow2 ? static_cast<float>(static_cast<int>(__float_as_uint(grad_scale) >> 23) - 127) : 0.0f;
+    const float mul_scale = pow2 ? 1.0f : grad_scale;
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x)
     {
         const T* x = logits + row * ldl;
@@ -113,27 +160,20 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
             for (int u = 0; u < U; ++u)
             {
                 if constexpr (VEC)
-                    load16(x + i + static_cast<int64_t>(u) * kThreads * V, v[u]);
+                    load16_hint(x + i + static_cast<int64_t>(u) * kThreads * V, v[u], keep);
                 else
                     v[u][0] = to_f32(x[i]);
             }
 #pragma unroll
-            for (int u = 0; u < U; ++u)
-            {
-#pragma unroll
-                for (int j = 0; j < V; ++j) v[u][j] *= kLog2e;
-                online_add<V>(m, s, v[u]);
-            }
+            for (int u = 0; u < U; ++u) online_add<V>(m, s, v[u]);
         }
         for (; i < vocab; i += static_cast<int64_t>(kThreads) * V)
         {
             float v[V];
             if constexpr (VEC)
-                load16(x + i, v);
+                load16_hint(x + i, v, keep);
             else
                 v[0] = to_f32(x[i]);
-#pragma unroll
-            for (int j = 0; j < V; ++j) v[j] *= kLog2e;
             online_add<V>(m, s, v);
         }
         // warp then block merge of (m, s)
@@ -185,17 +225,16 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
         if (dlogits != nullptr && valid)
         {
             T* d = dlogits + row * ldd;
-            constexpr int U2 = VEC ? 2 : 1;   // vectors in flight per thread in the L2 pass
+            constexpr int U2 = VEC ? 4 : 1;   // vectors in flight per thread in the L2 pass
+            const float shift_g = shift - log2_scale;
             auto grad = [&](int64_t k, float (&v)[V]) {
 #pragma unroll
-                for (int j = 0; j < V; ++j)
+                for (int j = 0; j < V; ++j) v[j] = mul_scale * ex2(fmaf(v[j], kLog2e, -shift_g));
+                if (t >= k && t < k + V)
                 {
-                    float g = grad_scale * ex2(fmaf(v[j], kLog2e, -shift));
-                    if (k + j == t)
-                    {
-                        g -= grad_scale;
-                    }
-                    v[j] = g;
+#pragma unroll
+                    for (int j = 0; j < V; ++j)
+                        if (k + j == t) v[j] -= grad_scale;
                 }
             };
             int64_t k = static_cast<int64_t>(threadIdx.x) * V;
@@ -207,7 +246,7 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
                 for (int u = 0; u < U2; ++u)
                 {
                     if constexpr (VEC)
-                        load16(x + k + static_cast<int64_t>(u) * kThreads * V, v[u]);
+                        load16_hint(x + k + static_cast<int64_t>(u) * kThreads * V, v[u], drop);
                     else
                         v[u][0] = to_f32(x[k]);
                 }
@@ -217,7 +256,7 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
                     const int64_t ku = k + static_cast<int64_t>(u) * kThreads * V;
                     grad(ku, v[u]);
                     if constexpr (VEC)
-                        store16(d + ku, v[u]);
+                        store16_hint(d + ku, v[u], drop);
                     else
                         d[ku] = from_f32<T>(v[u][0]);
                 }
@@ -226,12 +265,12 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
             {
                 float v[V];
                 if constexpr (VEC)
-                    load16(x + k, v);
+                    load16_hint(x + k, v, drop);
                 else
                     v[0] = to_f32(x[k]);
                 grad(k, v);
                 if constexpr (VEC)
-                    store16(d + k, v);
+                    store16_hint(d + k, v, drop);
                 else
                     d[k] = from_f32<T>(v[0]);
             }

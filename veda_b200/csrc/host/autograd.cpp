@@ -1067,34 +1067,14 @@ Variable cross_entropy_device(const Variable& logits, const Tensor& targets)
 }
 
 // ---- fused modules ----------------------------------------------------------------------------
-Variable rms_norm(const Variable& x, const Variable& gamma, float eps)
+namespace
 {
-    const Tensor& xv = x.value();
-    const size_t n = xv.shape()[xv.rank() - 1];
-    if (gamma.value().shape() != Shape({n}))
-    {
-        throw std::invalid_argument("rms_norm: gain of shape " + gamma.value().shape().to_string() +
-                                    " for rows of " + std::to_string(n));
-    }
-    const Tensor xc = xv.rank() >= 2 ? (xv.strides().back() == 1 ? xv : make_contiguous(xv))
-                                     : make_contiguous(xv);
-    int64_t ld = static_cast<int64_t>(n);
-    Tensor xs = xc;
-    try
-    {
-        if (xc.rank() >= 2) ld = xc.ld();
-    }
-    catch (const std::invalid_argument&)
-    {
-        xs = make_contiguous(xc);
-        ld = static_cast<int64_t>(n);
-    }
+// The node of y = rms_norm(x) * gamma over rows of n, given its forward value; xs is x's value
+// (rows at stride ld) and gv the gain in x's dtype, both kept for the backward.
+Variable rms_norm_node(const Variable& x, const Variable& gamma, Tensor value, const Tensor& xs,
+                       int64_t ld, const Tensor& gv, size_t n, float eps)
+{
     const size_t rows = xs.numel() / n;
-    const Tensor gv = as_dtype(gamma.value(), xs.dtype());
-    Tensor value = Tensor::empty(xs.shape(), xs.dtype());
-    check(veda_rmsnorm_fwd(xs.data_ptr(), ld, gv.data_ptr(), value.data_ptr(), n, rows, n, eps,
-                           dt(xs.dtype()), S()),
-          "rms_norm");
     auto xin = x.node(), gin = gamma.node();
     return make({x, gamma}, std::move(value), [xin, gin, xs, gv, ld, n, rows, eps](const Tensor& g) {
         const Tensor gc = as_dtype(g, xs.dtype());
@@ -1147,6 +1127,81 @@ Variable rms_norm(const Variable& x, const Variable& gamma, float eps)
                   "rms_norm backward");
         }
     });
+}
+
+void check_gain(const Variable& gamma, size_t n, const char* what)
+{
+    if (gamma.value().shape() != Shape({n}))
+    {
+        throw std::invalid_argument(std::string(what) + ": gain of shape " +
+                                    gamma.value().shape().to_string() + " for rows of " +
+                                    std::to_string(n));
+    }
+}
+} // namespace
+
+Variable rms_norm(const Variable& x, const Variable& gamma, float eps)
+{
+    const Tensor& xv = x.value();
+    const size_t n = xv.shape()[xv.rank() - 1];
+    check_gain(gamma, n, "rms_norm");
+    const Tensor xc = xv.rank() >= 2 ? (xv.strides().back() == 1 ? xv : make_contiguous(xv))
+                                     : make_contiguous(xv);
+    int64_t ld = static_cast<int64_t>(n);
+    Tensor xs = xc;
+    try
+    {
+        if (xc.rank() >= 2) ld = xc.ld();
+    }
+    catch (const std::invalid_argument&)
+    {
+        xs = make_contiguous(xc);
+        ld = static_cast<int64_t>(n);
+    }
+    const size_t rows = xs.numel() / n;
+    const Tensor gv = as_dtype(gamma.value(), xs.dtype());
+    Tensor value = Tensor::empty(xs.shape(), xs.dtype());
+    check(veda_rmsnorm_fwd(xs.data_ptr(), ld, gv.data_ptr(), value.data_ptr(), n, rows, n, eps,
+                           dt(xs.dtype()), S()),
+          "rms_norm");
+    return rms_norm_node(x, gamma, std::move(value), xs, ld, gv, n, eps);
+}
+
+Variable add_rms_norm(const Variable& x, const Variable& r, const Variable& gamma, float eps,
+                      Variable* sum)
+{
+    const Tensor& xv = x.value();
+    const Tensor& rv = r.value();
+    if (xv.shape() != rv.shape() || xv.dtype() != rv.dtype() || xv.rank() < 1)
+    {
+        throw std::invalid_argument("add_rms_norm: operands " + xv.shape().to_string() + " and " +
+                                    rv.shape().to_string() + " differ");
+    }
+    if (sum == nullptr)
+    {
+        throw std::invalid_argument("add_rms_norm: no place for the sum");
+    }
+    const size_t n = xv.shape()[xv.rank() - 1];
+    check_gain(gamma, n, "add_rms_norm");
+    const Tensor xs = make_contiguous(xv);
+    const Tensor rs = make_contiguous(rv);
+    const size_t rows = xs.numel() / n;
+    const Tensor gv = as_dtype(gamma.value(), xs.dtype());
+    Tensor total = Tensor::empty(xs.shape(), xs.dtype());
+    Tensor value = Tensor::empty(xs.shape(), xs.dtype());
+    const int64_t ld = static_cast<int64_t>(n);
+    check(veda_add_rmsnorm_fwd(xs.data_ptr(), ld, rs.data_ptr(), ld, gv.data_ptr(), total.data_ptr(),
+                               ld, value.data_ptr(), ld, rows, n, eps, dt(xs.dtype()), S()),
+          "add_rms_norm");
+    // the sum node is add(x, r)'s (Variable.cpp:195-216): the gradient passes to both operands
+    auto left = x.node(), right = r.node();
+    const Tensor stored = total;
+    Variable s = make({x, r}, std::move(total), [left, right](const Tensor& g) {
+        if (left->requires_grad) accumulate(*left, g);
+        if (right->requires_grad) accumulate(*right, g);
+    });
+    *sum = s;
+    return rms_norm_node(s, gamma, std::move(value), stored, ld, gv, n, eps);
 }
 
 Variable linear(const Variable& x, const Variable& w)

@@ -205,6 +205,32 @@ void TinyTransformer::zero_grad()
     }
 }
 
+void TinyTransformer::mark_grads_zero()
+{
+    for (auto& p : parameters_)
+    {
+        p.node()->grad_zero = true;
+    }
+    for (auto& g : graph_leaves_)
+    {
+        g.var.node()->grad_zero = true;
+    }
+}
+
+void TinyTransformer::clear_untouched_grads()
+{
+    float* base = static_cast<float*>(grads_.data_ptr());
+    for (auto& g : graph_leaves_)
+    {
+        if (g.var.node()->grad_zero &&
+            cudaMemsetAsync(base + g.offset, 0, g.count * sizeof(float),
+                            reinterpret_cast<cudaStream_t>(current_stream())) != cudaSuccess)
+        {
+            throw std::runtime_error("TinyTransformer::clear_untouched_grads: memset failed");
+        }
+    }
+}
+
 Variable TinyTransformer::forward(const std::vector<int64_t>& ids, size_t batch, size_t length)
 {
     if (ids.size() != batch * length)
@@ -245,22 +271,23 @@ Variable TinyTransformer::forward_from(const Variable& x0, size_t B, size_t T)
     }
     const Tensor& cosines = it->second.first;
     const Tensor& sines = it->second.second;
+    // pre-norm residual blocks (Model.cpp:238-249); each residual add is fused with the norm
+    // that reads its sum (the next block's input norm, or the final norm)
     Variable x = x0;
-    for (const Layer& L : layers_)
+    Variable a = autograd::rms_norm(x, layers_.empty() ? final_norm_ : layers_[0].in_norm, eps);
+    for (size_t l = 0; l < layers_.size(); ++l)
     {
-        // pre-norm residual blocks (Model.cpp:238-249)
-        Variable a = autograd::rms_norm(x, L.in_norm, eps);
+        const Layer& L = layers_[l];
         Variable qkv = autograd::linear(a, L.qkv);
         Variable ctx = autograd::attention(qkv, L.q_norm, L.k_norm, cosines, sines, B, T, H, Hk,
                                            Dh, eps);
-        x = autograd::add(x, autograd::linear(ctx, L.o));
-        Variable b = autograd::rms_norm(x, L.post_norm, eps);
+        Variable b = autograd::add_rms_norm(x, autograd::linear(ctx, L.o), L.post_norm, eps, &x);
         Variable h = autograd::swiglu(autograd::linear(b, L.gate_up));
-        x = autograd::add(x, autograd::linear(h, L.down));
+        const Variable& next = l + 1 < layers_.size() ? layers_[l + 1].in_norm : final_norm_;
+        a = autograd::add_rms_norm(x, autograd::linear(h, L.down), next, eps, &x);
     }
-    x = autograd::rms_norm(x, final_norm_, eps);
     // tied LM head: the embedding matrix read the other way round (Model.cpp:253-254)
-    return autograd::linear(x, embed_);
+    return autograd::linear(a, embed_);
 }
 
 } // namespace veda::train

@@ -233,8 +233,9 @@ void Trainer::step(const Tensor& ids, const Tensor& targets)
 {
     profile::HostScope whole("host:step");
     {
+        // the backward overwrites each gradient on its first write, so no arena-wide memset
         profile::HostScope scope("host:zero_grad");
-        model_->zero_grad();
+        model_->mark_grads_zero();
     }
     Variable logits = [&] {
         profile::HostScope scope("host:forward");
@@ -252,6 +253,7 @@ void Trainer::step(const Tensor& ids, const Tensor& targets)
         profile::HostScope scope("host:backward");
         loss.backward(options);
     }
+    model_->clear_untouched_grads();
     if (dp_)
     {
         dp_->finish();

@@ -273,6 +273,22 @@ reduce_partials_kernel(const float* __restrict__ partials, int blocks, int n,
     }
 }
 
+// sum = x + r over rows of n (the residual add of the fused add + norm, when the streaming
+// kernel does not apply)
+template <typename T>
+__global__ void add_rows_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ r,
+                                int64_t ldr, T* __restrict__ sum, int64_t lds, int64_t rows,
+                                int64_t n)
+{
+    const int64_t total = rows * n;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    {
+        const int64_t row = i / n, c = i % n;
+        sum[row * lds + c] = from_f32<T>(to_f32(x[row * ldx + c]) + to_f32(r[row * ldr + c]));
+    }
+}
+
 inline void launch_reduce_partials(const float* partials, int blocks, int n, float* dgamma,
                                    cudaStream_t s)
 {
@@ -1089,8 +1105,9 @@ int launch_rms_fwd(const void* x, int64_t ldx, const void* gamma, void* y, int64
 {
     if constexpr (sizeof(T) == 2)
     {
-        const int rc = rms_fwd_stream(static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(gamma),
-                                      static_cast<bf16*>(y), ldy, rows, n, eps, s);
+        const int rc = rms_fwd_stream(static_cast<const bf16*>(x), ldx, nullptr, 0,
+                                      static_cast<const bf16*>(gamma), static_cast<bf16*>(y), ldy,
+                                      nullptr, 0, rows, n, eps, s);
         if (rc != -1)
         {
             return rc;
@@ -1261,6 +1278,48 @@ extern "C" int veda_rmsnorm_fwd(const void* x, int64_t ldx, const void* gamma, v
     return dtype == VEDA_BF16
                ? launch_rms_fwd<bf16>(x, ldx, gamma, y, ldy, rows, n, eps, stream)
                : launch_rms_fwd<float>(x, ldx, gamma, y, ldy, rows, n, eps, stream);
+}
+
+extern "C" int veda_add_rmsnorm_fwd(const void* x, int64_t ldx, const void* r, int64_t ldr,
+                                    const void* gamma, void* sum, int64_t lds, void* y,
+                                    int64_t ldy, int64_t rows, int64_t n, float eps, int dtype,
+                                    veda_stream_t stream)
+{
+    VEDA_REQUIRE(valid_dtype(dtype), "unknown dtype");
+    VEDA_REQUIRE(rows >= 0 && n > 0 && ldx >= n && ldr >= n && lds >= n && ldy >= n,
+                 "bad shape or leading dimension");
+    VEDA_REQUIRE(n <= (1 << 24), "row too long");
+    if (rows == 0)
+    {
+        return VEDA_OK;
+    }
+    VEDA_REQUIRE(x != nullptr && r != nullptr && sum != nullptr && y != nullptr, "null pointer");
+    if (dtype == VEDA_BF16)
+    {
+        const int rc = rms_fwd_stream(static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(r), ldr,
+                                      static_cast<const bf16*>(gamma), static_cast<bf16*>(y), ldy,
+                                      static_cast<bf16*>(sum), lds, rows, n, eps, stream);
+        if (rc != -1)
+        {
+            return rc;
+        }
+    }
+    const unsigned grid = grid_for(rows * n, 256);
+    if (dtype == VEDA_BF16)
+        add_rows_kernel<bf16><<<grid, 256, 0, stream>>>(static_cast<const bf16*>(x), ldx,
+                                                        static_cast<const bf16*>(r), ldr,
+                                                        static_cast<bf16*>(sum), lds, rows, n);
+    else
+        add_rows_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(x), ldx,
+                                                         static_cast<const float*>(r), ldr,
+                                                         static_cast<float*>(sum), lds, rows, n);
+    count_launch();
+    const int rc = check_launch("veda_add_rmsnorm_fwd");
+    if (rc != VEDA_OK)
+    {
+        return rc;
+    }
+    return veda_rmsnorm_fwd(sum, lds, gamma, y, ldy, rows, n, eps, dtype, stream);
 }
 
 extern "C" int veda_rmsnorm_bwd(const void* x, int64_t ldx, const void* gamma, const void* dy,

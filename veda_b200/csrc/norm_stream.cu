@@ -83,12 +83,15 @@ __device__ __forceinline__ void produce(uint8_t* ring, uint64_t* full, uint64_t*
     }
 }
 
-template <int CH>
+// NIN = 2: the rows normalised are s = x + r (rounded to bf16, as the residual add stores it),
+// and s is written out as well.
+template <int CH, int NIN>
 __global__ void __launch_bounds__(kThreadsStream, 1)
-rms_fwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ gamma,
-                      bf16* __restrict__ y, int64_t ldy, int64_t rows, float eps, int* status)
+rms_fwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ r, int64_t ldr,
+                      const bf16* __restrict__ gamma, bf16* __restrict__ y, int64_t ldy,
+                      bf16* __restrict__ sum, int64_t lds, int64_t rows, float eps, int* status)
 {
-    using R = Ring<CH, 1>;
+    using R = Ring<CH, NIN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* ring = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
@@ -116,9 +119,9 @@ rms_fwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __res
     {
         if (lane == 0)
         {
-            const bf16* const src[3] = {x, nullptr, nullptr};
-            const int64_t ld[3] = {ldx, 0, 0};
-            produce<CH, 1>(ring, full, empty, src, ld, rows, status, abort);
+            const bf16* const src[3] = {x, r, nullptr};
+            const int64_t ld[3] = {ldx, ldr, 0};
+            produce<CH, NIN>(ring, full, empty, src, ld, rows, status, abort);
         }
         return;
     }
@@ -132,10 +135,30 @@ rms_fwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __res
         const int64_t row = q * kRows + w;
         if (row < rows)
         {
-            const uint8_t* src = ring + st * R::STAGE + w * R::ROW;
+            const uint8_t* src = ring + st * R::STAGE + w * NIN * R::ROW;
             uint4 xr[CH];
 #pragma unroll
             for (int c = 0; c < CH; ++c) xr[c] = *reinterpret_cast<const uint4*>(src + (c * 32 + lane) * 16);
+            if constexpr (NIN == 2)
+            {
+#pragma unroll
+                for (int c = 0; c < CH; ++c)
+                {
+                    const uint4 rr = *reinterpret_cast<const uint4*>(src + R::ROW + (c * 32 + lane) * 16);
+                    float a[8], b[8];
+                    unpack8(xr[c], a);
+                    unpack8(rr, b);
+                    uint32_t w4[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                    {
+                        const __nv_bfloat162 t = __floats2bfloat162_rn(a[2 * j] + b[2 * j], a[2 * j + 1] + b[2 * j + 1]);
+                        w4[j] = *reinterpret_cast<const uint32_t*>(&t);
+                    }
+                    xr[c] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    *reinterpret_cast<uint4*>(sum + row * lds + (c * 32 + lane) * 8) = xr[c];
+                }
+            }
             float ss = 0.0f;
 #pragma unroll
             for (int c = 0; c < CH; ++c)
@@ -303,23 +326,24 @@ rms_bwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __res
 
 bool rows_aligned(const void* p, int64_t ld) { return aligned16(p) && ld % 8 == 0; }
 
-template <int CH>
-int launch_fwd(const bf16* x, int64_t ldx, const bf16* gamma, bf16* y, int64_t ldy, int64_t rows,
-               float eps, cudaStream_t s)
+template <int CH, int NIN>
+int launch_fwd(const bf16* x, int64_t ldx, const bf16* r, int64_t ldr, const bf16* gamma, bf16* y,
+               int64_t ldy, bf16* sum, int64_t lds, int64_t rows, float eps, cudaStream_t s)
 {
-    using R = Ring<CH, 1>;
+    using R = Ring<CH, NIN>;
     static int configured = -1;
     int device = 0;
     cudaGetDevice(&device);
     if (configured != device)
     {
-        cudaFuncSetAttribute(rms_fwd_stream_kernel<CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, R::SMEM);
+        cudaFuncSetAttribute(rms_fwd_stream_kernel<CH, NIN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             R::SMEM);
         configured = device;
     }
     const int64_t chunks = (rows + kRows - 1) / kRows;
     const unsigned grid = static_cast<unsigned>(chunks < compute_sms() ? chunks : compute_sms());
-    rms_fwd_stream_kernel<CH><<<grid, kThreadsStream, R::SMEM, s>>>(x, ldx, gamma, y, ldy, rows, eps,
-                                                                    device_status_ptr());
+    rms_fwd_stream_kernel<CH, NIN><<<grid, kThreadsStream, R::SMEM, s>>>(
+        x, ldx, r, ldr, gamma, y, ldy, sum, lds, rows, eps, device_status_ptr());
     count_launch();
     return check_launch("veda_rmsnorm_fwd (streaming)");
 }
@@ -352,19 +376,35 @@ int launch_bwd(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* dy, in
 
 } // namespace
 
-int rms_fwd_stream(const bf16* x, int64_t ldx, const bf16* gamma, bf16* y, int64_t ldy,
-                   int64_t rows, int64_t n, float eps, cudaStream_t s)
+int rms_fwd_stream(const bf16* x, int64_t ldx, const bf16* r, int64_t ldr, const bf16* gamma,
+                   bf16* y, int64_t ldy, bf16* sum, int64_t lds, int64_t rows, int64_t n, float eps,
+                   cudaStream_t s)
 {
     if (!rows_aligned(x, ldx) || !rows_aligned(y, ldy) || (gamma != nullptr && !aligned16(gamma)))
     {
         return -1;
     }
+    if (r != nullptr)
+    {
+        if (sum == nullptr || !rows_aligned(r, ldr) || !rows_aligned(sum, lds))
+        {
+            return -1;
+        }
+        switch (n)
+        {
+        case 256: return launch_fwd<1, 2>(x, ldx, r, ldr, gamma, y, ldy, sum, lds, rows, eps, s);
+        case 512: return launch_fwd<2, 2>(x, ldx, r, ldr, gamma, y, ldy, sum, lds, rows, eps, s);
+        case 1024: return launch_fwd<4, 2>(x, ldx, r, ldr, gamma, y, ldy, sum, lds, rows, eps, s);
+        case 2048: return launch_fwd<8, 2>(x, ldx, r, ldr, gamma, y, ldy, sum, lds, rows, eps, s);
+        default: return -1;
+        }
+    }
     switch (n)
     {
-    case 256: return launch_fwd<1>(x, ldx, gamma, y, ldy, rows, eps, s);
-    case 512: return launch_fwd<2>(x, ldx, gamma, y, ldy, rows, eps, s);
-    case 1024: return launch_fwd<4>(x, ldx, gamma, y, ldy, rows, eps, s);
-    case 2048: return launch_fwd<8>(x, ldx, gamma, y, ldy, rows, eps, s);
+    case 256: return launch_fwd<1, 1>(x, ldx, nullptr, 0, gamma, y, ldy, nullptr, 0, rows, eps, s);
+    case 512: return launch_fwd<2, 1>(x, ldx, nullptr, 0, gamma, y, ldy, nullptr, 0, rows, eps, s);
+    case 1024: return launch_fwd<4, 1>(x, ldx, nullptr, 0, gamma, y, ldy, nullptr, 0, rows, eps, s);
+    case 2048: return launch_fwd<8, 1>(x, ldx, nullptr, 0, gamma, y, ldy, nullptr, 0, rows, eps, s);
     default: return -1;
     }
 }

@@ -143,6 +143,8 @@ adamw_kernel(float* __restrict__ master, float* __restrict__ m, float* __restric
              const double* __restrict__ sumsq, AdamArgs a, bool vec)
 {
     const float clip = clip_scale(sumsq, a.max_norm, a.grad_scale);
+    // an unscaled gradient is already what the write-back would store
+    const bool store_g = a.write_grad && (clip != 1.0f || a.grad_scale != 1.0f);
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     const int64_t n4 = vec ? n / 4 : 0;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
@@ -174,7 +176,7 @@ adamw_kernel(float* __restrict__ master, float* __restrict__ m, float* __restric
         reinterpret_cast<float4*>(master)[i] = w4;
         reinterpret_cast<float4*>(m)[i] = m4;
         reinterpret_cast<float4*>(v)[i] = v4;
-        if (a.write_grad)
+        if (store_g)
         {
             reinterpret_cast<float4*>(g)[i] = g4;
         }
@@ -205,7 +207,7 @@ adamw_kernel(float* __restrict__ master, float* __restrict__ m, float* __restric
         master[i] = w;
         m[i] = mm;
         v[i] = vv;
-        if (a.write_grad)
+        if (store_g)
         {
             g[i] = gj;
         }
