@@ -5,7 +5,9 @@
     python bench.py --impl reference ...   (the reference's own CPU implementation)
 
 One step = one full training step of the named config on one synthetic micro-batch per GPU
-(data-parallel, NCCL all-reduce of 25 MB gradient buckets overlapped with the backward), inputs
+(data-parallel: 25 MB gradient buckets reduce-scattered by NCCL while the backward runs, the
+optimizer state sharded across the ranks and the updated weights all-gathered; --dp allreduce
+keeps the optimizer replicated and all-reduces the buckets instead), inputs
 uniform random token ids with shifted-by-one targets. Prints one JSON line (rank 0).
 """
 from __future__ import annotations
@@ -203,7 +205,7 @@ def run_veda(args):
     if world > 1:
         obj = [TA.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
-        tr.init_dp(obj[0], rank, world, 25 << 20)
+        tr.init_dp(obj[0], rank, world, 25 << 20, sharded=args.dp == "sharded")
 
     # synthetic batches (per rank, per step), pinned on the host and resident on the device
     nb = 4
@@ -296,7 +298,9 @@ def run_veda(args):
         "config": {"workload": args.workload, "model": args.workload, "global_batch": B * world,
                    "micro_batch": B, "seq_len": T, "parallelism": f"dp{world}",
                    "params": tr.n, "l2": "inputs and the step's working set exceed L2",
-                   "buckets_mb": 25},
+                   "buckets_mb": 25,
+                   "optimizer_state": ("sharded (ZeRO-1)" if world > 1 and args.dp == "sharded"
+                                       else "replicated")},
         "mfu_model_tflops": model_flops_per_token(c, T) * value / 1e12,
         "roofline": {"bound": "tensor", "kernel": "tcgen05 GEMM (gemm_fwd + gemm_bwd: dX beside dW)",
                      "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s",
@@ -349,6 +353,9 @@ def main():
     ap.add_argument("--impl", default="veda", choices=["veda", "reference"])
     ap.add_argument("--workload", default="qwen3-0.6b", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dp", default="sharded", choices=["sharded", "allreduce"],
+                    help="N > 1: optimizer state sharded across ranks (reduce-scatter + all-gather) "
+                         "or replicated (all-reduce)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -45,6 +45,7 @@ public:
     void zero_grad();
 
     size_t steps() const noexcept { return steps_; }
+    const AdamWConfig& config() const noexcept { return config_; }
     const std::vector<autograd::Variable>& parameters() const noexcept { return parameters_; }
     // fp32 master weights of parameter i (the value itself for fp32 parameters).
     core::Tensor master(size_t i) const { return masters_[i]; }

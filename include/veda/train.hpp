@@ -79,6 +79,10 @@ public:
     const core::Tensor& value_arena() const noexcept { return values_; }
     const core::Tensor& grad_arena() const noexcept { return grads_; }
     size_t parameter_count() const noexcept { return total_; }
+    // Elements the arenas hold: parameter_count() rounded up to a multiple of kArenaAlign, so a
+    // data-parallel job of up to 8 ranks can cut them into equal shards of whole 16-byte rows.
+    static constexpr size_t kArenaAlign = 8 * 840;   // 8 x lcm(1, ..., 8)
+    size_t arena_length() const noexcept { return arena_len_; }
     // Clears the whole gradient arena in one memset and marks every leaf's gradient as zero.
     void zero_grad();
     // zero_grad without the memset: every leaf is only marked as holding zeros, so the backward's
@@ -95,6 +99,7 @@ private:
     core::DType dtype_;
     core::Tensor values_, grads_;
     size_t total_ = 0;
+    size_t arena_len_ = 0;
     std::vector<autograd::Variable> parameters_;
     std::vector<std::string> names_;
     std::vector<GraphLeaf> graph_leaves_;
@@ -124,8 +129,22 @@ public:
 
     // One process per GPU: NCCL communicator from a unique id shared by the caller; gradients
     // are all-reduced in buckets of `bucket_bytes` as soon as the backward finishes them.
-    void init_data_parallel(const void* nccl_unique_id, int rank, int world, size_t bucket_bytes);
+    // sharded: the optimizer state is split across the ranks instead (ZeRO stage 1): each bucket
+    // is reduce-scattered, every rank clips and updates its shard of every bucket, and the
+    // updated weights are all-gathered. The host-side reads of the full master weights and
+    // gradients (read_master_weights / read_gradients) are then collective.
+    void init_data_parallel(const void* nccl_unique_id, int rank, int world, size_t bucket_bytes,
+                            bool sharded = false);
     int world() const noexcept;
+    bool sharded() const noexcept;
+    // Device pointer of the fp32 master weights in arena order (the value arena for fp32).
+    float* master_weights() noexcept;
+    // Brings master_weights() (and, sharded, the gradient arena) up to date on every rank;
+    // collective when sharded, a no-op otherwise.
+    void gather_master_weights();
+    void gather_gradients();
+    // After master_weights() was written from the host: refresh this rank's shard of it.
+    void master_weights_changed();
 
     // One training step on device-resident ids/targets (int64 [B*T]); asynchronous.
     void step(const core::Tensor& ids, const core::Tensor& targets);

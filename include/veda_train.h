@@ -46,7 +46,9 @@ int veda_trainer_destroy(veda_trainer* t);
 int64_t veda_trainer_param_count(const veda_trainer* t);
 /* Host fp32 flat vectors in parameter order. set_params writes the master weights (and their
  * bf16 rounding into the model in bf16 mode); get_params reads the master weights; get_grads
- * reads the last step's averaged pre-clip gradients. */
+ * reads the last step's pre-clip gradients, summed over the data-parallel ranks. With a sharded
+ * optimizer (veda_trainer_init_dp_sharded) get_params and get_grads are collective: every rank
+ * calls them together. */
 int veda_trainer_set_params(veda_trainer* t, const float* host);
 int veda_trainer_get_params(veda_trainer* t, float* host);
 int veda_trainer_get_grads(veda_trainer* t, float* host);
@@ -55,6 +57,13 @@ int veda_trainer_get_grads(veda_trainer* t, float* host);
 int veda_nccl_unique_id(void* out128);
 int veda_trainer_init_dp(veda_trainer* t, const void* unique_id128, int rank, int world,
                          size_t bucket_bytes);
+/* The same with the optimizer state sharded across the ranks (ZeRO stage 1; no reference
+ * counterpart: the reference trains on one CPU, AdamW.cpp:38-93 and Clip.cpp:12-61 give the
+ * arithmetic): buckets are reduce-scattered, each rank clips (global norm from one all-reduced
+ * sum of squares) and updates its 1/world of the parameters, and the updated weights are
+ * all-gathered. world <= 8. */
+int veda_trainer_init_dp_sharded(veda_trainer* t, const void* unique_id128, int rank, int world,
+                                 size_t bucket_bytes);
 
 /* One step from host ids/targets (int64 [batch*seq_len], targets = next ids); copies them in,
  * steps and reads back loss and pre-clip grad norm (synchronous). */

@@ -4,7 +4,8 @@ Each rank trains the Qwen3-shaped bf16 decoder through the C++ trainer on its ow
 (B 2 x T 128) with the library's NCCL bucketed all-reduce (small 1 MB buckets, so many are in
 flight during the backward). Rank 0 compares the averaged gradient with the oracle's gradient of
 the full batch (both micro-batches, B 4) and every rank checks that the updated weights are the
-same on both ranks."""
+same on both ranks. The same step with the optimizer state sharded across the ranks must give the
+same gradients, norm and weights."""
 import datetime
 import os
 import sys
@@ -58,7 +59,33 @@ def main():
         assert worst <= 2e-2, worst
         assert abs(norm - rnorm) <= 2e-2 * rnorm, (norm, rnorm)
         print(f"DP OK worst grad err {worst:.2e} norm {norm:.4f} vs {rnorm:.4f}", flush=True)
+    # The same step with the optimizer state sharded across the ranks (reduce-scatter, per-rank
+    # clip + AdamW on 1/world of the parameters, all-gather of the updated weights): the same
+    # gradient sums, norm and updated weights as the all-reduce run above.
+    ts = TA.Trainer(cfg, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, max_norm=1.0,
+                    dtype=1, batch=B, seq_len=T, seed=3)
+    ts.set_params(np.concatenate([p.ravel() for p in params]))
+    uid = [TA.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    ts.init_dp(uid[0], rank, world, 1 << 20, sharded=True)
+    for step in range(2):
+        l_s, n_s = ts.step_host(ids[mine], tg[mine])
+        if step == 0:
+            assert abs(l_s - loss) <= 1e-6 * abs(loss), (l_s, loss)
+            assert abs(n_s - norm) <= 1e-5 * norm, (n_s, norm)
+            g_s = ts.get_grads()
+            assert np.max(np.abs(g_s - grads_sum)) <= 1e-6 * np.max(np.abs(grads_sum)), "gradients"
+            w_s = ts.get_params()
+            assert np.max(np.abs(w_s - w)) <= 1e-5, np.max(np.abs(w_s - w))
+    # the second step ran on the all-gathered bf16 weights: identical on every rank
+    w2 = torch.from_numpy(ts.get_params().astype(np.float64))
+    w20 = w2.clone()
+    dist.broadcast(w20, src=0)
+    assert torch.equal(w2, w20), "sharded ranks diverged"
+    if rank == 0:
+        print(f"SHARDED OK loss {l_s:.4f}", flush=True)
     dist.barrier()
+    ts.close()
     t.close()
     dist.destroy_process_group()
 

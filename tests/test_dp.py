@@ -130,3 +130,4 @@ def test_nccl_two_gpus_match_full_batch():
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=str(ROOT))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "DP OK" in r.stdout, r.stdout[-2000:]
+    assert "SHARDED OK" in r.stdout, r.stdout[-2000:]

@@ -123,8 +123,9 @@ TinyTransformer::TinyTransformer(ModelConfig config, uint64_t seed, DType dtype)
         offsets.push_back(total_);
         total_ += s.shape.size();
     }
-    values_ = Tensor::empty(Shape({total_}), dtype_);
-    grads_ = Tensor(Shape({total_}), DType::F32);
+    arena_len_ = (total_ + kArenaAlign - 1) / kArenaAlign * kArenaAlign;
+    values_ = Tensor(Shape({arena_len_}), dtype_);
+    grads_ = Tensor(Shape({arena_len_}), DType::F32);
     for (size_t i = 0; i < specs.size(); ++i)
     {
         Tensor v = Tensor::view(values_.storage(), offsets[i], specs[i].shape, dtype_);

@@ -59,11 +59,7 @@ cudaStream_t cs() { return reinterpret_cast<cudaStream_t>(veda::current_stream()
 
 // The fp32 flat vector of master weights: the model's values in fp32 mode, AdamW's master arena
 // in bf16 mode (both contiguous in parameter order).
-void* master_base(veda::train::Trainer& t)
-{
-    return t.model().dtype() == veda::core::DType::F32 ? t.model().value_arena().data_ptr()
-                                                       : t.optimizer().master(0).data_ptr();
-}
+void* master_base(veda::train::Trainer& t) { return t.master_weights(); }
 } // namespace
 
 extern "C" {
@@ -139,6 +135,7 @@ int veda_trainer_set_params(veda_trainer* t, const float* host)
                                          static_cast<int64_t>(n), veda::current_stream()),
                         "veda_trainer_set_params");
         }
+        tr.master_weights_changed();
         cuda_check(cudaStreamSynchronize(cs()), "veda_trainer_set_params");
     });
 }
@@ -147,6 +144,7 @@ int veda_trainer_get_params(veda_trainer* t, float* host)
 {
     return guarded([&] {
         auto& tr = *t->impl;
+        tr.gather_master_weights();
         cuda_check(cudaMemcpyAsync(host, master_base(tr),
                                    tr.model().parameter_count() * sizeof(float),
                                    cudaMemcpyDeviceToHost, cs()),
@@ -159,6 +157,7 @@ int veda_trainer_get_grads(veda_trainer* t, float* host)
 {
     return guarded([&] {
         auto& tr = *t->impl;
+        tr.gather_gradients();
         cuda_check(cudaMemcpyAsync(host, tr.model().grad_arena().data_ptr(),
                                    tr.model().parameter_count() * sizeof(float),
                                    cudaMemcpyDeviceToHost, cs()),
@@ -184,6 +183,13 @@ int veda_trainer_init_dp(veda_trainer* t, const void* unique_id128, int rank, in
                          size_t bucket_bytes)
 {
     return guarded([&] { t->impl->init_data_parallel(unique_id128, rank, world, bucket_bytes); });
+}
+
+int veda_trainer_init_dp_sharded(veda_trainer* t, const void* unique_id128, int rank, int world,
+                                 size_t bucket_bytes)
+{
+    return guarded(
+        [&] { t->impl->init_data_parallel(unique_id128, rank, world, bucket_bytes, true); });
 }
 
 int veda_trainer_step_host(veda_trainer* t, const int64_t* ids, const int64_t* targets,

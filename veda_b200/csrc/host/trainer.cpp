@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <stdexcept>
@@ -52,7 +53,8 @@ void nccl_check(ncclResult_t r, const char* what)
 class DataParallel
 {
 public:
-    DataParallel(const void* unique_id, int rank, int world) : rank_(rank), world_(world)
+    DataParallel(const void* unique_id, int rank, int world, bool sharded)
+        : rank_(rank), world_(world), sharded_(sharded)
     {
         ncclUniqueId id;
         std::memcpy(&id, unique_id, sizeof(id));
@@ -64,6 +66,7 @@ public:
         cuda_check(cudaStreamCreateWithPriority(&stream_, cudaStreamNonBlocking, greatest),
                    "comm stream");
         cuda_check(cudaEventCreateWithFlags(&done_, cudaEventDisableTiming), "comm event");
+        cuda_check(cudaEventCreateWithFlags(&main_ready_, cudaEventDisableTiming), "comm event");
     }
 
     ~DataParallel()
@@ -73,6 +76,7 @@ public:
             cudaEventDestroy(b.ready);
         }
         cudaEventDestroy(done_);
+        cudaEventDestroy(main_ready_);
         if (comm_ != nullptr)
         {
             ncclCommDestroy(comm_);
@@ -81,16 +85,27 @@ public:
     }
 
     // Buckets of `bucket_bytes` cut from the end of the arena (the backward produces the last
-    // parameters first), each waiting for every graph leaf that overlaps it.
-    void attach(TinyTransformer& model, size_t bucket_bytes)
+    // parameters first), each waiting for every graph leaf that overlaps it. Sharded, every
+    // bucket is a whole number of 16-byte rows per rank, and rank r owns the r-th of the world
+    // equal parts of each bucket; its parts, in arena order, make up its shard.
+    void attach(TinyTransformer& model, size_t bucket_bytes, const float* master, size_t steps)
     {
         arena_ = static_cast<float*>(model.grad_arena().data_ptr());
-        const size_t total = model.parameter_count();
-        const size_t per = std::max<size_t>(1, bucket_bytes / sizeof(float));
-        for (size_t end = total; end > 0;)
+        values_ = model.value_arena().data_ptr();
+        bf16_ = model.dtype() == DType::BF16;
+        params_ = model.parameter_count();
+        total_ = sharded_ ? model.arena_length() : params_;
+        const size_t unit = sharded_ ? 8 * static_cast<size_t>(world_) : 1;
+        if (total_ % unit != 0)
+        {
+            throw std::invalid_argument("DataParallel: the arena does not split into " +
+                                        std::to_string(world_) + " shards");
+        }
+        const size_t per = std::max<size_t>(unit, bucket_bytes / sizeof(float) / unit * unit);
+        for (size_t end = total_; end > 0;)
         {
             const size_t begin = end > per ? end - per : 0;
-            Bucket b{begin, end, 0, 0, false, nullptr};
+            Bucket b{begin, end, 0, 0, 0, false, nullptr};
             cuda_check(cudaEventCreateWithFlags(&b.ready, cudaEventDisableTiming), "bucket event");
             buckets_.push_back(b);
             end = begin;
@@ -106,6 +121,51 @@ public:
                     list.push_back(i);
                     buckets_[i].waiting += 1;
                 }
+            }
+        }
+        if (!sharded_)
+        {
+            return;
+        }
+        // shard offsets in arena order (buckets_ runs from the end of the arena)
+        size_t at = 0;
+        for (size_t i = buckets_.size(); i-- > 0;)
+        {
+            buckets_[i].shard_at = at;
+            at += (buckets_[i].end - buckets_[i].begin) / world_;
+        }
+        shard_ = total_ / world_;
+        const Shape sh({shard_});
+        g_s_ = Tensor(sh, DType::F32);
+        master_s_ = Tensor(sh, DType::F32);
+        m_s_ = Tensor(sh, DType::F32);
+        v_s_ = Tensor(sh, DType::F32);
+        if (bf16_)
+        {
+            lowp_s_ = Tensor(Shape({shard_}), DType::BF16);
+        }
+        sumsq_ = Tensor(Shape({2}), DType::F32);   // one double
+        const size_t ws = veda_sumsq_workspace(static_cast<int64_t>(shard_));
+        ws_ = Tensor::empty(Shape({(ws + 3) / 4 + 1}), DType::F32);
+        steps_ = steps;
+        load_master(master);
+    }
+
+    // This rank's parts of the arena-ordered fp32 master weights (`params_` of them; the padding
+    // past them stays zero) into its shard.
+    void load_master(const float* master)
+    {
+        float* dst = static_cast<float*>(master_s_.data_ptr());
+        for (const Bucket& b : buckets_)
+        {
+            const size_t len = (b.end - b.begin) / world_;
+            const size_t lo = b.begin + static_cast<size_t>(rank_) * len;
+            const size_t hi = std::min(lo + len, params_);
+            if (hi > lo)
+            {
+                cuda_check(cudaMemcpyAsync(dst + b.shard_at, master + lo, (hi - lo) * sizeof(float),
+                                           cudaMemcpyDeviceToDevice, cs()),
+                           "shard master");
             }
         }
     }
@@ -148,17 +208,110 @@ public:
                 launch(i);
             }
         }
-        cuda_check(cudaEventRecord(done_, stream_), "comm done");
-        cuda_check(cudaStreamWaitEvent(cs(), done_, 0), "comm wait");
+        join_comm();
         veda_set_reserved_sms(0);
     }
 
+    // Sharded step: global norm of the averaged gradient (a sum over the shards), clip + AdamW on
+    // this rank's shard (optim::AdamW's arithmetic, AdamW.cpp:38-93), then the updated weights
+    // of every bucket all-gathered into the value arena.
+    void update(const optim::AdamWConfig& c, float max_norm)
+    {
+        ++steps_;
+        const double bias1 = 1.0 - std::pow(static_cast<double>(c.beta1), static_cast<double>(steps_));
+        const double bias2 = 1.0 - std::pow(static_cast<double>(c.beta2), static_cast<double>(steps_));
+        double* ss = static_cast<double*>(sumsq_.data_ptr());
+        float* g = static_cast<float*>(g_s_.data_ptr());
+        float* master = static_cast<float*>(master_s_.data_ptr());
+        check(veda_sumsq(g, static_cast<int64_t>(shard_), ss, 0, ws_.data_ptr(), ws_.numel() * 4,
+                         current_stream()),
+              "sharded clip (norm)");
+        fork_comm();
+        nccl_check(ncclAllReduce(ss, ss, 1, ncclFloat64, ncclSum, comm_, stream_), "norm all-reduce");
+        join_comm();
+        check(veda_adamw_step(master, static_cast<float*>(m_s_.data_ptr()),
+                              static_cast<float*>(v_s_.data_ptr()), g,
+                              bf16_ ? lowp_s_.data_ptr() : nullptr, static_cast<int64_t>(shard_),
+                              c.learning_rate, c.beta1, c.beta2, c.eps, c.weight_decay, bias1, bias2,
+                              ss, max_norm, 1.0f / static_cast<float>(world_), 0, current_stream()),
+              "sharded AdamW");
+        fork_comm();
+        nccl_check(ncclGroupStart(), "weight all-gather");
+        for (const Bucket& b : buckets_)
+        {
+            const size_t len = (b.end - b.begin) / world_;
+            if (bf16_)
+            {
+                nccl_check(ncclAllGather(static_cast<const uint16_t*>(lowp_s_.data_ptr()) + b.shard_at,
+                                         static_cast<uint16_t*>(values_) + b.begin, len, ncclBfloat16,
+                                         comm_, stream_),
+                           "weight all-gather");
+            }
+            else
+            {
+                nccl_check(ncclAllGather(master + b.shard_at, static_cast<float*>(values_) + b.begin, len,
+                                         ncclFloat, comm_, stream_),
+                           "weight all-gather");
+            }
+        }
+        nccl_check(ncclGroupEnd(), "weight all-gather");
+        join_comm();
+    }
+
+    // Pre-clip norm of the averaged gradient of the last sharded step (synchronises).
+    float grad_norm()
+    {
+        double ss = 0.0;
+        cuda_check(cudaMemcpyAsync(&ss, sumsq_.data_ptr(), sizeof(double), cudaMemcpyDeviceToHost, cs()),
+                   "norm read");
+        cuda_check(cudaStreamSynchronize(cs()), "norm read");
+        return static_cast<float>(std::sqrt(ss) / static_cast<double>(world_));
+    }
+
+    // Collective: every rank's reduced gradient parts into every rank's gradient arena (which
+    // then holds the summed gradient, as after an all-reduce).
+    void gather_gradients()
+    {
+        fork_comm();
+        nccl_check(ncclGroupStart(), "gradient all-gather");
+        for (const Bucket& b : buckets_)
+        {
+            nccl_check(ncclAllGather(static_cast<const float*>(g_s_.data_ptr()) + b.shard_at, arena_ + b.begin,
+                                     (b.end - b.begin) / world_, ncclFloat, comm_, stream_),
+                       "gradient all-gather");
+        }
+        nccl_check(ncclGroupEnd(), "gradient all-gather");
+        join_comm();
+    }
+
+    // Collective: the full master weights, in arena order, into `master` (params_ elements).
+    void gather_master(float* master)
+    {
+        Tensor full = Tensor::empty(Shape({total_}), DType::F32);
+        float* f = static_cast<float*>(full.data_ptr());
+        fork_comm();
+        nccl_check(ncclGroupStart(), "master all-gather");
+        for (const Bucket& b : buckets_)
+        {
+            nccl_check(ncclAllGather(static_cast<const float*>(master_s_.data_ptr()) + b.shard_at, f + b.begin,
+                                     (b.end - b.begin) / world_, ncclFloat, comm_, stream_),
+                       "master all-gather");
+        }
+        nccl_check(ncclGroupEnd(), "master all-gather");
+        join_comm();
+        cuda_check(cudaMemcpyAsync(master, f, params_ * sizeof(float), cudaMemcpyDeviceToDevice, cs()),
+                   "master copy");
+        cuda_check(cudaStreamSynchronize(cs()), "master copy");
+    }
+
     int world() const noexcept { return world_; }
+    bool sharded() const noexcept { return sharded_; }
 
 private:
     struct Bucket
     {
         size_t begin, end;
+        size_t shard_at;   // sharded: where this rank's part sits in its shard
         int waiting, pending;
         bool launched;
         cudaEvent_t ready;
@@ -170,9 +323,32 @@ private:
         b.launched = true;
         cuda_check(cudaEventRecord(b.ready, cs()), "bucket ready");
         cuda_check(cudaStreamWaitEvent(stream_, b.ready, 0), "bucket wait");
-        nccl_check(ncclAllReduce(arena_ + b.begin, arena_ + b.begin, b.end - b.begin, ncclFloat,
-                                 ncclSum, comm_, stream_),
-                   "ncclAllReduce");
+        if (sharded_)
+        {
+            nccl_check(ncclReduceScatter(arena_ + b.begin, static_cast<float*>(g_s_.data_ptr()) + b.shard_at,
+                                         (b.end - b.begin) / world_, ncclFloat, ncclSum, comm_, stream_),
+                       "ncclReduceScatter");
+        }
+        else
+        {
+            nccl_check(ncclAllReduce(arena_ + b.begin, arena_ + b.begin, b.end - b.begin, ncclFloat,
+                                     ncclSum, comm_, stream_),
+                       "ncclAllReduce");
+        }
+    }
+
+    // the communication stream waits for the work queued so far on the current stream
+    void fork_comm()
+    {
+        cuda_check(cudaEventRecord(main_ready_, cs()), "comm fork");
+        cuda_check(cudaStreamWaitEvent(stream_, main_ready_, 0), "comm fork");
+    }
+
+    // the current stream waits for the communication queued so far
+    void join_comm()
+    {
+        cuda_check(cudaEventRecord(done_, stream_), "comm done");
+        cuda_check(cudaStreamWaitEvent(cs(), done_, 0), "comm wait");
     }
 
     // SMs left to NCCL during the backward (VEDA_DP_RESERVED_SMS, default 16)
@@ -182,11 +358,15 @@ private:
     }();
     ncclComm_t comm_ = nullptr;
     cudaStream_t stream_ = nullptr;
-    cudaEvent_t done_ = nullptr;
+    cudaEvent_t done_ = nullptr, main_ready_ = nullptr;
     int rank_ = 0, world_ = 1;
+    bool sharded_ = false, bf16_ = false;
     float* arena_ = nullptr;
+    void* values_ = nullptr;
+    size_t params_ = 0, total_ = 0, shard_ = 0, steps_ = 0;
     std::vector<Bucket> buckets_;
     std::unordered_map<autograd::Node*, std::vector<size_t>> leaf_buckets_;
+    Tensor g_s_, master_s_, m_s_, v_s_, lowp_s_, sumsq_, ws_;
 };
 
 Trainer::Trainer(ModelConfig config, optim::AdamWConfig adam, float max_norm, DType dtype,
@@ -212,7 +392,7 @@ Trainer::Trainer(ModelConfig config, optim::AdamWConfig adam, float max_norm, DT
 Trainer::~Trainer() = default;
 
 void Trainer::init_data_parallel(const void* nccl_unique_id, int rank, int world,
-                                 size_t bucket_bytes)
+                                 size_t bucket_bytes, bool sharded)
 {
     if (world < 1 || rank < 0 || rank >= world)
     {
@@ -223,11 +403,43 @@ void Trainer::init_data_parallel(const void* nccl_unique_id, int rank, int world
         dp_.reset();
         return;
     }
-    dp_ = std::make_unique<DataParallel>(nccl_unique_id, rank, world);
-    dp_->attach(*model_, bucket_bytes);
+    dp_ = std::make_unique<DataParallel>(nccl_unique_id, rank, world, sharded);
+    dp_->attach(*model_, bucket_bytes, master_weights(), opt_->steps());
 }
 
 int Trainer::world() const noexcept { return dp_ ? dp_->world() : 1; }
+
+bool Trainer::sharded() const noexcept { return dp_ && dp_->sharded(); }
+
+float* Trainer::master_weights() noexcept
+{
+    return static_cast<float*>(model_->dtype() == DType::F32 ? model_->value_arena().data_ptr()
+                                                             : opt_->master(0).data_ptr());
+}
+
+void Trainer::gather_master_weights()
+{
+    if (sharded() && model_->dtype() != DType::F32)
+    {
+        dp_->gather_master(master_weights());
+    }
+}
+
+void Trainer::gather_gradients()
+{
+    if (sharded())
+    {
+        dp_->gather_gradients();
+    }
+}
+
+void Trainer::master_weights_changed()
+{
+    if (sharded())
+    {
+        dp_->load_master(master_weights());
+    }
+}
 
 void Trainer::step(const Tensor& ids, const Tensor& targets)
 {
@@ -259,10 +471,18 @@ void Trainer::step(const Tensor& ids, const Tensor& targets)
         dp_->finish();
     }
     {
-        const double n = static_cast<double>(model_->parameter_count());
+        const double n = static_cast<double>(model_->parameter_count()) /
+                         static_cast<double>(sharded() ? world() : 1);
         profile::Scope scope("adamw", 0.0,
                              n * (4.0 + 16.0 + 12.0 + (model_->dtype() == DType::BF16 ? 2.0 : 0.0)));
-        opt_->step_clipped(max_norm_, 1.0f / static_cast<float>(world()));
+        if (sharded())
+        {
+            dp_->update(opt_->config(), max_norm_);
+        }
+        else
+        {
+            opt_->step_clipped(max_norm_, 1.0f / static_cast<float>(world()));
+        }
     }
     cuda_check(cudaMemcpyAsync(loss_.data_ptr(), loss.value().data_ptr(), sizeof(float),
                                cudaMemcpyDeviceToDevice, cs()),
@@ -288,7 +508,7 @@ StepStats Trainer::last_stats()
     cuda_check(cudaMemcpyAsync(&s.loss, loss_.data_ptr(), sizeof(float), cudaMemcpyDeviceToHost,
                                cs()),
                "loss read");
-    s.grad_norm = opt_->last_grad_norm();   // synchronises
+    s.grad_norm = sharded() ? dp_->grad_norm() : opt_->last_grad_norm();   // synchronises
     autograd::detail::raise_device_flag();
     return s;
 }

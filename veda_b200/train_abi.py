@@ -32,6 +32,7 @@ SIGNATURES = {
     "veda_trainer_get_grads": (_i, [_p, _p]),
     "veda_nccl_unique_id": (_i, [_p]),
     "veda_trainer_init_dp": (_i, [_p, _p, _i, _i, _sz]),
+    "veda_trainer_init_dp_sharded": (_i, [_p, _p, _i, _i, _sz]),
     "veda_trainer_step_host": (_i, [_p, _p, _p, _p, _p]),
     "veda_trainer_step_device": (_i, [_p, _p, _p]),
     "veda_trainer_last_stats": (_i, [_p, _p, _p]),
@@ -109,9 +110,13 @@ class Trainer:
         _check(self.L, self.L.veda_trainer_get_grads(self.h, out.ctypes.data))
         return out
 
-    def init_dp(self, unique_id: bytes, rank: int, world: int, bucket_bytes=25 << 20):
+    def init_dp(self, unique_id: bytes, rank: int, world: int, bucket_bytes=25 << 20,
+                sharded=False):
+        """NCCL data parallelism; sharded=True splits the optimizer state across the ranks
+        (get_params / get_grads then have to be called on every rank together)."""
         buf = C.create_string_buffer(bytes(unique_id), 128)
-        _check(self.L, self.L.veda_trainer_init_dp(self.h, buf, rank, world, bucket_bytes))
+        fn = self.L.veda_trainer_init_dp_sharded if sharded else self.L.veda_trainer_init_dp
+        _check(self.L, fn(self.h, buf, rank, world, bucket_bytes))
 
     def step_host(self, ids: np.ndarray, targets: np.ndarray):
         ids = np.ascontiguousarray(ids, dtype=np.int64)
