@@ -244,6 +244,7 @@ def run_veda(args):
         start.record(stream)
         for i in range(args.steps):
             tr.step_device(dev_ids[i % nb].data_ptr(), dev_tg[i % nb].data_ptr())
+        tr.sync()   # the last step's weight all-gather (sharded optimizer) is inside the region
         stop.record(stream)
         stop.synchronize()
         launches = V.lib().veda_launch_count() - launches0
@@ -267,6 +268,7 @@ def run_veda(args):
         e0.record(stream)
         for i in range(args.steps):
             tr.step_host(host_ids[i % nb].numpy(), host_tg[i % nb].numpy())
+        tr.sync()
         e1.record(stream)
         e1.synchronize()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1))

@@ -16,6 +16,8 @@
 // all-reduce overlapped with the backward, fused clip + AdamW) on one GPU of a data-parallel job.
 #pragma once
 
+#include <functional>
+
 #include "veda/autograd.hpp"
 #include "veda/optim.hpp"
 
@@ -91,6 +93,9 @@ public:
     // the two calls the arena holds the previous step's values.
     void mark_grads_zero();
     void clear_untouched_grads();
+    // Called with an arena range [lo, hi) before the forward first reads the weights in it, so
+    // that a data-parallel step whose updated weights are still arriving waits only for them.
+    void set_weight_gate(std::function<void(size_t, size_t)> gate) { gate_ = std::move(gate); }
 
 private:
     autograd::Variable forward_from(const autograd::Variable& x, size_t batch, size_t length);
@@ -100,6 +105,9 @@ private:
     core::Tensor values_, grads_;
     size_t total_ = 0;
     size_t arena_len_ = 0;
+    std::function<void(size_t, size_t)> gate_;
+    std::pair<size_t, size_t> embed_range_, final_range_;
+    std::vector<std::pair<size_t, size_t>> layer_ranges_;
     std::vector<autograd::Variable> parameters_;
     std::vector<std::string> names_;
     std::vector<GraphLeaf> graph_leaves_;
@@ -139,6 +147,9 @@ public:
     bool sharded() const noexcept;
     // Device pointer of the fp32 master weights in arena order (the value arena for fp32).
     float* master_weights() noexcept;
+    // The current stream waits for all communication the trainer has queued (a sharded step
+    // leaves the all-gather of the updated weights running into the next step's forward).
+    void sync();
     // Brings master_weights() (and, sharded, the gradient arena) up to date on every rank;
     // collective when sharded, a no-op otherwise.
     void gather_master_weights();

@@ -65,6 +65,12 @@ int veda_trainer_init_dp(veda_trainer* t, const void* unique_id128, int rank, in
 int veda_trainer_init_dp_sharded(veda_trainer* t, const void* unique_id128, int rank, int world,
                                  size_t bucket_bytes);
 
+/* The current stream waits for all communication the trainer has queued: a step with a sharded
+ * optimizer returns with the all-gather of its updated weights still running (the next step's
+ * forward waits for each bucket where it first reads it). Call before timing the end of a run or
+ * reading the weights on the device by other means. */
+int veda_trainer_sync(veda_trainer* t);
+
 /* One step from host ids/targets (int64 [batch*seq_len], targets = next ids); copies them in,
  * steps and reads back loss and pre-clip grad norm (synchronous). */
 int veda_trainer_step_host(veda_trainer* t, const int64_t* ids, const int64_t* targets,

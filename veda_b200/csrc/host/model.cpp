@@ -173,10 +173,13 @@ TinyTransformer::TinyTransformer(ModelConfig config, uint64_t seed, DType dtype)
         graph_leaves_.push_back({layer.post_norm, offsets[b + 7], D});
         graph_leaves_.push_back({layer.gate_up, offsets[b + 8], 2 * F * D});
         graph_leaves_.push_back({layer.down, offsets[b + 10], D * F});
+        layer_ranges_.push_back({offsets[b], offsets[b + 10] + D * F});
         layers_.push_back(std::move(layer));
     }
     final_norm_ = parameters_.back();
     graph_leaves_.push_back({final_norm_, offsets.back(), D});
+    embed_range_ = {offsets[0], offsets[0] + specs[0].shape.size()};
+    final_range_ = {offsets.back(), offsets.back() + D};
 }
 
 std::vector<std::pair<std::string, Tensor>> TinyTransformer::named_parameters() const
@@ -246,6 +249,7 @@ Variable TinyTransformer::forward(const std::vector<int64_t>& ids, size_t batch,
                                     std::to_string(length) + " exceeds the context limit " +
                                     std::to_string(config_.max_position_embeddings));
     }
+    if (gate_) gate_(embed_range_.first, embed_range_.second);
     Variable x = autograd::embedding(embed_, ids, Shape({batch * length}));
     return autograd::reshape(forward_from(x, batch, length),
                              Shape({batch, length, config_.vocab_size}));
@@ -257,6 +261,7 @@ Variable TinyTransformer::forward_device(const Tensor& ids, size_t batch, size_t
     {
         throw std::invalid_argument("TinyTransformer::forward: window exceeds the context limit");
     }
+    if (gate_) gate_(embed_range_.first, embed_range_.second);
     Variable x = autograd::embedding_device(embed_, ids);
     return forward_from(x, batch, length);
 }
@@ -275,10 +280,14 @@ Variable TinyTransformer::forward_from(const Variable& x0, size_t B, size_t T)
     // pre-norm residual blocks (Model.cpp:238-249); each residual add is fused with the norm
     // that reads its sum (the next block's input norm, or the final norm)
     Variable x = x0;
+    if (gate_ && layers_.empty()) gate_(final_range_.first, final_range_.second);
+    if (gate_ && !layers_.empty()) gate_(layer_ranges_[0].first, layer_ranges_[0].second);
     Variable a = autograd::rms_norm(x, layers_.empty() ? final_norm_ : layers_[0].in_norm, eps);
     for (size_t l = 0; l < layers_.size(); ++l)
     {
         const Layer& L = layers_[l];
+        if (gate_ && l > 0) gate_(layer_ranges_[l].first, layer_ranges_[l].second);
+        if (gate_ && l + 1 == layers_.size()) gate_(final_range_.first, final_range_.second);
         Variable qkv = autograd::linear(a, L.qkv);
         Variable ctx = autograd::attention(qkv, L.q_norm, L.k_norm, cosines, sines, B, T, H, Hk,
                                            Dh, eps);

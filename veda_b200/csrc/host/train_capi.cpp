@@ -124,6 +124,7 @@ int veda_trainer_set_params(veda_trainer* t, const float* host)
 {
     return guarded([&] {
         auto& tr = *t->impl;
+        tr.sync();   // no weight gather may still be writing the arena
         const size_t n = tr.model().parameter_count();
         void* master = master_base(tr);
         cuda_check(cudaMemcpyAsync(master, host, n * sizeof(float), cudaMemcpyHostToDevice, cs()),
@@ -183,6 +184,11 @@ int veda_trainer_init_dp(veda_trainer* t, const void* unique_id128, int rank, in
                          size_t bucket_bytes)
 {
     return guarded([&] { t->impl->init_data_parallel(unique_id128, rank, world, bucket_bytes); });
+}
+
+int veda_trainer_sync(veda_trainer* t)
+{
+    return guarded([&] { t->impl->sync(); });
 }
 
 int veda_trainer_init_dp_sharded(veda_trainer* t, const void* unique_id128, int rank, int world,

@@ -71,9 +71,11 @@ public:
 
     ~DataParallel()
     {
+        cudaStreamSynchronize(stream_);
         for (Bucket& b : buckets_)
         {
             cudaEventDestroy(b.ready);
+            cudaEventDestroy(b.gathered);
         }
         cudaEventDestroy(done_);
         cudaEventDestroy(main_ready_);
@@ -105,8 +107,9 @@ public:
         for (size_t end = total_; end > 0;)
         {
             const size_t begin = end > per ? end - per : 0;
-            Bucket b{begin, end, 0, 0, 0, false, nullptr};
+            Bucket b{begin, end, 0, 0, 0, false, true, nullptr, nullptr};
             cuda_check(cudaEventCreateWithFlags(&b.ready, cudaEventDisableTiming), "bucket event");
+            cuda_check(cudaEventCreateWithFlags(&b.gathered, cudaEventDisableTiming), "bucket event");
             buckets_.push_back(b);
             end = begin;
         }
@@ -235,10 +238,12 @@ public:
                               c.learning_rate, c.beta1, c.beta2, c.eps, c.weight_decay, bias1, bias2,
                               ss, max_norm, 1.0f / static_cast<float>(world_), 0, current_stream()),
               "sharded AdamW");
+        // the weights are gathered in arena order (the order the next forward reads them) and
+        // not waited for here: the next forward waits for each bucket where it first needs it
         fork_comm();
-        nccl_check(ncclGroupStart(), "weight all-gather");
-        for (const Bucket& b : buckets_)
+        for (size_t i = buckets_.size(); i-- > 0;)
         {
+            Bucket& b = buckets_[i];
             const size_t len = (b.end - b.begin) / world_;
             if (bf16_)
             {
@@ -253,10 +258,75 @@ public:
                                          ncclFloat, comm_, stream_),
                            "weight all-gather");
             }
+            cuda_check(cudaEventRecord(b.gathered, stream_), "bucket gathered");
+            b.gate_open = false;
         }
-        nccl_check(ncclGroupEnd(), "weight all-gather");
-        join_comm();
+        gathering_ = true;
+        if (!overlap_gather_)
+        {
+            sync();
+        }
     }
+
+    // The current stream waits for the gathered weights of every bucket overlapping [lo, hi).
+    // While the gather runs, kernels launched by the forward leave reserved_sms_ SMs to it; the
+    // host launches about as far ahead as the device runs, so the reservation ends at the first
+    // gate after the last bucket has arrived.
+    void gate(size_t lo, size_t hi)
+    {
+        if (!gathering_)
+        {
+            return;
+        }
+        for (Bucket& b : buckets_)
+        {
+            if (!b.gate_open && b.begin < hi && lo < b.end)
+            {
+                cuda_check(cudaStreamWaitEvent(cs(), b.gathered, 0), "weight gate");
+                b.gate_open = true;
+            }
+        }
+        if (reserving_ && cudaEventQuery(buckets_.front().gathered) == cudaSuccess)
+        {
+            veda_set_reserved_sms(0);
+            reserving_ = false;
+        }
+    }
+
+    void begin_forward()
+    {
+        if (gathering_ && forward_reserved_sms_ > 0)
+        {
+            veda_set_reserved_sms(forward_reserved_sms_);
+            reserving_ = true;
+        }
+    }
+
+    void end_forward()
+    {
+        if (gathering_)
+        {
+            sync();   // the forward has waited for every bucket but a padding-only one
+        }
+        if (reserving_)
+        {
+            veda_set_reserved_sms(0);
+            reserving_ = false;
+        }
+    }
+
+    // The current stream waits for everything queued on the communication stream.
+    void sync()
+    {
+        join_comm();
+        gathering_ = false;
+        for (Bucket& b : buckets_)
+        {
+            b.gate_open = true;
+        }
+    }
+
+
 
     // Pre-clip norm of the averaged gradient of the last sharded step (synchronises).
     float grad_norm()
@@ -272,6 +342,7 @@ public:
     // then holds the summed gradient, as after an all-reduce).
     void gather_gradients()
     {
+        sync();
         fork_comm();
         nccl_check(ncclGroupStart(), "gradient all-gather");
         for (const Bucket& b : buckets_)
@@ -287,6 +358,7 @@ public:
     // Collective: the full master weights, in arena order, into `master` (params_ elements).
     void gather_master(float* master)
     {
+        sync();
         Tensor full = Tensor::empty(Shape({total_}), DType::F32);
         float* f = static_cast<float*>(full.data_ptr());
         fork_comm();
@@ -314,7 +386,8 @@ private:
         size_t shard_at;   // sharded: where this rank's part sits in its shard
         int waiting, pending;
         bool launched;
-        cudaEvent_t ready;
+        bool gate_open;    // sharded: the current stream already waits for its gathered weights
+        cudaEvent_t ready, gathered;
     };
 
     void launch(size_t i)
@@ -351,16 +424,27 @@ private:
         cuda_check(cudaStreamWaitEvent(cs(), done_, 0), "comm wait");
     }
 
-    // SMs left to NCCL during the backward (VEDA_DP_RESERVED_SMS, default 16)
+    // SMs left to NCCL during the backward (VEDA_DP_RESERVED_SMS, default 16) and during a
+    // forward that overlaps the weight all-gather (VEDA_DP_FORWARD_RESERVED_SMS, default 0)
     int reserved_sms_ = [] {
         const char* v = std::getenv("VEDA_DP_RESERVED_SMS");
         return v != nullptr ? std::atoi(v) : 16;
+    }();
+    // the weight all-gather runs into the next forward (VEDA_DP_GATHER_OVERLAP, default 1) or
+    // is waited for at the end of the step
+    bool overlap_gather_ = [] {
+        const char* v = std::getenv("VEDA_DP_GATHER_OVERLAP");
+        return v == nullptr || std::atoi(v) != 0;
+    }();
+    int forward_reserved_sms_ = [] {
+        const char* v = std::getenv("VEDA_DP_FORWARD_RESERVED_SMS");
+        return v != nullptr ? std::atoi(v) : 0;
     }();
     ncclComm_t comm_ = nullptr;
     cudaStream_t stream_ = nullptr;
     cudaEvent_t done_ = nullptr, main_ready_ = nullptr;
     int rank_ = 0, world_ = 1;
-    bool sharded_ = false, bf16_ = false;
+    bool sharded_ = false, bf16_ = false, gathering_ = false, reserving_ = false;
     float* arena_ = nullptr;
     void* values_ = nullptr;
     size_t params_ = 0, total_ = 0, shard_ = 0, steps_ = 0;
@@ -405,6 +489,23 @@ void Trainer::init_data_parallel(const void* nccl_unique_id, int rank, int world
     }
     dp_ = std::make_unique<DataParallel>(nccl_unique_id, rank, world, sharded);
     dp_->attach(*model_, bucket_bytes, master_weights(), opt_->steps());
+    if (sharded)
+    {
+        DataParallel* dp = dp_.get();
+        model_->set_weight_gate([dp](size_t lo, size_t hi) { dp->gate(lo, hi); });
+    }
+    else
+    {
+        model_->set_weight_gate({});
+    }
+}
+
+void Trainer::sync()
+{
+    if (dp_)
+    {
+        dp_->sync();
+    }
 }
 
 int Trainer::world() const noexcept { return dp_ ? dp_->world() : 1; }
@@ -437,6 +538,7 @@ void Trainer::master_weights_changed()
 {
     if (sharded())
     {
+        dp_->sync();
         dp_->load_master(master_weights());
     }
 }
@@ -449,10 +551,18 @@ void Trainer::step(const Tensor& ids, const Tensor& targets)
         profile::HostScope scope("host:zero_grad");
         model_->mark_grads_zero();
     }
+    if (dp_)
+    {
+        dp_->begin_forward();
+    }
     Variable logits = [&] {
         profile::HostScope scope("host:forward");
         return model_->forward_device(ids, batch_, length_);
     }();
+    if (dp_)
+    {
+        dp_->end_forward();
+    }
     Variable loss = autograd::cross_entropy_device(logits, targets);
     autograd::BackwardOptions options;
     options.retain_intermediate_grads = false;

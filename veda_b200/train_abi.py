@@ -33,6 +33,7 @@ SIGNATURES = {
     "veda_nccl_unique_id": (_i, [_p]),
     "veda_trainer_init_dp": (_i, [_p, _p, _i, _i, _sz]),
     "veda_trainer_init_dp_sharded": (_i, [_p, _p, _i, _i, _sz]),
+    "veda_trainer_sync": (_i, [_p]),
     "veda_trainer_step_host": (_i, [_p, _p, _p, _p, _p]),
     "veda_trainer_step_device": (_i, [_p, _p, _p]),
     "veda_trainer_last_stats": (_i, [_p, _p, _p]),
@@ -117,6 +118,10 @@ class Trainer:
         buf = C.create_string_buffer(bytes(unique_id), 128)
         fn = self.L.veda_trainer_init_dp_sharded if sharded else self.L.veda_trainer_init_dp
         _check(self.L, fn(self.h, buf, rank, world, bucket_bytes))
+
+    def sync(self):
+        """The current stream waits for the trainer's queued communication."""
+        _check(self.L, self.L.veda_trainer_sync(self.h))
 
     def step_host(self, ids: np.ndarray, targets: np.ndarray):
         ids = np.ascontiguousarray(ids, dtype=np.int64)
