@@ -46,6 +46,11 @@ public:
 
     size_t steps() const noexcept { return steps_; }
     const AdamWConfig& config() const noexcept { return config_; }
+    // First and second moments of every parameter, fp32, back to back in parameter order.
+    const core::Tensor& first_moments() const noexcept { return m_arena_; }
+    const core::Tensor& second_moments() const noexcept { return v_arena_; }
+    // Restores the step count (the bias corrections of the next step use steps + 1).
+    void set_steps(size_t steps) noexcept { steps_ = steps; }
     const std::vector<autograd::Variable>& parameters() const noexcept { return parameters_; }
     // fp32 master weights of parameter i (the value itself for fp32 parameters).
     core::Tensor master(size_t i) const { return masters_[i]; }

@@ -156,6 +156,13 @@ public:
     void gather_gradients();
     // After master_weights() was written from the host: refresh this rank's shard of it.
     void master_weights_changed();
+    // Checkpoint: dir/model.safetensors (the weights under the reference's parameter names, bf16
+    // or fp32 as the model computes) and dir/optimizer.safetensors (per parameter its fp32
+    // master weights, first and second moments as "<name>.master", ".exp_avg", ".exp_avg_sq";
+    // metadata "step"). Data-parallel: rank 0 writes; collective when sharded. Loading without
+    // an optimizer file starts the optimizer afresh from the file's weights.
+    void save_checkpoint(const std::string& dir);
+    void load_checkpoint(const std::string& dir);
 
     // One training step on device-resident ids/targets (int64 [B*T]); asynchronous.
     void step(const core::Tensor& ids, const core::Tensor& targets);

@@ -65,6 +65,23 @@ int veda_trainer_init_dp(veda_trainer* t, const void* unique_id128, int rank, in
 int veda_trainer_init_dp_sharded(veda_trainer* t, const void* unique_id128, int rank, int world,
                                  size_t bucket_bytes);
 
+/* Checkpoints (a writer the reference lacks; its reader is src/libs/io/Safetensors.cpp:106-257):
+ * dir/model.safetensors holds the weights under the reference's parameter names
+ * (Model.cpp:120-140) in the model's dtype; dir/optimizer.safetensors holds per parameter the fp32
+ * master weights, first and second moments ("<name>.master", ".exp_avg", ".exp_avg_sq") and the
+ * step count (metadata "step"). Loading restores all of it, so training resumes bit-exactly; a
+ * directory without optimizer.safetensors loads the weights and starts the optimizer afresh.
+ * Data-parallel: rank 0 writes; with a sharded optimizer both calls are collective. */
+int veda_trainer_save_checkpoint(veda_trainer* t, const char* dir);
+int veda_trainer_load_checkpoint(veda_trainer* t, const char* dir);
+/* Writes host tensors as one safetensors file (the checkpoint writer's format): count tensors with
+ * names, dtype names ("BF16", "F32", "I64", ...), ranks and their dims back to back, raw
+ * little-endian data; meta_count string pairs of metadata. No device is touched. */
+int veda_safetensors_write(const char* path, int64_t count, const char* const* names,
+                           const char* const* dtypes, const int64_t* ranks, const int64_t* dims,
+                           const void* const* data, int64_t meta_count, const char* const* meta_keys,
+                           const char* const* meta_values);
+
 /* The current stream waits for all communication the trainer has queued: a step with a sharded
  * optimizer returns with the all-gather of its updated weights still running (the next step's
  * forward waits for each bucket where it first reads it). Call before timing the end of a run or

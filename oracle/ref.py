@@ -261,3 +261,29 @@ def train_steps(c, params, ids, targets, max_norm, adam, steps=1):
             at += p.size
         return out
     return split(flat), losses, norms, split(grads)
+
+
+def read_safetensors(path):
+    """Every tensor of a safetensors file as the reference's reader returns it (widened to fp32),
+    in header order: [(name, array)] (src/libs/io/Safetensors.cpp:106-257)."""
+    L = lib()
+    fn = L.vref_read_safetensors
+    fn.restype = C.c_int64
+    fn.argtypes = [C.c_char_p, C.c_int64, C.c_char_p, C.c_int64, C.POINTER(C.c_int64),
+                   C.POINTER(C.c_int64), C.c_void_p, C.c_int64]
+    name = C.create_string_buffer(512)
+    rank = C.c_int64(0)
+    dims = (C.c_int64 * 8)()
+    count = fn(str(path).encode(), -1, name, 512, C.byref(rank), dims, None, 0)
+    if count < 0:
+        raise RuntimeError(L.vref_last_error().decode())
+    out = []
+    for i in range(count):
+        fn(str(path).encode(), i, name, 512, C.byref(rank), dims, None, 0)
+        shape = tuple(dims[j] for j in range(rank.value))
+        vals = np.empty(int(np.prod(shape)) if shape else 1, np.float32)
+        rc = fn(str(path).encode(), i, name, 512, C.byref(rank), dims, vals.ctypes.data, vals.size)
+        if rc < 0:
+            raise RuntimeError(L.vref_last_error().decode())
+        out.append((name.value.decode(), vals.reshape(shape)))
+    return out

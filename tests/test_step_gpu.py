@@ -137,3 +137,42 @@ def test_qwen_06b_full_shape_step_properties():
     assert math.isfinite(n1) and math.isfinite(n2) and n1 > 0
     assert l2 < l1
     t.close()
+
+
+def test_checkpoint_resume_is_bit_exact(tmp_path):
+    """Save after one step, load into a fresh trainer, take the next step: the same loss, norm,
+    gradients and weights as continuing without the checkpoint. The model file, read by the
+    reference's own safetensors reader, holds the bf16 weights under the reference's names."""
+    from oracle import ref as R
+    cfg = QWEN_SMALL
+    B, T = 2, 128
+    params = O.init_params(cfg, 3, bf16=True)
+    b1, b2 = O.synthetic_batch(cfg, B, T, 3), O.synthetic_batch(cfg, B, T, 4)
+    t = make_trainer(cfg, 1, B, T)
+    t.set_params(np.concatenate([p.ravel() for p in params]))
+    t.step_host(*b1)
+    w1 = t.get_params()
+    ck = tmp_path / "ck"
+    t.save(ck)
+    loss, norm = t.step_host(*b2)
+    w2, g2 = t.get_params(), t.get_grads()
+    u = make_trainer(cfg, 1, B, T, seed=9)
+    u.load(ck)
+    assert np.array_equal(u.get_params(), w1)
+    loss_u, norm_u = u.step_host(*b2)
+    assert loss_u == loss and norm_u == norm
+    assert np.array_equal(u.get_grads(), g2)
+    assert np.array_equal(u.get_params(), w2)
+    if R.available():
+        got = R.read_safetensors(ck / "model.safetensors")
+        specs = O.param_specs(cfg)
+        assert [name for name, _ in got] == [name for name, _ in specs]
+        for (name, arr), ref in zip(got, split(cfg, O.bf16_round(w1))):
+            assert arr.shape == ref.shape and np.array_equal(arr, ref), name
+    # weights only (no optimizer file): the bf16 weights, the optimizer starting afresh
+    (ck / "optimizer.safetensors").unlink()
+    v = make_trainer(cfg, 1, B, T, seed=11)
+    v.load(ck)
+    assert np.array_equal(v.get_params(), O.bf16_round(w1))
+    for x in (t, u, v):
+        x.close()

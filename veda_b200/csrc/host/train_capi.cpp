@@ -1,5 +1,6 @@
 // C ABI of libveda.so (include/veda_train.h): exceptions become status codes.
 #include "veda_train.h"
+#include "veda/checkpoint.hpp"
 
 #include "veda/profile.hpp"
 #include "veda/train.hpp"
@@ -184,6 +185,55 @@ int veda_trainer_init_dp(veda_trainer* t, const void* unique_id128, int rank, in
                          size_t bucket_bytes)
 {
     return guarded([&] { t->impl->init_data_parallel(unique_id128, rank, world, bucket_bytes); });
+}
+
+int veda_trainer_save_checkpoint(veda_trainer* t, const char* dir)
+{
+    return guarded([&] {
+        if (dir == nullptr) throw std::invalid_argument("veda_trainer_save_checkpoint: null path");
+        t->impl->save_checkpoint(dir);
+    });
+}
+
+int veda_trainer_load_checkpoint(veda_trainer* t, const char* dir)
+{
+    return guarded([&] {
+        if (dir == nullptr) throw std::invalid_argument("veda_trainer_load_checkpoint: null path");
+        t->impl->load_checkpoint(dir);
+    });
+}
+
+int veda_safetensors_write(const char* path, int64_t count, const char* const* names,
+                           const char* const* dtypes, const int64_t* ranks, const int64_t* dims,
+                           const void* const* data, int64_t meta_count, const char* const* meta_keys,
+                           const char* const* meta_values)
+{
+    return guarded([&] {
+        if (path == nullptr || count < 0 || meta_count < 0)
+            throw std::invalid_argument("veda_safetensors_write: bad arguments");
+        std::vector<veda::io::SafetensorsTensor> tensors;
+        size_t d = 0;
+        for (int64_t i = 0; i < count; ++i)
+        {
+            veda::io::SafetensorsTensor t;
+            t.name = names[i];
+            t.dtype = dtypes[i];
+            size_t elems = 1;
+            for (int64_t r = 0; r < ranks[i]; ++r)
+            {
+                t.shape.push_back(dims[d]);
+                elems *= static_cast<size_t>(dims[d]);
+                ++d;
+            }
+            const size_t bytes = elems * veda::io::dtype_bytes(t.dtype);
+            const auto* p = static_cast<const uint8_t*>(data[i]);
+            t.bytes.assign(p, p + bytes);
+            tensors.push_back(std::move(t));
+        }
+        std::map<std::string, std::string> meta;
+        for (int64_t i = 0; i < meta_count; ++i) meta[meta_keys[i]] = meta_values[i];
+        veda::io::write_safetensors(path, tensors, meta);
+    });
 }
 
 int veda_trainer_sync(veda_trainer* t)

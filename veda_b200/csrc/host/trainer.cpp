@@ -7,6 +7,7 @@
 // has produced the last gradient that falls into it (the tape reports each leaf as it becomes
 // final), so the exchange of layer L's gradients overlaps the backward of layers L-1..0. The
 // update waits for the last bucket; the 1/world average is folded into the AdamW kernel.
+#include "veda/checkpoint.hpp"
 #include "veda/profile.hpp"
 #include "veda/train.hpp"
 
@@ -18,6 +19,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <filesystem>
 #include <stdexcept>
 #include <unordered_map>
 
@@ -154,11 +156,14 @@ public:
         load_master(master);
     }
 
-    // This rank's parts of the arena-ordered fp32 master weights (`params_` of them; the padding
-    // past them stays zero) into its shard.
-    void load_master(const float* master)
+    void load_master(const float* master) { load_shard(master, master_s_); }
+
+    // This rank's parts of an arena-ordered fp32 vector (`params_` elements; the padding past
+    // them stays zero) into one of its shards.
+    void load_shard(const float* full, Tensor& shard)
     {
-        float* dst = static_cast<float*>(master_s_.data_ptr());
+        const float* master = full;
+        float* dst = static_cast<float*>(shard.data_ptr());
         for (const Bucket& b : buckets_)
         {
             const size_t len = (b.end - b.begin) / world_;
@@ -356,25 +361,43 @@ public:
     }
 
     // Collective: the full master weights, in arena order, into `master` (params_ elements).
-    void gather_master(float* master)
+    void gather_master(float* master) { gather_shard(master_s_, master); }
+
+    // Collective: every rank's parts of a shard, in arena order, into `full` (params_ elements).
+    void gather_shard(const Tensor& shard, float* full)
     {
         sync();
-        Tensor full = Tensor::empty(Shape({total_}), DType::F32);
-        float* f = static_cast<float*>(full.data_ptr());
+        Tensor whole = Tensor::empty(Shape({total_}), DType::F32);
+        float* f = static_cast<float*>(whole.data_ptr());
         fork_comm();
-        nccl_check(ncclGroupStart(), "master all-gather");
+        nccl_check(ncclGroupStart(), "shard all-gather");
         for (const Bucket& b : buckets_)
         {
-            nccl_check(ncclAllGather(static_cast<const float*>(master_s_.data_ptr()) + b.shard_at, f + b.begin,
+            nccl_check(ncclAllGather(static_cast<const float*>(shard.data_ptr()) + b.shard_at, f + b.begin,
                                      (b.end - b.begin) / world_, ncclFloat, comm_, stream_),
-                       "master all-gather");
+                       "shard all-gather");
         }
-        nccl_check(ncclGroupEnd(), "master all-gather");
+        nccl_check(ncclGroupEnd(), "shard all-gather");
         join_comm();
-        cuda_check(cudaMemcpyAsync(master, f, params_ * sizeof(float), cudaMemcpyDeviceToDevice, cs()),
-                   "master copy");
-        cuda_check(cudaStreamSynchronize(cs()), "master copy");
+        cuda_check(cudaMemcpyAsync(full, f, params_ * sizeof(float), cudaMemcpyDeviceToDevice, cs()),
+                   "shard copy");
+        cuda_check(cudaStreamSynchronize(cs()), "shard copy");
     }
+
+    // Moments and step count for a checkpoint (sharded; collective) and back.
+    void gather_moments(float* m, float* v)
+    {
+        gather_shard(m_s_, m);
+        gather_shard(v_s_, v);
+    }
+    void load_moments(const float* m, const float* v, size_t steps)
+    {
+        load_shard(m, m_s_);
+        load_shard(v, v_s_);
+        steps_ = steps;
+    }
+    size_t steps() const noexcept { return steps_; }
+    int rank() const noexcept { return rank_; }
 
     int world() const noexcept { return world_; }
     bool sharded() const noexcept { return sharded_; }
@@ -597,6 +620,153 @@ void Trainer::step(const Tensor& ids, const Tensor& targets)
     cuda_check(cudaMemcpyAsync(loss_.data_ptr(), loss.value().data_ptr(), sizeof(float),
                                cudaMemcpyDeviceToDevice, cs()),
                "loss copy");
+}
+
+namespace
+{
+template <typename T>
+std::vector<uint8_t> to_host_bytes(const void* device, size_t count)
+{
+    std::vector<uint8_t> out(count * sizeof(T));
+    cuda_check(cudaMemcpyAsync(out.data(), device, out.size(), cudaMemcpyDeviceToHost, cs()), "checkpoint read");
+    return out;
+}
+} // namespace
+
+void Trainer::save_checkpoint(const std::string& dir)
+{
+    sync();
+    const size_t n = model_->parameter_count();
+    const bool bf16 = model_->dtype() == DType::BF16;
+    float* master = master_weights();
+    const float* m = static_cast<const float*>(opt_->first_moments().data_ptr());
+    const float* v = static_cast<const float*>(opt_->second_moments().data_ptr());
+    size_t steps = opt_->steps();
+    Tensor m_full, v_full;
+    if (sharded())
+    {
+        gather_master_weights();   // collective: the shards' master weights into master_weights()
+        m_full = Tensor::empty(Shape({n}), DType::F32);
+        v_full = Tensor::empty(Shape({n}), DType::F32);
+        dp_->gather_moments(static_cast<float*>(m_full.data_ptr()), static_cast<float*>(v_full.data_ptr()));
+        m = static_cast<const float*>(m_full.data_ptr());
+        v = static_cast<const float*>(v_full.data_ptr());
+        steps = dp_->steps();
+    }
+    if (dp_ && dp_->rank() != 0)
+    {
+        return;   // every rank holds the same state; rank 0 writes it
+    }
+    std::filesystem::create_directories(dir);
+    std::vector<io::SafetensorsTensor> weights, state;
+    size_t at = 0;
+    for (const auto& [name, value] : model_->named_parameters())
+    {
+        const size_t count = value.numel();
+        std::vector<int64_t> shape(value.shape().dims().begin(), value.shape().dims().end());
+        weights.push_back({name, bf16 ? "BF16" : "F32", shape,
+                           bf16 ? to_host_bytes<uint16_t>(value.data_ptr(), count)
+                                : to_host_bytes<float>(value.data_ptr(), count)});
+        state.push_back({name + ".master", "F32", shape, to_host_bytes<float>(master + at, count)});
+        state.push_back({name + ".exp_avg", "F32", shape, to_host_bytes<float>(m + at, count)});
+        state.push_back({name + ".exp_avg_sq", "F32", shape, to_host_bytes<float>(v + at, count)});
+        at += count;
+    }
+    cuda_check(cudaStreamSynchronize(cs()), "checkpoint read");
+    if (at != n)
+    {
+        throw std::logic_error("save_checkpoint: parameters do not tile the arena");
+    }
+    io::write_safetensors(dir + "/model.safetensors", weights, {{"format", "pt"}});
+    io::write_safetensors(dir + "/optimizer.safetensors", state,
+                          {{"format", "pt"}, {"step", std::to_string(steps)}});
+}
+
+void Trainer::load_checkpoint(const std::string& dir)
+{
+    sync();
+    const io::SafetensorsFile weights = io::read_safetensors(dir + "/model.safetensors");
+    const bool resume = std::filesystem::exists(dir + "/optimizer.safetensors");
+    io::SafetensorsFile state;
+    if (resume)
+    {
+        state = io::read_safetensors(dir + "/optimizer.safetensors");
+    }
+    const size_t n = model_->parameter_count();
+    std::vector<float> master(n), m(n, 0.0f), v(n, 0.0f);
+    size_t at = 0;
+    auto take = [&](const io::SafetensorsTensor& t, const std::vector<int64_t>& shape, size_t count, float* dst) {
+        if (t.shape != shape)
+        {
+            throw std::invalid_argument("load_checkpoint: " + t.name + " has the wrong shape");
+        }
+        if (t.dtype == "F32")
+        {
+            std::memcpy(dst, t.bytes.data(), count * sizeof(float));
+        }
+        else if (t.dtype == "BF16")
+        {
+            for (size_t i = 0; i < count; ++i)
+            {
+                uint16_t h;
+                std::memcpy(&h, t.bytes.data() + 2 * i, 2);
+                const uint32_t w = static_cast<uint32_t>(h) << 16;
+                std::memcpy(dst + i, &w, 4);
+            }
+        }
+        else
+        {
+            throw std::invalid_argument("load_checkpoint: " + t.name + " is " + t.dtype);
+        }
+    };
+    for (const auto& [name, value] : model_->named_parameters())
+    {
+        const size_t count = value.numel();
+        const std::vector<int64_t> shape(value.shape().dims().begin(), value.shape().dims().end());
+        if (resume)
+        {
+            take(state.at(name + ".master"), shape, count, master.data() + at);
+            take(state.at(name + ".exp_avg"), shape, count, m.data() + at);
+            take(state.at(name + ".exp_avg_sq"), shape, count, v.data() + at);
+        }
+        else
+        {
+            take(weights.at(name), shape, count, master.data() + at);
+        }
+        at += count;
+    }
+    size_t steps = 0;
+    if (resume)
+    {
+        auto it = state.metadata.find("step");
+        if (it == state.metadata.end())
+        {
+            throw std::invalid_argument("load_checkpoint: optimizer.safetensors has no step");
+        }
+        steps = static_cast<size_t>(std::stoull(it->second));
+    }
+    float* dmaster = master_weights();
+    cuda_check(cudaMemcpyAsync(dmaster, master.data(), n * sizeof(float), cudaMemcpyHostToDevice, cs()),
+               "checkpoint write");
+    if (model_->dtype() == DType::BF16)
+    {
+        check(veda_f32_to_bf16(dmaster, model_->value_arena().data_ptr(), static_cast<int64_t>(n), cs()),
+              "checkpoint write");
+    }
+    cuda_check(cudaMemcpyAsync(opt_->first_moments().data_ptr(), m.data(), n * sizeof(float),
+                               cudaMemcpyHostToDevice, cs()),
+               "checkpoint write");
+    cuda_check(cudaMemcpyAsync(opt_->second_moments().data_ptr(), v.data(), n * sizeof(float),
+                               cudaMemcpyHostToDevice, cs()),
+               "checkpoint write");
+    opt_->set_steps(steps);
+    if (sharded())
+    {
+        dp_->load_master(dmaster);
+        dp_->load_moments(static_cast<const float*>(opt_->first_moments().data_ptr()),
+                          static_cast<const float*>(opt_->second_moments().data_ptr()), steps);
+    }
+    cuda_check(cudaStreamSynchronize(cs()), "checkpoint write");
 }
 
 StepStats Trainer::step_host(const int64_t* ids, const int64_t* targets)

@@ -34,6 +34,9 @@ SIGNATURES = {
     "veda_trainer_init_dp": (_i, [_p, _p, _i, _i, _sz]),
     "veda_trainer_init_dp_sharded": (_i, [_p, _p, _i, _i, _sz]),
     "veda_trainer_sync": (_i, [_p]),
+    "veda_trainer_save_checkpoint": (_i, [_p, C.c_char_p]),
+    "veda_trainer_load_checkpoint": (_i, [_p, C.c_char_p]),
+    "veda_safetensors_write": (_i, [C.c_char_p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p]),
     "veda_trainer_step_host": (_i, [_p, _p, _p, _p, _p]),
     "veda_trainer_step_device": (_i, [_p, _p, _p]),
     "veda_trainer_last_stats": (_i, [_p, _p, _p]),
@@ -119,6 +122,13 @@ class Trainer:
         fn = self.L.veda_trainer_init_dp_sharded if sharded else self.L.veda_trainer_init_dp
         _check(self.L, fn(self.h, buf, rank, world, bucket_bytes))
 
+    def save(self, directory: str):
+        """dir/model.safetensors + dir/optimizer.safetensors (collective when sharded)."""
+        _check(self.L, self.L.veda_trainer_save_checkpoint(self.h, str(directory).encode()))
+
+    def load(self, directory: str):
+        _check(self.L, self.L.veda_trainer_load_checkpoint(self.h, str(directory).encode()))
+
     def sync(self):
         """The current stream waits for the trainer's queued communication."""
         _check(self.L, self.L.veda_trainer_sync(self.h))
@@ -165,3 +175,22 @@ def profile_collect():
     la = (C.c_uint64 * cap)()
     n = _check(L, L.veda_profile_collect(names, ms, fl, by, la, cap))
     return {names[i].value.decode(): (ms[i], fl[i], by[i], int(la[i])) for i in range(min(n, cap))}
+
+
+def write_safetensors(path, tensors, metadata=None):
+    """Writes host arrays with the library's safetensors writer. tensors: list of (name, dtype
+    name, numpy array holding the raw little-endian values)."""
+    from . import host_lib
+    L = host_lib()
+    names = [n.encode() for n, _, _ in tensors]
+    dtypes = [d.encode() for _, d, _ in tensors]
+    arrays = [np.ascontiguousarray(a) for _, _, a in tensors]
+    ranks = np.array([a.ndim for a in arrays], np.int64)
+    dims = np.array([x for a in arrays for x in a.shape], np.int64)
+    meta = list((metadata or {}).items())
+    strs = lambda xs: (C.c_char_p * max(1, len(xs)))(*xs)  # noqa: E731
+    ptrs = (C.c_void_p * max(1, len(arrays)))(*[a.ctypes.data for a in arrays])
+    _check(L, L.veda_safetensors_write(str(path).encode(), len(arrays), strs(names), strs(dtypes),
+                                       ranks.ctypes.data, dims.ctypes.data if dims.size else None,
+                                       ptrs, len(meta), strs([k.encode() for k, _ in meta]),
+                                       strs([v.encode() for _, v in meta])))
