@@ -271,6 +271,17 @@ int veda_randn(void* x, int64_t n, float std, uint64_t seed, int dtype, veda_str
 int veda_f32_to_bf16(const float* src, void* dst, int64_t n, veda_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------- */
+/* Corpus batches (data::Corpus::next_batch, src/libs/data/Corpus.cpp:64-107) from device ids. */
+/* ---------------------------------------------------------------------------------------- */
+/* Row k (0-based) of the batch starts at begin + splitmix64_mix(state + (k+1)*0x9E3779B97F4A7C15)
+ * % (end - begin - length), the k-th draw of the reference's generator from `state`;
+ * inputs[k*length + t] = ids[start + t], targets[...] = ids[start + t + 1]. The caller advances
+ * its state by batch * 0x9E3779B97F4A7C15. Bit-identical to the reference's windows. */
+int veda_corpus_gather(const int64_t* ids, int64_t begin, int64_t end, uint64_t state,
+                       int64_t batch, int64_t length, int64_t* inputs, int64_t* targets,
+                       veda_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------- */
 /* Causal GQA attention (the composition of src/libs/train/Model.cpp:182-189:                 */
 /* softmax(q k^T * scale + mask) v, KV head of query head h = h / (H/Hkv),                    */
 /* src/libs/model/Attention.cpp:191).                                                          */

@@ -82,6 +82,18 @@ int veda_safetensors_write(const char* path, int64_t count, const char* const* n
                            const void* const* data, int64_t meta_count, const char* const* meta_keys,
                            const char* const* meta_values);
 
+/* A corpus on the device (data::Corpus, src/libs/data/Corpus.cpp:25-107): the same split rule,
+ * generator and draw order as the reference, so the same ids and seed give bit-identical batches.
+ * next_batch writes batch*length int64 inputs and targets into device buffers on the current
+ * stream (split 0 = train, 1 = validation), ready for veda_trainer_step_device. */
+typedef struct veda_corpus veda_corpus;
+int veda_corpus_create(const int64_t* ids, int64_t n, double validation_fraction, uint64_t seed,
+                       veda_corpus** out);
+int veda_corpus_destroy(veda_corpus* c);
+int64_t veda_corpus_boundary(const veda_corpus* c);
+int veda_corpus_next_batch(veda_corpus* c, int64_t batch, int64_t length, int split,
+                           int64_t* inputs, int64_t* targets);
+
 /* The current stream waits for all communication the trainer has queued: a step with a sharded
  * optimizer returns with the all-gather of its updated weights still running (the next step's
  * forward waits for each bucket where it first reads it). Call before timing the end of a run or

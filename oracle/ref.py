@@ -287,3 +287,39 @@ def read_safetensors(path):
             raise RuntimeError(L.vref_last_error().decode())
         out.append((name.value.decode(), vals.reshape(shape)))
     return out
+
+
+class RefCorpus:
+    """The reference's data::Corpus (src/libs/data/Corpus.cpp), compiled from its sources."""
+
+    def __init__(self, ids, validation_fraction, seed):
+        L = lib()
+        L.vref_corpus_create.restype = C.c_void_p
+        L.vref_corpus_create.argtypes = [I64P, C.c_int64, C.c_double, C.c_uint64]
+        L.vref_corpus_next_batch.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_int, I64P, I64P]
+        L.vref_corpus_boundary.restype = C.c_int64
+        L.vref_corpus_boundary.argtypes = [C.c_void_p]
+        L.vref_corpus_destroy.argtypes = [C.c_void_p]
+        self.L = L
+        ids = np.ascontiguousarray(ids, dtype=np.int64)
+        self.h = L.vref_corpus_create(ids, ids.size, validation_fraction, seed)
+        if not self.h:
+            raise ValueError(L.vref_last_error().decode())
+
+    @property
+    def boundary(self):
+        return self.L.vref_corpus_boundary(self.h)
+
+    def next_batch(self, batch, length, split="train"):
+        inputs = np.empty(batch * length, np.int64)
+        targets = np.empty(batch * length, np.int64)
+        rc = self.L.vref_corpus_next_batch(self.h, batch, length, 1 if split == "validation" else 0,
+                                           inputs, targets)
+        if rc != 0:
+            raise ValueError(self.L.vref_last_error().decode())
+        return inputs.reshape(batch, length), targets.reshape(batch, length)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.L.vref_corpus_destroy(self.h)
+            self.h = None

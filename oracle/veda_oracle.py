@@ -552,3 +552,47 @@ def max_abs_rel(a, b) -> float:
     if den == 0.0:
         return num
     return num / den
+
+
+# ---- corpus batcher ----------------------------------------------------------------------------
+_U64 = (1 << 64) - 1
+_GOLDEN = 0x9E3779B97F4A7C15
+
+
+class Corpus:
+    """The reference's batcher, restated (src/libs/data/Corpus.cpp:25-107): contiguous split at
+    int(size * (1 - validation_fraction)); splitmix64 (state += 0x9E3779B97F4A7C15, then the
+    published mix) with seed 0 meaning 0x9E3779B97F4A7C15; one draw per row, start = begin +
+    draw % (available - window + 1); targets are the inputs' successors."""
+
+    def __init__(self, ids, validation_fraction, seed):
+        if not 0.0 <= validation_fraction <= 1.0:
+            raise ValueError("Corpus: validation_fraction must lie in [0, 1]")
+        self.ids = np.asarray(ids, dtype=np.int64)
+        self.boundary = min(int(float(len(self.ids)) * (1.0 - validation_fraction)), len(self.ids))
+        self.state = _GOLDEN if seed == 0 else seed & _U64
+
+    def _next_random(self):
+        # Corpus.cpp:55-64
+        self.state = (self.state + _GOLDEN) & _U64
+        z = self.state
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _U64
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _U64
+        return z ^ (z >> 31)
+
+    def next_batch(self, batch, length, split="train"):
+        # Corpus.cpp:66-107
+        if batch == 0 or length == 0:
+            raise ValueError("Corpus: batch size and length must be positive")
+        begin, end = (0, self.boundary) if split == "train" else (self.boundary, len(self.ids))
+        window = length + 1
+        if end - begin < window:
+            raise ValueError("Corpus: the split is shorter than one window")
+        offsets = end - begin - window + 1
+        inputs = np.empty((batch, length), np.int64)
+        targets = np.empty((batch, length), np.int64)
+        for row in range(batch):
+            start = begin + self._next_random() % offsets
+            inputs[row] = self.ids[start:start + length]
+            targets[row] = self.ids[start + 1:start + length + 1]
+        return inputs, targets

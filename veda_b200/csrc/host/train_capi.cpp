@@ -1,6 +1,7 @@
 // C ABI of libveda.so (include/veda_train.h): exceptions become status codes.
 #include "veda_train.h"
 #include "veda/checkpoint.hpp"
+#include "veda/data.hpp"
 
 #include "veda/profile.hpp"
 #include "veda/train.hpp"
@@ -11,6 +12,7 @@
 #include <nccl.h>
 
 #include <cstring>
+#include <memory>
 #include <stdexcept>
 #include <string>
 
@@ -233,6 +235,47 @@ int veda_safetensors_write(const char* path, int64_t count, const char* const* n
         std::map<std::string, std::string> meta;
         for (int64_t i = 0; i < meta_count; ++i) meta[meta_keys[i]] = meta_values[i];
         veda::io::write_safetensors(path, tensors, meta);
+    });
+}
+
+struct veda_corpus
+{
+    std::unique_ptr<veda::data::Corpus> impl;
+};
+
+int veda_corpus_create(const int64_t* ids, int64_t n, double validation_fraction, uint64_t seed,
+                       veda_corpus** out)
+{
+    return guarded([&] {
+        if (out == nullptr || n < 0 || (n > 0 && ids == nullptr))
+            throw std::invalid_argument("veda_corpus_create: bad arguments");
+        auto c = std::make_unique<veda_corpus>();
+        c->impl = std::make_unique<veda::data::Corpus>(std::vector<int64_t>(ids, ids + n),
+                                                       validation_fraction, seed);
+        *out = c.release();
+    });
+}
+
+int veda_corpus_destroy(veda_corpus* c)
+{
+    delete c;
+    return 0;
+}
+
+int64_t veda_corpus_boundary(const veda_corpus* c)
+{
+    return c == nullptr ? -1 : static_cast<int64_t>(c->impl->boundary());
+}
+
+int veda_corpus_next_batch(veda_corpus* c, int64_t batch, int64_t length, int split,
+                           int64_t* inputs, int64_t* targets)
+{
+    return guarded([&] {
+        if (c == nullptr || batch < 0 || length < 0 || (split != 0 && split != 1))
+            throw std::invalid_argument("veda_corpus_next_batch: bad arguments");
+        c->impl->next_batch_into(static_cast<size_t>(batch), static_cast<size_t>(length),
+                                 split ? veda::data::Split::Validation : veda::data::Split::Train,
+                                 inputs, targets);
     });
 }
 

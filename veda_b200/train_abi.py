@@ -34,6 +34,10 @@ SIGNATURES = {
     "veda_trainer_init_dp": (_i, [_p, _p, _i, _i, _sz]),
     "veda_trainer_init_dp_sharded": (_i, [_p, _p, _i, _i, _sz]),
     "veda_trainer_sync": (_i, [_p]),
+    "veda_corpus_create": (_i, [_p, _i64, C.c_double, C.c_uint64, _p]),
+    "veda_corpus_destroy": (_i, [_p]),
+    "veda_corpus_boundary": (_i64, [_p]),
+    "veda_corpus_next_batch": (_i, [_p, _i64, _i64, _i, _p, _p]),
     "veda_trainer_save_checkpoint": (_i, [_p, C.c_char_p]),
     "veda_trainer_load_checkpoint": (_i, [_p, C.c_char_p]),
     "veda_safetensors_write": (_i, [C.c_char_p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p]),
@@ -194,3 +198,31 @@ def write_safetensors(path, tensors, metadata=None):
                                        ranks.ctypes.data, dims.ctypes.data if dims.size else None,
                                        ptrs, len(meta), strs([k.encode() for k, _ in meta]),
                                        strs([v.encode() for _, v in meta])))
+
+
+class Corpus:
+    """data::Corpus on the current CUDA device; next_batch fills device int64 buffers."""
+
+    def __init__(self, ids, validation_fraction, seed):
+        from . import host_lib
+        self.L = host_lib()
+        ids = np.ascontiguousarray(ids, dtype=np.int64)
+        h = C.c_void_p()
+        _check(self.L, self.L.veda_corpus_create(ids.ctypes.data if ids.size else None, ids.size,
+                                                 float(validation_fraction), int(seed),
+                                                 C.byref(h)))
+        self.h = h
+
+    @property
+    def boundary(self):
+        return self.L.veda_corpus_boundary(self.h)
+
+    def next_batch(self, batch, length, split, inputs_ptr, targets_ptr):
+        _check(self.L, self.L.veda_corpus_next_batch(self.h, batch, length,
+                                                     1 if split == "validation" else 0,
+                                                     inputs_ptr, targets_ptr))
+
+    def close(self):
+        if self.h:
+            self.L.veda_corpus_destroy(self.h)
+            self.h = None
