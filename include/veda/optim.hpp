@@ -40,6 +40,11 @@ public:
     // Clip to max_norm (the global norm of grad_scale * g) and step, in two launches per run of
     // contiguous parameters; nothing is synchronised. grad_scale carries a data-parallel 1/world.
     void step_clipped(float max_norm, float grad_scale = 1.0f);
+    // step_clipped split in two for a step replayed from a CUDA graph: advance() counts the step
+    // and leaves its bias corrections in device memory (not capturable: call it before each
+    // replay); launch_clipped() only launches kernels, which read them there.
+    void advance();
+    void launch_clipped(float max_norm, float grad_scale = 1.0f);
     // The pre-clip global norm of the last step_clipped() (synchronises the stream).
     float last_grad_norm();
     void zero_grad();
@@ -78,6 +83,8 @@ private:
     AdamWConfig config_;
     size_t steps_ = 0;
     core::Tensor sumsq_;     // device double
+    core::Tensor bias_;      // device double [2]: 1 - beta1^t, 1 - beta2^t of the current step
+    double bias_host_[2] = {1.0, 1.0};
     core::Tensor workspace_;
     float last_scale_ = 1.0f;
 };

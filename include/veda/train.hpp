@@ -28,6 +28,8 @@
 #include <utility>
 #include <vector>
 
+struct CUgraphExec_st;
+
 namespace veda::train
 {
 
@@ -166,6 +168,9 @@ public:
 
     // One training step on device-resident ids/targets (int64 [B*T]); asynchronous.
     void step(const core::Tensor& ids, const core::Tensor& targets);
+    // Single-GPU steps are captured once into a CUDA graph and replayed (on by default; the
+    // environment variable VEDA_STEP_GRAPH=0 turns it off for the process).
+    void set_step_graph(bool on);
     // One step from host buffers: copies in, steps, reads loss and grad norm back (synchronous).
     StepStats step_host(const int64_t* ids, const int64_t* targets);
     // Loss and pre-clip grad norm of the last step (synchronises).
@@ -184,6 +189,13 @@ private:
     size_t batch_, length_;
     core::Tensor ids_, targets_, loss_;
     core::Tensor pinned_;   // host-side staging is done by the caller; kept for symmetry
+    bool graph_eligible() const;
+    void step_impl(const core::Tensor& ids, const core::Tensor& targets);
+    ::CUgraphExec_st* graph_exec_ = nullptr;
+    int64_t graph_launches_ = 0;
+    int eager_steps_ = 0;
+    bool use_graph_ = true;
+    void* capture_stream_ = nullptr;   // cudaStream_t the step is captured on
 };
 
 } // namespace veda::train

@@ -49,6 +49,9 @@ const char* veda_last_error(void);
 int veda_device_info(int* sm_count, int* cc_major, int* cc_minor);
 /* Kernel launches issued by this library since load (all threads); a diagnostic counter. */
 uint64_t veda_launch_count(void);
+/* Adds n (may be negative) to that counter: a caller replaying a CUDA graph of this library's
+ * kernels adds the graph's kernel count per replay. */
+int veda_launch_count_add(int64_t n);
 /* The current device's status word: 0, or VEDA_ERR_TIMEOUT if a kernel's bounded device-side
  * wait gave up since the last reset. Synchronises with the device; reset = 1 clears it. */
 int veda_kernel_status(int reset);
@@ -218,6 +221,12 @@ int veda_adamw_step(float* master, float* m, float* v, float* g, void* lowp, int
                     float beta1, float beta2, float eps, float weight_decay, double bias1,
                     double bias2, const double* sumsq, float max_norm, float grad_scale,
                     int write_grad, veda_stream_t stream);
+/* The same with bias1, bias2 read from device memory (bias[0], bias[1], doubles) when the kernel
+ * runs, so one launch recorded in a CUDA graph serves every step. */
+int veda_adamw_step_dev(float* master, float* m, float* v, float* g, void* lowp, int64_t n,
+                        float lr, float beta1, float beta2, float eps, float weight_decay,
+                        const double* bias, const double* sumsq, float max_norm, float grad_scale,
+                        int write_grad, veda_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------- */
 /* Element-wise and per-lane ops of the fine-grained autograd API.                           */

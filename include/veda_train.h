@@ -100,6 +100,10 @@ int veda_corpus_next_batch(veda_corpus* c, int64_t batch, int64_t length, int sp
  * reading the weights on the device by other means. */
 int veda_trainer_sync(veda_trainer* t);
 
+/* On one GPU a step is captured once into a CUDA graph (after one eager step) and replayed: one
+ * host call per step instead of ~850 launches. on = 0 keeps this trainer's steps eager. */
+int veda_trainer_set_step_graph(veda_trainer* t, int on);
+
 /* One step from host ids/targets (int64 [batch*seq_len], targets = next ids); copies them in,
  * steps and reads back loss and pre-clip grad norm (synchronous). */
 int veda_trainer_step_host(veda_trainer* t, const int64_t* ids, const int64_t* targets,

@@ -68,6 +68,8 @@ SIGNATURES = {
     "veda_clip_apply": (_i, [_p, _i64, _p, _f, _p]),
     "veda_adamw_step": (_i, [_p, _p, _p, _p, _p, _i64, _f, _f, _f, _f, _f, _d, _d, _p, _f, _f,
                              _i, _p]),
+    "veda_adamw_step_dev": (_i, [_p, _p, _p, _p, _p, _i64, _f, _f, _f, _f, _f, _p, _p, _f, _f, _i, _p]),
+    "veda_launch_count_add": (_i, [_i64]),
     "veda_binary": (_i, [_i, _p, _p, _p, _p, _p, _p, _i, _i, _p]),
     "veda_scale": (_i, [_p, _f, _p, _i64, _i, _p]),
     "veda_accumulate": (_i, [_p, _i, _p, _i, _i64, _p]),

@@ -73,6 +73,7 @@ AdamW::AdamW(std::vector<autograd::Variable> parameters, AdamWConfig config)
         }
     }
     sumsq_ = Tensor(Shape({2}), DType::F32);   // 8 bytes: one double
+    bias_ = Tensor(Shape({4}), DType::F32);    // two doubles
     build_runs();
 }
 
@@ -129,23 +130,43 @@ void AdamW::build_runs()
     workspace_ = Tensor::empty(Shape({(ws + 3) / 4 + 1}), DType::F32);
 }
 
-void AdamW::launch(const double* sumsq, float max_norm, float grad_scale)
+void AdamW::advance()
 {
     ++steps_;
-    const double bias1 = 1.0 - std::pow(static_cast<double>(config_.beta1), static_cast<double>(steps_));
-    const double bias2 = 1.0 - std::pow(static_cast<double>(config_.beta2), static_cast<double>(steps_));
+    bias_host_[0] = 1.0 - std::pow(static_cast<double>(config_.beta1), static_cast<double>(steps_));
+    bias_host_[1] = 1.0 - std::pow(static_cast<double>(config_.beta2), static_cast<double>(steps_));
+    if (cudaMemcpyAsync(bias_.data_ptr(), bias_host_, sizeof(bias_host_), cudaMemcpyHostToDevice, cs()) !=
+        cudaSuccess)
+    {
+        throw std::runtime_error("AdamW: bias correction upload failed");
+    }
+}
+
+void AdamW::launch(const double* sumsq, float max_norm, float grad_scale)
+{
+    const double* bias = static_cast<const double*>(bias_.data_ptr());
     for (const Run& r : runs_)
     {
-        check(veda_adamw_step(r.master, r.m, r.v, r.grad, r.lowp, r.n, config_.learning_rate,
-                              config_.beta1, config_.beta2, config_.eps, config_.weight_decay,
-                              bias1, bias2, sumsq, max_norm, grad_scale, 0, current_stream()),
+        check(veda_adamw_step_dev(r.master, r.m, r.v, r.grad, r.lowp, r.n, config_.learning_rate,
+                                  config_.beta1, config_.beta2, config_.eps, config_.weight_decay,
+                                  bias, sumsq, max_norm, grad_scale, 0, current_stream()),
               "AdamW::step");
     }
 }
 
-void AdamW::step() { launch(nullptr, 1.0f, 1.0f); }
+void AdamW::step()
+{
+    advance();
+    launch(nullptr, 1.0f, 1.0f);
+}
 
 void AdamW::step_clipped(float max_norm, float grad_scale)
+{
+    advance();
+    launch_clipped(max_norm, grad_scale);
+}
+
+void AdamW::launch_clipped(float max_norm, float grad_scale)
 {
     if (!(max_norm > 0.0f))
     {

@@ -6,6 +6,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cstdio>
 #include <cstring>
 #include <sstream>
 #include <stdexcept>
@@ -139,9 +140,11 @@ Storage::Storage(void* external, size_t bytes) : data_(external), bytes_(bytes),
 
 Storage::~Storage()
 {
-    if (owned_ && data_ != nullptr)
+    if (owned_ && data_ != nullptr && cudaFreeAsync(data_, cs()) != cudaSuccess)
     {
-        cudaFreeAsync(data_, cs());
+        // a destructor cannot throw: leave the error for the next check, and say which block
+        std::fprintf(stderr, "veda: freeing %zu device bytes failed: %s\n", bytes_,
+                     cudaGetErrorString(cudaPeekAtLastError()));
     }
 }
 

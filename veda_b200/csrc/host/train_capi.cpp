@@ -279,6 +279,11 @@ int veda_corpus_next_batch(veda_corpus* c, int64_t batch, int64_t length, int sp
     });
 }
 
+int veda_trainer_set_step_graph(veda_trainer* t, int on)
+{
+    return guarded([&] { t->impl->set_step_graph(on != 0); });
+}
+
 int veda_trainer_sync(veda_trainer* t)
 {
     return guarded([&] { t->impl->sync(); });

@@ -496,7 +496,17 @@ Trainer::Trainer(ModelConfig config, optim::AdamWConfig adam, float max_norm, DT
     loss_ = Tensor(Shape({1}), DType::F32);
 }
 
-Trainer::~Trainer() = default;
+Trainer::~Trainer()
+{
+    if (graph_exec_ != nullptr)
+    {
+        cudaGraphExecDestroy(graph_exec_);
+    }
+    if (capture_stream_ != nullptr)
+    {
+        cudaStreamDestroy(static_cast<cudaStream_t>(capture_stream_));
+    }
+}
 
 void Trainer::init_data_parallel(const void* nccl_unique_id, int rank, int world,
                                  size_t bucket_bytes, bool sharded)
@@ -566,7 +576,110 @@ void Trainer::master_weights_changed()
     }
 }
 
+// One process on one GPU, no profiling: the step is captured once into a CUDA graph (after one
+// eager step has created every persistent buffer) and replayed, so the ~850 launches of a step
+// cost one graph launch on the host and the device runs them back to back. The graph reads its
+// inputs from ids_ / targets_ and the optimizer's bias corrections from device memory, which are
+// the only things that change between steps. VEDA_STEP_GRAPH=0 keeps every step eager.
+bool Trainer::graph_eligible() const
+{
+    static const bool enabled = [] {
+        const char* v = std::getenv("VEDA_STEP_GRAPH");
+        return v == nullptr || std::atoi(v) != 0;
+    }();
+    return enabled && use_graph_ && !dp_ && !profile::enabled();
+}
+
+void Trainer::set_step_graph(bool on)
+{
+    use_graph_ = on;
+}
+
 void Trainer::step(const Tensor& ids, const Tensor& targets)
+{
+    if (!graph_eligible())
+    {
+        if (!sharded())
+        {
+            opt_->advance();
+        }
+        step_impl(ids, targets);
+        return;
+    }
+    const size_t bytes = batch_ * length_ * sizeof(int64_t);
+    if (ids.data_ptr() != ids_.data_ptr())
+    {
+        cuda_check(cudaMemcpyAsync(ids_.data_ptr(), ids.data_ptr(), bytes, cudaMemcpyDeviceToDevice, cs()),
+                   "ids copy");
+        cuda_check(cudaMemcpyAsync(targets_.data_ptr(), targets.data_ptr(), bytes,
+                                   cudaMemcpyDeviceToDevice, cs()),
+                   "targets copy");
+    }
+    opt_->advance();
+    if (graph_exec_ == nullptr && eager_steps_ < 1)
+    {
+        step_impl(ids_, targets_);   // creates the persistent buffers outside any graph
+        ++eager_steps_;
+        return;
+    }
+    if (graph_exec_ == nullptr)
+    {
+        // recorded on a private stream (the caller's may be the legacy default stream, which
+        // cannot be captured); nothing runs during the capture, the graph is launched below
+        if (capture_stream_ == nullptr)
+        {
+            cudaStream_t st = nullptr;
+            cuda_check(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "capture stream");
+            capture_stream_ = st;
+        }
+        const veda_stream_t caller = current_stream();
+        cudaStream_t cap = static_cast<cudaStream_t>(capture_stream_);
+        const uint64_t before = veda_launch_count();
+        cudaGraph_t graph = nullptr;
+        cuda_check(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal), "step capture");
+        set_current_stream(cap);
+        try
+        {
+            step_impl(ids_, targets_);
+        }
+        catch (...)
+        {
+            set_current_stream(caller);
+            cudaStreamEndCapture(cap, &graph);
+            if (graph != nullptr) cudaGraphDestroy(graph);
+            use_graph_ = false;   // later steps run eagerly
+            throw;
+        }
+        set_current_stream(caller);
+        cuda_check(cudaStreamEndCapture(cap, &graph), "step capture");
+        const cudaError_t e = cudaGraphInstantiateWithFlags(&graph_exec_, graph,
+                                                            cudaGraphInstantiateFlagAutoFreeOnLaunch);
+        cudaGraphDestroy(graph);
+        cuda_check(e, "step graph instantiate");
+        graph_launches_ = static_cast<int64_t>(veda_launch_count() - before);
+        veda_launch_count_add(-graph_launches_);   // captured, not launched
+    }
+    cuda_check(cudaGraphLaunch(graph_exec_, cs()), "step graph launch");
+    veda_launch_count_add(graph_launches_);
+}
+
+namespace
+{
+// While a step is being captured: names the phase in which an operation that cannot be
+// recorded invalidated the capture.
+void capture_checkpoint(const char* phase)
+{
+    cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(cs(), &status) == cudaSuccess &&
+        status == cudaStreamCaptureStatusInvalidated)
+    {
+        throw std::runtime_error(std::string("step capture invalidated during ") + phase + ": " +
+                                 cudaGetErrorString(cudaGetLastError()));
+    }
+}
+} // namespace
+
+void Trainer::step_impl(const Tensor& ids, const Tensor& targets)
 {
     profile::HostScope whole("host:step");
     {
@@ -582,11 +695,13 @@ void Trainer::step(const Tensor& ids, const Tensor& targets)
         profile::HostScope scope("host:forward");
         return model_->forward_device(ids, batch_, length_);
     }();
+    capture_checkpoint("the forward");
     if (dp_)
     {
         dp_->end_forward();
     }
     Variable loss = autograd::cross_entropy_device(logits, targets);
+    capture_checkpoint("the cross-entropy");
     autograd::BackwardOptions options;
     options.retain_intermediate_grads = false;
     if (dp_)
@@ -598,6 +713,7 @@ void Trainer::step(const Tensor& ids, const Tensor& targets)
         profile::HostScope scope("host:backward");
         loss.backward(options);
     }
+    capture_checkpoint("the backward");
     model_->clear_untouched_grads();
     if (dp_)
     {
@@ -614,7 +730,7 @@ void Trainer::step(const Tensor& ids, const Tensor& targets)
         }
         else
         {
-            opt_->step_clipped(max_norm_, 1.0f / static_cast<float>(world()));
+            opt_->launch_clipped(max_norm_, 1.0f / static_cast<float>(world()));
         }
     }
     cuda_check(cudaMemcpyAsync(loss_.data_ptr(), loss.value().data_ptr(), sizeof(float),

@@ -140,8 +140,15 @@ __device__ __forceinline__ float adam_one(float& w, float& m, float& v, float g,
 __global__ void __launch_bounds__(kThreads)
 adamw_kernel(float* __restrict__ master, float* __restrict__ m, float* __restrict__ v,
              float* __restrict__ g, bf16* __restrict__ lowp, int64_t n,
-             const double* __restrict__ sumsq, AdamArgs a, bool vec)
+             const double* __restrict__ sumsq, AdamArgs a, const double* __restrict__ bias, bool vec)
 {
+    if (bias != nullptr)
+    {
+        // bias corrections computed by the host for this step and left in device memory (a step
+        // replayed from a CUDA graph reads the current ones)
+        a.bias1 = bias[0];
+        a.bias2 = bias[1];
+    }
     const float clip = clip_scale(sumsq, a.max_norm, a.grad_scale);
     // an unscaled gradient is already what the write-back would store
     const bool store_g = a.write_grad && (clip != 1.0f || a.grad_scale != 1.0f);
@@ -261,16 +268,18 @@ extern "C" int veda_clip_apply(float* g, int64_t n, const double* sumsq, float m
     return check_launch("veda_clip_apply");
 }
 
-extern "C" int veda_adamw_step(float* master, float* m, float* v, float* g, void* lowp, int64_t n,
-                               float lr, float beta1, float beta2, float eps, float weight_decay,
-                               double bias1, double bias2, const double* sumsq, float max_norm,
-                               float grad_scale, int write_grad, veda_stream_t stream)
+namespace
+{
+int adamw_launch(float* master, float* m, float* v, float* g, void* lowp, int64_t n, float lr,
+                 float beta1, float beta2, float eps, float weight_decay, double bias1, double bias2,
+                 const double* bias_dev, const double* sumsq, float max_norm, float grad_scale,
+                 int write_grad, veda_stream_t stream)
 {
     VEDA_REQUIRE(lr >= 0.0f && eps > 0.0f && weight_decay >= 0.0f,
                  "learning rate, eps and weight decay must be positive");
     VEDA_REQUIRE(beta1 >= 0.0f && beta1 < 1.0f && beta2 >= 0.0f && beta2 < 1.0f,
                  "betas must lie in [0, 1)");
-    VEDA_REQUIRE(bias1 > 0.0 && bias2 > 0.0, "bias corrections must be positive");
+    VEDA_REQUIRE(bias_dev != nullptr || (bias1 > 0.0 && bias2 > 0.0), "bias corrections must be positive");
     VEDA_REQUIRE(sumsq == nullptr || max_norm > 0.0f, "max_norm must be positive");
     VEDA_REQUIRE(n >= 0, "bad size");
     if (n == 0)
@@ -284,7 +293,34 @@ extern "C" int veda_adamw_step(float* master, float* m, float* v, float* g, void
                write_grad};
     const unsigned grid = grid_for(vec ? n / 4 + 1 : n, kThreads, 4);
     adamw_kernel<<<grid, kThreads, 0, stream>>>(master, m, v, g, static_cast<bf16*>(lowp), n,
-                                                sumsq, a, vec);
+                                                sumsq, a, bias_dev, vec);
     count_launch();
     return check_launch("veda_adamw_step");
+}
+} // namespace
+
+extern "C" int veda_adamw_step(float* master, float* m, float* v, float* g, void* lowp, int64_t n,
+                               float lr, float beta1, float beta2, float eps, float weight_decay,
+                               double bias1, double bias2, const double* sumsq, float max_norm,
+                               float grad_scale, int write_grad, veda_stream_t stream)
+{
+    return adamw_launch(master, m, v, g, lowp, n, lr, beta1, beta2, eps, weight_decay, bias1, bias2,
+                        nullptr, sumsq, max_norm, grad_scale, write_grad, stream);
+}
+
+extern "C" int veda_adamw_step_dev(float* master, float* m, float* v, float* g, void* lowp,
+                                   int64_t n, float lr, float beta1, float beta2, float eps,
+                                   float weight_decay, const double* bias, const double* sumsq,
+                                   float max_norm, float grad_scale, int write_grad,
+                                   veda_stream_t stream)
+{
+    VEDA_REQUIRE(bias != nullptr, "null bias corrections");
+    return adamw_launch(master, m, v, g, lowp, n, lr, beta1, beta2, eps, weight_decay, 0.0, 0.0,
+                        bias, sumsq, max_norm, grad_scale, write_grad, stream);
+}
+
+extern "C" int veda_launch_count_add(int64_t n)
+{
+    count_launch(static_cast<uint64_t>(n));
+    return VEDA_OK;
 }

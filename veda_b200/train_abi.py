@@ -34,6 +34,7 @@ SIGNATURES = {
     "veda_trainer_init_dp": (_i, [_p, _p, _i, _i, _sz]),
     "veda_trainer_init_dp_sharded": (_i, [_p, _p, _i, _i, _sz]),
     "veda_trainer_sync": (_i, [_p]),
+    "veda_trainer_set_step_graph": (_i, [_p, _i]),
     "veda_corpus_create": (_i, [_p, _i64, C.c_double, C.c_uint64, _p]),
     "veda_corpus_destroy": (_i, [_p]),
     "veda_corpus_boundary": (_i64, [_p]),
@@ -132,6 +133,9 @@ class Trainer:
 
     def load(self, directory: str):
         _check(self.L, self.L.veda_trainer_load_checkpoint(self.h, str(directory).encode()))
+
+    def set_step_graph(self, on: bool):
+        _check(self.L, self.L.veda_trainer_set_step_graph(self.h, 1 if on else 0))
 
     def sync(self):
         """The current stream waits for the trainer's queued communication."""
