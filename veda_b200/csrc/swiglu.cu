@@ -11,37 +11,69 @@ namespace veda::cuda
 namespace
 {
 
-__device__ __forceinline__ float silu_of(float g) { return g / (1.0f + expf(-g)); }
+// sigmoid(g) = 1 / (1 + e^-g) with the hardware exponential and reciprocal-divide: a few ulp,
+// far inside the fp32 tolerance, and exact at the ends (e^-g = inf gives 0, e^-g = 0 gives 1)
+__device__ __forceinline__ float sigmoid_of(float g) { return __fdividef(1.0f, 1.0f + __expf(-g)); }
 
+template <typename T, int V>
+__device__ __forceinline__ void load_vec(const T* p, float (&out)[V])
+{
+    if constexpr (V == 1)
+        out[0] = to_f32(*p);
+    else
+        load16(p, out);
+}
+
+template <typename T, int V>
+__device__ __forceinline__ void store_vec(T* p, const float (&in)[V])
+{
+    if constexpr (V == 1)
+        *p = from_f32<T>(in[0]);
+    else
+        store16(p, in);
+}
+
+// rows a thread loads before computing (bytes in flight); four in the forward measured slower
+// (fewer blocks fit an SM)
+constexpr int kFwdRows = 2;
+constexpr int kBwdRows = 2;
+
+// Row-blocked: a block takes kFwdRows (kBwdRows) rows at a time, its threads the 16-byte vectors of
+// those rows, so no index needs a division and every thread keeps two rows' loads in flight.
 template <typename T, bool VEC>
 __global__ void swiglu_fwd_kernel(const T* __restrict__ gate, int64_t ldg, const T* __restrict__ up,
                                   int64_t ldu, T* __restrict__ h, int64_t ldh, int64_t rows,
                                   int64_t n)
 {
     constexpr int V = VEC ? Vec16<T>::N : 1;
-    const int64_t per_row = n / V;
-    const int64_t total = rows * per_row;
-    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    constexpr int U = kFwdRows;
+    const int64_t nv = n / V;
+    for (int64_t r0 = static_cast<int64_t>(blockIdx.x) * U; r0 < rows;
+         r0 += static_cast<int64_t>(gridDim.x) * U)
     {
-        const int64_t r = idx / per_row;
-        const int64_t c = (idx - r * per_row) * V;
-        if constexpr (VEC)
+        for (int64_t cv = threadIdx.x; cv < nv; cv += blockDim.x)
         {
-            float g[V], u[V];
-            load16(gate + r * ldg + c, g);
-            load16(up + r * ldu + c, u);
+            const int64_t c = cv * V;
+            float g[U][V], u[U][V];
 #pragma unroll
-            for (int j = 0; j < V; ++j)
+            for (int k = 0; k < U; ++k)
             {
-                g[j] = silu_of(g[j]) * u[j];
+                if (r0 + k < rows)
+                {
+                    load_vec<T, V>(gate + (r0 + k) * ldg + c, g[k]);
+                    load_vec<T, V>(up + (r0 + k) * ldu + c, u[k]);
+                }
             }
-            store16(h + r * ldh + c, g);
-        }
-        else
-        {
-            const float g = to_f32(gate[r * ldg + c]);
-            h[r * ldh + c] = from_f32<T>(silu_of(g) * to_f32(up[r * ldu + c]));
+#pragma unroll
+            for (int k = 0; k < U; ++k)
+            {
+                if (r0 + k < rows)
+                {
+#pragma unroll
+                    for (int j = 0; j < V; ++j) g[k][j] = g[k][j] * sigmoid_of(g[k][j]) * u[k][j];
+                    store_vec<T, V>(h + (r0 + k) * ldh + c, g[k]);
+                }
+            }
         }
     }
 }
@@ -53,47 +85,60 @@ __global__ void swiglu_bwd_kernel(const T* __restrict__ gate, int64_t ldg, const
                                   int64_t lddu, int64_t rows, int64_t n)
 {
     constexpr int V = VEC ? Vec16<T>::N : 1;
-    const int64_t per_row = n / V;
-    const int64_t total = rows * per_row;
-    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    constexpr int U = kBwdRows;
+    const int64_t nv = n / V;
+    for (int64_t r0 = static_cast<int64_t>(blockIdx.x) * U; r0 < rows;
+         r0 += static_cast<int64_t>(gridDim.x) * U)
     {
-        const int64_t r = idx / per_row;
-        const int64_t c = (idx - r * per_row) * V;
-        float g[V], u[V], d[V];
-        if constexpr (VEC)
+        for (int64_t cv = threadIdx.x; cv < nv; cv += blockDim.x)
         {
-            load16(gate + r * ldg + c, g);
-            load16(up + r * ldu + c, u);
-            load16(dh + r * lddh + c, d);
-        }
-        else
-        {
-            g[0] = to_f32(gate[r * ldg + c]);
-            u[0] = to_f32(up[r * ldu + c]);
-            d[0] = to_f32(dh[r * lddh + c]);
-        }
-        float dg[V], du[V];
+            const int64_t c = cv * V;
+            float g[U][V], u[U][V], d[U][V];
 #pragma unroll
-        for (int j = 0; j < V; ++j)
-        {
-            const float e = expf(-g[j]);
-            const float s = 1.0f / (1.0f + e);
-            const float through = d[j] * u[j];
-            dg[j] = through * s * (1.0f + g[j] * (1.0f - s));
-            du[j] = d[j] * (g[j] / (1.0f + e));
-        }
-        if constexpr (VEC)
-        {
-            store16(dgate + r * lddg + c, dg);
-            store16(dup + r * lddu + c, du);
-        }
-        else
-        {
-            dgate[r * lddg + c] = from_f32<T>(dg[0]);
-            dup[r * lddu + c] = from_f32<T>(du[0]);
+            for (int k = 0; k < U; ++k)
+            {
+                if (r0 + k < rows)
+                {
+                    load_vec<T, V>(gate + (r0 + k) * ldg + c, g[k]);
+                    load_vec<T, V>(up + (r0 + k) * ldu + c, u[k]);
+                    load_vec<T, V>(dh + (r0 + k) * lddh + c, d[k]);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < U; ++k)
+            {
+                if (r0 + k < rows)
+                {
+                    float dg[V], du[V];
+#pragma unroll
+                    for (int j = 0; j < V; ++j)
+                    {
+                        const float sg = sigmoid_of(g[k][j]);
+                        const float through = d[k][j] * u[k][j];
+                        dg[j] = through * sg * (1.0f + g[k][j] * (1.0f - sg));
+                        du[j] = d[k][j] * (g[k][j] * sg);
+                    }
+                    store_vec<T, V>(dgate + (r0 + k) * lddg + c, dg);
+                    store_vec<T, V>(dup + (r0 + k) * lddu + c, du);
+                }
+            }
         }
     }
+}
+
+// Block size: the row's vectors rounded up to warps (one vector per thread per row), 64-512.
+unsigned row_threads(int64_t nv)
+{
+    int64_t t = (nv + 31) / 32 * 32;
+    t = t < 64 ? 64 : (t > 512 ? 512 : t);
+    return static_cast<unsigned>(t);
+}
+
+unsigned row_blocks(int64_t rows, unsigned threads, int rows_per_block)
+{
+    const int64_t want = (rows + rows_per_block - 1) / rows_per_block;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / threads);
+    return static_cast<unsigned>(want < cap ? want : cap);
 }
 
 bool vec_ok(const void* p, int64_t ld, int64_t n, size_t es)
@@ -120,10 +165,10 @@ extern "C" int veda_swiglu_fwd(const void* gate, int64_t ldg, const void* up, in
     VEDA_REQUIRE(gate && up && h, "null pointer");
     const size_t es = dtype_size(dtype);
     const bool vec = vec_ok(gate, ldg, n, es) && vec_ok(up, ldu, n, es) && vec_ok(h, ldh, n, es);
-    const int64_t work = rows * (vec ? n / (16 / static_cast<int64_t>(es)) : n);
-    const unsigned grid = grid_for(work, 256);
+    const unsigned threads = row_threads(vec ? n / (16 / static_cast<int64_t>(es)) : n);
+    const unsigned grid = row_blocks(rows, threads, kFwdRows);
 #define VEDA_SW_FWD(T, VEC)                                                                       \
-    swiglu_fwd_kernel<T, VEC><<<grid, 256, 0, stream>>>(static_cast<const T*>(gate), ldg,        \
+    swiglu_fwd_kernel<T, VEC><<<grid, threads, 0, stream>>>(static_cast<const T*>(gate), ldg,        \
                                                         static_cast<const T*>(up), ldu,          \
                                                         static_cast<T*>(h), ldh, rows, n)
     if (dtype == VEDA_BF16)
@@ -157,10 +202,10 @@ extern "C" int veda_swiglu_bwd(const void* gate, int64_t ldg, const void* up, in
     const bool vec = vec_ok(gate, ldg, n, es) && vec_ok(up, ldu, n, es) &&
                      vec_ok(dh, lddh, n, es) && vec_ok(dgate, lddg, n, es) &&
                      vec_ok(dup, lddu, n, es);
-    const int64_t work = rows * (vec ? n / (16 / static_cast<int64_t>(es)) : n);
-    const unsigned grid = grid_for(work, 256);
+    const unsigned threads = row_threads(vec ? n / (16 / static_cast<int64_t>(es)) : n);
+    const unsigned grid = row_blocks(rows, threads, kBwdRows);
 #define VEDA_SW_BWD(T, VEC)                                                                       \
-    swiglu_bwd_kernel<T, VEC><<<grid, 256, 0, stream>>>(                                          \
+    swiglu_bwd_kernel<T, VEC><<<grid, threads, 0, stream>>>(                                          \
         static_cast<const T*>(gate), ldg, static_cast<const T*>(up), ldu,                        \
         static_cast<const T*>(dh), lddh, static_cast<T*>(dgate), lddg, static_cast<T*>(dup),     \
         lddu, rows, n)
