@@ -783,8 +783,11 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
 
 
 // dQ[q-tile] = sum over key tiles of dS K, from dS^T stored as [B*H][keys][queries].
-// One CTA per (batch, head, 128-query tile); warp 0 TMA (3-stage ring of a dS^T tile and a K tile),
-// warp 1 MMA (M128 queries, N128 dims, K128 keys; both operands MN-major), warps 2-5 epilogue.
+// Persistent: one CTA per SM walks the (batch, head, 128-query tile) items, longest first, with
+// the TMA ring (a dS^T tile and a K tile per stage) streaming across item boundaries and two TMEM
+// accumulators, so one item's epilogue overlaps the next item's products (a CTA per item paid the
+// ring's fill and the epilogue on every short item). Warp 0 TMA, warp 1 MMA (M128 queries, N128
+// dims, K128 keys; both operands MN-major), warps 2-5 epilogue.
 constexpr int kDqStages = 3;
 constexpr int kDqSmem = 1024 + kDqStages * 2 * kTileBytes + 256;
 
@@ -792,11 +795,18 @@ struct DqParams
 {
     bf16* dq;
     int64_t lddq;
-    int T, H, Hkv;
+    int T, H, Hkv, B;
     float scale;
     int causal;
     int* status;
 };
+
+// item k -> (query tile, batch*head), heaviest (latest) query tiles first
+__device__ __forceinline__ void dq_item(int k, int bhs, int nq, int& qt, int& bh)
+{
+    qt = nq - 1 - k / bhs;
+    bh = k % bhs;
+}
 
 __global__ void __launch_bounds__(192, 1)
 attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tds, const __grid_constant__ CUtensorMap tk,
@@ -808,19 +818,18 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tds, const __grid_constant
     uint8_t* sds = smem;                                   // [stages]
     uint8_t* sk = sds + kDqStages * kTileBytes;            // [stages]
     uint64_t* bars = reinterpret_cast<uint64_t*>(sk + kDqStages * kTileBytes);
-    uint64_t* full = bars;                  // [stages]
-    uint64_t* empty = bars + kDqStages;     // [stages]
-    uint64_t* done = bars + 2 * kDqStages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* full = bars;                     // [stages]
+    uint64_t* empty = bars + kDqStages;        // [stages]
+    uint64_t* acc_full = bars + 2 * kDqStages;       // [2]
+    uint64_t* acc_empty = bars + 2 * kDqStages + 2;  // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kDqStages + 4);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nq = (p.T + 127) / 128;
-    const int qt = nq - 1 - static_cast<int>(blockIdx.y);   // longest rows first
-    const int bh = blockIdx.x;
-    const int b = bh / p.H, h = bh % p.H;
-    const int kvh = h / (p.H / p.Hkv);
-    const int nk = p.causal ? qt + 1 : nq;
+    const int bhs = p.B * p.H;
+    const int items = bhs * nq;
+    const int rep = p.H / p.Hkv;
 
     if (threadIdx.x == 0)
     {
@@ -830,12 +839,16 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tds, const __grid_constant
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(done, 1);
+        for (int i = 0; i < 2; ++i)
+        {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 4);   // one arrival per epilogue warp
+        }
         mbar_fence_init();
     }
     if (warp == 1)
     {
-        tmem_alloc(tmem_slot, 128);
+        tmem_alloc(tmem_slot, 256);
     }
     fence_before();
     __syncthreads();
@@ -846,61 +859,91 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tds, const __grid_constant
     {
         tma_prefetch(&tds);
         tma_prefetch(&tk);
-        for (int j = 0; j < nk; ++j)
+        int g = 0;   // stages issued so far
+        for (int k = blockIdx.x; k < items; k += gridDim.x)
         {
-            const int s = j % kDqStages;
-            mbar_wait(&empty[s], ((j / kDqStages) & 1) ^ 1, p.status, abort);
-            mbar_expect_tx(&full[s], 2 * kTileBytes);
-            // dS^T tile: rows = keys j*128.., columns = this tile's 128 queries
-            load_tile_3d(sds + s * kTileBytes, &tds, &full[s], qt * 128, j * 128, bh);
-            load_tile_3d(sk + s * kTileBytes, &tk, &full[s], kvh * 128, j * 128, b);
+            int qt, bh;
+            dq_item(k, bhs, nq, qt, bh);
+            const int b = bh / p.H, kvh = (bh % p.H) / rep;
+            const int nk = p.causal ? qt + 1 : nq;
+            for (int j = 0; j < nk; ++j, ++g)
+            {
+                const int s = g % kDqStages;
+                mbar_wait(&empty[s], ((g / kDqStages) & 1) ^ 1, p.status, abort);
+                mbar_expect_tx(&full[s], 2 * kTileBytes);
+                // dS^T tile: rows = keys j*128.., columns = this item's 128 queries
+                load_tile_3d(sds + s * kTileBytes, &tds, &full[s], qt * 128, j * 128, bh);
+                load_tile_3d(sk + s * kTileBytes, &tk, &full[s], kvh * 128, j * 128, b);
+            }
         }
     }
     else if (warp == 1 && lane == 0)
     {
         constexpr uint32_t idesc = instr_desc(128, 128, true, true);
-        for (int j = 0; j < nk; ++j)
+        int g = 0, i = 0;
+        for (int k = blockIdx.x; k < items; k += gridDim.x, ++i)
         {
-            const int s = j % kDqStages;
-            mbar_wait(&full[s], (j / kDqStages) & 1, p.status, abort);
+            int qt, bh;
+            dq_item(k, bhs, nq, qt, bh);
+            const int nk = p.causal ? qt + 1 : nq;
+            const int buf = i & 1;
+            // the epilogue has drained this accumulator (item i - 2)
+            mbar_wait(&acc_empty[buf], ((i >> 1) & 1) ^ 1, p.status, abort);
             fence_after();
-            const uint32_t a_base = smem_u32(sds + s * kTileBytes);
-            const uint32_t b_base = smem_u32(sk + s * kTileBytes);
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks)
+            for (int j = 0; j < nk; ++j, ++g)
             {
-                mma(tmem, mnmajor_desc(a_base, ks, kHalf), mnmajor_desc(b_base, ks, kHalf), idesc,
-                    (j > 0 || ks > 0) ? 1u : 0u);
+                const int s = g % kDqStages;
+                mbar_wait(&full[s], (g / kDqStages) & 1, p.status, abort);
+                fence_after();
+                const uint32_t a_base = smem_u32(sds + s * kTileBytes);
+                const uint32_t b_base = smem_u32(sk + s * kTileBytes);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+                {
+                    mma(tmem + buf * 128, mnmajor_desc(a_base, ks, kHalf), mnmajor_desc(b_base, ks, kHalf),
+                        idesc, (j > 0 || ks > 0) ? 1u : 0u);
+                }
+                commit(&empty[s]);
             }
-            commit(&empty[s]);
+            commit(&acc_full[buf]);
         }
-        commit(done);
     }
     else if (warp >= 2)
     {
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
-        const int query = qt * 128 + r;
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-        mbar_wait(done, 0, p.status, abort);
-        fence_after();
-        bf16* row = p.dq + (static_cast<int64_t>(b) * p.T + query) * p.lddq + static_cast<int64_t>(h) * 128;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c)
+        int i = 0;
+        for (int k = blockIdx.x; k < items; k += gridDim.x, ++i)
         {
-            uint32_t raw[32];
-            tmem_ld32(tmem + lane_base + c * 32, raw);
-            if (query < p.T)
+            int qt, bh;
+            dq_item(k, bhs, nq, qt, bh);
+            const int b = bh / p.H, h = bh % p.H;
+            const int query = qt * 128 + r;
+            const int buf = i & 1;
+            mbar_wait(&acc_full[buf], (i >> 1) & 1, p.status, abort);
+            fence_after();
+            bf16* row = p.dq + (static_cast<int64_t>(b) * p.T + query) * p.lddq + static_cast<int64_t>(h) * 128;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c)
             {
-#pragma unroll
-                for (int e = 0; e < 32; e += 8)
+                uint32_t raw[32];
+                tmem_ld32(tmem + lane_base + buf * 128 + c * 32, raw);
+                if (query < p.T)
                 {
-                    float v8[8];
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) v8[q] = nk > 0 ? __uint_as_float(raw[e + q]) * p.scale : 0.0f;
-                    store16(row + c * 32 + e, v8);
+                    for (int e = 0; e < 32; e += 8)
+                    {
+                        float v8[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) v8[q] = __uint_as_float(raw[e + q]) * p.scale;
+                        store16(row + c * 32 + e, v8);
+                    }
                 }
             }
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
     }
     fence_before();
@@ -908,7 +951,7 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tds, const __grid_constant
     if (warp == 1)
     {
         fence_after();
-        tmem_dealloc(tmem, 128);
+        tmem_dealloc(tmem, 256);
     }
 }
 
@@ -1071,8 +1114,9 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     const dim3 grid(static_cast<unsigned>(B * Hkv), static_cast<unsigned>((T + 127) / 128));
     attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, mds, p);
     DqParams pq{static_cast<bf16*>(dq), lddq, static_cast<int>(T), static_cast<int>(H),
-                static_cast<int>(Hkv), scale, causal, device_status_ptr()};
-    const dim3 gq(static_cast<unsigned>(B * H), static_cast<unsigned>((T + 127) / 128));
+                static_cast<int>(Hkv), static_cast<int>(B), scale, causal, device_status_ptr()};
+    const int64_t dq_items = B * H * ((T + 127) / 128);
+    const unsigned gq = static_cast<unsigned>(dq_items < compute_sms() ? dq_items : compute_sms());
     attn_dq_tc_kernel<<<gq, 192, kDqSmem, s>>>(mds, mk, pq);
     count_launch(3);
     return check_launch("veda_attention_bwd (tcgen05)");
