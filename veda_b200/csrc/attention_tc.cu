@@ -956,32 +956,51 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tds, const __grid_constant
 }
 
 // D = rowsum(dO * O) and -LSE log2(e) for every (batch, head, query); 16 threads per (token, head)
-// row, rows in token-major order so a warp reads two contiguous 256-byte rows of O and dO.
+// row, rows in token-major order so a warp reads two contiguous 256-byte rows of O and dO. Each
+// 16-lane group keeps kRowdotRows rows' loads in flight (one row at a time left the loads
+// latency-bound).
+constexpr int kRowdotRows = 4;
+
 __global__ void attn_rowdot_kernel(const bf16* __restrict__ o, int64_t ldo,
                                    const bf16* __restrict__ dout, int64_t lddo,
                                    const float* __restrict__ lse, float* __restrict__ dvec,
                                    float* __restrict__ nlse2, int64_t B, int64_t T, int64_t H)
 {
     const int sub = threadIdx.x & 15;
+    // the two 16-lane groups of a warp may leave the loop at different iterations: shuffles
+    // name only the group's own lanes
+    const unsigned half = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
     const int64_t rows = B * T * H;
-    const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 4;
-    for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4; r < rows; r += stride)
+    const int64_t groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 4;
+    const int64_t group = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
+    for (int64_t r0 = group * kRowdotRows; r0 < rows; r0 += groups * kRowdotRows)
     {
-        const int64_t h = r % H, bt = r / H;
-        float x[8], y[8];
-        load16(o + bt * ldo + h * 128 + sub * 8, x);
-        load16(dout + bt * lddo + h * 128 + sub * 8, y);
-        float s = 0.0f;
+        float x[kRowdotRows][8], y[kRowdotRows][8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) s += x[e] * y[e];
-#pragma unroll
-        for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, off);
-        if (sub == 0)
+        for (int u = 0; u < kRowdotRows; ++u)
         {
-            const int64_t b = bt / T, t = bt % T;
-            const int64_t at = (b * H + h) * T + t;
-            dvec[at] = s;
-            nlse2[at] = -lse[at] * kLog2e;
+            const int64_t r = r0 + u < rows ? r0 + u : rows - 1;
+            const int64_t h = r % H, bt = r / H;
+            load16(o + bt * ldo + h * 128 + sub * 8, x[u]);
+            load16(dout + bt * lddo + h * 128 + sub * 8, y[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < kRowdotRows; ++u)
+        {
+            float s = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s += x[u][e] * y[u][e];
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(half, s, off);
+            const int64_t r = r0 + u;
+            if (sub == 0 && r < rows)
+            {
+                const int64_t h = r % H, bt = r / H;
+                const int64_t b = bt / T, t = bt % T;
+                const int64_t at = (b * H + h) * T + t;
+                dvec[at] = s;
+                nlse2[at] = -lse[at] * kLog2e;
+            }
         }
     }
 }
@@ -1106,7 +1125,7 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     }
     bf16* ds = static_cast<bf16*>(extra);
     float* nlse2 = reinterpret_cast<float*>(static_cast<char*>(extra) + tc_bwd_ds_bytes(B, T, H));
-    attn_rowdot_kernel<<<grid_for(B * H * T * 16, 256), 256, 0, s>>>(
+    attn_rowdot_kernel<<<grid_for(B * H * T * 16 / kRowdotRows, 256), 256, 0, s>>>(
         static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, lse, dvec, nlse2, B, T, H);
     BwdParams p{nlse2, dvec, static_cast<bf16*>(dk), static_cast<bf16*>(dv), ds, lddk, lddv,
                 static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
