@@ -30,6 +30,11 @@
 
 struct CUgraphExec_st;
 
+namespace veda::generate
+{
+class Generator;
+}
+
 namespace veda::train
 {
 
@@ -102,6 +107,7 @@ public:
 private:
     autograd::Variable forward_from(const autograd::Variable& x, size_t batch, size_t length);
 
+    friend class generate::Generator;   // reads the weights for inference
     ModelConfig config_;
     core::DType dtype_;
     core::Tensor values_, grads_;

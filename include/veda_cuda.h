@@ -274,6 +274,12 @@ int veda_gelu_bwd(const void* x, const void* g, void* dx, int64_t n, int dtype,
  * (generate::greedy_of, src/libs/generate/Sampling.cpp:97-113). */
 int veda_argmax(const void* x, int64_t ld, int64_t rows, int64_t n, int64_t* out, int* status,
                 int dtype, veda_stream_t stream);
+/* One query row per head against a KV cache (generation): out[h] = softmax(q[h] . k[j] * scale
+ * over j < len) . v[j], k/v rows of len positions at stride ldkv holding kv_heads heads; query
+ * head h reads KV head h / (heads / kv_heads) (ScaledDotProductAttention.cpp:138-191, one row). */
+int veda_attention_decode(const void* q, const void* k, const void* v, int64_t ldkv, int64_t len,
+                          int64_t heads, int64_t kv_heads, int64_t head_dim, float scale,
+                          void* out, int dtype, veda_stream_t stream);
 /* Seeded N(0, std) fill (counter-based hash + Box-Muller) for synthetic weights. */
 int veda_randn(void* x, int64_t n, float std, uint64_t seed, int dtype, veda_stream_t stream);
 /* fp32 -> bf16 rounding copy (round to nearest even). */

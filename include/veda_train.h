@@ -94,6 +94,17 @@ int64_t veda_corpus_boundary(const veda_corpus* c);
 int veda_corpus_next_batch(veda_corpus* c, int64_t batch, int64_t length, int split,
                            int64_t* inputs, int64_t* targets);
 
+/* Greedy generation with the trainer's current weights (generate::Generator with a
+ * GreedySampler, src/libs/generate/Generator.cpp:20-109, Sampling.cpp:97-113): cached = 1
+ * prefills a device KV cache once and feeds one token per step; cached = 0 reruns the forward over
+ * the whole sequence. Writes up to max_new_tokens ids to out, their count, whether a stop token
+ * ended it (never emitted) and the number of forward passes. A NaN logit is an error. */
+int veda_trainer_generate(veda_trainer* t, const int32_t* prompt, int64_t n, int64_t max_new_tokens,
+                          const int32_t* stop_tokens, int64_t n_stop, int cached, int32_t* out,
+                          int64_t* out_count, int* stopped, int64_t* forward_passes);
+/* The fp32 logits [vocab] of the last of n ids after a forward with the current weights. */
+int veda_trainer_last_logits(veda_trainer* t, const int32_t* ids, int64_t n, float* out);
+
 /* The current stream waits for all communication the trainer has queued: a step with a sharded
  * optimizer returns with the all-gather of its updated weights still running (the next step's
  * forward waits for each bucket where it first reads it). Call before timing the end of a run or

@@ -596,3 +596,55 @@ class Corpus:
             inputs[row] = self.ids[start:start + length]
             targets[row] = self.ids[start + 1:start + length + 1]
         return inputs, targets
+
+
+# ---- generation --------------------------------------------------------------------------------
+def forward_logits(c: ModelConfig, params, ids):
+    """Logits [T, V] of one sequence (the forward of forward_backward, Model.cpp:206-255)."""
+    ids = np.asarray(ids, dtype=np.int64).reshape(1, -1)
+    T = ids.shape[1]
+    D, H, Hk, Dh = c.hidden, c.heads, c.kv_heads, c.head_dim
+    embed, layers, final = _unpack(c, params)
+    cos, sin = rope_tables(T, Dh, c.theta)
+    scale = F32(1.0) / F32(math.sqrt(Dh))
+
+    def heads_of(a, nh):
+        return a.reshape(1, T, nh, Dh).transpose(0, 2, 1, 3)
+
+    x = embedding(embed, ids)
+    for L in layers:
+        a, _, _ = rms_norm_gamma(x, L["in_norm"], c.eps)
+        q, k, v = ((a @ L[n].T).astype(F32) for n in ("q", "k", "v"))
+        qn, _, _ = rms_norm_gamma(heads_of(q, H), L["q_norm"], c.eps)
+        kn, _, _ = rms_norm_gamma(heads_of(k, Hk), L["k_norm"], c.eps)
+        ctx, _, _ = attention(rope(qn, cos, sin), rope(kn, cos, sin), heads_of(v, Hk), scale)
+        ctx = np.ascontiguousarray(ctx.transpose(0, 2, 1, 3)).reshape(T, -1)
+        x = (x + ctx @ L["o"].T).astype(F32)
+        b, _, _ = rms_norm_gamma(x, L["post_norm"], c.eps)
+        h = swiglu((b @ L["gate"].T).astype(F32), (b @ L["up"].T).astype(F32))
+        x = (x + h @ L["down"].T).astype(F32)
+    xf, _, _ = rms_norm_gamma(x, final, c.eps)
+    return (xf @ embed.T).astype(F32)
+
+
+def greedy(logits):
+    """The first index of the largest logit; NaN raises (Sampling.cpp:97-113)."""
+    logits = np.asarray(logits, dtype=F32).ravel()
+    if np.isnan(logits).any():
+        raise ValueError("generate: a logit is NaN")
+    return int(np.argmax(logits))   # numpy returns the first maximum
+
+
+def generate(c: ModelConfig, params, prompt, max_new_tokens, stop_tokens=()):
+    """The uncached generation loop of Generator.cpp:20-55 with greedy sampling: (tokens,
+    stopped_on_token, forward_passes)."""
+    ids = list(prompt)
+    out, passes = [], 0
+    for _ in range(max_new_tokens):
+        nxt = greedy(forward_logits(c, params, ids)[-1])
+        passes += 1
+        if nxt in stop_tokens:
+            return out, True, passes
+        out.append(nxt)
+        ids.append(nxt)
+    return out, False, passes

@@ -1,0 +1,92 @@
+"""Greedy generation on the device (src/libs/generate/Generator.cpp:20-109, Sampling.cpp:97-113)
+against the oracle's uncached loop, and the KV-cached loop against the uncached one (the
+reference's acceptance rule for its cache)."""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import veda_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+QWEN_SMALL = O.ModelConfig(vocab=2048, hidden=256, intermediate=512, layers=2, heads=4,
+                           kv_heads=2, head_dim=128, eps=1e-6, theta=1e6)
+
+
+@pytest.fixture(autouse=True)
+def _gpu(cuda):
+    yield
+
+
+def trainer(cfg, dtype, params):
+    from veda_b200.train_abi import Trainer
+    t = Trainer(cfg, dtype=dtype, batch=1, seq_len=8, seed=1)
+    t.set_params(np.concatenate([p.ravel() for p in params]))
+    return t
+
+
+@pytest.mark.parametrize("dtype,heads,kv,dh,length", [(0, 4, 2, 16, 1), (0, 4, 2, 16, 37),
+                                                      (1, 16, 8, 128, 1000), (1, 4, 4, 64, 5)])
+def test_attention_decode_matches_softmax_row(dtype, heads, kv, dh, length):
+    import torch
+    import veda_b200 as V
+    from tests.gpu_util import bf, call, stream
+    r = np.random.default_rng(length + dh)
+    q = r.standard_normal((heads, dh)).astype(np.float32)
+    k = r.standard_normal((length, kv * dh)).astype(np.float32)
+    v = r.standard_normal((length, kv * dh)).astype(np.float32)
+    if dtype == 1:
+        q, k, v = bf(q), bf(k), bf(v)
+    scale = 1.0 / math.sqrt(dh)
+    ref = np.empty((heads, dh), np.float32)
+    for h in range(heads):
+        g = h // (heads // kv)
+        kh, vh = k[:, g * dh:(g + 1) * dh], v[:, g * dh:(g + 1) * dh]
+        s = (kh @ q[h]) * scale
+        p = np.exp(s - s.max())
+        ref[h] = (p / p.sum()) @ vh
+    tdt = torch.float32 if dtype == 0 else torch.bfloat16
+    dq, dk, dv = (torch.from_numpy(a).to("cuda").to(tdt) for a in (q, k, v))
+    out = torch.empty((heads, dh), dtype=tdt, device="cuda")
+    call("veda_attention_decode", dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), kv * dh, length, heads,
+         kv, dh, scale, out.data_ptr(), V.F32 if dtype == 0 else V.BF16, stream())
+    got = out.float().cpu().numpy()
+    assert O.max_abs_rel(got, ref) <= (1e-5 if dtype == 0 else 2e-2)
+
+
+def test_tiny_fp32_generation_matches_oracle_and_cache():
+    cfg = O.TINY
+    params = O.init_params(cfg, 0)
+    t = trainer(cfg, 0, params)
+    prompt = [5, 77, 300, 12, 1, 480, 33]
+    logits = t.last_logits(prompt)
+    assert O.max_abs_rel(logits, O.forward_logits(cfg, params, prompt)[-1]) <= 1e-4
+    ref, ref_stopped, ref_passes = O.generate(cfg, params, prompt, 12)
+    toks, stopped, passes = t.generate(prompt, 12, cached=False)
+    assert toks == ref and not stopped and passes == ref_passes == 12
+    toks_c, stopped_c, passes_c = t.generate(prompt, 12, cached=True)
+    assert toks_c == ref and not stopped_c and passes_c == 13   # the limit still runs the last feed
+    # a stop token ends the loop and is never emitted
+    stop = ref[2]
+    first = ref.index(stop)
+    toks_s, stopped_s, _ = t.generate(prompt, 12, stop_tokens=[stop], cached=True)
+    assert toks_s == ref[:first] and stopped_s
+    with pytest.raises(ValueError):
+        t.generate([], 4)
+    with pytest.raises(ValueError):
+        t.generate([cfg.vocab], 4)
+    t.close()
+
+
+def test_qwen_shaped_bf16_cached_generation_matches_uncached():
+    cfg = QWEN_SMALL
+    params = O.init_params(cfg, 3, bf16=True)
+    t = trainer(cfg, 1, params)
+    prompt = list(np.random.default_rng(4).integers(0, cfg.vocab, 40))
+    logits = t.last_logits(prompt)
+    assert O.max_abs_rel(logits, O.forward_logits(cfg, params, prompt)[-1]) <= 2e-2
+    toks, _, _ = t.generate(prompt, 16, cached=False)
+    toks_c, _, _ = t.generate(prompt, 16, cached=True)
+    assert len(toks) == 16 and toks_c == toks
+    t.close()

@@ -2,6 +2,7 @@
 #include "veda_train.h"
 #include "veda/checkpoint.hpp"
 #include "veda/data.hpp"
+#include "veda/generate.hpp"
 
 #include "veda/profile.hpp"
 #include "veda/train.hpp"
@@ -11,6 +12,7 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstring>
 #include <memory>
 #include <stdexcept>
@@ -282,6 +284,49 @@ int veda_corpus_next_batch(veda_corpus* c, int64_t batch, int64_t length, int sp
 int veda_trainer_set_step_graph(veda_trainer* t, int on)
 {
     return guarded([&] { t->impl->set_step_graph(on != 0); });
+}
+
+int veda_trainer_generate(veda_trainer* t, const int32_t* prompt, int64_t n, int64_t max_new_tokens,
+                          const int32_t* stop_tokens, int64_t n_stop, int cached, int32_t* out,
+                          int64_t* out_count, int* stopped, int64_t* forward_passes)
+{
+    return guarded([&] {
+        if (n < 0 || max_new_tokens < 0 || n_stop < 0 || (n > 0 && prompt == nullptr) ||
+            (n_stop > 0 && stop_tokens == nullptr) || out_count == nullptr)
+        {
+            throw std::invalid_argument("veda_trainer_generate: bad arguments");
+        }
+        auto& tr = *t->impl;
+        tr.sync();
+        veda::generate::Options o;
+        o.max_new_tokens = static_cast<size_t>(max_new_tokens);
+        o.stop_tokens.assign(stop_tokens, stop_tokens + n_stop);
+        const veda::generate::Generator g(tr.model());
+        const std::vector<int32_t> p(prompt, prompt + n);
+        const veda::generate::Result r = cached ? g.generate_cached(p, o) : g.generate(p, o);
+        if (out != nullptr)
+        {
+            std::copy(r.generated.begin(), r.generated.end(), out);
+        }
+        *out_count = static_cast<int64_t>(r.generated.size());
+        if (stopped) *stopped = r.stopped_on_token ? 1 : 0;
+        if (forward_passes) *forward_passes = static_cast<int64_t>(r.forward_passes);
+    });
+}
+
+int veda_trainer_last_logits(veda_trainer* t, const int32_t* ids, int64_t n, float* out)
+{
+    return guarded([&] {
+        if (n <= 0 || ids == nullptr || out == nullptr)
+        {
+            throw std::invalid_argument("veda_trainer_last_logits: bad arguments");
+        }
+        auto& tr = *t->impl;
+        tr.sync();
+        const veda::generate::Generator g(tr.model());
+        const std::vector<float> l = g.last_logits(std::vector<int32_t>(ids, ids + n));
+        std::copy(l.begin(), l.end(), out);
+    });
 }
 
 int veda_trainer_sync(veda_trainer* t)

@@ -297,6 +297,39 @@ def one_gemm(op, M, N, K, reps):
           flush=True)
 
 
+def decode(prompt_len, new_tokens):
+    """Greedy generation with the KV cache on the Qwen3-0.6B-shaped model (random weights, batch 1):
+    decode tokens/s after the prefill, against the HBM roofline of one step (every weight read
+    once, plus the cache rows attended to)."""
+    import time
+    import types
+    import torch
+    from veda_b200 import train_abi as TA
+    _, hbm, kind = _peaks()
+    cfg = types.SimpleNamespace(vocab=151936, hidden=1024, intermediate=3072, layers=28, heads=16,
+                                kv_heads=8, head_dim=128, eps=1e-6, theta=1e6)
+    t = TA.Trainer(cfg, dtype=1, batch=1, seq_len=8, seed=3)
+    prompt = list(np.random.default_rng(0).integers(0, cfg.vocab, prompt_len))
+    t.generate(prompt, 2, cached=True)   # warm-up
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    _, _, p0 = t.generate(prompt, 0, cached=True)   # the prefill alone
+    t1 = time.perf_counter()
+    toks, _, passes = t.generate(prompt, new_tokens, cached=True)
+    t2 = time.perf_counter()
+    per_token = ((t2 - t1) - (t1 - t0)) / max(1, len(toks))
+    weights = t.n * 2.0
+    kv = 2 * cfg.layers * cfg.kv_heads * cfg.head_dim * 2.0 * (prompt_len + new_tokens / 2)
+    gbs = (weights + kv) / per_token / 1e9
+    print(json.dumps({"bench": "decode", "model": "qwen3-0.6b", "prompt": prompt_len,
+                      "new_tokens": len(toks), "ms_per_token": per_token * 1e3,
+                      "tokens_per_s": 1.0 / per_token, "bytes_per_token": weights + kv,
+                      "gbs": gbs, "frac": gbs / hbm, "peak_kind": kind,
+                      "timing": "host wall clock per token (each token is read back to pick the next)"}),
+          flush=True)
+    t.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -315,7 +348,13 @@ def main():
     d.add_argument("--tokens", type=int, default=8192)
     d.add_argument("--reps", type=int, default=20)
     d.add_argument("--kernels", nargs="+", default=None)
+    e = sub.add_parser("decode")
+    e.add_argument("--prompt", type=int, default=128)
+    e.add_argument("--new-tokens", type=int, default=64)
     args = ap.parse_args()
+    if args.cmd == "decode":
+        decode(args.prompt, args.new_tokens)
+        return
     if args.cmd == "mm-sweep":
         mm_sweep(args.reps)
     elif args.cmd == "attn-bwd":

@@ -34,6 +34,8 @@ SIGNATURES = {
     "veda_trainer_init_dp": (_i, [_p, _p, _i, _i, _sz]),
     "veda_trainer_init_dp_sharded": (_i, [_p, _p, _i, _i, _sz]),
     "veda_trainer_sync": (_i, [_p]),
+    "veda_trainer_generate": (_i, [_p, _p, _i64, _i64, _p, _i64, _i, _p, _p, _p, _p]),
+    "veda_trainer_last_logits": (_i, [_p, _p, _i64, _p]),
     "veda_trainer_set_step_graph": (_i, [_p, _i]),
     "veda_corpus_create": (_i, [_p, _i64, C.c_double, C.c_uint64, _p]),
     "veda_corpus_destroy": (_i, [_p]),
@@ -92,6 +94,7 @@ class Trainer:
         self.h = h
         self.batch, self.seq_len = batch, seq_len
         self.n = int(self.L.veda_trainer_param_count(h))
+        self.cfg_vocab = int(cfg.vocab)
 
     def close(self):
         if self.h:
@@ -136,6 +139,24 @@ class Trainer:
 
     def set_step_graph(self, on: bool):
         _check(self.L, self.L.veda_trainer_set_step_graph(self.h, 1 if on else 0))
+
+    def generate(self, prompt, max_new_tokens, stop_tokens=(), cached=True):
+        """Greedy generation: (tokens, stopped_on_token, forward_passes)."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        st = np.ascontiguousarray(list(stop_tokens) or [0], dtype=np.int32)
+        out = np.empty(max(1, max_new_tokens), np.int32)
+        cnt, stopped, passes = C.c_int64(0), C.c_int(0), C.c_int64(0)
+        _check(self.L, self.L.veda_trainer_generate(self.h, p.ctypes.data if p.size else None, p.size,
+                                                    max_new_tokens, st.ctypes.data, len(stop_tokens),
+                                                    1 if cached else 0, out.ctypes.data, C.byref(cnt),
+                                                    C.byref(stopped), C.byref(passes)))
+        return out[:cnt.value].tolist(), bool(stopped.value), passes.value
+
+    def last_logits(self, ids):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.empty(self.cfg_vocab, np.float32)
+        _check(self.L, self.L.veda_trainer_last_logits(self.h, ids.ctypes.data, ids.size, out.ctypes.data))
+        return out
 
     def sync(self):
         """The current stream waits for the trainer's queued communication."""
