@@ -723,7 +723,8 @@ qknorm_rope_fwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16*
     auto load_row = [&](int64_t r, uint4& a, uint4& b) {
         if (r < rows)
         {
-            const int64_t token = r / heads;
+            // rows < 2^31 (checked by the launcher): 32-bit division
+            const int64_t token = static_cast<uint32_t>(r) / static_cast<uint32_t>(heads);
             const bf16* xr = x + token * ldx + (r - token * heads) * 128;
             a = *reinterpret_cast<const uint4*>(xr + 8 * q);
             b = *reinterpret_cast<const uint4*>(xr + 64 + 8 * q);
@@ -753,8 +754,8 @@ qknorm_rope_fwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16*
         if (row < rows)
         {
             const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
-            const int64_t token = row / heads;
-            const int t = static_cast<int>(token % seq_len);
+            const int64_t token = static_cast<uint32_t>(row) / static_cast<uint32_t>(heads);
+            const int t = static_cast<int>(static_cast<uint32_t>(token) % static_cast<uint32_t>(seq_len));
             float ga[8], gb[8], cs[8], sn[8];
             load16(gamma + 8 * q, ga);
             load16(gamma + 64 + 8 * q, gb);
@@ -798,7 +799,7 @@ qknorm_rope_bwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx,
     auto load_row = [&](int64_t r, uint4& a, uint4& b, uint4& da, uint4& db) {
         if (r < rows)
         {
-            const int64_t token = r / heads;
+            const int64_t token = static_cast<uint32_t>(r) / static_cast<uint32_t>(heads);
             const int64_t h = r - token * heads;
             const bf16* xr = x + token * ldx + h * 128;
             const bf16* gr = dy + token * lddy + h * 128;
@@ -821,8 +822,8 @@ qknorm_rope_bwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx,
         uint4 na, nb, nda, ndb;
         load_row(row + stride, na, nb, nda, ndb);
         const bool valid = row < rows;
-        const int64_t token = valid ? row / heads : 0;
-        const int t = static_cast<int>(token % seq_len);
+        const int64_t token = valid ? static_cast<uint32_t>(row) / static_cast<uint32_t>(heads) : 0;
+        const int t = static_cast<int>(static_cast<uint32_t>(token) % static_cast<uint32_t>(seq_len));
         float cs[8], sn[8], ga[8], gb[8];
         rope_row(cosv, sinv, t, q, cs, sn);
         load16(gamma + 8 * q, ga);
@@ -1402,7 +1403,7 @@ extern "C" int veda_qknorm_rope_fwd(const void* x, int64_t ldx, const void* gamm
     const int64_t rows = tokens * heads;
     const unsigned grid = static_cast<unsigned>(
         std::min<int64_t>((rows + kWarps - 1) / kWarps, static_cast<int64_t>(sm_count()) * 16));
-    if (d128_ok(x, ldx, gamma, cosv, sinv, y, ldy, head_dim, dtype))
+    if (d128_ok(x, ldx, gamma, cosv, sinv, y, ldy, head_dim, dtype) && rows < (1ll << 31))
     {
         const unsigned g4 = static_cast<unsigned>(std::min<int64_t>(
             (rows + 4 * kWarps - 1) / (4 * kWarps), static_cast<int64_t>(sm_count()) * 4));
@@ -1459,7 +1460,7 @@ extern "C" int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamm
     float* partials = dgamma != nullptr ? static_cast<float*>(workspace) : nullptr;
     const size_t smem = partials != nullptr ? kWarps * head_dim * sizeof(float) : 0;
     if (d128_ok(x, ldx, gamma, cosv, sinv, dy, lddy, head_dim, dtype) &&
-        d128_ok(x, ldx, gamma, cosv, sinv, dx, lddx, head_dim, dtype))
+        d128_ok(x, ldx, gamma, cosv, sinv, dx, lddx, head_dim, dtype) && rows < (1ll << 31))
     {
         qknorm_rope_bwd_d128_kernel<<<grid, kWarps * 32, 0, stream>>>(
             static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(gamma), cosv, sinv,
