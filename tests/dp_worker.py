@@ -5,7 +5,8 @@ Each rank trains the Qwen3-shaped bf16 decoder through the C++ trainer on its ow
 flight during the backward). Rank 0 compares the averaged gradient with the oracle's gradient of
 the full batch (both micro-batches, B 4) and every rank checks that the updated weights are the
 same on both ranks. The same step with the optimizer state sharded across the ranks must give the
-same gradients, norm and weights."""
+same gradients, norm and weights. With VEDA_DP_OUT set, rank 0 saves the sharded trainer's
+weights after its three steps there."""
 import datetime
 import os
 import sys
@@ -68,7 +69,7 @@ def main():
     uid = [TA.nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
     ts.init_dp(uid[0], rank, world, 1 << 20, sharded=True)
-    for step in range(2):
+    for step in range(3):
         l_s, n_s = ts.step_host(ids[mine], tg[mine])
         if step == 0:
             assert abs(l_s - loss) <= 1e-6 * abs(loss), (l_s, loss)
@@ -78,11 +79,15 @@ def main():
             w_s = ts.get_params()
             assert np.max(np.abs(w_s - w)) <= 1e-5, np.max(np.abs(w_s - w))
     # the second step ran on the all-gathered bf16 weights: identical on every rank
-    w2 = torch.from_numpy(ts.get_params().astype(np.float64))
+    wfin = ts.get_params()
+    w2 = torch.from_numpy(wfin.astype(np.float64))
     w20 = w2.clone()
     dist.broadcast(w20, src=0)
     assert torch.equal(w2, w20), "sharded ranks diverged"
     if rank == 0:
+        out = os.environ.get("VEDA_DP_OUT")
+        if out:
+            np.save(out, wfin)
         print(f"SHARDED OK loss {l_s:.4f}", flush=True)
     dist.barrier()
     ts.close()

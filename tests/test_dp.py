@@ -131,3 +131,25 @@ def test_nccl_two_gpus_match_full_batch():
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "DP OK" in r.stdout, r.stdout[-2000:]
     assert "SHARDED OK" in r.stdout, r.stdout[-2000:]
+
+
+@pytest.mark.gpu
+@pytest.mark.timeout(900)
+def test_nccl_two_gpus_graph_replay_matches_eager(tmp_path):
+    """The data-parallel steps captured into CUDA graphs (VEDA_DP_GRAPH=1; NCCL calls inside the
+    graph) give the same weights, bit for bit, as the eager steps."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    results = []
+    for graph in ("0", "1"):
+        out = tmp_path / f"w{graph}.npy"
+        env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=str(ROOT), VEDA_DP_GRAPH=graph,
+                   VEDA_DP_OUT=str(out))
+        cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
+               "--nnodes=1", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+               "--master-port", str(_free_port()), str(ROOT / "tests" / "dp_worker.py")]
+        r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=str(ROOT))
+        assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+        results.append(np.load(out))
+    assert np.array_equal(results[0], results[1])

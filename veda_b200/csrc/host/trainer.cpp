@@ -150,6 +150,7 @@ public:
             lowp_s_ = Tensor(Shape({shard_}), DType::BF16);
         }
         sumsq_ = Tensor(Shape({2}), DType::F32);   // one double
+        bias_ = Tensor(Shape({4}), DType::F32);    // two doubles
         const size_t ws = veda_sumsq_workspace(static_cast<int64_t>(shard_));
         ws_ = Tensor::empty(Shape({(ws + 3) / 4 + 1}), DType::F32);
         steps_ = steps;
@@ -223,11 +224,19 @@ public:
     // Sharded step: global norm of the averaged gradient (a sum over the shards), clip + AdamW on
     // this rank's shard (optim::AdamW's arithmetic, AdamW.cpp:38-93), then the updated weights
     // of every bucket all-gathered into the value arena.
-    void update(const optim::AdamWConfig& c, float max_norm)
+    // Counts the step and leaves its bias corrections in device memory (outside any captured
+    // graph: the update's kernel reads them when it runs).
+    void advance(const optim::AdamWConfig& c)
     {
         ++steps_;
-        const double bias1 = 1.0 - std::pow(static_cast<double>(c.beta1), static_cast<double>(steps_));
-        const double bias2 = 1.0 - std::pow(static_cast<double>(c.beta2), static_cast<double>(steps_));
+        bias_host_[0] = 1.0 - std::pow(static_cast<double>(c.beta1), static_cast<double>(steps_));
+        bias_host_[1] = 1.0 - std::pow(static_cast<double>(c.beta2), static_cast<double>(steps_));
+        cuda_check(cudaMemcpyAsync(bias_.data_ptr(), bias_host_, sizeof(bias_host_), cudaMemcpyHostToDevice, cs()),
+                   "sharded bias corrections");
+    }
+
+    void update(const optim::AdamWConfig& c, float max_norm)
+    {
         double* ss = static_cast<double*>(sumsq_.data_ptr());
         float* g = static_cast<float*>(g_s_.data_ptr());
         float* master = static_cast<float*>(master_s_.data_ptr());
@@ -237,11 +246,12 @@ public:
         fork_comm();
         nccl_check(ncclAllReduce(ss, ss, 1, ncclFloat64, ncclSum, comm_, stream_), "norm all-reduce");
         join_comm();
-        check(veda_adamw_step(master, static_cast<float*>(m_s_.data_ptr()),
-                              static_cast<float*>(v_s_.data_ptr()), g,
-                              bf16_ ? lowp_s_.data_ptr() : nullptr, static_cast<int64_t>(shard_),
-                              c.learning_rate, c.beta1, c.beta2, c.eps, c.weight_decay, bias1, bias2,
-                              ss, max_norm, 1.0f / static_cast<float>(world_), 0, current_stream()),
+        check(veda_adamw_step_dev(master, static_cast<float*>(m_s_.data_ptr()),
+                                  static_cast<float*>(v_s_.data_ptr()), g,
+                                  bf16_ ? lowp_s_.data_ptr() : nullptr, static_cast<int64_t>(shard_),
+                                  c.learning_rate, c.beta1, c.beta2, c.eps, c.weight_decay,
+                                  static_cast<const double*>(bias_.data_ptr()), ss, max_norm,
+                                  1.0f / static_cast<float>(world_), 0, current_stream()),
               "sharded AdamW");
         // the weights are gathered in arena order (the order the next forward reads them) and
         // not waited for here: the next forward waits for each bucket where it first needs it
@@ -401,6 +411,9 @@ public:
 
     int world() const noexcept { return world_; }
     bool sharded() const noexcept { return sharded_; }
+    // A step replayed from a CUDA graph ends with its weight gather (the next graph cannot wait
+    // on a bucket event recorded by the previous one).
+    void set_overlap_gather(bool on) noexcept { overlap_gather_ = on; }
 
 private:
     struct Bucket
@@ -473,7 +486,8 @@ private:
     size_t params_ = 0, total_ = 0, shard_ = 0, steps_ = 0;
     std::vector<Bucket> buckets_;
     std::unordered_map<autograd::Node*, std::vector<size_t>> leaf_buckets_;
-    Tensor g_s_, master_s_, m_s_, v_s_, lowp_s_, sumsq_, ws_;
+    Tensor g_s_, master_s_, m_s_, v_s_, lowp_s_, sumsq_, ws_, bias_;
+    double bias_host_[2] = {1.0, 1.0};
 };
 
 Trainer::Trainer(ModelConfig config, optim::AdamWConfig adam, float max_norm, DType dtype,
@@ -587,7 +601,13 @@ bool Trainer::graph_eligible() const
         const char* v = std::getenv("VEDA_STEP_GRAPH");
         return v == nullptr || std::atoi(v) != 0;
     }();
-    return enabled && use_graph_ && !dp_ && !profile::enabled();
+    // data-parallel steps too when VEDA_DP_GRAPH=1 (every rank captures the same step, NCCL
+    // calls included)
+    static const bool dp_graph = [] {
+        const char* v = std::getenv("VEDA_DP_GRAPH");
+        return v != nullptr && std::atoi(v) != 0;
+    }();
+    return enabled && use_graph_ && (!dp_ || dp_graph) && !profile::enabled();
 }
 
 void Trainer::set_step_graph(bool on)
@@ -599,12 +619,21 @@ void Trainer::step(const Tensor& ids, const Tensor& targets)
 {
     if (!graph_eligible())
     {
-        if (!sharded())
+        if (sharded())
+        {
+            dp_->advance(opt_->config());
+        }
+        else
         {
             opt_->advance();
         }
         step_impl(ids, targets);
         return;
+    }
+    if (dp_)
+    {
+        dp_->set_overlap_gather(false);
+        dp_->sync();
     }
     const size_t bytes = batch_ * length_ * sizeof(int64_t);
     if (ids.data_ptr() != ids_.data_ptr())
@@ -615,7 +644,14 @@ void Trainer::step(const Tensor& ids, const Tensor& targets)
                                    cudaMemcpyDeviceToDevice, cs()),
                    "targets copy");
     }
-    opt_->advance();
+    if (sharded())
+    {
+        dp_->advance(opt_->config());
+    }
+    else
+    {
+        opt_->advance();
+    }
     if (graph_exec_ == nullptr && eager_steps_ < 1)
     {
         step_impl(ids_, targets_);   // creates the persistent buffers outside any graph
