@@ -80,11 +80,13 @@ def test_tiny_fp32_loss_decreases_and_is_log_v_at_init():
 
 QWEN_SMALL = O.ModelConfig(vocab=2048, hidden=256, intermediate=512, layers=2, heads=4,
                            kv_heads=2, head_dim=128, eps=1e-6, theta=1e6)
+# the Qwen3-1.7B widths (d_model 2048, SwiGLU 6144, 16/8 heads) at one layer and a small vocabulary
+QWEN_WIDE = O.ModelConfig(vocab=2048, hidden=2048, intermediate=6144, layers=1, heads=16,
+                          kv_heads=8, head_dim=128, eps=1e-6, theta=1e6)
 
 
-def test_qwen_shaped_bf16_step_matches_oracle():
-    cfg = QWEN_SMALL
-    B, T = 2, 128
+@pytest.mark.parametrize("cfg,B,T", [(QWEN_SMALL, 2, 128), (QWEN_WIDE, 1, 128)])
+def test_qwen_shaped_bf16_step_matches_oracle(cfg, B, T):
     params = O.init_params(cfg, 3, bf16=True)
     ids, tg = O.synthetic_batch(cfg, B, T, 3)
     t = make_trainer(cfg, 1, B, T)
@@ -123,14 +125,13 @@ def test_qwen_shaped_bf16_step_matches_oracle():
     t.close()
 
 
-def test_qwen_06b_full_shape_step_properties():
-    """The Qwen3-0.6B-shaped step at its full size (28 layers, B 4 x T 2048): the CPU oracle
-    cannot run it, so check size-independent properties: initial loss ~ log V, finite grad norm,
-    and a second step on the same batch lowering the loss."""
-    cfg = O.QWEN3_06B
-    B, T = 4, 2048
-    ids, tg = O.synthetic_batch(cfg, B, T, 3)
-    t = make_trainer(cfg, 1, B, T, seed=3)
+@pytest.mark.parametrize("cfg,B,T,seed", [(O.QWEN3_06B, 4, 2048, 3), (O.QWEN3_17B, 2, 4096, 4)])
+def test_qwen_full_shape_step_properties(cfg, B, T, seed):
+    """The Qwen3-0.6B (B 4 x T 2048) and Qwen3-1.7B (B 2 x T 4096) shaped steps at full size: the
+    CPU oracle cannot run them, so check size-independent properties: initial loss ~ log V,
+    finite grad norm, and a second step on the same batch lowering the loss."""
+    ids, tg = O.synthetic_batch(cfg, B, T, seed)
+    t = make_trainer(cfg, 1, B, T, seed=seed)
     l1, n1 = t.step_host(ids, tg)
     l2, n2 = t.step_host(ids, tg)
     assert abs(l1 - math.log(cfg.vocab)) < 0.5, l1
