@@ -5,7 +5,9 @@
 //
 // generate() reruns the forward over the whole sequence for every new token; generate_cached()
 // prefills the prompt once (keys and values of every layer kept on the device, after QK-norm and
-// RoPE) and then feeds one token per step, attending to the cache. Both take the last position's
+// RoPE) and then feeds one token per step, attending to the cache. A decode step is recorded once
+// into a CUDA graph (token, position and every intermediate in fixed device buffers) and replayed
+// per token; VEDA_DECODE_GRAPH=0 launches its kernels one by one instead. Both take the last position's
 // logits and the first of the largest (ties to the lower id; a NaN logit throws). The reference's
 // acceptance rule for the cache is that both give the same tokens.
 #pragma once
@@ -54,6 +56,11 @@ private:
     core::Tensor forward(const std::vector<int32_t>& ids, size_t pos0, Cache* cache,
                          const core::Tensor& cosines, const core::Tensor& sines) const;
     int32_t pick(const core::Tensor& logits) const;
+    struct DecodeStep;
+    // Records one decode step (the token and its position read from device buffers, the next
+    // token written back, the position advanced) into st's graph.
+    void record_step(DecodeStep& st, Cache& cache, const core::Tensor& cosines,
+                     const core::Tensor& sines) const;
 
     const train::TinyTransformer& model_;
 };

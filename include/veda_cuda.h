@@ -280,6 +280,20 @@ int veda_argmax(const void* x, int64_t ld, int64_t rows, int64_t n, int64_t* out
 int veda_attention_decode(const void* q, const void* k, const void* v, int64_t ldkv, int64_t len,
                           int64_t heads, int64_t kv_heads, int64_t head_dim, float scale,
                           void* out, int dtype, veda_stream_t stream);
+/* The same with the query's position read from device memory (len = *pos + 1), so a decode
+ * step recorded once in a CUDA graph serves every position. */
+int veda_attention_decode_at(const void* q, const void* k, const void* v, int64_t ldkv,
+                             const int64_t* pos, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                             float scale, void* out, int dtype, veda_stream_t stream);
+/* One decoded token's projections qkv [(H + 2 Hkv) Dh] at position *pos (device memory): QK-norm
+ * and RoPE of the query heads into q_out and of the KV heads into row *pos of k_cache, the
+ * values into row *pos of v_cache (rows of ldkv elements). Model.cpp:173-178, Views.cpp:78-134. */
+int veda_decode_qkv_at(const void* qkv, const void* q_gain, const void* k_gain, const float* cos,
+                       const float* sin, const int64_t* pos, void* q_out, void* k_cache,
+                       void* v_cache, int64_t ldkv, int64_t heads, int64_t kv_heads,
+                       int64_t head_dim, float eps, int dtype, veda_stream_t stream);
+/* *pos += 1 on the device (the last node of a recorded decode step). */
+int veda_decode_advance(int64_t* pos, veda_stream_t stream);
 /* Seeded N(0, std) fill (counter-based hash + Box-Muller) for synthetic weights. */
 int veda_randn(void* x, int64_t n, float std, uint64_t seed, int dtype, veda_stream_t stream);
 /* fp32 -> bf16 rounding copy (round to nearest even). */

@@ -90,3 +90,57 @@ def test_qwen_shaped_bf16_cached_generation_matches_uncached():
     toks_c, _, _ = t.generate(prompt, 16, cached=True)
     assert len(toks) == 16 and toks_c == toks
     t.close()
+
+
+@pytest.mark.parametrize("dtype,heads,kv,dh,pos", [(0, 4, 2, 16, 0), (1, 16, 8, 128, 37)])
+def test_decode_step_kernels_read_the_device_position(dtype, heads, kv, dh, pos):
+    """One token's QK-norm + RoPE at the position held in device memory, its K/V rows written into
+    the cache at that position, and attention over positions 0..pos, against the oracle and the
+    length-argument kernel; the position then advances by one on the device."""
+    import torch
+    import veda_b200 as V
+    from tests.gpu_util import bf, call, stream
+    r = np.random.default_rng(pos + dh)
+    cap = pos + 3
+    W = (heads + 2 * kv) * dh
+    qkv = r.standard_normal((1, W)).astype(np.float32)
+    qg = (1 + 0.1 * r.standard_normal(dh)).astype(np.float32)
+    kg = (1 + 0.1 * r.standard_normal(dh)).astype(np.float32)
+    kc = r.standard_normal((cap, kv * dh)).astype(np.float32)
+    vc = r.standard_normal((cap, kv * dh)).astype(np.float32)
+    if dtype == 1:
+        qkv, qg, kg, kc, vc = bf(qkv), bf(qg), bf(kg), bf(kc), bf(vc)
+    cos, sin = O.rope_tables(cap, dh, 1e6)
+    q = qkv[0, :heads * dh].reshape(heads, dh)
+    k = qkv[0, heads * dh:(heads + kv) * dh].reshape(kv, dh)
+    v = qkv[0, (heads + kv) * dh:].reshape(kv * dh)
+    q_ref = O.rope(O.rms_norm_gamma(q, qg, 1e-6)[0], cos[pos], sin[pos]).reshape(-1)
+    k_ref = O.rope(O.rms_norm_gamma(k, kg, 1e-6)[0], cos[pos], sin[pos]).reshape(-1)
+    tdt = torch.float32 if dtype == 0 else torch.bfloat16
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to("cuda").to(tdt)
+    dqkv, dqg, dkg, dk, dv = d(qkv), d(qg), d(kg), d(kc), d(vc)
+    dcos, dsin = (torch.from_numpy(a).to("cuda") for a in (cos, sin))
+    dpos = torch.tensor([pos], dtype=torch.int64, device="cuda")
+    qr = torch.empty((heads * dh,), dtype=tdt, device="cuda")
+    dt = V.F32 if dtype == 0 else V.BF16
+    call("veda_decode_qkv_at", dqkv.data_ptr(), dqg.data_ptr(), dkg.data_ptr(), dcos.data_ptr(),
+         dsin.data_ptr(), dpos.data_ptr(), qr.data_ptr(), dk.data_ptr(), dv.data_ptr(), kv * dh, heads,
+         kv, dh, 1e-6, dt, stream())
+    tol = 1e-5 if dtype == 0 else 2e-2
+    assert O.max_abs_rel(qr.float().cpu().numpy(), q_ref) <= tol
+    kc_got, vc_got = dk.float().cpu().numpy(), dv.float().cpu().numpy()
+    assert O.max_abs_rel(kc_got[pos], k_ref) <= tol
+    assert np.array_equal(vc_got[pos], v.astype(np.float32))
+    rows = [i for i in range(cap) if i != pos]
+    assert np.array_equal(kc_got[rows], kc[rows].astype(np.float32))   # other rows untouched
+    assert np.array_equal(vc_got[rows], vc[rows].astype(np.float32))
+    scale = 1.0 / math.sqrt(dh)
+    out_at = torch.empty((heads, dh), dtype=tdt, device="cuda")
+    out_len = torch.empty((heads, dh), dtype=tdt, device="cuda")
+    call("veda_attention_decode_at", qr.data_ptr(), dk.data_ptr(), dv.data_ptr(), kv * dh, dpos.data_ptr(),
+         heads, kv, dh, scale, out_at.data_ptr(), dt, stream())
+    call("veda_attention_decode", qr.data_ptr(), dk.data_ptr(), dv.data_ptr(), kv * dh, pos + 1, heads, kv,
+         dh, scale, out_len.data_ptr(), dt, stream())
+    assert torch.equal(out_at, out_len)
+    call("veda_decode_advance", dpos.data_ptr(), stream())
+    assert int(dpos.item()) == pos + 1

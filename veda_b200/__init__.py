@@ -85,6 +85,10 @@ SIGNATURES = {
     "veda_gelu_bwd": (_i, [_p, _p, _p, _i64, _i, _p]),
     "veda_argmax": (_i, [_p, _i64, _i64, _i64, _p, _p, _i, _p]),
     "veda_attention_decode": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f, _p, _i, _p]),
+    "veda_attention_decode_at": (_i, [_p, _p, _p, _i64, _p, _i64, _i64, _i64, _f, _p, _i, _p]),
+    "veda_decode_qkv_at": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f, _i,
+                                _p]),
+    "veda_decode_advance": (_i, [_p, _p]),
     "veda_randn": (_i, [_p, _i64, _f, _u64, _i, _p]),
     "veda_f32_to_bf16": (_i, [_p, _p, _i64, _p]),
     "veda_corpus_gather": (_i, [_p, _i64, _i64, C.c_uint64, _i64, _i64, _p, _p, _p]),

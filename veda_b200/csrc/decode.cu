@@ -19,9 +19,13 @@ constexpr int kDecodeWarps = 4;
 template <typename T, int DL>
 __global__ void __launch_bounds__(kDecodeWarps * 32)
 attn_decode_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-                   int64_t ldkv, int64_t len, int heads, int kv_heads, int head_dim, float scale,
-                   T* __restrict__ out)
+                   int64_t ldkv, int64_t len, const int64_t* __restrict__ pos, int heads, int kv_heads,
+                   int head_dim, float scale, T* __restrict__ out)
 {
+    if (pos != nullptr)
+    {
+        len = *pos + 1;   // the query sits at position *pos and sees every position up to it
+    }
     __shared__ float s_m[kDecodeWarps], s_l[kDecodeWarps], s_acc[kDecodeWarps][DL * 32];
     const int h = blockIdx.x;
     const int kvh = h / (heads / kv_heads);
@@ -97,19 +101,16 @@ attn_decode_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
 
 using namespace veda::cuda;
 
-extern "C" int veda_attention_decode(const void* q, const void* k, const void* v, int64_t ldkv,
-                                     int64_t len, int64_t heads, int64_t kv_heads, int64_t head_dim,
-                                     float scale, void* out, int dtype, veda_stream_t stream)
+namespace
 {
-    VEDA_REQUIRE(valid_dtype(dtype), "unknown dtype");
-    VEDA_REQUIRE(len > 0 && heads > 0 && kv_heads > 0 && heads % kv_heads == 0, "bad shape");
-    VEDA_REQUIRE(head_dim > 0 && head_dim <= 256, "head_dim must lie in [1, 256]");
-    VEDA_REQUIRE(ldkv >= kv_heads * head_dim, "bad cache leading dimension");
-    VEDA_REQUIRE(q && k && v && out, "null pointer");
+int launch_decode(const void* q, const void* k, const void* v, int64_t ldkv, int64_t len,
+                  const int64_t* pos, int64_t heads, int64_t kv_heads, int64_t head_dim, float scale,
+                  void* out, int dtype, veda_stream_t stream)
+{
     const int dl = static_cast<int>((head_dim + 31) / 32);
 #define VEDA_DEC(T, DL)                                                                               \
     attn_decode_kernel<T, DL><<<static_cast<unsigned>(heads), kDecodeWarps * 32, 0, stream>>>(       \
-        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), ldkv, len,      \
+        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), ldkv, len, pos, \
         static_cast<int>(heads), static_cast<int>(kv_heads), static_cast<int>(head_dim), scale,      \
         static_cast<T*>(out))
 #define VEDA_DEC_DL(T)                                                                                \
@@ -136,4 +137,120 @@ extern "C" int veda_attention_decode(const void* q, const void* k, const void* v
 #undef VEDA_DEC
     count_launch();
     return check_launch("veda_attention_decode");
+}
+} // namespace
+
+extern "C" int veda_attention_decode(const void* q, const void* k, const void* v, int64_t ldkv,
+                                     int64_t len, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                     float scale, void* out, int dtype, veda_stream_t stream)
+{
+    VEDA_REQUIRE(valid_dtype(dtype), "unknown dtype");
+    VEDA_REQUIRE(len > 0 && heads > 0 && kv_heads > 0 && heads % kv_heads == 0, "bad shape");
+    VEDA_REQUIRE(head_dim > 0 && head_dim <= 256, "head_dim must lie in [1, 256]");
+    VEDA_REQUIRE(ldkv >= kv_heads * head_dim, "bad cache leading dimension");
+    VEDA_REQUIRE(q && k && v && out, "null pointer");
+    return launch_decode(q, k, v, ldkv, len, nullptr, heads, kv_heads, head_dim, scale, out, dtype,
+                         stream);
+}
+
+extern "C" int veda_attention_decode_at(const void* q, const void* k, const void* v, int64_t ldkv,
+                                        const int64_t* pos, int64_t heads, int64_t kv_heads,
+                                        int64_t head_dim, float scale, void* out, int dtype,
+                                        veda_stream_t stream)
+{
+    VEDA_REQUIRE(valid_dtype(dtype), "unknown dtype");
+    VEDA_REQUIRE(heads > 0 && kv_heads > 0 && heads % kv_heads == 0, "bad shape");
+    VEDA_REQUIRE(head_dim > 0 && head_dim <= 256, "head_dim must lie in [1, 256]");
+    VEDA_REQUIRE(ldkv >= kv_heads * head_dim, "bad cache leading dimension");
+    VEDA_REQUIRE(q && k && v && out && pos, "null pointer");
+    return launch_decode(q, k, v, ldkv, 0, pos, heads, kv_heads, head_dim, scale, out, dtype, stream);
+}
+
+// One token's q, k, v at the position held in device memory: QK-norm (x / sqrt(mean(x^2) + eps)
+// * gain, Model.cpp:173-178) and RoPE (half-split rotation by the table row of that position,
+// Views.cpp:78-134) for every query head into q_out and every KV head into its cache row, and the
+// values copied into theirs. Block b: query head b, KV head b - H, or value head b - H - Hkv.
+template <typename T>
+__global__ void __launch_bounds__(128)
+decode_qkv_kernel(const T* __restrict__ qkv, const T* __restrict__ qgain, const T* __restrict__ kgain,
+                  const float* __restrict__ cosv, const float* __restrict__ sinv,
+                  const int64_t* __restrict__ pos, T* __restrict__ q_out, T* __restrict__ k_cache,
+                  T* __restrict__ v_cache, int64_t ldkv, int heads, int kv_heads, int head_dim,
+                  float eps)
+{
+    __shared__ float red[4];
+    const int64_t p = *pos;
+    const int b = blockIdx.x, tid = threadIdx.x;
+    if (b >= heads + kv_heads)
+    {
+        const int vh = b - heads - kv_heads;
+        const T* src = qkv + static_cast<int64_t>(heads + kv_heads + vh) * head_dim;
+        T* dst = v_cache + p * ldkv + static_cast<int64_t>(vh) * head_dim;
+        for (int d = tid; d < head_dim; d += blockDim.x) dst[d] = src[d];
+        return;
+    }
+    const bool is_q = b < heads;
+    const T* x = qkv + static_cast<int64_t>(b) * head_dim;   // q heads, then k heads, in order
+    const T* gain = is_q ? qgain : kgain;
+    float ss = 0.0f;
+    for (int d = tid; d < head_dim; d += blockDim.x)
+    {
+        const float v = to_f32(x[d]);
+        ss += v * v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    ss = 0.0f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) ss += red[w];
+    const float r = sqrtf(ss / static_cast<float>(head_dim) + eps);   // x / r, as RMSNorm divides
+    T* dst = is_q ? q_out + static_cast<int64_t>(b) * head_dim
+                  : k_cache + p * ldkv + static_cast<int64_t>(b - heads) * head_dim;
+    const int half = head_dim / 2;
+    const float* cr = cosv + p * head_dim;
+    const float* sr = sinv + p * head_dim;
+    for (int d = tid; d < half; d += blockDim.x)
+    {
+        const float a = (to_f32(x[d]) / r) * to_f32(gain[d]);
+        const float c = (to_f32(x[d + half]) / r) * to_f32(gain[d + half]);
+        dst[d] = from_f32<T>(a * cr[d] - c * sr[d]);
+        dst[d + half] = from_f32<T>(c * cr[d] + a * sr[d]);
+    }
+}
+
+__global__ void advance_kernel(int64_t* pos)
+{
+    *pos += 1;
+}
+
+extern "C" int veda_decode_qkv_at(const void* qkv, const void* q_gain, const void* k_gain,
+                                  const float* cos, const float* sin, const int64_t* pos,
+                                  void* q_out, void* k_cache, void* v_cache, int64_t ldkv,
+                                  int64_t heads, int64_t kv_heads, int64_t head_dim, float eps,
+                                  int dtype, veda_stream_t stream)
+{
+    VEDA_REQUIRE(valid_dtype(dtype), "unknown dtype");
+    VEDA_REQUIRE(heads > 0 && kv_heads > 0 && head_dim > 0 && head_dim % 2 == 0, "bad shape");
+    VEDA_REQUIRE(ldkv >= kv_heads * head_dim, "bad cache leading dimension");
+    VEDA_REQUIRE(qkv && q_gain && k_gain && cos && sin && pos && q_out && k_cache && v_cache,
+                 "null pointer");
+    const unsigned blocks = static_cast<unsigned>(heads + 2 * kv_heads);
+#define VEDA_QKV(T)                                                                                   \
+    decode_qkv_kernel<T><<<blocks, 128, 0, stream>>>(                                                 \
+        static_cast<const T*>(qkv), static_cast<const T*>(q_gain), static_cast<const T*>(k_gain), cos, \
+        sin, pos, static_cast<T*>(q_out), static_cast<T*>(k_cache), static_cast<T*>(v_cache), ldkv,   \
+        static_cast<int>(heads), static_cast<int>(kv_heads), static_cast<int>(head_dim), eps)
+    if (dtype == VEDA_BF16) VEDA_QKV(bf16); else VEDA_QKV(float);
+#undef VEDA_QKV
+    count_launch();
+    return check_launch("veda_decode_qkv_at");
+}
+
+extern "C" int veda_decode_advance(int64_t* pos, veda_stream_t stream)
+{
+    VEDA_REQUIRE(pos != nullptr, "null pointer");
+    advance_kernel<<<1, 1, 0, stream>>>(pos);
+    count_launch();
+    return check_launch("veda_decode_advance");
 }

@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -55,7 +56,129 @@ struct Generator::Cache
     std::vector<Tensor> k, v;
 };
 
+// One recorded decode step: its graph, the stream it was recorded on, and the fixed buffers it
+// reads and writes. io holds the token id (int64) at [0, 8) and the argmax status (int) at [8, 12);
+// pos the position (int64) of the token being fed.
+struct Generator::DecodeStep
+{
+    Tensor io, pos, x, xs, a, qkv, qr, ctx, o, gu, hb, dn, logits;
+    cudaGraphExec_t exec = nullptr;
+    cudaStream_t stream = nullptr;
+
+    DecodeStep() = default;
+    DecodeStep(const DecodeStep&) = delete;
+    DecodeStep& operator=(const DecodeStep&) = delete;
+    ~DecodeStep()
+    {
+        if (exec != nullptr) cudaGraphExecDestroy(exec);
+        if (stream != nullptr) cudaStreamDestroy(stream);
+    }
+};
+
 Generator::Generator(const train::TinyTransformer& model) : model_(model) {}
+
+void Generator::record_step(DecodeStep& st, Cache& cache, const Tensor& cosines,
+                            const Tensor& sines) const
+{
+    const train::ModelConfig& c = model_.config_;
+    const size_t D = c.hidden_size, F = c.intermediate_size, H = c.num_heads, Hk = c.num_kv_heads,
+                 Dh = c.head_dim, V = c.vocab_size;
+    const size_t W = (H + 2 * Hk) * Dh, KV = Hk * Dh;
+    const DType dtype = model_.dtype_;
+    const int d = dt(dtype);
+    const float eps = c.rms_norm_eps;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(Dh));
+    st.io = Tensor(Shape({4}), DType::F32);
+    st.pos = Tensor(Shape({2}), DType::F32);
+    st.x = Tensor::empty(Shape({1, D}), dtype);
+    st.xs = Tensor::empty(Shape({1, D}), dtype);
+    st.a = Tensor::empty(Shape({1, D}), dtype);
+    st.qkv = Tensor::empty(Shape({1, W}), dtype);
+    st.qr = Tensor::empty(Shape({1, H * Dh}), dtype);
+    st.ctx = Tensor::empty(Shape({1, H * Dh}), dtype);
+    st.o = Tensor::empty(Shape({1, D}), dtype);
+    st.gu = Tensor::empty(Shape({1, 2 * F}), dtype);
+    st.hb = Tensor::empty(Shape({1, F}), dtype);
+    st.dn = Tensor::empty(Shape({1, D}), dtype);
+    st.logits = Tensor::empty(Shape({V}), dtype);
+    cuda_check(cudaStreamSynchronize(cs()), "decode step buffers");
+    cuda_check(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking), "decode stream");
+    const veda_stream_t caller = current_stream();
+    set_current_stream(st.stream);
+    cudaGraph_t graph = nullptr;
+    cuda_check(cudaStreamBeginCapture(st.stream, cudaStreamCaptureModeThreadLocal), "decode capture");
+    try
+    {
+        int64_t* token = static_cast<int64_t*>(st.io.data_ptr());
+        int* status = reinterpret_cast<int*>(token + 1);
+        const int64_t* pos = static_cast<const int64_t*>(st.pos.data_ptr());
+        const float* cp = static_cast<const float*>(cosines.data_ptr());
+        const float* sp = static_cast<const float*>(sines.data_ptr());
+        Tensor* x = &st.x;
+        Tensor* xs = &st.xs;
+        check(veda_embedding_fwd(token, 1, model_.embed_.value().data_ptr(), static_cast<int64_t>(V),
+                                 static_cast<int64_t>(D), x->data_ptr(), static_cast<int64_t>(D), nullptr, d,
+                                 current_stream()),
+              "generate: embedding");
+        const auto& layers = model_.layers_;
+        const Tensor& first_gain = layers.empty() ? model_.final_norm_.value() : layers[0].in_norm.value();
+        check(veda_rmsnorm_fwd(x->data_ptr(), static_cast<int64_t>(D), first_gain.data_ptr(), st.a.data_ptr(),
+                               static_cast<int64_t>(D), 1, static_cast<int64_t>(D), eps, d, current_stream()),
+              "generate: norm");
+        for (size_t l = 0; l < layers.size(); ++l)
+        {
+            const auto& L = layers[l];
+            gemm_nt(1, W, D, st.a.data_ptr(), D, L.qkv.value().data_ptr(), D, st.qkv.data_ptr(), W, d);
+            check(veda_decode_qkv_at(st.qkv.data_ptr(), L.q_norm.value().data_ptr(), L.k_norm.value().data_ptr(),
+                                     cp, sp, pos, st.qr.data_ptr(), cache.k[l].data_ptr(), cache.v[l].data_ptr(),
+                                     static_cast<int64_t>(KV), static_cast<int64_t>(H), static_cast<int64_t>(Hk),
+                                     static_cast<int64_t>(Dh), eps, d, current_stream()),
+                  "generate: q/k/v");
+            check(veda_attention_decode_at(st.qr.data_ptr(), cache.k[l].data_ptr(), cache.v[l].data_ptr(),
+                                           static_cast<int64_t>(KV), pos, static_cast<int64_t>(H),
+                                           static_cast<int64_t>(Hk), static_cast<int64_t>(Dh), scale,
+                                           st.ctx.data_ptr(), d, current_stream()),
+                  "generate: attention");
+            gemm_nt(1, D, H * Dh, st.ctx.data_ptr(), H * Dh, L.o.value().data_ptr(), H * Dh, st.o.data_ptr(), D, d);
+            check(veda_add_rmsnorm_fwd(x->data_ptr(), static_cast<int64_t>(D), st.o.data_ptr(),
+                                       static_cast<int64_t>(D), L.post_norm.value().data_ptr(), xs->data_ptr(),
+                                       static_cast<int64_t>(D), st.a.data_ptr(), static_cast<int64_t>(D), 1,
+                                       static_cast<int64_t>(D), eps, d, current_stream()),
+                  "generate: residual + norm");
+            std::swap(x, xs);
+            gemm_nt(1, 2 * F, D, st.a.data_ptr(), D, L.gate_up.value().data_ptr(), D, st.gu.data_ptr(), 2 * F, d);
+            check(veda_swiglu_fwd(st.gu.data_ptr(), static_cast<int64_t>(2 * F), at(st.gu, F),
+                                  static_cast<int64_t>(2 * F), st.hb.data_ptr(), static_cast<int64_t>(F), 1,
+                                  static_cast<int64_t>(F), d, current_stream()),
+                  "generate: swiglu");
+            gemm_nt(1, D, F, st.hb.data_ptr(), F, L.down.value().data_ptr(), F, st.dn.data_ptr(), D, d);
+            const Tensor& next = l + 1 < layers.size() ? layers[l + 1].in_norm.value() : model_.final_norm_.value();
+            check(veda_add_rmsnorm_fwd(x->data_ptr(), static_cast<int64_t>(D), st.dn.data_ptr(),
+                                       static_cast<int64_t>(D), next.data_ptr(), xs->data_ptr(),
+                                       static_cast<int64_t>(D), st.a.data_ptr(), static_cast<int64_t>(D), 1,
+                                       static_cast<int64_t>(D), eps, d, current_stream()),
+                  "generate: residual + norm");
+            std::swap(x, xs);
+        }
+        gemm_nt(1, V, D, st.a.data_ptr(), D, model_.embed_.value().data_ptr(), D, st.logits.data_ptr(), V, d);
+        check(veda_argmax(st.logits.data_ptr(), static_cast<int64_t>(V), 1, static_cast<int64_t>(V), token, status,
+                          d, current_stream()),
+              "generate: argmax");
+        check(veda_decode_advance(static_cast<int64_t*>(st.pos.data_ptr()), current_stream()), "generate: position");
+    }
+    catch (...)
+    {
+        set_current_stream(caller);
+        cudaStreamEndCapture(st.stream, &graph);
+        if (graph != nullptr) cudaGraphDestroy(graph);
+        throw;
+    }
+    set_current_stream(caller);
+    cuda_check(cudaStreamEndCapture(st.stream, &graph), "decode capture");
+    const cudaError_t e = cudaGraphInstantiate(&st.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    cuda_check(e, "decode graph instantiate");
+}
 
 Tensor Generator::forward(const std::vector<int32_t>& ids, size_t pos0, Cache* cache,
                           const Tensor& cosines, const Tensor& sines) const
@@ -246,27 +369,74 @@ Result Generator::generate_cached(const std::vector<int32_t>& prompt, const Opti
         cache.k.push_back(Tensor::empty(Shape({capacity, c.num_kv_heads * c.head_dim}), model_.dtype_));
         cache.v.push_back(Tensor::empty(Shape({capacity, c.num_kv_heads * c.head_dim}), model_.dtype_));
     }
+    static const bool use_graph = [] {
+        const char* v = std::getenv("VEDA_DECODE_GRAPH");
+        return v == nullptr || std::atoi(v) != 0;
+    }();
     Result result;
-    std::vector<int32_t> pending(prompt);
-    size_t pos = 0;
-    for (size_t step = 0; step <= options.max_new_tokens; ++step)
+    // the prefill (Generator.cpp:73-78 with the whole prompt pending)
+    Tensor logits = forward(prompt, 0, &cache, tables.first, tables.second);
+    ++result.forward_passes;
+    size_t pos = prompt.size();
+    if (options.max_new_tokens == 0)
     {
-        const Tensor logits = forward(pending, pos, &cache, tables.first, tables.second);
-        ++result.forward_passes;
-        pos += pending.size();
-        if (step == options.max_new_tokens)
-        {
-            break;   // the prefill still had to run; this is the limit, not an extra token
-        }
-        const int32_t next = pick(logits);
+        return result;   // the prefill still had to run; this is the limit, not an extra token
+    }
+    int32_t next = pick(logits);
+    DecodeStep st;
+    for (size_t step = 1;; ++step)
+    {
         if (stops(options, next))
         {
             result.stopped_on_token = true;
             break;
         }
         result.generated.push_back(next);
-        pending = {next};
+        // feed the token just chosen (one token per step after the prefill)
+        if (use_graph)
+        {
+            if (st.exec == nullptr)
+            {
+                record_step(st, cache, tables.first, tables.second);
+                const int64_t init[2] = {next, 0};
+                const auto p = static_cast<int64_t>(pos);
+                cuda_check(cudaMemcpyAsync(st.io.data_ptr(), init, sizeof(init), cudaMemcpyHostToDevice, cs()),
+                           "decode token");
+                cuda_check(cudaMemcpyAsync(st.pos.data_ptr(), &p, sizeof(p), cudaMemcpyHostToDevice, cs()),
+                           "decode position");
+            }
+            cuda_check(cudaGraphLaunch(st.exec, cs()), "decode step");
+        }
+        else
+        {
+            logits = forward({next}, pos, &cache, tables.first, tables.second);
+        }
+        ++pos;
+        ++result.forward_passes;
+        if (step == options.max_new_tokens)
+        {
+            break;   // the limit: the last token was fed, none is chosen from it
+        }
+        if (use_graph)
+        {
+            int64_t io[2] = {0, 0};
+            cuda_check(cudaMemcpyAsync(io, st.io.data_ptr(), sizeof(io), cudaMemcpyDeviceToHost, cs()),
+                       "decode token");
+            cuda_check(cudaStreamSynchronize(cs()), "decode token");
+            int status = 0;
+            std::memcpy(&status, &io[1], sizeof(int));
+            if (status != 0)
+            {
+                throw std::runtime_error("generate: a logit is NaN");
+            }
+            next = static_cast<int32_t>(io[0]);
+        }
+        else
+        {
+            next = pick(logits);
+        }
     }
+    cuda_check(cudaStreamSynchronize(cs()), "decode");
     return result;
 }
 
