@@ -294,6 +294,16 @@ int veda_decode_qkv_at(const void* qkv, const void* q_gain, const void* k_gain, 
                        int64_t head_dim, float eps, int dtype, veda_stream_t stream);
 /* *pos += 1 on the device (the last node of a recorded decode step). */
 int veda_decode_advance(int64_t* pos, veda_stream_t stream);
+/* One activation row through a Linear layer (x . W^T of Variable.cpp:325, matmul_nt, at M = 1):
+ * y[i] = sum_j x[j] * w[i, j] for i < n, j < k, rows of w at stride ldw; fp32 accumulation, each
+ * output rounded once. HBM-bound: every weight byte is read once. k * element size <= 48 KB. */
+int veda_gemv_nt(const void* x, const void* w, int64_t ldw, void* y, int64_t n, int64_t k, int dtype,
+                 veda_stream_t stream);
+/* The gate/up Linear and SwiGLU of one row in one pass: w_gate_up holds the gate rows [0, f) and
+ * the up rows [f, 2f); h[i] = silu(g_i) * u_i on g and u rounded to the dtype, the arithmetic of
+ * veda_gemv_nt followed by veda_swiglu_fwd (Model.cpp:198-204). */
+int veda_gemv_swiglu(const void* x, const void* w_gate_up, int64_t ldw, void* h, int64_t f,
+                     int64_t k, int dtype, veda_stream_t stream);
 /* Seeded N(0, std) fill (counter-based hash + Box-Muller) for synthetic weights. */
 int veda_randn(void* x, int64_t n, float std, uint64_t seed, int dtype, veda_stream_t stream);
 /* fp32 -> bf16 rounding copy (round to nearest even). */

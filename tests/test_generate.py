@@ -144,3 +144,32 @@ def test_decode_step_kernels_read_the_device_position(dtype, heads, kv, dh, pos)
     assert torch.equal(out_at, out_len)
     call("veda_decode_advance", dpos.data_ptr(), stream())
     assert int(dpos.item()) == pos + 1
+
+
+@pytest.mark.parametrize("dtype,n,k,ldw", [(0, 37, 24, 24), (1, 1024, 3072, 3072), (1, 9000, 1024, 1032),
+                                          (1, 5, 19, 21), (0, 8200, 96, 100)])
+def test_gemv_matches_row_product(dtype, n, k, ldw):
+    """One activation row through a Linear layer (both rows-per-warp variants, the 16-byte and the
+    element-wise paths) against the float64 product; gate/up + SwiGLU in one pass equals
+    the projection followed by veda_swiglu_fwd bit for bit."""
+    import torch
+    import veda_b200 as V
+    from tests.gpu_util import bf, call, stream
+    r = np.random.default_rng(n + k)
+    x = r.standard_normal(k).astype(np.float32)
+    w = r.standard_normal((2 * n, ldw)).astype(np.float32)
+    if dtype == 1:
+        x, w = bf(x), bf(w)
+    tdt = torch.float32 if dtype == 0 else torch.bfloat16
+    dt = V.F32 if dtype == 0 else V.BF16
+    dx, dw = (torch.from_numpy(a).to("cuda").to(tdt) for a in (x, w))
+    y = torch.empty(2 * n, dtype=tdt, device="cuda")
+    call("veda_gemv_nt", dx.data_ptr(), dw.data_ptr(), ldw, y.data_ptr(), 2 * n, k, dt, stream())
+    ref = w[:, :k].astype(np.float64) @ x.astype(np.float64)
+    tol = 1e-5 if dtype == 0 else 8e-3
+    assert O.max_abs_rel(y.float().cpu().numpy(), ref) <= tol
+    h = torch.empty(n, dtype=tdt, device="cuda")
+    call("veda_gemv_swiglu", dx.data_ptr(), dw.data_ptr(), ldw, h.data_ptr(), n, k, dt, stream())
+    h2 = torch.empty(n, dtype=tdt, device="cuda")
+    call("veda_swiglu_fwd", y.data_ptr(), n, y[n:].data_ptr(), n, h2.data_ptr(), n, 1, n, dt, stream())
+    assert torch.equal(h, h2)

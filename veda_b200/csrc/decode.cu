@@ -254,3 +254,212 @@ extern "C" int veda_decode_advance(int64_t* pos, veda_stream_t stream)
     count_launch();
     return check_launch("veda_decode_advance");
 }
+
+// ---- the decode step's Linear layers at one row --------------------------------------------
+// y[n] = sum_k x[k] * w[n, k] (matmul_nt, Variable.cpp:325, for a single activation row). Every weight
+// byte is read once and nothing is reused, so the bound is HBM bandwidth, not the tensor cores: a
+// warp owns R weight rows, each lane streams 16-byte pieces of them (L1 bypassed) against the
+// activation staged in shared memory, accumulates in fp32 with fmaf in piece order, and the warp
+// reduces the row sums and rounds each to the output dtype once. kGemvUnroll pieces per row are
+// loaded before any is used, so R * kGemvUnroll 16-byte loads per lane are in flight.
+namespace veda::cuda
+{
+namespace
+{
+constexpr int kGemvWarps = 8;
+constexpr int kGemvUnroll = 4;
+constexpr int64_t kGemvSmem = 48 * 1024;   // the activation row, staged whole
+
+__device__ __forceinline__ uint4 load_stream16(const void* p)
+{
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p));
+    return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4 raw, float (&out)[16 / sizeof(T)])
+{
+    if constexpr (sizeof(T) == 4)
+    {
+        out[0] = __uint_as_float(raw.x);
+        out[1] = __uint_as_float(raw.y);
+        out[2] = __uint_as_float(raw.z);
+        out[3] = __uint_as_float(raw.w);
+    }
+    else
+    {
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+        {
+            out[2 * i] = __uint_as_float(w[i] << 16);
+            out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        }
+    }
+}
+
+__device__ __forceinline__ float silu_gate(float g) { return g * __fdividef(1.0f, 1.0f + __expf(-g)); }
+
+// SWIGLU: the warp's two rows are gate row j and up row n + j of the fused [2n, k] weight, and the
+// output is h[j] = silu(g) * u on the values rounded to the dtype (the separate Linear then SwiGLU
+// of Model.cpp:198-204, same arithmetic as veda_swiglu_fwd).
+template <typename T, int R, bool SWIGLU, bool VEC>
+__global__ void __launch_bounds__(kGemvWarps * 32)
+gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __restrict__ y, int n, int k)
+{
+    extern __shared__ __align__(16) unsigned char gemv_smem[];
+    T* xs = reinterpret_cast<T*>(gemv_smem);
+    constexpr int E = 16 / sizeof(T);
+    if constexpr (VEC)
+    {
+        for (int i = threadIdx.x * E; i < k; i += blockDim.x * E)
+            *reinterpret_cast<uint4*>(xs + i) = *reinterpret_cast<const uint4*>(x + i);
+    }
+    else
+    {
+        for (int i = threadIdx.x; i < k; i += blockDim.x) xs[i] = x[i];
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int per_warp = SWIGLU ? 1 : R;
+    const int base = (blockIdx.x * kGemvWarps + warp) * per_warp;
+    if (base >= n) return;
+    const T* rows[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+    {
+        const int row = SWIGLU ? base : min(base + r, n - 1);   // a row past n repeats the last one
+        rows[r] = w + (static_cast<int64_t>(row) + (SWIGLU ? static_cast<int64_t>(r) * n : 0)) * ldw;
+    }
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+    if constexpr (VEC)
+    {
+        for (int c0 = lane * E; c0 < k; c0 += 32 * E * kGemvUnroll)
+        {
+            uint4 wv[kGemvUnroll][R];
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; ++u)
+            {
+                const int c = c0 + u * 32 * E;
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                    if (c < k) wv[u][r] = load_stream16(rows[r] + c);
+            }
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; ++u)
+            {
+                const int c = c0 + u * 32 * E;
+                if (c < k)
+                {
+                    float xv[E];
+                    load16(xs + c, xv);
+#pragma unroll
+                    for (int r = 0; r < R; ++r)
+                    {
+                        float wf[E];
+                        unpack16<T>(wv[u][r], wf);
+#pragma unroll
+                        for (int j = 0; j < E; ++j) acc[r] = fmaf(xv[j], wf[j], acc[r]);
+                    }
+                }
+            }
+        }
+    }
+    else
+    {
+        for (int c = lane; c < k; c += 32)
+        {
+            const float xv = to_f32(xs[c]);
+#pragma unroll
+            for (int r = 0; r < R; ++r) acc[r] = fmaf(xv, to_f32(rows[r][c]), acc[r]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]);
+    if (lane != 0) return;
+    if constexpr (SWIGLU)
+    {
+        const float g = to_f32(from_f32<T>(acc[0])), u = to_f32(from_f32<T>(acc[1]));
+        y[base] = from_f32<T>(silu_gate(g) * u);
+    }
+    else
+    {
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            if (base + r < n) y[base + r] = from_f32<T>(acc[r]);
+    }
+}
+
+template <typename T, int R, bool SWIGLU>
+void launch_gemv(const void* x, const void* w, int64_t ldw, void* y, int64_t n, int64_t k, bool vec,
+                 cudaStream_t stream)
+{
+    constexpr int per_warp = SWIGLU ? 1 : R;
+    const auto blocks = static_cast<unsigned>((n + kGemvWarps * per_warp - 1) / (kGemvWarps * per_warp));
+    const size_t smem = static_cast<size_t>(k) * sizeof(T);
+    const auto xp = static_cast<const T*>(x);
+    const auto wp = static_cast<const T*>(w);
+    const auto yp = static_cast<T*>(y);
+    if (vec)
+        gemv_kernel<T, R, SWIGLU, true><<<blocks, kGemvWarps * 32, smem, stream>>>(
+            xp, wp, ldw, yp, static_cast<int>(n), static_cast<int>(k));
+    else
+        gemv_kernel<T, R, SWIGLU, false><<<blocks, kGemvWarps * 32, smem, stream>>>(
+            xp, wp, ldw, yp, static_cast<int>(n), static_cast<int>(k));
+}
+
+int gemv_checks(const void* x, const void* w, int64_t ldw, const void* y, int64_t n, int64_t k, int dtype)
+{
+    VEDA_REQUIRE(valid_dtype(dtype), "unknown dtype");
+    VEDA_REQUIRE(x && w && y, "null pointer");
+    VEDA_REQUIRE(n > 0 && k > 0 && n < (1ll << 30), "bad shape");
+    VEDA_REQUIRE(ldw >= k, "bad weight leading dimension");
+    VEDA_REQUIRE(k * static_cast<int64_t>(dtype_size(dtype)) <= kGemvSmem,
+                 "the activation row exceeds the 48 KB staged in shared memory");
+    return 0;
+}
+
+bool gemv_vec(const void* x, const void* w, int64_t ldw, int64_t k, int dtype)
+{
+    const int64_t e = 16 / static_cast<int64_t>(dtype_size(dtype));
+    return aligned16(x) && aligned16(w) && k % e == 0 && ldw % e == 0;
+}
+} // namespace
+} // namespace veda::cuda
+
+extern "C" int veda_gemv_nt(const void* x, const void* w, int64_t ldw, void* y, int64_t n, int64_t k,
+                            int dtype, veda_stream_t stream)
+{
+    if (const int rc = gemv_checks(x, w, ldw, y, n, k, dtype)) return rc;
+    const bool vec = gemv_vec(x, w, ldw, k, dtype);
+    // two rows a warp once there are enough rows to fill the SMs with them
+    const bool two = n >= 8192;
+    if (dtype == VEDA_BF16)
+    {
+        if (two) launch_gemv<bf16, 2, false>(x, w, ldw, y, n, k, vec, stream);
+        else launch_gemv<bf16, 1, false>(x, w, ldw, y, n, k, vec, stream);
+    }
+    else
+    {
+        if (two) launch_gemv<float, 2, false>(x, w, ldw, y, n, k, vec, stream);
+        else launch_gemv<float, 1, false>(x, w, ldw, y, n, k, vec, stream);
+    }
+    count_launch();
+    return check_launch("veda_gemv_nt");
+}
+
+extern "C" int veda_gemv_swiglu(const void* x, const void* w_gate_up, int64_t ldw, void* h, int64_t f,
+                                int64_t k, int dtype, veda_stream_t stream)
+{
+    if (const int rc = gemv_checks(x, w_gate_up, ldw, h, f, k, dtype)) return rc;
+    const bool vec = gemv_vec(x, w_gate_up, ldw, k, dtype);
+    if (dtype == VEDA_BF16) launch_gemv<bf16, 2, true>(x, w_gate_up, ldw, h, f, k, vec, stream);
+    else launch_gemv<float, 2, true>(x, w_gate_up, ldw, h, f, k, vec, stream);
+    count_launch();
+    return check_launch("veda_gemv_swiglu");
+}

@@ -39,6 +39,14 @@ char* at(const Tensor& t, size_t i)
     return static_cast<char*>(t.data_ptr()) + i * core::dtype_size(t.dtype());
 }
 
+// One row through a Linear layer: y[n] = x[k] . w[n, k] (the decode step's projections).
+void gemv(const void* x, const void* w, size_t ldw, void* y, size_t n, size_t k, int d)
+{
+    check(veda_gemv_nt(x, w, static_cast<int64_t>(ldw), y, static_cast<int64_t>(n), static_cast<int64_t>(k), d,
+                       current_stream()),
+          "generate: gemv");
+}
+
 void gemm_nt(size_t m, size_t n, size_t k, const void* a, size_t lda, const void* b, size_t ldb,
              void* c, size_t ldc, int dtype)
 {
@@ -61,7 +69,7 @@ struct Generator::Cache
 // pos the position (int64) of the token being fed.
 struct Generator::DecodeStep
 {
-    Tensor io, pos, x, xs, a, qkv, qr, ctx, o, gu, hb, dn, logits;
+    Tensor io, pos, x, xs, a, qkv, qr, ctx, o, hb, dn, logits;
     cudaGraphExec_t exec = nullptr;
     cudaStream_t stream = nullptr;
 
@@ -97,7 +105,6 @@ void Generator::record_step(DecodeStep& st, Cache& cache, const Tensor& cosines,
     st.qr = Tensor::empty(Shape({1, H * Dh}), dtype);
     st.ctx = Tensor::empty(Shape({1, H * Dh}), dtype);
     st.o = Tensor::empty(Shape({1, D}), dtype);
-    st.gu = Tensor::empty(Shape({1, 2 * F}), dtype);
     st.hb = Tensor::empty(Shape({1, F}), dtype);
     st.dn = Tensor::empty(Shape({1, D}), dtype);
     st.logits = Tensor::empty(Shape({V}), dtype);
@@ -128,7 +135,7 @@ void Generator::record_step(DecodeStep& st, Cache& cache, const Tensor& cosines,
         for (size_t l = 0; l < layers.size(); ++l)
         {
             const auto& L = layers[l];
-            gemm_nt(1, W, D, st.a.data_ptr(), D, L.qkv.value().data_ptr(), D, st.qkv.data_ptr(), W, d);
+            gemv(st.a.data_ptr(), L.qkv.value().data_ptr(), D, st.qkv.data_ptr(), W, D, d);
             check(veda_decode_qkv_at(st.qkv.data_ptr(), L.q_norm.value().data_ptr(), L.k_norm.value().data_ptr(),
                                      cp, sp, pos, st.qr.data_ptr(), cache.k[l].data_ptr(), cache.v[l].data_ptr(),
                                      static_cast<int64_t>(KV), static_cast<int64_t>(H), static_cast<int64_t>(Hk),
@@ -139,19 +146,18 @@ void Generator::record_step(DecodeStep& st, Cache& cache, const Tensor& cosines,
                                            static_cast<int64_t>(Hk), static_cast<int64_t>(Dh), scale,
                                            st.ctx.data_ptr(), d, current_stream()),
                   "generate: attention");
-            gemm_nt(1, D, H * Dh, st.ctx.data_ptr(), H * Dh, L.o.value().data_ptr(), H * Dh, st.o.data_ptr(), D, d);
+            gemv(st.ctx.data_ptr(), L.o.value().data_ptr(), H * Dh, st.o.data_ptr(), D, H * Dh, d);
             check(veda_add_rmsnorm_fwd(x->data_ptr(), static_cast<int64_t>(D), st.o.data_ptr(),
                                        static_cast<int64_t>(D), L.post_norm.value().data_ptr(), xs->data_ptr(),
                                        static_cast<int64_t>(D), st.a.data_ptr(), static_cast<int64_t>(D), 1,
                                        static_cast<int64_t>(D), eps, d, current_stream()),
                   "generate: residual + norm");
             std::swap(x, xs);
-            gemm_nt(1, 2 * F, D, st.a.data_ptr(), D, L.gate_up.value().data_ptr(), D, st.gu.data_ptr(), 2 * F, d);
-            check(veda_swiglu_fwd(st.gu.data_ptr(), static_cast<int64_t>(2 * F), at(st.gu, F),
-                                  static_cast<int64_t>(2 * F), st.hb.data_ptr(), static_cast<int64_t>(F), 1,
-                                  static_cast<int64_t>(F), d, current_stream()),
-                  "generate: swiglu");
-            gemm_nt(1, D, F, st.hb.data_ptr(), F, L.down.value().data_ptr(), F, st.dn.data_ptr(), D, d);
+            check(veda_gemv_swiglu(st.a.data_ptr(), L.gate_up.value().data_ptr(), static_cast<int64_t>(D),
+                                   st.hb.data_ptr(), static_cast<int64_t>(F), static_cast<int64_t>(D), d,
+                                   current_stream()),
+                  "generate: gate/up + swiglu");
+            gemv(st.hb.data_ptr(), L.down.value().data_ptr(), F, st.dn.data_ptr(), D, F, d);
             const Tensor& next = l + 1 < layers.size() ? layers[l + 1].in_norm.value() : model_.final_norm_.value();
             check(veda_add_rmsnorm_fwd(x->data_ptr(), static_cast<int64_t>(D), st.dn.data_ptr(),
                                        static_cast<int64_t>(D), next.data_ptr(), xs->data_ptr(),
@@ -160,7 +166,7 @@ void Generator::record_step(DecodeStep& st, Cache& cache, const Tensor& cosines,
                   "generate: residual + norm");
             std::swap(x, xs);
         }
-        gemm_nt(1, V, D, st.a.data_ptr(), D, model_.embed_.value().data_ptr(), D, st.logits.data_ptr(), V, d);
+        gemv(st.a.data_ptr(), model_.embed_.value().data_ptr(), D, st.logits.data_ptr(), V, D, d);
         check(veda_argmax(st.logits.data_ptr(), static_cast<int64_t>(V), 1, static_cast<int64_t>(V), token, status,
                           d, current_stream()),
               "generate: argmax");

@@ -328,6 +328,28 @@ def decode(prompt_len, new_tokens):
                       "timing": "host wall clock per token (each token is read back to pick the next)"}),
           flush=True)
     t.close()
+    # the step's projections alone: one activation row against each weight matrix, L2 flushed
+    import veda_b200 as V
+    s = torch.cuda.current_stream()
+    flush = torch.empty(256 << 20, dtype=torch.float32, device="cuda")
+    x = torch.randn(cfg.intermediate, device="cuda").to(torch.bfloat16)
+    W = (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim
+    shapes = [("qkv", W, cfg.hidden, False), ("o", cfg.hidden, cfg.heads * cfg.head_dim, False),
+              ("gate_up+swiglu", cfg.intermediate, cfg.hidden, True),
+              ("down", cfg.hidden, cfg.intermediate, False), ("lm_head", cfg.vocab, cfg.hidden, False)]
+    for name, n, k, swiglu in shapes:
+        rows = 2 * n if swiglu else n
+        w = torch.randn(rows, k, device="cuda").to(torch.bfloat16)
+        y = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+        fn = V.lib().veda_gemv_swiglu if swiglu else V.lib().veda_gemv_nt
+
+        def run():
+            V.check(fn(x.data_ptr(), w.data_ptr(), k, y.data_ptr(), n, k, V.BF16, s.cuda_stream))
+        ms = _time(run, 20, s, flush)
+        gbs = rows * k * 2.0 / (ms / 1e3) / 1e9
+        print(json.dumps({"bench": "gemv", "layer": name, "n": n, "k": k, "us": ms * 1e3, "gbs": gbs,
+                          "frac": gbs / hbm, "peak_kind": kind}), flush=True)
+        del w
 
 
 def main():
