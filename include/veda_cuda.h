@@ -304,6 +304,30 @@ int veda_gemv_nt(const void* x, const void* w, int64_t ldw, void* y, int64_t n, 
  * veda_gemv_nt followed by veda_swiglu_fwd (Model.cpp:198-204). */
 int veda_gemv_swiglu(const void* x, const void* w_gate_up, int64_t ldw, void* h, int64_t f,
                      int64_t k, int dtype, veda_stream_t stream);
+/* veda_gemv_nt / veda_gemv_swiglu on the pre-norm of a residual row (Model.cpp:242-249): the
+ * activation is RMSNorm(s) * gamma with s = x + r (r may be NULL: s = x), s rounded to the dtype
+ * and written to sum when sum is not NULL (sum must not alias x or r). */
+int veda_gemv_rmsnorm(const void* x, const void* r, const void* gamma, float eps, void* sum,
+                      const void* w, int64_t ldw, void* y, int64_t n, int64_t k, int dtype,
+                      veda_stream_t stream);
+int veda_gemv_rmsnorm_swiglu(const void* x, const void* r, const void* gamma, float eps, void* sum,
+                             const void* w_gate_up, int64_t ldw, void* h, int64_t f, int64_t k,
+                             int dtype, veda_stream_t stream);
+/* veda_decode_qkv_at followed by veda_attention_decode_at in one launch (head_dim 128, heads /
+ * kv_heads in {1, 2, 4, 8}, 16-byte aligned cache rows, else VEDA_ERR_UNSUPPORTED): the token's
+ * QK-norm + RoPE, its key and value written into cache row *pos, and out[h] = attention of query
+ * head h over positions 0..*pos. The positions are split across CTAs by the cache's capacity (rows)
+ * and the slices merged by the last CTA of each KV head to finish, through `workspace` (at least
+ * veda_decode_attention_workspace bytes, 16-byte aligned, zero before its first use; every call
+ * leaves it ready for the next; one call at a time per workspace). A *pos outside [0, capacity)
+ * writes nothing. */
+int64_t veda_decode_attention_workspace(int64_t heads, int64_t kv_heads, int64_t capacity);
+int veda_decode_attention_at(const void* qkv, const void* q_gain, const void* k_gain,
+                             const float* cos, const float* sin, const int64_t* pos, void* k_cache,
+                             void* v_cache, int64_t ldkv, int64_t capacity, int64_t heads,
+                             int64_t kv_heads, int64_t head_dim, float eps, float scale, void* out,
+                             void* workspace, int64_t workspace_bytes, int dtype,
+                             veda_stream_t stream);
 /* Seeded N(0, std) fill (counter-based hash + Box-Muller) for synthetic weights. */
 int veda_randn(void* x, int64_t n, float std, uint64_t seed, int dtype, veda_stream_t stream);
 /* fp32 -> bf16 rounding copy (round to nearest even). */

@@ -92,15 +92,18 @@ def test_qwen_shaped_bf16_cached_generation_matches_uncached():
     t.close()
 
 
-@pytest.mark.parametrize("dtype,heads,kv,dh,pos", [(0, 4, 2, 16, 0), (1, 16, 8, 128, 37)])
+@pytest.mark.parametrize("dtype,heads,kv,dh,pos", [(0, 4, 2, 16, 0), (1, 16, 8, 128, 37), (0, 4, 4, 128, 5),
+                                                  (1, 16, 4, 128, 300), (1, 32, 4, 128, 50), (1, 16, 8, 128, 0),
+                                                  (1, 16, 8, 128, 1000), (0, 8, 4, 128, 200)])
 def test_decode_step_kernels_read_the_device_position(dtype, heads, kv, dh, pos):
     """One token's QK-norm + RoPE at the position held in device memory, its K/V rows written into
-    the cache at that position, and attention over positions 0..pos, against the oracle and the
-    length-argument kernel; the position then advances by one on the device."""
+    the cache at that position, and attention over positions 0..pos: the two-launch path against
+    the oracle and the length-argument kernel, the fused launch (head_dim 128) against both; the
+    position then advances by one on the device."""
     import torch
     import veda_b200 as V
     from tests.gpu_util import bf, call, stream
-    r = np.random.default_rng(pos + dh)
+    r = np.random.default_rng(pos + dh + heads)
     cap = pos + 3
     W = (heads + 2 * kv) * dh
     qkv = r.standard_normal((1, W)).astype(np.float32)
@@ -114,27 +117,41 @@ def test_decode_step_kernels_read_the_device_position(dtype, heads, kv, dh, pos)
     q = qkv[0, :heads * dh].reshape(heads, dh)
     k = qkv[0, heads * dh:(heads + kv) * dh].reshape(kv, dh)
     v = qkv[0, (heads + kv) * dh:].reshape(kv * dh)
-    q_ref = O.rope(O.rms_norm_gamma(q, qg, 1e-6)[0], cos[pos], sin[pos]).reshape(-1)
+    q_ref = O.rope(O.rms_norm_gamma(q, qg, 1e-6)[0], cos[pos], sin[pos])
     k_ref = O.rope(O.rms_norm_gamma(k, kg, 1e-6)[0], cos[pos], sin[pos]).reshape(-1)
+    scale = 1.0 / math.sqrt(dh)
+    keys, vals = kc[:pos + 1].copy(), vc[:pos + 1].copy()
+    keys[pos], vals[pos] = k_ref, v
+    att_ref = np.empty((heads, dh), np.float32)
+    for h in range(heads):
+        g = h // (heads // kv)
+        sc = (keys[:, g * dh:(g + 1) * dh] @ q_ref[h]) * scale
+        e = np.exp(sc - sc.max())
+        att_ref[h] = (e / e.sum()) @ vals[:, g * dh:(g + 1) * dh]
     tdt = torch.float32 if dtype == 0 else torch.bfloat16
     d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to("cuda").to(tdt)
-    dqkv, dqg, dkg, dk, dv = d(qkv), d(qg), d(kg), d(kc), d(vc)
+    dqkv, dqg, dkg = d(qkv), d(qg), d(kg)
     dcos, dsin = (torch.from_numpy(a).to("cuda") for a in (cos, sin))
     dpos = torch.tensor([pos], dtype=torch.int64, device="cuda")
-    qr = torch.empty((heads * dh,), dtype=tdt, device="cuda")
     dt = V.F32 if dtype == 0 else V.BF16
+    tol = 1e-5 if dtype == 0 else 2e-2
+    rows = [i for i in range(cap) if i != pos]
+
+    def check_cache(dk, dv):
+        kc_got, vc_got = dk.float().cpu().numpy(), dv.float().cpu().numpy()
+        assert O.max_abs_rel(kc_got[pos], k_ref) <= tol
+        assert np.array_equal(vc_got[pos], v.astype(np.float32))
+        assert np.array_equal(kc_got[rows], kc[rows].astype(np.float32))   # other rows untouched
+        assert np.array_equal(vc_got[rows], vc[rows].astype(np.float32))
+
+    # two launches: q/k/v at the position, then attention reading it
+    dk, dv = d(kc), d(vc)
+    qr = torch.empty((heads * dh,), dtype=tdt, device="cuda")
     call("veda_decode_qkv_at", dqkv.data_ptr(), dqg.data_ptr(), dkg.data_ptr(), dcos.data_ptr(),
          dsin.data_ptr(), dpos.data_ptr(), qr.data_ptr(), dk.data_ptr(), dv.data_ptr(), kv * dh, heads,
          kv, dh, 1e-6, dt, stream())
-    tol = 1e-5 if dtype == 0 else 2e-2
-    assert O.max_abs_rel(qr.float().cpu().numpy(), q_ref) <= tol
-    kc_got, vc_got = dk.float().cpu().numpy(), dv.float().cpu().numpy()
-    assert O.max_abs_rel(kc_got[pos], k_ref) <= tol
-    assert np.array_equal(vc_got[pos], v.astype(np.float32))
-    rows = [i for i in range(cap) if i != pos]
-    assert np.array_equal(kc_got[rows], kc[rows].astype(np.float32))   # other rows untouched
-    assert np.array_equal(vc_got[rows], vc[rows].astype(np.float32))
-    scale = 1.0 / math.sqrt(dh)
+    assert O.max_abs_rel(qr.float().cpu().numpy(), q_ref.reshape(-1)) <= tol
+    check_cache(dk, dv)
     out_at = torch.empty((heads, dh), dtype=tdt, device="cuda")
     out_len = torch.empty((heads, dh), dtype=tdt, device="cuda")
     call("veda_attention_decode_at", qr.data_ptr(), dk.data_ptr(), dv.data_ptr(), kv * dh, dpos.data_ptr(),
@@ -142,8 +159,84 @@ def test_decode_step_kernels_read_the_device_position(dtype, heads, kv, dh, pos)
     call("veda_attention_decode", qr.data_ptr(), dk.data_ptr(), dv.data_ptr(), kv * dh, pos + 1, heads, kv,
          dh, scale, out_len.data_ptr(), dt, stream())
     assert torch.equal(out_at, out_len)
+    assert O.max_abs_rel(out_at.float().cpu().numpy(), att_ref) <= tol
+    # one launch, the positions split across CTAs by the capacity (cap rows) and merged through the
+    # workspace; a second call on the same workspace gives the same result (its counters reset)
+    ws = V.lib().veda_decode_attention_workspace(heads, kv, cap)
+    work = torch.zeros(ws, dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        dk2, dv2 = d(kc), d(vc)
+        out_f = torch.empty((heads, dh), dtype=tdt, device="cuda")
+        args = (dqkv.data_ptr(), dqg.data_ptr(), dkg.data_ptr(), dcos.data_ptr(), dsin.data_ptr(),
+                dpos.data_ptr(), dk2.data_ptr(), dv2.data_ptr(), kv * dh, cap, heads, kv, dh, 1e-6, scale,
+                out_f.data_ptr(), work.data_ptr(), ws, dt, stream())
+        if dh != 128:
+            assert V.lib().veda_decode_attention_at(*args) == V.ERR_UNSUPPORTED
+            break
+        call("veda_decode_attention_at", *args)
+        check_cache(dk2, dv2)
+        assert O.max_abs_rel(out_f.float().cpu().numpy(), att_ref) <= tol
+        assert O.max_abs_rel(out_f.float().cpu().numpy(), out_at.float().cpu().numpy()) <= tol
+    if dh == 128:
+        assert not bool(work[:256].any())   # the merge counters are back at zero
+        small = args[:16] + (work.data_ptr(), ws - 4) + args[18:]
+        assert V.lib().veda_decode_attention_at(*small) == V.ERR_INVALID_ARGUMENT
     call("veda_decode_advance", dpos.data_ptr(), stream())
     assert int(dpos.item()) == pos + 1
+
+
+@pytest.mark.parametrize("dtype,k,with_r", [(1, 1024, True), (1, 1024, False), (1, 2048, True),
+                                            (0, 96, True), (1, 200, True)])
+def test_gemv_with_rmsnorm_prologue(dtype, k, with_r):
+    """The pre-norm computed inside the projection equals the separate add + RMSNorm then the
+    projection: the residual sum bit for bit, the outputs within one rounding of the dtype."""
+    import torch
+    import veda_b200 as V
+    from tests.gpu_util import bf, call, stream
+    r = np.random.default_rng(k + with_r)
+    n = 3 * 96
+    x = r.standard_normal(k).astype(np.float32)
+    dlt = r.standard_normal(k).astype(np.float32)
+    gam = (1 + 0.1 * r.standard_normal(k)).astype(np.float32)
+    w = r.standard_normal((2 * n, k)).astype(np.float32)
+    if dtype == 1:
+        x, dlt, gam, w = bf(x), bf(dlt), bf(gam), bf(w)
+    tdt = torch.float32 if dtype == 0 else torch.bfloat16
+    dt = V.F32 if dtype == 0 else V.BF16
+    dx, dr, dg, dw = (torch.from_numpy(a).to("cuda").to(tdt) for a in (x, dlt, gam, w))
+    rp = dr.data_ptr() if with_r else None
+    s_sep, a_sep = torch.empty(k, dtype=tdt, device="cuda"), torch.empty(k, dtype=tdt, device="cuda")
+    if with_r:
+        call("veda_add_rmsnorm_fwd", dx.data_ptr(), k, dr.data_ptr(), k, dg.data_ptr(), s_sep.data_ptr(), k,
+             a_sep.data_ptr(), k, 1, k, 1e-6, dt, stream())
+    else:
+        s_sep.copy_(dx)
+        call("veda_rmsnorm_fwd", dx.data_ptr(), k, dg.data_ptr(), a_sep.data_ptr(), k, 1, k, 1e-6, dt, stream())
+    y_sep = torch.empty(2 * n, dtype=tdt, device="cuda")
+    call("veda_gemv_nt", a_sep.data_ptr(), dw.data_ptr(), k, y_sep.data_ptr(), 2 * n, k, dt, stream())
+    h_sep = torch.empty(n, dtype=tdt, device="cuda")
+    call("veda_gemv_swiglu", a_sep.data_ptr(), dw.data_ptr(), k, h_sep.data_ptr(), n, k, dt, stream())
+    s = torch.zeros(k, dtype=tdt, device="cuda")
+    y = torch.empty(2 * n, dtype=tdt, device="cuda")
+    call("veda_gemv_rmsnorm", dx.data_ptr(), rp, dg.data_ptr(), 1e-6, s.data_ptr() if with_r else None,
+         dw.data_ptr(), k, y.data_ptr(), 2 * n, k, dt, stream())
+    h = torch.empty(n, dtype=tdt, device="cuda")
+    call("veda_gemv_rmsnorm_swiglu", dx.data_ptr(), rp, dg.data_ptr(), 1e-6, None, dw.data_ptr(), k,
+         h.data_ptr(), n, k, dt, stream())
+    if with_r:
+        assert torch.equal(s, s_sep)
+    tol = 1e-5 if dtype == 0 else 1e-2
+    assert O.max_abs_rel(y.float().cpu().numpy(), y_sep.float().cpu().numpy()) <= tol
+    assert O.max_abs_rel(h.float().cpu().numpy(), h_sep.float().cpu().numpy()) <= tol
+    # the oracle: s = x + r rounded, RMSNorm * gamma, then the product
+    sr = (x + dlt) if with_r else x
+    if dtype == 1:
+        sr = bf(sr)
+    a_ref = O.rms_norm_gamma(sr[None, :], gam, 1e-6)[0][0]
+    assert O.max_abs_rel(y.float().cpu().numpy(), w.astype(np.float64) @ a_ref.astype(np.float64)) <= \
+        (1e-4 if dtype == 0 else 2e-2)
+    assert V.lib().veda_gemv_rmsnorm(dx.data_ptr(), rp, dg.data_ptr(), 1e-6, dx.data_ptr(), dw.data_ptr(), k,
+                                     y.data_ptr(), 2 * n, k, dt, stream()) == V.ERR_INVALID_ARGUMENT
 
 
 @pytest.mark.parametrize("dtype,n,k,ldw", [(0, 37, 24, 24), (1, 1024, 3072, 3072), (1, 9000, 1024, 1032),

@@ -91,6 +91,11 @@ SIGNATURES = {
     "veda_decode_advance": (_i, [_p, _p]),
     "veda_gemv_nt": (_i, [_p, _p, _i64, _p, _i64, _i64, _i, _p]),
     "veda_gemv_swiglu": (_i, [_p, _p, _i64, _p, _i64, _i64, _i, _p]),
+    "veda_gemv_rmsnorm": (_i, [_p, _p, _p, _f, _p, _p, _i64, _p, _i64, _i64, _i, _p]),
+    "veda_gemv_rmsnorm_swiglu": (_i, [_p, _p, _p, _f, _p, _p, _i64, _p, _i64, _i64, _i, _p]),
+    "veda_decode_attention_workspace": (_i64, [_i64, _i64, _i64]),
+    "veda_decode_attention_at": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f, _f,
+                                      _p, _p, _i64, _i, _p]),
     "veda_randn": (_i, [_p, _i64, _f, _u64, _i, _p]),
     "veda_f32_to_bf16": (_i, [_p, _p, _i64, _p]),
     "veda_corpus_gather": (_i, [_p, _i64, _i64, C.c_uint64, _i64, _i64, _p, _p, _p]),

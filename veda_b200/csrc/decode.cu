@@ -5,6 +5,8 @@
 // veda_argmax (elementwise.cu).
 #include "common.cuh"
 
+#include <algorithm>
+
 
 namespace veda::cuda
 {
@@ -306,14 +308,83 @@ __device__ __forceinline__ float silu_gate(float g) { return g * __fdividef(1.0f
 // SWIGLU: the warp's two rows are gate row j and up row n + j of the fused [2n, k] weight, and the
 // output is h[j] = silu(g) * u on the values rounded to the dtype (the separate Linear then SwiGLU
 // of Model.cpp:198-204, same arithmetic as veda_swiglu_fwd).
-template <typename T, int R, bool SWIGLU, bool VEC>
+// NORM: the activation is RMSNorm(s) * gamma of the residual row s = x (+ r), computed by every
+// block into its shared copy (the pre-norm of Model.cpp:242-249 ahead of its Linear layer): s is
+// rounded to the dtype as the residual add stores it, and block 0 writes it to sum_out; the sum of
+// squares runs in the order of the streaming RMSNorm (16-byte pieces, piece lane + 32 c of lane,
+// then across the warp), y = (s / rms) * gamma rounded once.
+template <typename T, int R, bool SWIGLU, bool VEC, bool NORM>
 __global__ void __launch_bounds__(kGemvWarps * 32)
-gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __restrict__ y, int n, int k)
+gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __restrict__ y, int n, int k,
+            const T* __restrict__ r_in, const T* __restrict__ gamma, T* __restrict__ sum_out, float eps)
 {
     extern __shared__ __align__(16) unsigned char gemv_smem[];
     T* xs = reinterpret_cast<T*>(gemv_smem);
     constexpr int E = 16 / sizeof(T);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int per_warp = SWIGLU ? 1 : R;
+    const int base = (blockIdx.x * kGemvWarps + warp) * per_warp;
+    const bool active = base < n;
+    const T* rows[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+    {
+        const int row = SWIGLU ? base : min(base + r, n - 1);   // a row past n repeats the last one
+        rows[r] = w + (static_cast<int64_t>(row) + (SWIGLU ? static_cast<int64_t>(r) * n : 0)) * ldw;
+    }
+    // The first pieces of the weight rows do not depend on the activation: their loads are issued
+    // before it is staged, so the HBM latency overlaps the staging (and the norm).
+    uint4 wv0[kGemvUnroll][R];
     if constexpr (VEC)
+    {
+        if (active)
+        {
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; ++u)
+            {
+                const int c = lane * E + u * 32 * E;
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                    if (c < k) wv0[u][r] = load_stream16(rows[r] + c);
+            }
+        }
+    }
+    if constexpr (NORM)
+    {
+        __shared__ float inv_s;
+        for (int i = threadIdx.x; i < k; i += blockDim.x)
+        {
+            float v = to_f32(x[i]);
+            if (r_in != nullptr) v += to_f32(r_in[i]);
+            const T t = from_f32<T>(v);
+            xs[i] = t;
+            if (blockIdx.x == 0 && sum_out != nullptr) sum_out[i] = t;
+        }
+        __syncthreads();
+        if (warp == 0)
+        {
+            float ss = 0.0f;
+            for (int i = lane * E; i < k; i += 32 * E)
+            {
+#pragma unroll
+                for (int j = 0; j < E; ++j)
+                {
+                    if (i + j < k)
+                    {
+                        const float v = to_f32(xs[i + j]);
+                        ss += v * v;
+                    }
+                }
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) inv_s = 1.0f / sqrtf(ss / static_cast<float>(k) + eps);
+        }
+        __syncthreads();
+        const float inv = inv_s;
+        for (int i = threadIdx.x; i < k; i += blockDim.x)
+            xs[i] = from_f32<T>((to_f32(xs[i]) * inv) * to_f32(gamma[i]));
+    }
+    else if constexpr (VEC)
     {
         for (int i = threadIdx.x * E; i < k; i += blockDim.x * E)
             *reinterpret_cast<uint4*>(xs + i) = *reinterpret_cast<const uint4*>(x + i);
@@ -323,33 +394,13 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
         for (int i = threadIdx.x; i < k; i += blockDim.x) xs[i] = x[i];
     }
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    constexpr int per_warp = SWIGLU ? 1 : R;
-    const int base = (blockIdx.x * kGemvWarps + warp) * per_warp;
-    if (base >= n) return;
-    const T* rows[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-    {
-        const int row = SWIGLU ? base : min(base + r, n - 1);   // a row past n repeats the last one
-        rows[r] = w + (static_cast<int64_t>(row) + (SWIGLU ? static_cast<int64_t>(r) * n : 0)) * ldw;
-    }
+    if (!active) return;
     float acc[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) acc[r] = 0.0f;
     if constexpr (VEC)
     {
-        for (int c0 = lane * E; c0 < k; c0 += 32 * E * kGemvUnroll)
-        {
-            uint4 wv[kGemvUnroll][R];
-#pragma unroll
-            for (int u = 0; u < kGemvUnroll; ++u)
-            {
-                const int c = c0 + u * 32 * E;
-#pragma unroll
-                for (int r = 0; r < R; ++r)
-                    if (c < k) wv[u][r] = load_stream16(rows[r] + c);
-            }
+        auto consume = [&](const uint4 (&wv)[kGemvUnroll][R], int c0) {
 #pragma unroll
             for (int u = 0; u < kGemvUnroll; ++u)
             {
@@ -368,6 +419,20 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
                     }
                 }
             }
+        };
+        consume(wv0, lane * E);
+        for (int c0 = lane * E + 32 * E * kGemvUnroll; c0 < k; c0 += 32 * E * kGemvUnroll)
+        {
+            uint4 wv[kGemvUnroll][R];
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; ++u)
+            {
+                const int c = c0 + u * 32 * E;
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                    if (c < k) wv[u][r] = load_stream16(rows[r] + c);
+            }
+            consume(wv, c0);
         }
     }
     else
@@ -395,9 +460,18 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
     }
 }
 
+// The pre-norm operands of a NORM launch (all null for a plain one).
+struct GemvNorm
+{
+    const void* r = nullptr;
+    const void* gamma = nullptr;
+    void* sum = nullptr;
+    float eps = 0.0f;
+};
+
 template <typename T, int R, bool SWIGLU>
 void launch_gemv(const void* x, const void* w, int64_t ldw, void* y, int64_t n, int64_t k, bool vec,
-                 cudaStream_t stream)
+                 const GemvNorm* norm, cudaStream_t stream)
 {
     constexpr int per_warp = SWIGLU ? 1 : R;
     const auto blocks = static_cast<unsigned>((n + kGemvWarps * per_warp - 1) / (kGemvWarps * per_warp));
@@ -405,12 +479,305 @@ void launch_gemv(const void* x, const void* w, int64_t ldw, void* y, int64_t n, 
     const auto xp = static_cast<const T*>(x);
     const auto wp = static_cast<const T*>(w);
     const auto yp = static_cast<T*>(y);
-    if (vec)
-        gemv_kernel<T, R, SWIGLU, true><<<blocks, kGemvWarps * 32, smem, stream>>>(
-            xp, wp, ldw, yp, static_cast<int>(n), static_cast<int>(k));
+    const auto ni = static_cast<int>(n), ki = static_cast<int>(k);
+    const auto rp = norm ? static_cast<const T*>(norm->r) : nullptr;
+    const auto gp = norm ? static_cast<const T*>(norm->gamma) : nullptr;
+    const auto sp = norm ? static_cast<T*>(norm->sum) : nullptr;
+    const float eps = norm ? norm->eps : 0.0f;
+#define VEDA_GEMV(V, N)                                                                            \
+    gemv_kernel<T, R, SWIGLU, V, N><<<blocks, kGemvWarps * 32, smem, stream>>>(xp, wp, ldw, yp, ni, \
+                                                                              ki, rp, gp, sp, eps)
+    if (norm != nullptr)
+    {
+        if (vec) VEDA_GEMV(true, true);
+        else VEDA_GEMV(false, true);
+    }
     else
-        gemv_kernel<T, R, SWIGLU, false><<<blocks, kGemvWarps * 32, smem, stream>>>(
-            xp, wp, ldw, yp, static_cast<int>(n), static_cast<int>(k));
+    {
+        if (vec) VEDA_GEMV(true, false);
+        else VEDA_GEMV(false, false);
+    }
+#undef VEDA_GEMV
+}
+
+// ---- the decode step's attention, fused with the q/k/v handling of its token ---------------
+// One CTA per KV head and the G = H / Hkv query heads that read it (Dh = 128): warps first take
+// QK-norm + RoPE of those query heads (into shared memory, rounded to the dtype as the projection
+// output would be stored) and of the KV head's new key (into cache row *pos), and copy its value
+// row; then 16 half-warps walk the positions 0..*pos, lane l of a half-warp holding dimensions
+// [8l, 8l + 8), two positions per half-warp loaded before either is used, each keeping an online
+// softmax state per query head in fp32; half-warps merge through shuffles, warps through shared
+// memory. Reads every cached key and value once per KV head instead of once per query head.
+// WARPS warps, U positions per half-warp loaded before any is used: 16 and 4 for G <= 2 (128
+// positions in flight per KV head), fewer where G's per-head registers need the room.
+constexpr int kFusedDim = 128;
+
+template <typename T>
+struct Raw8
+{
+    uint4 v[sizeof(T) / 2];   // 8 elements: one 16-byte vector (bf16) or two (fp32)
+};
+
+template <typename T>
+__device__ __forceinline__ Raw8<T> load_raw8(const T* p)
+{
+    Raw8<T> r;
+#pragma unroll
+    for (int i = 0; i < static_cast<int>(sizeof(T) / 2); ++i) r.v[i] = reinterpret_cast<const uint4*>(p)[i];
+    return r;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack_raw8(const Raw8<T>& r, float (&o)[8])
+{
+    if constexpr (sizeof(T) == 2)
+    {
+        unpack16<T>(r.v[0], o);
+    }
+    else
+    {
+        float a[4], b[4];
+        unpack16<T>(r.v[0], a);
+        unpack16<T>(r.v[1], b);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+        {
+            o[i] = a[i];
+            o[4 + i] = b[i];
+        }
+    }
+}
+
+template <typename T, int G, int WARPS, int U>
+__global__ void __launch_bounds__(WARPS * 32)
+decode_attn_fused_kernel(const T* __restrict__ qkv, const T* __restrict__ qgain, const T* __restrict__ kgain,
+                         const float* __restrict__ cosv, const float* __restrict__ sinv,
+                         const int64_t* __restrict__ pos, T* __restrict__ k_cache, T* __restrict__ v_cache,
+                         int64_t ldkv, int kv_heads, float eps, float scale, T* __restrict__ out,
+                         int64_t capacity, int64_t chunk, float* __restrict__ part,
+                         unsigned* __restrict__ counters)
+{
+    constexpr int D = kFusedDim;
+    constexpr int S = WARPS * 2;   // half-warps, each a stride-S slice of the positions
+    __shared__ __align__(16) float q_s[G][D];
+    __shared__ float m_s[WARPS][G], l_s[WARPS][G];
+    __shared__ __align__(16) float acc_s[WARPS][G][D];
+    __shared__ bool last_s;
+    const int64_t p = *pos;
+    if (p < 0 || p >= capacity) return;   // a position outside the cache writes nothing
+    const int kvh = blockIdx.x;
+    const int heads = kv_heads * G;
+    // this CTA's slice of the positions 0..p; the slice holding p also writes the new key and value
+    const int split = blockIdx.y;
+    const int64_t lo = static_cast<int64_t>(split) * chunk;
+    if (lo > p) return;
+    const int64_t hi = min(lo + chunk, p + 1);
+    const int active = static_cast<int>(p / chunk) + 1;
+    const bool owner = split == active - 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // item g < G: query head kvh * G + g; item G: the key; item G + 1: the value
+    for (int item = warp; item < G + 2; item += WARPS)
+    {
+        if (item >= G && !owner) continue;
+        if (item == G + 1)
+        {
+            const T* src = qkv + static_cast<int64_t>(heads + kv_heads + kvh) * D;
+            T* dst = v_cache + p * ldkv + static_cast<int64_t>(kvh) * D;
+            for (int d = lane; d < D; d += 32) dst[d] = src[d];
+            continue;
+        }
+        const bool is_q = item < G;
+        const T* src = qkv + static_cast<int64_t>(is_q ? kvh * G + item : heads + kvh) * D;
+        const T* gain = is_q ? qgain : kgain;
+        float xv[4], ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+        {
+            xv[i] = to_f32(src[lane + 32 * i]);
+            ss += xv[i] * xv[i];
+        }
+        ss = warp_sum(ss);
+        const float r = sqrtf(ss / static_cast<float>(D) + eps);   // x / r, as RMSNorm divides
+        float a[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = (xv[i] / r) * to_f32(gain[lane + 32 * i]);
+        // half-split rotation: dimension d < 64 pairs with d + 64 (lane + 32 i with lane + 32 (i + 2))
+        const float* cr = cosv + p * D;
+        const float* sr = sinv + p * D;
+        float o[4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+        {
+            const int d = lane + 32 * i;
+            o[i] = a[i] * cr[d] - a[i + 2] * sr[d];
+            o[i + 2] = a[i + 2] * cr[d] + a[i] * sr[d];
+        }
+        if (is_q)
+        {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) q_s[item][lane + 32 * i] = to_f32(from_f32<T>(o[i]));
+        }
+        else
+        {
+            T* dst = k_cache + p * ldkv + static_cast<int64_t>(kvh) * D;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = from_f32<T>(o[i]);
+        }
+    }
+    __syncthreads();   // the new key and value rows and the queries are visible to the whole block
+
+    const int hw = lane >> 4, hl = lane & 15;
+    const unsigned half = 0xFFFFu << (16 * hw);
+    const int slot = warp * 2 + hw;
+    const int d0 = hl * 8;
+    float qf[G][8], m[G], l[G], acc[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+    {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+        {
+            qf[g][i] = q_s[g][d0 + i];
+            acc[g][i] = 0.0f;
+        }
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+    }
+    const T* kb = k_cache + static_cast<int64_t>(kvh) * D + d0;
+    const T* vb = v_cache + static_cast<int64_t>(kvh) * D + d0;
+    auto step = [&](const Raw8<T>& kr, const Raw8<T>& vr) {
+        float kf[8], vf[8], dot[G];
+        unpack_raw8<T>(kr, kf);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+        {
+            dot[g] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dot[g] += qf[g][i] * kf[i];
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+        {
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) dot[g] += __shfl_xor_sync(half, dot[g], o);
+        }
+        unpack_raw8<T>(vr, vf);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+        {
+            const float sc = dot[g] * scale;
+            const float mn = fmaxf(m[g], sc);
+            const float corr = expf(m[g] - mn);   // 0 on the first position (m = -inf)
+            const float pe = expf(sc - mn);
+            l[g] = l[g] * corr + pe;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[g][i] = acc[g][i] * corr + pe * vf[i];
+            m[g] = mn;
+        }
+    };
+    for (int64_t j0 = lo + slot; j0 < hi; j0 += U * S)
+    {
+        Raw8<T> kr[U], vr[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+        {
+            const int64_t j = j0 + u * S;
+            if (j < hi)
+            {
+                kr[u] = load_raw8(kb + j * ldkv);
+                vr[u] = load_raw8(vb + j * ldkv);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (j0 + u * S < hi) step(kr[u], vr[u]);
+    }
+
+    // merge the two half-warps of each warp, then the warps
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+    {
+        const float m2 = __shfl_xor_sync(0xFFFFFFFFu, m[g], 16);
+        const float l2 = __shfl_xor_sync(0xFFFFFFFFu, l[g], 16);
+        const float mx = fmaxf(m[g], m2);
+        const float c1 = m[g] == -INFINITY ? 0.0f : expf(m[g] - mx);
+        const float c2 = m2 == -INFINITY ? 0.0f : expf(m2 - mx);
+        l[g] = l[g] * c1 + l2 * c2;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+        {
+            const float a2 = __shfl_xor_sync(0xFFFFFFFFu, acc[g][i], 16);
+            acc[g][i] = acc[g][i] * c1 + a2 * c2;
+        }
+        m[g] = mx;
+        if (hw == 0)
+        {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc_s[warp][g][d0 + i] = acc[g][i];
+            if (hl == 0)
+            {
+                m_s[warp][g] = m[g];
+                l_s[warp][g] = l[g];
+            }
+        }
+    }
+    __syncthreads();
+    // the CTA's (max, sum, unnormalised output) per query head and dimension; one slice: the result
+    constexpr int PS = D + 2;   // a partial: max, sum, then D outputs
+    for (int t = threadIdx.x; t < G * D; t += blockDim.x)
+    {
+        const int g = t / D, d = t % D;
+        float mx = -INFINITY;
+        for (int w = 0; w < WARPS; ++w) mx = fmaxf(mx, m_s[w][g]);
+        float ls = 0.0f, o = 0.0f;
+        for (int w = 0; w < WARPS; ++w)
+        {
+            const float c = m_s[w][g] == -INFINITY ? 0.0f : expf(m_s[w][g] - mx);
+            ls += l_s[w][g] * c;
+            o += acc_s[w][g][d] * c;
+        }
+        if (active == 1)
+        {
+            out[static_cast<int64_t>(kvh * G + g) * D + d] = from_f32<T>(o / ls);
+        }
+        else
+        {
+            float* pr = part + ((static_cast<int64_t>(kvh) * gridDim.y + split) * G + g) * PS;
+            pr[2 + d] = o;
+            if (d == 0)
+            {
+                pr[0] = mx;
+                pr[1] = ls;
+            }
+        }
+    }
+    if (active == 1) return;
+    // The last slice of this KV head to finish merges them all (no CTA waits on another): each
+    // CTA's partials are made visible device-wide before its arrival is counted.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last_s = atomicAdd(&counters[kvh], 1u) == static_cast<unsigned>(active - 1);
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+    for (int t = threadIdx.x; t < G * D; t += blockDim.x)
+    {
+        const int g = t / D, d = t % D;
+        const float* pr = part + (static_cast<int64_t>(kvh) * gridDim.y * G + g) * PS;
+        const int64_t stride = static_cast<int64_t>(G) * PS;   // from one slice to the next
+        float mx = -INFINITY;
+        for (int sp = 0; sp < active; ++sp) mx = fmaxf(mx, __ldcg(pr + sp * stride));
+        float ls = 0.0f, o = 0.0f;
+        for (int sp = 0; sp < active; ++sp)
+        {
+            const float c = expf(__ldcg(pr + sp * stride) - mx);   // every slice has >= 1 position
+            ls += __ldcg(pr + sp * stride + 1) * c;
+            o += __ldcg(pr + sp * stride + 2 + d) * c;
+        }
+        out[static_cast<int64_t>(kvh * G + g) * D + d] = from_f32<T>(o / ls);
+    }
+    if (threadIdx.x == 0) counters[kvh] = 0u;   // ready for the next call
 }
 
 int gemv_checks(const void* x, const void* w, int64_t ldw, const void* y, int64_t n, int64_t k, int dtype)
@@ -427,7 +794,37 @@ int gemv_checks(const void* x, const void* w, int64_t ldw, const void* y, int64_
 bool gemv_vec(const void* x, const void* w, int64_t ldw, int64_t k, int dtype)
 {
     const int64_t e = 16 / static_cast<int64_t>(dtype_size(dtype));
-    return aligned16(x) && aligned16(w) && k % e == 0 && ldw % e == 0;
+    return (x == nullptr || aligned16(x)) && aligned16(w) && k % e == 0 && ldw % e == 0;
+}
+
+int gemv_dispatch(const void* x, const void* w, int64_t ldw, void* y, int64_t n, int64_t k, int dtype,
+                  bool swiglu, const GemvNorm* norm, cudaStream_t stream)
+{
+    const bool vec = gemv_vec(norm ? nullptr : x, w, ldw, k, dtype);
+    // two rows a warp once there are enough rows to fill the SMs with them
+    const bool two = n >= 8192;
+    if (dtype == VEDA_BF16)
+    {
+        if (swiglu) launch_gemv<bf16, 2, true>(x, w, ldw, y, n, k, vec, norm, stream);
+        else if (two) launch_gemv<bf16, 2, false>(x, w, ldw, y, n, k, vec, norm, stream);
+        else launch_gemv<bf16, 1, false>(x, w, ldw, y, n, k, vec, norm, stream);
+    }
+    else
+    {
+        if (swiglu) launch_gemv<float, 2, true>(x, w, ldw, y, n, k, vec, norm, stream);
+        else if (two) launch_gemv<float, 2, false>(x, w, ldw, y, n, k, vec, norm, stream);
+        else launch_gemv<float, 1, false>(x, w, ldw, y, n, k, vec, norm, stream);
+    }
+    count_launch();
+    return 0;
+}
+
+int norm_checks(const void* x, const void* r, const void* gamma, const void* sum)
+{
+    VEDA_REQUIRE(gamma != nullptr, "null pointer");
+    VEDA_REQUIRE(sum == nullptr || (sum != x && sum != r), "sum must not alias x or r (block 0 writes it "
+                                                          "while the others read them)");
+    return 0;
 }
 } // namespace
 } // namespace veda::cuda
@@ -436,20 +833,7 @@ extern "C" int veda_gemv_nt(const void* x, const void* w, int64_t ldw, void* y, 
                             int dtype, veda_stream_t stream)
 {
     if (const int rc = gemv_checks(x, w, ldw, y, n, k, dtype)) return rc;
-    const bool vec = gemv_vec(x, w, ldw, k, dtype);
-    // two rows a warp once there are enough rows to fill the SMs with them
-    const bool two = n >= 8192;
-    if (dtype == VEDA_BF16)
-    {
-        if (two) launch_gemv<bf16, 2, false>(x, w, ldw, y, n, k, vec, stream);
-        else launch_gemv<bf16, 1, false>(x, w, ldw, y, n, k, vec, stream);
-    }
-    else
-    {
-        if (two) launch_gemv<float, 2, false>(x, w, ldw, y, n, k, vec, stream);
-        else launch_gemv<float, 1, false>(x, w, ldw, y, n, k, vec, stream);
-    }
-    count_launch();
+    gemv_dispatch(x, w, ldw, y, n, k, dtype, false, nullptr, stream);
     return check_launch("veda_gemv_nt");
 }
 
@@ -457,9 +841,104 @@ extern "C" int veda_gemv_swiglu(const void* x, const void* w_gate_up, int64_t ld
                                 int64_t k, int dtype, veda_stream_t stream)
 {
     if (const int rc = gemv_checks(x, w_gate_up, ldw, h, f, k, dtype)) return rc;
-    const bool vec = gemv_vec(x, w_gate_up, ldw, k, dtype);
-    if (dtype == VEDA_BF16) launch_gemv<bf16, 2, true>(x, w_gate_up, ldw, h, f, k, vec, stream);
-    else launch_gemv<float, 2, true>(x, w_gate_up, ldw, h, f, k, vec, stream);
-    count_launch();
+    gemv_dispatch(x, w_gate_up, ldw, h, f, k, dtype, true, nullptr, stream);
     return check_launch("veda_gemv_swiglu");
+}
+
+extern "C" int veda_gemv_rmsnorm(const void* x, const void* r, const void* gamma, float eps, void* sum,
+                                 const void* w, int64_t ldw, void* y, int64_t n, int64_t k, int dtype,
+                                 veda_stream_t stream)
+{
+    if (const int rc = gemv_checks(x, w, ldw, y, n, k, dtype)) return rc;
+    if (const int rc = norm_checks(x, r, gamma, sum)) return rc;
+    const GemvNorm norm{r, gamma, sum, eps};
+    gemv_dispatch(x, w, ldw, y, n, k, dtype, false, &norm, stream);
+    return check_launch("veda_gemv_rmsnorm");
+}
+
+extern "C" int veda_gemv_rmsnorm_swiglu(const void* x, const void* r, const void* gamma, float eps, void* sum,
+                                        const void* w_gate_up, int64_t ldw, void* h, int64_t f, int64_t k,
+                                        int dtype, veda_stream_t stream)
+{
+    if (const int rc = gemv_checks(x, w_gate_up, ldw, h, f, k, dtype)) return rc;
+    if (const int rc = norm_checks(x, r, gamma, sum)) return rc;
+    const GemvNorm norm{r, gamma, sum, eps};
+    gemv_dispatch(x, w_gate_up, ldw, h, f, k, dtype, true, &norm, stream);
+    return check_launch("veda_gemv_rmsnorm_swiglu");
+}
+
+namespace
+{
+// Positions per CTA slice for a cache of `capacity` rows: 64, or more so that at most 64 slices
+// cover it.
+int64_t decode_chunk(int64_t capacity)
+{
+    const int64_t c = (capacity + 63) / 64;
+    return std::max<int64_t>(64, (c + 63) / 64 * 64);
+}
+
+int64_t decode_workspace(int64_t heads, int64_t kv_heads, int64_t capacity)
+{
+    const int64_t splits = (capacity + decode_chunk(capacity) - 1) / decode_chunk(capacity);
+    const int64_t counters = (kv_heads * 4 + 255) / 256 * 256;
+    return counters + kv_heads * splits * (heads / kv_heads) * (kFusedDim + 2) * 4;
+}
+} // namespace
+
+extern "C" int64_t veda_decode_attention_workspace(int64_t heads, int64_t kv_heads, int64_t capacity)
+{
+    if (heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || capacity <= 0) return -1;
+    return decode_workspace(heads, kv_heads, capacity);
+}
+
+extern "C" int veda_decode_attention_at(const void* qkv, const void* q_gain, const void* k_gain,
+                                        const float* cos, const float* sin, const int64_t* pos, void* k_cache,
+                                        void* v_cache, int64_t ldkv, int64_t capacity, int64_t heads,
+                                        int64_t kv_heads, int64_t head_dim, float eps, float scale, void* out,
+                                        void* workspace, int64_t workspace_bytes, int dtype, veda_stream_t stream)
+{
+    VEDA_REQUIRE(valid_dtype(dtype), "unknown dtype");
+    VEDA_REQUIRE(qkv && q_gain && k_gain && cos && sin && pos && k_cache && v_cache && out && workspace,
+                 "null pointer");
+    VEDA_REQUIRE(heads > 0 && kv_heads > 0 && heads % kv_heads == 0 && heads < (1 << 20), "bad shape");
+    VEDA_REQUIRE(capacity > 0 && capacity < (1ll << 40), "bad cache capacity");
+    VEDA_REQUIRE(ldkv >= kv_heads * head_dim, "bad cache leading dimension");
+    const int64_t g = heads / kv_heads;
+    if (head_dim != kFusedDim || !(g == 1 || g == 2 || g == 4 || g == 8) || ldkv % 8 != 0 ||
+        !aligned16(k_cache) || !aligned16(v_cache))
+    {
+        return fail(VEDA_ERR_UNSUPPORTED, "veda_decode_attention_at: head_dim 128, 1/2/4/8 query heads per "
+                                          "KV head and 16-byte aligned cache rows");
+    }
+    VEDA_REQUIRE(aligned16(workspace) && workspace_bytes >= decode_workspace(heads, kv_heads, capacity),
+                 "workspace smaller than veda_decode_attention_workspace or not 16-byte aligned");
+    const int64_t chunk = decode_chunk(capacity);
+    const dim3 grid(static_cast<unsigned>(kv_heads), static_cast<unsigned>((capacity + chunk - 1) / chunk));
+    auto* counters = static_cast<unsigned*>(workspace);
+    auto* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + (kv_heads * 4 + 255) / 256 * 256);
+#define VEDA_FUSED(T, G, WARPS, U)                                                                        \
+    decode_attn_fused_kernel<T, G, WARPS, U><<<grid, WARPS * 32, 0, stream>>>(                            \
+        static_cast<const T*>(qkv), static_cast<const T*>(q_gain), static_cast<const T*>(k_gain), cos, sin, \
+        pos, static_cast<T*>(k_cache), static_cast<T*>(v_cache), ldkv, static_cast<int>(kv_heads), eps,   \
+        scale, static_cast<T*>(out), capacity, chunk, part, counters)
+#define VEDA_FUSED_G(T)                                                                                   \
+    switch (g)                                                                                             \
+    {                                                                                                      \
+    case 1: VEDA_FUSED(T, 1, 16, 4); break;                                                                \
+    case 2: VEDA_FUSED(T, 2, 16, 4); break;                                                                \
+    case 4: VEDA_FUSED(T, 4, 8, 4); break;                                                                 \
+    default: VEDA_FUSED(T, 8, 8, 2); break;                                                                \
+    }
+    if (dtype == VEDA_BF16)
+    {
+        VEDA_FUSED_G(bf16)
+    }
+    else
+    {
+        VEDA_FUSED_G(float)
+    }
+#undef VEDA_FUSED_G
+#undef VEDA_FUSED
+    count_launch();
+    return check_launch("veda_decode_attention_at");
 }

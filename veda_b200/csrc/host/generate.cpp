@@ -69,7 +69,7 @@ struct Generator::Cache
 // pos the position (int64) of the token being fed.
 struct Generator::DecodeStep
 {
-    Tensor io, pos, x, xs, a, qkv, qr, ctx, o, hb, dn, logits;
+    Tensor io, pos, x, xs, a, qkv, qr, ctx, o, hb, dn, logits, workspace;
     cudaGraphExec_t exec = nullptr;
     cudaStream_t stream = nullptr;
 
@@ -108,6 +108,16 @@ void Generator::record_step(DecodeStep& st, Cache& cache, const Tensor& cosines,
     st.hb = Tensor::empty(Shape({1, F}), dtype);
     st.dn = Tensor::empty(Shape({1, D}), dtype);
     st.logits = Tensor::empty(Shape({V}), dtype);
+    // q/k/v handling and attention in one launch where its kernel takes the shape
+    const bool fused = Dh == 128 && (H / Hk == 1 || H / Hk == 2 || H / Hk == 4 || H / Hk == 8) && KV % 8 == 0 &&
+                       !cache.k.empty();
+    const int64_t capacity = cache.k.empty() ? 0 : static_cast<int64_t>(cache.k[0].shape()[0]);
+    const int64_t ws =
+        fused ? veda_decode_attention_workspace(static_cast<int64_t>(H), static_cast<int64_t>(Hk), capacity) : 0;
+    if (fused)
+    {
+        st.workspace = Tensor(Shape({static_cast<size_t>(ws + 3) / 4}), DType::F32);   // zero-filled
+    }
     cuda_check(cudaStreamSynchronize(cs()), "decode step buffers");
     cuda_check(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking), "decode stream");
     const veda_stream_t caller = current_stream();
@@ -128,45 +138,58 @@ void Generator::record_step(DecodeStep& st, Cache& cache, const Tensor& cosines,
                                  current_stream()),
               "generate: embedding");
         const auto& layers = model_.layers_;
-        const Tensor& first_gain = layers.empty() ? model_.final_norm_.value() : layers[0].in_norm.value();
-        check(veda_rmsnorm_fwd(x->data_ptr(), static_cast<int64_t>(D), first_gain.data_ptr(), st.a.data_ptr(),
-                               static_cast<int64_t>(D), 1, static_cast<int64_t>(D), eps, d, current_stream()),
-              "generate: norm");
+        // Each pre-norm runs inside the projection that follows it; `delta` is the sublayer output
+        // still to be added to the residual x (none before the first layer).
+        const void* delta = nullptr;
+        auto normed_gemv = [&](const Tensor& gain, const Tensor& w, size_t n, void* y, bool swiglu) {
+            void* sum = delta != nullptr ? xs->data_ptr() : nullptr;
+            const int rc = swiglu ? veda_gemv_rmsnorm_swiglu(x->data_ptr(), delta, gain.data_ptr(), eps, sum,
+                                                             w.data_ptr(), static_cast<int64_t>(D), y,
+                                                             static_cast<int64_t>(n), static_cast<int64_t>(D), d,
+                                                             current_stream())
+                                  : veda_gemv_rmsnorm(x->data_ptr(), delta, gain.data_ptr(), eps, sum,
+                                                      w.data_ptr(), static_cast<int64_t>(D), y,
+                                                      static_cast<int64_t>(n), static_cast<int64_t>(D), d,
+                                                      current_stream());
+            check(rc, "generate: norm + projection");
+            if (delta != nullptr) std::swap(x, xs);
+            delta = nullptr;
+        };
         for (size_t l = 0; l < layers.size(); ++l)
         {
             const auto& L = layers[l];
-            gemv(st.a.data_ptr(), L.qkv.value().data_ptr(), D, st.qkv.data_ptr(), W, D, d);
-            check(veda_decode_qkv_at(st.qkv.data_ptr(), L.q_norm.value().data_ptr(), L.k_norm.value().data_ptr(),
-                                     cp, sp, pos, st.qr.data_ptr(), cache.k[l].data_ptr(), cache.v[l].data_ptr(),
-                                     static_cast<int64_t>(KV), static_cast<int64_t>(H), static_cast<int64_t>(Hk),
-                                     static_cast<int64_t>(Dh), eps, d, current_stream()),
-                  "generate: q/k/v");
-            check(veda_attention_decode_at(st.qr.data_ptr(), cache.k[l].data_ptr(), cache.v[l].data_ptr(),
-                                           static_cast<int64_t>(KV), pos, static_cast<int64_t>(H),
-                                           static_cast<int64_t>(Hk), static_cast<int64_t>(Dh), scale,
-                                           st.ctx.data_ptr(), d, current_stream()),
-                  "generate: attention");
+            normed_gemv(L.in_norm.value(), L.qkv.value(), W, st.qkv.data_ptr(), false);
+            if (fused)
+            {
+                check(veda_decode_attention_at(st.qkv.data_ptr(), L.q_norm.value().data_ptr(),
+                                               L.k_norm.value().data_ptr(), cp, sp, pos, cache.k[l].data_ptr(),
+                                               cache.v[l].data_ptr(), static_cast<int64_t>(KV), capacity,
+                                               static_cast<int64_t>(H), static_cast<int64_t>(Hk),
+                                               static_cast<int64_t>(Dh), eps, scale, st.ctx.data_ptr(),
+                                               st.workspace.data_ptr(), ws, d, current_stream()),
+                      "generate: q/k/v + attention");
+            }
+            else
+            {
+                check(veda_decode_qkv_at(st.qkv.data_ptr(), L.q_norm.value().data_ptr(),
+                                         L.k_norm.value().data_ptr(), cp, sp, pos, st.qr.data_ptr(),
+                                         cache.k[l].data_ptr(), cache.v[l].data_ptr(), static_cast<int64_t>(KV),
+                                         static_cast<int64_t>(H), static_cast<int64_t>(Hk),
+                                         static_cast<int64_t>(Dh), eps, d, current_stream()),
+                      "generate: q/k/v");
+                check(veda_attention_decode_at(st.qr.data_ptr(), cache.k[l].data_ptr(), cache.v[l].data_ptr(),
+                                               static_cast<int64_t>(KV), pos, static_cast<int64_t>(H),
+                                               static_cast<int64_t>(Hk), static_cast<int64_t>(Dh), scale,
+                                               st.ctx.data_ptr(), d, current_stream()),
+                      "generate: attention");
+            }
             gemv(st.ctx.data_ptr(), L.o.value().data_ptr(), H * Dh, st.o.data_ptr(), D, H * Dh, d);
-            check(veda_add_rmsnorm_fwd(x->data_ptr(), static_cast<int64_t>(D), st.o.data_ptr(),
-                                       static_cast<int64_t>(D), L.post_norm.value().data_ptr(), xs->data_ptr(),
-                                       static_cast<int64_t>(D), st.a.data_ptr(), static_cast<int64_t>(D), 1,
-                                       static_cast<int64_t>(D), eps, d, current_stream()),
-                  "generate: residual + norm");
-            std::swap(x, xs);
-            check(veda_gemv_swiglu(st.a.data_ptr(), L.gate_up.value().data_ptr(), static_cast<int64_t>(D),
-                                   st.hb.data_ptr(), static_cast<int64_t>(F), static_cast<int64_t>(D), d,
-                                   current_stream()),
-                  "generate: gate/up + swiglu");
+            delta = st.o.data_ptr();
+            normed_gemv(L.post_norm.value(), L.gate_up.value(), F, st.hb.data_ptr(), true);
             gemv(st.hb.data_ptr(), L.down.value().data_ptr(), F, st.dn.data_ptr(), D, F, d);
-            const Tensor& next = l + 1 < layers.size() ? layers[l + 1].in_norm.value() : model_.final_norm_.value();
-            check(veda_add_rmsnorm_fwd(x->data_ptr(), static_cast<int64_t>(D), st.dn.data_ptr(),
-                                       static_cast<int64_t>(D), next.data_ptr(), xs->data_ptr(),
-                                       static_cast<int64_t>(D), st.a.data_ptr(), static_cast<int64_t>(D), 1,
-                                       static_cast<int64_t>(D), eps, d, current_stream()),
-                  "generate: residual + norm");
-            std::swap(x, xs);
+            delta = st.dn.data_ptr();
         }
-        gemv(st.a.data_ptr(), model_.embed_.value().data_ptr(), D, st.logits.data_ptr(), V, D, d);
+        normed_gemv(model_.final_norm_.value(), model_.embed_.value(), V, st.logits.data_ptr(), false);
         check(veda_argmax(st.logits.data_ptr(), static_cast<int64_t>(V), 1, static_cast<int64_t>(V), token, status,
                           d, current_stream()),
               "generate: argmax");
