@@ -313,6 +313,16 @@ int veda_gemv_rmsnorm(const void* x, const void* r, const void* gamma, float eps
 int veda_gemv_rmsnorm_swiglu(const void* x, const void* r, const void* gamma, float eps, void* sum,
                              const void* w_gate_up, int64_t ldw, void* h, int64_t f, int64_t k,
                              int dtype, veda_stream_t stream);
+/* veda_gemv_rmsnorm over the LM head with the greedy choice fused in: *token = argmax of the
+ * rounded outputs y (ties to the lower index; a NaN anywhere: *token = -1 and *status =
+ * VEDA_ERR_INVALID_ARGUMENT, as veda_argmax), merged by the last block to finish through
+ * `workspace` (at least veda_gemv_argmax_workspace(n) bytes, 16-byte aligned, zero before its
+ * first use, left ready for the next call; one call at a time per workspace). */
+int64_t veda_gemv_argmax_workspace(int64_t n);
+int veda_gemv_rmsnorm_argmax(const void* x, const void* r, const void* gamma, float eps, void* sum,
+                             const void* w, int64_t ldw, void* y, int64_t n, int64_t k,
+                             int64_t* token, int* status, void* workspace,
+                             int64_t workspace_bytes, int dtype, veda_stream_t stream);
 /* veda_decode_qkv_at followed by veda_attention_decode_at in one launch (head_dim 128, heads /
  * kv_heads in {1, 2, 4, 8}, 16-byte aligned cache rows, else VEDA_ERR_UNSUPPORTED): the token's
  * QK-norm + RoPE, its key and value written into cache row *pos, and out[h] = attention of query

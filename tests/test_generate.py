@@ -266,3 +266,56 @@ def test_gemv_matches_row_product(dtype, n, k, ldw):
     h2 = torch.empty(n, dtype=tdt, device="cuda")
     call("veda_swiglu_fwd", y.data_ptr(), n, y[n:].data_ptr(), n, h2.data_ptr(), n, 1, n, dt, stream())
     assert torch.equal(h, h2)
+
+
+@pytest.mark.parametrize("dtype,n,k", [(1, 151936, 1024), (1, 3000, 256), (0, 9000, 64)])
+def test_lm_head_gemv_with_greedy_choice(dtype, n, k):
+    """The norm + LM head with the argmax fused in: the logits equal the unfused projection's bit
+    for bit, the token equals veda_argmax over them, ties go to the lower index, a NaN sets the
+    status; the merge workspace is left ready for the next call."""
+    import torch
+    import veda_b200 as V
+    from tests.gpu_util import bf, call, stream
+    r = np.random.default_rng(n)
+    x = r.standard_normal(k).astype(np.float32)
+    dlt = r.standard_normal(k).astype(np.float32)
+    gam = (1 + 0.1 * r.standard_normal(k)).astype(np.float32)
+    w = r.standard_normal((n, k)).astype(np.float32)
+    if dtype == 1:
+        x, dlt, gam, w = bf(x), bf(dlt), bf(gam), bf(w)
+    tdt = torch.float32 if dtype == 0 else torch.bfloat16
+    dt = V.F32 if dtype == 0 else V.BF16
+    dx, dr, dg = (torch.from_numpy(a).to("cuda").to(tdt) for a in (x, dlt, gam))
+    ws = V.lib().veda_gemv_argmax_workspace(n)
+    work = torch.zeros(ws, dtype=torch.uint8, device="cuda")
+
+    def both(wt):
+        y_sep = torch.empty(n, dtype=tdt, device="cuda")
+        call("veda_gemv_rmsnorm", dx.data_ptr(), dr.data_ptr(), dg.data_ptr(), 1e-6, None, wt.data_ptr(), k,
+             y_sep.data_ptr(), n, k, dt, stream())
+        ref = torch.zeros(1, dtype=torch.int64, device="cuda")
+        ref_status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        call("veda_argmax", y_sep.data_ptr(), n, 1, n, ref.data_ptr(), ref_status.data_ptr(), dt, stream())
+        y = torch.empty(n, dtype=tdt, device="cuda")
+        tok = torch.zeros(1, dtype=torch.int64, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        call("veda_gemv_rmsnorm_argmax", dx.data_ptr(), dr.data_ptr(), dg.data_ptr(), 1e-6, None, wt.data_ptr(),
+             k, y.data_ptr(), n, k, tok.data_ptr(), status.data_ptr(), work.data_ptr(), ws, dt, stream())
+        assert torch.allclose(y, y_sep, rtol=0, atol=0, equal_nan=True)   # bit for bit, NaN where NaN
+        return int(tok.item()), int(status.item()), int(ref.item()), y_sep
+
+    dw = torch.from_numpy(w).to("cuda").to(tdt)
+    tok, status, ref, y = both(dw)
+    assert tok == ref and status == 0
+    assert tok == int(np.argmax(y.float().cpu().numpy()))
+    # copies of the winning row further down and further up: the lowest index wins
+    lo, hi = min(5, tok), n - 3
+    dw[5] = dw[tok]
+    dw[hi] = dw[tok]
+    tok2, status2, ref2, _ = both(dw)
+    assert tok2 == ref2 == lo and status2 == 0
+    assert not bool(work[:4].any())
+    # a NaN weight row makes one logit NaN: no token, the status set
+    dw[n // 2] = float("nan")
+    tok3, status3, ref3, _ = both(dw)
+    assert tok3 == -1 and status3 == V.ERR_INVALID_ARGUMENT and ref3 == -1

@@ -94,6 +94,9 @@ SIGNATURES = {
     "veda_gemv_rmsnorm": (_i, [_p, _p, _p, _f, _p, _p, _i64, _p, _i64, _i64, _i, _p]),
     "veda_gemv_rmsnorm_swiglu": (_i, [_p, _p, _p, _f, _p, _p, _i64, _p, _i64, _i64, _i, _p]),
     "veda_decode_attention_workspace": (_i64, [_i64, _i64, _i64]),
+    "veda_gemv_argmax_workspace": (_i64, [_i64]),
+    "veda_gemv_rmsnorm_argmax": (_i, [_p, _p, _p, _f, _p, _p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _i,
+                                      _p]),
     "veda_decode_attention_at": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f, _f,
                                       _p, _p, _i64, _i, _p]),
     "veda_randn": (_i, [_p, _i64, _f, _u64, _i, _p]),

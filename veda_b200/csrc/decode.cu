@@ -313,10 +313,29 @@ __device__ __forceinline__ float silu_gate(float g) { return g * __fdividef(1.0f
 // rounded to the dtype as the residual add stores it, and block 0 writes it to sum_out; the sum of
 // squares runs in the order of the streaming RMSNorm (16-byte pieces, piece lane + 32 c of lane,
 // then across the warp), y = (s / rms) * gamma rounded once.
-template <typename T, int R, bool SWIGLU, bool VEC, bool NORM>
+// PICK: the greedy choice over the outputs as well (argmax of the rounded values, ties to the lower
+// index, a NaN anywhere an error: Sampling.cpp:97-113): each block's best goes to `part`, and the
+// last block to finish (atomic arrival count, no block waits) reduces them into *token.
+struct GemvPick
+{
+    int64_t* token = nullptr;
+    int* status = nullptr;
+    unsigned* counter = nullptr;
+    float* val = nullptr;   // per block
+    int* idx = nullptr;     // per block; -2 marks a NaN
+};
+
+// (v, i) is the better candidate than (bv, bi): larger, or equal with the lower index.
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi)
+{
+    return i >= 0 && (bi < 0 || v > bv || (v == bv && i < bi));
+}
+
+template <typename T, int R, bool SWIGLU, bool VEC, bool NORM, bool PICK = false>
 __global__ void __launch_bounds__(kGemvWarps * 32)
 gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __restrict__ y, int n, int k,
-            const T* __restrict__ r_in, const T* __restrict__ gamma, T* __restrict__ sum_out, float eps)
+            const T* __restrict__ r_in, const T* __restrict__ gamma, T* __restrict__ sum_out, float eps,
+            GemvPick pick = GemvPick{})
 {
     extern __shared__ __align__(16) unsigned char gemv_smem[];
     T* xs = reinterpret_cast<T*>(gemv_smem);
@@ -337,7 +356,7 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
     uint4 wv0[kGemvUnroll][R];
     if constexpr (VEC)
     {
-        if (active)
+        if (active || PICK)   // with PICK an idle warp computes a copy of row n - 1 and drops it
         {
 #pragma unroll
             for (int u = 0; u < kGemvUnroll; ++u)
@@ -394,7 +413,10 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
         for (int i = threadIdx.x; i < k; i += blockDim.x) xs[i] = x[i];
     }
     __syncthreads();
-    if (!active) return;
+    if constexpr (!PICK)
+    {
+        if (!active) return;
+    }
     float acc[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) acc[r] = 0.0f;
@@ -446,6 +468,82 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
     }
 #pragma unroll
     for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]);
+    if constexpr (PICK)
+    {
+        __shared__ float pv_s[kGemvWarps];
+        __shared__ int pi_s[kGemvWarps];
+        __shared__ bool last_s;
+        float best = -INFINITY;
+        int bi = -1;
+        bool nan = false;
+        if (lane == 0 && active)
+        {
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+            {
+                if (base + r < n)
+                {
+                    const T t = from_f32<T>(acc[r]);
+                    y[base + r] = t;
+                    const float v = to_f32(t);
+                    if (v != v) nan = true;
+                    else if (better(v, base + r, best, bi)) { best = v; bi = base + r; }
+                }
+            }
+        }
+        if (lane == 0)
+        {
+            pv_s[warp] = best;
+            pi_s[warp] = bi;
+        }
+        const bool block_nan = __syncthreads_or(nan);
+        if (threadIdx.x == 0)
+        {
+            float b = -INFINITY;
+            int j = -1;
+            for (int q = 0; q < kGemvWarps; ++q)
+                if (better(pv_s[q], pi_s[q], b, j)) { b = pv_s[q]; j = pi_s[q]; }
+            pick.val[blockIdx.x] = b;
+            pick.idx[blockIdx.x] = block_nan ? -2 : j;
+            __threadfence();
+            last_s = atomicAdd(pick.counter, 1u) == gridDim.x - 1;
+        }
+        __syncthreads();
+        if (!last_s) return;
+        __threadfence();
+        float b = -INFINITY;
+        int j = -1;
+        bool bad = false;
+        for (int q = threadIdx.x; q < static_cast<int>(gridDim.x); q += blockDim.x)
+        {
+            const int qi = __ldcg(pick.idx + q);
+            const float qv = __ldcg(pick.val + q);
+            if (qi == -2) bad = true;
+            else if (better(qv, qi, b, j)) { b = qv; j = qi; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+        {
+            const float ov = __shfl_xor_sync(0xFFFFFFFFu, b, o);
+            const int oi = __shfl_xor_sync(0xFFFFFFFFu, j, o);
+            if (better(ov, oi, b, j)) { b = ov; j = oi; }
+        }
+        if (lane == 0)
+        {
+            pv_s[warp] = b;
+            pi_s[warp] = j;
+        }
+        bad = __syncthreads_or(bad);
+        if (threadIdx.x == 0)
+        {
+            for (int q = 1; q < kGemvWarps; ++q)
+                if (better(pv_s[q], pi_s[q], pv_s[0], pi_s[0])) { pv_s[0] = pv_s[q]; pi_s[0] = pi_s[q]; }
+            *pick.token = bad ? -1 : pi_s[0];
+            if (bad && pick.status != nullptr) *pick.status = VEDA_ERR_INVALID_ARGUMENT;
+            *pick.counter = 0u;   // ready for the next call
+        }
+        return;
+    }
     if (lane != 0) return;
     if constexpr (SWIGLU)
     {
@@ -780,6 +878,29 @@ decode_attn_fused_kernel(const T* __restrict__ qkv, const T* __restrict__ qgain,
     if (threadIdx.x == 0) counters[kvh] = 0u;   // ready for the next call
 }
 
+template <typename T, int R>
+void launch_gemv_pick(const void* x, const void* w, int64_t ldw, void* y, int64_t n, int64_t k, bool vec,
+                      const GemvNorm& norm, const GemvPick& pick, cudaStream_t stream)
+{
+    const auto blocks = static_cast<unsigned>((n + kGemvWarps * R - 1) / (kGemvWarps * R));
+    const size_t smem = static_cast<size_t>(k) * sizeof(T);
+    const auto ni = static_cast<int>(n), ki = static_cast<int>(k);
+#define VEDA_GEMV_PICK(V)                                                                               \
+    gemv_kernel<T, R, false, V, true, true><<<blocks, kGemvWarps * 32, smem, stream>>>(                 \
+        static_cast<const T*>(x), static_cast<const T*>(w), ldw, static_cast<T*>(y), ni, ki,            \
+        static_cast<const T*>(norm.r), static_cast<const T*>(norm.gamma), static_cast<T*>(norm.sum),    \
+        norm.eps, pick)
+    if (vec) VEDA_GEMV_PICK(true);
+    else VEDA_GEMV_PICK(false);
+#undef VEDA_GEMV_PICK
+}
+
+int64_t pick_blocks(int64_t n)
+{
+    const int64_t per_block = kGemvWarps * (n >= 8192 ? 2 : 1);
+    return (n + per_block - 1) / per_block;
+}
+
 int gemv_checks(const void* x, const void* w, int64_t ldw, const void* y, int64_t n, int64_t k, int dtype)
 {
     VEDA_REQUIRE(valid_dtype(dtype), "unknown dtype");
@@ -941,4 +1062,42 @@ extern "C" int veda_decode_attention_at(const void* qkv, const void* q_gain, con
 #undef VEDA_FUSED
     count_launch();
     return check_launch("veda_decode_attention_at");
+}
+
+extern "C" int64_t veda_gemv_argmax_workspace(int64_t n)
+{
+    if (n <= 0 || n >= (1ll << 30)) return -1;
+    return 256 + pick_blocks(n) * 8;
+}
+
+extern "C" int veda_gemv_rmsnorm_argmax(const void* x, const void* r, const void* gamma, float eps, void* sum,
+                                        const void* w, int64_t ldw, void* y, int64_t n, int64_t k,
+                                        int64_t* token, int* status, void* workspace, int64_t workspace_bytes,
+                                        int dtype, veda_stream_t stream)
+{
+    if (const int rc = gemv_checks(x, w, ldw, y, n, k, dtype)) return rc;
+    if (const int rc = norm_checks(x, r, gamma, sum)) return rc;
+    VEDA_REQUIRE(token != nullptr && workspace != nullptr, "null pointer");
+    VEDA_REQUIRE(aligned16(workspace) && workspace_bytes >= 256 + pick_blocks(n) * 8,
+                 "workspace smaller than veda_gemv_argmax_workspace or not 16-byte aligned");
+    const GemvNorm norm{r, gamma, sum, eps};
+    GemvPick pick;
+    pick.token = token;
+    pick.status = status;
+    pick.counter = static_cast<unsigned*>(workspace);
+    pick.val = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+    pick.idx = reinterpret_cast<int*>(static_cast<char*>(workspace) + 256 + pick_blocks(n) * 4);
+    const bool vec = gemv_vec(nullptr, w, ldw, k, dtype);
+    if (dtype == VEDA_BF16)
+    {
+        if (n >= 8192) launch_gemv_pick<bf16, 2>(x, w, ldw, y, n, k, vec, norm, pick, stream);
+        else launch_gemv_pick<bf16, 1>(x, w, ldw, y, n, k, vec, norm, pick, stream);
+    }
+    else
+    {
+        if (n >= 8192) launch_gemv_pick<float, 2>(x, w, ldw, y, n, k, vec, norm, pick, stream);
+        else launch_gemv_pick<float, 1>(x, w, ldw, y, n, k, vec, norm, pick, stream);
+    }
+    count_launch();
+    return check_launch("veda_gemv_rmsnorm_argmax");
 }

@@ -69,7 +69,7 @@ struct Generator::Cache
 // pos the position (int64) of the token being fed.
 struct Generator::DecodeStep
 {
-    Tensor io, pos, x, xs, a, qkv, qr, ctx, o, hb, dn, logits, workspace;
+    Tensor io, pos, x, xs, a, qkv, qr, ctx, o, hb, dn, logits, workspace, pick;
     cudaGraphExec_t exec = nullptr;
     cudaStream_t stream = nullptr;
 
@@ -118,6 +118,8 @@ void Generator::record_step(DecodeStep& st, Cache& cache, const Tensor& cosines,
     {
         st.workspace = Tensor(Shape({static_cast<size_t>(ws + 3) / 4}), DType::F32);   // zero-filled
     }
+    const int64_t pick_ws = veda_gemv_argmax_workspace(static_cast<int64_t>(V));
+    st.pick = Tensor(Shape({static_cast<size_t>(pick_ws + 3) / 4}), DType::F32);
     cuda_check(cudaStreamSynchronize(cs()), "decode step buffers");
     cuda_check(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking), "decode stream");
     const veda_stream_t caller = current_stream();
@@ -189,10 +191,12 @@ void Generator::record_step(DecodeStep& st, Cache& cache, const Tensor& cosines,
             gemv(st.hb.data_ptr(), L.down.value().data_ptr(), F, st.dn.data_ptr(), D, F, d);
             delta = st.dn.data_ptr();
         }
-        normed_gemv(model_.final_norm_.value(), model_.embed_.value(), V, st.logits.data_ptr(), false);
-        check(veda_argmax(st.logits.data_ptr(), static_cast<int64_t>(V), 1, static_cast<int64_t>(V), token, status,
-                          d, current_stream()),
-              "generate: argmax");
+        // the final norm, the tied LM head and the greedy choice in one launch
+        check(veda_gemv_rmsnorm_argmax(x->data_ptr(), delta, model_.final_norm_.value().data_ptr(), eps, nullptr,
+                                       model_.embed_.value().data_ptr(), static_cast<int64_t>(D),
+                                       st.logits.data_ptr(), static_cast<int64_t>(V), static_cast<int64_t>(D),
+                                       token, status, st.pick.data_ptr(), pick_ws, d, current_stream()),
+              "generate: norm + LM head + argmax");
         check(veda_decode_advance(static_cast<int64_t*>(st.pos.data_ptr()), current_stream()), "generate: position");
     }
     catch (...)
