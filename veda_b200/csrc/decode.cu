@@ -270,6 +270,7 @@ namespace
 {
 constexpr int kGemvWarps = 8;
 constexpr int kGemvUnroll = 4;
+constexpr int kGemvBlocksPerSm = 4;   // registers capped at 64 a thread
 constexpr int64_t kGemvSmem = 48 * 1024;   // the activation row, staged whole
 
 __device__ __forceinline__ uint4 load_stream16(const void* p)
@@ -331,8 +332,10 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi)
     return i >= 0 && (bi < 0 || v > bv || (v == bv && i < bi));
 }
 
+// Blocks loop over tiles of kGemvWarps * (rows per warp) rows, so a grid of a few blocks per SM
+// pays the activation staging (and the norm) once per block however large n is.
 template <typename T, int R, bool SWIGLU, bool VEC, bool NORM, bool PICK = false>
-__global__ void __launch_bounds__(kGemvWarps * 32)
+__global__ void __launch_bounds__(kGemvWarps * 32, kGemvBlocksPerSm)
 gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __restrict__ y, int n, int k,
             const T* __restrict__ r_in, const T* __restrict__ gamma, T* __restrict__ sum_out, float eps,
             GemvPick pick = GemvPick{})
@@ -342,31 +345,35 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
     constexpr int E = 16 / sizeof(T);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int per_warp = SWIGLU ? 1 : R;
-    const int base = (blockIdx.x * kGemvWarps + warp) * per_warp;
-    const bool active = base < n;
-    const T* rows[R];
+    constexpr int tile_rows = kGemvWarps * per_warp;
+    const int tiles = (n + tile_rows - 1) / tile_rows;
+    auto row_ptrs = [&](int base, const T* (&rows)[R]) {
 #pragma unroll
-    for (int r = 0; r < R; ++r)
-    {
-        const int row = SWIGLU ? base : min(base + r, n - 1);   // a row past n repeats the last one
-        rows[r] = w + (static_cast<int64_t>(row) + (SWIGLU ? static_cast<int64_t>(r) * n : 0)) * ldw;
-    }
-    // The first pieces of the weight rows do not depend on the activation: their loads are issued
-    // before it is staged, so the HBM latency overlaps the staging (and the norm).
+        for (int r = 0; r < R; ++r)
+        {
+            const int row = min(SWIGLU ? base : base + r, n - 1);   // a row past n repeats the last one
+            rows[r] = w + (static_cast<int64_t>(row) + (SWIGLU ? static_cast<int64_t>(r) * n : 0)) * ldw;
+        }
+    };
+    auto load_pieces = [&](const T* const (&rows)[R], int c0, uint4 (&wv)[kGemvUnroll][R]) {
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u)
+        {
+            const int c = c0 + u * 32 * E;
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                if (c < k) wv[u][r] = load_stream16(rows[r] + c);
+        }
+    };
+    // The first pieces of this block's first rows do not depend on the activation: their loads are
+    // issued before it is staged, so the HBM latency overlaps the staging (and the norm). A warp
+    // past n computes a copy of row n - 1 and drops it.
     uint4 wv0[kGemvUnroll][R];
     if constexpr (VEC)
     {
-        if (active || PICK)   // with PICK an idle warp computes a copy of row n - 1 and drops it
-        {
-#pragma unroll
-            for (int u = 0; u < kGemvUnroll; ++u)
-            {
-                const int c = lane * E + u * 32 * E;
-#pragma unroll
-                for (int r = 0; r < R; ++r)
-                    if (c < k) wv0[u][r] = load_stream16(rows[r] + c);
-            }
-        }
+        const T* rows0[R];
+        row_ptrs((blockIdx.x * kGemvWarps + warp) * per_warp, rows0);
+        load_pieces(rows0, lane * E, wv0);
     }
     if constexpr (NORM)
     {
@@ -413,70 +420,62 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
         for (int i = threadIdx.x; i < k; i += blockDim.x) xs[i] = x[i];
     }
     __syncthreads();
-    if constexpr (!PICK)
-    {
-        if (!active) return;
-    }
+
+    float best = -INFINITY;   // PICK: this warp's best output so far, rows in ascending order
+    int best_i = -1;
+    bool nan = false;
     float acc[R];
+    auto consume = [&](const uint4 (&wv)[kGemvUnroll][R], int c0) {
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
-    if constexpr (VEC)
-    {
-        auto consume = [&](const uint4 (&wv)[kGemvUnroll][R], int c0) {
-#pragma unroll
-            for (int u = 0; u < kGemvUnroll; ++u)
-            {
-                const int c = c0 + u * 32 * E;
-                if (c < k)
-                {
-                    float xv[E];
-                    load16(xs + c, xv);
-#pragma unroll
-                    for (int r = 0; r < R; ++r)
-                    {
-                        float wf[E];
-                        unpack16<T>(wv[u][r], wf);
-#pragma unroll
-                        for (int j = 0; j < E; ++j) acc[r] = fmaf(xv[j], wf[j], acc[r]);
-                    }
-                }
-            }
-        };
-        consume(wv0, lane * E);
-        for (int c0 = lane * E + 32 * E * kGemvUnroll; c0 < k; c0 += 32 * E * kGemvUnroll)
+        for (int u = 0; u < kGemvUnroll; ++u)
         {
-            uint4 wv[kGemvUnroll][R];
-#pragma unroll
-            for (int u = 0; u < kGemvUnroll; ++u)
+            const int c = c0 + u * 32 * E;
+            if (c < k)
             {
-                const int c = c0 + u * 32 * E;
+                float xv[E];
+                load16(xs + c, xv);
 #pragma unroll
                 for (int r = 0; r < R; ++r)
-                    if (c < k) wv[u][r] = load_stream16(rows[r] + c);
+                {
+                    float wf[E];
+                    unpack16<T>(wv[u][r], wf);
+#pragma unroll
+                    for (int j = 0; j < E; ++j) acc[r] = fmaf(xv[j], wf[j], acc[r]);
+                }
             }
-            consume(wv, c0);
         }
-    }
-    else
-    {
-        for (int c = lane; c < k; c += 32)
+    };
+    // the pieces of a tile's rows from c0 on (16-byte pieces), or every element (VEC false)
+    auto dot_from = [&](const T* const (&rows)[R], int c0) {
+        if constexpr (VEC)
         {
-            const float xv = to_f32(xs[c]);
-#pragma unroll
-            for (int r = 0; r < R; ++r) acc[r] = fmaf(xv, to_f32(rows[r][c]), acc[r]);
+            for (; c0 < k; c0 += 32 * E * kGemvUnroll)
+            {
+                uint4 wv[kGemvUnroll][R];
+                load_pieces(rows, c0, wv);
+                consume(wv, c0);
+            }
         }
-    }
+        else
+        {
+            for (int c = lane; c < k; c += 32)
+            {
+                const float xv = to_f32(xs[c]);
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]);
-    if constexpr (PICK)
-    {
-        __shared__ float pv_s[kGemvWarps];
-        __shared__ int pi_s[kGemvWarps];
-        __shared__ bool last_s;
-        float best = -INFINITY;
-        int bi = -1;
-        bool nan = false;
-        if (lane == 0 && active)
+                for (int r = 0; r < R; ++r) acc[r] = fmaf(xv, to_f32(rows[r][c]), acc[r]);
+            }
+        }
+    };
+    auto finish = [&](int base) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]);
+        if (lane != 0 || base >= n) return;
+        if constexpr (SWIGLU)
+        {
+            const float g = to_f32(from_f32<T>(acc[0])), u = to_f32(from_f32<T>(acc[1]));
+            y[base] = from_f32<T>(silu_gate(g) * u);
+        }
+        else
         {
 #pragma unroll
             for (int r = 0; r < R; ++r)
@@ -485,16 +484,53 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
                 {
                     const T t = from_f32<T>(acc[r]);
                     y[base + r] = t;
-                    const float v = to_f32(t);
-                    if (v != v) nan = true;
-                    else if (better(v, base + r, best, bi)) { best = v; bi = base + r; }
+                    if constexpr (PICK)
+                    {
+                        const float v = to_f32(t);
+                        if (v != v) nan = true;
+                        else if (better(v, base + r, best, best_i)) { best = v; best_i = base + r; }
+                    }
                 }
             }
         }
+    };
+    {
+        // the block's first tile, its first pieces already loaded
+        const int base = (blockIdx.x * kGemvWarps + warp) * per_warp;
+        const T* rows[R];
+        row_ptrs(base, rows);
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+        if constexpr (VEC)
+        {
+            consume(wv0, lane * E);
+            dot_from(rows, lane * E + 32 * E * kGemvUnroll);
+        }
+        else
+        {
+            dot_from(rows, 0);
+        }
+        finish(base);
+    }
+    for (int tile = blockIdx.x + gridDim.x; tile < tiles; tile += gridDim.x)
+    {
+        const int base = (tile * kGemvWarps + warp) * per_warp;
+        const T* rows[R];
+        row_ptrs(base, rows);
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+        dot_from(rows, lane * E);
+        finish(base);
+    }
+    if constexpr (PICK)
+    {
+        __shared__ float pv_s[kGemvWarps];
+        __shared__ int pi_s[kGemvWarps];
+        __shared__ bool last_s;
         if (lane == 0)
         {
             pv_s[warp] = best;
-            pi_s[warp] = bi;
+            pi_s[warp] = best_i;
         }
         const bool block_nan = __syncthreads_or(nan);
         if (threadIdx.x == 0)
@@ -542,20 +578,15 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
             if (bad && pick.status != nullptr) *pick.status = VEDA_ERR_INVALID_ARGUMENT;
             *pick.counter = 0u;   // ready for the next call
         }
-        return;
     }
-    if (lane != 0) return;
-    if constexpr (SWIGLU)
-    {
-        const float g = to_f32(from_f32<T>(acc[0])), u = to_f32(from_f32<T>(acc[1]));
-        y[base] = from_f32<T>(silu_gate(g) * u);
-    }
-    else
-    {
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-            if (base + r < n) y[base + r] = from_f32<T>(acc[r]);
-    }
+}
+
+// Blocks of a launch over n rows, per_warp rows a warp: one per tile up to kGemvBlocksPerSm per SM
+// (the blocks the kernel's launch bounds keep resident at once), tiles beyond that looped over.
+int64_t gemv_grid(int64_t n, int per_warp)
+{
+    const int64_t tiles = (n + kGemvWarps * per_warp - 1) / (kGemvWarps * per_warp);
+    return std::min<int64_t>(tiles, static_cast<int64_t>(sm_count()) * kGemvBlocksPerSm);
 }
 
 // The pre-norm operands of a NORM launch (all null for a plain one).
@@ -572,7 +603,7 @@ void launch_gemv(const void* x, const void* w, int64_t ldw, void* y, int64_t n, 
                  const GemvNorm* norm, cudaStream_t stream)
 {
     constexpr int per_warp = SWIGLU ? 1 : R;
-    const auto blocks = static_cast<unsigned>((n + kGemvWarps * per_warp - 1) / (kGemvWarps * per_warp));
+    const auto blocks = static_cast<unsigned>(gemv_grid(n, per_warp));
     const size_t smem = static_cast<size_t>(k) * sizeof(T);
     const auto xp = static_cast<const T*>(x);
     const auto wp = static_cast<const T*>(w);
@@ -882,7 +913,7 @@ template <typename T, int R>
 void launch_gemv_pick(const void* x, const void* w, int64_t ldw, void* y, int64_t n, int64_t k, bool vec,
                       const GemvNorm& norm, const GemvPick& pick, cudaStream_t stream)
 {
-    const auto blocks = static_cast<unsigned>((n + kGemvWarps * R - 1) / (kGemvWarps * R));
+    const auto blocks = static_cast<unsigned>(gemv_grid(n, R));
     const size_t smem = static_cast<size_t>(k) * sizeof(T);
     const auto ni = static_cast<int>(n), ki = static_cast<int>(k);
 #define VEDA_GEMV_PICK(V)                                                                               \
@@ -895,11 +926,7 @@ void launch_gemv_pick(const void* x, const void* w, int64_t ldw, void* y, int64_
 #undef VEDA_GEMV_PICK
 }
 
-int64_t pick_blocks(int64_t n)
-{
-    const int64_t per_block = kGemvWarps * (n >= 8192 ? 2 : 1);
-    return (n + per_block - 1) / per_block;
-}
+int64_t pick_blocks(int64_t n) { return gemv_grid(n, n >= 8192 ? 2 : 1); }
 
 int gemv_checks(const void* x, const void* w, int64_t ldw, const void* y, int64_t n, int64_t k, int dtype)
 {
