@@ -240,10 +240,11 @@ def test_gemv_with_rmsnorm_prologue(dtype, k, with_r):
 
 
 @pytest.mark.parametrize("dtype,n,k,ldw", [(0, 37, 24, 24), (1, 1024, 3072, 3072), (1, 9000, 1024, 1032),
-                                          (1, 5, 19, 21), (0, 8200, 96, 100)])
+                                          (1, 5, 19, 21), (0, 8200, 96, 100), (1, 300, 2048, 2048),
+                                          (0, 100, 1536, 1540), (1, 7, 2056, 2056)])
 def test_gemv_matches_row_product(dtype, n, k, ldw):
-    """One activation row through a Linear layer (both rows-per-warp variants, the 16-byte and the
-    element-wise paths) against the float64 product; gate/up + SwiGLU in one pass equals
+    """One activation row through a Linear layer (both rows-per-warp variants, rows split across 1, 2
+    or 4 warps, the 16-byte and the element-wise paths) against the float64 product; gate/up + SwiGLU in one pass equals
     the projection followed by veda_swiglu_fwd bit for bit."""
     import torch
     import veda_b200 as V
@@ -319,3 +320,34 @@ def test_lm_head_gemv_with_greedy_choice(dtype, n, k):
     dw[n // 2] = float("nan")
     tok3, status3, ref3, _ = both(dw)
     assert tok3 == -1 and status3 == V.ERR_INVALID_ARGUMENT and ref3 == -1
+
+
+def test_decode_graph_and_per_launch_decode_agree(tmp_path):
+    """VEDA_DECODE_GRAPH=0 (the decode step's kernels launched one by one, the pre-graph path)
+    generates the same tokens as the replayed graph, in fp32 and bf16."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    script = (
+        "import sys, json, numpy as np\n"
+        "from oracle import veda_oracle as O\n"
+        "from veda_b200.train_abi import Trainer\n"
+        "out = {}\n"
+        "for name, cfg, dtype, seed in [('tiny', O.TINY, 0, 0), ('qwen', O.ModelConfig(vocab=2048, hidden=256, "
+        "intermediate=512, layers=2, heads=4, kv_heads=2, head_dim=128, eps=1e-6, theta=1e6), 1, 3)]:\n"
+        "    params = O.init_params(cfg, seed, bf16=(dtype == 1))\n"
+        "    t = Trainer(cfg, dtype=dtype, batch=1, seq_len=8, seed=1)\n"
+        "    t.set_params(np.concatenate([p.ravel() for p in params]))\n"
+        "    prompt = [int(v) for v in np.random.default_rng(4).integers(0, cfg.vocab, 24)]\n"
+        "    out[name] = t.generate(prompt, 12, cached=True)[0]\n"
+        "    t.close()\n"
+        "print(json.dumps(out))\n")
+    runs = []
+    for flag in ("1", "0"):
+        env = dict(os.environ, VEDA_DECODE_GRAPH=flag)
+        r = subprocess.run([sys.executable, "-c", script], cwd=root, env=env, capture_output=True, text=True,
+                           timeout=600)
+        assert r.returncode == 0, r.stderr[-2000:]
+        runs.append(r.stdout.strip().splitlines()[-1])
+    assert runs[0] == runs[1]

@@ -334,7 +334,10 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi)
 
 // Blocks loop over tiles of kGemvWarps * (rows per warp) rows, so a grid of a few blocks per SM
 // pays the activation staging (and the norm) once per block however large n is.
-template <typename T, int R, bool SWIGLU, bool VEC, bool NORM, bool PICK = false>
+// KS > 1 (16-byte path only): KS consecutive warps share a row group, warp part p taking the
+// 16-byte pieces p, p + KS, ... of each row, their sums added in part order through shared memory;
+// fewer dependent load rounds per row where k is long (o and down projections).
+template <typename T, int R, bool SWIGLU, bool VEC, bool NORM, bool PICK = false, int KS = 1>
 __global__ void __launch_bounds__(kGemvWarps * 32, kGemvBlocksPerSm)
 gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __restrict__ y, int n, int k,
             const T* __restrict__ r_in, const T* __restrict__ gamma, T* __restrict__ sum_out, float eps,
@@ -344,8 +347,11 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
     T* xs = reinterpret_cast<T*>(gemv_smem);
     constexpr int E = 16 / sizeof(T);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    constexpr int per_warp = SWIGLU ? 1 : R;
-    constexpr int tile_rows = kGemvWarps * per_warp;
+    constexpr int per_warp = SWIGLU ? 1 : R;   // output rows of a row group
+    constexpr int groups = kGemvWarps / KS;
+    constexpr int tile_rows = groups * per_warp;
+    const int group = warp / KS, part = warp % KS;
+    constexpr int PSTEP = KS * 32 * E;          // elements from one of a warp's pieces to its next
     const int tiles = (n + tile_rows - 1) / tile_rows;
     auto row_ptrs = [&](int base, const T* (&rows)[R]) {
 #pragma unroll
@@ -359,7 +365,7 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
 #pragma unroll
         for (int u = 0; u < kGemvUnroll; ++u)
         {
-            const int c = c0 + u * 32 * E;
+            const int c = c0 + u * PSTEP;
 #pragma unroll
             for (int r = 0; r < R; ++r)
                 if (c < k) wv[u][r] = load_stream16(rows[r] + c);
@@ -372,8 +378,8 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
     if constexpr (VEC)
     {
         const T* rows0[R];
-        row_ptrs((blockIdx.x * kGemvWarps + warp) * per_warp, rows0);
-        load_pieces(rows0, lane * E, wv0);
+        row_ptrs((blockIdx.x * groups + group) * per_warp, rows0);
+        load_pieces(rows0, lane * E + part * 32 * E, wv0);
     }
     if constexpr (NORM)
     {
@@ -429,7 +435,7 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
 #pragma unroll
         for (int u = 0; u < kGemvUnroll; ++u)
         {
-            const int c = c0 + u * 32 * E;
+            const int c = c0 + u * PSTEP;
             if (c < k)
             {
                 float xv[E];
@@ -449,7 +455,7 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
     auto dot_from = [&](const T* const (&rows)[R], int c0) {
         if constexpr (VEC)
         {
-            for (; c0 < k; c0 += 32 * E * kGemvUnroll)
+            for (; c0 < k; c0 += PSTEP * kGemvUnroll)
             {
                 uint4 wv[kGemvUnroll][R];
                 load_pieces(rows, c0, wv);
@@ -466,9 +472,30 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
             }
         }
     };
+    __shared__ float ks_s[KS > 1 ? kGemvWarps : 1][R];
     auto finish = [&](int base) {
 #pragma unroll
         for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]);
+        if constexpr (KS > 1)
+        {
+            if (lane == 0)
+            {
+#pragma unroll
+                for (int r = 0; r < R; ++r) ks_s[warp][r] = acc[r];
+            }
+            __syncthreads();
+            if (part == 0)
+            {
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                {
+                    acc[r] = ks_s[warp][r];
+                    for (int q = 1; q < KS; ++q) acc[r] += ks_s[warp + q][r];
+                }
+            }
+            __syncthreads();   // ks_s is free for the next tile
+            if (part != 0) return;
+        }
         if (lane != 0 || base >= n) return;
         if constexpr (SWIGLU)
         {
@@ -496,15 +523,15 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
     };
     {
         // the block's first tile, its first pieces already loaded
-        const int base = (blockIdx.x * kGemvWarps + warp) * per_warp;
+        const int base = (blockIdx.x * groups + group) * per_warp;
         const T* rows[R];
         row_ptrs(base, rows);
 #pragma unroll
         for (int r = 0; r < R; ++r) acc[r] = 0.0f;
         if constexpr (VEC)
         {
-            consume(wv0, lane * E);
-            dot_from(rows, lane * E + 32 * E * kGemvUnroll);
+            consume(wv0, lane * E + part * 32 * E);
+            dot_from(rows, lane * E + part * 32 * E + PSTEP * kGemvUnroll);
         }
         else
         {
@@ -514,12 +541,12 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
     }
     for (int tile = blockIdx.x + gridDim.x; tile < tiles; tile += gridDim.x)
     {
-        const int base = (tile * kGemvWarps + warp) * per_warp;
+        const int base = (tile * groups + group) * per_warp;
         const T* rows[R];
         row_ptrs(base, rows);
 #pragma unroll
         for (int r = 0; r < R; ++r) acc[r] = 0.0f;
-        dot_from(rows, lane * E);
+        dot_from(rows, VEC ? lane * E + part * 32 * E : 0);
         finish(base);
     }
     if constexpr (PICK)
@@ -583,10 +610,20 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
 
 // Blocks of a launch over n rows, per_warp rows a warp: one per tile up to kGemvBlocksPerSm per SM
 // (the blocks the kernel's launch bounds keep resident at once), tiles beyond that looped over.
-int64_t gemv_grid(int64_t n, int per_warp)
+int64_t gemv_grid(int64_t n, int per_warp, int ks = 1)
 {
-    const int64_t tiles = (n + kGemvWarps * per_warp - 1) / (kGemvWarps * per_warp);
+    const int64_t tile_rows = static_cast<int64_t>(kGemvWarps / ks) * per_warp;
+    const int64_t tiles = (n + tile_rows - 1) / tile_rows;
     return std::min<int64_t>(tiles, static_cast<int64_t>(sm_count()) * kGemvBlocksPerSm);
+}
+
+// Warps a row group is split across: one per round of kGemvUnroll 16-byte pieces a lane would
+// otherwise load one after another (1024 bf16 or 512 fp32 elements a round), up to 4.
+int gemv_split(int64_t k, int dtype)
+{
+    const int64_t per_round = 32 * kGemvUnroll * (16 / static_cast<int64_t>(dtype_size(dtype)));
+    const int64_t rounds = (k + per_round - 1) / per_round;
+    return rounds >= 3 ? 4 : static_cast<int>(rounds);
 }
 
 // The pre-norm operands of a NORM launch (all null for a plain one).
@@ -603,7 +640,8 @@ void launch_gemv(const void* x, const void* w, int64_t ldw, void* y, int64_t n, 
                  const GemvNorm* norm, cudaStream_t stream)
 {
     constexpr int per_warp = SWIGLU ? 1 : R;
-    const auto blocks = static_cast<unsigned>(gemv_grid(n, per_warp));
+    const int ks = vec ? gemv_split(k, sizeof(T) == 2 ? VEDA_BF16 : VEDA_F32) : 1;
+    const auto blocks = static_cast<unsigned>(gemv_grid(n, per_warp, ks));
     const size_t smem = static_cast<size_t>(k) * sizeof(T);
     const auto xp = static_cast<const T*>(x);
     const auto wp = static_cast<const T*>(w);
@@ -613,19 +651,24 @@ void launch_gemv(const void* x, const void* w, int64_t ldw, void* y, int64_t n, 
     const auto gp = norm ? static_cast<const T*>(norm->gamma) : nullptr;
     const auto sp = norm ? static_cast<T*>(norm->sum) : nullptr;
     const float eps = norm ? norm->eps : 0.0f;
-#define VEDA_GEMV(V, N)                                                                            \
-    gemv_kernel<T, R, SWIGLU, V, N><<<blocks, kGemvWarps * 32, smem, stream>>>(xp, wp, ldw, yp, ni, \
-                                                                              ki, rp, gp, sp, eps)
+#define VEDA_GEMV(V, N, KS)                                                                            \
+    gemv_kernel<T, R, SWIGLU, V, N, false, KS><<<blocks, kGemvWarps * 32, smem, stream>>>(xp, wp, ldw, yp, \
+                                                                                         ni, ki, rp, gp,   \
+                                                                                         sp, eps)
+#define VEDA_GEMV_KS(N)                                                                                \
+    if (!vec) VEDA_GEMV(false, N, 1);                                                                  \
+    else if (ks == 4) VEDA_GEMV(true, N, 4);                                                           \
+    else if (ks == 2) VEDA_GEMV(true, N, 2);                                                           \
+    else VEDA_GEMV(true, N, 1)
     if (norm != nullptr)
     {
-        if (vec) VEDA_GEMV(true, true);
-        else VEDA_GEMV(false, true);
+        VEDA_GEMV_KS(true);
     }
     else
     {
-        if (vec) VEDA_GEMV(true, false);
-        else VEDA_GEMV(false, false);
+        VEDA_GEMV_KS(false);
     }
+#undef VEDA_GEMV_KS
 #undef VEDA_GEMV
 }
 
