@@ -1,8 +1,9 @@
-// Token-by-token generation on the device: the attention of one new query per head against a KV
+// Token-by-token generation on the device. The attention of one new query per head against a KV
 // cache (src/libs/model/ScaledDotProductAttention.cpp:138-191 for one query row): softmax over
 // every cached position (all precede or equal the query, so no mask), weighted sum of the cached
-// values; GQA query head h reads KV head h / (H / Hkv). The greedy choice of the next token is
-// veda_argmax (elementwise.cu).
+// values; GQA query head h reads KV head h / (H / Hkv). Then the kernels of one recorded decode
+// step: one-row GEMVs for the Linear layers (the pre-norm, SwiGLU or the greedy argmax fused in),
+// the token's q/k/v handling fused with a split-position attention, and the position increment.
 #include "common.cuh"
 
 #include <algorithm>
@@ -673,15 +674,16 @@ void launch_gemv(const void* x, const void* w, int64_t ldw, void* y, int64_t n, 
 }
 
 // ---- the decode step's attention, fused with the q/k/v handling of its token ---------------
-// One CTA per KV head and the G = H / Hkv query heads that read it (Dh = 128): warps first take
-// QK-norm + RoPE of those query heads (into shared memory, rounded to the dtype as the projection
-// output would be stored) and of the KV head's new key (into cache row *pos), and copy its value
-// row; then 16 half-warps walk the positions 0..*pos, lane l of a half-warp holding dimensions
-// [8l, 8l + 8), two positions per half-warp loaded before either is used, each keeping an online
+// CTAs (KV head, slice of the positions) serve the G = H / Hkv query heads that read the KV head
+// (Dh = 128). Warps first take QK-norm + RoPE of those query heads (into shared memory, rounded to
+// the dtype as the projection output would be stored); the CTA whose slice holds *pos also
+// normalises and rotates the KV head's new key into cache row *pos and copies its value row. Then
+// the 2 * WARPS half-warps walk the slice's positions, lane l of a half-warp holding dimensions
+// [8l, 8l + 8), U positions per half-warp loaded before any is used, each keeping an online
 // softmax state per query head in fp32; half-warps merge through shuffles, warps through shared
-// memory. Reads every cached key and value once per KV head instead of once per query head.
-// WARPS warps, U positions per half-warp loaded before any is used: 16 and 4 for G <= 2 (128
-// positions in flight per KV head), fewer where G's per-head registers need the room.
+// memory, slices through the workspace (the last CTA of the KV head to finish). Every cached key
+// and value is read once per KV head instead of once per query head. WARPS and U: 16 and 4 for
+// G <= 2 (128 positions in flight per CTA), fewer where G's per-head registers need the room.
 constexpr int kFusedDim = 128;
 
 template <typename T>
