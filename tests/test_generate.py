@@ -323,8 +323,8 @@ def test_lm_head_gemv_with_greedy_choice(dtype, n, k):
 
 
 def test_decode_graph_and_per_launch_decode_agree(tmp_path):
-    """VEDA_DECODE_GRAPH=0 (the decode step's kernels launched one by one, the pre-graph path)
-    generates the same tokens as the replayed graph, in fp32 and bf16."""
+    """VEDA_DECODE_GRAPH=0 (each decode step an eager one-token forward through the prefill's
+    kernels) generates the same tokens as the replayed graph, in fp32 and bf16."""
     import os
     import subprocess
     import sys
