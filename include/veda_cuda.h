@@ -306,7 +306,8 @@ int veda_gemv_swiglu(const void* x, const void* w_gate_up, int64_t ldw, void* h,
                      int64_t k, int dtype, veda_stream_t stream);
 /* veda_gemv_nt / veda_gemv_swiglu on the pre-norm of a residual row (Model.cpp:242-249): the
  * activation is RMSNorm(s) * gamma with s = x + r (r may be NULL: s = x), s rounded to the dtype
- * and written to sum when sum is not NULL (sum must not alias x or r). */
+ * and written to sum when sum is not NULL (sum must not alias x or r); 2 k * element size
+ * <= 48 KB. */
 int veda_gemv_rmsnorm(const void* x, const void* r, const void* gamma, float eps, void* sum,
                       const void* w, int64_t ldw, void* y, int64_t n, int64_t k, int dtype,
                       veda_stream_t stream);

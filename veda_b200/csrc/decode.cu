@@ -385,10 +385,12 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
     if constexpr (NORM)
     {
         __shared__ float inv_s;
+        T* gs = xs + k;   // the gain, staged with the row so its loads overlap the row's
         for (int i = threadIdx.x; i < k; i += blockDim.x)
         {
             float v = to_f32(x[i]);
             if (r_in != nullptr) v += to_f32(r_in[i]);
+            gs[i] = gamma[i];
             const T t = from_f32<T>(v);
             xs[i] = t;
             if (blockIdx.x == 0 && sum_out != nullptr) sum_out[i] = t;
@@ -415,7 +417,7 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
         __syncthreads();
         const float inv = inv_s;
         for (int i = threadIdx.x; i < k; i += blockDim.x)
-            xs[i] = from_f32<T>((to_f32(xs[i]) * inv) * to_f32(gamma[i]));
+            xs[i] = from_f32<T>((to_f32(xs[i]) * inv) * to_f32(gs[i]));
     }
     else if constexpr (VEC)
     {
@@ -643,7 +645,7 @@ void launch_gemv(const void* x, const void* w, int64_t ldw, void* y, int64_t n, 
     constexpr int per_warp = SWIGLU ? 1 : R;
     const int ks = vec ? gemv_split(k, sizeof(T) == 2 ? VEDA_BF16 : VEDA_F32) : 1;
     const auto blocks = static_cast<unsigned>(gemv_grid(n, per_warp, ks));
-    const size_t smem = static_cast<size_t>(k) * sizeof(T);
+    const size_t smem = static_cast<size_t>(k) * sizeof(T) * (norm != nullptr ? 2 : 1);
     const auto xp = static_cast<const T*>(x);
     const auto wp = static_cast<const T*>(w);
     const auto yp = static_cast<T*>(y);
@@ -959,7 +961,7 @@ void launch_gemv_pick(const void* x, const void* w, int64_t ldw, void* y, int64_
                       const GemvNorm& norm, const GemvPick& pick, cudaStream_t stream)
 {
     const auto blocks = static_cast<unsigned>(gemv_grid(n, R));
-    const size_t smem = static_cast<size_t>(k) * sizeof(T);
+    const size_t smem = static_cast<size_t>(k) * sizeof(T) * 2;   // the row and the gain
     const auto ni = static_cast<int>(n), ki = static_cast<int>(k);
 #define VEDA_GEMV_PICK(V)                                                                               \
     gemv_kernel<T, R, false, V, true, true><<<blocks, kGemvWarps * 32, smem, stream>>>(                 \
@@ -1012,9 +1014,11 @@ int gemv_dispatch(const void* x, const void* w, int64_t ldw, void* y, int64_t n,
     return 0;
 }
 
-int norm_checks(const void* x, const void* r, const void* gamma, const void* sum)
+int norm_checks(const void* x, const void* r, const void* gamma, const void* sum, int64_t k, int dtype)
 {
     VEDA_REQUIRE(gamma != nullptr, "null pointer");
+    VEDA_REQUIRE(2 * k * static_cast<int64_t>(dtype_size(dtype)) <= kGemvSmem,
+                 "the activation row and its gain exceed the 48 KB staged in shared memory");
     VEDA_REQUIRE(sum == nullptr || (sum != x && sum != r), "sum must not alias x or r (block 0 writes it "
                                                           "while the others read them)");
     return 0;
@@ -1043,7 +1047,7 @@ extern "C" int veda_gemv_rmsnorm(const void* x, const void* r, const void* gamma
                                  veda_stream_t stream)
 {
     if (const int rc = gemv_checks(x, w, ldw, y, n, k, dtype)) return rc;
-    if (const int rc = norm_checks(x, r, gamma, sum)) return rc;
+    if (const int rc = norm_checks(x, r, gamma, sum, k, dtype)) return rc;
     const GemvNorm norm{r, gamma, sum, eps};
     gemv_dispatch(x, w, ldw, y, n, k, dtype, false, &norm, stream);
     return check_launch("veda_gemv_rmsnorm");
@@ -1054,7 +1058,7 @@ extern "C" int veda_gemv_rmsnorm_swiglu(const void* x, const void* r, const void
                                         int dtype, veda_stream_t stream)
 {
     if (const int rc = gemv_checks(x, w_gate_up, ldw, h, f, k, dtype)) return rc;
-    if (const int rc = norm_checks(x, r, gamma, sum)) return rc;
+    if (const int rc = norm_checks(x, r, gamma, sum, k, dtype)) return rc;
     const GemvNorm norm{r, gamma, sum, eps};
     gemv_dispatch(x, w_gate_up, ldw, h, f, k, dtype, true, &norm, stream);
     return check_launch("veda_gemv_rmsnorm_swiglu");
@@ -1148,7 +1152,7 @@ extern "C" int veda_gemv_rmsnorm_argmax(const void* x, const void* r, const void
                                         int dtype, veda_stream_t stream)
 {
     if (const int rc = gemv_checks(x, w, ldw, y, n, k, dtype)) return rc;
-    if (const int rc = norm_checks(x, r, gamma, sum)) return rc;
+    if (const int rc = norm_checks(x, r, gamma, sum, k, dtype)) return rc;
     VEDA_REQUIRE(token != nullptr && workspace != nullptr, "null pointer");
     VEDA_REQUIRE(aligned16(workspace) && workspace_bytes >= 256 + pick_blocks(n) * 8,
                  "workspace smaller than veda_gemv_argmax_workspace or not 16-byte aligned");
