@@ -766,28 +766,34 @@ decode_attn_fused_kernel(const T* __restrict__ qkv, const T* __restrict__ qgain,
         const bool is_q = item < G;
         const T* src = qkv + static_cast<int64_t>(is_q ? kvh * G + item : heads + kvh) * D;
         const T* gain = is_q ? qgain : kgain;
-        float xv[4], ss = 0.0f;
+        // every load of the item first (row, gain, and the rotation's table row), then the math
+        float xv[4], gv[4], cv[2], sv[2], ss = 0.0f;
 #pragma unroll
         for (int i = 0; i < 4; ++i)
         {
             xv[i] = to_f32(src[lane + 32 * i]);
-            ss += xv[i] * xv[i];
+            gv[i] = to_f32(gain[lane + 32 * i]);
         }
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+        {
+            cv[i] = cosv[p * D + lane + 32 * i];
+            sv[i] = sinv[p * D + lane + 32 * i];
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ss += xv[i] * xv[i];
         ss = warp_sum(ss);
         const float r = sqrtf(ss / static_cast<float>(D) + eps);   // x / r, as RMSNorm divides
         float a[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) a[i] = (xv[i] / r) * to_f32(gain[lane + 32 * i]);
+        for (int i = 0; i < 4; ++i) a[i] = (xv[i] / r) * gv[i];
         // half-split rotation: dimension d < 64 pairs with d + 64 (lane + 32 i with lane + 32 (i + 2))
-        const float* cr = cosv + p * D;
-        const float* sr = sinv + p * D;
         float o[4];
 #pragma unroll
         for (int i = 0; i < 2; ++i)
         {
-            const int d = lane + 32 * i;
-            o[i] = a[i] * cr[d] - a[i + 2] * sr[d];
-            o[i + 2] = a[i + 2] * cr[d] + a[i] * sr[d];
+            o[i] = a[i] * cv[i] - a[i + 2] * sv[i];
+            o[i + 2] = a[i + 2] * cv[i] + a[i] * sv[i];
         }
         if (is_q)
         {
@@ -1066,12 +1072,12 @@ extern "C" int veda_gemv_rmsnorm_swiglu(const void* x, const void* r, const void
 
 namespace
 {
-// Positions per CTA slice for a cache of `capacity` rows: 64, or more so that at most 64 slices
-// cover it.
+// Positions per CTA slice for a cache of `capacity` rows: 128 (one round of loads for 16 warps),
+// or more so that at most 64 slices cover it.
 int64_t decode_chunk(int64_t capacity)
 {
     const int64_t c = (capacity + 63) / 64;
-    return std::max<int64_t>(64, (c + 63) / 64 * 64);
+    return std::max<int64_t>(128, (c + 63) / 64 * 64);
 }
 
 int64_t decode_workspace(int64_t heads, int64_t kv_heads, int64_t capacity)
