@@ -1072,10 +1072,12 @@ extern "C" int veda_gemv_rmsnorm_swiglu(const void* x, const void* r, const void
 
 namespace
 {
-// Positions per CTA slice for a cache of `capacity` rows: 128 (one round of loads for 16 warps),
-// or more so that at most 64 slices cover it.
+// Positions per CTA slice for a cache of `capacity` rows: the whole cache up to 256 rows (two
+// rounds of loads for 16 warps cost less than merging slices), else 128 (one round), or more so
+// that at most 64 slices cover it.
 int64_t decode_chunk(int64_t capacity)
 {
+    if (capacity <= 256) return 256;
     const int64_t c = (capacity + 63) / 64;
     return std::max<int64_t>(128, (c + 63) / 64 * 64);
 }
