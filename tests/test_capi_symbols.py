@@ -53,3 +53,24 @@ def test_argument_errors_without_a_gpu():
     rc = lib.veda_attention_fwd(None, 64, None, 32, None, 32, None, 64, None, 1, 4, 3, 2, 16,
                                 0.25, 1, 0, None)
     assert rc == V.ERR_INVALID_ARGUMENT and "multiple" in lib.veda_last_error().decode()
+
+
+def test_decode_workspace_sizes_and_argument_errors_without_a_gpu():
+    # the decode step's workspace sizes are host arithmetic: one 256-position slice (no merge) up to
+    # 256 cache rows, 128-position slices beyond, at most 64 slices; counters padded to 256 bytes
+    lib = V.lib()
+    per_slice = lambda heads, kv: kv * (heads // kv) * 130 * 4
+    assert lib.veda_decode_attention_workspace(16, 8, 200) == 256 + 1 * per_slice(16, 8)
+    assert lib.veda_decode_attention_workspace(16, 8, 256) == 256 + 1 * per_slice(16, 8)
+    assert lib.veda_decode_attention_workspace(16, 8, 257) == 256 + 3 * per_slice(16, 8)
+    assert lib.veda_decode_attention_workspace(32, 4, 1000) == 256 + 8 * per_slice(32, 4)
+    big = lib.veda_decode_attention_workspace(16, 8, 100000)
+    assert big <= 256 + 64 * per_slice(16, 8)
+    assert lib.veda_decode_attention_workspace(16, 6, 100) == -1      # heads not a multiple
+    assert lib.veda_decode_attention_workspace(16, 8, 0) == -1
+    # the GEMV entries check their arguments before any launch
+    rc = lib.veda_gemv_nt(None, None, 8, None, 4, 8, 1, None)
+    assert rc == V.ERR_INVALID_ARGUMENT and "null" in lib.veda_last_error().decode()
+    # a 16000-element bf16 row fits the staged 48 KB alone, not together with its gain
+    rc = lib.veda_gemv_rmsnorm(8, None, 8, 1e-6, None, 8, 16000, 8, 4, 16000, 1, None)
+    assert rc == V.ERR_INVALID_ARGUMENT and "gain exceed" in lib.veda_last_error().decode()
