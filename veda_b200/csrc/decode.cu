@@ -313,8 +313,7 @@ __device__ __forceinline__ float silu_gate(float g) { return g * __fdividef(1.0f
 // NORM: the activation is RMSNorm(s) * gamma of the residual row s = x (+ r), computed by every
 // block into its shared copy (the pre-norm of Model.cpp:242-249 ahead of its Linear layer): s is
 // rounded to the dtype as the residual add stores it, and block 0 writes it to sum_out; the sum of
-// squares runs in the order of the streaming RMSNorm (16-byte pieces, piece lane + 32 c of lane,
-// then across the warp), y = (s / rms) * gamma rounded once.
+// squares is taken by all threads in a fixed order, y = (s / rms) * gamma rounded once.
 // PICK: the greedy choice over the outputs as well (argmax of the rounded values, ties to the lower
 // index, a NaN anywhere an error: Sampling.cpp:97-113): each block's best goes to `part`, and the
 // last block to finish (atomic arrival count, no block waits) reduces them into *token.
@@ -385,7 +384,11 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
     if constexpr (NORM)
     {
         __shared__ float inv_s;
+        __shared__ float ss_s[kGemvWarps];
         T* gs = xs + k;   // the gain, staged with the row so its loads overlap the row's
+        // sum of squares: each thread over the elements it stages, then across the warp, then the
+        // warps in order (fixed, so every block computes the same value)
+        float ss = 0.0f;
         for (int i = threadIdx.x; i < k; i += blockDim.x)
         {
             float v = to_f32(x[i]);
@@ -394,25 +397,17 @@ gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t ldw, T* __
             const T t = from_f32<T>(v);
             xs[i] = t;
             if (blockIdx.x == 0 && sum_out != nullptr) sum_out[i] = t;
+            const float tv = to_f32(t);
+            ss += tv * tv;
         }
+        ss = warp_sum(ss);
+        if (lane == 0) ss_s[warp] = ss;
         __syncthreads();
-        if (warp == 0)
+        if (threadIdx.x == 0)
         {
-            float ss = 0.0f;
-            for (int i = lane * E; i < k; i += 32 * E)
-            {
-#pragma unroll
-                for (int j = 0; j < E; ++j)
-                {
-                    if (i + j < k)
-                    {
-                        const float v = to_f32(xs[i + j]);
-                        ss += v * v;
-                    }
-                }
-            }
-            ss = warp_sum(ss);
-            if (lane == 0) inv_s = 1.0f / sqrtf(ss / static_cast<float>(k) + eps);
+            float total = 0.0f;
+            for (int q = 0; q < kGemvWarps; ++q) total += ss_s[q];
+            inv_s = 1.0f / sqrtf(total / static_cast<float>(k) + eps);
         }
         __syncthreads();
         const float inv = inv_s;
