@@ -53,7 +53,9 @@ uint64_t veda_launch_count(void);
  * kernels adds the graph's kernel count per replay. */
 int veda_launch_count_add(int64_t n);
 /* The current device's status word: 0, or VEDA_ERR_TIMEOUT if a kernel's bounded device-side
- * wait gave up since the last reset. Synchronises with the device; reset = 1 clears it. */
+ * wait gave up since the last reset. Synchronises with the device; reset = 1 clears it. The word
+ * is a device variable compiled into the library (one per GPU, never allocated); its address is
+ * looked up once per device and cached, so after a cudaDeviceReset use a fresh process. */
 int veda_kernel_status(int reset);
 /* Number of SMs the persistent kernels (tensor-core GEMMs, streaming RMSNorm) leave free for
  * work running beside them, such as NCCL all-reduce blocks during a data-parallel backward;
@@ -121,7 +123,8 @@ size_t veda_rmsnorm_bwd_workspace(int64_t rows, int64_t n);
  * scratch needed, veda_rmsnorm_bwd_workspace(rows, n) bytes, must be at most 4 MiB (rows of up
  * to 3542 elements on a 148-SM B200); larger sizes are rejected with VEDA_ERR_INVALID_ARGUMENT.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress); make
- * that first call before any stream capture. All calls share the one array, so calls that
+ * that first call before any stream capture. The address is cached per device for the life of
+ * the process, so after a cudaDeviceReset use a fresh process. All calls share the one array, so calls that
  * overlap on the GPU (on different streams without ordering) race; calls ordered on one stream
  * do not (each call overwrites the partials it reads). Allocates nothing. */
 int veda_rmsnorm_bwd_noalloc(const void* x, int64_t ldx, const void* gamma, const void* dy,

@@ -55,6 +55,84 @@ def test_noalloc_matches_workspace_entry_point_twice(dtype, rows, n):
     assert rel(host(dg), dg_o) <= (1e-4 if dtype == V.F32 else 1e-3)
 
 
+# The bf16 path is the streaming kernel, whose bounded waits report through the device status
+# word. Runs in a fresh process with no torch: the library and the CUDA runtime only (ctypes), every
+# module loaded when the context is created (CUDA_MODULE_LOADING=EAGER), inputs allocated before
+# the first measurement. Between the two cudaMemGetInfo readings the process makes its FIRST call
+# of the entry point (and so the first lookups of the scratch array and of the device status word
+# on this device); a cudaMalloc anywhere on that path would take at least one 2 MiB page.
+_FIRST_CALL = r"""
+import ctypes as C, json, sys
+import numpy as np
+lib = C.CDLL(sys.argv[1])
+rt = C.CDLL("libcudart.so.12")
+rows, n = int(sys.argv[2]), int(sys.argv[3])
+assert rt.cudaSetDevice(0) == 0 and rt.cudaFree(None) == 0
+def dalloc(nbytes):
+    p = C.c_void_p()
+    assert rt.cudaMalloc(C.byref(p), C.c_size_t(nbytes)) == 0
+    return p
+def put(p, a):
+    a = np.ascontiguousarray(a)
+    assert rt.cudaMemcpy(p, a.ctypes.data_as(C.c_void_p), C.c_size_t(a.nbytes), 1) == 0
+def get(p, a):
+    assert rt.cudaMemcpy(a.ctypes.data_as(C.c_void_p), p, C.c_size_t(a.nbytes), 2) == 0
+    return a
+def to_bf16(a):   # round to nearest even, as the device copies in the other tests
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+r = np.random.default_rng(7)
+x = to_bf16(r.standard_normal((rows, n)))
+gam = to_bf16(1 + 0.1 * r.standard_normal(n))
+dy = to_bf16(r.standard_normal((rows, n)))
+px, pg, pdy, pdx, pdg = (dalloc(x.nbytes), dalloc(gam.nbytes), dalloc(dy.nbytes),
+                         dalloc(x.nbytes), dalloc(4 * n))
+put(px, x); put(pg, gam); put(pdy, dy); put(pdg, np.zeros(n, np.float32))
+assert rt.cudaDeviceSynchronize() == 0
+free0, total = C.c_size_t(), C.c_size_t()
+free1 = C.c_size_t()
+assert rt.cudaMemGetInfo(C.byref(free0), C.byref(total)) == 0
+f = lib.veda_rmsnorm_bwd_noalloc
+f.restype = C.c_int
+f.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
+              C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_int64, C.c_float, C.c_int,
+              C.c_void_p]
+rc = f(px, n, pg, pdy, n, None, n, pdx, n, pdg, rows, n, 1e-6, 1, None)   # bf16
+sync_rc = rt.cudaDeviceSynchronize()
+assert rt.cudaMemGetInfo(C.byref(free1), C.byref(total)) == 0
+status = lib.veda_kernel_status(0)
+dx = (get(pdx, np.empty((rows, n), np.uint16)).astype(np.uint32) << 16).view(np.float32)
+dg = get(pdg, np.empty(n, np.float32))
+np.save(sys.argv[4] + "/dx.npy", dx)
+np.save(sys.argv[4] + "/dg.npy", dg)
+print(json.dumps({"rc": rc, "sync": sync_rc, "status": status, "free_before": free0.value,
+                  "free_after": free1.value}))
+"""
+
+
+def test_noalloc_first_call_in_a_fresh_process_allocates_nothing(tmp_path):
+    import json
+    import os
+    import subprocess
+    import sys
+    rows, n = 1024, 1024
+    env = dict(os.environ, CUDA_MODULE_LOADING="EAGER")
+    out = subprocess.run([sys.executable, "-c", _FIRST_CALL, str(V.CUDA_LIB_PATH), str(rows),
+                          str(n), str(tmp_path)], env=env, capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr
+    res = json.loads(out.stdout.strip().splitlines()[-1])
+    assert res["rc"] == 0 and res["sync"] == 0 and res["status"] == 0, res
+    assert res["free_after"] == res["free_before"], res
+    r = np.random.default_rng(7)
+    x = bf(r.standard_normal((rows, n)))
+    gam = bf(1 + 0.1 * r.standard_normal(n))
+    dy = bf(r.standard_normal((rows, n)))
+    dx_o, dg_o = O.rms_norm_gamma_backward(x, gam, dy, 1e-6)
+    assert rel(np.load(tmp_path / "dx.npy"), dx_o) <= TOL[V.BF16]
+    assert rel(np.load(tmp_path / "dg.npy"), dg_o) <= 1e-3
+
+
 def test_noalloc_rejects_rows_beyond_its_scratch():
     lib = V.lib()
     rows, n = 8192, 8192   # needs 2 x SMs x 8192 floats of scratch: above the fixed 4 MiB

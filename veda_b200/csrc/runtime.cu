@@ -65,8 +65,18 @@ int compute_sms()
 
 const char* last_error_cstr() { return g_last_error.c_str(); }
 
-// One int per device, allocated on first use: kernels whose bounded waits give up write
-// VEDA_ERR_TIMEOUT here instead of spinning forever.
+namespace
+{
+// The status word itself: a file-scope device variable, so every GPU that loads the library has
+// its own copy, zero when the module loads, and no call ever allocates it.
+__device__ int g_device_status;
+} // namespace
+
+// Device address of the current device's status word: kernels whose bounded waits give up write
+// VEDA_ERR_TIMEOUT there instead of spinning forever. The address is looked up with
+// cudaGetSymbolAddress while the device is current (host code cannot use the variable's name as
+// a device pointer) and cached per device for the life of the process; a context destroyed by
+// cudaDeviceReset leaves the cached address stale, so a reset needs a fresh process.
 int* device_status_ptr()
 {
     static int* ptrs[64] = {nullptr};
@@ -79,11 +89,10 @@ int* device_status_ptr()
     std::lock_guard<std::mutex> lock(mu);
     if (ptrs[device] == nullptr)
     {
-        int* p = nullptr;
-        if (cudaMalloc(&p, sizeof(int)) == cudaSuccess)
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_status) == cudaSuccess)
         {
-            cudaMemset(p, 0, sizeof(int));
-            ptrs[device] = p;
+            ptrs[device] = static_cast<int*>(p);
         }
     }
     return ptrs[device];
