@@ -371,7 +371,10 @@ int veda_attention_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, c
                        float scale, int causal, int dtype, veda_stream_t stream);
 /* Recomputes P from lse; dq, dk, dv written (not accumulated) in dtype; dk/dv are summed over
  * the H/Hkv query heads of each group (the unbroadcast of the KV expansion).
- * workspace: veda_attention_bwd_workspace() bytes. */
+ * workspace: veda_attention_bwd_workspace() bytes, sized for the mode set when it is asked
+ * (bf16, head_dim 128: O(B*T*H*head_dim) fp32 for the fused kernel, O(B*H*T^2) bf16 in the
+ * deterministic mode). The reference's backward of the composition is
+ * src/libs/autograd/NonLinear.cpp:89-151 (softmax) with Variable.cpp:300-346 (the products). */
 int veda_attention_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
                        int64_t ldv, const void* o, int64_t ldo, const void* dout, int64_t lddo,
                        const float* lse, void* dq, int64_t lddq, void* dk, int64_t lddk, void* dv,
@@ -380,6 +383,12 @@ int veda_attention_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, c
                        float scale, int causal, int dtype, veda_stream_t stream);
 size_t veda_attention_bwd_workspace(int64_t batch, int64_t seq_len, int64_t heads,
                                     int64_t kv_heads, int64_t head_dim, int dtype);
+/* on = 1: the bf16 backward runs its two-kernel form, whose dQ is bit-reproducible run to run
+ * (dS^T through HBM, O(B*H*T^2) workspace); on = 0 (the default; VEDA_ATTENTION_DETERMINISTIC=1
+ * in the environment starts at 1): the fused kernel, whose dQ sums key tiles in a varying order.
+ * Process-wide; returns the previous setting. No counterpart in the reference (its CPU backward
+ * is sequential). */
+int veda_attention_set_deterministic(int on);
 
 #ifdef __cplusplus
 }

@@ -513,6 +513,74 @@ def test_attention(dtype, B, T, H, Hk, Dh):
     assert rel(dv, dv_ref) <= tol
 
 
+@pytest.fixture
+def deterministic_attention():
+    """Runs a test with the two-kernel (bit-reproducible) attention backward, then restores."""
+    prev = V.lib().veda_attention_set_deterministic(1)
+    yield
+    V.lib().veda_attention_set_deterministic(prev)
+
+
+@pytest.mark.parametrize("B,T,H,Hk", [(2, 256, 16, 8), (1, 200, 4, 2)])
+def test_attention_deterministic_mode(deterministic_attention, B, T, H, Hk):
+    o, o_ref, lse, lse_ref, dq, dq_ref, dk, dk_ref, dv, dv_ref = _attention_case(
+        V.BF16, B, T, H, Hk, 128, T + 7)
+    for got, want in ((dq, dq_ref), (dk, dk_ref), (dv, dv_ref)):
+        assert rel(got, want) <= TOL[V.BF16]
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_attention_bwd_t1024_h16_against_oracle(mode):
+    """Attention backward at T 1024 with 16 query heads over 8 KV heads, head_dim 128 (one batch
+    row of the isolated attention-backward config): dQ, dK and dV against the oracle, for the
+    fused kernel (mode 0) and the two-kernel path (mode 1). Reference: the softmax backward of
+    src/libs/autograd/NonLinear.cpp:123-133 inside the composition of src/libs/train/Model.cpp:182-189."""
+    prev = V.lib().veda_attention_set_deterministic(mode)
+    try:
+        _, _, _, _, dq, dq_ref, dk, dk_ref, dv, dv_ref = _attention_case(V.BF16, 1, 1024, 16, 8, 128, 2)
+    finally:
+        V.lib().veda_attention_set_deterministic(prev)
+    assert rel(dq, dq_ref) <= TOL[V.BF16]
+    assert rel(dk, dk_ref) <= TOL[V.BF16]
+    assert rel(dv, dv_ref) <= TOL[V.BF16]
+
+
+@pytest.mark.parametrize("B,T", [(8, 1024), (2, 4096)])
+def test_attention_fused_equals_deterministic(B, T):
+    """The fused backward against the two-kernel one on the same inputs at the isolated config's
+    sizes (B 8 x T 1024, and T 4096): dK and dV come from the same products in the same order, so
+    they are bit-identical; dQ differs only in the order key tiles are summed in fp32."""
+    H, Hk, Dh = 16, 8, 128
+    r = rng(2)
+    tok = (B * T, H * Dh)
+    q, do = bf(r.standard_normal(tok)), bf(r.standard_normal(tok))
+    k, v = bf(r.standard_normal((B * T, Hk * Dh))), bf(r.standard_normal((B * T, Hk * Dh)))
+    qd, kd, vd, dod = dev(q, V.BF16), dev(k, V.BF16), dev(v, V.BF16), dev(do, V.BF16)
+    o, lse = empty(tok, V.BF16), empty(B * H * T)
+    scale = 1.0 / math.sqrt(Dh)
+    call("veda_attention_fwd", ptr(qd), H * Dh, ptr(kd), Hk * Dh, ptr(vd), Hk * Dh, ptr(o), H * Dh,
+         ptr(lse), B, T, H, Hk, Dh, scale, 1, V.BF16, stream())
+    out = []
+    for mode in (0, 1):
+        prev = V.lib().veda_attention_set_deterministic(mode)
+        try:
+            dq, dk, dv = empty(tok, V.BF16), empty((B * T, Hk * Dh), V.BF16), empty((B * T, Hk * Dh), V.BF16)
+            ws = workspace(V.lib().veda_attention_bwd_workspace(B, T, H, Hk, Dh, V.BF16))
+            call("veda_attention_bwd", ptr(qd), H * Dh, ptr(kd), Hk * Dh, ptr(vd), Hk * Dh, ptr(o),
+                 H * Dh, ptr(dod), H * Dh, ptr(lse), ptr(dq), H * Dh, ptr(dk), Hk * Dh, ptr(dv),
+                 Hk * Dh, ptr(ws), ws.numel(), B, T, H, Hk, Dh, scale, 1, V.BF16, stream())
+            sync()
+            out.append((host(dq), host(dk), host(dv)))
+            del ws
+        finally:
+            V.lib().veda_attention_set_deterministic(prev)
+    (dq0, dk0, dv0), (dq1, dk1, dv1) = out
+    assert np.array_equal(dk0, dk1)
+    assert np.array_equal(dv0, dv1)
+    assert np.isfinite(dq0).all()
+    assert rel(dq0, dq1) <= 1e-2
+
+
 def test_attention_golden():
     from pathlib import Path
     ops = np.load(Path(__file__).parent / "golden" / "ops_small.npz")

@@ -108,6 +108,7 @@ SIGNATURES = {
                                 _p, _i64, _p, _i64, _p, _sz, _i64, _i64, _i64, _i64, _i64, _f,
                                 _i, _i, _p]),
     "veda_attention_bwd_workspace": (_sz, [_i64, _i64, _i64, _i64, _i64, _i]),
+    "veda_attention_set_deterministic": (_i, [_i]),
 }
 
 _cuda = None

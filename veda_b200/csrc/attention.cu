@@ -8,10 +8,12 @@
 // sum_j dP_ij P_ij = dO_i . O_i.
 //
 // Two implementations sit behind the entry points:
-//   * attention_flash.cu — bf16, head_dim 128: tiled flash kernels on the tensor cores;
+//   * attention_tc.cu — bf16, head_dim 128: tcgen05 / TMEM kernels (forward; fused backward, or
+//     the bit-reproducible two-kernel backward under veda_attention_set_deterministic(1));
 //   * this file — any dtype and head_dim <= 256: one warp per query (forward, dQ) or per key
 //     (dK, dV), fp32 accumulation, keys visited in ascending order. It is the fp32 path used for
-//     fp32 parity and the fallback for shapes the tiled kernels do not cover.
+//     fp32 parity and serves bf16 shapes the tensor maps cannot describe (sequence lengths that
+//     are not a multiple of 8, operands not 16-byte aligned).
 #include "attention.cuh"
 
 #include <algorithm>
@@ -257,19 +259,14 @@ using namespace veda::cuda;
 extern "C" size_t veda_attention_bwd_workspace(int64_t batch, int64_t seq_len, int64_t heads,
                                                int64_t kv_heads, int64_t head_dim, int dtype)
 {
-    // D = rowsum(dO * O) [B, H, T] fp32, plus what the tiled kernels keep between launches: the
-    // fp32 dQ accumulator (mma.sync) or dS^T (tcgen05); sized for either, since the tcgen05 path
-    // falls back to the mma.sync one for shapes its tensor maps cannot describe.
+    // D = rowsum(dO * O) [B, H, T] fp32, plus what the tensor-core backward keeps between its
+    // launches: the fused path's fp32 dQ accumulator, or the deterministic path's dS^T.
+    (void)kv_heads;
     size_t bytes = (static_cast<size_t>(batch * heads * seq_len) * sizeof(float) + 255) &
                    ~static_cast<size_t>(255);
-    if (flash_supported(head_dim, dtype))
+    if (tc_supported(head_dim, dtype))
     {
-        size_t extra = flash_bwd_extra_workspace(batch, seq_len, heads, kv_heads, head_dim);
-        if (attention_tc_enabled())
-        {
-            extra = std::max(extra, tc_bwd_extra_workspace(batch, seq_len, heads));
-        }
-        bytes += extra;
+        bytes += tc_bwd_extra_workspace(batch, seq_len, heads);
     }
     return (bytes + 255) & ~static_cast<size_t>(255);
 }
@@ -284,20 +281,14 @@ extern "C" int veda_attention_fwd(const void* q, int64_t ldq, const void* k, int
     if (rc != VEDA_OK) return rc;
     if (batch == 0 || seq_len == 0) return VEDA_OK;
     VEDA_REQUIRE(q && k && v && o && lse, "null pointer");
-    if (flash_supported(head_dim, dtype) &&
-        flash_aligned(q, ldq, k, ldk, v, ldv, o, ldo))
+    if (tc_supported(head_dim, dtype) && tc_aligned(q, ldq, k, ldk, v, ldv, o, ldo))
     {
-        if (attention_tc_enabled())
+        const int rc2 = attn_tc_fwd(q, ldq, k, ldk, v, ldv, o, ldo, lse, batch, seq_len, heads,
+                                    kv_heads, scale, causal, stream);
+        if (rc2 != -1)
         {
-            const int rc2 = attn_tc_fwd(q, ldq, k, ldk, v, ldv, o, ldo, lse, batch, seq_len, heads,
-                                        kv_heads, scale, causal, stream);
-            if (rc2 != -1)
-            {
-                return rc2;
-            }
+            return rc2;
         }
-        return flash_fwd(q, ldq, k, ldk, v, ldv, o, ldo, lse, batch, seq_len, heads, kv_heads,
-                         scale, causal, stream);
     }
     AttnShape s{batch, seq_len, heads, kv_heads, head_dim, ldq, ldk, ldv, ldo, scale, causal};
     const unsigned grid = grid_for(batch * heads * seq_len * 32, 256);
@@ -334,24 +325,18 @@ extern "C" int veda_attention_bwd(const void* q, int64_t ldq, const void* k, int
                                                                      kv_heads, head_dim, dtype),
                  "workspace too small (see veda_attention_bwd_workspace)");
     float* dvec = static_cast<float*>(workspace);
-    if (flash_supported(head_dim, dtype) && flash_aligned(q, ldq, k, ldk, v, ldv, o, ldo) &&
-        flash_aligned(dout, lddo, dq, lddq, dk, lddk, dv, lddv))
+    if (tc_supported(head_dim, dtype) && tc_aligned(q, ldq, k, ldk, v, ldv, o, ldo) &&
+        tc_aligned(dout, lddo, dq, lddq, dk, lddk, dv, lddv))
     {
         char* extra = static_cast<char*>(workspace) +
                       ((static_cast<size_t>(batch * heads * seq_len) * sizeof(float) + 255) & ~static_cast<size_t>(255));
-        if (attention_tc_enabled())
+        const int rc2 = attn_tc_bwd(q, ldq, k, ldk, v, ldv, o, ldo, dout, lddo, lse, dq, lddq, dk,
+                                    lddk, dv, lddv, dvec, extra, batch, seq_len, heads, kv_heads,
+                                    scale, causal, stream);
+        if (rc2 != -1)
         {
-            const int rc2 = attn_tc_bwd(q, ldq, k, ldk, v, ldv, o, ldo, dout, lddo, lse, dq, lddq,
-                                        dk, lddk, dv, lddv, dvec, extra, batch, seq_len, heads,
-                                        kv_heads, scale, causal, stream);
-            if (rc2 != -1)
-            {
-                return rc2;
-            }
+            return rc2;
         }
-        return flash_bwd(q, ldq, k, ldk, v, ldv, o, ldo, dout, lddo, lse, dq, lddq, dk, lddk, dv,
-                         lddv, dvec, extra, batch, seq_len, heads, kv_heads, scale, causal,
-                         stream);
     }
     AttnShape s{batch, seq_len, heads, kv_heads, head_dim, ldq, ldk, ldv, ldo, scale, causal};
     const unsigned gq = grid_for(batch * heads * seq_len * 32, 256);
@@ -383,4 +368,9 @@ extern "C" int veda_attention_bwd(const void* q, int64_t ldq, const void* k, int
     }
     count_launch(3);
     return check_launch("veda_attention_bwd");
+}
+
+extern "C" int veda_attention_set_deterministic(int on)
+{
+    return veda::cuda::g_attn_deterministic.exchange(on ? 1 : 0);
 }

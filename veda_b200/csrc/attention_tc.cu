@@ -23,6 +23,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 
@@ -781,6 +782,467 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Fused backward (the default): the four products of attn_bwd_tc_kernel plus the query gradient
+// in one kernel, so dS^T never leaves the SM and the workspace is O(B H T). One CTA per (batch,
+// KV head, 128-key tile), 14 warps:
+//   warp 0       TMA: K and V once, then Q, dO (64 x 128 each) with the tile's -LSE log2(e) and D
+//                into a 3-stage ring;
+//   warp 1       MMA, per 64-query tile i:  S^T = K Q^T and dP^T = V dO^T (M128 keys, N64
+//                queries, K128 dims) into one of two TMEM buffer pairs; then, for tile i-1,
+//                dV += P^T dO and dK += dS^T Q (A read from TMEM) and dQ^T = K^T dS^T (M128 dims,
+//                N64 queries, K128 keys; the K tile and the staged dS^T tile read as MN-major
+//                operands) into that tile's dP^T columns, which are free once every elementwise
+//                warp has loaded its dP^T piece;
+//   warps 2-5    dQ drain, one per TMEM lane quarter (32 dims x 64 queries): TMEM -> a shared
+//                staging tile -> one TMA bulk reduce-add into the fp32 accumulator [B, T, H*128]
+//                (zeroed by attn_rowdot_kernel; attn_dq_cast_kernel scales and rounds it into dQ);
+//   warps 6-13   elementwise, thread = key row, 32 query columns each: P^T = exp2(S^T scale
+//                log2e - LSE log2e) (causal mask on diagonal tiles only), dS^T = P^T (dP^T - D);
+//                P^T and dS^T (bf16 pairs) overwrite the warp's own 32 S^T columns (P^T in the
+//                first 16, dS^T in the last 16) and dS^T also goes to the swizzled shared tile the
+//                dQ^T product reads.
+// dK and dV are summed over the group's query heads in TMEM and written once. The order in which
+// the key tiles of a query add into its accumulator varies between runs, so dQ is not
+// bit-reproducible; the two-kernel path is (veda_attention_set_deterministic).
+// TMEM columns: S^T[2] (64 each, then P^T | dS^T) | dP^T[2] (64 each, then dQ^T) | dV | dK.
+// ---------------------------------------------------------------------------------------------
+constexpr int kSoftWarps = 8;                       // two per TMEM lane quarter, 32 columns each
+constexpr int kDrainWarps = 4;                      // one per lane quarter
+constexpr int kFusedThreads = 64 + 32 * (kDrainWarps + kSoftWarps);
+constexpr int kDqStageBytes = 64 * 32 * 4;          // [64 queries][32 dims] fp32 per drain warp
+// kBwdSmem's layout (K, V | (Q, dO)[3] | dS^T[2] | (-LSE log2e, D)[3] | barriers) + dQ staging
+constexpr int kFusedSmem = kBwdSmem + kDrainWarps * kDqStageBytes;
+static_assert(kFusedSmem <= 232448, "fused attention backward exceeds the shared memory of an SM");
+
+struct FusedParams
+{
+    const float* nlse2;   // -LSE log2(e) [B, H, T]
+    const float* dvec;    // D [B, H, T]
+    bf16 *dk, *dv;
+    int64_t lddk, lddv;
+    int T, H, Hkv;
+    float scale, scale_log2;
+    int causal;
+    int* status;
+};
+
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int x,
+                                                  int y, int z)
+{
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group"
+        " [%0, {%2, %3, %4}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+// The descriptor of the operand `bytes` further on in shared memory: only the start-address field
+// (address >> 4, the low 14 bits) changes, and it cannot carry for addresses below 256 KB.
+__device__ __forceinline__ uint64_t desc_at(uint64_t d, uint32_t bytes)
+{
+    return d + (bytes >> 4);
+}
+
+// P^T (and, 16 columns further, dS^T) of the k-th 16-query step inside a 64-column buffer
+__device__ __forceinline__ uint32_t pt_col(int ks)
+{
+    return static_cast<uint32_t>(32 * (ks >> 1) + 8 * (ks & 1));
+}
+
+__global__ void __launch_bounds__(kFusedThreads, 1)
+attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                      const __grid_constant__ CUtensorMap tdq, const FusedParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* sk = smem;
+    uint8_t* sv = sk + kTileBytes;
+    uint8_t* sq = sv + kTileBytes;                          // [stages]
+    uint8_t* sdo = sq + kQStages * kQTileBytes;             // [stages]
+    uint8_t* sdst = sdo + kQStages * kQTileBytes;            // [2] dS^T tiles (dQ^T operand)
+    float* srow = reinterpret_cast<float*>(sdst + 2 * kDsTileBytes);   // [stages][2][64]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(srow + kQStages * 2 * kBq);
+    uint64_t* kv_full = bars + 0;
+    uint64_t* qd_full = bars + 1;                  // [stages]
+    uint64_t* qd_empty = bars + 1 + kQStages;      // [stages]
+    uint64_t* sp_full = bars + 1 + 2 * kQStages;   // [2] S^T, dP^T in TMEM
+    uint64_t* ds_full = bars + 3 + 2 * kQStages;   // [2] P^T, dS^T in TMEM, dS^T in smem
+    uint64_t* dq_full = bars + 5 + 2 * kQStages;   // [2] dQ^T in TMEM
+    uint64_t* dq_empty = bars + 7 + 2 * kQStages;  // [2] dQ^T read out of TMEM
+    uint64_t* done = bars + 9 + 2 * kQStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10 + 2 * kQStages);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* sdq = reinterpret_cast<float*>(smem + (kBwdSmem - 1024));   // [4][64][32] fp32
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kt = static_cast<int>(blockIdx.y);   // launch order: all heads' key tile 0 (the
+    const int bk = blockIdx.x;                      // longest under the causal mask) first
+    const int b = bk / p.Hkv, kvh = bk % p.Hkv;
+    const int rep = p.H / p.Hkv;
+    const int nq = (p.T + kBq - 1) / kBq;
+    const int qi0 = p.causal ? (kt * 128) / kBq : 0;
+    const int per_head = nq - qi0;
+    const int iters = rep * per_head;
+
+    if (threadIdx.x == 0)
+    {
+        *abort = 0;
+        mbar_init(kv_full, 1);
+        for (int i = 0; i < kQStages; ++i)
+        {
+            mbar_init(&qd_full[i], 1);
+            mbar_init(&qd_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i)
+        {
+            mbar_init(&sp_full[i], 1);
+            mbar_init(&ds_full[i], kSoftWarps);
+            mbar_init(&dq_full[i], 1);
+            mbar_init(&dq_empty[i], kDrainWarps);
+        }
+        mbar_init(done, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1)
+    {
+        tmem_alloc(tmem_slot, 512);
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+    constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 384;
+
+    if (warp == 0)
+    {
+        if (lane == 0)
+        {
+            tma_prefetch(&tq);
+            tma_prefetch(&tk);
+            tma_prefetch(&tv);
+            tma_prefetch(&tdo);
+            tma_prefetch(&tdq);
+            mbar_expect_tx(kv_full, 2 * kTileBytes);
+            load_tile_3d(sk, &tk, kv_full, kvh * 128, kt * 128, b);
+            load_tile_3d(sv, &tv, kv_full, kvh * 128, kt * 128, b);
+            for (int it = 0; it < iters; ++it)
+            {
+                const int sq_i = it % kQStages;
+                const int h = kvh * rep + it / per_head;
+                const int q0 = (qi0 + it % per_head) * kBq;
+                const int nrow = p.T - q0 < kBq ? p.T - q0 : kBq;   // a multiple of 8 (T % 8 == 0)
+                const uint32_t rbytes = static_cast<uint32_t>(nrow) * 4;
+                const int64_t at = (static_cast<int64_t>(b) * p.H + h) * p.T + q0;
+                mbar_wait(&qd_empty[sq_i], ((it / kQStages) & 1) ^ 1, p.status, abort);
+                mbar_expect_tx(&qd_full[sq_i], 2 * kQTileBytes + 2 * rbytes);
+                load_qtile_3d(sq + sq_i * kQTileBytes, &tq, &qd_full[sq_i], h * 128, q0, b);
+                load_qtile_3d(sdo + sq_i * kQTileBytes, &tdo, &qd_full[sq_i], h * 128, q0, b);
+                bulk_load(srow + sq_i * 2 * kBq, p.nlse2 + at, rbytes, &qd_full[sq_i]);
+                bulk_load(srow + sq_i * 2 * kBq + kBq, p.dvec + at, rbytes, &qd_full[sq_i]);
+            }
+        }
+    }
+    else if (warp == 1)
+    {
+        if (lane == 0)
+        {
+            constexpr uint32_t idesc_s = instr_desc(128, kBq, false, false);
+            constexpr uint32_t idesc_kv = instr_desc(128, 128, false, true);
+            constexpr uint32_t idesc_dq = instr_desc(128, kBq, true, true);
+            // Every operand descriptor is a base descriptor plus a constant offset (desc_at), so
+            // the issuing thread spends almost nothing between MMAs.
+            const uint64_t k_kmaj = smem_desc(smem_u32(sk), 16, 1024);     // K for S^T
+            const uint64_t v_kmaj = smem_desc(smem_u32(sv), 16, 1024);     // V for dP^T
+            const uint64_t k_mnmaj = smem_desc(smem_u32(sk), kHalf, 1024); // K^T for dQ^T
+            const uint64_t q_kmaj = smem_desc(smem_u32(sq), 16, 1024);     // stage 0 of Q, dO
+            const uint64_t do_kmaj = smem_desc(smem_u32(sdo), 16, 1024);
+            const uint64_t q_mnmaj = smem_desc(smem_u32(sq), kQHalf, 1024);
+            const uint64_t do_mnmaj = smem_desc(smem_u32(sdo), kQHalf, 1024);
+            const uint64_t ds_mnmaj = smem_desc(smem_u32(sdst), 16, 1024);
+            mbar_wait(kv_full, 0, p.status, abort);
+            // dV += P^T dO, dK += dS^T Q and dQ^T = K^T dS^T of tile i
+            auto issue_tail = [&](int i) {
+                const int s = i & 1, sq_i = i % kQStages;
+                const uint32_t stage = static_cast<uint32_t>(sq_i) * kQTileBytes;
+                const uint64_t dq = desc_at(q_mnmaj, stage), ddo = desc_at(do_mnmaj, stage);
+                mbar_wait(&ds_full[s], (i >> 1) & 1, p.status, abort);
+                fence_after();
+#pragma unroll
+                for (int ks = 0; ks < kBq / 16; ++ks)
+                {
+                    const uint32_t acc = (i > 0 || ks > 0) ? 1u : 0u;
+                    const uint32_t col = kST + s * 64 + pt_col(ks);   // queries [16 ks, 16 ks + 16)
+                    mma_ts(tmem + kDV, tmem + col, desc_at(ddo, ks * 2048), idesc_kv, acc);
+                    mma_ts(tmem + kDK, tmem + col + 16, desc_at(dq, ks * 2048), idesc_kv, acc);
+                }
+                commit(&qd_empty[sq_i]);
+                const uint64_t dds = desc_at(ds_mnmaj, static_cast<uint32_t>(s) * kDsTileBytes);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+                {
+                    mma(tmem + kDPT + s * 64, desc_at(k_mnmaj, ks * 2048), desc_at(dds, ks * 2048),
+                        idesc_dq, ks > 0 ? 1u : 0u);
+                }
+                commit(&dq_full[s]);
+            };
+            for (int it = 0; it < iters; ++it)
+            {
+                const int st = it & 1, sq_i = it % kQStages;
+                const uint32_t stage = static_cast<uint32_t>(sq_i) * kQTileBytes;
+                const uint64_t dq = desc_at(q_kmaj, stage), ddo = desc_at(do_kmaj, stage);
+                mbar_wait(&qd_full[sq_i], (it / kQStages) & 1, p.status, abort);
+                fence_after();
+                // S^T of buffer st was last read (as P^T / dS^T) by tile it-2's dV / dK products,
+                // issued before these: the MMAs of one thread execute in issue order.
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+                {
+                    const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;   // K-major k-step
+                    const uint32_t koff = (ks >> 2) * kHalf + (ks & 3) * 32;
+                    mma(tmem + kST + st * 64, desc_at(k_kmaj, koff), desc_at(dq, off), idesc_s,
+                        ks > 0 ? 1u : 0u);
+                }
+                // dP^T of buffer st held tile it-2's dQ^T until the drain warps read it out
+                if (it >= 2)
+                {
+                    mbar_wait(&dq_empty[st], ((it - 2) >> 1) & 1, p.status, abort);
+                    fence_after();
+                }
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+                {
+                    const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;
+                    const uint32_t koff = (ks >> 2) * kHalf + (ks & 3) * 32;
+                    mma(tmem + kDPT + st * 64, desc_at(v_kmaj, koff), desc_at(ddo, off), idesc_s,
+                        ks > 0 ? 1u : 0u);
+                }
+                commit(&sp_full[st]);
+                if (it > 0)
+                {
+                    issue_tail(it - 1);
+                }
+            }
+            if (iters > 0)
+            {
+                issue_tail(iters - 1);
+            }
+            commit(done);
+        }
+    }
+    else if (warp < 2 + kDrainWarps)
+    {
+        // dQ^T (lane = dim, column = query) of each tile into the fp32 accumulator
+        const int quarter = warp & 3;
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        float* stage = sdq + quarter * (kDqStageBytes / 4);
+        for (int i = 0; i < iters; ++i)
+        {
+            const int s = i & 1;
+            const int h = kvh * rep + i / per_head;
+            const int q0 = (qi0 + i % per_head) * kBq;
+            mbar_wait(&dq_full[s], (i >> 1) & 1, p.status, abort);
+            fence_after();
+            uint32_t v0[32], v1[32];
+            tmem_ld32_async(tmem + lane_base + kDPT + s * 64, v0);
+            tmem_ld32_async(tmem + lane_base + kDPT + s * 64 + 32, v1);
+            tmem_wait_ld();
+            reg_fence(v0);
+            reg_fence(v1);
+            fence_before();
+            __syncwarp();
+            if (lane == 0)
+            {
+                mbar_arrive(&dq_empty[s]);
+                bulk_wait_group_read<0>();   // the previous tile's reduce has read the staging
+            }
+            __syncwarp();
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+            {
+                stage[c * 32 + lane] = __uint_as_float(v0[c]);
+                stage[(c + 32) * 32 + lane] = __uint_as_float(v1[c]);
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0)
+            {
+                // rows past T fall outside the tensor map and are not written
+                tma_reduce_add_3d(&tdq, stage, h * 128 + quarter * 32, q0, b);
+                bulk_commit_group();
+            }
+        }
+        if (lane == 0)
+        {
+            bulk_wait_group<0>();
+        }
+    }
+    else
+    {
+        const int quarter = warp & 3;
+        const int grp = (warp - 2 - kDrainWarps) >> 2;   // query columns [32 grp, 32 grp + 32)
+        const int r = quarter * 32 + lane;                 // key row
+        const int key = kt * 128 + r;
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
+        const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
+        for (int it = 0; it < iters; ++it)
+        {
+            const int st = it & 1, sq_i = it % kQStages;
+            const int q0 = (qi0 + it % per_head) * kBq;
+            // the stage's -LSE log2e / D rows arrive with its Q / dO, before S^T / dP^T
+            mbar_wait(&qd_full[sq_i], (it / kQStages) & 1, p.status, abort);
+            mbar_wait(&sp_full[st], (it >> 1) & 1, p.status, abort);
+            fence_after();
+            uint32_t sraw[32], draw[32];
+            const uint32_t col = st * 64 + grp * 32;
+            tmem_ld32_async(tmem + lane_base + kST + col, sraw);
+            tmem_ld32_async(tmem + lane_base + kDPT + col, draw);
+            tmem_wait_ld();
+            reg_fence(sraw);
+            reg_fence(draw);
+            uint8_t* stile = sdst + st * kDsTileBytes;
+#pragma unroll
+            for (int half = 0; half < 2; ++half)
+            {
+                const int qc = q0 + grp * 32 + half * 16;   // first query of these 16 columns
+                const float* nl = srow + sq_i * 2 * kBq + grp * 32 + half * 16;
+                const float* dd = nl + kBq;
+                const uint32_t* sr = sraw + half * 16;
+                const uint32_t* dr = draw + half * 16;
+                // visible columns c: lo <= c < hi (queries before T and, causal, not before the key)
+                const int hi = qc + 16 > p.T ? (p.T - qc > 0 ? p.T - qc : 0) : 16;
+                const bool causal_tile = p.causal && qc < kt * 128 + 127;   // some key > query here
+                const int lo = causal_tile ? (key - qc > 0 ? key - qc : 0) : 0;
+                uint32_t pk[8], dk[8];
+                if (!causal_tile && hi == 16)
+                {
+#pragma unroll
+                    for (int c = 0; c < 16; c += 4)
+                    {
+                        const float4 nl4 = *reinterpret_cast<const float4*>(nl + c);
+                        const float4 d4 = *reinterpret_cast<const float4*>(dd + c);
+#pragma unroll
+                        for (int u = 0; u < 4; u += 2)
+                        {
+                            const int e = c + u;
+                            float p0, p1;
+                            f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[e]), __uint_as_float(sr[e + 1])), sc2,
+                                             u == 0 ? f2_pack(nl4.x, nl4.y) : f2_pack(nl4.z, nl4.w)),
+                                      p0, p1);
+                            p0 = ex2(p0);
+                            p1 = ex2(p1);
+                            const uint64_t t = f2_fma(u == 0 ? f2_pack(d4.x, d4.y) : f2_pack(d4.z, d4.w), neg1,
+                                                      f2_pack(__uint_as_float(dr[e]), __uint_as_float(dr[e + 1])));
+                            float d0, d1;
+                            f2_unpack(f2_mul(f2_pack(p0, p1), t), d0, d1);
+                            pk[e >> 1] = pack2(p0, p1);
+                            dk[e >> 1] = pack2(d0, d1);
+                        }
+                    }
+                }
+                else
+                {
+#pragma unroll
+                    for (int c = 0; c < 16; c += 2)
+                    {
+                        const float2 nl2 = *reinterpret_cast<const float2*>(nl + c);
+                        const float2 d2 = *reinterpret_cast<const float2*>(dd + c);
+                        float p0, p1;
+                        f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc2,
+                                         f2_pack(nl2.x, nl2.y)),
+                                  p0, p1);
+                        const bool v0 = c >= lo && c < hi;
+                        const bool v1 = c + 1 >= lo && c + 1 < hi;
+                        p0 = v0 ? ex2(p0) : 0.0f;
+                        p1 = v1 ? ex2(p1) : 0.0f;
+                        const uint64_t t = f2_fma(f2_pack(d2.x, d2.y), neg1,
+                                                  f2_pack(__uint_as_float(dr[c]), __uint_as_float(dr[c + 1])));
+                        float d0, d1;
+                        f2_unpack(f2_mul(f2_pack(p0, p1), t), d0, d1);
+                        d0 = v0 ? d0 : 0.0f;   // masked columns may hold stale -LSE / D values
+                        d1 = v1 ? d1 : 0.0f;
+                        pk[c >> 1] = pack2(p0, p1);
+                        dk[c >> 1] = pack2(d0, d1);
+                    }
+                }
+                // every S^T / dP^T column of this warp is in registers: overwrite in place
+                const uint32_t pc = kST + st * 64 + pt_col(2 * grp + half);
+                tmem_st8_async(tmem + lane_base + pc, pk);
+                tmem_st8_async(tmem + lane_base + pc + 16, dk);
+                // dS^T row piece into the swizzled tile the dQ^T product reads. Its last reader, tile
+                // it-2's dQ^T product, was issued before this tile's S^T / dP^T products, so the
+                // sp_full signal (which covers every earlier product) saw it complete.
+                *reinterpret_cast<uint4*>(stile + sw128_offset(r, grp * 4 + half * 2)) =
+                    make_uint4(dk[0], dk[1], dk[2], dk[3]);
+                *reinterpret_cast<uint4*>(stile + sw128_offset(r, grp * 4 + half * 2 + 1)) =
+                    make_uint4(dk[4], dk[5], dk[6], dk[7]);
+            }
+            fence_proxy_async();
+            tmem_wait_st();
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ds_full[st]);
+        }
+        // dV and dK rows of this key (summed over the group's heads in TMEM): 64 dims per warp
+        mbar_wait(done, 0, p.status, abort);
+        fence_after();
+        const bool valid = key < p.T;
+        bf16* vrow = p.dv + (static_cast<int64_t>(b) * p.T + key) * p.lddv + static_cast<int64_t>(kvh) * 128;
+        bf16* krow = p.dk + (static_cast<int64_t>(b) * p.T + key) * p.lddk + static_cast<int64_t>(kvh) * 128;
+#pragma unroll 1
+        for (int c = grp * 2; c < grp * 2 + 2; ++c)
+        {
+            uint32_t rv[32], rk[32];
+            tmem_ld32(tmem + lane_base + kDV + c * 32, rv);
+            tmem_ld32(tmem + lane_base + kDK + c * 32, rk);
+            if (valid)
+            {
+#pragma unroll
+                for (int e = 0; e < 32; e += 8)
+                {
+                    float a8[8], k8[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                    {
+                        a8[q] = __uint_as_float(rv[e + q]);
+                        k8[q] = __uint_as_float(rk[e + q]) * p.scale;
+                    }
+                    store16(vrow + c * 32 + e, a8);
+                    store16(krow + c * 32 + e, k8);
+                }
+            }
+        }
+    }
+    fence_before();
+    __syncthreads();
+    if (warp == 1)
+    {
+        fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// dQ = scale * the fp32 accumulator [B*T][H*128], rounded to bf16 into the caller's layout; eight
+// dims per thread.
+__global__ void attn_dq_cast_kernel(const float* __restrict__ acc, bf16* __restrict__ dq,
+                                    int64_t lddq, int64_t rows, int64_t width, float scale)
+{
+    const int64_t per_row = width >> 3;
+    const int64_t n = rows * per_row;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    {
+        const int64_t row = i / per_row, c = (i - row * per_row) << 3;
+        const float4 a = *reinterpret_cast<const float4*>(acc + row * width + c);
+        const float4 b = *reinterpret_cast<const float4*>(acc + row * width + c + 4);
+        const float v8[8] = {a.x * scale, a.y * scale, a.z * scale, a.w * scale,
+                             b.x * scale, b.y * scale, b.z * scale, b.w * scale};
+        store16(dq + row * lddq + c, v8);
+    }
+}
 
 // dQ[q-tile] = sum over key tiles of dS K, from dS^T stored as [B*H][keys][queries].
 // Persistent: one CTA per SM walks the (batch, head, 128-query tile) items, longest first, with
@@ -964,7 +1426,8 @@ constexpr int kRowdotRows = 4;
 __global__ void attn_rowdot_kernel(const bf16* __restrict__ o, int64_t ldo,
                                    const bf16* __restrict__ dout, int64_t lddo,
                                    const float* __restrict__ lse, float* __restrict__ dvec,
-                                   float* __restrict__ nlse2, int64_t B, int64_t T, int64_t H)
+                                   float* __restrict__ nlse2, float* __restrict__ dqacc, int64_t B,
+                                   int64_t T, int64_t H)
 {
     const int sub = threadIdx.x & 15;
     // the two 16-lane groups of a warp may leave the loop at different iterations: shuffles
@@ -983,6 +1446,20 @@ __global__ void attn_rowdot_kernel(const bf16* __restrict__ o, int64_t ldo,
             const int64_t h = r % H, bt = r / H;
             load16(o + bt * ldo + h * 128 + sub * 8, x[u]);
             load16(dout + bt * lddo + h * 128 + sub * 8, y[u]);
+        }
+        if (dqacc != nullptr)
+        {
+            // row r of the fused path's dQ accumulator [B*T][H*128] is (token r / H, head r % H)
+#pragma unroll
+            for (int u = 0; u < kRowdotRows; ++u)
+            {
+                if (r0 + u < rows)
+                {
+                    float4* z = reinterpret_cast<float4*>(dqacc + (r0 + u) * 128 + sub * 8);
+                    z[0] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    z[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+            }
         }
 #pragma unroll
         for (int u = 0; u < kRowdotRows; ++u)
@@ -1042,18 +1519,37 @@ bool make_map3(CUtensorMap* map, const void* base, int64_t width, int64_t T, int
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [B, T, width] fp32 (row stride width) with an unswizzled box of box_w columns x box_rows rows,
+// for bulk reduce-adds from shared memory.
+bool make_map3_f32(CUtensorMap* map, void* base, int64_t width, int64_t T, int64_t B,
+                   uint32_t box_w, uint32_t box_rows)
+{
+    auto fn = encode_fn();
+    if (fn == nullptr)
+    {
+        return false;
+    }
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(T),
+                                static_cast<cuuint64_t>(B)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(width) * 4,
+                                   static_cast<cuuint64_t>(width) * 4 * static_cast<cuuint64_t>(T)};
+    const cuuint32_t box[3] = {box_w, box_rows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 } // namespace
 
-// The tcgen05 kernels serve bf16 / head_dim 128 unless VEDA_ATTENTION_MMA_SYNC=1 selects the
-// mma.sync kernels of attention_flash.cu (kept for comparison and as the fallback).
-int attention_tc_enabled()
-{
-    static const int enabled = [] {
-        const char* v = std::getenv("VEDA_ATTENTION_MMA_SYNC");
-        return (v != nullptr && v[0] == '1') ? 0 : 1;
-    }();
-    return enabled;
-}
+// Which backward serves bf16 / head_dim 128: 0 the fused kernel (the default), 1 the two-kernel
+// path whose dQ is bit-reproducible. Process-wide; VEDA_ATTENTION_DETERMINISTIC=1 sets 1 at load.
+std::atomic<int> g_attn_deterministic{[] {
+    const char* v = std::getenv("VEDA_ATTENTION_DETERMINISTIC");
+    return (v != nullptr && v[0] == '1') ? 1 : 0;
+}()};
+
+int attention_deterministic() { return g_attn_deterministic.load(std::memory_order_relaxed); }
 
 int attn_tc_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
                 void* o, int64_t ldo, float* lse, int64_t B, int64_t T, int64_t H, int64_t Hkv,
@@ -1082,10 +1578,15 @@ int attn_tc_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     return check_launch("veda_attention_fwd (tcgen05)");
 }
 
-// Workspace of the tcgen05 backward: dS^T [B*H][T][T] bf16, then -LSE log2(e) [B, H, T] fp32.
+// Workspace of the tcgen05 backward after D: the fused path's fp32 dQ accumulator
+// [B*T][H*128] (O(B H T)), or the deterministic path's dS^T [B*H][T][T] bf16 (O(B H T^2)); then
+// -LSE log2(e) [B, H, T] fp32.
 size_t tc_bwd_ds_bytes(int64_t B, int64_t T, int64_t H)
 {
-    const size_t bytes = static_cast<size_t>(B * H) * static_cast<size_t>(T) * static_cast<size_t>(T) * sizeof(bf16);
+    const size_t bytes =
+        attention_deterministic()
+            ? static_cast<size_t>(B * H) * static_cast<size_t>(T) * static_cast<size_t>(T) * sizeof(bf16)
+            : static_cast<size_t>(B * T * H) * 128 * sizeof(float);
     return (bytes + 255) & ~static_cast<size_t>(255);
 }
 
@@ -1109,8 +1610,8 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     CUtensorMap mq, mk, mv, mdo, mds;
     if (!make_map3(&mq, q, H * 128, T, B, ldq, kBq) || !make_map3(&mk, k, Hkv * 128, T, B, ldk, 128) ||
         !make_map3(&mv, v, Hkv * 128, T, B, ldv, 128) ||
-        !make_map3(&mdo, dout, H * 128, T, B, lddo, kBq) ||
-        !make_map3(&mds, extra, T, T, B * H, T, 128) || !aligned16(dvec))
+        !make_map3(&mdo, dout, H * 128, T, B, lddo, kBq) || !aligned16(dvec) || !aligned16(extra) ||
+        (attention_deterministic() && !make_map3(&mds, extra, T, T, B * H, T, 128)))
     {
         return -1;   // caller falls back
     }
@@ -1120,17 +1621,39 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     if (configured != device)
     {
         cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
+        cudaFuncSetAttribute(attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFusedSmem);
         cudaFuncSetAttribute(attn_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDqSmem);
         configured = device;
     }
-    bf16* ds = static_cast<bf16*>(extra);
     float* nlse2 = reinterpret_cast<float*>(static_cast<char*>(extra) + tc_bwd_ds_bytes(B, T, H));
+    const dim3 grid(static_cast<unsigned>(B * Hkv), static_cast<unsigned>((T + 127) / 128));
+    if (!attention_deterministic())
+    {
+        float* dqacc = static_cast<float*>(extra);
+        CUtensorMap mdq;
+        if (!make_map3_f32(&mdq, dqacc, H * 128, T, B, 32, kBq))
+        {
+            return -1;
+        }
+        attn_rowdot_kernel<<<grid_for(B * H * T * 16 / kRowdotRows, 256), 256, 0, s>>>(
+            static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, lse, dvec, nlse2,
+            dqacc, B, T, H);
+        FusedParams p{nlse2, dvec, static_cast<bf16*>(dk), static_cast<bf16*>(dv), lddk, lddv,
+                      static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
+                      scale * kLog2e, causal, device_status_ptr()};
+        attn_bwd_fused_kernel<<<grid, kFusedThreads, kFusedSmem, s>>>(mq, mk, mv, mdo, mdq, p);
+        attn_dq_cast_kernel<<<grid_for(B * T * H * 16, 256), 256, 0, s>>>(
+            dqacc, static_cast<bf16*>(dq), lddq, B * T, H * 128, scale);
+        count_launch(3);
+        return check_launch("veda_attention_bwd (tcgen05, fused)");
+    }
+    bf16* ds = static_cast<bf16*>(extra);
     attn_rowdot_kernel<<<grid_for(B * H * T * 16 / kRowdotRows, 256), 256, 0, s>>>(
-        static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, lse, dvec, nlse2, B, T, H);
+        static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, lse, dvec, nlse2,
+        nullptr, B, T, H);
     BwdParams p{nlse2, dvec, static_cast<bf16*>(dk), static_cast<bf16*>(dv), ds, lddk, lddv,
                 static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
                 scale * kLog2e, causal, device_status_ptr()};
-    const dim3 grid(static_cast<unsigned>(B * Hkv), static_cast<unsigned>((T + 127) / 128));
     attn_bwd_tc_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, mds, p);
     DqParams pq{static_cast<bf16*>(dq), lddq, static_cast<int>(T), static_cast<int>(H),
                 static_cast<int>(Hkv), static_cast<int>(B), scale, causal, device_status_ptr()};

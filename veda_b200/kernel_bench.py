@@ -4,7 +4,7 @@
         the matmul-backward sweep: for X[M,K], W[K,N], dY[M,N] (bf16, ~N(0,1)/sqrt(K), seed 1)
         time dX = dY W^T and dW = X^T dY (fp32 out) for (M,K,N) in the five sweep shapes, the
         pair as one CUDA graph replayed after an L2-clearing read; 4*M*K*N FLOP per shape.
-    python -m veda_b200.kernel_bench attn-bwd [--seq 1024 4096] [--reps 5]
+    python -m veda_b200.kernel_bench attn-bwd [--seq 1024 4096] [--reps 5] [--modes 0 1]
         causal GQA attention backward, B 8, H 16, Hkv 8, Dh 128, bf16, seed 2; 5*B*H*T^2*Dh FLOP.
     python -m veda_b200.kernel_bench gemm --op nt --m 8192 --n 151936 --k 1024 [--reps 3]
         one GEMM shape (used for the ncu captures).
@@ -107,15 +107,18 @@ def mm_sweep(reps):
         torch.cuda.empty_cache()
 
 
-def attn_bwd(seqs, reps):
+def attn_bwd(seqs, reps, modes=(0, 1), B=8):
+    """Attention fwd and bwd at B x H16 / Hkv8 x Dh128; each backward mode: 0 the fused kernel,
+    1 the deterministic two-kernel path."""
     import torch
     import veda_b200 as V
     L = V.lib()
     s = torch.cuda.current_stream()
     peak, _, kind = _peaks()
-    B, H, Hk, Dh = 8, 16, 8, 128
+    H, Hk, Dh = 16, 8, 128
     g = torch.Generator(device="cuda").manual_seed(2)
-    for T in seqs:
+    for T, mode in [(T, m) for T in seqs for m in modes]:
+        L.veda_attention_set_deterministic(mode)
         q = torch.randn(B * T, H * Dh, device="cuda", generator=g).to(torch.bfloat16)
         k = torch.randn(B * T, Hk * Dh, device="cuda", generator=g).to(torch.bfloat16)
         v = torch.randn(B * T, Hk * Dh, device="cuda", generator=g).to(torch.bfloat16)
@@ -145,7 +148,8 @@ def attn_bwd(seqs, reps):
         ms_f = _time(fwd, reps, s)
         fl_b = 5.0 * B * H * T * T * Dh
         fl_f = 2.0 * B * H * T * T * Dh
-        print(json.dumps({"bench": "attn", "B": B, "H": H, "Hkv": Hk, "Dh": Dh, "T": T,
+        print(json.dumps({"bench": "attn", "mode": ["fused", "deterministic"][mode], "B": B,
+                          "H": H, "Hkv": Hk, "Dh": Dh, "T": T,
                           "bwd_ms": ms_b, "bwd_tflops": fl_b / (ms_b / 1e3) / 1e12,
                           "fwd_ms": ms_f, "fwd_tflops": fl_f / (ms_f / 1e3) / 1e12,
                           "peak": peak, "bwd_frac": fl_b / (ms_b / 1e3) / 1e12 / peak,
@@ -365,6 +369,8 @@ def main():
     b = sub.add_parser("attn-bwd")
     b.add_argument("--seq", type=int, nargs="+", default=[1024, 4096])
     b.add_argument("--reps", type=int, default=5)
+    b.add_argument("--modes", type=int, nargs="+", default=[0, 1])
+    b.add_argument("--batch", type=int, default=8)
     c = sub.add_parser("gemm")
     c.add_argument("--op", default="nt", choices=["nt", "nn", "tn"])
     c.add_argument("--m", type=int, default=8192)
@@ -385,7 +391,7 @@ def main():
     if args.cmd == "mm-sweep":
         mm_sweep(args.reps)
     elif args.cmd == "attn-bwd":
-        attn_bwd(args.seq, args.reps)
+        attn_bwd(args.seq, args.reps, args.modes, args.batch)
     elif args.cmd == "bw":
         bandwidth_kernels(args.tokens, args.reps, args.kernels)
     else:
