@@ -548,8 +548,9 @@ def test_attention_bwd_t1024_h16_against_oracle(mode):
 @pytest.mark.parametrize("B,T", [(8, 1024), (2, 4096)])
 def test_attention_fused_equals_deterministic(B, T):
     """The fused backward against the two-kernel one on the same inputs at the isolated config's
-    sizes (B 8 x T 1024, and T 4096): dK and dV come from the same products in the same order, so
-    they are bit-identical; dQ differs only in the order key tiles are summed in fp32."""
+    sizes (B 8 x T 1024, and T 4096): dV comes from the same bf16 P and the same products in the
+    same order, so it is bit-identical; dK differs in that the fused kernel forms dS from the
+    bf16 P (the two-kernel path from fp32 P), and dQ also in the order key tiles are summed."""
     H, Hk, Dh = 16, 8, 128
     r = rng(2)
     tok = (B * T, H * Dh)
@@ -575,9 +576,9 @@ def test_attention_fused_equals_deterministic(B, T):
         finally:
             V.lib().veda_attention_set_deterministic(prev)
     (dq0, dk0, dv0), (dq1, dk1, dv1) = out
-    assert np.array_equal(dk0, dk1)
     assert np.array_equal(dv0, dv1)
-    assert np.isfinite(dq0).all()
+    assert np.isfinite(dq0).all() and np.isfinite(dk0).all()
+    assert rel(dk0, dk1) <= 1e-2
     assert rel(dq0, dq1) <= 1e-2
 
 

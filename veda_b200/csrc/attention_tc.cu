@@ -783,37 +783,50 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
 }
 
 // ---------------------------------------------------------------------------------------------
-// Fused backward (the default): the four products of attn_bwd_tc_kernel plus the query gradient
-// in one kernel, so dS^T never leaves the SM and the workspace is O(B H T). One CTA per (batch,
-// KV head, 128-key tile), 14 warps:
-//   warp 0       TMA: K and V once, then Q, dO (64 x 128 each) with the tile's -LSE log2(e) and D
-//                into a 3-stage ring;
-//   warp 1       MMA, per 64-query tile i:  S^T = K Q^T and dP^T = V dO^T (M128 keys, N64
-//                queries, K128 dims) into one of two TMEM buffer pairs; then, for tile i-1,
-//                dV += P^T dO and dK += dS^T Q (A read from TMEM) and dQ^T = K^T dS^T (M128 dims,
-//                N64 queries, K128 keys; the K tile and the staged dS^T tile read as MN-major
-//                operands) into that tile's dP^T columns, which are free once every elementwise
-//                warp has loaded its dP^T piece;
-//   warps 2-5    dQ drain, one per TMEM lane quarter (32 dims x 64 queries): TMEM -> a shared
-//                staging tile -> one TMA bulk reduce-add into the fp32 accumulator [B, T, H*128]
-//                (zeroed by attn_rowdot_kernel; attn_dq_cast_kernel scales and rounds it into dQ);
-//   warps 6-13   elementwise, thread = key row, 32 query columns each: P^T = exp2(S^T scale
-//                log2e - LSE log2e) (causal mask on diagonal tiles only), dS^T = P^T (dP^T - D);
-//                P^T and dS^T (bf16 pairs) overwrite the warp's own 32 S^T columns (P^T in the
-//                first 16, dS^T in the last 16) and dS^T also goes to the swizzled shared tile the
-//                dQ^T product reads.
+// Fused backward (the default): the five products of the backward in one kernel on 128 x 128
+// tiles, so dS^T never leaves the SM and the workspace is O(B H T). One CTA per (batch, KV head,
+// 128-key tile), looping over the GQA group's query heads x 128-query tiles; 16 warps in four
+// warpgroups, with registers moved between them by setmaxnreg:
+//   warps 0-3    dQ drain (144 registers), one per TMEM lane quarter (32 queries x 128 dims): the
+//                whole tile out of TMEM at once (the next dP^T reuses the columns), then 32-dim
+//                slices through a swizzled shared ring into TMA bulk reduce-adds on the fp32
+//                accumulator [B, T, H*128] (zeroed by attn_rowdot_kernel; attn_dq_cast_kernel
+//                scales and rounds it into dQ);
+//   warps 4-11   elementwise, thread = key row, 64 query columns each. Phase 1: P^T = exp2(S^T
+//                scale log2e - LSE log2e) (causal mask on the diagonal tile only), written as bf16
+//                pairs over the first half of the warp's own S^T columns. Phase 2: dS^T = P^T (dP^T
+//                - D), bf16 pairs over the first half of the warp's dP^T columns and into the
+//                swizzled shared tile the dQ product reads;
+//   warp 12      TMA (112 registers): K and V once; per query tile Q with its -LSE log2(e) and D
+//                rows (2 stages) and dO (1 stage);
+//   warp 13      MMA (112 registers), every product M128 x N128 x K128: per tile i the order is
+//                  S^T(i+1) = K Q^T,  dK += dS^T(i) Q,  dQ(i) = dS(i) K,  dP^T(i+1) = V dO^T,
+//                  dV += P^T(i+1) dO
+//                so the elementwise work of each phase overlaps other products: P(i+1) is formed
+//                while dK(i) and dQ(i) run, dS(i+1) while dV(i+1) and S^T(i+2) run;
+//   warps 14-15  idle (they complete the warpgroup that gives up registers).
 // dK and dV are summed over the group's query heads in TMEM and written once. The order in which
 // the key tiles of a query add into its accumulator varies between runs, so dQ is not
 // bit-reproducible; the two-kernel path is (veda_attention_set_deterministic).
-// TMEM columns: S^T[2] (64 each, then P^T | dS^T) | dP^T[2] (64 each, then dQ^T) | dV | dK.
+// TMEM columns: S^T -> P^T [0, 128) | dP^T -> dS^T, then dQ [128, 256) | dV | dK.
 // ---------------------------------------------------------------------------------------------
-constexpr int kSoftWarps = 8;                       // two per TMEM lane quarter, 32 columns each
+constexpr int kFq = 128;                            // queries per tile
+constexpr int kSoftWarps = 8;                       // two per TMEM lane quarter, 64 columns each
 constexpr int kDrainWarps = 4;                      // one per lane quarter
-constexpr int kFusedThreads = 64 + 32 * (kDrainWarps + kSoftWarps);
-constexpr int kDqStageBytes = 64 * 32 * 4;          // [64 queries][32 dims] fp32 per drain warp
-// kBwdSmem's layout (K, V | (Q, dO)[3] | dS^T[2] | (-LSE log2e, D)[3] | barriers) + dQ staging
-constexpr int kFusedSmem = kBwdSmem + kDrainWarps * kDqStageBytes;
-static_assert(kFusedSmem <= 232448, "fused attention backward exceeds the shared memory of an SM");
+// warpgroup 0: drain; 1-2: elementwise; 3: TMA, MMA and two idle warps (whole warpgroups, so
+// setmaxnreg can move registers: launched at 128 a thread = 65536, then 144 + 128 + 128 + 112)
+constexpr int kFusedThreads = 512;
+constexpr int kTmaWarp = 12, kMmaWarp = 13;
+constexpr int kDrainRegs = 144, kIssueRegs = 112;
+static_assert(kDrainRegs + 2 * 128 + kIssueRegs == 4 * 128, "register split must add up");
+constexpr int kDqSlice = 32 * 32 * 4;               // [32 queries][32 dims] fp32, 128-byte rows
+// K, V | Q[2] | dO | dS^T | dQ staging [4 warps][2] | -LSE log2e [2][128] | D [2][128] | barriers,
+// from a 1024-byte aligned base; the request is the largest an SM allows, and the kernel checks
+// that the aligned layout fits in it.
+constexpr int kFusedBytes = 2 * kTileBytes + 2 * kTileBytes + kTileBytes + kTileBytes +
+                            kDrainWarps * 2 * kDqSlice + 2 * kFq * 4 + 2 * kFq * 4 + 256;
+constexpr int kFusedSmem = 232448;
+static_assert(kFusedBytes <= kFusedSmem, "fused attention backward exceeds the shared memory of an SM");
 
 struct FusedParams
 {
@@ -844,10 +857,60 @@ __device__ __forceinline__ uint64_t desc_at(uint64_t d, uint32_t bytes)
     return d + (bytes >> 4);
 }
 
-// P^T (and, 16 columns further, dS^T) of the k-th 16-query step inside a 64-column buffer
+// Column (inside the 128-column S^T or dP^T region) of the bf16 P^T / dS^T pairs of the k-th
+// 16-query step: each elementwise warp packs its 64 queries into the first 32 of its own columns.
 __device__ __forceinline__ uint32_t pt_col(int ks)
 {
-    return static_cast<uint32_t>(32 * (ks >> 1) + 8 * (ks & 1));
+    return static_cast<uint32_t>(64 * (ks >> 2) + 8 * (ks & 3));
+}
+
+template <int N>
+__device__ __forceinline__ void regs_inc()
+{
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_dec()
+{
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// P^T = exp2(S^T scale log2e - LSE log2e) for 16 query columns (c visible iff lo <= c < hi).
+__device__ __forceinline__ void p_block(const uint32_t* sr, const float* nl, float* pv, bool full,
+                                        int lo, int hi, uint64_t sc2)
+{
+    if (full)
+    {
+#pragma unroll
+        for (int c = 0; c < 16; c += 4)
+        {
+            const float4 nl4 = *reinterpret_cast<const float4*>(nl + c);
+#pragma unroll
+            for (int u = 0; u < 4; u += 2)
+            {
+                float p0, p1;
+                f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[c + u]), __uint_as_float(sr[c + u + 1])), sc2,
+                                 u == 0 ? f2_pack(nl4.x, nl4.y) : f2_pack(nl4.z, nl4.w)),
+                          p0, p1);
+                pv[c + u] = ex2(p0);
+                pv[c + u + 1] = ex2(p1);
+            }
+        }
+    }
+    else
+    {
+#pragma unroll
+        for (int c = 0; c < 16; c += 2)
+        {
+            const float2 nl2 = *reinterpret_cast<const float2*>(nl + c);
+            float p0, p1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc2,
+                             f2_pack(nl2.x, nl2.y)),
+                      p0, p1);
+            pv[c] = (c >= lo && c < hi) ? ex2(p0) : 0.0f;
+            pv[c + 1] = (c + 1 >= lo && c + 1 < hi) ? ex2(p1) : 0.0f;
+        }
+    }
 }
 
 __global__ void __launch_bounds__(kFusedThreads, 1)
@@ -860,30 +923,41 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* sk = smem;
     uint8_t* sv = sk + kTileBytes;
-    uint8_t* sq = sv + kTileBytes;                          // [stages]
-    uint8_t* sdo = sq + kQStages * kQTileBytes;             // [stages]
-    uint8_t* sdst = sdo + kQStages * kQTileBytes;            // [2] dS^T tiles (dQ^T operand)
-    float* srow = reinterpret_cast<float*>(sdst + 2 * kDsTileBytes);   // [stages][2][64]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(srow + kQStages * 2 * kBq);
+    uint8_t* sq = sv + kTileBytes;                 // [2]
+    uint8_t* sdo = sq + 2 * kTileBytes;
+    uint8_t* sds = sdo + kTileBytes;               // dS^T [128 keys][128 queries], two halves
+    uint8_t* sdq = sds + kTileBytes;               // [4 warps][2][32 x 32 fp32]
+    float* snl = reinterpret_cast<float*>(sdq + kDrainWarps * 2 * kDqSlice);   // [2][128]
+    float* sdv = snl + 2 * kFq;                                               // [2][128]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sdv + 2 * kFq);
     uint64_t* kv_full = bars + 0;
-    uint64_t* qd_full = bars + 1;                  // [stages]
-    uint64_t* qd_empty = bars + 1 + kQStages;      // [stages]
-    uint64_t* sp_full = bars + 1 + 2 * kQStages;   // [2] S^T, dP^T in TMEM
-    uint64_t* ds_full = bars + 3 + 2 * kQStages;   // [2] P^T, dS^T in TMEM, dS^T in smem
-    uint64_t* dq_full = bars + 5 + 2 * kQStages;   // [2] dQ^T in TMEM
-    uint64_t* dq_empty = bars + 7 + 2 * kQStages;  // [2] dQ^T read out of TMEM
-    uint64_t* done = bars + 9 + 2 * kQStages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10 + 2 * kQStages);
+    uint64_t* q_full = bars + 1;      // [2] Q (+ -LSE log2e, D) staged
+    uint64_t* q_empty = bars + 3;     // [2] S^T and dK of that Q done
+    uint64_t* do_full = bars + 5;     // dO staged
+    uint64_t* do_empty = bars + 6;    // dP^T and dV of that dO done
+    uint64_t* s_full = bars + 7;      // S^T in TMEM
+    uint64_t* p_full = bars + 8;      // P^T in TMEM
+    uint64_t* dp_full = bars + 9;     // dP^T in TMEM
+    uint64_t* ds_full = bars + 10;    // dS^T in TMEM and in shared memory
+    uint64_t* dq_full = bars + 11;    // dQ in TMEM
+    uint64_t* dq_empty = bars + 12;   // dQ read out of TMEM
+    uint64_t* done = bars + 13;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    float* sdq = reinterpret_cast<float*>(smem + (kBwdSmem - 1024));   // [4][64][32] fp32
 
+    if (static_cast<int>(smem - smem_raw) + kFusedBytes > kFusedSmem)
+    {
+        // the dynamic shared memory base is not aligned as this layout assumes (uniform exit)
+        if (threadIdx.x == 0 && p.status != nullptr) atomicExch(p.status, VEDA_ERR_UNSUPPORTED);
+        return;
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kt = static_cast<int>(blockIdx.y);   // launch order: all heads' key tile 0 (the
     const int bk = blockIdx.x;                      // longest under the causal mask) first
     const int b = bk / p.Hkv, kvh = bk % p.Hkv;
     const int rep = p.H / p.Hkv;
-    const int nq = (p.T + kBq - 1) / kBq;
-    const int qi0 = p.causal ? (kt * 128) / kBq : 0;
+    const int nq = (p.T + kFq - 1) / kFq;
+    const int qi0 = p.causal ? kt : 0;
     const int per_head = nq - qi0;
     const int iters = rep * per_head;
 
@@ -891,22 +965,28 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
     {
         *abort = 0;
         mbar_init(kv_full, 1);
-        for (int i = 0; i < kQStages; ++i)
-        {
-            mbar_init(&qd_full[i], 1);
-            mbar_init(&qd_empty[i], 1);
-        }
         for (int i = 0; i < 2; ++i)
         {
-            mbar_init(&sp_full[i], 1);
-            mbar_init(&ds_full[i], kSoftWarps);
-            mbar_init(&dq_full[i], 1);
-            mbar_init(&dq_empty[i], kDrainWarps);
+            mbar_init(&q_full[i], 1);
+            mbar_init(&q_empty[i], 1);
         }
+        mbar_init(do_full, 1);
+        mbar_init(do_empty, 1);
+        mbar_init(s_full, 1);
+        mbar_init(p_full, kSoftWarps);
+        mbar_init(dp_full, 1);
+        mbar_init(ds_full, kSoftWarps);
+        mbar_init(dq_full, 1);
+        mbar_init(dq_empty, kDrainWarps);
         mbar_init(done, 1);
         mbar_fence_init();
     }
-    if (warp == 1)
+    // rows of -LSE log2e / D past T are never loaded: keep them finite (0 * NaN would be NaN)
+    for (int i = threadIdx.x; i < 4 * kFq; i += blockDim.x)
+    {
+        snl[i] = 0.0f;   // snl [2][128] and sdv [2][128] are contiguous
+    }
+    if (warp == kMmaWarp)
     {
         tmem_alloc(tmem_slot, 512);
     }
@@ -914,10 +994,11 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
-    constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 384;
+    constexpr uint32_t kS = 0, kDP = 128, kDV = 256, kDK = 384;
 
-    if (warp == 0)
+    if (warp == kTmaWarp)
     {
+        regs_dec<kIssueRegs>();
         if (lane == 0)
         {
             tma_prefetch(&tq);
@@ -930,148 +1011,176 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
             load_tile_3d(sv, &tv, kv_full, kvh * 128, kt * 128, b);
             for (int it = 0; it < iters; ++it)
             {
-                const int sq_i = it % kQStages;
+                const int s = it & 1;
                 const int h = kvh * rep + it / per_head;
-                const int q0 = (qi0 + it % per_head) * kBq;
-                const int nrow = p.T - q0 < kBq ? p.T - q0 : kBq;   // a multiple of 8 (T % 8 == 0)
+                const int q0 = (qi0 + it % per_head) * kFq;
+                const int nrow = p.T - q0 < kFq ? p.T - q0 : kFq;   // a multiple of 8 (T % 8 == 0)
                 const uint32_t rbytes = static_cast<uint32_t>(nrow) * 4;
                 const int64_t at = (static_cast<int64_t>(b) * p.H + h) * p.T + q0;
-                mbar_wait(&qd_empty[sq_i], ((it / kQStages) & 1) ^ 1, p.status, abort);
-                mbar_expect_tx(&qd_full[sq_i], 2 * kQTileBytes + 2 * rbytes);
-                load_qtile_3d(sq + sq_i * kQTileBytes, &tq, &qd_full[sq_i], h * 128, q0, b);
-                load_qtile_3d(sdo + sq_i * kQTileBytes, &tdo, &qd_full[sq_i], h * 128, q0, b);
-                bulk_load(srow + sq_i * 2 * kBq, p.nlse2 + at, rbytes, &qd_full[sq_i]);
-                bulk_load(srow + sq_i * 2 * kBq + kBq, p.dvec + at, rbytes, &qd_full[sq_i]);
+                // Q stage s (and its -LSE log2e, D rows) is free once dK(it-2) is done, which
+                // follows dS^T(it-2), the last elementwise read of those rows
+                mbar_wait(&q_empty[s], ((it >> 1) & 1) ^ 1, p.status, abort);
+                mbar_expect_tx(&q_full[s], kTileBytes + 2 * rbytes);
+                load_tile_3d(sq + s * kTileBytes, &tq, &q_full[s], h * 128, q0, b);
+                bulk_load(snl + s * kFq, p.nlse2 + at, rbytes, &q_full[s]);
+                bulk_load(sdv + s * kFq, p.dvec + at, rbytes, &q_full[s]);
+                mbar_wait(do_empty, (it & 1) ^ 1, p.status, abort);   // dV(it-1) done
+                mbar_expect_tx(do_full, kTileBytes);
+                load_tile_3d(sdo, &tdo, do_full, h * 128, q0, b);
             }
         }
     }
-    else if (warp == 1)
+    else if (warp == kMmaWarp)
     {
+        regs_dec<kIssueRegs>();
         if (lane == 0)
         {
-            constexpr uint32_t idesc_s = instr_desc(128, kBq, false, false);
+            constexpr uint32_t idesc_s = instr_desc(128, kFq, false, false);
             constexpr uint32_t idesc_kv = instr_desc(128, 128, false, true);
-            constexpr uint32_t idesc_dq = instr_desc(128, kBq, true, true);
+            constexpr uint32_t idesc_dq = instr_desc(kFq, 128, true, true);
             // Every operand descriptor is a base descriptor plus a constant offset (desc_at), so
             // the issuing thread spends almost nothing between MMAs.
             const uint64_t k_kmaj = smem_desc(smem_u32(sk), 16, 1024);     // K for S^T
             const uint64_t v_kmaj = smem_desc(smem_u32(sv), 16, 1024);     // V for dP^T
-            const uint64_t k_mnmaj = smem_desc(smem_u32(sk), kHalf, 1024); // K^T for dQ^T
-            const uint64_t q_kmaj = smem_desc(smem_u32(sq), 16, 1024);     // stage 0 of Q, dO
-            const uint64_t do_kmaj = smem_desc(smem_u32(sdo), 16, 1024);
-            const uint64_t q_mnmaj = smem_desc(smem_u32(sq), kQHalf, 1024);
-            const uint64_t do_mnmaj = smem_desc(smem_u32(sdo), kQHalf, 1024);
-            const uint64_t ds_mnmaj = smem_desc(smem_u32(sdst), 16, 1024);
-            mbar_wait(kv_full, 0, p.status, abort);
-            // dV += P^T dO, dK += dS^T Q and dQ^T = K^T dS^T of tile i
-            auto issue_tail = [&](int i) {
-                const int s = i & 1, sq_i = i % kQStages;
-                const uint32_t stage = static_cast<uint32_t>(sq_i) * kQTileBytes;
-                const uint64_t dq = desc_at(q_mnmaj, stage), ddo = desc_at(do_mnmaj, stage);
-                mbar_wait(&ds_full[s], (i >> 1) & 1, p.status, abort);
-                fence_after();
-#pragma unroll
-                for (int ks = 0; ks < kBq / 16; ++ks)
-                {
-                    const uint32_t acc = (i > 0 || ks > 0) ? 1u : 0u;
-                    const uint32_t col = kST + s * 64 + pt_col(ks);   // queries [16 ks, 16 ks + 16)
-                    mma_ts(tmem + kDV, tmem + col, desc_at(ddo, ks * 2048), idesc_kv, acc);
-                    mma_ts(tmem + kDK, tmem + col + 16, desc_at(dq, ks * 2048), idesc_kv, acc);
-                }
-                commit(&qd_empty[sq_i]);
-                const uint64_t dds = desc_at(ds_mnmaj, static_cast<uint32_t>(s) * kDsTileBytes);
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks)
-                {
-                    mma(tmem + kDPT + s * 64, desc_at(k_mnmaj, ks * 2048), desc_at(dds, ks * 2048),
-                        idesc_dq, ks > 0 ? 1u : 0u);
-                }
-                commit(&dq_full[s]);
+            const uint64_t k_mnmaj = smem_desc(smem_u32(sk), kHalf, 1024); // K for dQ
+            const uint64_t q_kmaj = smem_desc(smem_u32(sq), 16, 1024);     // Q (stage 0) for S^T
+            const uint64_t q_mnmaj = smem_desc(smem_u32(sq), kHalf, 1024); // Q (stage 0) for dK
+            const uint64_t do_kmaj = smem_desc(smem_u32(sdo), 16, 1024);   // dO for dP^T
+            const uint64_t do_mnmaj = smem_desc(smem_u32(sdo), kHalf, 1024); // dO for dV
+            const uint64_t ds_mnmaj = smem_desc(smem_u32(sds), kHalf, 1024); // dS for dQ
+            auto kmaj_step = [](int ks) {   // k-step of a K-major [128 x 128] tile
+                return static_cast<uint32_t>((ks >> 2) * kHalf + (ks & 3) * 32);
             };
-            for (int it = 0; it < iters; ++it)
-            {
-                const int st = it & 1, sq_i = it % kQStages;
-                const uint32_t stage = static_cast<uint32_t>(sq_i) * kQTileBytes;
-                const uint64_t dq = desc_at(q_kmaj, stage), ddo = desc_at(do_kmaj, stage);
-                mbar_wait(&qd_full[sq_i], (it / kQStages) & 1, p.status, abort);
+            auto issue_s = [&](int i) {
+                const int s = i & 1;
+                mbar_wait(&q_full[s], (i >> 1) & 1, p.status, abort);
                 fence_after();
-                // S^T of buffer st was last read (as P^T / dS^T) by tile it-2's dV / dK products,
-                // issued before these: the MMAs of one thread execute in issue order.
+                const uint64_t dq = desc_at(q_kmaj, static_cast<uint32_t>(s) * kTileBytes);
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
                 {
-                    const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;   // K-major k-step
-                    const uint32_t koff = (ks >> 2) * kHalf + (ks & 3) * 32;
-                    mma(tmem + kST + st * 64, desc_at(k_kmaj, koff), desc_at(dq, off), idesc_s,
+                    mma(tmem + kS, desc_at(k_kmaj, kmaj_step(ks)), desc_at(dq, kmaj_step(ks)), idesc_s,
                         ks > 0 ? 1u : 0u);
                 }
-                // dP^T of buffer st held tile it-2's dQ^T until the drain warps read it out
-                if (it >= 2)
-                {
-                    mbar_wait(&dq_empty[st], ((it - 2) >> 1) & 1, p.status, abort);
-                    fence_after();
-                }
+                commit(s_full);
+            };
+            auto issue_dp_dv = [&](int i) {
+                mbar_wait(do_full, i & 1, p.status, abort);
+                fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
                 {
-                    const uint32_t off = (ks >> 2) * kQHalf + (ks & 3) * 32;
-                    const uint32_t koff = (ks >> 2) * kHalf + (ks & 3) * 32;
-                    mma(tmem + kDPT + st * 64, desc_at(v_kmaj, koff), desc_at(ddo, off), idesc_s,
-                        ks > 0 ? 1u : 0u);
+                    mma(tmem + kDP, desc_at(v_kmaj, kmaj_step(ks)), desc_at(do_kmaj, kmaj_step(ks)),
+                        idesc_s, ks > 0 ? 1u : 0u);
                 }
-                commit(&sp_full[st]);
-                if (it > 0)
+                commit(dp_full);
+                mbar_wait(p_full, i & 1, p.status, abort);   // P^T(i) written over S^T(i)
+                fence_after();
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
                 {
-                    issue_tail(it - 1);
+                    mma_ts(tmem + kDV, tmem + kS + pt_col(ks), desc_at(do_mnmaj, ks * 2048), idesc_kv,
+                           (i > 0 || ks > 0) ? 1u : 0u);
                 }
-            }
+                commit(do_empty);
+            };
+            mbar_wait(kv_full, 0, p.status, abort);
             if (iters > 0)
             {
-                issue_tail(iters - 1);
+                issue_s(0);
+                issue_dp_dv(0);
+            }
+            for (int it = 0; it < iters; ++it)
+            {
+                const int s = it & 1;
+                // S^T(it+1): its columns held P^T(it), read by dV(it), issued before this
+                if (it + 1 < iters)
+                {
+                    issue_s(it + 1);
+                }
+                mbar_wait(ds_full, it & 1, p.status, abort);   // dS^T(it) in TMEM and smem
+                fence_after();
+                const uint64_t dq = desc_at(q_mnmaj, static_cast<uint32_t>(s) * kTileBytes);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+                {
+                    mma_ts(tmem + kDK, tmem + kDP + pt_col(ks), desc_at(dq, ks * 2048), idesc_kv,
+                           (it > 0 || ks > 0) ? 1u : 0u);
+                }
+                commit(&q_empty[s]);
+                // dQ(it) over dP^T / dS^T(it): dK(it), which reads dS^T, was issued first
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+                {
+                    mma(tmem + kDP, desc_at(ds_mnmaj, ks * 2048), desc_at(k_mnmaj, ks * 2048), idesc_dq,
+                        ks > 0 ? 1u : 0u);
+                }
+                commit(dq_full);
+                if (it + 1 < iters)
+                {
+                    mbar_wait(dq_empty, it & 1, p.status, abort);   // dQ(it) read out of TMEM
+                    fence_after();
+                    issue_dp_dv(it + 1);
+                }
             }
             commit(done);
         }
     }
-    else if (warp < 2 + kDrainWarps)
+    else if (warp < kDrainWarps)
     {
-        // dQ^T (lane = dim, column = query) of each tile into the fp32 accumulator
+        regs_inc<kDrainRegs>();
+        // dQ (lane = query, column = dim) of each tile into the fp32 accumulator: the whole
+        // tile leaves TMEM at once (the next dP^T reuses its columns), then 32-dim slices go
+        // through a swizzled shared ring into TMA bulk reduce-adds
         const int quarter = warp & 3;
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-        float* stage = sdq + quarter * (kDqStageBytes / 4);
+        uint8_t* ring = sdq + quarter * 2 * kDqSlice;
+        int g = 0;   // slices issued by this warp
         for (int i = 0; i < iters; ++i)
         {
-            const int s = i & 1;
             const int h = kvh * rep + i / per_head;
-            const int q0 = (qi0 + i % per_head) * kBq;
-            mbar_wait(&dq_full[s], (i >> 1) & 1, p.status, abort);
+            const int q0 = (qi0 + i % per_head) * kFq;
+            mbar_wait(dq_full, i & 1, p.status, abort);
             fence_after();
-            uint32_t v0[32], v1[32];
-            tmem_ld32_async(tmem + lane_base + kDPT + s * 64, v0);
-            tmem_ld32_async(tmem + lane_base + kDPT + s * 64 + 32, v1);
+            uint32_t v[4][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+            {
+                tmem_ld32_async(tmem + lane_base + kDP + c * 32, v[c]);
+            }
             tmem_wait_ld();
-            reg_fence(v0);
-            reg_fence(v1);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+            {
+                reg_fence(v[c]);
+            }
             fence_before();
             __syncwarp();
-            if (lane == 0)
-            {
-                mbar_arrive(&dq_empty[s]);
-                bulk_wait_group_read<0>();   // the previous tile's reduce has read the staging
-            }
-            __syncwarp();
+            if (lane == 0) mbar_arrive(dq_empty);
 #pragma unroll
-            for (int c = 0; c < 32; ++c)
+            for (int c = 0; c < 4; ++c, ++g)
             {
-                stage[c * 32 + lane] = __uint_as_float(v0[c]);
-                stage[(c + 32) * 32 + lane] = __uint_as_float(v1[c]);
-            }
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0)
-            {
-                // rows past T fall outside the tensor map and are not written
-                tma_reduce_add_3d(&tdq, stage, h * 128 + quarter * 32, q0, b);
-                bulk_commit_group();
+                uint8_t* slice = ring + (g & 1) * kDqSlice;
+                if (lane == 0)
+                {
+                    bulk_wait_group_read<1>();   // the reduce that last read this slice is done
+                }
+                __syncwarp();
+                // row = this lane's query, 16-byte chunks XOR-swizzled by the row (128-byte rows)
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                {
+                    *reinterpret_cast<uint4*>(slice + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                        make_uint4(v[c][4 * j], v[c][4 * j + 1], v[c][4 * j + 2], v[c][4 * j + 3]);
+                }
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0)
+                {
+                    // rows past T fall outside the tensor map and are not written
+                    tma_reduce_add_3d(&tdq, slice, h * 128 + c * 32, q0 + quarter * 32, b);
+                    bulk_commit_group();
+                }
             }
         }
         if (lane == 0)
@@ -1079,10 +1188,10 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
             bulk_wait_group<0>();
         }
     }
-    else
+    else if (warp < kDrainWarps + kSoftWarps)
     {
         const int quarter = warp & 3;
-        const int grp = (warp - 2 - kDrainWarps) >> 2;   // query columns [32 grp, 32 grp + 32)
+        const int grp = (warp - kDrainWarps) >> 2;   // query columns [64 grp, 64 grp + 64)
         const int r = quarter * 32 + lane;                 // key row
         const int key = kt * 128 + r;
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
@@ -1090,101 +1199,90 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
         const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
         for (int it = 0; it < iters; ++it)
         {
-            const int st = it & 1, sq_i = it % kQStages;
-            const int q0 = (qi0 + it % per_head) * kBq;
-            // the stage's -LSE log2e / D rows arrive with its Q / dO, before S^T / dP^T
-            mbar_wait(&qd_full[sq_i], (it / kQStages) & 1, p.status, abort);
-            mbar_wait(&sp_full[st], (it >> 1) & 1, p.status, abort);
+            const int s = it & 1;
+            const int q0 = (qi0 + it % per_head) * kFq;
+            const int qg = q0 + grp * 64;   // first query of this warp's columns
+            // Phase 1: P^T. The -LSE log2e rows arrived with Q, before S^T.
+            mbar_wait(&q_full[s], (it >> 1) & 1, p.status, abort);
+            mbar_wait(s_full, it & 1, p.status, abort);
             fence_after();
-            uint32_t sraw[32], draw[32];
-            const uint32_t col = st * 64 + grp * 32;
-            tmem_ld32_async(tmem + lane_base + kST + col, sraw);
-            tmem_ld32_async(tmem + lane_base + kDPT + col, draw);
-            tmem_wait_ld();
-            reg_fence(sraw);
-            reg_fence(draw);
-            uint8_t* stile = sdst + st * kDsTileBytes;
+            // 32 columns at a time; P^T of a half goes to the first 16 of the 32 columns that half
+            // loaded itself, so nothing is overwritten before it is read
+            uint32_t pk[32];   // P^T of the 64 columns as bf16 pairs, kept for phase 2
+            const float* nl = snl + s * kFq + grp * 64;
 #pragma unroll
             for (int half = 0; half < 2; ++half)
             {
-                const int qc = q0 + grp * 32 + half * 16;   // first query of these 16 columns
-                const float* nl = srow + sq_i * 2 * kBq + grp * 32 + half * 16;
-                const float* dd = nl + kBq;
-                const uint32_t* sr = sraw + half * 16;
-                const uint32_t* dr = draw + half * 16;
-                // visible columns c: lo <= c < hi (queries before T and, causal, not before the key)
-                const int hi = qc + 16 > p.T ? (p.T - qc > 0 ? p.T - qc : 0) : 16;
-                const bool causal_tile = p.causal && qc < kt * 128 + 127;   // some key > query here
-                const int lo = causal_tile ? (key - qc > 0 ? key - qc : 0) : 0;
-                uint32_t pk[8], dk[8];
-                if (!causal_tile && hi == 16)
+                uint32_t sraw[32];
+                tmem_ld32_async(tmem + lane_base + kS + grp * 64 + half * 32, sraw);
+                tmem_wait_ld();
+                reg_fence(sraw);
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
                 {
+                    const int qc = qg + 32 * half + 16 * j;
+                    const int hi = qc + 16 > p.T ? (p.T - qc > 0 ? p.T - qc : 0) : 16;
+                    const bool causal_tile = p.causal && qc < kt * 128 + 127;   // a key > a query
+                    const int lo = causal_tile ? (key - qc > 0 ? key - qc : 0) : 0;
+                    float pv[16];
+                    p_block(sraw + 16 * j, nl + 32 * half + 16 * j, pv, !causal_tile && hi == 16, lo,
+                            hi, sc2);
 #pragma unroll
-                    for (int c = 0; c < 16; c += 4)
-                    {
-                        const float4 nl4 = *reinterpret_cast<const float4*>(nl + c);
-                        const float4 d4 = *reinterpret_cast<const float4*>(dd + c);
-#pragma unroll
-                        for (int u = 0; u < 4; u += 2)
-                        {
-                            const int e = c + u;
-                            float p0, p1;
-                            f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[e]), __uint_as_float(sr[e + 1])), sc2,
-                                             u == 0 ? f2_pack(nl4.x, nl4.y) : f2_pack(nl4.z, nl4.w)),
-                                      p0, p1);
-                            p0 = ex2(p0);
-                            p1 = ex2(p1);
-                            const uint64_t t = f2_fma(u == 0 ? f2_pack(d4.x, d4.y) : f2_pack(d4.z, d4.w), neg1,
-                                                      f2_pack(__uint_as_float(dr[e]), __uint_as_float(dr[e + 1])));
-                            float d0, d1;
-                            f2_unpack(f2_mul(f2_pack(p0, p1), t), d0, d1);
-                            pk[e >> 1] = pack2(p0, p1);
-                            dk[e >> 1] = pack2(d0, d1);
-                        }
-                    }
+                    for (int e = 0; e < 8; ++e) pk[16 * half + 8 * j + e] = pack2(pv[2 * e], pv[2 * e + 1]);
                 }
-                else
-                {
+                tmem_st16_async(tmem + lane_base + kS + grp * 64 + half * 16,
+                                *reinterpret_cast<uint32_t(*)[16]>(pk + 16 * half));
+            }
+            tmem_wait_st();
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+            // Phase 2: dS^T. D arrived with Q; the dS^T tile's last reader, dQ(it-1), completed
+            // before the drain released dQ(it-1), which came before dP^T(it).
+            mbar_wait(dp_full, it & 1, p.status, abort);
+            fence_after();
+            // this warp's 64 queries are the 128-byte row r of half grp of the dS^T tile
+            uint8_t* row = sds + grp * kHalf;
 #pragma unroll
-                    for (int c = 0; c < 16; c += 2)
+            for (int half = 0; half < 2; ++half)
+            {
+                uint32_t draw[32];
+                tmem_ld32_async(tmem + lane_base + kDP + grp * 64 + half * 32, draw);
+                tmem_wait_ld();
+                reg_fence(draw);
+                uint32_t dk[16];
+#pragma unroll
+                for (int c = 0; c < 32; c += 4)
+                {
+                    const float4 d4 = *reinterpret_cast<const float4*>(sdv + s * kFq + grp * 64 + half * 32 + c);
+#pragma unroll
+                    for (int u = 0; u < 4; u += 2)
                     {
-                        const float2 nl2 = *reinterpret_cast<const float2*>(nl + c);
-                        const float2 d2 = *reinterpret_cast<const float2*>(dd + c);
-                        float p0, p1;
-                        f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc2,
-                                         f2_pack(nl2.x, nl2.y)),
-                                  p0, p1);
-                        const bool v0 = c >= lo && c < hi;
-                        const bool v1 = c + 1 >= lo && c + 1 < hi;
-                        p0 = v0 ? ex2(p0) : 0.0f;
-                        p1 = v1 ? ex2(p1) : 0.0f;
-                        const uint64_t t = f2_fma(f2_pack(d2.x, d2.y), neg1,
-                                                  f2_pack(__uint_as_float(dr[c]), __uint_as_float(dr[c + 1])));
+                        // masked columns have P = 0, so dS = 0 (D and dP^T are finite there)
+                        const uint64_t t = f2_fma(u == 0 ? f2_pack(d4.x, d4.y) : f2_pack(d4.z, d4.w), neg1,
+                                                  f2_pack(__uint_as_float(draw[c + u]),
+                                                          __uint_as_float(draw[c + u + 1])));
+                        // dS from the bf16 P the dV product uses (the pair's low half is the even column)
+                        const uint32_t pp = pk[16 * half + ((c + u) >> 1)];
                         float d0, d1;
-                        f2_unpack(f2_mul(f2_pack(p0, p1), t), d0, d1);
-                        d0 = v0 ? d0 : 0.0f;   // masked columns may hold stale -LSE / D values
-                        d1 = v1 ? d1 : 0.0f;
-                        pk[c >> 1] = pack2(p0, p1);
-                        dk[c >> 1] = pack2(d0, d1);
+                        f2_unpack(f2_mul(f2_pack(__uint_as_float(pp << 16), __uint_as_float(pp & 0xFFFF0000u)), t),
+                                  d0, d1);
+                        dk[(c + u) >> 1] = pack2(d0, d1);
                     }
                 }
-                // every S^T / dP^T column of this warp is in registers: overwrite in place
-                const uint32_t pc = kST + st * 64 + pt_col(2 * grp + half);
-                tmem_st8_async(tmem + lane_base + pc, pk);
-                tmem_st8_async(tmem + lane_base + pc + 16, dk);
-                // dS^T row piece into the swizzled tile the dQ^T product reads. Its last reader, tile
-                // it-2's dQ^T product, was issued before this tile's S^T / dP^T products, so the
-                // sp_full signal (which covers every earlier product) saw it complete.
-                *reinterpret_cast<uint4*>(stile + sw128_offset(r, grp * 4 + half * 2)) =
-                    make_uint4(dk[0], dk[1], dk[2], dk[3]);
-                *reinterpret_cast<uint4*>(stile + sw128_offset(r, grp * 4 + half * 2 + 1)) =
-                    make_uint4(dk[4], dk[5], dk[6], dk[7]);
+                tmem_st16_async(tmem + lane_base + kDP + grp * 64 + half * 16, dk);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                {
+                    *reinterpret_cast<uint4*>(row + sw128_offset(r, 4 * half + c)) =
+                        make_uint4(dk[4 * c], dk[4 * c + 1], dk[4 * c + 2], dk[4 * c + 3]);
+                }
             }
             fence_proxy_async();
             tmem_wait_st();
             fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&ds_full[st]);
+            if (lane == 0) mbar_arrive(ds_full);
         }
         // dV and dK rows of this key (summed over the group's heads in TMEM): 64 dims per warp
         mbar_wait(done, 0, p.status, abort);
@@ -1216,9 +1314,13 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
             }
         }
     }
+    else if (warp > kMmaWarp)
+    {
+        regs_dec<kIssueRegs>();   // the idle warps of the TMA / MMA warpgroup
+    }
     fence_before();
     __syncthreads();
-    if (warp == 1)
+    if (warp == kMmaWarp)
     {
         fence_after();
         tmem_dealloc(tmem, 512);
@@ -1519,8 +1621,8 @@ bool make_map3(CUtensorMap* map, const void* base, int64_t width, int64_t T, int
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// [B, T, width] fp32 (row stride width) with an unswizzled box of box_w columns x box_rows rows,
-// for bulk reduce-adds from shared memory.
+// [B, T, width] fp32 (row stride width) with a box of 32 columns (128-byte rows, 128-byte swizzle
+// in shared memory) x box_rows rows, for bulk reduce-adds from shared memory.
 bool make_map3_f32(CUtensorMap* map, void* base, int64_t width, int64_t T, int64_t B,
                    uint32_t box_w, uint32_t box_rows)
 {
@@ -1536,7 +1638,7 @@ bool make_map3_f32(CUtensorMap* map, void* base, int64_t width, int64_t T, int64
     const cuuint32_t box[3] = {box_w, box_rows, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -1607,11 +1709,14 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     {
         return -1;
     }
+    // Q and dO tiles: 128 query rows for the fused kernel, 64 for the two-kernel path
+    const bool det = attention_deterministic() != 0;
+    const uint32_t qrows = det ? kBq : kFq;
     CUtensorMap mq, mk, mv, mdo, mds;
-    if (!make_map3(&mq, q, H * 128, T, B, ldq, kBq) || !make_map3(&mk, k, Hkv * 128, T, B, ldk, 128) ||
+    if (!make_map3(&mq, q, H * 128, T, B, ldq, qrows) || !make_map3(&mk, k, Hkv * 128, T, B, ldk, 128) ||
         !make_map3(&mv, v, Hkv * 128, T, B, ldv, 128) ||
-        !make_map3(&mdo, dout, H * 128, T, B, lddo, kBq) || !aligned16(dvec) || !aligned16(extra) ||
-        (attention_deterministic() && !make_map3(&mds, extra, T, T, B * H, T, 128)))
+        !make_map3(&mdo, dout, H * 128, T, B, lddo, qrows) || !aligned16(dvec) || !aligned16(extra) ||
+        (det && !make_map3(&mds, extra, T, T, B * H, T, 128)))
     {
         return -1;   // caller falls back
     }
@@ -1627,11 +1732,11 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     }
     float* nlse2 = reinterpret_cast<float*>(static_cast<char*>(extra) + tc_bwd_ds_bytes(B, T, H));
     const dim3 grid(static_cast<unsigned>(B * Hkv), static_cast<unsigned>((T + 127) / 128));
-    if (!attention_deterministic())
+    if (!det)
     {
         float* dqacc = static_cast<float*>(extra);
         CUtensorMap mdq;
-        if (!make_map3_f32(&mdq, dqacc, H * 128, T, B, 32, kBq))
+        if (!make_map3_f32(&mdq, dqacc, H * 128, T, B, 32, 32))
         {
             return -1;
         }
