@@ -70,12 +70,14 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_gpu{gpu_index}.csv"
+        self.path = None
 
     def start(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
-            self.f = open(self.path, "w")
+            import tempfile
+            self.f = tempfile.NamedTemporaryFile("w+", prefix=f"veda_clocks_gpu{self.gpu}_",
+                                                 suffix=".csv", delete=False)
+            self.path = Path(self.f.name)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200", "-i", str(self.gpu)], stdout=self.f, stderr=subprocess.DEVNULL)
@@ -92,7 +94,12 @@ class ClockSampler:
             self.proc.kill()
         self.f.close()
         rows = []
-        for line in self.path.read_text().splitlines():
+        text = self.path.read_text()
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
+        for line in text.splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -289,7 +296,7 @@ def run_veda(args):
                    "gbs": (v[2] / (v[0] / 1000.0) / 1e9) if v[2] and v[0] else None}
                for k, v in sorted(prof.items())}
     # DRAM bytes (read + write) per GEMM launch, averaged over the 339 GEMM launches of one step,
-    # from one ncu capture: profiles/gemm_dram_traffic_qwen3_0.6b_b4t2048.md
+    # from one ncu capture of the same step
     traffic = GEMM_DRAM_BYTES_PER_LAUNCH.get(args.workload)
 
     line = {

@@ -16,7 +16,7 @@
  * The reference (pictaile/veda) has no C ABI: its boundary is the C++ autograd API of
  * src/libs/autograd/Variable.h:69-119. Each entry point names the reference function whose
  * arithmetic it carries. The C++ host library (include/veda/*.hpp) calls these and turns status
- * codes into the reference's exception types (see INTEGRATION.md).
+ * codes into the reference's exception types.
  */
 #ifndef VEDA_CUDA_H
 #define VEDA_CUDA_H

@@ -33,10 +33,11 @@ class VrefAdamConfig(C.Structure):
 
 
 def build(ref_dir: str | None = None) -> bool:
-    """Run oracle/Makefile when the reference checkout is present. Returns True if built."""
+    """Run oracle/Makefile when the reference checkout (ref_dir, else $VEDA_REF_DIR) is present.
+    Returns True if the library exists afterwards."""
     import subprocess
-    ref_dir = ref_dir or os.environ.get("VEDA_REF_DIR", "/root/reference")
-    if not Path(ref_dir, "src", "libs", "autograd", "Variable.cpp").exists():
+    ref_dir = ref_dir or os.environ.get("VEDA_REF_DIR")
+    if not ref_dir or not Path(ref_dir, "src", "libs", "autograd", "Variable.cpp").exists():
         return LIB_PATH.exists()
     subprocess.run(["make", "-s", "-C", str(_HERE), f"VEDA_REF_DIR={ref_dir}",
                     f"-j{os.cpu_count() or 4}"], check=True)

@@ -10,7 +10,7 @@ import pytest
 
 import veda_b200 as V
 from oracle import veda_oracle as O
-from tests.gpu_util import (bf, call, dev, empty, host, ptr, rel, stream, sync, workspace,
+from tests.gpu_util import (bf, call, dev, empty, host, ptr, rel, stream, sync, torch, workspace,
                             zeros)
 
 pytestmark = pytest.mark.gpu
@@ -463,6 +463,84 @@ def test_gemm_fp32_small_shapes(op):
          V.F32, V.F32, 1.0, 0.0, stream())
     sync()
     assert rel(host(c), am @ bm) <= 1e-6
+
+
+@pytest.mark.parametrize("M,K,N", [(8192, 2048, 6144), (8192, 1024, 151936)])
+def test_matmul_backward_sweep_shapes_against_fp64(M, K, N):
+    """The two largest shapes of the isolated matmul-backward sweep: dX = dY W^T (NT) and
+    dW = X^T dY (TN), bf16 inputs ~ N(0,1)/sqrt(K) (seed 1), fp32 outputs, checked against fp64
+    products on a slab of dX rows and a slab of dW columns (src/libs/autograd/Variable.cpp:325-346
+    is the reference's backward of matmul_nt)."""
+    t = torch()
+    g = t.Generator(device="cuda").manual_seed(1)
+    x = (t.randn(M, K, device="cuda", generator=g) / math.sqrt(K)).to(t.bfloat16)
+    w = (t.randn(K, N, device="cuda", generator=g) / math.sqrt(K)).to(t.bfloat16)
+    dy = (t.randn(M, N, device="cuda", generator=g) / math.sqrt(K)).to(t.bfloat16)
+    dx = t.empty(M, K, dtype=t.float32, device="cuda")
+    dw = t.empty(K, N, dtype=t.float32, device="cuda")
+    call("veda_gemm_nt", M, K, N, dy.data_ptr(), N, w.data_ptr(), N, dx.data_ptr(), K, V.BF16, V.F32,
+         1.0, 0.0, stream())
+    call("veda_gemm_tn", K, N, M, x.data_ptr(), K, dy.data_ptr(), N, dw.data_ptr(), N, V.BF16, V.F32,
+         1.0, 0.0, stream())
+    sync()
+    rows = t.arange(0, M, M // 16, device="cuda")
+    cols = t.arange(0, N, max(1, N // 64), device="cuda")
+    ref_dx = (dy[rows].double() @ w.double().T).cpu().numpy()
+    ref_dw = (x.double().T @ dy[:, cols].double()).cpu().numpy()
+    assert rel(dx[rows].double().cpu().numpy(), ref_dx) <= 1e-4
+    assert rel(dw[:, cols].double().cpu().numpy(), ref_dw) <= 1e-4
+
+
+@pytest.mark.parametrize("op,dtype,M,N,K", [(0, V.BF16, 70, 136, 48), (1, V.BF16, 70, 136, 48),
+                                            (2, V.BF16, 70, 136, 48), (1, V.F32, 70, 136, 48),
+                                            (0, V.BF16, 256, 384, 128), (1, V.BF16, 256, 384, 128),
+                                            (2, V.BF16, 256, 384, 128)])
+def test_gemm_batched_against_oracle(op, dtype, M, N, K):
+    """veda_gemm_batched, the products of autograd::matmul on batched operands (P.V of attention
+    and its backward: src/libs/autograd/Variable.cpp:300-323), with an operand broadcast over the
+    batch (stride 0, the weight of a batched matmul): every batch entry against numpy. Ragged
+    shapes take the CUDA-core kernel, 16-byte-aligned ones the tensor-core kernel."""
+    r = rng(21 + op)
+    batch = 3
+    shp_a = (batch, K, M) if op == 2 else (batch, M, K)
+    shp_b = (N, K) if op == 0 else (K, N)        # broadcast over the batch
+    a = r.standard_normal(shp_a).astype(F32)
+    b = r.standard_normal(shp_b).astype(F32)
+    c0 = r.standard_normal((batch, M, N)).astype(F32)
+    if dtype == V.BF16:
+        a, b = bf(a), bf(b)
+    ad, bd = dev(a, dtype), dev(b, dtype)
+    c = dev(c0)
+    lda = shp_a[2]
+    ldb = shp_b[1]
+    call("veda_gemm_batched", op, batch, M, N, K, ptr(ad), lda, M * K, ptr(bd), ldb, 0, ptr(c), N,
+         M * N, dtype, V.F32, 0.5, 1.0, stream())
+    sync()
+    am = np.transpose(a, (0, 2, 1)) if op == 2 else a
+    bm = b.T if op == 0 else b
+    want = 0.5 * (am.astype(np.float64) @ bm.astype(np.float64)) + c0
+    assert rel(host(c), want) <= (1e-5 if dtype == V.F32 else 1e-4)
+
+
+@pytest.mark.parametrize("dtype", [V.F32, V.BF16])
+def test_scale_and_accumulate(dtype):
+    """veda_scale (autograd::mul by a scalar, src/libs/autograd/Variable.cpp:241-258) and
+    veda_accumulate (the gradient += of Variable.cpp:27-38), fp32 and bf16, ragged length."""
+    r = rng(5)
+    n = 100003
+    x = r.standard_normal(n).astype(F32)
+    d0 = r.standard_normal(n).astype(F32)
+    if dtype == V.BF16:
+        x = bf(x)
+    xd = dev(x, dtype)
+    out = empty(n, dtype)
+    call("veda_scale", ptr(xd), 0.125, ptr(out), n, dtype, stream())
+    dst = dev(d0)
+    call("veda_accumulate", ptr(dst), V.F32, ptr(xd), dtype, n, stream())
+    sync()
+    want = x * np.float32(0.125)
+    assert np.array_equal(host(out), bf(want) if dtype == V.BF16 else want)   # exact: a power of 2
+    assert np.array_equal(host(dst), d0 + x)
 
 
 # ---------------------------------------------------------------------------------------------

@@ -104,7 +104,8 @@ def test_golden_tiny_step(tiny):
     assert abs(norm - tiny["norm"][0]) <= 1e-5 * abs(norm)
     for i in range(n):
         close(grads[i], tiny[f"g_{i:03d}"], 1e-5)
-        # updated weights: see DESIGN.md on elements whose gradient is ~eps
+        # updated weights: AdamW's g / (sqrt(v) + eps) turns last-bit gradient differences into
+        # visible weight differences where |g| is about eps, hence the looser bound
         close(params[i], tiny[f"w1_{i:03d}"], 2e-4)
 
 

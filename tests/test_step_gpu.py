@@ -85,8 +85,19 @@ QWEN_WIDE = O.ModelConfig(vocab=2048, hidden=2048, intermediate=6144, layers=1, 
                           kv_heads=8, head_dim=128, eps=1e-6, theta=1e6)
 
 
-@pytest.mark.parametrize("cfg,B,T", [(QWEN_SMALL, 2, 128), (QWEN_WIDE, 1, 128)])
+# the full Qwen3-0.6B width and vocabulary (d_model 1024, SwiGLU 3072, 16/8 heads, head_dim 128,
+# vocab 151936 with the tied embedding) at two layers
+QWEN06_FULL_WIDTH = O.ModelConfig(vocab=151936, hidden=1024, intermediate=3072, layers=2, heads=16,
+                                  kv_heads=8, head_dim=128, eps=1e-6, theta=1e6)
+
+
+@pytest.mark.parametrize("cfg,B,T", [(QWEN_SMALL, 2, 128), (QWEN_WIDE, 1, 128),
+                                     (QWEN06_FULL_WIDTH, 1, 512)])
 def test_qwen_shaped_bf16_step_matches_oracle(cfg, B, T):
+    """One bf16 step (forward, cross-entropy, backward, clip, AdamW) against the oracle's fp32
+    step on the same bf16-rounded weights and batch (src/libs/train/Model.cpp:206-255,
+    src/libs/autograd/Loss.cpp:18-103, src/libs/optim/AdamW.cpp:38-93): loss, norm, every
+    gradient and every updated weight. The last case is the Qwen3-0.6B width and vocabulary."""
     params = O.init_params(cfg, 3, bf16=True)
     ids, tg = O.synthetic_batch(cfg, B, T, 3)
     t = make_trainer(cfg, 1, B, T)
