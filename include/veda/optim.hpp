@@ -56,6 +56,11 @@ public:
     const core::Tensor& second_moments() const noexcept { return v_arena_; }
     // Restores the step count (the bias corrections of the next step use steps + 1).
     void set_steps(size_t steps) noexcept { steps_ = steps; }
+    // On: a clipped step whose global norm is not finite updates nothing (weights, moments and
+    // gradients are left as they were); the caller, who reads the norm, then takes the step back
+    // with set_steps(steps() - 1). Off (the default, the reference's behaviour): the step runs.
+    void set_skip_nonfinite(bool on) noexcept { skip_nonfinite_ = on; }
+    bool skip_nonfinite() const noexcept { return skip_nonfinite_; }
     const std::vector<autograd::Variable>& parameters() const noexcept { return parameters_; }
     // fp32 master weights of parameter i (the value itself for fp32 parameters).
     core::Tensor master(size_t i) const { return masters_[i]; }
@@ -63,6 +68,7 @@ public:
     size_t runs() const noexcept { return runs_.size(); }
 
 private:
+    bool skip_nonfinite_ = false;
     struct Run
     {
         size_t first, count;

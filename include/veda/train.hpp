@@ -134,6 +134,7 @@ struct StepStats
 {
     float loss = 0.0f;
     float grad_norm = 0.0f;
+    bool skipped = false;   // set_skip_nonfinite: the norm was not finite and nothing was updated
 };
 
 class Trainer
@@ -179,8 +180,21 @@ public:
     void set_step_graph(bool on);
     // One step from host buffers: copies in, steps, reads loss and grad norm back (synchronous).
     StepStats step_host(const int64_t* ids, const int64_t* targets);
-    // Loss and pre-clip grad norm of the last step (synchronises).
+    // Loss and pre-clip grad norm of the last step (synchronises). Data-parallel, the wait polls
+    // the stream and the communicator (ncclCommGetAsyncError) instead of blocking: an error, or
+    // no progress within the communication timeout, aborts the communicator (ncclCommAbort) and
+    // throws std::runtime_error instead of hanging on a failed peer.
     StepStats last_stats();
+    // Data-parallel: the communication timeout of those waits (default 600 s, or
+    // VEDA_DP_TIMEOUT_S).
+    void set_comm_timeout(double seconds);
+    // Data-parallel: abort the communicator without waiting for the peers (for a caller that has
+    // learned on the host that a peer is gone); every later step throws.
+    void abort_communication();
+    // On: a step whose global gradient norm is not finite updates nothing, last_stats() reports
+    // it as skipped, and the step is not counted (the next uses the same bias corrections).
+    // Off (the default): the reference's behaviour, the update runs with the unclipped gradient.
+    void set_skip_nonfinite(bool on);
 
     TinyTransformer& model() noexcept { return *model_; }
     optim::AdamW& optimizer() noexcept { return *opt_; }
@@ -201,6 +215,7 @@ private:
     int64_t graph_launches_ = 0;
     int eager_steps_ = 0;
     bool use_graph_ = true;
+    bool skip_nonfinite_ = false;
     void* capture_stream_ = nullptr;   // cudaStream_t the step is captured on
 };
 

@@ -57,6 +57,11 @@ int veda_launch_count_add(int64_t n);
  * is a device variable compiled into the library (one per GPU, never allocated); its address is
  * looked up once per device and cached, so after a cudaDeviceReset use a fresh process. */
 int veda_kernel_status(int reset);
+/* Diagnostic of the bounded waits: one CTA waits, through the same bounded mbarrier wait the
+ * tensor-core and streaming kernels use, on a barrier nothing arrives on, giving up after
+ * budget_cycles (at most 2^32, the kernels' own budget, about two seconds) with VEDA_ERR_TIMEOUT
+ * in the status word; nothing else is in flight. No counterpart in the reference. */
+int veda_wait_timeout_check(long long budget_cycles, veda_stream_t stream);
 /* Number of SMs the persistent kernels (tensor-core GEMMs, streaming RMSNorm) leave free for
  * work running beside them, such as NCCL all-reduce blocks during a data-parallel backward;
  * 0 (the default) uses every SM. Process-wide; returns the previous value. No counterpart in
@@ -218,8 +223,12 @@ int veda_clip_apply(float* g, int64_t n, const double* sumsq, float max_norm,
  *   w -= lr*wd*w;  w -= lr * float((m/bias1) / (sqrt(v/bias2) + eps))  (m_hat, v_hat in double)
  * bias1 = 1 - beta1^t, bias2 = 1 - beta2^t computed by the caller in double.
  * lowp (bf16 [n], may be NULL) receives the rounded copy the forward reads.
- * write_grad = 1 leaves g' in g (the clipped gradient, as Clip.cpp:52-58 leaves it); the store
- * is skipped when g' == g (no clip and grad_scale 1). */
+ * write_grad is a set of bits. Bit 0 (1) leaves g' in g (the clipped gradient, as Clip.cpp:52-58
+ * leaves it); the store is skipped when g' == g (no clip and grad_scale 1). Bit 1
+ * (VEDA_ADAMW_SKIP_NONFINITE) leaves master, m, v, g and lowp untouched when the norm
+ * float(sqrt(*sumsq) * |grad_scale|) is not finite: the step is skipped (the reference has no
+ * skip; its clip only declines to scale a non-finite norm, Clip.cpp:36-40). */
+#define VEDA_ADAMW_SKIP_NONFINITE 2
 int veda_adamw_step(float* master, float* m, float* v, float* g, void* lowp, int64_t n, float lr,
                     float beta1, float beta2, float eps, float weight_decay, double bias1,
                     double bias2, const double* sumsq, float max_norm, float grad_scale,

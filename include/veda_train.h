@@ -121,8 +121,24 @@ int veda_trainer_step_host(veda_trainer* t, const int64_t* ids, const int64_t* t
                            float* loss, float* grad_norm);
 /* One step on device-resident ids/targets; asynchronous on the current stream. */
 int veda_trainer_step_device(veda_trainer* t, const int64_t* ids, const int64_t* targets);
-/* Loss and grad norm of the last step (synchronises). */
+/* Loss and grad norm of the last step (synchronises). Data-parallel, the wait polls the stream and
+ * the NCCL communicator (ncclCommGetAsyncError) instead of blocking: an asynchronous error, or no
+ * progress within the communication timeout, aborts the communicator (ncclCommAbort) and returns
+ * an error instead of hanging on a failed peer. */
 int veda_trainer_last_stats(veda_trainer* t, float* loss, float* grad_norm);
+
+/* Failure handling (no reference counterpart: the reference is one CPU process).
+ * set_comm_timeout: the data-parallel communication timeout of those waits in seconds (default
+ * 600, or VEDA_DP_TIMEOUT_S). abort_comm: aborts the communicator without waiting for the peers,
+ * for a caller that has learned on the host (a heartbeat, a store) that a peer is gone; every
+ * later step returns an error. set_skip_nonfinite (default off, the reference's behaviour): on,
+ * a step whose global gradient norm is not finite updates nothing and is not counted (the next
+ * uses the same bias corrections); step_skipped reports whether the step read by the last
+ * step_host / last_stats was such a step. */
+int veda_trainer_set_comm_timeout(veda_trainer* t, double seconds);
+int veda_trainer_abort_comm(veda_trainer* t);
+int veda_trainer_set_skip_nonfinite(veda_trainer* t, int on);
+int veda_trainer_step_skipped(veda_trainer* t, int* skipped);
 
 /* Device-time profile of kernel classes (gemm_fwd, gemm_dx, gemm_dw, attn_fwd, attn_bwd,
  * cross_entropy, rmsnorm_bwd, swiglu_bwd, adamw), recorded with CUDA events while enabled. */

@@ -95,5 +95,55 @@ def main():
     dist.destroy_process_group()
 
 
+def lost_peer():
+    """Rank 1 leaves between steps (after a host barrier: none of its work is in flight). Rank 0
+    learns of it on the host (a monitored barrier that times out) before its next launch, aborts
+    its communicator without waiting for the peer, gets an error from the next step instead of a
+    hang, and its CUDA context still runs kernels."""
+    import torch
+    import torch.distributed as dist
+    from oracle import veda_oracle as O
+    from veda_b200 import train_abi as TA
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+    cfg = O.ModelConfig(vocab=2048, hidden=256, intermediate=512, layers=2, heads=4, kv_heads=2,
+                        head_dim=128, eps=1e-6, theta=1e6)
+    B, T = 2, 128
+    ids, tg = O.synthetic_batch(cfg, B * world, T, 7)
+    mine = slice(B * rank, B * rank + B)
+    t = TA.Trainer(cfg, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, max_norm=1.0,
+                   dtype=1, batch=B, seq_len=T, seed=3)
+    uid = [TA.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    t.init_dp(uid[0], rank, world, 1 << 20)
+    t.set_comm_timeout(30.0)
+    t.step_host(ids[mine], tg[mine])          # one healthy step; last_stats waited for it
+    dist.barrier()                            # both ranks are past the step: nothing in flight
+    if rank == 1:
+        os._exit(0)                           # the rank leaves between steps
+    try:
+        dist.monitored_barrier(timeout=datetime.timedelta(seconds=10))
+        print("LOST PEER NOT DETECTED", flush=True)
+        os._exit(1)
+    except Exception:  # noqa: BLE001 - the host learns the peer is gone
+        pass
+    t.abort_comm()                            # nothing of ours is in flight either
+    try:
+        t.step_host(ids[mine], tg[mine])
+        print("STEP AFTER ABORT DID NOT FAIL", flush=True)
+        os._exit(1)
+    except RuntimeError as e:
+        assert "abort" in str(e), str(e)
+    x = torch.ones(1 << 20, device="cuda")    # the context still runs kernels
+    assert float(x.sum().item()) == float(1 << 20)
+    print("LOST PEER OK", flush=True)
+    os._exit(0)
+
+
 if __name__ == "__main__":
-    main()
+    if os.environ.get("VEDA_DP_MODE") == "lost_peer":
+        lost_peer()
+    else:
+        main()

@@ -134,6 +134,23 @@ def test_nccl_two_gpus_match_full_batch():
 
 
 @pytest.mark.gpu
+@pytest.mark.timeout(600)
+def test_nccl_two_gpus_lost_peer_is_detected_and_aborted():
+    """A rank leaves between steps; the survivor learns of it on the host, aborts its NCCL
+    communicator (nothing in flight), gets an error from its next step instead of a hang, and
+    keeps a working CUDA context. NVLS is off (no multicast memory bound to the leaving rank)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=str(ROOT), VEDA_DP_MODE="lost_peer")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+           "--master-port", str(_free_port()), str(ROOT / "tests" / "dp_worker.py")]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=str(ROOT))
+    assert "LOST PEER OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.gpu
 @pytest.mark.timeout(900)
 def test_nccl_two_gpus_graph_replay_matches_eager(tmp_path):
     """The data-parallel steps captured into CUDA graphs (VEDA_DP_GRAPH=1; NCCL calls inside the

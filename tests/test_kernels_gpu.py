@@ -767,3 +767,20 @@ def test_randn_statistics():
     sync()
     h = host(x)
     assert abs(h.mean()) < 1e-4 and abs(h.std() - 0.02) < 2e-4
+
+
+def test_bounded_wait_gives_up_with_timeout_status_and_context_survives():
+    """The bounded mbarrier wait of the tensor-core and streaming kernels, driven to its limit on a
+    barrier nothing arrives on (veda_wait_timeout_check, a small spin budget): the device status
+    word reads VEDA_ERR_TIMEOUT, the reset clears it, and the context still runs kernels."""
+    lib = V.lib()
+    lib.veda_kernel_status(1)
+    call("veda_wait_timeout_check", 1 << 20, stream())
+    torch().cuda.synchronize()
+    assert lib.veda_kernel_status(1) == V.ERR_TIMEOUT
+    assert lib.veda_kernel_status(0) == 0
+    x = dev(np.arange(1000, dtype=F32))
+    out = empty(1000)
+    call("veda_scale", ptr(x), 2.0, ptr(out), 1000, V.F32, stream())
+    sync()
+    assert np.array_equal(host(out), np.arange(1000, dtype=F32) * 2)

@@ -190,6 +190,37 @@ def test_checkpoint_resume_is_bit_exact(tmp_path):
         x.close()
 
 
+def test_nonfinite_step_is_skipped_and_not_counted():
+    """set_skip_nonfinite: a step whose gradient norm is not finite (here an infinite final-norm
+    gain makes the loss NaN) updates nothing and is reported as skipped; the step after it, with
+    finite weights again, equals a fresh trainer's first step bit for bit (the skipped step was
+    not counted, so the bias corrections are those of step 1)."""
+    cfg = O.TINY
+    ids, tg = O.synthetic_batch(cfg, 4, 32, 0)
+    flat = np.concatenate([p.ravel() for p in O.init_params(cfg, 0)])
+    bad = flat.copy()
+    names = [name for name, _ in O.param_specs(cfg)]
+    at = sum(int(np.prod(shape)) for name, shape in O.param_specs(cfg)[:names.index("model.norm.weight")])
+    bad[at] = np.inf
+    t = make_trainer(cfg, 0, 4, 32)
+    t.set_skip_nonfinite(True)
+    t.set_params(bad)
+    loss, norm = t.step_host(ids, tg)
+    assert not math.isfinite(norm) and t.step_skipped()
+    got = t.get_params()
+    assert np.array_equal(got[np.isfinite(got)], bad[np.isfinite(bad)])   # nothing was updated
+    t.set_params(flat)
+    loss2, norm2 = t.step_host(ids, tg)
+    assert math.isfinite(norm2) and not t.step_skipped()
+    fresh = make_trainer(cfg, 0, 4, 32)
+    fresh.set_params(flat)
+    loss3, norm3 = fresh.step_host(ids, tg)
+    assert loss2 == loss3 and norm2 == norm3
+    assert np.array_equal(t.get_params(), fresh.get_params())
+    t.close()
+    fresh.close()
+
+
 @pytest.mark.parametrize("dtype", [0, 1])
 def test_step_graph_replay_matches_eager(dtype):
     """A trainer replaying its step from a CUDA graph (captured at the second step) gives the same

@@ -35,6 +35,7 @@ SIGNATURES = {
     "veda_device_info": (_i, [_p, _p, _p]),
     "veda_launch_count": (_u64, []),
     "veda_kernel_status": (_i, [_i]),
+    "veda_wait_timeout_check": (_i, [C.c_longlong, _p]),
     "veda_set_reserved_sms": (_i, [_i]),
     "veda_gemm_nt": (_i, [_i64, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _i, _f, _f, _p]),
     "veda_gemm_nn": (_i, [_i64, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _i, _f, _f, _p]),

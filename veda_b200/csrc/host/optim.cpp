@@ -149,7 +149,9 @@ void AdamW::launch(const double* sumsq, float max_norm, float grad_scale)
     {
         check(veda_adamw_step_dev(r.master, r.m, r.v, r.grad, r.lowp, r.n, config_.learning_rate,
                                   config_.beta1, config_.beta2, config_.eps, config_.weight_decay,
-                                  bias, sumsq, max_norm, grad_scale, 0, current_stream()),
+                                  bias, sumsq, max_norm, grad_scale,
+                                  skip_nonfinite_ && sumsq != nullptr ? VEDA_ADAMW_SKIP_NONFINITE : 0,
+                                  current_stream()),
               "AdamW::step");
     }
 }

@@ -21,6 +21,7 @@
 struct veda_trainer
 {
     std::unique_ptr<veda::train::Trainer> impl;
+    int last_skipped = 0;   // the step read by the last step_host / last_stats was skipped
 };
 
 namespace
@@ -348,6 +349,7 @@ int veda_trainer_step_host(veda_trainer* t, const int64_t* ids, const int64_t* t
         const auto s = t->impl->step_host(ids, targets);
         if (loss) *loss = s.loss;
         if (grad_norm) *grad_norm = s.grad_norm;
+        t->last_skipped = s.skipped ? 1 : 0;
     });
 }
 
@@ -372,6 +374,29 @@ int veda_trainer_last_stats(veda_trainer* t, float* loss, float* grad_norm)
         const auto s = t->impl->last_stats();
         if (loss) *loss = s.loss;
         if (grad_norm) *grad_norm = s.grad_norm;
+        t->last_skipped = s.skipped ? 1 : 0;
+    });
+}
+
+int veda_trainer_set_comm_timeout(veda_trainer* t, double seconds)
+{
+    return guarded([&] { t->impl->set_comm_timeout(seconds); });
+}
+
+int veda_trainer_abort_comm(veda_trainer* t)
+{
+    return guarded([&] { t->impl->abort_communication(); });
+}
+
+int veda_trainer_set_skip_nonfinite(veda_trainer* t, int on)
+{
+    return guarded([&] { t->impl->set_skip_nonfinite(on != 0); });
+}
+
+int veda_trainer_step_skipped(veda_trainer* t, int* skipped)
+{
+    return guarded([&] {
+        if (skipped) *skipped = t->last_skipped;
     });
 }
 

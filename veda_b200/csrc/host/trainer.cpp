@@ -16,6 +16,8 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include "watchdog.hpp"
+
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -43,24 +45,38 @@ void cuda_check(cudaError_t e, const char* what)
     }
 }
 
-void nccl_check(ncclResult_t r, const char* what)
-{
-    if (r != ncclSuccess)
-    {
-        throw std::runtime_error(std::string(what) + ": " + ncclGetErrorString(r));
-    }
-}
 } // namespace
 
 class DataParallel
 {
 public:
+    // The communicator comes from ncclCommInitRankConfig: VEDA_NCCL_NONBLOCKING=1 makes it
+    // non-blocking (every call is then settled by polling ncclCommGetAsyncError, bounded by the
+    // communication timeout); VEDA_NCCL_MAX_CTAS / VEDA_NCCL_MIN_CTAS bound the blocks NCCL's
+    // kernels take (the SMs they share with the backward's kernels).
     DataParallel(const void* unique_id, int rank, int world, bool sharded)
         : rank_(rank), world_(world), sharded_(sharded)
     {
         ncclUniqueId id;
         std::memcpy(&id, unique_id, sizeof(id));
-        nccl_check(ncclCommInitRank(&comm_, world, id, rank), "ncclCommInitRank");
+        ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+        if (const char* v = std::getenv("VEDA_NCCL_NONBLOCKING"); v != nullptr && std::atoi(v) != 0)
+        {
+            config.blocking = 0;
+        }
+        if (const char* v = std::getenv("VEDA_NCCL_MAX_CTAS"); v != nullptr && std::atoi(v) > 0)
+        {
+            config.maxCTAs = std::atoi(v);
+        }
+        if (const char* v = std::getenv("VEDA_NCCL_MIN_CTAS"); v != nullptr && std::atoi(v) > 0)
+        {
+            config.minCTAs = std::atoi(v);
+        }
+        if (const char* v = std::getenv("VEDA_DP_TIMEOUT_S"); v != nullptr && std::atof(v) > 0.0)
+        {
+            timeout_s_ = std::atof(v);
+        }
+        settle(ncclCommInitRankConfig(&comm_, world, id, rank, &config), "ncclCommInitRankConfig");
         // Highest priority: the compute kernels hold every SM (one large block per SM), so the
         // all-reduce blocks must win each SM slot that frees up to overlap with the backward.
         int least = 0, greatest = 0;
@@ -73,7 +89,10 @@ public:
 
     ~DataParallel()
     {
-        cudaStreamSynchronize(stream_);
+        if (!aborted_)
+        {
+            cudaStreamSynchronize(stream_);
+        }
         for (Bucket& b : buckets_)
         {
             cudaEventDestroy(b.ready);
@@ -86,6 +105,54 @@ public:
             ncclCommDestroy(comm_);
         }
         cudaStreamDestroy(stream_);
+    }
+
+    // Host wait for the work queued on `s` (which waits for the communication it depends on):
+    // polls instead of blocking, so a collective stuck on a failed peer ends in an exception
+    // (after ncclCommAbort) instead of a hang.
+    void wait(cudaStream_t s)
+    {
+        ensure_alive();
+        const detail::WaitOutcome o = detail::watch(
+            [&] {
+                const cudaError_t e = cudaStreamQuery(s);
+                return e == cudaSuccess ? 0 : (e == cudaErrorNotReady ? 1 : -1);
+            },
+            [&] {
+                ncclResult_t a = ncclSuccess;
+                if (ncclCommGetAsyncError(comm_, &a) != ncclSuccess)
+                {
+                    return -1;
+                }
+                return a == ncclSuccess ? 0 : (a == ncclInProgress ? 1 : -1);
+            },
+            [&] { abort(); }, detail::monotonic_seconds, detail::short_pause, timeout_s_);
+        if (o != detail::WaitOutcome::done)
+        {
+            throw std::runtime_error(std::string("data parallel (rank ") + std::to_string(rank_) +
+                                     "): " + detail::describe(o));
+        }
+    }
+
+    // Tears the communicator down without waiting for its peers (ncclCommAbort): for a caller
+    // that has learned on the host that a peer is gone. Every later collective call throws.
+    void abort()
+    {
+        if (comm_ != nullptr)
+        {
+            ncclCommAbort(comm_);
+            comm_ = nullptr;
+        }
+        aborted_ = true;
+    }
+
+    void set_timeout(double seconds)
+    {
+        if (!(seconds > 0.0))
+        {
+            throw std::invalid_argument("data parallel: the communication timeout must be positive");
+        }
+        timeout_s_ = seconds;
     }
 
     // Buckets of `bucket_bytes` cut from the end of the arena (the backward produces the last
@@ -184,6 +251,7 @@ public:
     // between kernels (each compute block holds a whole SM).
     void begin_step()
     {
+        ensure_alive();
         for (Bucket& b : buckets_)
         {
             b.pending = b.waiting;
@@ -244,14 +312,15 @@ public:
                          current_stream()),
               "sharded clip (norm)");
         fork_comm();
-        nccl_check(ncclAllReduce(ss, ss, 1, ncclFloat64, ncclSum, comm_, stream_), "norm all-reduce");
+        settle(ncclAllReduce(ss, ss, 1, ncclFloat64, ncclSum, comm_, stream_), "norm all-reduce");
         join_comm();
         check(veda_adamw_step_dev(master, static_cast<float*>(m_s_.data_ptr()),
                                   static_cast<float*>(v_s_.data_ptr()), g,
                                   bf16_ ? lowp_s_.data_ptr() : nullptr, static_cast<int64_t>(shard_),
                                   c.learning_rate, c.beta1, c.beta2, c.eps, c.weight_decay,
                                   static_cast<const double*>(bias_.data_ptr()), ss, max_norm,
-                                  1.0f / static_cast<float>(world_), 0, current_stream()),
+                                  1.0f / static_cast<float>(world_),
+                                  skip_nonfinite_ ? VEDA_ADAMW_SKIP_NONFINITE : 0, current_stream()),
               "sharded AdamW");
         // the weights are gathered in arena order (the order the next forward reads them) and
         // not waited for here: the next forward waits for each bucket where it first needs it
@@ -262,14 +331,14 @@ public:
             const size_t len = (b.end - b.begin) / world_;
             if (bf16_)
             {
-                nccl_check(ncclAllGather(static_cast<const uint16_t*>(lowp_s_.data_ptr()) + b.shard_at,
+                settle(ncclAllGather(static_cast<const uint16_t*>(lowp_s_.data_ptr()) + b.shard_at,
                                          static_cast<uint16_t*>(values_) + b.begin, len, ncclBfloat16,
                                          comm_, stream_),
                            "weight all-gather");
             }
             else
             {
-                nccl_check(ncclAllGather(master + b.shard_at, static_cast<float*>(values_) + b.begin, len,
+                settle(ncclAllGather(master + b.shard_at, static_cast<float*>(values_) + b.begin, len,
                                          ncclFloat, comm_, stream_),
                            "weight all-gather");
             }
@@ -310,6 +379,7 @@ public:
 
     void begin_forward()
     {
+        ensure_alive();
         if (gathering_ && forward_reserved_sms_ > 0)
         {
             veda_set_reserved_sms(forward_reserved_sms_);
@@ -359,14 +429,14 @@ public:
     {
         sync();
         fork_comm();
-        nccl_check(ncclGroupStart(), "gradient all-gather");
+        settle(ncclGroupStart(), "gradient all-gather");
         for (const Bucket& b : buckets_)
         {
-            nccl_check(ncclAllGather(static_cast<const float*>(g_s_.data_ptr()) + b.shard_at, arena_ + b.begin,
+            settle(ncclAllGather(static_cast<const float*>(g_s_.data_ptr()) + b.shard_at, arena_ + b.begin,
                                      (b.end - b.begin) / world_, ncclFloat, comm_, stream_),
                        "gradient all-gather");
         }
-        nccl_check(ncclGroupEnd(), "gradient all-gather");
+        settle(ncclGroupEnd(), "gradient all-gather");
         join_comm();
     }
 
@@ -380,14 +450,14 @@ public:
         Tensor whole = Tensor::empty(Shape({total_}), DType::F32);
         float* f = static_cast<float*>(whole.data_ptr());
         fork_comm();
-        nccl_check(ncclGroupStart(), "shard all-gather");
+        settle(ncclGroupStart(), "shard all-gather");
         for (const Bucket& b : buckets_)
         {
-            nccl_check(ncclAllGather(static_cast<const float*>(shard.data_ptr()) + b.shard_at, f + b.begin,
+            settle(ncclAllGather(static_cast<const float*>(shard.data_ptr()) + b.shard_at, f + b.begin,
                                      (b.end - b.begin) / world_, ncclFloat, comm_, stream_),
                        "shard all-gather");
         }
-        nccl_check(ncclGroupEnd(), "shard all-gather");
+        settle(ncclGroupEnd(), "shard all-gather");
         join_comm();
         cuda_check(cudaMemcpyAsync(full, f, params_ * sizeof(float), cudaMemcpyDeviceToDevice, cs()),
                    "shard copy");
@@ -407,6 +477,12 @@ public:
         steps_ = steps;
     }
     size_t steps() const noexcept { return steps_; }
+    // a skipped step (non-finite norm) is not counted: the next uses the same bias corrections
+    void rewind_step() noexcept
+    {
+        if (steps_ > 0) --steps_;
+    }
+    void set_skip_nonfinite(bool on) noexcept { skip_nonfinite_ = on; }
     int rank() const noexcept { return rank_; }
 
     int world() const noexcept { return world_; }
@@ -434,15 +510,59 @@ private:
         cuda_check(cudaStreamWaitEvent(stream_, b.ready, 0), "bucket wait");
         if (sharded_)
         {
-            nccl_check(ncclReduceScatter(arena_ + b.begin, static_cast<float*>(g_s_.data_ptr()) + b.shard_at,
+            settle(ncclReduceScatter(arena_ + b.begin, static_cast<float*>(g_s_.data_ptr()) + b.shard_at,
                                          (b.end - b.begin) / world_, ncclFloat, ncclSum, comm_, stream_),
                        "ncclReduceScatter");
         }
         else
         {
-            nccl_check(ncclAllReduce(arena_ + b.begin, arena_ + b.begin, b.end - b.begin, ncclFloat,
+            settle(ncclAllReduce(arena_ + b.begin, arena_ + b.begin, b.end - b.begin, ncclFloat,
                                      ncclSum, comm_, stream_),
                        "ncclAllReduce");
+        }
+    }
+
+    void ensure_alive() const
+    {
+        if (aborted_)
+        {
+            throw std::runtime_error("data parallel: the communicator was aborted");
+        }
+    }
+
+    // An NCCL call's result: on a non-blocking communicator ncclInProgress means the call is
+    // still being queued, so poll until it has been (bounded by the communication timeout). Any
+    // error aborts the communicator and throws.
+    void settle(ncclResult_t r, const char* what)
+    {
+        ensure_alive();
+        if (r == ncclInProgress && comm_ != nullptr)
+        {
+            const double start = detail::monotonic_seconds();
+            while (r == ncclInProgress)
+            {
+                if (ncclCommGetAsyncError(comm_, &r) != ncclSuccess)
+                {
+                    r = ncclInternalError;
+                    break;
+                }
+                if (r == ncclInProgress && detail::monotonic_seconds() - start > timeout_s_)
+                {
+                    abort();
+                    throw std::runtime_error(std::string(what) + ": not queued within the "
+                                             "communication timeout; the communicator was aborted");
+                }
+                if (r == ncclInProgress)
+                {
+                    detail::short_pause();
+                }
+            }
+        }
+        if (r != ncclSuccess)
+        {
+            abort();
+            throw std::runtime_error(std::string(what) + ": " + ncclGetErrorString(r) +
+                                     "; the communicator was aborted");
         }
     }
 
@@ -477,6 +597,9 @@ private:
         return v != nullptr ? std::atoi(v) : 0;
     }();
     ncclComm_t comm_ = nullptr;
+    bool aborted_ = false;
+    bool skip_nonfinite_ = false;
+    double timeout_s_ = 600.0;   // VEDA_DP_TIMEOUT_S or set_timeout
     cudaStream_t stream_ = nullptr;
     cudaEvent_t done_ = nullptr, main_ready_ = nullptr;
     int rank_ = 0, world_ = 1;
@@ -536,6 +659,7 @@ void Trainer::init_data_parallel(const void* nccl_unique_id, int rank, int world
     }
     dp_ = std::make_unique<DataParallel>(nccl_unique_id, rank, world, sharded);
     dp_->attach(*model_, bucket_bytes, master_weights(), opt_->steps());
+    dp_->set_skip_nonfinite(skip_nonfinite_);
     if (sharded)
     {
         DataParallel* dp = dp_.get();
@@ -552,6 +676,34 @@ void Trainer::sync()
     if (dp_)
     {
         dp_->sync();
+        dp_->wait(cs());
+    }
+}
+
+void Trainer::set_comm_timeout(double seconds)
+{
+    if (!dp_)
+    {
+        throw std::logic_error("set_comm_timeout: not data parallel");
+    }
+    dp_->set_timeout(seconds);
+}
+
+void Trainer::abort_communication()
+{
+    if (dp_)
+    {
+        dp_->abort();
+    }
+}
+
+void Trainer::set_skip_nonfinite(bool on)
+{
+    skip_nonfinite_ = on;
+    opt_->set_skip_nonfinite(on);
+    if (dp_)
+    {
+        dp_->set_skip_nonfinite(on);
     }
 }
 
@@ -937,11 +1089,28 @@ StepStats Trainer::step_host(const int64_t* ids, const int64_t* targets)
 StepStats Trainer::last_stats()
 {
     StepStats s;
+    if (dp_)
+    {
+        dp_->wait(cs());   // a peer that failed mid-step ends here in an exception, not a hang
+    }
     cuda_check(cudaMemcpyAsync(&s.loss, loss_.data_ptr(), sizeof(float), cudaMemcpyDeviceToHost,
                                cs()),
                "loss read");
     s.grad_norm = sharded() ? dp_->grad_norm() : opt_->last_grad_norm();   // synchronises
     autograd::detail::raise_device_flag();
+    if (skip_nonfinite_ && !std::isfinite(s.grad_norm))
+    {
+        // AdamW left every weight and moment as it was: take the step count back
+        s.skipped = true;
+        if (sharded())
+        {
+            dp_->rewind_step();
+        }
+        else if (opt_->steps() > 0)
+        {
+            opt_->set_steps(opt_->steps() - 1);
+        }
+    }
     return s;
 }
 

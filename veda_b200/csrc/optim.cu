@@ -122,7 +122,7 @@ struct AdamArgs
     float lr, beta1, beta2, eps, wd;
     double bias1, bias2;
     float max_norm, grad_scale;
-    int write_grad;
+    int write_grad;   // bit 0: store g' back; bit 1: skip the step on a non-finite norm
 };
 
 __device__ __forceinline__ float adam_one(float& w, float& m, float& v, float g, const AdamArgs& a)
@@ -149,9 +149,14 @@ adamw_kernel(float* __restrict__ master, float* __restrict__ m, float* __restric
         a.bias1 = bias[0];
         a.bias2 = bias[1];
     }
+    if ((a.write_grad & 2) && sumsq != nullptr &&
+        !isfinite(static_cast<float>(sqrt(*sumsq) * fabs(static_cast<double>(a.grad_scale)))))
+    {
+        return;   // a non-finite norm: the whole step is skipped, nothing is written
+    }
     const float clip = clip_scale(sumsq, a.max_norm, a.grad_scale);
     // an unscaled gradient is already what the write-back would store
-    const bool store_g = a.write_grad && (clip != 1.0f || a.grad_scale != 1.0f);
+    const bool store_g = (a.write_grad & 1) && (clip != 1.0f || a.grad_scale != 1.0f);
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     const int64_t n4 = vec ? n / 4 : 0;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;

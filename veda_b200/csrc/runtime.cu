@@ -1,6 +1,7 @@
 // Library-wide state of libveda_cuda.so: the per-thread error message, the launch counter and
 // the cached device properties.
 #include "common.cuh"
+#include "tc_common.cuh"
 
 #include <mutex>
 
@@ -121,6 +122,40 @@ extern "C" int veda_kernel_status(int reset)
         veda::cuda::set_error("a kernel's bounded wait gave up (device status word)");
     }
     return value;
+}
+
+namespace veda::cuda
+{
+namespace
+{
+// One CTA waits, through the same bounded mbarrier wait as the tensor-core and streaming kernels,
+// on a barrier nothing arrives on; nothing else is in flight, so the timeout path can be taken
+// safely. Every thread of the CTA waits (as the consumer warps of those kernels do).
+__global__ void wait_timeout_check_kernel(long long budget, int* status)
+{
+    __shared__ uint64_t bar;
+    __shared__ int abort;
+    if (threadIdx.x == 0)
+    {
+        abort = 0;
+        tc::mbar_init(&bar, 1);
+        tc::mbar_fence_init();
+    }
+    __syncthreads();
+    tc::mbar_wait(&bar, 0, status, &abort, budget);
+}
+} // namespace
+} // namespace veda::cuda
+
+extern "C" int veda_wait_timeout_check(long long budget_cycles, veda_stream_t stream)
+{
+    VEDA_REQUIRE(budget_cycles > 0 && budget_cycles <= veda::cuda::tc::kWaitBudget,
+                 "budget must lie in (0, 2^32] cycles");
+    int* status = veda::cuda::device_status_ptr();
+    VEDA_REQUIRE(status != nullptr, "no device status word");
+    veda::cuda::wait_timeout_check_kernel<<<1, 128, 0, stream>>>(budget_cycles, status);
+    veda::cuda::count_launch();
+    return veda::cuda::check_launch("veda_wait_timeout_check");
 }
 
 extern "C" const char* veda_last_error(void) { return veda::cuda::last_error_cstr(); }

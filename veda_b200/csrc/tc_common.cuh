@@ -50,11 +50,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t phase)
     return ok != 0;
 }
 
-// Bounded wait: about two seconds of spinning, then the status word records a timeout, the CTA's
-// shared abort flag is raised so every later wait returns at once, and the caller proceeds
-// (results are then garbage, but the kernel ends promptly and the context survives).
+// Bounded wait: about two seconds of spinning (budget clock cycles), then the status word records
+// a timeout, the CTA's shared abort flag is raised so every later wait returns at once, and the
+// caller proceeds (results are then garbage, but the kernel ends promptly and the context
+// survives).
+constexpr long long kWaitBudget = 1ll << 32;
 __device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t phase, int* status,
-                                          volatile int* abort)
+                                          volatile int* abort, long long budget = kWaitBudget)
 {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, phase))
@@ -68,7 +70,7 @@ __device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t phase, int* st
         {
             return;
         }
-        if (clock64() - start > (1ll << 32))
+        if (clock64() - start > budget)
         {
             *abort = 1;
             if (status != nullptr)

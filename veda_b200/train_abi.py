@@ -47,6 +47,10 @@ SIGNATURES = {
     "veda_trainer_step_host": (_i, [_p, _p, _p, _p, _p]),
     "veda_trainer_step_device": (_i, [_p, _p, _p]),
     "veda_trainer_last_stats": (_i, [_p, _p, _p]),
+    "veda_trainer_set_comm_timeout": (_i, [_p, C.c_double]),
+    "veda_trainer_abort_comm": (_i, [_p]),
+    "veda_trainer_set_skip_nonfinite": (_i, [_p, _i]),
+    "veda_trainer_step_skipped": (_i, [_p, _p]),
     "veda_profile_enable": (_i, [_i]),
     "veda_profile_collect": (_i, [_p, _p, _p, _p, _p, _i]),
 }
@@ -177,6 +181,20 @@ class Trainer:
         loss, norm = C.c_float(0), C.c_float(0)
         _check(self.L, self.L.veda_trainer_last_stats(self.h, C.byref(loss), C.byref(norm)))
         return float(loss.value), float(norm.value)
+
+    def set_comm_timeout(self, seconds: float):
+        _check(self.L, self.L.veda_trainer_set_comm_timeout(self.h, float(seconds)))
+
+    def abort_comm(self):
+        _check(self.L, self.L.veda_trainer_abort_comm(self.h))
+
+    def set_skip_nonfinite(self, on: bool):
+        _check(self.L, self.L.veda_trainer_set_skip_nonfinite(self.h, 1 if on else 0))
+
+    def step_skipped(self) -> bool:
+        out = C.c_int(0)
+        _check(self.L, self.L.veda_trainer_step_skipped(self.h, C.byref(out)))
+        return bool(out.value)
 
 
 def nccl_unique_id() -> bytes:
