@@ -25,6 +25,7 @@
 #include <cstdint>
 #include <functional>
 #include <memory>
+#include <string>
 #include <vector>
 
 namespace veda::autograd
@@ -117,6 +118,24 @@ Variable swiglu(const Variable& gate_up);
 Variable embedding_device(const Variable& table, const core::Tensor& ids);
 // Mean cross-entropy with device targets (int64 [lanes]).
 Variable cross_entropy_device(const Variable& logits, const core::Tensor& targets);
+
+// Central finite differences against the tape's gradient (src/libs/autograd/GradientCheck.h):
+// dL/dx_i ~ (L(x + h e_i) - L(x - h e_i)) / 2h for every element of `at`, compared relatively per
+// element with max(|numeric|, |analytic|, 1e-3) as the scale. ok iff the worst relative
+// difference is within `tolerance`; loss_of must return a scalar. Costs 2n forward passes: for
+// small tensors in tests.
+struct GradientCheck
+{
+    bool ok = true;
+    double worst_relative = 0.0;
+    size_t worst_index = 0;
+    double analytic = 0.0;
+    double numeric = 0.0;
+    std::string message;
+};
+
+GradientCheck check_gradient(const std::function<Variable(const Variable&)>& loss_of,
+                             const core::Tensor& at, float step = 1e-2f, double tolerance = 2e-2);
 
 namespace detail
 {

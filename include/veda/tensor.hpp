@@ -6,8 +6,10 @@
 //   * Storage is device memory from a stream-ordered pool (cudaMallocAsync on the current veda
 //     stream), so allocation per op, which the reference's tape does, stays cheap;
 //   * every Tensor has a DType: F32 (the reference's only arithmetic type) or BF16;
-//   * element access from the host (at(), to_host()) copies through PCIe and synchronises — meant
-//     for tests, exactly like the reference's at() is meant for them.
+//   * element access from the host (at(), to_host(), data()) copies through PCIe and synchronises
+//     — meant for tests, exactly like the reference's at() and data() are meant for them. data()
+//     returns a pointer into a host mirror of the storage, filled from the device when it is
+//     asked for and written back before the next device access after a writable data() call.
 // Errors keep the reference's exception types: std::invalid_argument for bad shapes and
 // arguments, std::out_of_range for bad indices and views, std::logic_error for reshaping a
 // non-contiguous view, std::runtime_error for device failures.
@@ -17,6 +19,7 @@
 #include <cstdint>
 #include <initializer_list>
 #include <memory>
+#include <ostream>
 #include <string>
 #include <vector>
 
@@ -64,6 +67,11 @@ private:
     size_t size_ = 1;
 };
 
+inline std::ostream& operator<<(std::ostream& os, const Shape& shape)
+{
+    return os << shape.to_string();
+}
+
 std::vector<size_t> contiguous_strides(const Shape& shape);
 
 // A device buffer. Freed (stream-ordered) when the last Tensor viewing it goes away.
@@ -77,14 +85,24 @@ public:
     Storage(const Storage&) = delete;
     Storage& operator=(const Storage&) = delete;
 
-    void* data() noexcept { return data_; }
-    const void* data() const noexcept { return data_; }
+    // Device address. If the host mirror may have been written since the last device access,
+    // it is copied back first (synchronously).
+    void* data();
+    const void* data() const;
     size_t bytes() const noexcept { return bytes_; }
+    // Host mirror of the whole buffer for Tensor::data(): filled from the device (after a device
+    // synchronisation) unless it already holds the current contents; `writable` means the caller
+    // may change it, so the next device access copies it back.
+    unsigned char* host_mirror(bool writable) const;
 
 private:
+    void flush_mirror() const;
     void* data_ = nullptr;
     size_t bytes_ = 0;
     bool owned_ = true;
+    mutable std::unique_ptr<unsigned char[]> mirror_;
+    mutable bool mirror_valid_ = false;
+    mutable bool mirror_dirty_ = false;
 };
 
 class Tensor
@@ -115,6 +133,12 @@ public:
 
     // Reads one element (a device-to-host copy; synchronises).
     float at(std::initializer_list<size_t> indices) const;
+    // The reference's host element access (Tensor.h:76-77) for fp32 tensors: a host pointer to
+    // this view's first element, strides as in strides(). It points into the storage's host
+    // mirror (see Storage::host_mirror); device work queued before the call is waited for, and
+    // writes through the non-const form reach the device before its next use there.
+    float* data();
+    const float* data() const;
     bool is_contiguous() const;
     Tensor reshape(const Shape& new_shape) const;
     Tensor transpose(size_t a, size_t b) const;

@@ -273,6 +273,10 @@ int veda_softmax_fwd(const void* x, void* y, int64_t lanes, int64_t length, int 
                      veda_stream_t stream);
 int veda_softmax_bwd(const void* y, const void* g, void* dx, int64_t lanes, int64_t length,
                      int dtype, veda_stream_t stream);
+/* log_softmax over the last dim of [lanes, length] (ops::log_softmax,
+ * src/libs/ops/Softmax.cpp:82-151): x - m - log(sum exp(x - m)); an all -inf lane stays -inf. */
+int veda_log_softmax_fwd(const void* x, void* y, int64_t lanes, int64_t length, int dtype,
+                         veda_stream_t stream);
 /* silu and its backward on n elements (Activations.cpp:13-16, NonLinear.cpp:47-63). */
 int veda_silu_fwd(const void* x, void* y, int64_t n, int dtype, veda_stream_t stream);
 int veda_silu_bwd(const void* x, const void* g, void* dx, int64_t n, int dtype,

@@ -1,0 +1,3 @@
+// The reference's AdamW.h mapped onto this library's header (drop-in shim for its tests).
+#pragma once
+#include "veda/optim.hpp"

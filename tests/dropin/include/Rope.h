@@ -1,0 +1,3 @@
+// The reference's Rope.h mapped onto this library's header (drop-in shim for its tests).
+#pragma once
+#include "veda/model.hpp"

@@ -110,6 +110,7 @@ SIGNATURES = {
                                 _i, _i, _p]),
     "veda_attention_bwd_workspace": (_sz, [_i64, _i64, _i64, _i64, _i64, _i]),
     "veda_attention_set_deterministic": (_i, [_i]),
+    "veda_log_softmax_fwd": (_i, [_p, _p, _i64, _i64, _i, _p]),
 }
 
 _cuda = None

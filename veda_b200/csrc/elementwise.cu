@@ -630,6 +630,80 @@ extern "C" int veda_softmax_fwd(const void* x, void* y, int64_t lanes, int64_t l
     return check_launch("veda_softmax_fwd");
 }
 
+namespace veda::cuda
+{
+namespace
+{
+// log_softmax over the last dim (ops::log_softmax, src/libs/ops/Softmax.cpp:82-151): x - m -
+// log(sum exp(x - m)) with m the lane's maximum; a lane that is -inf everywhere stays -inf (no
+// inf - inf). One block per lane.
+template <typename T>
+__global__ void log_softmax_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t lanes,
+                                   int64_t length)
+{
+    __shared__ float red[32];
+    __shared__ float bcast;
+    for (int64_t lane_i = blockIdx.x; lane_i < lanes; lane_i += gridDim.x)
+    {
+        const T* xr = x + lane_i * length;
+        T* yr = y + lane_i * length;
+        float m = -INFINITY;
+        for (int64_t i = threadIdx.x; i < length; i += blockDim.x) m = fmaxf(m, to_f32(xr[i]));
+        m = warp_max(m);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+        __syncthreads();
+        if (threadIdx.x == 0)
+        {
+            float t = red[0];
+            for (int w = 1; w < static_cast<int>(blockDim.x / 32); ++w) t = fmaxf(t, red[w]);
+            bcast = t;
+        }
+        __syncthreads();
+        m = bcast;
+        __syncthreads();
+        if (m == -INFINITY)
+        {
+            for (int64_t i = threadIdx.x; i < length; i += blockDim.x) yr[i] = from_f32<T>(-INFINITY);
+            continue;
+        }
+        float s = 0.0f;
+        for (int64_t i = threadIdx.x; i < length; i += blockDim.x) s += expf(to_f32(xr[i]) - m);
+        s = warp_sum(s);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+        __syncthreads();
+        if (threadIdx.x == 0)
+        {
+            float t = 0.0f;
+            for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) t += red[w];
+            bcast = logf(t);
+        }
+        __syncthreads();
+        const float log_sum = bcast;
+        __syncthreads();
+        for (int64_t i = threadIdx.x; i < length; i += blockDim.x)
+        {
+            yr[i] = from_f32<T>(to_f32(xr[i]) - m - log_sum);
+        }
+    }
+}
+} // namespace
+} // namespace veda::cuda
+
+extern "C" int veda_log_softmax_fwd(const void* x, void* y, int64_t lanes, int64_t length, int dtype,
+                                    veda_stream_t stream)
+{
+    VEDA_REQUIRE(valid_dtype(dtype) && lanes >= 0 && length >= 0, "bad arguments");
+    if (lanes == 0 || length == 0) return VEDA_OK;
+    VEDA_REQUIRE(x && y, "null pointer");
+    const unsigned grid = static_cast<unsigned>(
+        lanes < static_cast<int64_t>(sm_count()) * 8 ? lanes : static_cast<int64_t>(sm_count()) * 8);
+    VEDA_DISPATCH(dtype, T,
+                  log_softmax_kernel<T><<<grid, 256, 0, stream>>>(
+                      static_cast<const T*>(x), static_cast<T*>(y), lanes, length));
+    count_launch();
+    return check_launch("veda_log_softmax_fwd");
+}
+
 extern "C" int veda_softmax_bwd(const void* y, const void* g, void* dx, int64_t lanes,
                                 int64_t length, int dtype, veda_stream_t stream)
 {

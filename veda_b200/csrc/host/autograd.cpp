@@ -3,12 +3,14 @@
 // behind include/veda_cuda.h. The arithmetic of every op is the reference's; see the kernels for
 // the line-by-line correspondence.
 #include "veda/autograd.hpp"
+#include "veda/ops.hpp"
 
 #include "veda/profile.hpp"
 #include "veda_cuda.h"
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <limits>
@@ -314,6 +316,14 @@ Variable Variable::leaf(Tensor value, bool requires_grad)
     auto node = std::make_shared<Node>(std::move(value));
     node->requires_grad = requires_grad;
     node->is_leaf = true;
+    if (requires_grad)
+    {
+        // as in the reference, a leaf that takes a gradient has a zero fp32 gradient buffer from
+        // the start (callers may read or write node()->grad before any backward)
+        node->grad = Tensor(node->value.shape(), DType::F32);
+        node->grad_owned = true;
+        node->grad_zero = true;
+    }
     return Variable(std::move(node));
 }
 
@@ -1467,4 +1477,110 @@ Variable swiglu(const Variable& gate_up)
     });
 }
 
+GradientCheck check_gradient(const std::function<Variable(const Variable&)>& loss_of,
+                             const Tensor& at, float step, double tolerance)
+{
+    // the restatement of src/libs/autograd/GradientCheck.cpp:14-64: one analytic gradient from
+    // the tape, then a central difference per element of `at`
+    GradientCheck result;
+    Variable x = Variable::leaf(core::contiguous(core::to_dtype(at, DType::F32)));
+    Variable loss = loss_of(x);
+    if (loss.value().numel() != 1)
+    {
+        result.ok = false;
+        result.message = "check_gradient: the function must return a scalar, got " +
+                         loss.value().shape().to_string();
+        return result;
+    }
+    loss.backward();
+    const std::vector<float> analytic = x.grad().to_host();
+    const Tensor base = core::contiguous(core::to_dtype(at, DType::F32));
+    std::vector<float> point = base.to_host();
+    auto value_at = [&](const std::vector<float>& p) {
+        const Variable v = loss_of(Variable::leaf(Tensor::from_host(p, base.shape()), false));
+        return static_cast<double>(v.value().to_host()[0]);
+    };
+    for (size_t i = 0; i < point.size(); ++i)
+    {
+        const float keep = point[i];
+        point[i] = keep + step;
+        const double up = value_at(point);
+        point[i] = (keep + step) - 2.0f * step;
+        const double down = value_at(point);
+        point[i] = keep;
+        const double numeric = (up - down) / (2.0 * static_cast<double>(step));
+        const double a = analytic[i];
+        const double scale = std::max({std::fabs(numeric), std::fabs(a), 1e-3});
+        const double relative = std::fabs(numeric - a) / scale;
+        if (relative > result.worst_relative)
+        {
+            result.worst_relative = relative;
+            result.worst_index = i;
+            result.analytic = a;
+            result.numeric = numeric;
+        }
+    }
+    result.ok = result.worst_relative <= tolerance;
+    if (!result.ok)
+    {
+        result.message = "gradient mismatch at index " + std::to_string(result.worst_index) +
+                         ": analytic " + std::to_string(result.analytic) + ", numeric " +
+                         std::to_string(result.numeric) + ", relative " +
+                         std::to_string(result.worst_relative);
+    }
+    return result;
+}
+
 } // namespace veda::autograd
+
+namespace veda::ops
+{
+
+using core::DType;
+using core::Shape;
+using core::Tensor;
+
+Tensor add(const Tensor& a, const Tensor& b) { return autograd::binary(0, a, b); }
+Tensor mul(const Tensor& a, const Tensor& b) { return autograd::binary(1, a, b); }
+
+Tensor add(const Tensor& a, float scalar)
+{
+    return autograd::binary(0, a, Tensor::from_host({scalar}, Shape({}), a.dtype()));
+}
+
+Tensor mul(const Tensor& a, float scalar) { return autograd::scale(a, scalar); }
+
+namespace
+{
+// f over the last dim of a contiguous [lanes, length] view of `tensor` with `dim` moved last
+Tensor along(const Tensor& tensor, size_t dim, const char* what,
+             int (*f)(const void*, void*, int64_t, int64_t, int, veda_stream_t))
+{
+    if (dim >= tensor.rank())
+    {
+        throw std::invalid_argument(std::string(what) + ": dimension " + std::to_string(dim) +
+                                    " is out of range for shape " + tensor.shape().to_string());
+    }
+    const size_t last = tensor.rank() - 1;
+    const Tensor moved = core::contiguous(dim == last ? tensor : tensor.transpose(dim, last));
+    Tensor out = Tensor::empty(moved.shape(), moved.dtype());
+    const size_t length = moved.shape()[last];
+    const size_t lanes = length == 0 ? 0 : moved.numel() / length;
+    check(f(moved.data_ptr(), out.data_ptr(), static_cast<int64_t>(lanes),
+            static_cast<int64_t>(length), static_cast<int>(moved.dtype()), current_stream()),
+          what);
+    return dim == last ? out : core::contiguous(out.transpose(dim, last));
+}
+} // namespace
+
+Tensor softmax(const Tensor& tensor, size_t dim)
+{
+    return along(tensor, dim, "softmax", veda_softmax_fwd);
+}
+
+Tensor log_softmax(const Tensor& tensor, size_t dim)
+{
+    return along(tensor, dim, "log_softmax", veda_log_softmax_fwd);
+}
+
+} // namespace veda::ops

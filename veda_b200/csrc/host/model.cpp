@@ -1,4 +1,5 @@
 // veda::train::TinyTransformer on the device (src/libs/train/Model.cpp:72-255, with GQA).
+#include "veda/model.hpp"
 #include "veda/train.hpp"
 
 #include "veda_cuda.h"
@@ -35,6 +36,20 @@ ModelConfig tiny_config()
 
 std::pair<Tensor, Tensor> rope_tables(size_t positions, size_t head_dim, float theta)
 {
+    model::RopeTables t = model::rope_tables(positions, head_dim, theta, 0);
+    return {t.cosines, t.sines};
+}
+
+} // namespace veda::train
+
+namespace veda::model
+{
+
+using core::Shape;
+using core::Tensor;
+
+RopeTables rope_tables(size_t positions, size_t head_dim, float theta, size_t first_position)
+{
     if (head_dim == 0 || head_dim % 2 != 0)
     {
         throw std::invalid_argument("rope_tables: head_dim must be even, got " +
@@ -53,7 +68,7 @@ std::pair<Tensor, Tensor> rope_tables(size_t positions, size_t head_dim, float t
         {
             const double freq = std::pow(static_cast<double>(theta),
                                          -2.0 * static_cast<double>(i) / static_cast<double>(head_dim));
-            const double angle = static_cast<double>(p) * freq;
+            const double angle = static_cast<double>(first_position + p) * freq;
             const float cv = static_cast<float>(std::cos(angle));
             const float sv = static_cast<float>(std::sin(angle));
             c[p * head_dim + i] = c[p * head_dim + i + pairs] = cv;
@@ -63,6 +78,38 @@ std::pair<Tensor, Tensor> rope_tables(size_t positions, size_t head_dim, float t
     return {Tensor::from_host(c, Shape({positions, head_dim})),
             Tensor::from_host(s, Shape({positions, head_dim}))};
 }
+
+Tensor apply_rope(const Tensor& x, const RopeTables& tables)
+{
+    if (x.rank() < 2 || tables.cosines.rank() != 2 || tables.sines.shape() != tables.cosines.shape())
+    {
+        throw std::invalid_argument("apply_rope: expected x [.., T, Dh] and tables [T, Dh], got " +
+                                    x.shape().to_string() + " and " +
+                                    tables.cosines.shape().to_string());
+    }
+    const size_t T = x.shape()[x.rank() - 2], Dh = x.shape()[x.rank() - 1];
+    if (tables.cosines.shape()[0] != T || tables.cosines.shape()[1] != Dh)
+    {
+        throw std::invalid_argument("apply_rope: tables " + tables.cosines.shape().to_string() +
+                                    " do not match x " + x.shape().to_string());
+    }
+    const Tensor c = core::contiguous(x);
+    Tensor out = Tensor::empty(c.shape(), c.dtype());
+    const Tensor cs = core::to_dtype(tables.cosines, core::DType::F32);
+    const Tensor sn = core::to_dtype(tables.sines, core::DType::F32);
+    const size_t lanes = T * Dh == 0 ? 0 : c.numel() / (T * Dh);
+    check(veda_rope(c.data_ptr(), out.data_ptr(), static_cast<const float*>(cs.data_ptr()),
+                    static_cast<const float*>(sn.data_ptr()), static_cast<int64_t>(lanes),
+                    static_cast<int64_t>(T), static_cast<int64_t>(Dh), 0,
+                    static_cast<int>(c.dtype()), current_stream()),
+          "apply_rope");
+    return out;
+}
+
+} // namespace veda::model
+
+namespace veda::train
+{
 
 namespace
 {

@@ -20,6 +20,20 @@ namespace
 cudaStream_t cs() { return reinterpret_cast<cudaStream_t>(current_stream()); }
 
 float* fptr(const Tensor& t) { return static_cast<float*>(t.data_ptr()); }
+
+// The runs launch through device addresses taken once: bring any value or gradient the host wrote
+// through Tensor::data() since then back to the device first (a no-op without host mirrors).
+void flush_host_writes(const std::vector<autograd::Variable>& parameters)
+{
+    for (const auto& p : parameters)
+    {
+        p.value().storage()->data();
+        if (p.node()->grad.defined())
+        {
+            p.node()->grad.storage()->data();
+        }
+    }
+}
 } // namespace
 
 AdamW::AdamW(std::vector<autograd::Variable> parameters, AdamWConfig config)
@@ -144,6 +158,7 @@ void AdamW::advance()
 
 void AdamW::launch(const double* sumsq, float max_norm, float grad_scale)
 {
+    flush_host_writes(parameters_);
     const double* bias = static_cast<const double*>(bias_.data_ptr());
     for (const Run& r : runs_)
     {
@@ -174,6 +189,7 @@ void AdamW::launch_clipped(float max_norm, float grad_scale)
     {
         throw std::invalid_argument("clip_gradient_norm: max_norm must be positive");
     }
+    flush_host_writes(parameters_);
     double* ss = static_cast<double*>(sumsq_.data_ptr());
     for (size_t k = 0; k < runs_.size(); ++k)
     {

@@ -138,6 +138,59 @@ Storage::Storage(size_t bytes, bool zero) : bytes_(bytes)
 
 Storage::Storage(void* external, size_t bytes) : data_(external), bytes_(bytes), owned_(false) {}
 
+void Storage::flush_mirror() const
+{
+    if (mirror_dirty_)
+    {
+        cuda_check(cudaDeviceSynchronize(), "Storage: host mirror write-back (synchronize)");
+        cuda_check(cudaMemcpy(data_, mirror_.get(), bytes_, cudaMemcpyHostToDevice),
+                   "Storage: host mirror write-back");
+        mirror_dirty_ = false;
+    }
+    mirror_valid_ = false;   // the device may change the buffer from here on
+}
+
+void* Storage::data()
+{
+    if (mirror_)
+    {
+        flush_mirror();
+    }
+    return data_;
+}
+
+const void* Storage::data() const
+{
+    if (mirror_)
+    {
+        flush_mirror();
+    }
+    return data_;
+}
+
+unsigned char* Storage::host_mirror(bool writable) const
+{
+    if (!mirror_)
+    {
+        mirror_ = std::make_unique<unsigned char[]>(bytes_ > 0 ? bytes_ : 1);
+    }
+    if (!mirror_valid_ && !mirror_dirty_)
+    {
+        cuda_check(cudaDeviceSynchronize(), "Storage: host mirror (synchronize)");
+        if (bytes_ > 0)
+        {
+            cuda_check(cudaMemcpy(mirror_.get(), data_, bytes_, cudaMemcpyDeviceToHost),
+                       "Storage: host mirror");
+        }
+        mirror_valid_ = true;
+    }
+    if (writable)
+    {
+        mirror_dirty_ = true;
+    }
+    return mirror_.get();
+}
+
 Storage::~Storage()
 {
     if (owned_ && data_ != nullptr && cudaFreeAsync(data_, cs()) != cudaSuccess)
@@ -305,6 +358,32 @@ Tensor Tensor::slice(size_t dim, size_t start, size_t count) const
     dims[dim] = count;
     return Tensor(storage_, offset_ + start * strides_[dim], Shape(std::move(dims)), strides_,
                   dtype_);
+}
+
+float* Tensor::data()
+{
+    if (dtype_ != DType::F32)
+    {
+        throw std::logic_error("Tensor::data: host element access is for fp32 tensors");
+    }
+    if (!storage_)
+    {
+        return nullptr;
+    }
+    return reinterpret_cast<float*>(storage_->host_mirror(true)) + offset_;
+}
+
+const float* Tensor::data() const
+{
+    if (dtype_ != DType::F32)
+    {
+        throw std::logic_error("Tensor::data: host element access is for fp32 tensors");
+    }
+    if (!storage_)
+    {
+        return nullptr;
+    }
+    return reinterpret_cast<const float*>(storage_->host_mirror(false)) + offset_;
 }
 
 void* Tensor::data_ptr() const
