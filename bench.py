@@ -256,6 +256,8 @@ def run_veda(args):
     tr = TA.Trainer(cfg, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, max_norm=1.0,
                     dtype=0 if args.workload == "tiny" else 1, batch=B, seq_len=T, seed=seed,
                     stream=stream.cuda_stream)
+    recompute = args.recompute == "on" or (args.recompute == "auto" and args.workload == "qwen3-1.7b")
+    tr.set_recompute_attention(recompute)
     if world > 1:
         obj = [TA.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
@@ -354,7 +356,7 @@ def run_veda(args):
         "config": {"workload": args.workload, "model": args.workload, "global_batch": B * world,
                    "micro_batch": B, "seq_len": T, "parallelism": f"dp{world}",
                    "params": tr.n, "l2": "inputs and the step's working set exceed L2",
-                   "buckets_mb": 25,
+                   "buckets_mb": 25, "attention_recompute": recompute,
                    "optimizer_state": ("sharded (ZeRO-1)" if world > 1 and args.dp == "sharded"
                                        else "replicated")},
         "mfu_model_tflops": model_flops_per_token(c, T) * value / 1e12,
@@ -417,6 +419,9 @@ def main():
     ap.add_argument("--impl", default="veda", choices=["veda", "reference"])
     ap.add_argument("--workload", default="qwen3-0.6b", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--recompute", default="auto", choices=["auto", "on", "off"],
+                    help="activation recompute of attention (auto: on for qwen3-1.7b, the config "
+                         "that names it)")
     ap.add_argument("--dp", default="sharded", choices=["sharded", "allreduce"],
                     help="N > 1: optimizer state sharded across ranks (reduce-scatter + all-gather) "
                          "or replicated (all-reduce)")

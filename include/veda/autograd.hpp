@@ -111,6 +111,13 @@ Variable linear(const Variable& x, const Variable& w);
 Variable attention(const Variable& qkv, const Variable& q_norm, const Variable& k_norm,
                    const core::Tensor& cosines, const core::Tensor& sines, size_t batch,
                    size_t length, size_t heads, size_t kv_heads, size_t head_dim, float eps);
+// attention(...) followed by linear(context, o), as one node that keeps only the projection, the
+// gains and the log-sum-exp: the backward forms q, k (norm + RoPE) and the context again before
+// the output projection's and the attention's backward (activation recompute of attention).
+Variable attention_output(const Variable& qkv, const Variable& q_norm, const Variable& k_norm,
+                          const Variable& o, const core::Tensor& cosines, const core::Tensor& sines,
+                          size_t batch, size_t length, size_t heads, size_t kv_heads,
+                          size_t head_dim, float eps);
 // mul(silu(gate), up) on a fused gate|up buffer [rows, 2F] -> [rows, F].
 Variable swiglu(const Variable& gate_up);
 // Token ids already on the device (int64 [count]); ids are checked on the device and an

@@ -103,6 +103,11 @@ public:
     // Called with an arena range [lo, hi) before the forward first reads the weights in it, so
     // that a data-parallel step whose updated weights are still arriving waits only for them.
     void set_weight_gate(std::function<void(size_t, size_t)> gate) { gate_ = std::move(gate); }
+    // Activation recompute of attention: each layer's attention and output projection become one
+    // node that keeps the fused projection and the log-sum-exp only, and forms q, k and the
+    // context again in the backward (off by default).
+    void set_recompute_attention(bool on) noexcept { recompute_attention_ = on; }
+    bool recompute_attention() const noexcept { return recompute_attention_; }
 
 private:
     autograd::Variable forward_from(const autograd::Variable& x, size_t batch, size_t length);
@@ -114,6 +119,7 @@ private:
     size_t total_ = 0;
     size_t arena_len_ = 0;
     std::function<void(size_t, size_t)> gate_;
+    bool recompute_attention_ = false;
     std::pair<size_t, size_t> embed_range_, final_range_;
     std::vector<std::pair<size_t, size_t>> layer_ranges_;
     std::vector<autograd::Variable> parameters_;
@@ -195,6 +201,9 @@ public:
     // it as skipped, and the step is not counted (the next uses the same bias corrections).
     // Off (the default): the reference's behaviour, the update runs with the unclipped gradient.
     void set_skip_nonfinite(bool on);
+    // Activation recompute of attention in the model (TinyTransformer::set_recompute_attention);
+    // a captured step graph is dropped and captured again with the new path.
+    void set_recompute_attention(bool on);
 
     TinyTransformer& model() noexcept { return *model_; }
     optim::AdamW& optimizer() noexcept { return *opt_; }

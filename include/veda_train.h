@@ -140,6 +140,11 @@ int veda_trainer_abort_comm(veda_trainer* t);
 int veda_trainer_set_skip_nonfinite(veda_trainer* t, int on);
 int veda_trainer_step_skipped(veda_trainer* t, int* skipped);
 
+/* Activation recompute of attention (default off): each layer keeps its fused q|k|v projection and
+ * the attention log-sum-exp only, and the backward forms q, k (norm + RoPE) and the attention
+ * output again before the output projection's and the attention's backward. */
+int veda_trainer_set_recompute_attention(veda_trainer* t, int on);
+
 /* Device-time profile of kernel classes (gemm_fwd, gemm_dx, gemm_dw, attn_fwd, attn_bwd,
  * cross_entropy, rmsnorm_bwd, swiglu_bwd, adamw), recorded with CUDA events while enabled. */
 int veda_profile_enable(int on);

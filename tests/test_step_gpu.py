@@ -91,16 +91,20 @@ QWEN06_FULL_WIDTH = O.ModelConfig(vocab=151936, hidden=1024, intermediate=3072, 
                                   kv_heads=8, head_dim=128, eps=1e-6, theta=1e6)
 
 
-@pytest.mark.parametrize("cfg,B,T", [(QWEN_SMALL, 2, 128), (QWEN_WIDE, 1, 128),
-                                     (QWEN06_FULL_WIDTH, 1, 512)])
-def test_qwen_shaped_bf16_step_matches_oracle(cfg, B, T):
+@pytest.mark.parametrize("cfg,B,T,recompute", [(QWEN_SMALL, 2, 128, False),
+                                               (QWEN_WIDE, 1, 128, False),
+                                               (QWEN_WIDE, 1, 256, True),
+                                               (QWEN06_FULL_WIDTH, 1, 512, False)])
+def test_qwen_shaped_bf16_step_matches_oracle(cfg, B, T, recompute):
     """One bf16 step (forward, cross-entropy, backward, clip, AdamW) against the oracle's fp32
     step on the same bf16-rounded weights and batch (src/libs/train/Model.cpp:206-255,
     src/libs/autograd/Loss.cpp:18-103, src/libs/optim/AdamW.cpp:38-93): loss, norm, every
-    gradient and every updated weight. The last case is the Qwen3-0.6B width and vocabulary."""
+    gradient and every updated weight. QWEN_WIDE with recompute is the Qwen3-1.7B layer width with
+    activation recompute of attention; the last case is the Qwen3-0.6B width and vocabulary."""
     params = O.init_params(cfg, 3, bf16=True)
     ids, tg = O.synthetic_batch(cfg, B, T, 3)
     t = make_trainer(cfg, 1, B, T)
+    t.set_recompute_attention(recompute)
     t.set_params(np.concatenate([p.ravel() for p in params]))
     loss, norm = t.step_host(ids, tg)
     ref = [p.copy() for p in params]
@@ -143,6 +147,7 @@ def test_qwen_full_shape_step_properties(cfg, B, T, seed):
     finite grad norm, and a second step on the same batch lowering the loss."""
     ids, tg = O.synthetic_batch(cfg, B, T, seed)
     t = make_trainer(cfg, 1, B, T, seed=seed)
+    t.set_recompute_attention(cfg is O.QWEN3_17B)   # the 1.7B step recomputes attention
     l1, n1 = t.step_host(ids, tg)
     l2, n2 = t.step_host(ids, tg)
     assert abs(l1 - math.log(cfg.vocab)) < 0.5, l1
@@ -219,6 +224,31 @@ def test_nonfinite_step_is_skipped_and_not_counted():
     assert np.array_equal(t.get_params(), fresh.get_params())
     t.close()
     fresh.close()
+
+
+def test_recompute_attention_is_bit_exact():
+    """Activation recompute of attention forms q, k and the attention output again with the same
+    deterministic kernels, so a trainer that recomputes (its step replayed from a CUDA graph) and
+    one that keeps them (eager) agree bit for bit: losses, norms, gradients and weights. Switching
+    recompute off mid-run drops the captured graph and the steps still agree."""
+    cfg, B, T = QWEN_SMALL, 2, 128
+    flat = np.concatenate([p.ravel() for p in O.init_params(cfg, 3, bf16=True)])
+    a, b = make_trainer(cfg, 1, B, T), make_trainer(cfg, 1, B, T)
+    a.set_params(flat)
+    b.set_params(flat)
+    a.set_recompute_attention(True)
+    b.set_step_graph(False)
+    for s in range(6):
+        if s == 4:
+            a.set_recompute_attention(False)
+        ids, tg = O.synthetic_batch(cfg, B, T, 20 + s)
+        la, na = a.step_host(ids, tg)
+        lb, nb = b.step_host(ids, tg)
+        assert la == lb and na == nb, (s, la, lb, na, nb)
+    assert np.array_equal(a.get_grads(), b.get_grads())
+    assert np.array_equal(a.get_params(), b.get_params())
+    a.close()
+    b.close()
 
 
 @pytest.mark.parametrize("dtype", [0, 1])

@@ -1214,9 +1214,20 @@ Variable add_rms_norm(const Variable& x, const Variable& r, const Variable& gamm
     return rms_norm_node(s, gamma, std::move(value), stored, ld, gv, n, eps);
 }
 
-Variable linear(const Variable& x, const Variable& w)
+namespace
 {
-    const Tensor& xv = x.value();
+// What the linear backward reads: the input (rows of `in`, leading dimension ldx) and the
+// contiguous weight [out, in], with the nodes the gradients go to.
+struct LinearSaved
+{
+    std::shared_ptr<Node> xin, win;
+    Tensor xs, wc;
+    int64_t ldx = 0;
+    size_t rows = 0, in = 0, out = 0;
+};
+
+LinearSaved linear_setup(const Tensor& xv, std::shared_ptr<Node> xin, const Variable& w)
+{
     const Tensor& wv = w.value();
     if (wv.rank() != 2 || xv.rank() < 1)
     {
@@ -1232,125 +1243,153 @@ Variable linear(const Variable& x, const Variable& w)
     {
         throw std::invalid_argument("linear: input and weight dtypes differ");
     }
-    Tensor xs = xv;
-    int64_t ldx = static_cast<int64_t>(in);
+    LinearSaved l;
+    l.xin = std::move(xin);
+    l.win = w.node();
+    l.xs = xv;
+    l.ldx = static_cast<int64_t>(in);
     if (xv.rank() >= 2 && xv.strides().back() == 1)
     {
         try
         {
-            ldx = xv.ld();
+            l.ldx = xv.ld();
         }
         catch (const std::invalid_argument&)
         {
-            xs = make_contiguous(xv);
-            ldx = static_cast<int64_t>(in);
+            l.xs = make_contiguous(xv);
+            l.ldx = static_cast<int64_t>(in);
         }
     }
     else
     {
-        xs = make_contiguous(xv);
+        l.xs = make_contiguous(xv);
     }
-    const Tensor wc = make_contiguous(wv);
-    const size_t rows = xs.numel() / in;
-    std::vector<size_t> od = xv.shape().dims();
-    od.back() = out;
-    Tensor value = Tensor::empty(Shape(od), xs.dtype());
-    {
-        const double es = static_cast<double>(core::dtype_size(xs.dtype()));
-        profile::Scope scope("gemm_fwd", 2.0 * rows * in * out,
-                             es * (static_cast<double>(rows) * in + static_cast<double>(out) * in +
-                                   static_cast<double>(rows) * out));
-        check(veda_gemm_nt(rows, out, in, xs.data_ptr(), ldx, wc.data_ptr(), in, value.data_ptr(),
-                           out, dt(xs.dtype()), dt(xs.dtype()), 1.0f, 0.0f, S()),
-              "linear");
-    }
-    auto xin = x.node(), win = w.node();
-    return make({x, w}, std::move(value), [xin, win, xs, ldx, wc, rows, in, out](const Tensor& g) {
-        const Tensor gc = as_dtype(g, xs.dtype());
-        const double es = static_cast<double>(core::dtype_size(xs.dtype()));
-        if (xin->requires_grad && win->requires_grad && gemm_overlap_enabled())
-        {
-            // dW (+)= G^T X on the side stream, dX = G W on this one, then join: everything
-            // after this (including the release of G and X) is ordered after both.
-            bool fresh = false;
-            Tensor& gw = grad_target(*win, &fresh, DType::F32);
-            profile::Scope scope("gemm_bwd", 4.0 * rows * in * out,
-                                 es * (2.0 * static_cast<double>(rows) * out +
-                                       static_cast<double>(out) * in +
-                                       2.0 * static_cast<double>(rows) * in) +
-                                     4.0 * static_cast<double>(out) * in * (fresh ? 1.0 : 2.0));
-            SideStream& side = side_stream();
-            const cudaStream_t main = reinterpret_cast<cudaStream_t>(S());
-            cuda_check(cudaEventRecord(side.fork, main), "gemm fork");
-            cuda_check(cudaStreamWaitEvent(side.stream, side.fork, 0), "gemm fork wait");
-            check(veda_gemm_tn(out, in, rows, gc.data_ptr(), out, xs.data_ptr(), ldx,
-                               gw.data_ptr(), in, dt(xs.dtype()), dt(gw.dtype()), 1.0f,
-                               fresh ? 0.0f : 1.0f, side.stream),
-                  "linear backward (weight)");
-            if (!xin->grad.defined() || xin->is_leaf || xin->grad_zero || !xin->grad_owned)
-            {
-                Tensor d = Tensor::empty(xin->value.shape(), xs.dtype());
-                check(veda_gemm_nn(rows, in, out, gc.data_ptr(), out, wc.data_ptr(), in,
-                                   d.data_ptr(), in, dt(xs.dtype()), dt(xs.dtype()), 1.0f, 0.0f,
-                                   S()),
-                      "linear backward (input)");
-                accumulate(*xin, d);
-            }
-            else
-            {
-                check(veda_gemm_nn(rows, in, out, gc.data_ptr(), out, wc.data_ptr(), in,
-                                   xin->grad.data_ptr(), in, dt(xs.dtype()),
-                                   dt(xin->grad.dtype()), 1.0f, 1.0f, S()),
-                      "linear backward (input)");
-            }
-            cuda_check(cudaEventRecord(side.join, side.stream), "gemm join");
-            cuda_check(cudaStreamWaitEvent(main, side.join, 0), "gemm join wait");
-            return;
-        }
-        if (xin->requires_grad)
-        {
-            // dX = G W  (NN)
-            profile::Scope scope("gemm_dx", 2.0 * rows * in * out,
-                                 es * (static_cast<double>(rows) * out +
-                                       static_cast<double>(out) * in +
-                                       static_cast<double>(rows) * in));
-            if (!xin->grad.defined() || xin->is_leaf || xin->grad_zero || !xin->grad_owned)
-            {
-                Tensor d = Tensor::empty(xin->value.shape(), xs.dtype());
-                check(veda_gemm_nn(rows, in, out, gc.data_ptr(), out, wc.data_ptr(), in,
-                                   d.data_ptr(), in, dt(xs.dtype()), dt(xs.dtype()), 1.0f, 0.0f,
-                                   S()),
-                      "linear backward (input)");
-                accumulate(*xin, d);
-            }
-            else
-            {
-                check(veda_gemm_nn(rows, in, out, gc.data_ptr(), out, wc.data_ptr(), in,
-                                   xin->grad.data_ptr(), in, dt(xs.dtype()),
-                                   dt(xin->grad.dtype()), 1.0f, 1.0f, S()),
-                      "linear backward (input)");
-            }
-        }
-        if (win->requires_grad)
-        {
-            // dW (+)= G^T X  (TN), straight into the fp32 parameter gradient
-            bool fresh = false;
-            Tensor& gw = grad_target(*win, &fresh, DType::F32);
-            profile::Scope scope("gemm_dw", 2.0 * rows * in * out,
-                                 es * (static_cast<double>(rows) * out +
-                                       static_cast<double>(rows) * in) +
-                                     4.0 * static_cast<double>(out) * in * (fresh ? 1.0 : 2.0));
-            check(veda_gemm_tn(out, in, rows, gc.data_ptr(), out, xs.data_ptr(), ldx,
-                               gw.data_ptr(), in, dt(xs.dtype()), dt(gw.dtype()), 1.0f,
-                               fresh ? 0.0f : 1.0f, S()),
-                  "linear backward (weight)");
-        }
-    });
+    l.wc = make_contiguous(wv);
+    l.rows = l.xs.numel() / in;
+    l.in = in;
+    l.out = out;
+    return l;
 }
 
-Variable attention(const Variable& qkv, const Variable& q_norm, const Variable& k_norm,
-                   const Tensor& cosines, const Tensor& sines, size_t B, size_t T, size_t H,
-                   size_t Hkv, size_t Dh, float eps)
+Tensor linear_forward(const LinearSaved& l, const Shape& input_shape)
+{
+    std::vector<size_t> od = input_shape.dims();
+    od.back() = l.out;
+    Tensor value = Tensor::empty(Shape(od), l.xs.dtype());
+    const double es = static_cast<double>(core::dtype_size(l.xs.dtype()));
+    profile::Scope scope("gemm_fwd", 2.0 * l.rows * l.in * l.out,
+                         es * (static_cast<double>(l.rows) * l.in + static_cast<double>(l.out) * l.in +
+                               static_cast<double>(l.rows) * l.out));
+    check(veda_gemm_nt(l.rows, l.out, l.in, l.xs.data_ptr(), l.ldx, l.wc.data_ptr(), l.in,
+                       value.data_ptr(), l.out, dt(l.xs.dtype()), dt(l.xs.dtype()), 1.0f, 0.0f, S()),
+          "linear");
+    return value;
+}
+
+void linear_backward(const LinearSaved& l, const Tensor& g)
+{
+    const auto& xin = l.xin;
+    const auto& win = l.win;
+    const Tensor& xs = l.xs;
+    const Tensor& wc = l.wc;
+    const int64_t ldx = l.ldx;
+    const size_t rows = l.rows, in = l.in, out = l.out;
+    const Tensor gc = as_dtype(g, xs.dtype());
+    const double es = static_cast<double>(core::dtype_size(xs.dtype()));
+    if (xin->requires_grad && win->requires_grad && gemm_overlap_enabled())
+    {
+        // dW (+)= G^T X on the side stream, dX = G W on this one, then join: everything
+        // after this (including the release of G and X) is ordered after both.
+        bool fresh = false;
+        Tensor& gw = grad_target(*win, &fresh, DType::F32);
+        profile::Scope scope("gemm_bwd", 4.0 * rows * in * out,
+                             es * (2.0 * static_cast<double>(rows) * out +
+                                   static_cast<double>(out) * in +
+                                   2.0 * static_cast<double>(rows) * in) +
+                                 4.0 * static_cast<double>(out) * in * (fresh ? 1.0 : 2.0));
+        SideStream& side = side_stream();
+        const cudaStream_t main = reinterpret_cast<cudaStream_t>(S());
+        cuda_check(cudaEventRecord(side.fork, main), "gemm fork");
+        cuda_check(cudaStreamWaitEvent(side.stream, side.fork, 0), "gemm fork wait");
+        check(veda_gemm_tn(out, in, rows, gc.data_ptr(), out, xs.data_ptr(), ldx,
+                           gw.data_ptr(), in, dt(xs.dtype()), dt(gw.dtype()), 1.0f,
+                           fresh ? 0.0f : 1.0f, side.stream),
+              "linear backward (weight)");
+        if (!xin->grad.defined() || xin->is_leaf || xin->grad_zero || !xin->grad_owned)
+        {
+            Tensor d = Tensor::empty(xin->value.shape(), xs.dtype());
+            check(veda_gemm_nn(rows, in, out, gc.data_ptr(), out, wc.data_ptr(), in,
+                               d.data_ptr(), in, dt(xs.dtype()), dt(xs.dtype()), 1.0f, 0.0f,
+                               S()),
+                  "linear backward (input)");
+            accumulate(*xin, d);
+        }
+        else
+        {
+            check(veda_gemm_nn(rows, in, out, gc.data_ptr(), out, wc.data_ptr(), in,
+                               xin->grad.data_ptr(), in, dt(xs.dtype()),
+                               dt(xin->grad.dtype()), 1.0f, 1.0f, S()),
+                  "linear backward (input)");
+        }
+        cuda_check(cudaEventRecord(side.join, side.stream), "gemm join");
+        cuda_check(cudaStreamWaitEvent(main, side.join, 0), "gemm join wait");
+        return;
+    }
+    if (xin->requires_grad)
+    {
+        // dX = G W  (NN)
+        profile::Scope scope("gemm_dx", 2.0 * rows * in * out,
+                             es * (static_cast<double>(rows) * out +
+                                   static_cast<double>(out) * in +
+                                   static_cast<double>(rows) * in));
+        if (!xin->grad.defined() || xin->is_leaf || xin->grad_zero || !xin->grad_owned)
+        {
+            Tensor d = Tensor::empty(xin->value.shape(), xs.dtype());
+            check(veda_gemm_nn(rows, in, out, gc.data_ptr(), out, wc.data_ptr(), in,
+                               d.data_ptr(), in, dt(xs.dtype()), dt(xs.dtype()), 1.0f, 0.0f,
+                               S()),
+                  "linear backward (input)");
+            accumulate(*xin, d);
+        }
+        else
+        {
+            check(veda_gemm_nn(rows, in, out, gc.data_ptr(), out, wc.data_ptr(), in,
+                               xin->grad.data_ptr(), in, dt(xs.dtype()),
+                               dt(xin->grad.dtype()), 1.0f, 1.0f, S()),
+                  "linear backward (input)");
+        }
+    }
+    if (win->requires_grad)
+    {
+        // dW (+)= G^T X  (TN), straight into the fp32 parameter gradient
+        bool fresh = false;
+        Tensor& gw = grad_target(*win, &fresh, DType::F32);
+        profile::Scope scope("gemm_dw", 2.0 * rows * in * out,
+                             es * (static_cast<double>(rows) * out +
+                                   static_cast<double>(rows) * in) +
+                                 4.0 * static_cast<double>(out) * in * (fresh ? 1.0 : 2.0));
+        check(veda_gemm_tn(out, in, rows, gc.data_ptr(), out, xs.data_ptr(), ldx,
+                           gw.data_ptr(), in, dt(xs.dtype()), dt(gw.dtype()), 1.0f,
+                           fresh ? 0.0f : 1.0f, S()),
+              "linear backward (weight)");
+    }
+}
+
+// What the attention backward reads: the fused projection and its leading dimension, the gains
+// and RoPE tables, the normalised rotated q and k, the output and the forward's log-sum-exp.
+struct AttentionSaved
+{
+    std::shared_ptr<Node> xin, qn, kn;
+    Tensor x, qg, kg, c, s;
+    int64_t ld = 0;
+    Tensor qr, kr, out, lse;
+    size_t B = 0, T = 0, H = 0, Hkv = 0, Dh = 0;
+    float eps = 0.0f, scale = 0.0f;
+};
+
+AttentionSaved attention_setup(const Variable& qkv, const Variable& q_norm, const Variable& k_norm,
+                               const Tensor& cosines, const Tensor& sines, size_t B, size_t T,
+                               size_t H, size_t Hkv, size_t Dh, float eps)
 {
     const Tensor& xv = qkv.value();
     const size_t N = B * T;
@@ -1364,88 +1403,155 @@ Variable attention(const Variable& qkv, const Variable& q_norm, const Variable& 
     {
         throw std::invalid_argument("attention: heads must be a multiple of kv_heads");
     }
-    const Tensor x = xv.strides().back() == 1 ? xv : make_contiguous(xv);
-    const int64_t ld = x.ld();
-    const DType d = x.dtype();
+    AttentionSaved a;
+    a.xin = qkv.node();
+    a.qn = q_norm.node();
+    a.kn = k_norm.node();
+    a.x = xv.strides().back() == 1 ? xv : make_contiguous(xv);
+    a.ld = a.x.ld();
+    const DType d = a.x.dtype();
+    a.qg = as_dtype(q_norm.value(), d);
+    a.kg = as_dtype(k_norm.value(), d);
+    a.c = as_dtype(cosines, DType::F32);
+    a.s = as_dtype(sines, DType::F32);
+    a.lse = Tensor::empty(Shape({B * H * T}), DType::F32);
+    a.B = B;
+    a.T = T;
+    a.H = H;
+    a.Hkv = Hkv;
+    a.Dh = Dh;
+    a.eps = eps;
+    a.scale = 1.0f / std::sqrt(static_cast<float>(Dh));
+    return a;
+}
+
+// q and k: RMS norm with their gains, then RoPE, into a.qr and a.kr; then causal GQA attention
+// into a.out, its log-sum-exp into `lse`. Deterministic, so a second run gives the same bits.
+void attention_forward(AttentionSaved& a, float* lse, const char* scope_name)
+{
+    const DType d = a.x.dtype();
     const size_t es = core::dtype_size(d);
-    char* base = static_cast<char*>(x.data_ptr());
-    const Tensor qg = as_dtype(q_norm.value(), d), kg = as_dtype(k_norm.value(), d);
-    const Tensor c = as_dtype(cosines, DType::F32), s = as_dtype(sines, DType::F32);
-    Tensor qr = Tensor::empty(Shape({N, H * Dh}), d);
-    Tensor kr = Tensor::empty(Shape({N, Hkv * Dh}), d);
-    check(veda_qknorm_rope_fwd(base, ld, qg.data_ptr(), static_cast<const float*>(c.data_ptr()),
-                               static_cast<const float*>(s.data_ptr()), qr.data_ptr(), H * Dh, N, H,
-                               T, Dh, eps, dt(d), S()),
+    const size_t N = a.B * a.T, H = a.H, Hkv = a.Hkv, Dh = a.Dh;
+    char* base = static_cast<char*>(a.x.data_ptr());
+    const float* cp = static_cast<const float*>(a.c.data_ptr());
+    const float* sp = static_cast<const float*>(a.s.data_ptr());
+    a.qr = Tensor::empty(Shape({N, H * Dh}), d);
+    a.kr = Tensor::empty(Shape({N, Hkv * Dh}), d);
+    check(veda_qknorm_rope_fwd(base, a.ld, a.qg.data_ptr(), cp, sp, a.qr.data_ptr(), H * Dh, N, H,
+                               a.T, Dh, a.eps, dt(d), S()),
           "attention: q norm + rope");
-    check(veda_qknorm_rope_fwd(base + H * Dh * es, ld, kg.data_ptr(),
-                               static_cast<const float*>(c.data_ptr()),
-                               static_cast<const float*>(s.data_ptr()), kr.data_ptr(), Hkv * Dh, N,
-                               Hkv, T, Dh, eps, dt(d), S()),
+    check(veda_qknorm_rope_fwd(base + H * Dh * es, a.ld, a.kg.data_ptr(), cp, sp, a.kr.data_ptr(),
+                               Hkv * Dh, N, Hkv, a.T, Dh, a.eps, dt(d), S()),
           "attention: k norm + rope");
-    Tensor ctx = Tensor::empty(Shape({N, H * Dh}), d);
-    Tensor lse = Tensor::empty(Shape({B * H * T}), DType::F32);
-    const float scale = 1.0f / std::sqrt(static_cast<float>(Dh));
+    a.out = Tensor::empty(Shape({N, H * Dh}), d);
     // causal: half of the 2 T^2 Dh products per (batch, head) for each of QK^T and PV
-    profile::Scope scope("attn_fwd", 2.0 * B * H * static_cast<double>(T) * T * Dh, 0.0);
-    check(veda_attention_fwd(qr.data_ptr(), H * Dh, kr.data_ptr(), Hkv * Dh,
-                             base + (H + Hkv) * Dh * es, ld, ctx.data_ptr(), H * Dh,
-                             static_cast<float*>(lse.data_ptr()), B, T, H, Hkv, Dh, scale, 1, dt(d),
-                             S()),
+    profile::Scope scope(scope_name, 2.0 * a.B * H * static_cast<double>(a.T) * a.T * Dh, 0.0);
+    check(veda_attention_fwd(a.qr.data_ptr(), H * Dh, a.kr.data_ptr(), Hkv * Dh,
+                             base + (H + Hkv) * Dh * es, a.ld, a.out.data_ptr(), H * Dh, lse, a.B,
+                             a.T, H, Hkv, Dh, a.scale, 1, dt(d), S()),
           "attention");
-    auto xin = qkv.node(), qn = q_norm.node(), kn = k_norm.node();
-    const Tensor out = ctx;
+}
+
+void attention_backward(const AttentionSaved& a, const Tensor& g)
+{
+    const DType d = a.x.dtype();
+    const size_t es = core::dtype_size(d);
+    const size_t B = a.B, T = a.T, H = a.H, Hkv = a.Hkv, Dh = a.Dh;
+    const size_t N = B * T, W = (H + 2 * Hkv) * Dh;
+    const int64_t ld = a.ld;
+    const char* base = static_cast<const char*>(a.x.data_ptr());
+    const Tensor gc = as_dtype(g, d);
+    Tensor dqr = Tensor::empty(Shape({N, H * Dh}), d);
+    Tensor dkr = Tensor::empty(Shape({N, Hkv * Dh}), d);
+    Tensor dx = Tensor::empty(Shape({N, W}), d);
+    char* dbase = static_cast<char*>(dx.data_ptr());
+    const size_t ws_bytes = veda_attention_bwd_workspace(B, T, H, Hkv, Dh, dt(d));
+    Tensor ws = Tensor::empty(Shape({(ws_bytes + 3) / 4}), DType::F32);
+    {
+        // causal backward with the softmax recomputed: 5 products of T^2 Dh per (batch, head)
+        profile::Scope scope("attn_bwd", 5.0 * B * H * static_cast<double>(T) * T * Dh, 0.0);
+        check(veda_attention_bwd(a.qr.data_ptr(), H * Dh, a.kr.data_ptr(), Hkv * Dh,
+                                 base + (H + Hkv) * Dh * es, ld, a.out.data_ptr(), H * Dh,
+                                 gc.data_ptr(), H * Dh, static_cast<const float*>(a.lse.data_ptr()),
+                                 dqr.data_ptr(), H * Dh, dkr.data_ptr(), Hkv * Dh,
+                                 dbase + (H + Hkv) * Dh * es, W, ws.data_ptr(), ws_bytes, B, T, H,
+                                 Hkv, Dh, a.scale, 1, dt(d), S()),
+              "attention backward");
+    }
+    auto norm_bwd = [&](const std::shared_ptr<Node>& gain, const Tensor& gv, const char* src,
+                        const Tensor& dy, char* dst, size_t heads) {
+        float* dgamma = nullptr;
+        if (gain->requires_grad)
+        {
+            bool fresh = false;
+            Tensor& gg = grad_target(*gain, &fresh, DType::F32);
+            if (fresh) memset_zero(gg);
+            dgamma = static_cast<float*>(gg.data_ptr());
+        }
+        const size_t wsb = veda_qknorm_rope_bwd_workspace(N, heads, Dh);
+        Tensor w2 = Tensor::empty(Shape({(wsb + 3) / 4 + 1}), DType::F32);
+        check(veda_qknorm_rope_bwd(src, ld, gv.data_ptr(), static_cast<const float*>(a.c.data_ptr()),
+                                   static_cast<const float*>(a.s.data_ptr()), dy.data_ptr(),
+                                   heads * Dh, dst, W, dgamma, w2.data_ptr(), wsb, N, heads, T, Dh,
+                                   a.eps, dt(d), S()),
+              "attention backward: norm + rope");
+    };
+    norm_bwd(a.qn, a.qg, base, dqr, dbase, H);
+    norm_bwd(a.kn, a.kg, base + H * Dh * es, dkr, dbase + H * Dh * es, Hkv);
+    if (a.xin->requires_grad)
+    {
+        accumulate(*a.xin, dx);
+    }
+}
+} // namespace
+
+Variable linear(const Variable& x, const Variable& w)
+{
+    LinearSaved l = linear_setup(x.value(), x.node(), w);
+    Tensor value = linear_forward(l, x.value().shape());
+    return make({x, w}, std::move(value), [l](const Tensor& g) { linear_backward(l, g); });
+}
+
+Variable attention(const Variable& qkv, const Variable& q_norm, const Variable& k_norm,
+                   const Tensor& cosines, const Tensor& sines, size_t B, size_t T, size_t H,
+                   size_t Hkv, size_t Dh, float eps)
+{
+    AttentionSaved a = attention_setup(qkv, q_norm, k_norm, cosines, sines, B, T, H, Hkv, Dh, eps);
+    attention_forward(a, static_cast<float*>(a.lse.data_ptr()), "attn_fwd");
+    Tensor ctx = a.out;
     return make({qkv, q_norm, k_norm}, std::move(ctx),
-                [xin, qn, kn, x, ld, qg, kg, c, s, qr, kr, out, lse, B, T, H, Hkv, Dh, eps,
-                 scale](const Tensor& g) {
-                    const DType d = x.dtype();
-                    const size_t es = core::dtype_size(d);
-                    const size_t N = B * T, W = (H + 2 * Hkv) * Dh;
-                    const char* base = static_cast<const char*>(x.data_ptr());
-                    const Tensor gc = as_dtype(g, d);
-                    Tensor dqr = Tensor::empty(Shape({N, H * Dh}), d);
-                    Tensor dkr = Tensor::empty(Shape({N, Hkv * Dh}), d);
-                    Tensor dx = Tensor::empty(Shape({N, W}), d);
-                    char* dbase = static_cast<char*>(dx.data_ptr());
-                    const size_t ws_bytes = veda_attention_bwd_workspace(B, T, H, Hkv, Dh, dt(d));
-                    Tensor ws = Tensor::empty(Shape({(ws_bytes + 3) / 4}), DType::F32);
-                    // causal backward with recompute: 5 products of T^2 Dh per (batch, head)
-                    profile::Scope scope("attn_bwd", 5.0 * B * H * static_cast<double>(T) * T * Dh,
-                                         0.0);
-                    check(veda_attention_bwd(qr.data_ptr(), H * Dh, kr.data_ptr(), Hkv * Dh,
-                                             base + (H + Hkv) * Dh * es, ld, out.data_ptr(), H * Dh,
-                                             gc.data_ptr(), H * Dh,
-                                             static_cast<const float*>(lse.data_ptr()),
-                                             dqr.data_ptr(), H * Dh, dkr.data_ptr(), Hkv * Dh,
-                                             dbase + (H + Hkv) * Dh * es, W, ws.data_ptr(),
-                                             ws_bytes, B, T, H, Hkv, Dh, scale, 1, dt(d), S()),
-                          "attention backward");
-                    auto norm_bwd = [&](const std::shared_ptr<Node>& gain, const Tensor& gv,
-                                        const char* src, const Tensor& dy, char* dst, size_t heads) {
-                        float* dgamma = nullptr;
-                        if (gain->requires_grad)
-                        {
-                            bool fresh = false;
-                            Tensor& gg = grad_target(*gain, &fresh, DType::F32);
-                            if (fresh) memset_zero(gg);
-                            dgamma = static_cast<float*>(gg.data_ptr());
-                        }
-                        const size_t wsb = veda_qknorm_rope_bwd_workspace(N, heads, Dh);
-                        Tensor w2 = Tensor::empty(Shape({(wsb + 3) / 4 + 1}), DType::F32);
-                        check(veda_qknorm_rope_bwd(src, ld, gv.data_ptr(),
-                                                   static_cast<const float*>(c.data_ptr()),
-                                                   static_cast<const float*>(s.data_ptr()),
-                                                   dy.data_ptr(), heads * Dh, dst, W, dgamma,
-                                                   w2.data_ptr(), wsb, N, heads, T, Dh, eps, dt(d),
-                                                   S()),
-                              "attention backward: norm + rope");
-                    };
-                    norm_bwd(qn, qg, base, dqr, dbase, H);
-                    norm_bwd(kn, kg, base + H * Dh * es, dkr, dbase + H * Dh * es, Hkv);
-                    if (xin->requires_grad)
-                    {
-                        accumulate(*xin, dx);
-                    }
-                });
+                [a](const Tensor& g) { attention_backward(a, g); });
+}
+
+Variable attention_output(const Variable& qkv, const Variable& q_norm, const Variable& k_norm,
+                          const Variable& o, const Tensor& cosines, const Tensor& sines, size_t B,
+                          size_t T, size_t H, size_t Hkv, size_t Dh, float eps)
+{
+    AttentionSaved a = attention_setup(qkv, q_norm, k_norm, cosines, sines, B, T, H, Hkv, Dh, eps);
+    attention_forward(a, static_cast<float*>(a.lse.data_ptr()), "attn_fwd");
+    LinearSaved l = linear_setup(a.out, nullptr, o);
+    Tensor value = linear_forward(l, a.out.shape());
+    // keep the projection, the gains and the log-sum-exp; q, k after norm + RoPE and the
+    // context are dropped here and formed again by the backward
+    a.qr = Tensor();
+    a.kr = Tensor();
+    a.out = Tensor();
+    l.xs = Tensor();
+    return make({qkv, q_norm, k_norm, o}, std::move(value), [a, l](const Tensor& g) {
+        AttentionSaved r = a;
+        Tensor lse = Tensor::empty(Shape({r.B * r.H * r.T}), DType::F32);
+        attention_forward(r, static_cast<float*>(lse.data_ptr()), "attn_recompute");
+        // the output projection's backward with the recomputed context as its input, whose
+        // gradient a node of its own collects for the attention backward
+        auto ctx = std::make_shared<Node>(r.out);
+        ctx->requires_grad = true;
+        LinearSaved lr = l;
+        lr.xin = ctx;
+        lr.xs = r.out;
+        lr.ldx = static_cast<int64_t>(r.H * r.Dh);
+        linear_backward(lr, g);
+        attention_backward(r, ctx->grad);
+    });
 }
 
 Variable swiglu(const Variable& gate_up)

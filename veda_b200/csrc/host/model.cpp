@@ -336,9 +336,14 @@ Variable TinyTransformer::forward_from(const Variable& x0, size_t B, size_t T)
         if (gate_ && l > 0) gate_(layer_ranges_[l].first, layer_ranges_[l].second);
         if (gate_ && l + 1 == layers_.size()) gate_(final_range_.first, final_range_.second);
         Variable qkv = autograd::linear(a, L.qkv);
-        Variable ctx = autograd::attention(qkv, L.q_norm, L.k_norm, cosines, sines, B, T, H, Hk,
-                                           Dh, eps);
-        Variable b = autograd::add_rms_norm(x, autograd::linear(ctx, L.o), L.post_norm, eps, &x);
+        Variable proj =
+            recompute_attention_
+                ? autograd::attention_output(qkv, L.q_norm, L.k_norm, L.o, cosines, sines, B, T, H,
+                                             Hk, Dh, eps)
+                : autograd::linear(autograd::attention(qkv, L.q_norm, L.k_norm, cosines, sines, B,
+                                                       T, H, Hk, Dh, eps),
+                                   L.o);
+        Variable b = autograd::add_rms_norm(x, proj, L.post_norm, eps, &x);
         Variable h = autograd::swiglu(autograd::linear(b, L.gate_up));
         const Variable& next = l + 1 < layers_.size() ? layers_[l + 1].in_norm : final_norm_;
         a = autograd::add_rms_norm(x, autograd::linear(h, L.down), next, eps, &x);

@@ -393,6 +393,11 @@ int veda_trainer_set_skip_nonfinite(veda_trainer* t, int on)
     return guarded([&] { t->impl->set_skip_nonfinite(on != 0); });
 }
 
+int veda_trainer_set_recompute_attention(veda_trainer* t, int on)
+{
+    return guarded([&] { t->impl->set_recompute_attention(on != 0); });
+}
+
 int veda_trainer_step_skipped(veda_trainer* t, int* skipped)
 {
     return guarded([&] {

@@ -707,6 +707,22 @@ void Trainer::set_skip_nonfinite(bool on)
     }
 }
 
+void Trainer::set_recompute_attention(bool on)
+{
+    if (on == model_->recompute_attention())
+    {
+        return;
+    }
+    model_->set_recompute_attention(on);
+    if (graph_exec_ != nullptr)
+    {
+        cuda_check(cudaStreamSynchronize(cs()), "recompute switch");
+        cudaGraphExecDestroy(graph_exec_);
+        graph_exec_ = nullptr;
+    }
+    eager_steps_ = 0;   // the next step runs eagerly before a capture of the new path
+}
+
 int Trainer::world() const noexcept { return dp_ ? dp_->world() : 1; }
 
 bool Trainer::sharded() const noexcept { return dp_ && dp_->sharded(); }

@@ -50,6 +50,7 @@ SIGNATURES = {
     "veda_trainer_set_comm_timeout": (_i, [_p, C.c_double]),
     "veda_trainer_abort_comm": (_i, [_p]),
     "veda_trainer_set_skip_nonfinite": (_i, [_p, _i]),
+    "veda_trainer_set_recompute_attention": (_i, [_p, _i]),
     "veda_trainer_step_skipped": (_i, [_p, _p]),
     "veda_profile_enable": (_i, [_i]),
     "veda_profile_collect": (_i, [_p, _p, _p, _p, _p, _i]),
@@ -190,6 +191,9 @@ class Trainer:
 
     def set_skip_nonfinite(self, on: bool):
         _check(self.L, self.L.veda_trainer_set_skip_nonfinite(self.h, 1 if on else 0))
+
+    def set_recompute_attention(self, on: bool):
+        _check(self.L, self.L.veda_trainer_set_recompute_attention(self.h, 1 if on else 0))
 
     def step_skipped(self) -> bool:
         out = C.c_int(0)
