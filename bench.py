@@ -261,7 +261,7 @@ def run_veda(args):
     if world > 1:
         obj = [TA.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
-        tr.init_dp(obj[0], rank, world, 25 << 20, sharded=args.dp == "sharded")
+        tr.init_dp(obj[0], rank, world, args.bucket_mb << 20, sharded=args.dp == "sharded")
 
     # synthetic batches (per rank, per step), pinned on the host and resident on the device
     nb = 4
@@ -356,7 +356,7 @@ def run_veda(args):
         "config": {"workload": args.workload, "model": args.workload, "global_batch": B * world,
                    "micro_batch": B, "seq_len": T, "parallelism": f"dp{world}",
                    "params": tr.n, "l2": "inputs and the step's working set exceed L2",
-                   "buckets_mb": 25, "attention_recompute": recompute,
+                   "buckets_mb": args.bucket_mb, "attention_recompute": recompute,
                    "optimizer_state": ("sharded (ZeRO-1)" if world > 1 and args.dp == "sharded"
                                        else "replicated")},
         "mfu_model_tflops": model_flops_per_token(c, T) * value / 1e12,
@@ -419,6 +419,8 @@ def main():
     ap.add_argument("--impl", default="veda", choices=["veda", "reference"])
     ap.add_argument("--workload", default="qwen3-0.6b", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--bucket-mb", type=int, default=25,
+                    help="N > 1: gradient bucket size in MiB")
     ap.add_argument("--recompute", default="auto", choices=["auto", "on", "off"],
                     help="activation recompute of attention (auto: on for qwen3-1.7b, the config "
                          "that names it)")

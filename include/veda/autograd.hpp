@@ -123,6 +123,14 @@ Variable swiglu(const Variable& gate_up);
 // Token ids already on the device (int64 [count]); ids are checked on the device and an
 // out-of-range id raises std::out_of_range at the next synchronisation point.
 Variable embedding_device(const Variable& table, const core::Tensor& ids);
+// Receives the ids (int64 [count] on the device) and the output gradient rows [count, D] of an
+// embedding_device_rows node.
+using RowsSink = std::function<void(const core::Tensor& ids, size_t count, const core::Tensor& rows)>;
+// embedding_device whose backward hands the ids and the gradient rows to `sink` instead of
+// scattering them into the table's gradient. The table is not an input of the node, so with a
+// tied LM head the table's gradient is final as soon as the head's backward has run (a
+// data-parallel step exchanges it then, and the scattered rows separately at the end).
+Variable embedding_device_rows(const Variable& table, const core::Tensor& ids, RowsSink sink);
 // Mean cross-entropy with device targets (int64 [lanes]).
 Variable cross_entropy_device(const Variable& logits, const core::Tensor& targets);
 

@@ -103,6 +103,11 @@ public:
     // Called with an arena range [lo, hi) before the forward first reads the weights in it, so
     // that a data-parallel step whose updated weights are still arriving waits only for them.
     void set_weight_gate(std::function<void(size_t, size_t)> gate) { gate_ = std::move(gate); }
+    // forward_device looks the tokens up through autograd::embedding_device_rows with this sink
+    // (empty: the plain embedding, whose backward scatters into the table's gradient).
+    void set_embedding_rows_sink(autograd::RowsSink sink) { rows_sink_ = std::move(sink); }
+    // The embedding table's range in the arenas, in elements.
+    std::pair<size_t, size_t> embedding_range() const noexcept { return embed_range_; }
     // Activation recompute of attention: each layer's attention and output projection become one
     // node that keeps the fused projection and the log-sum-exp only, and forms q, k and the
     // context again in the backward (off by default).
@@ -120,6 +125,7 @@ private:
     size_t arena_len_ = 0;
     std::function<void(size_t, size_t)> gate_;
     bool recompute_attention_ = false;
+    autograd::RowsSink rows_sink_;
     std::pair<size_t, size_t> embed_range_, final_range_;
     std::vector<std::pair<size_t, size_t>> layer_ranges_;
     std::vector<autograd::Variable> parameters_;

@@ -201,6 +201,17 @@ int veda_embedding_bwd(const int64_t* ids, int64_t count, const void* dout, int6
                        int64_t vocab, int64_t dim, float* dtable, int deterministic,
                        void* workspace, size_t workspace_bytes, int dtype, veda_stream_t stream);
 size_t veda_embedding_bwd_workspace(int64_t count);
+/* The deterministic scatter of veda_embedding_bwd in two halves, for a caller that moves the rows
+ * between them (the data-parallel exchange of the embedding's scattered rows). sort: keys[i] =
+ * (id << 32 | position) of `count` <= 16384 positions, ascending (out-of-range ids last).
+ * apply_sorted: for every id in [id_lo, id_hi), dtable[(id - id_lo) * dim ..] += its rows of
+ * dout in key order; other ids are skipped. Applying the key lists of several senders one after
+ * the other adds each id's rows in (sender, position) order. */
+int veda_embedding_sort(const int64_t* ids, int64_t count, int64_t vocab, uint64_t* keys,
+                        veda_stream_t stream);
+int veda_embedding_apply_sorted(const uint64_t* keys, int64_t count, const void* dout, int64_t ldd,
+                                int64_t dim, int64_t id_lo, int64_t id_hi, float* dtable,
+                                int dtype, veda_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------- */
 /* Global-norm clip + AdamW (optim::clip_gradient_norm, src/libs/optim/Clip.cpp:12-61;        */

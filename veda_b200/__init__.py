@@ -64,6 +64,8 @@ SIGNATURES = {
     "veda_embedding_fwd": (_i, [_p, _i64, _p, _i64, _i64, _p, _i64, _p, _i, _p]),
     "veda_embedding_bwd": (_i, [_p, _i64, _p, _i64, _i64, _i64, _p, _i, _p, _sz, _i, _p]),
     "veda_embedding_bwd_workspace": (_sz, [_i64]),
+    "veda_embedding_sort": (_i, [_p, _i64, _i64, _p, _p]),
+    "veda_embedding_apply_sorted": (_i, [_p, _i64, _p, _i64, _i64, _i64, _i64, _p, _i, _p]),
     "veda_sumsq": (_i, [_p, _i64, _p, _i, _p, _sz, _p]),
     "veda_sumsq_workspace": (_sz, [_i64]),
     "veda_clip_apply": (_i, [_p, _i64, _p, _f, _p]),

@@ -133,11 +133,12 @@ sort_chunk_kernel(const int64_t* __restrict__ ids, int64_t first, int n, int64_t
     }
 }
 
-// One warp per segment start: adds the segment's rows in position order onto dtable[id].
+// One warp per segment start: adds the segment's rows in position order onto
+// dtable[id - id_lo] for ids in [id_lo, id_hi) (the others are skipped).
 template <typename T>
 __global__ void apply_segments_kernel(const uint64_t* __restrict__ sorted, int n, int64_t first,
                                       const T* __restrict__ dout, int64_t ldd, int64_t dim,
-                                      float* __restrict__ dtable)
+                                      float* __restrict__ dtable, int64_t id_lo, int64_t id_hi)
 {
     const int lane = threadIdx.x & 31;
     const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -146,7 +147,7 @@ __global__ void apply_segments_kernel(const uint64_t* __restrict__ sorted, int n
     {
         const uint64_t key = sorted[e];
         const uint32_t id = static_cast<uint32_t>(key >> 32);
-        if (id == 0xFFFFFFFFu)
+        if (id == 0xFFFFFFFFu || static_cast<int64_t>(id) < id_lo || static_cast<int64_t>(id) >= id_hi)
         {
             continue;
         }
@@ -159,7 +160,7 @@ __global__ void apply_segments_kernel(const uint64_t* __restrict__ sorted, int n
         {
             ++end;
         }
-        float* row = dtable + static_cast<int64_t>(id) * dim;
+        float* row = dtable + (static_cast<int64_t>(id) - id_lo) * dim;
         for (int64_t d = lane; d < dim; d += 32)
         {
             float acc = row[d];
@@ -269,14 +270,70 @@ extern "C" int veda_embedding_bwd(const int64_t* ids, int64_t count, const void*
         if (dtype == VEDA_BF16)
         {
             apply_segments_kernel<bf16><<<grid, 256, 0, stream>>>(
-                sorted, n, first, static_cast<const bf16*>(dout), ldd, dim, dtable);
+                sorted, n, first, static_cast<const bf16*>(dout), ldd, dim, dtable, 0, vocab);
         }
         else
         {
             apply_segments_kernel<float><<<grid, 256, 0, stream>>>(
-                sorted, n, first, static_cast<const float*>(dout), ldd, dim, dtable);
+                sorted, n, first, static_cast<const float*>(dout), ldd, dim, dtable, 0, vocab);
         }
         count_launch(2);
     }
     return check_launch("veda_embedding_bwd");
+}
+
+extern "C" int veda_embedding_sort(const int64_t* ids, int64_t count, int64_t vocab,
+                                   uint64_t* keys, veda_stream_t stream)
+{
+    VEDA_REQUIRE(count >= 0 && count <= kChunk, "count must lie in [0, 16384]");
+    VEDA_REQUIRE(vocab > 0 && vocab < 0xFFFFFFFFll, "bad vocabulary");
+    if (count == 0)
+    {
+        return VEDA_OK;
+    }
+    VEDA_REQUIRE(ids != nullptr && keys != nullptr, "null pointer");
+    static bool configured = false;
+    if (!configured)
+    {
+        cudaFuncSetAttribute(sort_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kChunk * static_cast<int>(sizeof(uint64_t)));
+        configured = true;
+    }
+    const int n = static_cast<int>(count);
+    int size = 1;
+    while (size < n)
+    {
+        size <<= 1;
+    }
+    sort_chunk_kernel<<<1, kSortThreads, size * sizeof(uint64_t), stream>>>(ids, 0, n, vocab, keys);
+    count_launch();
+    return check_launch("veda_embedding_sort");
+}
+
+extern "C" int veda_embedding_apply_sorted(const uint64_t* keys, int64_t count, const void* dout,
+                                           int64_t ldd, int64_t dim, int64_t id_lo, int64_t id_hi,
+                                           float* dtable, int dtype, veda_stream_t stream)
+{
+    VEDA_REQUIRE(valid_dtype(dtype), "unknown dtype");
+    VEDA_REQUIRE(count >= 0 && count <= kChunk, "count must lie in [0, 16384]");
+    VEDA_REQUIRE(dim > 0 && ldd >= dim && id_lo >= 0 && id_hi >= id_lo, "bad shape");
+    if (count == 0 || id_hi == id_lo)
+    {
+        return VEDA_OK;
+    }
+    VEDA_REQUIRE(keys != nullptr && dout != nullptr && dtable != nullptr, "null pointer");
+    const int n = static_cast<int>(count);
+    const unsigned grid = grid_for(static_cast<int64_t>(n) * 32, 256);
+    if (dtype == VEDA_BF16)
+    {
+        apply_segments_kernel<bf16><<<grid, 256, 0, stream>>>(
+            keys, n, 0, static_cast<const bf16*>(dout), ldd, dim, dtable, id_lo, id_hi);
+    }
+    else
+    {
+        apply_segments_kernel<float><<<grid, 256, 0, stream>>>(
+            keys, n, 0, static_cast<const float*>(dout), ldd, dim, dtable, id_lo, id_hi);
+    }
+    count_launch();
+    return check_launch("veda_embedding_apply_sorted");
 }

@@ -925,6 +925,33 @@ Variable embedding_device(const Variable& table, const Tensor& ids)
     return embedding_impl(table, ids, count, Shape({count, table.value().shape()[1]}), true);
 }
 
+Variable embedding_device_rows(const Variable& table, const Tensor& ids, RowsSink sink)
+{
+    if (table.value().rank() != 2)
+    {
+        throw std::invalid_argument("embedding_device_rows: the table must be rank 2 [V, D]");
+    }
+    const size_t V = table.value().shape()[0], D = table.value().shape()[1];
+    const size_t count = ids.numel() * core::dtype_size(ids.dtype()) / sizeof(int64_t);
+    const Tensor tc = make_contiguous(table.value());
+    Tensor value = Tensor::empty(Shape({count, D}), tc.dtype());
+    check(veda_embedding_fwd(static_cast<const int64_t*>(ids.data_ptr()), count, tc.data_ptr(), V,
+                             D, value.data_ptr(), D, detail::device_flag(), dt(tc.dtype()), S()),
+          "embedding");
+    if (!table.requires_grad())
+    {
+        return Variable::leaf(std::move(value), false);
+    }
+    // on the tape (it receives its gradient) but with no parents: the table's gradient does not
+    // wait for this node
+    auto node = std::make_shared<Node>(std::move(value));
+    node->requires_grad = true;
+    node->backward = [sink = std::move(sink), ids, count](const Tensor& g) {
+        sink(ids, count, make_contiguous(g));
+    };
+    return Variable(std::move(node));
+}
+
 Variable reshape(const Variable& x, const Shape& shape)
 {
     Tensor value = x.value().reshape(shape);

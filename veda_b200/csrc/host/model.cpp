@@ -309,7 +309,8 @@ Variable TinyTransformer::forward_device(const Tensor& ids, size_t batch, size_t
         throw std::invalid_argument("TinyTransformer::forward: window exceeds the context limit");
     }
     if (gate_) gate_(embed_range_.first, embed_range_.second);
-    Variable x = autograd::embedding_device(embed_, ids);
+    Variable x = rows_sink_ ? autograd::embedding_device_rows(embed_, ids, rows_sink_)
+                            : autograd::embedding_device(embed_, ids);
     return forward_from(x, batch, length);
 }
 

@@ -159,7 +159,15 @@ public:
     // parameters first), each waiting for every graph leaf that overlaps it. Sharded, every
     // bucket is a whole number of 16-byte rows per rank, and rank r owns the r-th of the world
     // equal parts of each bucket; its parts, in arena order, make up its shard.
-    void attach(TinyTransformer& model, size_t bucket_bytes, const float* master, size_t steps)
+    //
+    // The tied embedding table is one bucket of its own when its rows split evenly across the
+    // ranks (rank r then owns the table rows [r V/world, (r+1) V/world)): its gradient holds only
+    // the LM head's dW until the end of the backward, so it is reduced as soon as the head's
+    // backward has run, and the rows the embedding lookup scatters (at most `tokens` per rank)
+    // are exchanged separately at the end and added onto the reduced table in (rank, position)
+    // order (embedding_rows).
+    void attach(TinyTransformer& model, size_t bucket_bytes, const float* master, size_t steps,
+                size_t tokens)
     {
         arena_ = static_cast<float*>(model.grad_arena().data_ptr());
         values_ = model.value_arena().data_ptr();
@@ -172,15 +180,38 @@ public:
             throw std::invalid_argument("DataParallel: the arena does not split into " +
                                         std::to_string(world_) + " shards");
         }
+        const auto [e0, e1] = model.embedding_range();
+        vocab_ = model.config().vocab_size;
+        dim_ = model.config().hidden_size;
+        tokens_ = tokens;
+        const char* rows_env = std::getenv("VEDA_DP_EMBEDDING_ROWS");
+        rows_exchange_ = model.config().tie_word_embeddings && tokens > 0 && tokens <= 16384 &&
+                         vocab_ % static_cast<size_t>(world_) == 0 && e0 % unit == 0 &&
+                         e1 % unit == 0 && e1 - e0 == vocab_ * dim_ &&
+                         (rows_env == nullptr || std::atoi(rows_env) != 0);
         const size_t per = std::max<size_t>(unit, bucket_bytes / sizeof(float) / unit * unit);
-        for (size_t end = total_; end > 0;)
+        auto cut = [&](size_t lo, size_t hi) {
+            for (size_t end = hi; end > lo;)
+            {
+                const size_t begin = end - lo > per ? end - per : lo;
+                add_bucket(begin, end);
+                end = begin;
+            }
+        };
+        if (rows_exchange_)
         {
-            const size_t begin = end > per ? end - per : 0;
-            Bucket b{begin, end, 0, 0, 0, false, true, nullptr, nullptr};
-            cuda_check(cudaEventCreateWithFlags(&b.ready, cudaEventDisableTiming), "bucket event");
-            cuda_check(cudaEventCreateWithFlags(&b.gathered, cudaEventDisableTiming), "bucket event");
-            buckets_.push_back(b);
-            end = begin;
+            cut(e1, total_);
+            rows_bucket_ = buckets_.size();
+            add_bucket(e0, e1);
+            cut(0, e0);
+            const size_t n = tokens * static_cast<size_t>(world_);
+            keys_ = Tensor::empty(Shape({2 * tokens}), DType::F32);   // uint64 payloads
+            keys_all_ = Tensor::empty(Shape({2 * n}), DType::F32);
+            rows_all_ = Tensor::empty(Shape({n, dim_}), model.dtype());
+        }
+        else
+        {
+            cut(0, total_);
         }
         for (const auto& leaf : model.graph_leaves())
         {
@@ -286,7 +317,59 @@ public:
             }
         }
         join_comm();
+        rows_held_ = Tensor();   // the exchange has read them (ordered before later work)
         veda_set_reserved_sms(0);
+    }
+
+    bool rows_exchange() const noexcept { return rows_exchange_; }
+
+    // The embedding lookup's backward (autograd::embedding_device_rows): this rank's (id,
+    // position) keys sorted, every rank's keys and gradient rows all-gathered on the
+    // communication stream after the table's own reduction, then each rank's rows added onto
+    // this rank's reduced table rows (sharded: its own row range; replicated: the whole table),
+    // rank after rank, each in its key order: deterministic, and the same sum on every rank.
+    void embedding_rows(const Tensor& ids, size_t count, const Tensor& rows)
+    {
+        if (count != tokens_ || rows.numel() != count * dim_ || rows.dtype() != rows_all_.dtype())
+        {
+            throw std::logic_error("data parallel: the embedding rows do not match the batch");
+        }
+        const int d = static_cast<int>(rows.dtype());
+        uint64_t* keys = static_cast<uint64_t*>(keys_.data_ptr());
+        check(veda_embedding_sort(static_cast<const int64_t*>(ids.data_ptr()),
+                                  static_cast<int64_t>(count), static_cast<int64_t>(vocab_), keys,
+                                  current_stream()),
+              "embedding rows: sort");
+        Bucket& table = buckets_[rows_bucket_];
+        if (!table.launched)
+        {
+            launch(rows_bucket_);
+        }
+        rows_held_ = rows;
+        fork_comm();
+        uint64_t* keys_all = static_cast<uint64_t*>(keys_all_.data_ptr());
+        settle(ncclGroupStart(), "embedding rows all-gather");
+        settle(ncclAllGather(keys, keys_all, count, ncclUint64, comm_, stream_),
+               "embedding rows all-gather");
+        settle(ncclAllGather(rows.data_ptr(), rows_all_.data_ptr(), count * dim_,
+                             rows.dtype() == DType::BF16 ? ncclBfloat16 : ncclFloat, comm_, stream_),
+               "embedding rows all-gather");
+        settle(ncclGroupEnd(), "embedding rows all-gather");
+        const size_t per_rank = vocab_ / static_cast<size_t>(world_);
+        float* target = sharded_ ? static_cast<float*>(g_s_.data_ptr()) + table.shard_at
+                                 : arena_ + table.begin;
+        const size_t lo = sharded_ ? static_cast<size_t>(rank_) * per_rank : 0;
+        const size_t hi = sharded_ ? lo + per_rank : vocab_;
+        const size_t es = core::dtype_size(rows.dtype());
+        for (int r = 0; r < world_; ++r)
+        {
+            check(veda_embedding_apply_sorted(
+                      keys_all + static_cast<size_t>(r) * count, static_cast<int64_t>(count),
+                      static_cast<const char*>(rows_all_.data_ptr()) + static_cast<size_t>(r) * count * dim_ * es,
+                      static_cast<int64_t>(dim_), static_cast<int64_t>(dim_),
+                      static_cast<int64_t>(lo), static_cast<int64_t>(hi), target, d, stream_),
+                  "embedding rows: apply");
+        }
     }
 
     // Sharded step: global norm of the averaged gradient (a sum over the shards), clip + AdamW on
@@ -502,6 +585,14 @@ private:
         cudaEvent_t ready, gathered;
     };
 
+    void add_bucket(size_t begin, size_t end)
+    {
+        Bucket b{begin, end, 0, 0, 0, false, true, nullptr, nullptr};
+        cuda_check(cudaEventCreateWithFlags(&b.ready, cudaEventDisableTiming), "bucket event");
+        cuda_check(cudaEventCreateWithFlags(&b.gathered, cudaEventDisableTiming), "bucket event");
+        buckets_.push_back(b);
+    }
+
     void launch(size_t i)
     {
         Bucket& b = buckets_[i];
@@ -609,6 +700,10 @@ private:
     size_t params_ = 0, total_ = 0, shard_ = 0, steps_ = 0;
     std::vector<Bucket> buckets_;
     std::unordered_map<autograd::Node*, std::vector<size_t>> leaf_buckets_;
+    // the embedding rows exchange (attach)
+    bool rows_exchange_ = false;
+    size_t rows_bucket_ = 0, vocab_ = 0, dim_ = 0, tokens_ = 0;
+    Tensor keys_, keys_all_, rows_all_, rows_held_;
     Tensor g_s_, master_s_, m_s_, v_s_, lowp_s_, sumsq_, ws_, bias_;
     double bias_host_[2] = {1.0, 1.0};
 };
@@ -635,6 +730,7 @@ Trainer::Trainer(ModelConfig config, optim::AdamWConfig adam, float max_norm, DT
 
 Trainer::~Trainer()
 {
+    model_->set_embedding_rows_sink({});   // it points into dp_
     if (graph_exec_ != nullptr)
     {
         cudaGraphExecDestroy(graph_exec_);
@@ -654,12 +750,25 @@ void Trainer::init_data_parallel(const void* nccl_unique_id, int rank, int world
     }
     if (world == 1)
     {
+        model_->set_embedding_rows_sink({});
+        model_->set_weight_gate({});
         dp_.reset();
         return;
     }
     dp_ = std::make_unique<DataParallel>(nccl_unique_id, rank, world, sharded);
-    dp_->attach(*model_, bucket_bytes, master_weights(), opt_->steps());
+    dp_->attach(*model_, bucket_bytes, master_weights(), opt_->steps(), batch_ * length_);
     dp_->set_skip_nonfinite(skip_nonfinite_);
+    if (dp_->rows_exchange())
+    {
+        DataParallel* dp = dp_.get();
+        model_->set_embedding_rows_sink([dp](const Tensor& ids, size_t count, const Tensor& rows) {
+            dp->embedding_rows(ids, count, rows);
+        });
+    }
+    else
+    {
+        model_->set_embedding_rows_sink({});
+    }
     if (sharded)
     {
         DataParallel* dp = dp_.get();
