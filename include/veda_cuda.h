@@ -112,8 +112,9 @@ int veda_add_rmsnorm_fwd(const void* x, int64_t ldx, const void* r, int64_t ldr,
                          int64_t rows, int64_t n, float eps, int dtype, veda_stream_t stream);
 /* Backward (src/libs/autograd/NonLinear.cpp:153-201 and the gain's mul/unbroadcast,
  * Variable.cpp:218-239): dx = dresid + (G/r - x * sum(G x)/(n r^3)), G = dy * gamma;
- * dgamma (fp32 [n], may be NULL) += sum over rows of dy * x / r. dresid may be NULL.
- * workspace: veda_rmsnorm_bwd_workspace(rows, n) bytes of device scratch (NULL if dgamma NULL). */
+ * dgamma (fp32 [n], may be NULL) += sum over rows of dy * x / r, in a fixed order. dresid may be
+ * NULL. workspace: veda_rmsnorm_bwd_workspace(rows, n) bytes of device scratch (NULL if dgamma
+ * NULL). */
 int veda_rmsnorm_bwd(const void* x, int64_t ldx, const void* gamma, const void* dy, int64_t lddy,
                      const void* dresid, int64_t ldr, void* dx, int64_t lddx, float* dgamma,
                      void* workspace, size_t workspace_bytes, int64_t rows, int64_t n, float eps,
@@ -148,7 +149,7 @@ int veda_qknorm_rope_fwd(const void* x, int64_t ldx, const void* gamma, const fl
                          int64_t seq_len, int64_t head_dim, float eps, int dtype,
                          veda_stream_t stream);
 /* Backward: rotate dy by -theta (Views.cpp:136-171), then the gain and norm backward as above.
- * dgamma (fp32 [head_dim]) += sum over tokens and heads. */
+ * dgamma (fp32 [head_dim]) += sum over tokens and heads, in a fixed order. */
 int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamma, const float* cos,
                          const float* sin, const void* dy, int64_t lddy, void* dx, int64_t lddx,
                          float* dgamma, void* workspace, size_t workspace_bytes, int64_t tokens,
@@ -323,7 +324,7 @@ int veda_decode_qkv_at(const void* qkv, const void* q_gain, const void* k_gain, 
 int veda_decode_advance(int64_t* pos, veda_stream_t stream);
 /* One activation row through a Linear layer (x . W^T of Variable.cpp:325, matmul_nt, at M = 1):
  * y[i] = sum_j x[j] * w[i, j] for i < n, j < k, rows of w at stride ldw; fp32 accumulation, each
- * output rounded once. HBM-bound: every weight byte is read once. k * element size <= 48 KB. */
+ * output rounded once. HBM-bound: every weight byte is read once. k * element size <= 47 KB. */
 int veda_gemv_nt(const void* x, const void* w, int64_t ldw, void* y, int64_t n, int64_t k, int dtype,
                  veda_stream_t stream);
 /* The gate/up Linear and SwiGLU of one row in one pass: w_gate_up holds the gate rows [0, f) and
@@ -334,7 +335,7 @@ int veda_gemv_swiglu(const void* x, const void* w_gate_up, int64_t ldw, void* h,
 /* veda_gemv_nt / veda_gemv_swiglu on the pre-norm of a residual row (Model.cpp:242-249): the
  * activation is RMSNorm(s) * gamma with s = x + r (r may be NULL: s = x), s rounded to the dtype
  * and written to sum when sum is not NULL (sum must not alias x or r); 2 k * element size
- * <= 48 KB. */
+ * <= 47 KB. */
 int veda_gemv_rmsnorm(const void* x, const void* r, const void* gamma, float eps, void* sum,
                       const void* w, int64_t ldw, void* y, int64_t n, int64_t k, int dtype,
                       veda_stream_t stream);

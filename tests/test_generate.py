@@ -94,7 +94,10 @@ def test_qwen_shaped_bf16_cached_generation_matches_uncached():
 
 @pytest.mark.parametrize("dtype,heads,kv,dh,pos", [(0, 4, 2, 16, 0), (1, 16, 8, 128, 37), (0, 4, 4, 128, 5),
                                                   (1, 16, 4, 128, 300), (1, 32, 4, 128, 50), (1, 16, 8, 128, 0),
-                                                  (1, 16, 8, 128, 1000), (0, 8, 4, 128, 200)])
+                                                  (1, 16, 8, 128, 1000), (0, 8, 4, 128, 200),
+                                                  # eight query heads a KV head over several slices;
+                                                  # capacity 257, one row past single-slice decode
+                                                  (1, 32, 4, 128, 300), (1, 16, 8, 128, 254)])
 def test_decode_step_kernels_read_the_device_position(dtype, heads, kv, dh, pos):
     """One token's QK-norm + RoPE at the position held in device memory, its K/V rows written into
     the cache at that position, and attention over positions 0..pos: the two-launch path against
@@ -186,7 +189,8 @@ def test_decode_step_kernels_read_the_device_position(dtype, heads, kv, dh, pos)
 
 
 @pytest.mark.parametrize("dtype,k,with_r", [(1, 1024, True), (1, 1024, False), (1, 2048, True),
-                                            (0, 96, True), (1, 200, True)])
+                                            (0, 96, True), (1, 200, True),
+                                            (1, 12032, True)])   # the largest row and gain staged
 def test_gemv_with_rmsnorm_prologue(dtype, k, with_r):
     """The pre-norm computed inside the projection equals the separate add + RMSNorm then the
     projection: the residual sum bit for bit, the outputs within one rounding of the dtype."""
@@ -237,11 +241,15 @@ def test_gemv_with_rmsnorm_prologue(dtype, k, with_r):
         (1e-4 if dtype == 0 else 2e-2)
     assert V.lib().veda_gemv_rmsnorm(dx.data_ptr(), rp, dg.data_ptr(), 1e-6, dx.data_ptr(), dw.data_ptr(), k,
                                      y.data_ptr(), 2 * n, k, dt, stream()) == V.ERR_INVALID_ARGUMENT
+    if k == 12032:   # one more 16-byte chunk of row and gain no longer fits the staged 47 KB
+        assert V.lib().veda_gemv_rmsnorm(dx.data_ptr(), rp, dg.data_ptr(), 1e-6, None, dw.data_ptr(), k,
+                                         y.data_ptr(), 2 * n, k + 8, dt, stream()) == V.ERR_INVALID_ARGUMENT
 
 
 @pytest.mark.parametrize("dtype,n,k,ldw", [(0, 37, 24, 24), (1, 1024, 3072, 3072), (1, 9000, 1024, 1032),
                                           (1, 5, 19, 21), (0, 8200, 96, 100), (1, 300, 2048, 2048),
-                                          (0, 100, 1536, 1540), (1, 7, 2056, 2056)])
+                                          (0, 100, 1536, 1540), (1, 7, 2056, 2056),
+                                          (1, 64, 24064, 24064)])   # the largest row staged
 def test_gemv_matches_row_product(dtype, n, k, ldw):
     """One activation row through a Linear layer (both rows-per-warp variants, rows split across 1, 2
     or 4 warps, the 16-byte and the element-wise paths) against the float64 product; gate/up + SwiGLU in one pass equals

@@ -32,7 +32,8 @@ def rng(seed):
 # ---------------------------------------------------------------------------------------------
 @pytest.mark.parametrize("dtype,rows,n", [(V.F32, 128, 64), (V.F32, 37, 100), (V.BF16, 8192, 1024),
                                           (V.BF16, 33, 2048), (V.F32, 8192, 1024),
-                                          (V.BF16, 1001, 512), (V.F32, 77, 2048)])
+                                          (V.BF16, 1001, 512), (V.F32, 77, 2048),
+                                          (V.BF16, 300, 256), (V.BF16, 20001, 1024)])
 def test_rmsnorm_fwd_bwd(dtype, rows, n):
     r = rng(rows + n)
     x = r.standard_normal((rows, n)).astype(F32)
@@ -129,7 +130,11 @@ def test_rmsnorm_plain_matches_golden():
 @pytest.mark.parametrize("dtype,B,T,H,Dh,theta", [(V.F32, 4, 32, 4, 16, 1e4),
                                                  (V.BF16, 2, 256, 16, 128, 1e6),
                                                  (V.BF16, 3, 100, 3, 128, 1e6),
-                                                 (V.F32, 1, 64, 8, 128, 1e6)])
+                                                 (V.F32, 1, 64, 8, 128, 1e6),
+                                                 # many rows per warp: positions and heads stepped
+                                                 # across the sequence and token boundaries
+                                                 (V.BF16, 8, 2048, 8, 128, 1e6),
+                                                 (V.BF16, 40, 100, 3, 128, 1e6)])
 def test_qknorm_rope(dtype, B, T, H, Dh, theta):
     r = rng(T + H)
     N = B * T

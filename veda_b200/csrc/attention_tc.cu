@@ -795,20 +795,20 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
 //   warps 4-11   elementwise, thread = key row, 64 query columns each. Phase 1: P^T = exp2(S^T
 //                scale log2e - LSE log2e) (causal mask on the diagonal tile only), written as bf16
 //                pairs over the first half of the warp's own S^T columns. Phase 2: dS^T = P^T (dP^T
-//                - D), bf16 pairs over the first half of the warp's dP^T columns and into the
-//                swizzled shared tile the dQ product reads;
+//                - D), bf16, into the swizzled shared tile both the dQ and the dK products read;
 //   warp 12      TMA (112 registers): K and V once; per query tile Q with its -LSE log2(e) and D
 //                rows (2 stages) and dO (1 stage);
 //   warp 13      MMA (112 registers), every product M128 x N128 x K128: per tile i the order is
-//                  S^T(i+1) = K Q^T,  dK += dS^T(i) Q,  dQ(i) = dS(i) K,  dP^T(i+1) = V dO^T,
+//                  S^T(i+1) = K Q^T,  dQ(i) = dS(i) K,  dK += dS^T(i) Q,  dP^T(i+1) = V dO^T,
 //                  dV += P^T(i+1) dO
 //                so the elementwise work of each phase overlaps other products: P(i+1) is formed
-//                while dK(i) and dQ(i) run, dS(i+1) while dV(i+1) and S^T(i+2) run;
+//                while dQ(i) and dK(i) run, dS(i+1) while dV(i+1) and S^T(i+2) run; dQ(i) comes
+//                before dK(i) so that its drain overlaps dK(i) (dP^T(i+1) reuses its columns);
 //   warps 14-15  idle (they complete the warpgroup that gives up registers).
 // dK and dV are summed over the group's query heads in TMEM and written once. The order in which
 // the key tiles of a query add into its accumulator varies between runs, so dQ is not
 // bit-reproducible; the two-kernel path is (veda_attention_set_deterministic).
-// TMEM columns: S^T -> P^T [0, 128) | dP^T -> dS^T, then dQ [128, 256) | dV | dK.
+// TMEM columns: S^T -> P^T [0, 128) | dP^T, then dQ [128, 256) | dV | dK.
 // ---------------------------------------------------------------------------------------------
 constexpr int kFq = 128;                            // queries per tile
 constexpr int kSoftWarps = 8;                       // two per TMEM lane quarter, 64 columns each
@@ -1048,6 +1048,7 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
             const uint64_t do_kmaj = smem_desc(smem_u32(sdo), 16, 1024);   // dO for dP^T
             const uint64_t do_mnmaj = smem_desc(smem_u32(sdo), kHalf, 1024); // dO for dV
             const uint64_t ds_mnmaj = smem_desc(smem_u32(sds), kHalf, 1024); // dS for dQ
+            const uint64_t ds_kmaj = smem_desc(smem_u32(sds), 16, 1024);     // dS^T for dK
             auto kmaj_step = [](int ks) {   // k-step of a K-major [128 x 128] tile
                 return static_cast<uint32_t>((ks >> 2) * kHalf + (ks & 3) * 32);
             };
@@ -1098,17 +1099,10 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
                 {
                     issue_s(it + 1);
                 }
-                mbar_wait(ds_full, it & 1, p.status, abort);   // dS^T(it) in TMEM and smem
+                mbar_wait(ds_full, it & 1, p.status, abort);   // dS^T(it) in shared memory
                 fence_after();
-                const uint64_t dq = desc_at(q_mnmaj, static_cast<uint32_t>(s) * kTileBytes);
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks)
-                {
-                    mma_ts(tmem + kDK, tmem + kDP + pt_col(ks), desc_at(dq, ks * 2048), idesc_kv,
-                           (it > 0 || ks > 0) ? 1u : 0u);
-                }
-                commit(&q_empty[s]);
-                // dQ(it) over dP^T / dS^T(it): dK(it), which reads dS^T, was issued first
+                // dQ(it) over the dP^T(it) columns (the elementwise warps have read them), first, so
+                // the drain empties it while dK(it) runs; both read the shared dS^T tile
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
                 {
@@ -1116,6 +1110,14 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
                         ks > 0 ? 1u : 0u);
                 }
                 commit(dq_full);
+                const uint64_t dq = desc_at(q_mnmaj, static_cast<uint32_t>(s) * kTileBytes);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+                {
+                    mma(tmem + kDK, desc_at(ds_kmaj, kmaj_step(ks)), desc_at(dq, ks * 2048), idesc_kv,
+                        (it > 0 || ks > 0) ? 1u : 0u);
+                }
+                commit(&q_empty[s]);
                 if (it + 1 < iters)
                 {
                     mbar_wait(dq_empty, it & 1, p.status, abort);   // dQ(it) read out of TMEM
@@ -1237,8 +1239,9 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full);
-            // Phase 2: dS^T. D arrived with Q; the dS^T tile's last reader, dQ(it-1), completed
-            // before the drain released dQ(it-1), which came before dP^T(it).
+            // Phase 2: dS^T. D arrived with Q; the dS^T tile's readers dQ(it-1) and dK(it-1) were
+            // issued before dP^T(it), so they are complete once dP^T(it) is (the commit tracks
+            // every earlier product of the issuing thread).
             mbar_wait(dp_full, it & 1, p.status, abort);
             fence_after();
             // this warp's 64 queries are the 128-byte row r of half grp of the dS^T tile
@@ -1270,7 +1273,6 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
                         dk[(c + u) >> 1] = pack2(d0, d1);
                     }
                 }
-                tmem_st16_async(tmem + lane_base + kDP + grp * 64 + half * 16, dk);
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
                 {
@@ -1279,7 +1281,6 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
                 }
             }
             fence_proxy_async();
-            tmem_wait_st();
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(ds_full);

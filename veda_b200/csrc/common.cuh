@@ -124,6 +124,43 @@ __device__ __forceinline__ void store16(T* p, const float (&in)[16 / sizeof(T)])
     *reinterpret_cast<uint4*>(p) = raw;
 }
 
+// ---- device: packed fp32 pairs (sm_100: one f32x2 instruction does the work of two) ---------
+__device__ __forceinline__ uint64_t pk(float a, float b)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk(uint64_t v, float& a, float& b)
+{
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// the 8 bf16 of a 16-byte chunk as four fp32 pairs
+__device__ __forceinline__ void unpack4x2(const uint4& raw, uint64_t (&o)[4])
+{
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = pk(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
+}
+
 // ---- device: reductions --------------------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v)
 {

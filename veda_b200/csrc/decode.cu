@@ -272,7 +272,10 @@ namespace
 constexpr int kGemvWarps = 8;
 constexpr int kGemvUnroll = 4;
 constexpr int kGemvBlocksPerSm = 4;   // registers capped at 64 a thread
-constexpr int64_t kGemvSmem = 48 * 1024;   // the activation row, staged whole
+// The activation row (and the norm's gain) staged whole in dynamic shared memory: 48 KB a block
+// can have without opting in to more, less 1 KB for the kernels' own static arrays (at most 112
+// bytes), so every accepted size launches.
+constexpr int64_t kGemvSmem = 47 * 1024;
 
 __device__ __forceinline__ uint4 load_stream16(const void* p)
 {
@@ -983,7 +986,7 @@ int gemv_checks(const void* x, const void* w, int64_t ldw, const void* y, int64_
     VEDA_REQUIRE(n > 0 && k > 0 && n < (1ll << 30), "bad shape");
     VEDA_REQUIRE(ldw >= k, "bad weight leading dimension");
     VEDA_REQUIRE(k * static_cast<int64_t>(dtype_size(dtype)) <= kGemvSmem,
-                 "the activation row exceeds the 48 KB staged in shared memory");
+                 "the activation row exceeds the 47 KB staged in shared memory");
     return 0;
 }
 
@@ -1019,7 +1022,7 @@ int norm_checks(const void* x, const void* r, const void* gamma, const void* sum
 {
     VEDA_REQUIRE(gamma != nullptr, "null pointer");
     VEDA_REQUIRE(2 * k * static_cast<int64_t>(dtype_size(dtype)) <= kGemvSmem,
-                 "the activation row and its gain exceed the 48 KB staged in shared memory");
+                 "the activation row and its gain exceed the 47 KB staged in shared memory");
     VEDA_REQUIRE(sum == nullptr || (sum != x && sum != r), "sum must not alias x or r (block 0 writes it "
                                                           "while the others read them)");
     return 0;

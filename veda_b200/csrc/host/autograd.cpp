@@ -1517,6 +1517,8 @@ void attention_backward(const AttentionSaved& a, const Tensor& g)
         }
         const size_t wsb = veda_qknorm_rope_bwd_workspace(N, heads, Dh);
         Tensor w2 = Tensor::empty(Shape({(wsb + 3) / 4 + 1}), DType::F32);
+        // reads x and dy, writes dx: 3 bytes-per-element passes over [N, heads * Dh]
+        profile::Scope scope("qknorm_bwd", 0.0, 3.0 * static_cast<double>(N) * heads * Dh * es);
         check(veda_qknorm_rope_bwd(src, ld, gv.data_ptr(), static_cast<const float*>(a.c.data_ptr()),
                                    static_cast<const float*>(a.s.data_ptr()), dy.data_ptr(),
                                    heads * Dh, dst, W, dgamma, w2.data_ptr(), wsb, N, heads, T, Dh,

@@ -789,20 +789,37 @@ qknorm_rope_bwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx,
 {
     __shared__ float part[kWarps * 4][128];
     const int lane = threadIdx.x & 31, q = lane & 7, slot = (threadIdx.x >> 5) * 4 + (lane >> 3);
-    const int64_t rows = tokens * heads;
-    float acca[8], accb[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acca[j] = accb[j] = 0.0f;
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps * 4;
+    const int64_t rows = tokens * heads;   // below 2^31 (checked by the launcher)
+    const int stride = static_cast<int>(gridDim.x) * kWarps * 4;
     int64_t row = (static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5)) * 4 + (lane >> 3);
+    // (token, head, position) of a row, stepped by `stride` rows without a division per step
+    const int sdiv = stride / heads, smod = stride % heads, tstep = sdiv % seq_len;
+    auto advance = [&](int& tok, int& hh, int& tt) {
+        hh += smod;
+        tok += sdiv;
+        tt += tstep;
+        if (hh >= heads)
+        {
+            hh -= heads;
+            ++tok;
+            ++tt;
+        }
+        if (tt >= seq_len) tt -= seq_len;
+    };
+    int token = static_cast<int>(row / heads);
+    int h = static_cast<int>(row - static_cast<int64_t>(token) * heads);
+    int t = token % seq_len;
+    // the gain of this lane's elements, as fp32 pairs
+    uint64_t ga[4], gb[4];
+    unpack4x2(*reinterpret_cast<const uint4*>(gamma + 8 * q), ga);
+    unpack4x2(*reinterpret_cast<const uint4*>(gamma + 64 + 8 * q), gb);
+    uint64_t acca[4] = {0, 0, 0, 0}, accb[4] = {0, 0, 0, 0};
     const uint4 zero = make_uint4(0, 0, 0, 0);
-    auto load_row = [&](int64_t r, uint4& a, uint4& b, uint4& da, uint4& db) {
+    auto load_row = [&](int64_t r, int tok, int hh, uint4& a, uint4& b, uint4& da, uint4& db) {
         if (r < rows)
         {
-            const int64_t token = static_cast<uint32_t>(r) / static_cast<uint32_t>(heads);
-            const int64_t h = r - token * heads;
-            const bf16* xr = x + token * ldx + h * 128;
-            const bf16* gr = dy + token * lddy + h * 128;
+            const bf16* xr = x + static_cast<int64_t>(tok) * ldx + hh * 128;
+            const bf16* gr = dy + static_cast<int64_t>(tok) * lddy + hh * 128;
             a = *reinterpret_cast<const uint4*>(xr + 8 * q);
             b = *reinterpret_cast<const uint4*>(xr + 64 + 8 * q);
             da = *reinterpret_cast<const uint4*>(gr + 8 * q);
@@ -814,58 +831,66 @@ qknorm_rope_bwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx,
         }
     };
     uint4 ca, cb, cda, cdb;
-    load_row(row, ca, cb, cda, cdb);
+    load_row(row, token, h, ca, cb, cda, cdb);
+    int ntok = token, nh = h, nt = t;
+    advance(ntok, nh, nt);
+    // every lane of a warp runs the same number of steps (the group sums shuffle across rows)
     const int64_t wfirst = row - (lane >> 3);
     const int64_t iters = wfirst < rows ? (rows - wfirst + stride - 1) / stride : 0;
+    constexpr uint64_t kSign = 0x8000000080000000ull;
     for (int64_t k = 0; k < iters; ++k)
     {
         uint4 na, nb, nda, ndb;
-        load_row(row + stride, na, nb, nda, ndb);
-        const bool valid = row < rows;
-        const int64_t token = valid ? static_cast<uint32_t>(row) / static_cast<uint32_t>(heads) : 0;
-        const int t = static_cast<int>(static_cast<uint32_t>(token) % static_cast<uint32_t>(seq_len));
-        float cs[8], sn[8], ga[8], gb[8];
-        rope_row(cosv, sinv, t, q, cs, sn);
-        load16(gamma + 8 * q, ga);
-        load16(gamma + 64 + 8 * q, gb);
-        float a[8], b[8], na2[8], nb2[8];
+        load_row(row + stride, ntok, nh, na, nb, nda, ndb);
+        const ulonglong2* cp = reinterpret_cast<const ulonglong2*>(cosv + static_cast<int64_t>(t) * 128 + 8 * q);
+        const ulonglong2* sp = reinterpret_cast<const ulonglong2*>(sinv + static_cast<int64_t>(t) * 128 + 8 * q);
+        const ulonglong2 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+        const uint64_t cs[4] = {c0.x, c0.y, c1.x, c1.y};
+        const uint64_t sn[4] = {s0.x, s0.y, s1.x, s1.y};
+        uint64_t a[4], b[4], ra[4], rb[4];
         {
-            float da[8], db[8];
-            bf16x8_to_f32(cda, da);
-            bf16x8_to_f32(cdb, db);
+            uint64_t da[4], db[4];
+            unpack4x2(cda, da);
+            unpack4x2(cdb, db);
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
+            for (int j = 0; j < 4; ++j)
             {
                 // rotation by -theta: the gradient at the normed-and-scaled value
-                na2[j] = da[j] * cs[j] + db[j] * sn[j];
-                nb2[j] = db[j] * cs[j] - da[j] * sn[j];
+                ra[j] = fma2(db[j], sn[j], mul2(da[j], cs[j]));
+                rb[j] = fma2(da[j], sn[j] ^ kSign, mul2(db[j], cs[j]));
             }
         }
-        bf16x8_to_f32(ca, a);
-        bf16x8_to_f32(cb, b);
-        float ss = 0.0f, w = 0.0f;
+        unpack4x2(ca, a);
+        unpack4x2(cb, b);
+        uint64_t ss2 = 0, w2 = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < 4; ++j)
         {
-            ss += a[j] * a[j] + b[j] * b[j];
-            w += (na2[j] * ga[j]) * a[j] + (nb2[j] * gb[j]) * b[j];
+            ss2 = fma2(a[j], a[j], ss2);
+            ss2 = fma2(b[j], b[j], ss2);
+            w2 = fma2(mul2(ra[j], ga[j]), a[j], w2);
+            w2 = fma2(mul2(rb[j], gb[j]), b[j], w2);
         }
-        ss = group8_sum(ss);
-        w = group8_sum(w);
-        if (valid)
+        float s0f, s1f, w0f, w1f;
+        upk(ss2, s0f, s1f);
+        upk(w2, w0f, w1f);
+        const float ss = group8_sum(s0f + s1f);
+        const float w = group8_sum(w0f + w1f);
+        if (row < rows)
         {
             const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
             const float coupling = w * inv * inv * inv / 128.0f;
+            const uint64_t inv2 = pk(inv, inv), ncp2 = pk(-coupling, -coupling);
             float oa[8], ob[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
+            for (int j = 0; j < 4; ++j)
             {
-                acca[j] += na2[j] * (a[j] * inv);
-                accb[j] += nb2[j] * (b[j] * inv);
-                oa[j] = (na2[j] * ga[j]) * inv - a[j] * coupling;
-                ob[j] = (nb2[j] * gb[j]) * inv - b[j] * coupling;
+                acca[j] = fma2(ra[j], mul2(a[j], inv2), acca[j]);
+                accb[j] = fma2(rb[j], mul2(b[j], inv2), accb[j]);
+                upk(fma2(mul2(ra[j], ga[j]), inv2, mul2(a[j], ncp2)), oa[2 * j], oa[2 * j + 1]);
+                upk(fma2(mul2(rb[j], gb[j]), inv2, mul2(b[j], ncp2)), ob[2 * j], ob[2 * j + 1]);
             }
-            bf16* out = dx + token * lddx + (row - token * heads) * 128;
+            bf16* out = dx + static_cast<int64_t>(token) * lddx + h * 128;
             store16(out + 8 * q, oa);
             store16(out + 64 + 8 * q, ob);
         }
@@ -874,14 +899,18 @@ qknorm_rope_bwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx,
         cda = nda;
         cdb = ndb;
         row += stride;
+        token = ntok;
+        h = nh;
+        t = nt;
+        advance(ntok, nh, nt);
     }
     if (partials != nullptr)
     {
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < 4; ++j)
         {
-            part[slot][8 * q + j] = acca[j];
-            part[slot][64 + 8 * q + j] = accb[j];
+            upk(acca[j], part[slot][8 * q + 2 * j], part[slot][8 * q + 2 * j + 1]);
+            upk(accb[j], part[slot][64 + 8 * q + 2 * j], part[slot][64 + 8 * q + 2 * j + 1]);
         }
         __syncthreads();
         for (int i = threadIdx.x; i < 128; i += blockDim.x)

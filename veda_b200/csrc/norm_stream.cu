@@ -5,18 +5,28 @@
 // r = sqrt(sum x^2 / n + eps), y = x / r * gamma; dx = G / r - x * sum(G x) / (n r^3) (+ the
 // residual gradient), G = dy * gamma, dgamma = sum over rows of dy * x / r.
 //
-// Structure: one block per SM, 1 producer warp + 8 consumer warps. The producer's lane 0 streams
+// Structure: one block per SM, 1 producer warp + consumer warps. The producer's lane 0 streams
 // whole rows (x; for the backward also dy and the residual gradient) into a ring of shared-memory
 // stages with bulk asynchronous copies (cp.async.bulk, no tensor map, no multicast) completing on
-// the stage's mbarrier; a stage holds 8 rows, one per consumer warp. Consumers wait for their
-// stage, reduce their row with warp shuffles only (no block barrier), write the output row with
-// coalesced 16-byte stores and release the stage. With 128-192 KB of rows in flight per SM the
-// loads no longer wait on the arithmetic, which is what the register-resident kernels could not
-// reach. Every mbarrier wait is bounded (tc_common.cuh).
+// the stage's mbarrier; a stage holds 8 rows. Consumers wait for their stage, reduce their row
+// with warp shuffles, write the output row with coalesced 16-byte stores and release the stage.
+// With 128-192 KB of rows in flight per SM the loads no longer wait on the arithmetic, which is
+// what the register-resident kernels could not reach. Every mbarrier wait is bounded
+// (tc_common.cuh).
+//   forward:  8 consumer warps, one row each;
+//   backward: rows of 512 or more elements are split between two warps (16 consumer warps, one
+//             half-row each; the two halves' sums meet through shared memory and a named barrier
+//             per row, added in the same order by both warps), with the arithmetic on packed fp32
+//             pairs. Eight warps each working through a whole row left the schedulers idle on the
+//             dependent sums (2.3 warps per scheduler, an instruction every 3.4 cycles, DRAM 35 %
+//             busy at 8192 x 1024).
 //
 // The gain gradient: each consumer warp accumulates its lanes' columns over the rows it processed;
-// at the end the 8 warps' rows are summed in warp order into one partial row per block (the
-// caller then sums the block partials in block order) — deterministic.
+// at the end the warps' rows are summed in row-slot order into one partial row per block (the
+// caller then sums the block partials in block order) — deterministic. Summing the block partials
+// inside this kernel instead (the last blocks to finish, after a memory fence and a completion
+// count) measured 19.9 us a call at 8192 x 1024 against 16.3 us for the two launches: the fence
+// waits for the block's output rows to drain, at the end of every block.
 #include "norm_stream.cuh"
 #include "tc_common.cuh"
 
@@ -58,8 +68,9 @@ __device__ __forceinline__ void unpack8(const uint4& raw, float (&o)[8])
 // Producer: streams NIN input rows per row of each of this block's chunks of kRows rows.
 template <int CH, int NIN>
 __device__ __forceinline__ void produce(uint8_t* ring, uint64_t* full, uint64_t* empty,
-                                        const bf16* const (&src)[3], const int64_t (&ld)[3],
-                                        int64_t rows, int* status, volatile int* abort)
+                                        const bf16* s0, int64_t ld0, const bf16* s1, int64_t ld1,
+                                        const bf16* s2, int64_t ld2, int64_t rows, int* status,
+                                        volatile int* abort)
 {
     using R = Ring<CH, NIN>;
     const int64_t chunks = (rows + kRows - 1) / kRows;
@@ -74,10 +85,14 @@ __device__ __forceinline__ void produce(uint8_t* ring, uint64_t* full, uint64_t*
         uint8_t* dst = ring + st * R::STAGE;
         for (int r = 0; r < nr; ++r)
         {
-#pragma unroll
-            for (int k = 0; k < NIN; ++k)
+            bulk_load(dst + (r * NIN) * R::ROW, s0 + (r0 + r) * ld0, R::ROW, &full[st]);
+            if constexpr (NIN >= 2)
             {
-                bulk_load(dst + (r * NIN + k) * R::ROW, src[k] + (r0 + r) * ld[k], R::ROW, &full[st]);
+                bulk_load(dst + (r * NIN + 1) * R::ROW, s1 + (r0 + r) * ld1, R::ROW, &full[st]);
+            }
+            if constexpr (NIN >= 3)
+            {
+                bulk_load(dst + (r * NIN + 2) * R::ROW, s2 + (r0 + r) * ld2, R::ROW, &full[st]);
             }
         }
     }
@@ -119,9 +134,7 @@ rms_fwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __res
     {
         if (lane == 0)
         {
-            const bf16* const src[3] = {x, r, nullptr};
-            const int64_t ld[3] = {ldx, ldr, 0};
-            produce<CH, NIN>(ring, full, empty, src, ld, rows, status, abort);
+            produce<CH, NIN>(ring, full, empty, x, ldx, r, ldr, nullptr, 0, rows, status, abort);
         }
         return;
     }
@@ -188,19 +201,43 @@ rms_fwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __res
     }
 }
 
+// Backward layout: rows of 512 or more elements are shared by two consumer warps (one half
+// each), so 16 consumer warps keep the schedulers busy where 8 could not hide the latency of
+// their dependent reductions; rows of 256 keep one warp per row.
+template <int CH>
+struct BwdSplit
+{
+    static constexpr int SPLIT = CH >= 2 ? 2 : 1;     // warps per row
+    static constexpr int CW = CH / SPLIT;             // 16-byte chunks per lane
+    static constexpr int WARPS = kRows * SPLIT;       // consumer warps
+    static constexpr int THREADS = 32 * (1 + WARPS);
+};
+
 template <int CH, int NIN>
-__global__ void __launch_bounds__(kThreadsStream, 1)
+struct BwdSmem
+{
+    using R = Ring<CH, NIN>;
+    // ring | gain (bf16 [N]) | row-half sums [2][kRows][SPLIT] float2 | barriers | abort flag,
+    // plus alignment slack
+    static constexpr int SMEM = R::STAGES * R::STAGE + R::N * 2 + 2 * kRows * BwdSplit<CH>::SPLIT * 8 +
+                                2 * R::STAGES * 8 + 16 + 128;
+};
+
+template <int CH, int NIN>
+__global__ void __launch_bounds__(BwdSplit<CH>::THREADS, 1)
 rms_bwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ gamma,
                       const bf16* __restrict__ dy, int64_t lddy, const bf16* __restrict__ dresid,
                       int64_t ldr, bf16* __restrict__ dx, int64_t lddx, float* __restrict__ partials,
                       int64_t rows, float eps, int* status)
 {
     using R = Ring<CH, NIN>;
+    using S = BwdSplit<CH>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* ring = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
-    float* gsm = reinterpret_cast<float*>(ring + R::STAGES * R::STAGE);   // gamma, fp32
-    uint64_t* full = reinterpret_cast<uint64_t*>(gsm + R::N);
+    uint4* gsm = reinterpret_cast<uint4*>(ring + R::STAGES * R::STAGE);      // gain, bf16
+    float2* xch = reinterpret_cast<float2*>(gsm + R::N / 8);                 // [2][kRows][SPLIT]
+    uint64_t* full = reinterpret_cast<uint64_t*>(xch + 2 * kRows * S::SPLIT);
     uint64_t* empty = full + R::STAGES;
     volatile int* abort = reinterpret_cast<volatile int*>(empty + R::STAGES);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -210,91 +247,120 @@ rms_bwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __res
         for (int s = 0; s < R::STAGES; ++s)
         {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kRows);
+            mbar_init(&empty[s], S::WARPS);
         }
         mbar_fence_init();
     }
-    for (int c = threadIdx.x; c < R::N; c += blockDim.x)
+    for (int c = threadIdx.x; c < R::N / 8; c += blockDim.x)
     {
-        gsm[c] = gamma != nullptr ? __bfloat162float(gamma[c]) : 1.0f;
+        // 1.0 in bf16 is 0x3F80
+        gsm[c] = gamma != nullptr ? reinterpret_cast<const uint4*>(gamma)[c]
+                                  : make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
     }
     __syncthreads();
-    float acc[CH][8];
+    constexpr int kPart = R::N / S::SPLIT;   // elements of a row per consumer warp
+    const int w = warp - 1;
+    const int r = w % kRows, hf = w / kRows;   // row of the stage, part of the row
+    const int col0 = hf * kPart;
+    uint64_t acc[S::CW][4];                    // gain gradient of this lane's columns
 #pragma unroll
-    for (int c = 0; c < CH; ++c)
+    for (int c = 0; c < S::CW; ++c)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[c][j] = 0.0f;
+        for (int j = 0; j < 4; ++j) acc[c][j] = 0;
     if (warp == 0)
     {
         if (lane == 0)
         {
-            const bf16* const src[3] = {x, dy, dresid};
-            const int64_t ld[3] = {ldx, lddy, ldr};
-            produce<CH, NIN>(ring, full, empty, src, ld, rows, status, abort);
+            produce<CH, NIN>(ring, full, empty, x, ldx, dy, lddy, dresid, ldr, rows, status, abort);
         }
     }
     else
     {
-        const int w = warp - 1;
-        auto gain = [&](int c, float (&gm)[8]) {
-            const float4 g0 = *reinterpret_cast<const float4*>(gsm + (c * 32 + lane) * 8);
-            const float4 g1 = *reinterpret_cast<const float4*>(gsm + (c * 32 + lane) * 8 + 4);
-            gm[0] = g0.x; gm[1] = g0.y; gm[2] = g0.z; gm[3] = g0.w;
-            gm[4] = g1.x; gm[5] = g1.y; gm[6] = g1.z; gm[7] = g1.w;
-        };
+        // this lane's 16-byte chunks of the gain (conflict-free: consecutive lanes, consecutive chunks)
+        const uint4* gl = gsm + col0 / 8 + lane;
         const int64_t chunks = (rows + kRows - 1) / kRows;
         int i = 0;
         for (int64_t q = blockIdx.x; q < chunks; q += gridDim.x, ++i)
         {
             const int st = i % R::STAGES;
             mbar_wait(&full[st], (i / R::STAGES) & 1, status, abort);
-            const int64_t row = q * kRows + w;
-            if (row < rows)
+            const int64_t row = q * kRows + r;
+            if (row < rows)   // the same for both warps of a row
             {
-                const uint8_t* xs = ring + st * R::STAGE + (w * NIN) * R::ROW;
+                const uint8_t* xs = ring + st * R::STAGE + (r * NIN) * R::ROW + col0 * 2;
                 const uint8_t* gs = xs + R::ROW;
-                float ss = 0.0f, wsum = 0.0f;
+                uint4 xr[S::CW], gr[S::CW];
 #pragma unroll
-                for (int c = 0; c < CH; ++c)
+                for (int c = 0; c < S::CW; ++c)
                 {
-                    float xv[8], gv[8], gm[8];
-                    unpack8(*reinterpret_cast<const uint4*>(xs + (c * 32 + lane) * 16), xv);
-                    unpack8(*reinterpret_cast<const uint4*>(gs + (c * 32 + lane) * 16), gv);
-                    gain(c, gm);
+                    xr[c] = *reinterpret_cast<const uint4*>(xs + (c * 32 + lane) * 16);
+                    gr[c] = *reinterpret_cast<const uint4*>(gs + (c * 32 + lane) * 16);
+                }
+                // G = dy * gamma; sums of x^2 and G x over this warp's part of the row
+                uint64_t ss2 = 0, ws2 = 0;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
+                for (int c = 0; c < S::CW; ++c)
+                {
+                    uint64_t xv[4], gv[4], gm[4];
+                    unpack4x2(xr[c], xv);
+                    unpack4x2(gr[c], gv);
+                    unpack4x2(gl[c * 32], gm);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
                     {
-                        ss += xv[j] * xv[j];
-                        wsum += (gv[j] * gm[j]) * xv[j];
+                        ss2 = fma2(xv[j], xv[j], ss2);
+                        ws2 = fma2(mul2(gv[j], gm[j]), xv[j], ws2);
                     }
                 }
-                ss = warp_sum(ss);
-                wsum = warp_sum(wsum);
+                float s0, s1, w0, w1;
+                upk(ss2, s0, s1);
+                upk(ws2, w0, w1);
+                float ss = s0 + s1, wsum = w0 + w1;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+                {
+                    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+                    wsum += __shfl_xor_sync(0xFFFFFFFFu, wsum, o);
+                }
+                if constexpr (S::SPLIT == 2)
+                {
+                    // both warps of the row add the two halves in the same order
+                    float2* slot = xch + ((i & 1) * kRows + r) * 2;
+                    if (lane == 0) slot[hf] = make_float2(ss, wsum);
+                    asm volatile("bar.sync %0, 64;" ::"r"(1 + r) : "memory");
+                    const float2 a = slot[0], b = slot[1];
+                    ss = a.x + b.x;
+                    wsum = a.y + b.y;
+                }
                 const float inv = 1.0f / sqrtf(ss / static_cast<float>(R::N) + eps);
                 const float coupling = wsum * inv * inv * inv / static_cast<float>(R::N);
+                const uint64_t inv2 = pk(inv, inv), ncp2 = pk(-coupling, -coupling);
 #pragma unroll
-                for (int c = 0; c < CH; ++c)
+                for (int c = 0; c < S::CW; ++c)
                 {
-                    float xv[8], gv[8], res[8], gm[8];
-                    unpack8(*reinterpret_cast<const uint4*>(xs + (c * 32 + lane) * 16), xv);
-                    unpack8(*reinterpret_cast<const uint4*>(gs + (c * 32 + lane) * 16), gv);
-                    gain(c, gm);
+                    uint64_t xv[4], gv[4], gm[4];
+                    unpack4x2(xr[c], xv);
+                    unpack4x2(gr[c], gv);
+                    unpack4x2(gl[c * 32], gm);
+                    uint64_t res[4];
                     if constexpr (NIN == 3)
                     {
-                        unpack8(*reinterpret_cast<const uint4*>(xs + 2 * R::ROW + (c * 32 + lane) * 16), res);
+                        unpack4x2(*reinterpret_cast<const uint4*>(xs + 2 * R::ROW + (c * 32 + lane) * 16), res);
                     }
+                    float out[8];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
+                    for (int j = 0; j < 4; ++j)
                     {
-                        float d = (gv[j] * gm[j]) * inv - xv[j] * coupling;
+                        // dx = G / r - x * coupling (+ the residual gradient); dgamma += dy * x / r
+                        uint64_t d = fma2(mul2(gv[j], gm[j]), inv2, mul2(xv[j], ncp2));
                         if constexpr (NIN == 3)
                         {
-                            d = res[j] + d;
+                            d = add2(res[j], d);
                         }
-                        acc[c][j] += gv[j] * (xv[j] * inv);
-                        xv[j] = d;
+                        acc[c][j] = fma2(gv[j], mul2(xv[j], inv2), acc[c][j]);
+                        upk(d, out[2 * j], out[2 * j + 1]);
                     }
-                    store16(dx + row * lddx + (c * 32 + lane) * 8, xv);
+                    store16(dx + row * lddx + col0 + (c * 32 + lane) * 8, out);
                 }
             }
             __syncwarp();
@@ -309,9 +375,15 @@ rms_bwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __res
         if (warp > 0)
         {
 #pragma unroll
-            for (int c = 0; c < CH; ++c)
+            for (int c = 0; c < S::CW; ++c)
+            {
+                float v[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) part[(warp - 1) * R::N + (c * 32 + lane) * 8 + j] = acc[c][j];
+                for (int j = 0; j < 4; ++j) upk(acc[c][j], v[2 * j], v[2 * j + 1]);
+                float* dst = part + r * R::N + col0 + (c * 32 + lane) * 8;
+                *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+                *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
+            }
         }
         __syncthreads();
         for (int col = threadIdx.x; col < R::N; col += blockDim.x)
@@ -353,14 +425,14 @@ int launch_bwd(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* dy, in
                const bf16* dresid, int64_t ldr, bf16* dx, int64_t lddx, float* partials, int max_blocks,
                int64_t rows, float eps, cudaStream_t s, int* blocks)
 {
-    using R = Ring<CH, NIN>;
+    constexpr int kSmem = BwdSmem<CH, NIN>::SMEM;
     static int configured = -1;
     int device = 0;
     cudaGetDevice(&device);
     if (configured != device)
     {
         cudaFuncSetAttribute(rms_bwd_stream_kernel<CH, NIN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             R::SMEM);
+                             kSmem);
         configured = device;
     }
     const int64_t chunks = (rows + kRows - 1) / kRows;
@@ -368,7 +440,7 @@ int launch_bwd(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* dy, in
     if (g > max_blocks) g = max_blocks;
     if (g < 1) g = 1;
     *blocks = static_cast<int>(g);
-    rms_bwd_stream_kernel<CH, NIN><<<static_cast<unsigned>(g), kThreadsStream, R::SMEM, s>>>(
+    rms_bwd_stream_kernel<CH, NIN><<<static_cast<unsigned>(g), BwdSplit<CH>::THREADS, kSmem, s>>>(
         x, ldx, gamma, dy, lddy, dresid, ldr, dx, lddx, partials, rows, eps, device_status_ptr());
     count_launch();
     return check_launch("veda_rmsnorm_bwd (streaming)");
@@ -429,8 +501,7 @@ int rms_bwd_stream(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* dy
     case 256: VEDA_BWD(1);
     case 512: VEDA_BWD(2);
     case 1024: VEDA_BWD(4);
-    default: return -1;   // 2048: the 64 per-lane gain sums would not fit in registers
-
+    default: return -1;   // 2048: the per-lane gain sums would not fit in registers
     }
 #undef VEDA_BWD
 }
