@@ -156,6 +156,22 @@ int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamma, const fl
                          int64_t heads, int64_t seq_len, int64_t head_dim, float eps, int dtype,
                          veda_stream_t stream);
 size_t veda_qknorm_rope_bwd_workspace(int64_t tokens, int64_t heads, int64_t head_dim);
+/* veda_qknorm_rope_bwd for the q and the k heads of one attention layer (Model.cpp:171-178 applies
+ * q_norm and k_norm to the same positions) in one launch, and one launch of the two gain
+ * reductions: x rows xq (heads) and xk (kv_heads) at stride ldx, gradients dyq / dyk at their
+ * strides, results dxq / dxk at stride lddx, dq_gamma / dk_gamma (either may be NULL) +=.
+ * The same arithmetic as two veda_qknorm_rope_bwd calls; the gain gradients are summed over a
+ * different number of blocks, so they agree with those calls to rounding. workspace:
+ * veda_qknorm_rope_bwd_qk_workspace() bytes. */
+int veda_qknorm_rope_bwd_qk(const void* xq, const void* xk, int64_t ldx, const void* q_gamma,
+                            const void* k_gamma, const float* cos, const float* sin,
+                            const void* dyq, int64_t lddyq, const void* dyk, int64_t lddyk,
+                            void* dxq, void* dxk, int64_t lddx, float* dq_gamma, float* dk_gamma,
+                            void* workspace, size_t workspace_bytes, int64_t tokens, int64_t heads,
+                            int64_t kv_heads, int64_t seq_len, int64_t head_dim, float eps,
+                            int dtype, veda_stream_t stream);
+size_t veda_qknorm_rope_bwd_qk_workspace(int64_t tokens, int64_t heads, int64_t kv_heads,
+                                         int64_t head_dim);
 
 /* Plain RoPE on a contiguous [lanes, seq_len, head_dim] tensor (autograd::rope,
  * src/libs/autograd/Views.cpp:78-171); inverse = 1 rotates by -theta (the backward). */

@@ -175,6 +175,67 @@ def test_qknorm_rope(dtype, B, T, H, Dh, theta):
     assert rel(host(dgam), dgam_ref) <= (1e-4 if dtype == V.F32 else 1e-3)
 
 
+@pytest.mark.parametrize("dtype,B,T,H,Hk,with_k_gain", [(V.BF16, 2, 256, 16, 8, True),
+                                                        (V.BF16, 4, 2048, 16, 8, True),
+                                                        (V.BF16, 3, 100, 6, 2, False),
+                                                        (V.F32, 2, 64, 4, 2, True)])
+def test_qknorm_rope_bwd_q_and_k_in_one_launch(dtype, B, T, H, Hk, with_k_gain):
+    """veda_qknorm_rope_bwd_qk (the q and k heads of a layer in one launch) against two
+    veda_qknorm_rope_bwd calls: dx bit for bit, the gain gradients to rounding; and the oracle."""
+    r = rng(7 * T + H + Hk)
+    Dh = 128
+    N = B * T
+    W = (H + 2 * Hk) * Dh   # the fused q|k|v projection
+    buf = r.standard_normal((N, W)).astype(F32)
+    qg = (1 + 0.1 * r.standard_normal(Dh)).astype(F32)
+    kg = (1 + 0.1 * r.standard_normal(Dh)).astype(F32)
+    gq = r.standard_normal((N, H * Dh)).astype(F32)
+    gk = r.standard_normal((N, Hk * Dh)).astype(F32)
+    if dtype == V.BF16:
+        buf, qg, kg, gq, gk = bf(buf), bf(qg), bf(kg), bf(gq), bf(gk)
+    cos, sin = O.rope_tables(T, Dh, 1e6)
+    es = 2 if dtype == V.BF16 else 4
+    bufd = dev(buf, dtype)
+    xq, xk = bufd.data_ptr(), bufd.data_ptr() + H * Dh * es
+    qgd, kgd, gqd, gkd = dev(qg, dtype), dev(kg, dtype), dev(gq, dtype), dev(gk, dtype)
+    cd, sd = dev(cos), dev(sin)
+    lib = V.lib()
+    # one launch: results into the q and k columns of one fused gradient
+    dx = empty((N, W), dtype)
+    dqg, dkg = dev(np.full(Dh, 0.25, F32)), dev(np.full(Dh, -0.5, F32))
+    ws = workspace(lib.veda_qknorm_rope_bwd_qk_workspace(N, H, Hk, Dh))
+    call("veda_qknorm_rope_bwd_qk", xq, xk, W, ptr(qgd), ptr(kgd), ptr(cd), ptr(sd), ptr(gqd), H * Dh,
+         ptr(gkd), Hk * Dh, ptr(dx), ptr(dx) + H * Dh * es, W, ptr(dqg),
+         ptr(dkg) if with_k_gain else None, ptr(ws), ws.numel(), N, H, Hk, T, Dh, 1e-6, dtype, stream())
+    # two calls
+    dxq, dxk = empty((N, H * Dh), dtype), empty((N, Hk * Dh), dtype)
+    dqg2, dkg2 = dev(np.full(Dh, 0.25, F32)), dev(np.full(Dh, -0.5, F32))
+    for x0, gd, g0, nh, out, dg in ((xq, qgd, gqd, H, dxq, dqg2), (xk, kgd, gkd, Hk, dxk, dkg2)):
+        w1 = workspace(lib.veda_qknorm_rope_bwd_workspace(N, nh, Dh))
+        call("veda_qknorm_rope_bwd", x0, W, ptr(gd), ptr(cd), ptr(sd), ptr(g0), nh * Dh, ptr(out), nh * Dh,
+             ptr(dg) if (dg is dqg2 or with_k_gain) else None, ptr(w1), w1.numel(), N, nh, T, Dh, 1e-6,
+             dtype, stream())
+    sync()
+    got = host(dx)
+    assert np.array_equal(got[:, :H * Dh], host(dxq))
+    assert np.array_equal(got[:, H * Dh:(H + Hk) * Dh], host(dxk))
+    assert rel(host(dqg), host(dqg2)) <= 1e-5
+    assert rel(host(dkg), host(dkg2)) <= 1e-5
+    if not with_k_gain:
+        assert np.array_equal(host(dkg), np.full(Dh, -0.5, F32))
+    # the oracle, per set
+    for x, g, gam, nh, got_x, got_g, base in ((buf[:, :H * Dh], gq, qg, H, got[:, :H * Dh], dqg, 0.25),
+                                               (buf[:, H * Dh:(H + Hk) * Dh], gk, kg, Hk,
+                                                got[:, H * Dh:(H + Hk) * Dh], dkg, -0.5)):
+        xh = x.reshape(B, T, nh, Dh).transpose(0, 2, 1, 3)
+        gh = g.reshape(B, T, nh, Dh).transpose(0, 2, 1, 3)
+        dyn = O.rope_backward(gh, cos, sin)
+        dx_ref, dg_ref = O.rms_norm_gamma_backward(xh, gam, dyn, 1e-6)
+        assert rel(got_x, dx_ref.transpose(0, 2, 1, 3).reshape(N, nh * Dh)) <= TOL[dtype]
+        if base > 0 or with_k_gain:
+            assert rel(host(got_g), dg_ref + base) <= (1e-4 if dtype == V.F32 else 1e-3)
+
+
 def test_rope_plain_matches_golden():
     from pathlib import Path
     ops = np.load(Path(__file__).parent / "golden" / "ops_small.npz")

@@ -55,6 +55,10 @@ SIGNATURES = {
     "veda_qknorm_rope_bwd": (_i, [_p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _p, _sz, _i64,
                                   _i64, _i64, _i64, _f, _i, _p]),
     "veda_qknorm_rope_bwd_workspace": (_sz, [_i64, _i64, _i64]),
+    "veda_qknorm_rope_bwd_qk": (_i, [_p, _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i64, _p, _p,
+                                     _i64, _p, _p, _p, _sz, _i64, _i64, _i64, _i64, _i64, _f, _i,
+                                     _p]),
+    "veda_qknorm_rope_bwd_qk_workspace": (_sz, [_i64, _i64, _i64, _i64]),
     "veda_rope": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _p]),
     "veda_swiglu_fwd": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i, _p]),
     "veda_swiglu_bwd": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i,

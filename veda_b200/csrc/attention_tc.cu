@@ -1520,69 +1520,69 @@ attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tds, const __grid_constant
     }
 }
 
-// D = rowsum(dO * O) and -LSE log2(e) for every (batch, head, query); 16 threads per (token, head)
-// row, rows in token-major order so a warp reads two contiguous 256-byte rows of O and dO. Each
-// 16-lane group keeps kRowdotRows rows' loads in flight (one row at a time left the loads
-// latency-bound).
+// D = rowsum(dO * O) and -LSE log2(e) per (batch, head, query), and (fused path) the zeroed dQ
+// accumulator rows. One block per (batch, head) and 64 consecutive queries: 16 groups of 16
+// lanes, each group four consecutive queries with all eight of a lane's 16-byte loads in flight
+// together; the per-query LSE read and D / -LSE log2(e) writes are contiguous in the query, and
+// no index needs a division (a grid-stride loop over (token, head) rows with 64-bit divisions and
+// LSE accesses strided by T took 34 us a launch at B 4, H 16, T 2048).
 constexpr int kRowdotRows = 4;
+constexpr int kRowdotBlockRows = 16 * kRowdotRows;
 
-__global__ void attn_rowdot_kernel(const bf16* __restrict__ o, int64_t ldo,
-                                   const bf16* __restrict__ dout, int64_t lddo,
-                                   const float* __restrict__ lse, float* __restrict__ dvec,
-                                   float* __restrict__ nlse2, float* __restrict__ dqacc, int64_t B,
-                                   int64_t T, int64_t H)
+__global__ void __launch_bounds__(256)
+attn_rowdot_kernel(const bf16* __restrict__ o, int64_t ldo, const bf16* __restrict__ dout,
+                   int64_t lddo, const float* __restrict__ lse, float* __restrict__ dvec,
+                   float* __restrict__ nlse2, float* __restrict__ dqacc, int T, int H)
 {
-    const int sub = threadIdx.x & 15;
-    // the two 16-lane groups of a warp may leave the loop at different iterations: shuffles
-    // name only the group's own lanes
+    const int sub = threadIdx.x & 15, grp = threadIdx.x >> 4;
     const unsigned half = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
-    const int64_t rows = B * T * H;
-    const int64_t groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 4;
-    const int64_t group = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
-    for (int64_t r0 = group * kRowdotRows; r0 < rows; r0 += groups * kRowdotRows)
+    const int bh = static_cast<int>(blockIdx.x);   // b * H + h
+    const int b = bh / H, h = bh - b * H;
+    const int t0 = static_cast<int>(blockIdx.y) * kRowdotBlockRows + grp * kRowdotRows;
+    float x[kRowdotRows][8], y[kRowdotRows][8];
+#pragma unroll
+    for (int u = 0; u < kRowdotRows; ++u)
     {
-        float x[kRowdotRows][8], y[kRowdotRows][8];
+        const int t = t0 + u < T ? t0 + u : T - 1;   // rows past T: a valid row, result unused
+        const int64_t bt = static_cast<int64_t>(b) * T + t;
+        load16(o + bt * ldo + h * 128 + sub * 8, x[u]);
+        load16(dout + bt * lddo + h * 128 + sub * 8, y[u]);
+    }
+    if (dqacc != nullptr)
+    {
+        // row (token b T + t, head h) of the fused path's dQ accumulator [B*T][H*128]
 #pragma unroll
         for (int u = 0; u < kRowdotRows; ++u)
         {
-            const int64_t r = r0 + u < rows ? r0 + u : rows - 1;
-            const int64_t h = r % H, bt = r / H;
-            load16(o + bt * ldo + h * 128 + sub * 8, x[u]);
-            load16(dout + bt * lddo + h * 128 + sub * 8, y[u]);
-        }
-        if (dqacc != nullptr)
-        {
-            // row r of the fused path's dQ accumulator [B*T][H*128] is (token r / H, head r % H)
-#pragma unroll
-            for (int u = 0; u < kRowdotRows; ++u)
+            if (t0 + u < T)
             {
-                if (r0 + u < rows)
-                {
-                    float4* z = reinterpret_cast<float4*>(dqacc + (r0 + u) * 128 + sub * 8);
-                    z[0] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    z[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                }
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < kRowdotRows; ++u)
-        {
-            float s = 0.0f;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) s += x[u][e] * y[u][e];
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(half, s, off);
-            const int64_t r = r0 + u;
-            if (sub == 0 && r < rows)
-            {
-                const int64_t h = r % H, bt = r / H;
-                const int64_t b = bt / T, t = bt % T;
-                const int64_t at = (b * H + h) * T + t;
-                dvec[at] = s;
-                nlse2[at] = -lse[at] * kLog2e;
+                float4* z = reinterpret_cast<float4*>(
+                    dqacc + ((static_cast<int64_t>(b) * T + t0 + u) * H + h) * 128 + sub * 8);
+                z[0] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                z[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             }
         }
     }
+#pragma unroll
+    for (int u = 0; u < kRowdotRows; ++u)
+    {
+        float s = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s += x[u][e] * y[u][e];
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(half, s, off);
+        if (sub == 0 && t0 + u < T)
+        {
+            const int64_t at = static_cast<int64_t>(bh) * T + t0 + u;
+            dvec[at] = s;
+            nlse2[at] = -lse[at] * kLog2e;
+        }
+    }
+}
+
+dim3 rowdot_grid(int64_t B, int64_t T, int64_t H)
+{
+    return dim3(static_cast<unsigned>(B * H), static_cast<unsigned>((T + kRowdotBlockRows - 1) / kRowdotBlockRows));
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
@@ -1741,9 +1741,9 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
         {
             return -1;
         }
-        attn_rowdot_kernel<<<grid_for(B * H * T * 16 / kRowdotRows, 256), 256, 0, s>>>(
+        attn_rowdot_kernel<<<rowdot_grid(B, T, H), 256, 0, s>>>(
             static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, lse, dvec, nlse2,
-            dqacc, B, T, H);
+            dqacc, static_cast<int>(T), static_cast<int>(H));
         FusedParams p{nlse2, dvec, static_cast<bf16*>(dk), static_cast<bf16*>(dv), lddk, lddv,
                       static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
                       scale * kLog2e, causal, device_status_ptr()};
@@ -1754,9 +1754,9 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
         return check_launch("veda_attention_bwd (tcgen05, fused)");
     }
     bf16* ds = static_cast<bf16*>(extra);
-    attn_rowdot_kernel<<<grid_for(B * H * T * 16 / kRowdotRows, 256), 256, 0, s>>>(
+    attn_rowdot_kernel<<<rowdot_grid(B, T, H), 256, 0, s>>>(
         static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, lse, dvec, nlse2,
-        nullptr, B, T, H);
+        nullptr, static_cast<int>(T), static_cast<int>(H));
     BwdParams p{nlse2, dvec, static_cast<bf16*>(dk), static_cast<bf16*>(dv), ds, lddk, lddv,
                 static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
                 scale * kLog2e, causal, device_status_ptr()};

@@ -1505,28 +1505,31 @@ void attention_backward(const AttentionSaved& a, const Tensor& g)
                                  Hkv, Dh, a.scale, 1, dt(d), S()),
               "attention backward");
     }
-    auto norm_bwd = [&](const std::shared_ptr<Node>& gain, const Tensor& gv, const char* src,
-                        const Tensor& dy, char* dst, size_t heads) {
-        float* dgamma = nullptr;
-        if (gain->requires_grad)
+    // q_norm and k_norm backward in one launch: dq, dk into their columns of the fused gradient
+    auto gain_target = [&](const std::shared_ptr<Node>& gain) -> float* {
+        if (!gain->requires_grad)
         {
-            bool fresh = false;
-            Tensor& gg = grad_target(*gain, &fresh, DType::F32);
-            if (fresh) memset_zero(gg);
-            dgamma = static_cast<float*>(gg.data_ptr());
+            return nullptr;
         }
-        const size_t wsb = veda_qknorm_rope_bwd_workspace(N, heads, Dh);
-        Tensor w2 = Tensor::empty(Shape({(wsb + 3) / 4 + 1}), DType::F32);
-        // reads x and dy, writes dx: 3 bytes-per-element passes over [N, heads * Dh]
-        profile::Scope scope("qknorm_bwd", 0.0, 3.0 * static_cast<double>(N) * heads * Dh * es);
-        check(veda_qknorm_rope_bwd(src, ld, gv.data_ptr(), static_cast<const float*>(a.c.data_ptr()),
-                                   static_cast<const float*>(a.s.data_ptr()), dy.data_ptr(),
-                                   heads * Dh, dst, W, dgamma, w2.data_ptr(), wsb, N, heads, T, Dh,
-                                   a.eps, dt(d), S()),
-              "attention backward: norm + rope");
+        bool fresh = false;
+        Tensor& gg = grad_target(*gain, &fresh, DType::F32);
+        if (fresh) memset_zero(gg);
+        return static_cast<float*>(gg.data_ptr());
     };
-    norm_bwd(a.qn, a.qg, base, dqr, dbase, H);
-    norm_bwd(a.kn, a.kg, base + H * Dh * es, dkr, dbase + H * Dh * es, Hkv);
+    float* dqg = gain_target(a.qn);
+    float* dkg = gain_target(a.kn);
+    const size_t wsb = veda_qknorm_rope_bwd_qk_workspace(N, H, Hkv, Dh);
+    Tensor w2 = Tensor::empty(Shape({(wsb + 3) / 4 + 1}), DType::F32);
+    {
+        // reads x and dy, writes dx: 3 bytes-per-element passes over [N, (H + Hkv) * Dh]
+        profile::Scope scope("qknorm_bwd", 0.0, 3.0 * static_cast<double>(N) * (H + Hkv) * Dh * es);
+        check(veda_qknorm_rope_bwd_qk(base, base + H * Dh * es, ld, a.qg.data_ptr(), a.kg.data_ptr(),
+                                      static_cast<const float*>(a.c.data_ptr()),
+                                      static_cast<const float*>(a.s.data_ptr()), dqr.data_ptr(), H * Dh,
+                                      dkr.data_ptr(), Hkv * Dh, dbase, dbase + H * Dh * es, W, dqg, dkg,
+                                      w2.data_ptr(), wsb, N, H, Hkv, T, Dh, a.eps, dt(d), S()),
+              "attention backward: norm + rope");
+    }
     if (a.xin->requires_grad)
     {
         accumulate(*a.xin, dx);

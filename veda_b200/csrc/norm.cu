@@ -240,11 +240,16 @@ rmsnorm_bwd_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ g
     }
 }
 
-// dgamma[i] += sum over blocks of partials[b][i], in a fixed order.
+// dgamma[i] += sum over blocks of partials[b][i], in a fixed order; blockIdx.y picks one of two
+// (partials, blocks, dgamma) sets (the q and k gains of a QK-norm backward).
 __global__ void __launch_bounds__(256)
-reduce_partials_kernel(const float* __restrict__ partials, int blocks, int n,
-                       float* __restrict__ dgamma)
+reduce_partials_kernel(const float* __restrict__ partials0, int blocks0, float* __restrict__ dgamma0,
+                       const float* __restrict__ partials1, int blocks1, float* __restrict__ dgamma1,
+                       int n)
 {
+    const float* __restrict__ partials = blockIdx.y == 0 ? partials0 : partials1;
+    const int blocks = blockIdx.y == 0 ? blocks0 : blocks1;
+    float* __restrict__ dgamma = blockIdx.y == 0 ? dgamma0 : dgamma1;
     // 8 columns x 32 row groups per block: group g sums partial rows g, g + 32, ... of its column
     // in that order, then the 32 group sums are added in group order (deterministic).
     __shared__ float part[32][9];
@@ -290,9 +295,11 @@ __global__ void add_rows_kernel(const T* __restrict__ x, int64_t ldx, const T* _
 }
 
 inline void launch_reduce_partials(const float* partials, int blocks, int n, float* dgamma,
-                                   cudaStream_t s)
+                                   cudaStream_t s, const float* partials1 = nullptr, int blocks1 = 0,
+                                   float* dgamma1 = nullptr)
 {
-    reduce_partials_kernel<<<(n + 7) / 8, 256, 0, s>>>(partials, blocks, n, dgamma);
+    const dim3 grid((n + 7) / 8, partials1 != nullptr ? 2 : 1);
+    reduce_partials_kernel<<<grid, 256, 0, s>>>(partials, blocks, dgamma, partials1, blocks1, dgamma1, n);
     count_launch();
 }
 
@@ -778,20 +785,42 @@ qknorm_rope_fwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16*
     }
 }
 
+// One of the (up to) two sets of rows a QK-norm backward launch works through: the q heads and
+// the k heads of one attention layer share a launch, each with its own blocks, gain and partial
+// rows of the gain gradient (blocks = 0: no second set).
+struct QkSet
+{
+    const bf16* x;
+    const bf16* gamma;
+    const bf16* dy;
+    bf16* dx;
+    float* partials;
+    int64_t ldx, lddy, lddx;
+    int heads, blocks;
+};
+
 // Shared memory: [kWarps * 4][128] fp32 gain-gradient rows (one per row slot).
 __global__ void __launch_bounds__(kWarps * 32, 2)
-qknorm_rope_bwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx,
-                            const bf16* __restrict__ gamma, const float* __restrict__ cosv,
-                            const float* __restrict__ sinv, const bf16* __restrict__ dy,
-                            int64_t lddy, bf16* __restrict__ dx, int64_t lddx,
-                            float* __restrict__ partials, int64_t tokens, int heads, int seq_len,
-                            float eps)
+qknorm_rope_bwd_d128_kernel(const QkSet s0, const QkSet s1, const float* __restrict__ cosv,
+                            const float* __restrict__ sinv, int64_t tokens, int seq_len, float eps)
 {
     __shared__ float part[kWarps * 4][128];
+    // this block's set, and the block's index within it
+    const bool second = static_cast<int>(blockIdx.x) >= s0.blocks;
+    const bf16* __restrict__ x = second ? s1.x : s0.x;
+    const bf16* __restrict__ gamma = second ? s1.gamma : s0.gamma;
+    const bf16* __restrict__ dy = second ? s1.dy : s0.dy;
+    bf16* __restrict__ dx = second ? s1.dx : s0.dx;
+    float* __restrict__ partials = second ? s1.partials : s0.partials;
+    const int64_t ldx = second ? s1.ldx : s0.ldx, lddy = second ? s1.lddy : s0.lddy,
+                  lddx = second ? s1.lddx : s0.lddx;
+    const int heads = second ? s1.heads : s0.heads;
+    const int nblk = second ? s1.blocks : s0.blocks;
+    const int blk = second ? static_cast<int>(blockIdx.x) - s0.blocks : static_cast<int>(blockIdx.x);
     const int lane = threadIdx.x & 31, q = lane & 7, slot = (threadIdx.x >> 5) * 4 + (lane >> 3);
     const int64_t rows = tokens * heads;   // below 2^31 (checked by the launcher)
-    const int stride = static_cast<int>(gridDim.x) * kWarps * 4;
-    int64_t row = (static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5)) * 4 + (lane >> 3);
+    const int stride = nblk * kWarps * 4;
+    int64_t row = (static_cast<int64_t>(blk) * kWarps + (threadIdx.x >> 5)) * 4 + (lane >> 3);
     // (token, head, position) of a row, stepped by `stride` rows without a division per step
     const int sdiv = stride / heads, smod = stride % heads, tstep = sdiv % seq_len;
     auto advance = [&](int& tok, int& hh, int& tt) {
@@ -920,7 +949,7 @@ qknorm_rope_bwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx,
             {
                 s += part[k2][i];
             }
-            partials[static_cast<size_t>(blockIdx.x) * 128 + i] = s;
+            partials[static_cast<size_t>(blk) * 128 + i] = s;
         }
     }
 }
@@ -1491,10 +1520,12 @@ extern "C" int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamm
     if (d128_ok(x, ldx, gamma, cosv, sinv, dy, lddy, head_dim, dtype) &&
         d128_ok(x, ldx, gamma, cosv, sinv, dx, lddx, head_dim, dtype) && rows < (1ll << 31))
     {
+        const QkSet one{static_cast<const bf16*>(x), static_cast<const bf16*>(gamma),
+                        static_cast<const bf16*>(dy), static_cast<bf16*>(dx), partials, ldx, lddy, lddx,
+                        static_cast<int>(heads), grid};
+        const QkSet none{nullptr, nullptr, nullptr, nullptr, nullptr, 0, 0, 0, 1, 0};
         qknorm_rope_bwd_d128_kernel<<<grid, kWarps * 32, 0, stream>>>(
-            static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(gamma), cosv, sinv,
-            static_cast<const bf16*>(dy), lddy, static_cast<bf16*>(dx), lddx, partials, tokens,
-            static_cast<int>(heads), static_cast<int>(seq_len), eps);
+            one, none, cosv, sinv, tokens, static_cast<int>(seq_len), eps);
     }
     else if (dtype == VEDA_BF16)
     {
@@ -1517,6 +1548,124 @@ extern "C" int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamm
         launch_reduce_partials(partials, grid, n, dgamma, stream);
     }
     return check_launch("veda_qknorm_rope_bwd");
+}
+
+namespace
+{
+// Blocks of a q + k launch: in proportion to their rows (both finish together), each set at least
+// one block and at most one per 4 x kWarps rows.
+void qk_pair_blocks(int64_t tokens, int64_t heads, int64_t kv_heads, int* gq, int* gk)
+{
+    const int64_t per = 4 * kWarps;
+    const int64_t total = 2LL * sm_count();
+    int64_t bq = total * heads / (heads + kv_heads);
+    bq = std::max<int64_t>(1, std::min<int64_t>(bq, (tokens * heads + per - 1) / per));
+    const int64_t bk =
+        std::max<int64_t>(1, std::min<int64_t>(total - bq, (tokens * kv_heads + per - 1) / per));
+    *gq = static_cast<int>(bq);
+    *gk = static_cast<int>(bk);
+}
+
+size_t round256(size_t b) { return (b + 255) / 256 * 256; }
+} // namespace
+
+extern "C" size_t veda_qknorm_rope_bwd_qk_workspace(int64_t tokens, int64_t heads, int64_t kv_heads,
+                                                    int64_t head_dim)
+{
+    // room for both forms: one launch over both sets, or the two sets one after the other
+    int gq = 1, gk = 1;
+    qk_pair_blocks(tokens, heads, kv_heads, &gq, &gk);
+    const size_t pair = static_cast<size_t>(gq + gk) * static_cast<size_t>(head_dim) * sizeof(float);
+    const size_t split = round256(veda_qknorm_rope_bwd_workspace(tokens, heads, head_dim)) +
+                         veda_qknorm_rope_bwd_workspace(tokens, kv_heads, head_dim);
+    return std::max(pair, split);
+}
+
+extern "C" int veda_qknorm_rope_bwd_qk(const void* xq, const void* xk, int64_t ldx,
+                                       const void* q_gamma, const void* k_gamma, const float* cosv,
+                                       const float* sinv, const void* dyq, int64_t lddyq,
+                                       const void* dyk, int64_t lddyk, void* dxq, void* dxk,
+                                       int64_t lddx, float* dq_gamma, float* dk_gamma,
+                                       void* workspace, size_t workspace_bytes, int64_t tokens,
+                                       int64_t heads, int64_t kv_heads, int64_t seq_len,
+                                       int64_t head_dim, float eps, int dtype, veda_stream_t stream)
+{
+    int rc = qk_checks(xq, ldx, q_gamma, cosv, sinv, tokens, heads, seq_len, head_dim, dtype);
+    if (rc == VEDA_OK)
+    {
+        rc = qk_checks(xk, ldx, k_gamma, cosv, sinv, tokens, kv_heads, seq_len, head_dim, dtype);
+    }
+    if (rc != VEDA_OK)
+    {
+        return rc;
+    }
+    VEDA_REQUIRE(dyq != nullptr && dyk != nullptr && dxq != nullptr && dxk != nullptr &&
+                     lddyq >= heads * head_dim && lddyk >= kv_heads * head_dim &&
+                     lddx >= heads * head_dim && lddx >= kv_heads * head_dim && lddyq % 2 == 0 &&
+                     lddyk % 2 == 0 && lddx % 2 == 0,
+                 "bad gradient operands");
+    if (tokens == 0)
+    {
+        return VEDA_OK;
+    }
+    if (dq_gamma != nullptr || dk_gamma != nullptr)
+    {
+        VEDA_REQUIRE(workspace != nullptr &&
+                         workspace_bytes >= veda_qknorm_rope_bwd_qk_workspace(tokens, heads, kv_heads,
+                                                                             head_dim),
+                     "workspace too small (see veda_qknorm_rope_bwd_qk_workspace)");
+    }
+    const bool one_launch =
+        d128_ok(xq, ldx, q_gamma, cosv, sinv, dyq, lddyq, head_dim, dtype) &&
+        d128_ok(xq, ldx, q_gamma, cosv, sinv, dxq, lddx, head_dim, dtype) &&
+        d128_ok(xk, ldx, k_gamma, cosv, sinv, dyk, lddyk, head_dim, dtype) &&
+        d128_ok(xk, ldx, k_gamma, cosv, sinv, dxk, lddx, head_dim, dtype) &&
+        tokens * std::max(heads, kv_heads) < (1ll << 31);
+    if (!one_launch)
+    {
+        // the general kernels: the two sets one after the other, each with its part of the
+        // workspace
+        const size_t wq = round256(veda_qknorm_rope_bwd_workspace(tokens, heads, head_dim));
+        char* w = static_cast<char*>(workspace);
+        rc = veda_qknorm_rope_bwd(xq, ldx, q_gamma, cosv, sinv, dyq, lddyq, dxq, lddx, dq_gamma,
+                                  w, w != nullptr ? wq : 0, tokens, heads, seq_len, head_dim, eps,
+                                  dtype, stream);
+        if (rc != VEDA_OK)
+        {
+            return rc;
+        }
+        return veda_qknorm_rope_bwd(xk, ldx, k_gamma, cosv, sinv, dyk, lddyk, dxk, lddx, dk_gamma,
+                                    w != nullptr ? w + wq : nullptr,
+                                    w != nullptr ? workspace_bytes - wq : 0, tokens, kv_heads,
+                                    seq_len, head_dim, eps, dtype, stream);
+    }
+    int gq = 1, gk = 1;
+    qk_pair_blocks(tokens, heads, kv_heads, &gq, &gk);
+    float* pq = dq_gamma != nullptr ? static_cast<float*>(workspace) : nullptr;
+    float* pk = dk_gamma != nullptr ? static_cast<float*>(workspace) + static_cast<size_t>(gq) * 128
+                                    : nullptr;
+    const QkSet sq{static_cast<const bf16*>(xq), static_cast<const bf16*>(q_gamma),
+                   static_cast<const bf16*>(dyq), static_cast<bf16*>(dxq), pq, ldx, lddyq, lddx,
+                   static_cast<int>(heads), gq};
+    const QkSet sk{static_cast<const bf16*>(xk), static_cast<const bf16*>(k_gamma),
+                   static_cast<const bf16*>(dyk), static_cast<bf16*>(dxk), pk, ldx, lddyk, lddx,
+                   static_cast<int>(kv_heads), gk};
+    qknorm_rope_bwd_d128_kernel<<<gq + gk, kWarps * 32, 0, stream>>>(
+        sq, sk, cosv, sinv, tokens, static_cast<int>(seq_len), eps);
+    count_launch();
+    if (pq != nullptr && pk != nullptr)
+    {
+        launch_reduce_partials(pq, gq, 128, dq_gamma, stream, pk, gk, dk_gamma);
+    }
+    else if (pq != nullptr)
+    {
+        launch_reduce_partials(pq, gq, 128, dq_gamma, stream);
+    }
+    else if (pk != nullptr)
+    {
+        launch_reduce_partials(pk, gk, 128, dk_gamma, stream);
+    }
+    return check_launch("veda_qknorm_rope_bwd_qk");
 }
 
 extern "C" int veda_rope(const void* x, void* y, const float* cosv, const float* sinv,
