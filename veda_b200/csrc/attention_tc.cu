@@ -838,6 +838,7 @@ struct FusedParams
     float scale, scale_log2;
     int causal;
     int* status;
+    int chunk;   // (batch, KV head) pairs per launch-order chunk (see attn_bwd_fused_kernel)
 };
 
 __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int x,
@@ -952,8 +953,17 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
         return;
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kt = static_cast<int>(blockIdx.y);   // launch order: all heads' key tile 0 (the
-    const int bk = blockIdx.x;                      // longest under the causal mask) first
+    // Launch order: the (batch, KV head) pairs in chunks of p.chunk, and inside a chunk every
+    // pair's key tile 0 (the longest under the causal mask) first, then tile 1, ... So the CTAs
+    // running at any time share the Q / dO tiles and dQ accumulator rows of one chunk, which stay
+    // in L2 (all pairs at once thrashed it: 45 % L2 hits, 1.59 GB of DRAM traffic at B 8 T 2048),
+    // while the longest-first order inside the chunk keeps the tail short.
+    const int npair = static_cast<int>(gridDim.x), ntile = static_cast<int>(gridDim.y);
+    const int order = static_cast<int>(blockIdx.y) * npair + static_cast<int>(blockIdx.x);
+    const int chunk = order / (p.chunk * ntile), within = order % (p.chunk * ntile);
+    const int in_chunk = npair - chunk * p.chunk < p.chunk ? npair - chunk * p.chunk : p.chunk;
+    const int kt = within / in_chunk;
+    const int bk = chunk * p.chunk + within % in_chunk;
     const int b = bk / p.Hkv, kvh = bk % p.Hkv;
     const int rep = p.H / p.Hkv;
     const int nq = (p.T + kFq - 1) / kFq;
@@ -1744,9 +1754,16 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
         attn_rowdot_kernel<<<rowdot_grid(B, T, H), 256, 0, s>>>(
             static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, lse, dvec, nlse2,
             dqacc, static_cast<int>(T), static_cast<int>(H));
+        // pairs per chunk: as many as keep a chunk's Q, dO (2 x 256 B) and dQ accumulator rows
+        // (512 B) per query and head within ~48 MB of L2, a power of two from 8 (fewer leaves a
+        // long tail of key-tile-0 CTAs) up to all pairs
+        const int64_t per_pair = 1024 * (H / Hkv) * T;
+        int chunk = 8;
+        while (chunk < B * Hkv && static_cast<int64_t>(chunk) * 2 * per_pair <= (48ll << 20)) chunk *= 2;
         FusedParams p{nlse2, dvec, static_cast<bf16*>(dk), static_cast<bf16*>(dv), lddk, lddv,
                       static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
-                      scale * kLog2e, causal, device_status_ptr()};
+                      scale * kLog2e, causal, device_status_ptr(),
+                      static_cast<int>(std::min<int64_t>(chunk, B * Hkv))};
         attn_bwd_fused_kernel<<<grid, kFusedThreads, kFusedSmem, s>>>(mq, mk, mv, mdo, mdq, p);
         attn_dq_cast_kernel<<<grid_for(B * T * H * 16, 256), 256, 0, s>>>(
             dqacc, static_cast<bf16*>(dq), lddq, B * T, H * 128, scale);
