@@ -1,7 +1,8 @@
 // Causal GQA attention on the 5th-generation tensor cores (tcgen05.mma, TMEM), bf16, head_dim 128.
 //
-// Same semantics as attention_flash.cu (the composition of src/libs/train/Model.cpp:182-189 with
-// kv head h / (H/Hkv), src/libs/model/Attention.cpp:191); this file is the sm_100a-native form.
+// Same semantics as the warp-per-row kernels of attention.cu (the composition of
+// src/libs/train/Model.cpp:182-189 with kv head h / (H/Hkv), src/libs/model/Attention.cpp:191);
+// this file is the bf16, head_dim-128 tensor-core form the entry points dispatch to.
 //
 // Forward — one CTA per (batch, head, pair of 128-query tiles A and B); 10 warps:
 //   warp 0     TMA (lane 0: both Q tiles, then 128-key K tiles; lane 1: the V tiles), each into
