@@ -139,16 +139,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 
-// Bulk tensor prefetch into L2: no shared-memory destination, no completion to wait for, no
-// multicast; a tile this CTA loads later leaves DRAM ahead of its load.
-__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int x, int y, int z)
-{
-    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(x), "r"(y), "r"(z)
-                 : "memory");
-}
-
 __device__ __forceinline__ void tma_prefetch(const CUtensorMap* map)
 {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
