@@ -161,13 +161,17 @@ size_t veda_qknorm_rope_bwd_workspace(int64_t tokens, int64_t heads, int64_t hea
  * reductions: x rows xq (heads) and xk (kv_heads) at stride ldx, gradients dyq / dyk at their
  * strides, results dxq / dxk at stride lddx, dq_gamma / dk_gamma (either may be NULL) +=.
  * The same arithmetic as two veda_qknorm_rope_bwd calls; the gain gradients are summed over a
- * different number of blocks, so they agree with those calls to rounding. workspace:
+ * different number of blocks, so they agree with those calls to rounding. dyq_f32 = 1 (bf16,
+ * head_dim 128 only): dyq holds fp32 rows (stride lddyq floats, 16-byte aligned), read as
+ * bf16(dyq * dyq_scale) — the dQ accumulator veda_attention_bwd_dq_f32 leaves, with the rounding
+ * veda_attention_bwd applies when it writes dq itself. workspace:
  * veda_qknorm_rope_bwd_qk_workspace() bytes. */
 int veda_qknorm_rope_bwd_qk(const void* xq, const void* xk, int64_t ldx, const void* q_gamma,
                             const void* k_gamma, const float* cos, const float* sin,
-                            const void* dyq, int64_t lddyq, const void* dyk, int64_t lddyk,
-                            void* dxq, void* dxk, int64_t lddx, float* dq_gamma, float* dk_gamma,
-                            void* workspace, size_t workspace_bytes, int64_t tokens, int64_t heads,
+                            const void* dyq, int64_t lddyq, int dyq_f32, float dyq_scale,
+                            const void* dyk, int64_t lddyk, void* dxq, void* dxk, int64_t lddx,
+                            float* dq_gamma, float* dk_gamma, void* workspace,
+                            size_t workspace_bytes, int64_t tokens, int64_t heads,
                             int64_t kv_heads, int64_t seq_len, int64_t head_dim, float eps,
                             int dtype, veda_stream_t stream);
 size_t veda_qknorm_rope_bwd_qk_workspace(int64_t tokens, int64_t heads, int64_t kv_heads,
@@ -424,6 +428,20 @@ int veda_attention_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, c
                        float scale, int causal, int dtype, veda_stream_t stream);
 size_t veda_attention_bwd_workspace(int64_t batch, int64_t seq_len, int64_t heads,
                                     int64_t kv_heads, int64_t head_dim, int dtype);
+/* veda_attention_bwd without its last pass: dQ is not written; it is left, unscaled, as fp32
+ * [batch * seq_len, heads * 128] token-major rows (dQ = scale * row) at
+ * workspace + veda_attention_bwd_dq_offset(), for a consumer that reads it directly
+ * (veda_qknorm_rope_bwd_qk with dyq_f32). dK and dV are written as by veda_attention_bwd. Only the
+ * fused tensor-core backward keeps dQ in fp32 (bf16, head_dim 128, 16-byte aligned operands, not
+ * the deterministic mode); otherwise VEDA_ERR_UNSUPPORTED is returned and nothing runs. */
+int veda_attention_bwd_dq_f32(const void* q, int64_t ldq, const void* k, int64_t ldk,
+                              const void* v, int64_t ldv, const void* o, int64_t ldo,
+                              const void* dout, int64_t lddo, const float* lse, void* dk,
+                              int64_t lddk, void* dv, int64_t lddv, void* workspace,
+                              size_t workspace_bytes, int64_t batch, int64_t seq_len, int64_t heads,
+                              int64_t kv_heads, int64_t head_dim, float scale, int causal,
+                              int dtype, veda_stream_t stream);
+size_t veda_attention_bwd_dq_offset(int64_t batch, int64_t seq_len, int64_t heads);
 /* on = 1: the bf16 backward runs its two-kernel form, whose dQ is bit-reproducible run to run
  * (dS^T through HBM, O(B*H*T^2) workspace); on = 0 (the default; VEDA_ATTENTION_DETERMINISTIC=1
  * in the environment starts at 1): the fused kernel, whose dQ sums key tiles in a varying order.

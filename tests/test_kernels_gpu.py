@@ -205,7 +205,7 @@ def test_qknorm_rope_bwd_q_and_k_in_one_launch(dtype, B, T, H, Hk, with_k_gain):
     dqg, dkg = dev(np.full(Dh, 0.25, F32)), dev(np.full(Dh, -0.5, F32))
     ws = workspace(lib.veda_qknorm_rope_bwd_qk_workspace(N, H, Hk, Dh))
     call("veda_qknorm_rope_bwd_qk", xq, xk, W, ptr(qgd), ptr(kgd), ptr(cd), ptr(sd), ptr(gqd), H * Dh,
-         ptr(gkd), Hk * Dh, ptr(dx), ptr(dx) + H * Dh * es, W, ptr(dqg),
+         0, 1.0, ptr(gkd), Hk * Dh, ptr(dx), ptr(dx) + H * Dh * es, W, ptr(dqg),
          ptr(dkg) if with_k_gain else None, ptr(ws), ws.numel(), N, H, Hk, T, Dh, 1e-6, dtype, stream())
     # two calls
     dxq, dxk = empty((N, H * Dh), dtype), empty((N, Hk * Dh), dtype)
@@ -639,6 +639,58 @@ def _attention_case(dtype, B, T, H, Hk, Dh, seed):
     sync()
     return (host(o), tok(o_ref), host(lse).reshape(B, H, T), lse_ref, host(dq), tok(dq_ref),
             host(dk), tok(dk_ref), host(dv), tok(dv_ref))
+
+
+def test_attention_bwd_dq_f32_feeds_the_norm_backward():
+    """veda_attention_bwd_dq_f32 leaves dQ unscaled in the fp32 accumulator of its workspace and
+    writes dK, dV like veda_attention_bwd; the q+k norm backward reading that accumulator
+    (dyq_f32, the attention scale) gives bit for bit what it gives on bf16(scale * accumulator),
+    the dQ veda_attention_bwd would have written."""
+    import torch as T_
+    B, T, H, Hk, Dh = 2, 256, 16, 8, 128
+    o, o_ref, lse, lse_ref, dq, dq_ref, dk, dk_ref, dv, dv_ref = _attention_case(V.BF16, B, T, H, Hk, Dh, 11)
+    lib = V.lib()
+    r = rng(11)   # the same inputs as _attention_case drew
+    q = bf(r.standard_normal((B, H, T, Dh)).astype(F32))
+    k = bf(r.standard_normal((B, Hk, T, Dh)).astype(F32))
+    v = bf(r.standard_normal((B, Hk, T, Dh)).astype(F32))
+    do = bf(r.standard_normal((B, H, T, Dh)).astype(F32))
+    tok = lambda a: np.ascontiguousarray(a.transpose(0, 2, 1, 3)).reshape(B * T, -1)  # noqa: E731
+    qd, kd, vd, dod = dev(tok(q), V.BF16), dev(tok(k), V.BF16), dev(tok(v), V.BF16), dev(tok(do), V.BF16)
+    od, lsed = dev(o_ref, V.BF16), dev(lse_ref.reshape(-1).astype(F32))
+    scale = 1.0 / math.sqrt(Dh)
+    ws = workspace(lib.veda_attention_bwd_workspace(B, T, H, Hk, Dh, V.BF16))
+    dk2, dv2 = empty((B * T, Hk * Dh), V.BF16), empty((B * T, Hk * Dh), V.BF16)
+    call("veda_attention_bwd_dq_f32", ptr(qd), H * Dh, ptr(kd), Hk * Dh, ptr(vd), Hk * Dh, ptr(od), H * Dh,
+         ptr(dod), H * Dh, ptr(lsed), ptr(dk2), Hk * Dh, ptr(dv2), Hk * Dh, ptr(ws), ws.numel(), B, T, H, Hk,
+         Dh, scale, 1, V.BF16, stream())
+    sync()
+    off = lib.veda_attention_bwd_dq_offset(B, T, H)
+    acc = ws[off:off + B * T * H * Dh * 4].view(T_.float32).reshape(B * T, H * Dh)
+    assert rel(host(dk2), dk_ref) <= TOL[V.BF16] and rel(host(dv2), dv_ref) <= TOL[V.BF16]
+    assert rel(acc.cpu().numpy() * scale, dq_ref) <= TOL[V.BF16]
+    # the norm backward on the accumulator and on its rounded copy
+    x = bf(r.standard_normal((B * T, (H + 2 * Hk) * Dh)).astype(F32))
+    W = x.shape[1]
+    xd = dev(x, V.BF16)
+    qg, kg = dev(bf((1 + 0.1 * r.standard_normal(Dh)).astype(F32)), V.BF16), dev(bf((1 + 0.1 * r.standard_normal(Dh)).astype(F32)), V.BF16)
+    cos, sin = O.rope_tables(T, Dh, 1e6)
+    cd, sd = dev(cos), dev(sin)
+    dkd = dev(bf(r.standard_normal((B * T, Hk * Dh)).astype(F32)), V.BF16)
+    dq_bf = (acc * scale).to(T_.bfloat16).contiguous()
+    outs = []
+    for f32 in (1, 0):
+        dx = empty((B * T, W), V.BF16)
+        dgq, dgk = dev(np.zeros(Dh, F32)), dev(np.zeros(Dh, F32))
+        w2 = workspace(lib.veda_qknorm_rope_bwd_qk_workspace(B * T, H, Hk, Dh))
+        src = acc.data_ptr() if f32 else dq_bf.data_ptr()
+        call("veda_qknorm_rope_bwd_qk", ptr(xd), ptr(xd) + H * Dh * 2, W, ptr(qg), ptr(kg), ptr(cd), ptr(sd),
+             src, H * Dh, f32, scale if f32 else 1.0, ptr(dkd), Hk * Dh, ptr(dx), ptr(dx) + H * Dh * 2, W,
+             ptr(dgq), ptr(dgk), ptr(w2), w2.numel(), B * T, H, Hk, T, Dh, 1e-6, V.BF16, stream())
+        sync()
+        outs.append((host(dx)[:, :(H + Hk) * Dh], host(dgq), host(dgk)))   # the q and k columns
+    for a_, b_ in zip(outs[0], outs[1]):
+        assert np.array_equal(a_, b_)
 
 
 @pytest.mark.parametrize("dtype,B,T,H,Hk,Dh", [(V.F32, 4, 32, 4, 2, 16), (V.F32, 2, 70, 4, 1, 64),

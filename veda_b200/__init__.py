@@ -55,9 +55,9 @@ SIGNATURES = {
     "veda_qknorm_rope_bwd": (_i, [_p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _p, _sz, _i64,
                                   _i64, _i64, _i64, _f, _i, _p]),
     "veda_qknorm_rope_bwd_workspace": (_sz, [_i64, _i64, _i64]),
-    "veda_qknorm_rope_bwd_qk": (_i, [_p, _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i64, _p, _p,
-                                     _i64, _p, _p, _p, _sz, _i64, _i64, _i64, _i64, _i64, _f, _i,
-                                     _p]),
+    "veda_qknorm_rope_bwd_qk": (_i, [_p, _p, _i64, _p, _p, _p, _p, _p, _i64, _i, _f, _p, _i64,
+                                     _p, _p, _i64, _p, _p, _p, _sz, _i64, _i64, _i64, _i64, _i64,
+                                     _f, _i, _p]),
     "veda_qknorm_rope_bwd_qk_workspace": (_sz, [_i64, _i64, _i64, _i64]),
     "veda_rope": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _p]),
     "veda_swiglu_fwd": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i, _p]),
@@ -115,6 +115,10 @@ SIGNATURES = {
                                 _p, _i64, _p, _i64, _p, _sz, _i64, _i64, _i64, _i64, _i64, _f,
                                 _i, _i, _p]),
     "veda_attention_bwd_workspace": (_sz, [_i64, _i64, _i64, _i64, _i64, _i]),
+    "veda_attention_bwd_dq_f32": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _p, _p,
+                                       _i64, _p, _i64, _p, _sz, _i64, _i64, _i64, _i64, _i64, _f,
+                                       _i, _i, _p]),
+    "veda_attention_bwd_dq_offset": (_sz, [_i64, _i64, _i64]),
     "veda_attention_set_deterministic": (_i, [_i]),
     "veda_log_softmax_fwd": (_i, [_p, _p, _i64, _i64, _i, _p]),
 }

@@ -370,6 +370,50 @@ extern "C" int veda_attention_bwd(const void* q, int64_t ldq, const void* k, int
     return check_launch("veda_attention_bwd");
 }
 
+extern "C" size_t veda_attention_bwd_dq_offset(int64_t batch, int64_t seq_len, int64_t heads)
+{
+    return (static_cast<size_t>(batch * heads * seq_len) * sizeof(float) + 255) &
+           ~static_cast<size_t>(255);
+}
+
+extern "C" int veda_attention_bwd_dq_f32(const void* q, int64_t ldq, const void* k, int64_t ldk,
+                                         const void* v, int64_t ldv, const void* o, int64_t ldo,
+                                         const void* dout, int64_t lddo, const float* lse, void* dk,
+                                         int64_t lddk, void* dv, int64_t lddv, void* workspace,
+                                         size_t workspace_bytes, int64_t batch, int64_t seq_len,
+                                         int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                         float scale, int causal, int dtype, veda_stream_t stream)
+{
+    int rc = checks(batch, seq_len, heads, kv_heads, head_dim, ldq, ldk, ldv, ldo, dtype);
+    if (rc != VEDA_OK) return rc;
+    VEDA_REQUIRE(lddo >= heads * head_dim && lddk >= kv_heads * head_dim &&
+                     lddv >= kv_heads * head_dim,
+                 "gradient leading dimension too small");
+    if (batch == 0 || seq_len == 0) return VEDA_OK;
+    VEDA_REQUIRE(q && k && v && o && dout && lse && dk && dv, "null pointer");
+    VEDA_REQUIRE(workspace != nullptr &&
+                     workspace_bytes >= veda_attention_bwd_workspace(batch, seq_len, heads,
+                                                                     kv_heads, head_dim, dtype),
+                 "workspace too small (see veda_attention_bwd_workspace)");
+    if (!tc_supported(head_dim, dtype) || attention_deterministic() != 0 ||
+        !tc_aligned(q, ldq, k, ldk, v, ldv, o, ldo) || !tc_aligned(dout, lddo, dk, lddk, dv, lddv, dk, lddk))
+    {
+        return fail(VEDA_ERR_UNSUPPORTED,
+                    "veda_attention_bwd_dq_f32: only the fused tensor-core backward (bf16, head_dim "
+                    "128, 16-byte aligned operands, not the deterministic mode) keeps dQ in fp32");
+    }
+    float* dvec = static_cast<float*>(workspace);
+    char* extra = static_cast<char*>(workspace) + veda_attention_bwd_dq_offset(batch, seq_len, heads);
+    const int rc2 = attn_tc_bwd(q, ldq, k, ldk, v, ldv, o, ldo, dout, lddo, lse, nullptr, 0, dk, lddk,
+                                dv, lddv, dvec, extra, batch, seq_len, heads, kv_heads, scale,
+                                causal, stream);
+    if (rc2 == -1)
+    {
+        return fail(VEDA_ERR_UNSUPPORTED, "veda_attention_bwd_dq_f32: the shape needs the general kernels");
+    }
+    return rc2;
+}
+
 extern "C" int veda_attention_set_deterministic(int on)
 {
     return veda::cuda::g_attn_deterministic.exchange(on ? 1 : 0);

@@ -27,7 +27,9 @@ inline bool tc_aligned(const void* a, int64_t lda, const void* b, int64_t ldb, c
 size_t tc_bwd_extra_workspace(int64_t B, int64_t T, int64_t H);
 
 // tcgen05 kernels (bf16, head_dim 128, 16-byte aligned operands); return -1 when a tensor map
-// cannot be built for the shape (the caller then runs the generic kernels).
+// cannot be built for the shape (the caller then runs the generic kernels). attn_tc_bwd with
+// dq == nullptr (fused kernel only, -1 in the deterministic mode) leaves dQ / scale in the fp32
+// accumulator at the start of `extra` instead of rounding it into dq.
 int attn_tc_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
                 void* o, int64_t ldo, float* lse, int64_t B, int64_t T, int64_t H, int64_t Hkv,
                 float scale, int causal, cudaStream_t s);

@@ -1723,6 +1723,10 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     }
     // Q and dO tiles: 128 query rows for the fused kernel, 64 for the two-kernel path
     const bool det = attention_deterministic() != 0;
+    if (det && dq == nullptr)
+    {
+        return -1;   // only the fused kernel leaves dQ in an fp32 accumulator
+    }
     const uint32_t qrows = det ? kBq : kFq;
     CUtensorMap mq, mk, mv, mdo, mds;
     if (!make_map3(&mq, q, H * 128, T, B, ldq, qrows) || !make_map3(&mk, k, Hkv * 128, T, B, ldk, 128) ||
@@ -1766,6 +1770,12 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
                       scale * kLog2e, causal, device_status_ptr(),
                       static_cast<int>(std::min<int64_t>(chunk, B * Hkv))};
         attn_bwd_fused_kernel<<<grid, kFusedThreads, kFusedSmem, s>>>(mq, mk, mv, mdo, mdq, p);
+        if (dq == nullptr)
+        {
+            // the caller reads dQ / scale from the fp32 accumulator itself
+            count_launch(2);
+            return check_launch("veda_attention_bwd (tcgen05, fused, dQ left in fp32)");
+        }
         attn_dq_cast_kernel<<<grid_for(B * T * H * 16, 256), 256, 0, s>>>(
             dqacc, static_cast<bf16*>(dq), lddq, B * T, H * 128, scale);
         count_launch(3);

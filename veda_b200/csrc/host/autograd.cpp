@@ -1488,22 +1488,46 @@ void attention_backward(const AttentionSaved& a, const Tensor& g)
     const int64_t ld = a.ld;
     const char* base = static_cast<const char*>(a.x.data_ptr());
     const Tensor gc = as_dtype(g, d);
-    Tensor dqr = Tensor::empty(Shape({N, H * Dh}), d);
+    Tensor dqr;
     Tensor dkr = Tensor::empty(Shape({N, Hkv * Dh}), d);
     Tensor dx = Tensor::empty(Shape({N, W}), d);
     char* dbase = static_cast<char*>(dx.data_ptr());
     const size_t ws_bytes = veda_attention_bwd_workspace(B, T, H, Hkv, Dh, dt(d));
     Tensor ws = Tensor::empty(Shape({(ws_bytes + 3) / 4}), DType::F32);
+    // where the norm backward reads dQ: the fused kernel's fp32 accumulator (no separate pass
+    // rounding it into a bf16 dQ), or a dQ written by the general path
+    const void* dq_src = nullptr;
+    int64_t dq_ld = H * Dh;
+    bool dq_f32 = false;
     {
         // causal backward with the softmax recomputed: 5 products of T^2 Dh per (batch, head)
         profile::Scope scope("attn_bwd", 5.0 * B * H * static_cast<double>(T) * T * Dh, 0.0);
-        check(veda_attention_bwd(a.qr.data_ptr(), H * Dh, a.kr.data_ptr(), Hkv * Dh,
-                                 base + (H + Hkv) * Dh * es, ld, a.out.data_ptr(), H * Dh,
-                                 gc.data_ptr(), H * Dh, static_cast<const float*>(a.lse.data_ptr()),
-                                 dqr.data_ptr(), H * Dh, dkr.data_ptr(), Hkv * Dh,
-                                 dbase + (H + Hkv) * Dh * es, W, ws.data_ptr(), ws_bytes, B, T, H,
-                                 Hkv, Dh, a.scale, 1, dt(d), S()),
-              "attention backward");
+        const int rc = veda_attention_bwd_dq_f32(
+            a.qr.data_ptr(), H * Dh, a.kr.data_ptr(), Hkv * Dh, base + (H + Hkv) * Dh * es, ld,
+            a.out.data_ptr(), H * Dh, gc.data_ptr(), H * Dh, static_cast<const float*>(a.lse.data_ptr()),
+            dkr.data_ptr(), Hkv * Dh, dbase + (H + Hkv) * Dh * es, W, ws.data_ptr(), ws_bytes, B, T, H,
+            Hkv, Dh, a.scale, 1, dt(d), S());
+        if (rc == VEDA_OK)
+        {
+            dq_src = static_cast<const char*>(ws.data_ptr()) + veda_attention_bwd_dq_offset(B, T, H);
+            dq_f32 = true;
+        }
+        else if (rc == VEDA_ERR_UNSUPPORTED)
+        {
+            dqr = Tensor::empty(Shape({N, H * Dh}), d);
+            check(veda_attention_bwd(a.qr.data_ptr(), H * Dh, a.kr.data_ptr(), Hkv * Dh,
+                                     base + (H + Hkv) * Dh * es, ld, a.out.data_ptr(), H * Dh,
+                                     gc.data_ptr(), H * Dh, static_cast<const float*>(a.lse.data_ptr()),
+                                     dqr.data_ptr(), H * Dh, dkr.data_ptr(), Hkv * Dh,
+                                     dbase + (H + Hkv) * Dh * es, W, ws.data_ptr(), ws_bytes, B, T,
+                                     H, Hkv, Dh, a.scale, 1, dt(d), S()),
+                  "attention backward");
+            dq_src = dqr.data_ptr();
+        }
+        else
+        {
+            check(rc, "attention backward");
+        }
     }
     // q_norm and k_norm backward in one launch: dq, dk into their columns of the fused gradient
     auto gain_target = [&](const std::shared_ptr<Node>& gain) -> float* {
@@ -1521,12 +1545,16 @@ void attention_backward(const AttentionSaved& a, const Tensor& g)
     const size_t wsb = veda_qknorm_rope_bwd_qk_workspace(N, H, Hkv, Dh);
     Tensor w2 = Tensor::empty(Shape({(wsb + 3) / 4 + 1}), DType::F32);
     {
-        // reads x and dy, writes dx: 3 bytes-per-element passes over [N, (H + Hkv) * Dh]
-        profile::Scope scope("qknorm_bwd", 0.0, 3.0 * static_cast<double>(N) * (H + Hkv) * Dh * es);
+        // reads x and dy, writes dx over [N, (H + Hkv) * Dh]; the q part of dy is the attention
+        // backward's fp32 dQ accumulator when it kept one
+        const double elems = static_cast<double>(N) * Dh;
+        profile::Scope scope("qknorm_bwd", 0.0,
+                             elems * ((H + Hkv) * 2.0 * es + H * (dq_f32 ? 4.0 : es) + Hkv * es));
         check(veda_qknorm_rope_bwd_qk(base, base + H * Dh * es, ld, a.qg.data_ptr(), a.kg.data_ptr(),
                                       static_cast<const float*>(a.c.data_ptr()),
-                                      static_cast<const float*>(a.s.data_ptr()), dqr.data_ptr(), H * Dh,
-                                      dkr.data_ptr(), Hkv * Dh, dbase, dbase + H * Dh * es, W, dqg, dkg,
+                                      static_cast<const float*>(a.s.data_ptr()), dq_src, dq_ld,
+                                      dq_f32 ? 1 : 0, a.scale, dkr.data_ptr(), Hkv * Dh, dbase,
+                                      dbase + H * Dh * es, W, dqg, dkg,
                                       w2.data_ptr(), wsb, N, H, Hkv, T, Dh, a.eps, dt(d), S()),
               "attention backward: norm + rope");
     }

@@ -797,6 +797,10 @@ struct QkSet
     float* partials;
     int64_t ldx, lddy, lddx;
     int heads, blocks;
+    // instead of dy: fp32 rows (stride lddy floats) read as bf16(dyf * dy_scale) — the attention
+    // backward's dQ accumulator and the rounding it would have applied itself
+    const float* dyf;
+    float dy_scale;
 };
 
 // Shared memory: [kWarps * 4][128] fp32 gain-gradient rows (one per row slot).
@@ -810,6 +814,8 @@ qknorm_rope_bwd_d128_kernel(const QkSet s0, const QkSet s1, const float* __restr
     const bf16* __restrict__ x = second ? s1.x : s0.x;
     const bf16* __restrict__ gamma = second ? s1.gamma : s0.gamma;
     const bf16* __restrict__ dy = second ? s1.dy : s0.dy;
+    const float* __restrict__ dyf = second ? s1.dyf : s0.dyf;
+    const float dy_scale = second ? s1.dy_scale : s0.dy_scale;
     bf16* __restrict__ dx = second ? s1.dx : s0.dx;
     float* __restrict__ partials = second ? s1.partials : s0.partials;
     const int64_t ldx = second ? s1.ldx : s0.ldx, lddy = second ? s1.lddy : s0.lddy,
@@ -848,11 +854,32 @@ qknorm_rope_bwd_d128_kernel(const QkSet s0, const QkSet s1, const float* __restr
         if (r < rows)
         {
             const bf16* xr = x + static_cast<int64_t>(tok) * ldx + hh * 128;
-            const bf16* gr = dy + static_cast<int64_t>(tok) * lddy + hh * 128;
             a = *reinterpret_cast<const uint4*>(xr + 8 * q);
             b = *reinterpret_cast<const uint4*>(xr + 64 + 8 * q);
-            da = *reinterpret_cast<const uint4*>(gr + 8 * q);
-            db = *reinterpret_cast<const uint4*>(gr + 64 + 8 * q);
+            if (dyf != nullptr)
+            {
+                const float* gf = dyf + static_cast<int64_t>(tok) * lddy + hh * 128;
+                auto round8 = [&](const float* src) {
+                    const float4 u = *reinterpret_cast<const float4*>(src);
+                    const float4 w = *reinterpret_cast<const float4*>(src + 4);
+                    const __nv_bfloat162 p0 = __floats2bfloat162_rn(u.x * dy_scale, u.y * dy_scale);
+                    const __nv_bfloat162 p1 = __floats2bfloat162_rn(u.z * dy_scale, u.w * dy_scale);
+                    const __nv_bfloat162 p2 = __floats2bfloat162_rn(w.x * dy_scale, w.y * dy_scale);
+                    const __nv_bfloat162 p3 = __floats2bfloat162_rn(w.z * dy_scale, w.w * dy_scale);
+                    return make_uint4(*reinterpret_cast<const uint32_t*>(&p0),
+                                      *reinterpret_cast<const uint32_t*>(&p1),
+                                      *reinterpret_cast<const uint32_t*>(&p2),
+                                      *reinterpret_cast<const uint32_t*>(&p3));
+                };
+                da = round8(gf + 8 * q);
+                db = round8(gf + 64 + 8 * q);
+            }
+            else
+            {
+                const bf16* gr = dy + static_cast<int64_t>(tok) * lddy + hh * 128;
+                da = *reinterpret_cast<const uint4*>(gr + 8 * q);
+                db = *reinterpret_cast<const uint4*>(gr + 64 + 8 * q);
+            }
         }
         else
         {
@@ -1522,8 +1549,8 @@ extern "C" int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamm
     {
         const QkSet one{static_cast<const bf16*>(x), static_cast<const bf16*>(gamma),
                         static_cast<const bf16*>(dy), static_cast<bf16*>(dx), partials, ldx, lddy, lddx,
-                        static_cast<int>(heads), grid};
-        const QkSet none{nullptr, nullptr, nullptr, nullptr, nullptr, 0, 0, 0, 1, 0};
+                        static_cast<int>(heads), grid, nullptr, 1.0f};
+        const QkSet none{nullptr, nullptr, nullptr, nullptr, nullptr, 0, 0, 0, 1, 0, nullptr, 1.0f};
         qknorm_rope_bwd_d128_kernel<<<grid, kWarps * 32, 0, stream>>>(
             one, none, cosv, sinv, tokens, static_cast<int>(seq_len), eps);
     }
@@ -1584,11 +1611,12 @@ extern "C" size_t veda_qknorm_rope_bwd_qk_workspace(int64_t tokens, int64_t head
 extern "C" int veda_qknorm_rope_bwd_qk(const void* xq, const void* xk, int64_t ldx,
                                        const void* q_gamma, const void* k_gamma, const float* cosv,
                                        const float* sinv, const void* dyq, int64_t lddyq,
-                                       const void* dyk, int64_t lddyk, void* dxq, void* dxk,
-                                       int64_t lddx, float* dq_gamma, float* dk_gamma,
-                                       void* workspace, size_t workspace_bytes, int64_t tokens,
-                                       int64_t heads, int64_t kv_heads, int64_t seq_len,
-                                       int64_t head_dim, float eps, int dtype, veda_stream_t stream)
+                                       int dyq_f32, float dyq_scale, const void* dyk, int64_t lddyk,
+                                       void* dxq, void* dxk, int64_t lddx, float* dq_gamma,
+                                       float* dk_gamma, void* workspace, size_t workspace_bytes,
+                                       int64_t tokens, int64_t heads, int64_t kv_heads,
+                                       int64_t seq_len, int64_t head_dim, float eps, int dtype,
+                                       veda_stream_t stream)
 {
     int rc = qk_checks(xq, ldx, q_gamma, cosv, sinv, tokens, heads, seq_len, head_dim, dtype);
     if (rc == VEDA_OK)
@@ -1615,14 +1643,18 @@ extern "C" int veda_qknorm_rope_bwd_qk(const void* xq, const void* xk, int64_t l
                                                                              head_dim),
                      "workspace too small (see veda_qknorm_rope_bwd_qk_workspace)");
     }
+    // fp32 dyq rows: 16-byte aligned rows of floats
+    const bool dyq_ok = dyq_f32 ? (aligned16(dyq) && lddyq % 4 == 0)
+                                : d128_ok(xq, ldx, q_gamma, cosv, sinv, dyq, lddyq, head_dim, dtype);
     const bool one_launch =
-        d128_ok(xq, ldx, q_gamma, cosv, sinv, dyq, lddyq, head_dim, dtype) &&
+        dyq_ok &&
         d128_ok(xq, ldx, q_gamma, cosv, sinv, dxq, lddx, head_dim, dtype) &&
         d128_ok(xk, ldx, k_gamma, cosv, sinv, dyk, lddyk, head_dim, dtype) &&
         d128_ok(xk, ldx, k_gamma, cosv, sinv, dxk, lddx, head_dim, dtype) &&
         tokens * std::max(heads, kv_heads) < (1ll << 31);
     if (!one_launch)
     {
+        VEDA_REQUIRE(!dyq_f32, "fp32 q gradients need bf16, head_dim 128 and 16-byte aligned rows");
         // the general kernels: the two sets one after the other, each with its part of the
         // workspace
         const size_t wq = round256(veda_qknorm_rope_bwd_workspace(tokens, heads, head_dim));
@@ -1645,11 +1677,12 @@ extern "C" int veda_qknorm_rope_bwd_qk(const void* xq, const void* xk, int64_t l
     float* pk = dk_gamma != nullptr ? static_cast<float*>(workspace) + static_cast<size_t>(gq) * 128
                                     : nullptr;
     const QkSet sq{static_cast<const bf16*>(xq), static_cast<const bf16*>(q_gamma),
-                   static_cast<const bf16*>(dyq), static_cast<bf16*>(dxq), pq, ldx, lddyq, lddx,
-                   static_cast<int>(heads), gq};
+                   dyq_f32 ? nullptr : static_cast<const bf16*>(dyq), static_cast<bf16*>(dxq), pq,
+                   ldx, lddyq, lddx, static_cast<int>(heads), gq,
+                   dyq_f32 ? static_cast<const float*>(dyq) : nullptr, dyq_scale};
     const QkSet sk{static_cast<const bf16*>(xk), static_cast<const bf16*>(k_gamma),
                    static_cast<const bf16*>(dyk), static_cast<bf16*>(dxk), pk, ldx, lddyk, lddx,
-                   static_cast<int>(kv_heads), gk};
+                   static_cast<int>(kv_heads), gk, nullptr, 1.0f};
     qknorm_rope_bwd_d128_kernel<<<gq + gk, kWarps * 32, 0, stream>>>(
         sq, sk, cosv, sinv, tokens, static_cast<int>(seq_len), eps);
     count_launch();
