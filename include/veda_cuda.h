@@ -148,6 +148,14 @@ int veda_qknorm_rope_fwd(const void* x, int64_t ldx, const void* gamma, const fl
                          const float* sin, void* y, int64_t ldy, int64_t tokens, int64_t heads,
                          int64_t seq_len, int64_t head_dim, float eps, int dtype,
                          veda_stream_t stream);
+/* veda_qknorm_rope_fwd for the q and the k heads of one attention layer in one launch: x rows xq
+ * (heads) and xk (kv_heads) at stride ldx, their gains, outputs yq / yk at their strides; the
+ * same arithmetic, bit for bit, as two veda_qknorm_rope_fwd calls. */
+int veda_qknorm_rope_fwd_qk(const void* xq, const void* xk, int64_t ldx, const void* q_gamma,
+                            const void* k_gamma, const float* cos, const float* sin, void* yq,
+                            int64_t ldyq, void* yk, int64_t ldyk, int64_t tokens, int64_t heads,
+                            int64_t kv_heads, int64_t seq_len, int64_t head_dim, float eps,
+                            int dtype, veda_stream_t stream);
 /* Backward: rotate dy by -theta (Views.cpp:136-171), then the gain and norm backward as above.
  * dgamma (fp32 [head_dim]) += sum over tokens and heads, in a fixed order. */
 int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamma, const float* cos,

@@ -175,6 +175,36 @@ def test_qknorm_rope(dtype, B, T, H, Dh, theta):
     assert rel(host(dgam), dgam_ref) <= (1e-4 if dtype == V.F32 else 1e-3)
 
 
+@pytest.mark.parametrize("dtype,B,T,H,Hk", [(V.BF16, 4, 2048, 16, 8), (V.BF16, 3, 100, 6, 2),
+                                             (V.F32, 2, 64, 4, 2)])
+def test_qknorm_rope_fwd_q_and_k_in_one_launch(dtype, B, T, H, Hk):
+    """veda_qknorm_rope_fwd_qk (the q and k heads of a layer in one launch) equals two
+    veda_qknorm_rope_fwd calls bit for bit."""
+    r = rng(3 * T + H)
+    Dh, N = 128, B * T
+    W = (H + 2 * Hk) * Dh
+    buf = r.standard_normal((N, W)).astype(F32)
+    qg = (1 + 0.1 * r.standard_normal(Dh)).astype(F32)
+    kg = (1 + 0.1 * r.standard_normal(Dh)).astype(F32)
+    if dtype == V.BF16:
+        buf, qg, kg = bf(buf), bf(qg), bf(kg)
+    cos, sin = O.rope_tables(T, Dh, 1e6)
+    es = 2 if dtype == V.BF16 else 4
+    bufd, qgd, kgd, cd, sd = dev(buf, dtype), dev(qg, dtype), dev(kg, dtype), dev(cos), dev(sin)
+    xq, xk = bufd.data_ptr(), bufd.data_ptr() + H * Dh * es
+    yq, yk = empty((N, H * Dh), dtype), empty((N, Hk * Dh), dtype)
+    call("veda_qknorm_rope_fwd_qk", xq, xk, W, ptr(qgd), ptr(kgd), ptr(cd), ptr(sd), ptr(yq), H * Dh,
+         ptr(yk), Hk * Dh, N, H, Hk, T, Dh, 1e-6, dtype, stream())
+    yq2, yk2 = empty((N, H * Dh), dtype), empty((N, Hk * Dh), dtype)
+    call("veda_qknorm_rope_fwd", xq, W, ptr(qgd), ptr(cd), ptr(sd), ptr(yq2), H * Dh, N, H, T, Dh, 1e-6,
+         dtype, stream())
+    call("veda_qknorm_rope_fwd", xk, W, ptr(kgd), ptr(cd), ptr(sd), ptr(yk2), Hk * Dh, N, Hk, T, Dh, 1e-6,
+         dtype, stream())
+    sync()
+    assert np.array_equal(host(yq), host(yq2))
+    assert np.array_equal(host(yk), host(yk2))
+
+
 @pytest.mark.parametrize("dtype,B,T,H,Hk,with_k_gain", [(V.BF16, 2, 256, 16, 8, True),
                                                         (V.BF16, 4, 2048, 16, 8, True),
                                                         (V.BF16, 3, 100, 6, 2, False),

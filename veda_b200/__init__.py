@@ -52,6 +52,8 @@ SIGNATURES = {
                                       _f, _i, _p]),
     "veda_qknorm_rope_fwd": (_i, [_p, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f,
                                   _i, _p]),
+    "veda_qknorm_rope_fwd_qk": (_i, [_p, _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64,
+                                     _i64, _i64, _i64, _f, _i, _p]),
     "veda_qknorm_rope_bwd": (_i, [_p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _p, _sz, _i64,
                                   _i64, _i64, _i64, _f, _i, _p]),
     "veda_qknorm_rope_bwd_workspace": (_sz, [_i64, _i64, _i64]),

@@ -1464,12 +1464,10 @@ void attention_forward(AttentionSaved& a, float* lse, const char* scope_name)
     const float* sp = static_cast<const float*>(a.s.data_ptr());
     a.qr = Tensor::empty(Shape({N, H * Dh}), d);
     a.kr = Tensor::empty(Shape({N, Hkv * Dh}), d);
-    check(veda_qknorm_rope_fwd(base, a.ld, a.qg.data_ptr(), cp, sp, a.qr.data_ptr(), H * Dh, N, H,
-                               a.T, Dh, a.eps, dt(d), S()),
-          "attention: q norm + rope");
-    check(veda_qknorm_rope_fwd(base + H * Dh * es, a.ld, a.kg.data_ptr(), cp, sp, a.kr.data_ptr(),
-                               Hkv * Dh, N, Hkv, a.T, Dh, a.eps, dt(d), S()),
-          "attention: k norm + rope");
+    check(veda_qknorm_rope_fwd_qk(base, base + H * Dh * es, a.ld, a.qg.data_ptr(), a.kg.data_ptr(),
+                                  cp, sp, a.qr.data_ptr(), H * Dh, a.kr.data_ptr(), Hkv * Dh, N, H, Hkv,
+                                  a.T, Dh, a.eps, dt(d), S()),
+          "attention: q and k norm + rope");
     a.out = Tensor::empty(Shape({N, H * Dh}), d);
     // causal: half of the 2 T^2 Dh products per (batch, head) for each of QK^T and PV
     profile::Scope scope(scope_name, 2.0 * a.B * H * static_cast<double>(a.T) * a.T * Dh, 0.0);

@@ -716,16 +716,35 @@ __device__ __forceinline__ void rope_row(const float* cosv, const float* sinv, i
     sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
 }
 
-__global__ void __launch_bounds__(kWarps * 32)
-qknorm_rope_fwd_d128_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ gamma,
-                            const float* __restrict__ cosv, const float* __restrict__ sinv,
-                            bf16* __restrict__ y, int64_t ldy, int64_t tokens, int heads,
-                            int seq_len, float eps)
+// One of the (up to) two sets of rows of a QK-norm forward launch: the q heads and the k heads of
+// one attention layer share a launch, each with its own blocks, gain and output (blocks = 0: no
+// second set).
+struct QkFwdSet
 {
+    const bf16* x;
+    const bf16* gamma;
+    bf16* y;
+    int64_t ldx, ldy;
+    int heads, blocks;
+};
+
+__global__ void __launch_bounds__(kWarps * 32)
+qknorm_rope_fwd_d128_kernel(const QkFwdSet s0, const QkFwdSet s1, const float* __restrict__ cosv,
+                            const float* __restrict__ sinv, int64_t tokens, int seq_len, float eps)
+{
+    // this block's set, and the block's index within it
+    const bool second = static_cast<int>(blockIdx.x) >= s0.blocks;
+    const bf16* __restrict__ x = second ? s1.x : s0.x;
+    const bf16* __restrict__ gamma = second ? s1.gamma : s0.gamma;
+    bf16* __restrict__ y = second ? s1.y : s0.y;
+    const int64_t ldx = second ? s1.ldx : s0.ldx, ldy = second ? s1.ldy : s0.ldy;
+    const int heads = second ? s1.heads : s0.heads;
+    const int nblk = second ? s1.blocks : s0.blocks;
+    const int blk = second ? static_cast<int>(blockIdx.x) - s0.blocks : static_cast<int>(blockIdx.x);
     const int lane = threadIdx.x & 31, q = lane & 7;
     const int64_t rows = tokens * heads;
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps * 4;
-    int64_t row = (static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5)) * 4 + (lane >> 3);
+    const int64_t stride = static_cast<int64_t>(nblk) * kWarps * 4;
+    int64_t row = (static_cast<int64_t>(blk) * kWarps + (threadIdx.x >> 5)) * 4 + (lane >> 3);
     const uint4 zero = make_uint4(0, 0, 0, 0);
     auto load_row = [&](int64_t r, uint4& a, uint4& b) {
         if (r < rows)
@@ -1492,10 +1511,12 @@ extern "C" int veda_qknorm_rope_fwd(const void* x, int64_t ldx, const void* gamm
     {
         const unsigned g4 = static_cast<unsigned>(std::min<int64_t>(
             (rows + 4 * kWarps - 1) / (4 * kWarps), static_cast<int64_t>(sm_count()) * 4));
-        qknorm_rope_fwd_d128_kernel<<<g4, kWarps * 32, 0, stream>>>(
-            static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(gamma), cosv, sinv,
-            static_cast<bf16*>(y), ldy, tokens, static_cast<int>(heads),
-            static_cast<int>(seq_len), eps);
+        const QkFwdSet one{static_cast<const bf16*>(x), static_cast<const bf16*>(gamma),
+                           static_cast<bf16*>(y), ldx, ldy, static_cast<int>(heads),
+                           static_cast<int>(g4)};
+        const QkFwdSet none{nullptr, nullptr, nullptr, 0, 0, 1, 0};
+        qknorm_rope_fwd_d128_kernel<<<g4, kWarps * 32, 0, stream>>>(one, none, cosv, sinv, tokens,
+                                                                   static_cast<int>(seq_len), eps);
     }
     else if (dtype == VEDA_BF16)
     {
@@ -1513,6 +1534,59 @@ extern "C" int veda_qknorm_rope_fwd(const void* x, int64_t ldx, const void* gamm
     }
     count_launch();
     return check_launch("veda_qknorm_rope_fwd");
+}
+
+extern "C" int veda_qknorm_rope_fwd_qk(const void* xq, const void* xk, int64_t ldx,
+                                       const void* q_gamma, const void* k_gamma, const float* cosv,
+                                       const float* sinv, void* yq, int64_t ldyq, void* yk,
+                                       int64_t ldyk, int64_t tokens, int64_t heads,
+                                       int64_t kv_heads, int64_t seq_len, int64_t head_dim,
+                                       float eps, int dtype, veda_stream_t stream)
+{
+    int rc = qk_checks(xq, ldx, q_gamma, cosv, sinv, tokens, heads, seq_len, head_dim, dtype);
+    if (rc == VEDA_OK)
+    {
+        rc = qk_checks(xk, ldx, k_gamma, cosv, sinv, tokens, kv_heads, seq_len, head_dim, dtype);
+    }
+    if (rc != VEDA_OK)
+    {
+        return rc;
+    }
+    VEDA_REQUIRE(yq != nullptr && yk != nullptr && ldyq >= heads * head_dim &&
+                     ldyk >= kv_heads * head_dim && ldyq % 2 == 0 && ldyk % 2 == 0,
+                 "bad output");
+    if (tokens == 0)
+    {
+        return VEDA_OK;
+    }
+    const bool one_launch = d128_ok(xq, ldx, q_gamma, cosv, sinv, yq, ldyq, head_dim, dtype) &&
+                            d128_ok(xk, ldx, k_gamma, cosv, sinv, yk, ldyk, head_dim, dtype) &&
+                            tokens * std::max(heads, kv_heads) < (1ll << 31);
+    if (!one_launch)
+    {
+        rc = veda_qknorm_rope_fwd(xq, ldx, q_gamma, cosv, sinv, yq, ldyq, tokens, heads, seq_len,
+                                  head_dim, eps, dtype, stream);
+        if (rc != VEDA_OK)
+        {
+            return rc;
+        }
+        return veda_qknorm_rope_fwd(xk, ldx, k_gamma, cosv, sinv, yk, ldyk, tokens, kv_heads,
+                                    seq_len, head_dim, eps, dtype, stream);
+    }
+    // blocks in proportion to the rows (both sets finish together), at most four per SM in all
+    const int64_t per = 4 * kWarps, total = static_cast<int64_t>(sm_count()) * 4;
+    int64_t bq = total * heads / (heads + kv_heads);
+    bq = std::max<int64_t>(1, std::min<int64_t>(bq, (tokens * heads + per - 1) / per));
+    const int64_t bk =
+        std::max<int64_t>(1, std::min<int64_t>(total - bq, (tokens * kv_heads + per - 1) / per));
+    const QkFwdSet sq{static_cast<const bf16*>(xq), static_cast<const bf16*>(q_gamma),
+                      static_cast<bf16*>(yq), ldx, ldyq, static_cast<int>(heads), static_cast<int>(bq)};
+    const QkFwdSet sk{static_cast<const bf16*>(xk), static_cast<const bf16*>(k_gamma),
+                      static_cast<bf16*>(yk), ldx, ldyk, static_cast<int>(kv_heads), static_cast<int>(bk)};
+    qknorm_rope_fwd_d128_kernel<<<static_cast<unsigned>(bq + bk), kWarps * 32, 0, stream>>>(
+        sq, sk, cosv, sinv, tokens, static_cast<int>(seq_len), eps);
+    count_launch();
+    return check_launch("veda_qknorm_rope_fwd_qk");
 }
 
 extern "C" int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamma,
