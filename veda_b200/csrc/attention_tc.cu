@@ -4,7 +4,14 @@
 // src/libs/train/Model.cpp:182-189 with kv head h / (H/Hkv), src/libs/model/Attention.cpp:191);
 // this file is the bf16, head_dim-128 tensor-core form the entry points dispatch to.
 //
-// Forward — one CTA per (batch, head, pair of 128-query tiles A and B); 10 warps:
+// Forward — persistent, one CTA per SM; a work item is one (batch, head, pair of 128-query tiles
+// A and B), pairs with the longest causal rows first, handed out in rounds of one item per CTA
+// whose direction over the CTAs alternates (round r gives CTA c item r G + c for even r and
+// r G + G - 1 - c for odd r, G CTAs), so the long items of one round and the shorter ones of the
+// next even out per CTA. Against one CTA per item this took B4 T2048 from 0.099 to 0.094 ms and
+// B8 T2048 from 0.178 to 0.170 ms (plain round robin, r G + c for every r, was slower than one
+// CTA per item: 0.108 ms). The rings and barrier phases run on across a CTA's items, and the next
+// item's Q tiles load once the last S products of the current one have read them. 10 warps:
 //   warp 0     TMA (lane 0: both Q tiles, then 128-key K tiles; lane 1: the V tiles), each into
 //              its own 2-stage ring shared by the two query tiles (3-D tensor maps [B, T, columns],
 //              so rows past T read as zeros; no multicast);
@@ -49,7 +56,7 @@ struct FwdParams
     bf16* o;
     float* lse;
     int64_t ldo;
-    int T, H, Hkv;
+    int B, T, H, Hkv;
     float scale_log2;
     int causal;
     int* status;
@@ -134,6 +141,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     uint64_t* s_full = bars + 9;     // [2] per query tile
     uint64_t* p_full = bars + 11;    // [2] per query tile
     uint64_t* o_done = bars + 13;    // [2] per query tile
+    uint64_t* q_empty = bars + 15;   // the item's last S products have read its Q tiles
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -141,19 +149,42 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     const int nq = (p.T + kTq - 1) / kTq;
     const int nkt = (p.T + kTk - 1) / kTk;
     const int npairs = (nq + 1) / 2;
-    const int qt0 = 2 * (npairs - 1 - static_cast<int>(blockIdx.y));   // longest rows first
-    const bool has_b = qt0 + 1 < nq;
-    const int bh = blockIdx.x;
-    const int b = bh / p.H, h = bh % p.H;
-    const int kvh = h / (p.H / p.Hkv);
-    const int n_a = p.causal ? qt0 + 1 : nkt;
-    const int n_b = has_b ? (p.causal ? qt0 + 2 : nkt) : 0;
-    const int nmax = n_a > n_b ? n_a : n_b;
+    const int bh_count = p.B * p.H;
+    const int items = bh_count * npairs;
+    // Work item w: (batch, head) w % (B H) and the pair of query tiles of index w / (B H), pairs
+    // with the longest rows first; this CTA takes one item a round, in snake order (item_at)
+    struct Item
+    {
+        int b, h, kvh, qt0, n_a, n_b, nmax;
+        bool has_b;
+    };
+    // round rr of the CTA's items: rounds alternate direction over the CTAs (a snake), so the
+    // long items of one round and the short ones of the next even out per CTA
+    auto item_at = [&](int rr) {
+        const int c = (rr & 1) ? static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x)
+                               : static_cast<int>(blockIdx.x);
+        const int w = rr * static_cast<int>(gridDim.x) + c;
+        return w < items ? w : -1;
+    };
+    auto item = [&](int w) {
+        Item it;
+        const int y = w / bh_count, bh = w - y * bh_count;
+        it.qt0 = 2 * (npairs - 1 - y);
+        it.has_b = it.qt0 + 1 < nq;
+        it.b = bh / p.H;
+        it.h = bh - it.b * p.H;
+        it.kvh = it.h / (p.H / p.Hkv);
+        it.n_a = p.causal ? it.qt0 + 1 : nkt;
+        it.n_b = it.has_b ? (p.causal ? it.qt0 + 2 : nkt) : 0;
+        it.nmax = it.n_a > it.n_b ? it.n_a : it.n_b;
+        return it;
+    };
 
     if (threadIdx.x == 0)
     {
         *abort = 0;
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
         for (int i = 0; i < 2; ++i)
         {
             mbar_init(&k_full[i], 1);
@@ -175,34 +206,51 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     fence_after();
     const uint32_t tmem = *tmem_slot;
     // TMEM columns: S_A | S_B | O_A | O_B (128 each); P_x (bf16 pairs) overwrites S_x's first 64
+    // Every ring and barrier phase runs on across the CTA's items (counters kept per role).
 
     if (warp == 0 && lane == 0)
     {
         tma_prefetch(&tq);
         tma_prefetch(&tk);
-        mbar_expect_tx(q_full, (has_b ? 2 : 1) * kTileBytes);
-        load_tile_3d(sq, &tq, q_full, h * 128, qt0 * kTq, b);
-        if (has_b)
+        int kc = 0, n_item = 0;
+        for (int rr = 0, w = item_at(0); w >= 0; w = item_at(++rr), ++n_item)
         {
-            load_tile_3d(sq + kTileBytes, &tq, q_full, h * 128, (qt0 + 1) * kTq, b);
-        }
-        for (int j = 0; j < nmax; ++j)
-        {
-            const int st = j & 1;
-            mbar_wait(&k_empty[st], ((j >> 1) & 1) ^ 1, p.status, abort);
-            mbar_expect_tx(&k_full[st], kTileBytes);
-            load_tile_3d(sk + st * kTileBytes, &tk, &k_full[st], kvh * 128, j * kTk, b);
+            const Item it = item(w);
+            // the Q tiles of this item replace the last item's once its final S products (issued
+            // one key tile before its end) have completed
+            if (n_item > 0)
+            {
+                mbar_wait(q_empty, (n_item - 1) & 1, p.status, abort);
+            }
+            mbar_expect_tx(q_full, (it.has_b ? 2 : 1) * kTileBytes);
+            load_tile_3d(sq, &tq, q_full, it.h * 128, it.qt0 * kTq, it.b);
+            if (it.has_b)
+            {
+                load_tile_3d(sq + kTileBytes, &tq, q_full, it.h * 128, (it.qt0 + 1) * kTq, it.b);
+            }
+            for (int j = 0; j < it.nmax; ++j, ++kc)
+            {
+                const int st = kc & 1;
+                mbar_wait(&k_empty[st], ((kc >> 1) & 1) ^ 1, p.status, abort);
+                mbar_expect_tx(&k_full[st], kTileBytes);
+                load_tile_3d(sk + st * kTileBytes, &tk, &k_full[st], it.kvh * 128, j * kTk, it.b);
+            }
         }
     }
     else if (warp == 0 && lane == 1)
     {
         tma_prefetch(&tv);
-        for (int j = 0; j < nmax; ++j)
+        int vc = 0;
+        for (int rr = 0, w = item_at(0); w >= 0; w = item_at(++rr))
         {
-            const int st = j & 1;
-            mbar_wait(&v_empty[st], ((j >> 1) & 1) ^ 1, p.status, abort);
-            mbar_expect_tx(&v_full[st], kTileBytes);
-            load_tile_3d(sv + st * kTileBytes, &tv, &v_full[st], kvh * 128, j * kTk, b);
+            const Item it = item(w);
+            for (int j = 0; j < it.nmax; ++j, ++vc)
+            {
+                const int st = vc & 1;
+                mbar_wait(&v_empty[st], ((vc >> 1) & 1) ^ 1, p.status, abort);
+                mbar_expect_tx(&v_full[st], kTileBytes);
+                load_tile_3d(sv + st * kTileBytes, &tv, &v_full[st], it.kvh * 128, j * kTk, it.b);
+            }
         }
     }
     else if (warp == 1 && lane == 0)
@@ -210,12 +258,16 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
         // Order per key tile j: P_A V_j, S_A(j+1), P_B V_j, S_B(j+1) — so the tensor core works
         // on one query tile while the softmax warps of the other compute its probabilities.
         // An S_x(j+1) issued after P_x V_j overwrites P_x only once that product has read it
-        // (the MMAs of one thread execute in issue order).
+        // (the MMAs of one thread execute in issue order); the same holds for the next item's
+        // S_x(0). The next item's first P_x V_0 overwrites O_x only after p_full, which the
+        // softmax warps of tile x arrive on after they have read O_x out for the last item.
         constexpr uint32_t idesc_s = instr_desc(128, 128, false, false);
         constexpr uint32_t idesc_o = instr_desc(128, 128, false, true);
         const uint32_t q_base = smem_u32(sq);
-        auto issue_s = [&](int x, int j) {
-            const uint32_t k_base = smem_u32(sk + (j & 1) * kTileBytes);
+        int kc = 0, vc = 0, n_item = 0;
+        int pc[2] = {0, 0};   // P tiles consumed per query tile
+        auto issue_s = [&](int x, int kslot) {
+            const uint32_t k_base = smem_u32(sk + kslot * kTileBytes);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks)
             {
@@ -224,10 +276,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
             }
             commit(&s_full[x]);
         };
-        auto issue_pv = [&](int x, int j, int n) {
-            mbar_wait(&p_full[x], j & 1, p.status, abort);
+        auto issue_pv = [&](int x, int j, int n, int vslot) {
+            mbar_wait(&p_full[x], pc[x] & 1, p.status, abort);
+            ++pc[x];
             fence_after();
-            const uint32_t v_base = smem_u32(sv + (j & 1) * kTileBytes);
+            const uint32_t v_base = smem_u32(sv + vslot * kTileBytes);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks)
             {
@@ -239,178 +292,200 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
                 commit(&o_done[x]);
             }
         };
-        mbar_wait(q_full, 0, p.status, abort);
-        mbar_wait(&k_full[0], 0, p.status, abort);
-        fence_after();
-        issue_s(0, 0);
-        if (n_b > 0)
+        for (int rr = 0, w = item_at(0); w >= 0; w = item_at(++rr), ++n_item)
         {
-            issue_s(1, 0);
-        }
-        commit(&k_empty[0]);
-        for (int j = 0; j < nmax; ++j)
-        {
-            const int st = j & 1, jn = j + 1;
-            mbar_wait(&v_full[st], (j >> 1) & 1, p.status, abort);
+            const Item it = item(w);
+            mbar_wait(q_full, n_item & 1, p.status, abort);
+            mbar_wait(&k_full[kc & 1], (kc >> 1) & 1, p.status, abort);
             fence_after();
-            if (j < n_a)
+            issue_s(0, kc & 1);
+            if (it.n_b > 0)
             {
-                issue_pv(0, j, n_a);
+                issue_s(1, kc & 1);
             }
-            if (jn < nmax)
+            commit(&k_empty[kc & 1]);
+            ++kc;
+            if (it.nmax == 1)
             {
-                mbar_wait(&k_full[jn & 1], (jn >> 1) & 1, p.status, abort);
+                commit(q_empty);   // every S product of the item has been issued
+            }
+            for (int j = 0; j < it.nmax; ++j, ++vc)
+            {
+                const int st = vc & 1, jn = j + 1;
+                mbar_wait(&v_full[st], (vc >> 1) & 1, p.status, abort);
                 fence_after();
-                if (jn < n_a)
+                if (j < it.n_a)
                 {
-                    issue_s(0, jn);
+                    issue_pv(0, j, it.n_a, st);
                 }
-            }
-            if (j < n_b)
-            {
-                issue_pv(1, j, n_b);
-            }
-            commit(&v_empty[st]);
-            if (jn < nmax)
-            {
-                if (jn < n_b)
+                if (jn < it.nmax)
                 {
-                    issue_s(1, jn);
+                    mbar_wait(&k_full[kc & 1], (kc >> 1) & 1, p.status, abort);
+                    fence_after();
+                    if (jn < it.n_a)
+                    {
+                        issue_s(0, kc & 1);
+                    }
                 }
-                commit(&k_empty[jn & 1]);
+                if (j < it.n_b)
+                {
+                    issue_pv(1, j, it.n_b, st);
+                }
+                commit(&v_empty[st]);
+                if (jn < it.nmax)
+                {
+                    if (jn < it.n_b)
+                    {
+                        issue_s(1, kc & 1);
+                    }
+                    commit(&k_empty[kc & 1]);
+                    ++kc;
+                    if (jn + 1 == it.nmax)
+                    {
+                        commit(q_empty);   // the item's last S products have been issued
+                    }
+                }
             }
         }
     }
     else if (warp >= 2)
     {
         const int x = warp >= 6 ? 1 : 0;                  // query tile of this warpgroup
-        const int n = x ? n_b : n_a;
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;                // row within the tile (TMEM lane)
-        const int qtile = qt0 + x;
-        const int query = qtile * kTq + r;
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
         const uint32_t s_addr = tmem + lane_base + x * 128;
         const uint32_t o_addr = tmem + lane_base + 256 + x * 128;
         const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
-        float m = -INFINITY, l = 0.0f;   // running max (scaled, log2 units) and row sum
-        for (int j = 0; j < n; ++j)
+        int sc = 0, oc = 0;                               // S tiles and items taken by this tile
+        for (int rr = 0, w = item_at(0); w >= 0; w = item_at(++rr))
         {
-            mbar_wait(&s_full[x], j & 1, p.status, abort);
-            fence_after();
-            uint32_t s[4][32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_ld32_async(s_addr + c * 32, s[c]);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) reg_fence(s[c]);
-            const int key0 = j * kTk;
-            if ((p.causal && j == qtile) || key0 + kTk > p.T)
+            const Item it = item(w);
+            const int n = x ? it.n_b : it.n_a;
+            const int b = it.b, h = it.h;
+            const int qtile = it.qt0 + x;
+            const int query = qtile * kTq + r;
+            float m = -INFINITY, l = 0.0f;   // running max (scaled, log2 units) and row sum
+            for (int j = 0; j < n; ++j)
             {
-                int limit = p.T - key0 - 1;               // last visible column of this row
-                if (p.causal && j == qtile && r < limit) limit = r;
+                mbar_wait(&s_full[x], sc & 1, p.status, abort);
+                ++sc;
+                fence_after();
+                uint32_t s[4][32];
 #pragma unroll
-                for (int e = 0; e < 128; ++e)
+                for (int c = 0; c < 4; ++c) tmem_ld32_async(s_addr + c * 32, s[c]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 4; ++c) reg_fence(s[c]);
+                const int key0 = j * kTk;
+                if ((p.causal && j == qtile) || key0 + kTk > p.T)
                 {
-                    if (e > limit) s[e >> 5][e & 31] = 0xFF800000u;   // -inf
+                    int limit = p.T - key0 - 1;               // last visible column of this row
+                    if (p.causal && j == qtile && r < limit) limit = r;
+#pragma unroll
+                    for (int e = 0; e < 128; ++e)
+                    {
+                        if (e > limit) s[e >> 5][e & 31] = 0xFF800000u;   // -inf
+                    }
                 }
-            }
-            float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+                float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-            for (int e = 0; e < 128; e += 8)
-            {
-                const uint32_t* v = &s[e >> 5][e & 31];
-                m0 = max3(m0, __uint_as_float(v[0]), __uint_as_float(v[1]));
-                m1 = max3(m1, __uint_as_float(v[2]), __uint_as_float(v[3]));
-                m2 = max3(m2, __uint_as_float(v[4]), __uint_as_float(v[5]));
-                m3 = max3(m3, __uint_as_float(v[6]), __uint_as_float(v[7]));
-            }
-            const float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * p.scale_log2;
-            const bool first = m == -INFINITY;
-            const bool grow = mx > m + kRescaleThreshold;
-            // O_x is rescaled after P is written (fewer live registers); corr = 1 for rows whose
-            // max is kept
-            const bool rescale = __any_sync(0xFFFFFFFFu, grow && !first);
-            const float corr = (grow && !first) ? ex2(m - mx) : 1.0f;
-            if (grow || first)
-            {
-                m = mx;
-            }
-            const float mu = m == -INFINITY ? 0.0f : m;
-            const uint64_t neg = f2_pack(-mu, -mu);
-            uint64_t acc0 = 0, acc1 = 0;   // two packed partial sums (+0.0f pairs)
-#pragma unroll
-            for (int g = 0; g < 4; ++g)
-            {
-                uint32_t pk[16];   // 32 probabilities as bf16 pairs, stored as soon as computed
-#pragma unroll
-                for (int c = 0; c < 16; ++c)
+                for (int e = 0; e < 128; e += 8)
                 {
-                    const uint32_t* v = &s[g][c * 2];
-                    float a, bb;
-                    f2_unpack(f2_fma(f2_pack(__uint_as_float(v[0]), __uint_as_float(v[1])), sc2, neg), a, bb);
-                    a = ex2(a);
-                    bb = ex2(bb);
-                    if (c & 1)
-                        acc1 = f2_add(acc1, f2_pack(a, bb));
-                    else
-                        acc0 = f2_add(acc0, f2_pack(a, bb));
-                    const __nv_bfloat162 t = __floats2bfloat162_rn(a, bb);
-                    pk[c] = *reinterpret_cast<const uint32_t*>(&t);
+                    const uint32_t* v = &s[e >> 5][e & 31];
+                    m0 = max3(m0, __uint_as_float(v[0]), __uint_as_float(v[1]));
+                    m1 = max3(m1, __uint_as_float(v[2]), __uint_as_float(v[3]));
+                    m2 = max3(m2, __uint_as_float(v[4]), __uint_as_float(v[5]));
+                    m3 = max3(m3, __uint_as_float(v[6]), __uint_as_float(v[7]));
                 }
-                tmem_st16_async(s_addr + g * 16, pk);
+                const float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * p.scale_log2;
+                const bool first = m == -INFINITY;
+                const bool grow = mx > m + kRescaleThreshold;
+                // O_x is rescaled after P is written (fewer live registers); corr = 1 for rows whose
+                // max is kept
+                const bool rescale = __any_sync(0xFFFFFFFFu, grow && !first);
+                const float corr = (grow && !first) ? ex2(m - mx) : 1.0f;
+                if (grow || first)
+                {
+                    m = mx;
+                }
+                const float mu = m == -INFINITY ? 0.0f : m;
+                const uint64_t neg = f2_pack(-mu, -mu);
+                uint64_t acc0 = 0, acc1 = 0;   // two packed partial sums (+0.0f pairs)
+#pragma unroll
+                for (int g = 0; g < 4; ++g)
+                {
+                    uint32_t pk[16];   // 32 probabilities as bf16 pairs, stored as soon as computed
+#pragma unroll
+                    for (int c = 0; c < 16; ++c)
+                    {
+                        const uint32_t* v = &s[g][c * 2];
+                        float a, bb;
+                        f2_unpack(f2_fma(f2_pack(__uint_as_float(v[0]), __uint_as_float(v[1])), sc2, neg), a, bb);
+                        a = ex2(a);
+                        bb = ex2(bb);
+                        if (c & 1)
+                            acc1 = f2_add(acc1, f2_pack(a, bb));
+                        else
+                            acc0 = f2_add(acc0, f2_pack(a, bb));
+                        const __nv_bfloat162 t = __floats2bfloat162_rn(a, bb);
+                        pk[c] = *reinterpret_cast<const uint32_t*>(&t);
+                    }
+                    tmem_st16_async(s_addr + g * 16, pk);
+                }
+                float a0, a1, b0, b1;
+                f2_unpack(acc0, a0, a1);
+                f2_unpack(acc1, b0, b1);
+                if (rescale)
+                {
+                    // the products of tiles < j have completed (S_x(j), issued after them, has), and
+                    // P_x V_j is not issued before this warp arrives on p_full
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c)
+                    {
+                        uint32_t raw[32];
+                        tmem_ld32(o_addr + c * 32, raw);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * corr);
+                        tmem_st32(o_addr + c * 32, raw);
+                    }
+                }
+                l = l * corr + ((a0 + a1) + (b0 + b1));
+                tmem_wait_st();
+                fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[x]);
             }
-            float a0, a1, b0, b1;
-            f2_unpack(acc0, a0, a1);
-            f2_unpack(acc1, b0, b1);
-            if (rescale)
+            if (n > 0)
             {
-                // the products of tiles < j have completed (S_x(j), issued after them, has), and
-                // P_x V_j is not issued before this warp arrives on p_full
+                // epilogue: O / l and the log-sum-exp
+                mbar_wait(&o_done[x], oc & 1, p.status, abort);
+                ++oc;
+                fence_after();
+                const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+                const bool valid = query < p.T;
+                bf16* orow = p.o + (static_cast<int64_t>(b) * p.T + query) * p.ldo + static_cast<int64_t>(h) * 128;
 #pragma unroll 1
                 for (int c = 0; c < 4; ++c)
                 {
                     uint32_t raw[32];
                     tmem_ld32(o_addr + c * 32, raw);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * corr);
-                    tmem_st32(o_addr + c * 32, raw);
-                }
-            }
-            l = l * corr + ((a0 + a1) + (b0 + b1));
-            tmem_wait_st();
-            fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[x]);
-        }
-        if (n > 0)
-        {
-            // epilogue: O / l and the log-sum-exp
-            mbar_wait(&o_done[x], 0, p.status, abort);
-            fence_after();
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            const bool valid = query < p.T;
-            bf16* orow = p.o + (static_cast<int64_t>(b) * p.T + query) * p.ldo + static_cast<int64_t>(h) * 128;
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c)
-            {
-                uint32_t raw[32];
-                tmem_ld32(o_addr + c * 32, raw);
-                if (valid)
-                {
-#pragma unroll
-                    for (int e = 0; e < 32; e += 8)
+                    if (valid)
                     {
-                        float v8[8];
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) v8[q] = __uint_as_float(raw[e + q]) * inv;
-                        store16(orow + c * 32 + e, v8);
+                        for (int e = 0; e < 32; e += 8)
+                        {
+                            float v8[8];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) v8[q] = __uint_as_float(raw[e + q]) * inv;
+                            store16(orow + c * 32 + e, v8);
+                        }
                     }
                 }
-            }
-            if (valid)
-            {
-                p.lse[(static_cast<int64_t>(b) * p.H + h) * p.T + query] = (m + log2f(l)) * kLn2;
+                if (valid)
+                {
+                    p.lse[(static_cast<int64_t>(b) * p.H + h) * p.T + query] = (m + log2f(l)) * kLn2;
+                }
             }
         }
     }
@@ -1683,10 +1758,12 @@ int attn_tc_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
         cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
         configured = device;
     }
-    FwdParams p{static_cast<bf16*>(o), lse, ldo, static_cast<int>(T), static_cast<int>(H),
-                static_cast<int>(Hkv), scale * kLog2e, causal, device_status_ptr()};
+    FwdParams p{static_cast<bf16*>(o), lse, ldo, static_cast<int>(B), static_cast<int>(T),
+                static_cast<int>(H), static_cast<int>(Hkv), scale * kLog2e, causal, device_status_ptr()};
+    // persistent: one CTA per SM working through the (batch, head, query-tile pair) items
     const int64_t pairs = ((T + kTq - 1) / kTq + 1) / 2;
-    const dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>(pairs));
+    const int64_t items = B * H * pairs;
+    const unsigned grid = static_cast<unsigned>(items < compute_sms() ? items : compute_sms());
     attn_fwd_tc_kernel<<<grid, kFwdThreads, kFwdSmem, s>>>(mq, mk, mv, p);
     count_launch();
     return check_launch("veda_attention_fwd (tcgen05)");
