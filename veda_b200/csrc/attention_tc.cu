@@ -205,6 +205,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    dep_wait();   // Q, K, V (and O, LSE) belong to the kernels before this one
+    dep_release();
     // TMEM columns: S_A | S_B | O_A | O_B (128 each); P_x (bf16 pairs) overwrites S_x's first 64
     // Every ring and barrier phase runs on across the CTA's items (counters kept per role).
 
@@ -1080,6 +1082,8 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    dep_wait();   // D, -LSE log2 e and the zeroed dQ accumulator come from attn_rowdot_kernel
+    dep_release();
     constexpr uint32_t kS = 0, kDP = 128, kDV = 256, kDK = 384;
 
     if (warp == kTmaWarp)
@@ -1419,6 +1423,8 @@ attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
 __global__ void attn_dq_cast_kernel(const float* __restrict__ acc, bf16* __restrict__ dq,
                                     int64_t lddq, int64_t rows, int64_t width, float scale)
 {
+    dep_wait();
+    dep_release();
     const int64_t per_row = width >> 3;
     const int64_t n = rows * per_row;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
@@ -1620,6 +1626,8 @@ attn_rowdot_kernel(const bf16* __restrict__ o, int64_t ldo, const bf16* __restri
                    int64_t lddo, const float* __restrict__ lse, float* __restrict__ dvec,
                    float* __restrict__ nlse2, float* __restrict__ dqacc, int T, int H)
 {
+    dep_wait();
+    dep_release();
     const int sub = threadIdx.x & 15, grp = threadIdx.x >> 4;
     const unsigned half = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
     const int bh = static_cast<int>(blockIdx.x);   // b * H + h
@@ -1764,9 +1772,8 @@ int attn_tc_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     const int64_t pairs = ((T + kTq - 1) / kTq + 1) / 2;
     const int64_t items = B * H * pairs;
     const unsigned grid = static_cast<unsigned>(items < compute_sms() ? items : compute_sms());
-    attn_fwd_tc_kernel<<<grid, kFwdThreads, kFwdSmem, s>>>(mq, mk, mv, p);
-    count_launch();
-    return check_launch("veda_attention_fwd (tcgen05)");
+    return launch("veda_attention_fwd (tcgen05)", attn_fwd_tc_kernel, dim3(grid), dim3(kFwdThreads),
+                  kFwdSmem, s, mq, mk, mv, p);
 }
 
 // Workspace of the tcgen05 backward after D: the fused path's fp32 dQ accumulator
@@ -1833,9 +1840,13 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
         {
             return -1;
         }
-        attn_rowdot_kernel<<<rowdot_grid(B, T, H), 256, 0, s>>>(
-            static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, lse, dvec, nlse2,
-            dqacc, static_cast<int>(T), static_cast<int>(H));
+        int rc = launch("veda_attention_bwd (D)", attn_rowdot_kernel, rowdot_grid(B, T, H), dim3(256), 0,
+                        s, static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo,
+                        lse, dvec, nlse2, dqacc, static_cast<int>(T), static_cast<int>(H));
+        if (rc != VEDA_OK)
+        {
+            return rc;
+        }
         // pairs per chunk: as many as keep a chunk's Q, dO (2 x 256 B) and dQ accumulator rows
         // (512 B) per query and head within ~48 MB of L2, a power of two from 8 (fewer leaves a
         // long tail of key-tile-0 CTAs) up to all pairs
@@ -1846,22 +1857,26 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
                       static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
                       scale * kLog2e, causal, device_status_ptr(),
                       static_cast<int>(std::min<int64_t>(chunk, B * Hkv))};
-        attn_bwd_fused_kernel<<<grid, kFusedThreads, kFusedSmem, s>>>(mq, mk, mv, mdo, mdq, p);
-        if (dq == nullptr)
+        rc = launch("veda_attention_bwd (tcgen05, fused)", attn_bwd_fused_kernel, grid,
+                    dim3(kFusedThreads), kFusedSmem, s, mq, mk, mv, mdo, mdq, p);
+        if (rc != VEDA_OK || dq == nullptr)
         {
-            // the caller reads dQ / scale from the fp32 accumulator itself
-            count_launch(2);
-            return check_launch("veda_attention_bwd (tcgen05, fused, dQ left in fp32)");
+            return rc;   // dq == nullptr: the caller reads dQ / scale from the fp32 accumulator
         }
-        attn_dq_cast_kernel<<<grid_for(B * T * H * 16, 256), 256, 0, s>>>(
-            dqacc, static_cast<bf16*>(dq), lddq, B * T, H * 128, scale);
-        count_launch(3);
-        return check_launch("veda_attention_bwd (tcgen05, fused)");
+        return launch("veda_attention_bwd (dQ cast)", attn_dq_cast_kernel,
+                      dim3(grid_for(B * T * H * 16, 256)), dim3(256), 0, s,
+                      static_cast<const float*>(dqacc), static_cast<bf16*>(dq), lddq, B * T, H * 128,
+                      scale);
     }
     bf16* ds = static_cast<bf16*>(extra);
-    attn_rowdot_kernel<<<rowdot_grid(B, T, H), 256, 0, s>>>(
-        static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, lse, dvec, nlse2,
-        nullptr, static_cast<int>(T), static_cast<int>(H));
+    const int rc = launch("veda_attention_bwd (D)", attn_rowdot_kernel, rowdot_grid(B, T, H), dim3(256),
+                          0, s, static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo,
+                          lse, dvec, nlse2, static_cast<float*>(nullptr), static_cast<int>(T),
+                          static_cast<int>(H));
+    if (rc != VEDA_OK)
+    {
+        return rc;
+    }
     BwdParams p{nlse2, dvec, static_cast<bf16*>(dk), static_cast<bf16*>(dv), ds, lddk, lddv,
                 static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hkv), scale,
                 scale * kLog2e, causal, device_status_ptr()};
@@ -1871,7 +1886,7 @@ int attn_tc_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const vo
     const int64_t dq_items = B * H * ((T + 127) / 128);
     const unsigned gq = static_cast<unsigned>(dq_items < compute_sms() ? dq_items : compute_sms());
     attn_dq_tc_kernel<<<gq, 192, kDqSmem, s>>>(mds, mk, pq);
-    count_launch(3);
+    count_launch(2);
     return check_launch("veda_attention_bwd (tcgen05)");
 }
 

@@ -8,6 +8,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "veda_cuda.h"
 
@@ -40,6 +41,46 @@ const char* last_error_cstr();
 inline bool valid_dtype(int d) { return d == VEDA_F32 || d == VEDA_BF16; }
 inline size_t dtype_size(int d) { return d == VEDA_BF16 ? 2 : 4; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- overlapped (programmatic dependent) launches -------------------------------------------
+// A kernel started by launch() may begin while the kernel before it on the stream is still
+// running, so that its launch and its set-up (shared memory, mbarriers, TMEM allocation) hide
+// under the tail of its predecessor. Such a kernel must touch no global memory before
+// dep_wait(), which returns once the predecessor has completed and its writes are visible; after
+// it, dep_release() lets the kernel's own successor start early. A kernel launched without the
+// attribute (or one whose predecessor never releases) sees both as no-ops. VEDA_PDL=0 launches
+// without the attribute.
+__device__ __forceinline__ void dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void dep_release()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+bool overlapped_launches();
+
+template <typename... Params, typename... Args>
+int launch(const char* what, void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+           cudaStream_t s, Args&&... args)
+{
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = overlapped_launches() ? 1 : 0;
+    count_launch();
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (err != cudaSuccess)
+    {
+        cudaGetLastError();
+        return fail(VEDA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+    }
+    return check_launch(what);
+}
 
 inline unsigned grid_for(int64_t work, int threads, int per_sm = 8)
 {

@@ -135,6 +135,8 @@ ce_kernel(const T* __restrict__ logits, int64_t ldl, const int64_t* __restrict__
     __shared__ float red_m[kThreads / 32];
     __shared__ float red_s[kThreads / 32];
     __shared__ float final_m, final_log2;
+    dep_wait();
+    dep_release();
     const uint64_t keep = l2_policy_keep(), drop = l2_policy_drop();
     // a power-of-two grad_scale (1 / lanes for a power-of-two lane count) folds into the exponent
     // exactly: grad_scale 2^a = 2^(a + log2 grad_scale)
@@ -284,6 +286,8 @@ __global__ void mean_f64_kernel(const float* __restrict__ v, int64_t n, float* o
                                 double* out_f64)
 {
     __shared__ double part[1024 / 32];
+    dep_wait();
+    dep_release();
     double s = 0.0;
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
     {
@@ -339,20 +343,15 @@ extern "C" int veda_cross_entropy(const void* logits, int64_t ldl, const int64_t
     const unsigned grid = static_cast<unsigned>(
         rows < static_cast<int64_t>(sm_count()) * 2 ? rows : static_cast<int64_t>(sm_count()) * 2);
 #define VEDA_CE(T, VEC)                                                                           \
-    ce_kernel<T, VEC><<<grid, kThreads, 0, stream>>>(static_cast<const T*>(logits), ldl, targets, \
-                                                     row_loss, static_cast<T*>(dlogits), ldd,    \
-                                                     rows, vocab, grad_scale, status)
+    launch("veda_cross_entropy", ce_kernel<T, VEC>, dim3(grid), dim3(kThreads), 0, stream,         \
+           static_cast<const T*>(logits), ldl, targets, row_loss, static_cast<T*>(dlogits), ldd,  \
+           rows, vocab, grad_scale, status)
     if (dtype == VEDA_BF16)
     {
-        if (vec) VEDA_CE(bf16, true); else VEDA_CE(bf16, false);
+        return vec ? VEDA_CE(bf16, true) : VEDA_CE(bf16, false);
     }
-    else
-    {
-        if (vec) VEDA_CE(float, true); else VEDA_CE(float, false);
-    }
+    return vec ? VEDA_CE(float, true) : VEDA_CE(float, false);
 #undef VEDA_CE
-    count_launch();
-    return check_launch("veda_cross_entropy");
 }
 
 extern "C" int veda_mean_f64(const float* v, int64_t n, float* out, double* out_f64,
@@ -360,7 +359,5 @@ extern "C" int veda_mean_f64(const float* v, int64_t n, float* out, double* out_
 {
     VEDA_REQUIRE(n > 0, "nothing to average over");
     VEDA_REQUIRE(v != nullptr, "null pointer");
-    mean_f64_kernel<<<1, 1024, 0, stream>>>(v, n, out, out_f64);
-    count_launch();
-    return check_launch("veda_mean_f64");
+    return launch("veda_mean_f64", mean_f64_kernel, dim3(1), dim3(1024), 0, stream, v, n, out, out_f64);
 }

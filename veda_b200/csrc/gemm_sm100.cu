@@ -346,6 +346,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    dep_wait();   // A, B and C belong to the kernels before this one
+    dep_release();
 
     const int units = p.num_m * p.num_n * p.splits;
 
@@ -620,6 +622,8 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
     cluster_sync();   // both CTAs' barriers are initialised before any cross-CTA signal
     fence_after();
     const uint32_t tmem = *tmem_slot;
+    dep_wait();   // A, B and C belong to the kernels before this one
+    dep_release();
 
     const int units = p.num_m * p.num_n * p.splits;
 
@@ -829,9 +833,8 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& m
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
         configured_device = device;
     }
-    kernel<<<grid, kThreads, Cfg<BN>::SMEM, s>>>(ma, mb, mc, p);
-    count_launch();
-    return check_launch("veda_gemm (tcgen05)");
+    return launch("veda_gemm (tcgen05)", kernel, dim3(grid), dim3(kThreads), Cfg<BN>::SMEM, s, ma, mb,
+                  mc, p);
 }
 
 // Launches the paired-CTA kernel on `clusters` clusters of two; -1 if clusters cannot be
@@ -841,9 +844,8 @@ int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
                int clusters, cudaStream_t s)
 {
     auto kernel = tc_gemm2_kernel<A_MN, B_MN>;
-    kernel<<<2 * clusters, kThreads, Cfg2::SMEM, s>>>(ma, mb, mc, p);
-    count_launch();
-    return check_launch("veda_gemm (tcgen05, CTA pair)");
+    return launch("veda_gemm (tcgen05, CTA pair)", kernel, dim3(2 * clusters), dim3(kThreads),
+                  Cfg2::SMEM, s, ma, mb, mc, p);
 }
 
 // How many two-CTA clusters of the paired kernel fit on the device at once (0: none).

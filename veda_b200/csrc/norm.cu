@@ -247,6 +247,8 @@ reduce_partials_kernel(const float* __restrict__ partials0, int blocks0, float* 
                        const float* __restrict__ partials1, int blocks1, float* __restrict__ dgamma1,
                        int n)
 {
+    dep_wait();
+    dep_release();
     const float* __restrict__ partials = blockIdx.y == 0 ? partials0 : partials1;
     const int blocks = blockIdx.y == 0 ? blocks0 : blocks1;
     float* __restrict__ dgamma = blockIdx.y == 0 ? dgamma0 : dgamma1;
@@ -294,13 +296,13 @@ __global__ void add_rows_kernel(const T* __restrict__ x, int64_t ldx, const T* _
     }
 }
 
-inline void launch_reduce_partials(const float* partials, int blocks, int n, float* dgamma,
-                                   cudaStream_t s, const float* partials1 = nullptr, int blocks1 = 0,
-                                   float* dgamma1 = nullptr)
+inline int launch_reduce_partials(const float* partials, int blocks, int n, float* dgamma,
+                                  cudaStream_t s, const float* partials1 = nullptr, int blocks1 = 0,
+                                  float* dgamma1 = nullptr)
 {
     const dim3 grid((n + 7) / 8, partials1 != nullptr ? 2 : 1);
-    reduce_partials_kernel<<<grid, 256, 0, s>>>(partials, blocks, dgamma, partials1, blocks1, dgamma1, n);
-    count_launch();
+    return launch("gain gradient (sum of block partials)", reduce_partials_kernel, grid, dim3(256), 0,
+                  s, partials, blocks, dgamma, partials1, blocks1, dgamma1, n);
 }
 
 // ---- register-resident row kernels (n == CH * 32 * V, 16-byte aligned rows) ------------------
@@ -732,6 +734,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 qknorm_rope_fwd_d128_kernel(const QkFwdSet s0, const QkFwdSet s1, const float* __restrict__ cosv,
                             const float* __restrict__ sinv, int64_t tokens, int seq_len, float eps)
 {
+    dep_wait();
+    dep_release();
     // this block's set, and the block's index within it
     const bool second = static_cast<int>(blockIdx.x) >= s0.blocks;
     const bf16* __restrict__ x = second ? s1.x : s0.x;
@@ -827,6 +831,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 qknorm_rope_bwd_d128_kernel(const QkSet s0, const QkSet s1, const float* __restrict__ cosv,
                             const float* __restrict__ sinv, int64_t tokens, int seq_len, float eps)
 {
+    dep_wait();
+    dep_release();
     __shared__ float part[kWarps * 4][128];
     // this block's set, and the block's index within it
     const bool second = static_cast<int>(blockIdx.x) >= s0.blocks;
@@ -1296,8 +1302,7 @@ int launch_rms_bwd(const void* x, int64_t ldx, const void* gamma, const void* dy
         {
             if (rc == VEDA_OK && partials != nullptr)
             {
-                launch_reduce_partials(partials, blocks, ni, dgamma, s);
-                return check_launch("veda_rmsnorm_bwd");
+                return launch_reduce_partials(partials, blocks, ni, dgamma, s);
             }
             return rc;
         }
@@ -1351,11 +1356,12 @@ int launch_rms_bwd(const void* x, int64_t ldx, const void* gamma, const void* dy
                                               partials, rows, ni, eps);
     }
     count_launch();
-    if (partials != nullptr)
+    const int rc = check_launch("veda_rmsnorm_bwd");
+    if (rc == VEDA_OK && partials != nullptr)
     {
-        launch_reduce_partials(partials, grid, ni, dgamma, s);
+        return launch_reduce_partials(partials, grid, ni, dgamma, s);
     }
-    return check_launch("veda_rmsnorm_bwd");
+    return rc;
 }
 
 } // namespace
@@ -1583,10 +1589,9 @@ extern "C" int veda_qknorm_rope_fwd_qk(const void* xq, const void* xk, int64_t l
                       static_cast<bf16*>(yq), ldx, ldyq, static_cast<int>(heads), static_cast<int>(bq)};
     const QkFwdSet sk{static_cast<const bf16*>(xk), static_cast<const bf16*>(k_gamma),
                       static_cast<bf16*>(yk), ldx, ldyk, static_cast<int>(kv_heads), static_cast<int>(bk)};
-    qknorm_rope_fwd_d128_kernel<<<static_cast<unsigned>(bq + bk), kWarps * 32, 0, stream>>>(
-        sq, sk, cosv, sinv, tokens, static_cast<int>(seq_len), eps);
-    count_launch();
-    return check_launch("veda_qknorm_rope_fwd_qk");
+    return launch("veda_qknorm_rope_fwd_qk", qknorm_rope_fwd_d128_kernel, dim3(static_cast<unsigned>(bq + bk)),
+                  dim3(kWarps * 32), 0, stream, sq, sk, cosv, sinv, tokens, static_cast<int>(seq_len),
+                  eps);
 }
 
 extern "C" int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamma,
@@ -1643,12 +1648,12 @@ extern "C" int veda_qknorm_rope_bwd(const void* x, int64_t ldx, const void* gamm
             static_cast<int>(heads), static_cast<int>(seq_len), static_cast<int>(head_dim), eps);
     }
     count_launch();
-    if (partials != nullptr)
+    rc = check_launch("veda_qknorm_rope_bwd");
+    if (rc == VEDA_OK && partials != nullptr)
     {
-        const int n = static_cast<int>(head_dim);
-        launch_reduce_partials(partials, grid, n, dgamma, stream);
+        return launch_reduce_partials(partials, grid, static_cast<int>(head_dim), dgamma, stream);
     }
-    return check_launch("veda_qknorm_rope_bwd");
+    return rc;
 }
 
 namespace
@@ -1757,22 +1762,26 @@ extern "C" int veda_qknorm_rope_bwd_qk(const void* xq, const void* xk, int64_t l
     const QkSet sk{static_cast<const bf16*>(xk), static_cast<const bf16*>(k_gamma),
                    static_cast<const bf16*>(dyk), static_cast<bf16*>(dxk), pk, ldx, lddyk, lddx,
                    static_cast<int>(kv_heads), gk, nullptr, 1.0f};
-    qknorm_rope_bwd_d128_kernel<<<gq + gk, kWarps * 32, 0, stream>>>(
-        sq, sk, cosv, sinv, tokens, static_cast<int>(seq_len), eps);
-    count_launch();
+    rc = launch("veda_qknorm_rope_bwd_qk", qknorm_rope_bwd_d128_kernel, dim3(gq + gk),
+                dim3(kWarps * 32), 0, stream, sq, sk, cosv, sinv, tokens, static_cast<int>(seq_len),
+                eps);
+    if (rc != VEDA_OK)
+    {
+        return rc;
+    }
     if (pq != nullptr && pk != nullptr)
     {
-        launch_reduce_partials(pq, gq, 128, dq_gamma, stream, pk, gk, dk_gamma);
+        return launch_reduce_partials(pq, gq, 128, dq_gamma, stream, pk, gk, dk_gamma);
     }
-    else if (pq != nullptr)
+    if (pq != nullptr)
     {
-        launch_reduce_partials(pq, gq, 128, dq_gamma, stream);
+        return launch_reduce_partials(pq, gq, 128, dq_gamma, stream);
     }
-    else if (pk != nullptr)
+    if (pk != nullptr)
     {
-        launch_reduce_partials(pk, gk, 128, dk_gamma, stream);
+        return launch_reduce_partials(pk, gk, 128, dk_gamma, stream);
     }
-    return check_launch("veda_qknorm_rope_bwd_qk");
+    return VEDA_OK;
 }
 
 extern "C" int veda_rope(const void* x, void* y, const float* cosv, const float* sinv,

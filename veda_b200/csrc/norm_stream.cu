@@ -125,6 +125,8 @@ rms_fwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __res
         }
         mbar_fence_init();
     }
+    dep_wait();   // the rows (and the gain) belong to the kernels before this one
+    dep_release();
     for (int c = threadIdx.x; c < R::N; c += blockDim.x)
     {
         gsm[c] = gamma != nullptr ? __bfloat162float(gamma[c]) : 1.0f;
@@ -251,6 +253,8 @@ rms_bwd_stream_kernel(const bf16* __restrict__ x, int64_t ldx, const bf16* __res
         }
         mbar_fence_init();
     }
+    dep_wait();   // the rows (and the gain) belong to the kernels before this one
+    dep_release();
     for (int c = threadIdx.x; c < R::N / 8; c += blockDim.x)
     {
         // 1.0 in bf16 is 0x3F80
@@ -414,10 +418,9 @@ int launch_fwd(const bf16* x, int64_t ldx, const bf16* r, int64_t ldr, const bf1
     }
     const int64_t chunks = (rows + kRows - 1) / kRows;
     const unsigned grid = static_cast<unsigned>(chunks < compute_sms() ? chunks : compute_sms());
-    rms_fwd_stream_kernel<CH, NIN><<<grid, kThreadsStream, R::SMEM, s>>>(
-        x, ldx, r, ldr, gamma, y, ldy, sum, lds, rows, eps, device_status_ptr());
-    count_launch();
-    return check_launch("veda_rmsnorm_fwd (streaming)");
+    return launch("veda_rmsnorm_fwd (streaming)", rms_fwd_stream_kernel<CH, NIN>, dim3(grid),
+                  dim3(kThreadsStream), R::SMEM, s, x, ldx, r, ldr, gamma, y, ldy, sum, lds, rows, eps,
+                  device_status_ptr());
 }
 
 template <int CH, int NIN>
@@ -440,10 +443,9 @@ int launch_bwd(const bf16* x, int64_t ldx, const bf16* gamma, const bf16* dy, in
     if (g > max_blocks) g = max_blocks;
     if (g < 1) g = 1;
     *blocks = static_cast<int>(g);
-    rms_bwd_stream_kernel<CH, NIN><<<static_cast<unsigned>(g), BwdSplit<CH>::THREADS, kSmem, s>>>(
-        x, ldx, gamma, dy, lddy, dresid, ldr, dx, lddx, partials, rows, eps, device_status_ptr());
-    count_launch();
-    return check_launch("veda_rmsnorm_bwd (streaming)");
+    return launch("veda_rmsnorm_bwd (streaming)", rms_bwd_stream_kernel<CH, NIN>,
+                  dim3(static_cast<unsigned>(g)), dim3(BwdSplit<CH>::THREADS), kSmem, s, x, ldx, gamma,
+                  dy, lddy, dresid, ldr, dx, lddx, partials, rows, eps, device_status_ptr());
 }
 
 } // namespace

@@ -30,6 +30,8 @@ __global__ void __launch_bounds__(kThreads)
 sumsq_partial_kernel(const float* __restrict__ g, int64_t n, double* __restrict__ partials)
 {
     __shared__ double part[kThreads / 32];
+    dep_wait();
+    dep_release();
     double s = 0.0;
     const int64_t n4 = (reinterpret_cast<uintptr_t>(g) & 15u) == 0 ? n / 4 : 0;
     const float4* g4 = reinterpret_cast<const float4*>(g);
@@ -69,6 +71,8 @@ sumsq_partial_kernel(const float* __restrict__ g, int64_t n, double* __restrict_
 __global__ void sumsq_final_kernel(const double* __restrict__ partials, int count, double* out,
                                    int accumulate)
 {
+    dep_wait();
+    dep_release();
     if (threadIdx.x == 0 && blockIdx.x == 0)
     {
         double t = accumulate ? *out : 0.0;
@@ -142,6 +146,8 @@ adamw_kernel(float* __restrict__ master, float* __restrict__ m, float* __restric
              float* __restrict__ g, bf16* __restrict__ lowp, int64_t n,
              const double* __restrict__ sumsq, AdamArgs a, const double* __restrict__ bias, bool vec)
 {
+    dep_wait();
+    dep_release();
     if (bias != nullptr)
     {
         // bias corrections computed by the host for this step and left in device memory (a step
@@ -251,12 +257,15 @@ extern "C" int veda_sumsq(const float* g, int64_t n, double* sumsq, int accumula
     double* partials = static_cast<double*>(workspace);
     if (n > 0)
     {
-        sumsq_partial_kernel<<<grid, kThreads, 0, stream>>>(g, n, partials);
-        count_launch();
+        const int rc = launch("veda_sumsq", sumsq_partial_kernel, dim3(grid), dim3(kThreads), 0, stream,
+                              g, n, partials);
+        if (rc != VEDA_OK)
+        {
+            return rc;
+        }
     }
-    sumsq_final_kernel<<<1, 32, 0, stream>>>(partials, n > 0 ? grid : 0, sumsq, accumulate);
-    count_launch();
-    return check_launch("veda_sumsq");
+    return launch("veda_sumsq", sumsq_final_kernel, dim3(1), dim3(32), 0, stream,
+                  static_cast<const double*>(partials), n > 0 ? grid : 0, sumsq, accumulate);
 }
 
 extern "C" int veda_clip_apply(float* g, int64_t n, const double* sumsq, float max_norm,
@@ -297,10 +306,8 @@ int adamw_launch(float* master, float* m, float* v, float* g, void* lowp, int64_
     AdamArgs a{lr, beta1, beta2, eps, weight_decay, bias1, bias2, max_norm, grad_scale,
                write_grad};
     const unsigned grid = grid_for(vec ? n / 4 + 1 : n, kThreads, 4);
-    adamw_kernel<<<grid, kThreads, 0, stream>>>(master, m, v, g, static_cast<bf16*>(lowp), n,
-                                                sumsq, a, bias_dev, vec);
-    count_launch();
-    return check_launch("veda_adamw_step");
+    return launch("veda_adamw_step", adamw_kernel, dim3(grid), dim3(kThreads), 0, stream, master, m, v, g,
+                  static_cast<bf16*>(lowp), n, sumsq, a, bias_dev, vec);
 }
 } // namespace
 

@@ -3,6 +3,7 @@
 #include "common.cuh"
 #include "tc_common.cuh"
 
+#include <cstdlib>
 #include <mutex>
 
 
@@ -36,6 +37,15 @@ int check_launch(const char* what)
 }
 
 void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+bool overlapped_launches()
+{
+    static const bool on = [] {
+        const char* v = std::getenv("VEDA_PDL");
+        return !(v != nullptr && v[0] == '0');
+    }();
+    return on;
+}
 
 uint64_t g_launches_value() { return g_launches.load(std::memory_order_relaxed); }
 

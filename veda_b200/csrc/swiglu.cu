@@ -45,6 +45,8 @@ __global__ void swiglu_fwd_kernel(const T* __restrict__ gate, int64_t ldg, const
                                   int64_t ldu, T* __restrict__ h, int64_t ldh, int64_t rows,
                                   int64_t n)
 {
+    dep_wait();
+    dep_release();
     constexpr int V = VEC ? Vec16<T>::N : 1;
     constexpr int U = kFwdRows;
     const int64_t nv = n / V;
@@ -84,6 +86,8 @@ __global__ void swiglu_bwd_kernel(const T* __restrict__ gate, int64_t ldg, const
                                   T* __restrict__ dgate, int64_t lddg, T* __restrict__ dup,
                                   int64_t lddu, int64_t rows, int64_t n)
 {
+    dep_wait();
+    dep_release();
     constexpr int V = VEC ? Vec16<T>::N : 1;
     constexpr int U = kBwdRows;
     const int64_t nv = n / V;
@@ -168,20 +172,15 @@ extern "C" int veda_swiglu_fwd(const void* gate, int64_t ldg, const void* up, in
     const unsigned threads = row_threads(vec ? n / (16 / static_cast<int64_t>(es)) : n);
     const unsigned grid = row_blocks(rows, threads, kFwdRows);
 #define VEDA_SW_FWD(T, VEC)                                                                       \
-    swiglu_fwd_kernel<T, VEC><<<grid, threads, 0, stream>>>(static_cast<const T*>(gate), ldg,        \
-                                                        static_cast<const T*>(up), ldu,          \
-                                                        static_cast<T*>(h), ldh, rows, n)
+    launch("veda_swiglu_fwd", swiglu_fwd_kernel<T, VEC>, dim3(grid), dim3(threads), 0, stream,     \
+           static_cast<const T*>(gate), ldg, static_cast<const T*>(up), ldu, static_cast<T*>(h),  \
+           ldh, rows, n)
     if (dtype == VEDA_BF16)
     {
-        if (vec) VEDA_SW_FWD(bf16, true); else VEDA_SW_FWD(bf16, false);
+        return vec ? VEDA_SW_FWD(bf16, true) : VEDA_SW_FWD(bf16, false);
     }
-    else
-    {
-        if (vec) VEDA_SW_FWD(float, true); else VEDA_SW_FWD(float, false);
-    }
+    return vec ? VEDA_SW_FWD(float, true) : VEDA_SW_FWD(float, false);
 #undef VEDA_SW_FWD
-    count_launch();
-    return check_launch("veda_swiglu_fwd");
 }
 
 extern "C" int veda_swiglu_bwd(const void* gate, int64_t ldg, const void* up, int64_t ldu,
@@ -205,19 +204,14 @@ extern "C" int veda_swiglu_bwd(const void* gate, int64_t ldg, const void* up, in
     const unsigned threads = row_threads(vec ? n / (16 / static_cast<int64_t>(es)) : n);
     const unsigned grid = row_blocks(rows, threads, kBwdRows);
 #define VEDA_SW_BWD(T, VEC)                                                                       \
-    swiglu_bwd_kernel<T, VEC><<<grid, threads, 0, stream>>>(                                          \
-        static_cast<const T*>(gate), ldg, static_cast<const T*>(up), ldu,                        \
-        static_cast<const T*>(dh), lddh, static_cast<T*>(dgate), lddg, static_cast<T*>(dup),     \
-        lddu, rows, n)
+    launch("veda_swiglu_bwd", swiglu_bwd_kernel<T, VEC>, dim3(grid), dim3(threads), 0, stream,     \
+           static_cast<const T*>(gate), ldg, static_cast<const T*>(up), ldu,                     \
+           static_cast<const T*>(dh), lddh, static_cast<T*>(dgate), lddg, static_cast<T*>(dup),  \
+           lddu, rows, n)
     if (dtype == VEDA_BF16)
     {
-        if (vec) VEDA_SW_BWD(bf16, true); else VEDA_SW_BWD(bf16, false);
+        return vec ? VEDA_SW_BWD(bf16, true) : VEDA_SW_BWD(bf16, false);
     }
-    else
-    {
-        if (vec) VEDA_SW_BWD(float, true); else VEDA_SW_BWD(float, false);
-    }
+    return vec ? VEDA_SW_BWD(float, true) : VEDA_SW_BWD(float, false);
 #undef VEDA_SW_BWD
-    count_launch();
-    return check_launch("veda_swiglu_bwd");
 }

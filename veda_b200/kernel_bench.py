@@ -281,15 +281,17 @@ def bandwidth_kernels(tokens, reps, only=None):
                           "frac": nbytes / (ms / 1e3) / 1e9 / hbm}), flush=True)
 
 
-def one_gemm(op, M, N, K, reps):
+def one_gemm(op, M, N, K, reps, out=None):
     import torch
     import veda_b200 as V
     L = V.lib()
     s = torch.cuda.current_stream()
     a = torch.randn(*((K, M) if op == "tn" else (M, K)), device="cuda").to(torch.bfloat16)
     b = torch.randn(*((N, K) if op == "nt" else (K, N)), device="cuda").to(torch.bfloat16)
-    c = torch.empty(M, N, dtype=torch.bfloat16 if op == "nt" else torch.float32, device="cuda")
-    dc = V.BF16 if op == "nt" else V.F32
+    # C in bf16 for nt (a forward layer) and fp32 otherwise (a gradient), unless `out` says
+    bf = out == "bf16" if out is not None else op == "nt"
+    c = torch.empty(M, N, dtype=torch.bfloat16 if bf else torch.float32, device="cuda")
+    dc = V.BF16 if bf else V.F32
     fn = getattr(L, f"veda_gemm_{op}")
 
     def run():
@@ -377,6 +379,7 @@ def main():
     c.add_argument("--n", type=int, default=151936)
     c.add_argument("--k", type=int, default=1024)
     c.add_argument("--reps", type=int, default=3)
+    c.add_argument("--out", choices=["bf16", "f32"], default=None)
     d = sub.add_parser("bw")
     d.add_argument("--tokens", type=int, default=8192)
     d.add_argument("--reps", type=int, default=20)
@@ -395,7 +398,7 @@ def main():
     elif args.cmd == "bw":
         bandwidth_kernels(args.tokens, args.reps, args.kernels)
     else:
-        one_gemm(args.op, args.m, args.n, args.k, args.reps)
+        one_gemm(args.op, args.m, args.n, args.k, args.reps, args.out)
 
 
 if __name__ == "__main__":
