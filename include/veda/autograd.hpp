@@ -120,6 +120,11 @@ Variable attention_output(const Variable& qkv, const Variable& q_norm, const Var
                           size_t head_dim, float eps);
 // mul(silu(gate), up) on a fused gate|up buffer [rows, 2F] -> [rows, F].
 Variable swiglu(const Variable& gate_up);
+// The feed-forward block linear(swiglu(linear(x, gate_up)), down) with gate_up [2F, D] (gate rows,
+// then up rows) and down [D, F], as one node: in bf16 the gate|up GEMM writes h as well and the
+// down projection's input-gradient GEMM writes dgate|up (SwiGLU in the GEMM epilogues, the same
+// bits); other dtypes and shapes run the three ops.
+Variable mlp(const Variable& x, const Variable& gate_up, const Variable& down);
 // Token ids already on the device (int64 [count]); ids are checked on the device and an
 // out-of-range id raises std::out_of_range at the next synchronisation point.
 Variable embedding_device(const Variable& table, const core::Tensor& ids);

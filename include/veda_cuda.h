@@ -96,6 +96,23 @@ int veda_gemm_batched(int op, int64_t batch, int64_t M, int64_t N, int64_t K, co
                       int64_t lda, int64_t stride_a, const void* B, int64_t ldb, int64_t stride_b,
                       void* C, int64_t ldc, int64_t stride_c, int dtype_ab, int dtype_c,
                       float alpha, float beta, veda_stream_t stream);
+/* The MLP's gate|up projection with SwiGLU fused into the GEMM (bf16): gate_up[rows, 2F] =
+ * x[rows, D] w_gate_up[2F, D]^T (rows 0..F-1 of the weight the gate projection, F..2F-1 the up
+ * projection) and h[rows, F] = silu(gate) * up (src/libs/train/Model.cpp:199-202). Bit for bit
+ * veda_gemm_nt followed by veda_swiglu_fwd; VEDA_ERR_UNSUPPORTED (nothing runs) unless F is a
+ * multiple of 128, rows >= 256 and D a multiple of 8, with 16-byte aligned rows. */
+int veda_gemm_swiglu_fwd(int64_t rows, int64_t F, int64_t D, const void* x, int64_t ldx,
+                         const void* w_gate_up, int64_t ldw, void* gate_up, int64_t ldgu, void* h,
+                         int64_t ldh, veda_stream_t stream);
+/* Its backward through the down projection (bf16): dh = dy[rows, D] w_down[D, F] is never
+ * stored; with gate and up from gate_up[rows, 2F] the GEMM writes dgate_up[rows, 2F] =
+ * (dgate | dup) (src/libs/autograd/Variable.cpp:338, NonLinear.cpp:47-63, Variable.cpp:218-239).
+ * Bit for bit veda_gemm_nn into a bf16 dh followed by veda_swiglu_bwd; VEDA_ERR_UNSUPPORTED
+ * (nothing runs) unless F is a multiple of 256, rows >= 256 and D a multiple of 8, with 16-byte
+ * aligned rows. */
+int veda_gemm_swiglu_bwd(int64_t rows, int64_t F, int64_t D, const void* dy, int64_t lddy,
+                         const void* w_down, int64_t ldw, const void* gate_up, int64_t ldgu,
+                         void* dgate_up, int64_t lddgu, veda_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------- */
 /* RMSNorm with gain: y = gamma * x / sqrt(mean(x^2) + eps) over rows of n.                   */

@@ -308,6 +308,59 @@ def test_swiglu(dtype, rows, F):
     assert rel(out[:, F:], du_ref) <= TOL[dtype]
 
 
+# The MLP's projections with SwiGLU fused into their GEMMs give the bits of the GEMM followed by
+# the stand-alone SwiGLU kernel: the Qwen3-0.6B shape, and ragged rows and K.
+@pytest.mark.parametrize("rows,F,D", [(8192, 3072, 1024), (300, 256, 64), (1000, 384, 136)])
+def test_gemm_swiglu_fwd_is_gemm_then_swiglu(rows, F, D):
+    t = torch()
+    g = t.Generator(device="cuda").manual_seed(rows + F + D)
+    x = t.randn(rows, D, device="cuda", generator=g).to(t.bfloat16)
+    w = (t.randn(2 * F, D, device="cuda", generator=g) / math.sqrt(D)).to(t.bfloat16)
+    gu_ref, h_ref = empty((rows, 2 * F), V.BF16), empty((rows, F), V.BF16)
+    call("veda_gemm_nt", rows, 2 * F, D, ptr(x), D, ptr(w), D, ptr(gu_ref), 2 * F, V.BF16, V.BF16,
+         1.0, 0.0, stream())
+    call("veda_swiglu_fwd", ptr(gu_ref), 2 * F, gu_ref.data_ptr() + 2 * F, 2 * F, ptr(h_ref), F,
+         rows, F, V.BF16, stream())
+    gu, h = empty((rows, 2 * F), V.BF16), empty((rows, F), V.BF16)
+    call("veda_gemm_swiglu_fwd", rows, F, D, ptr(x), D, ptr(w), D, ptr(gu), 2 * F, ptr(h), F,
+         stream())
+    sync()
+    assert t.equal(gu, gu_ref)
+    assert t.equal(h, h_ref)
+
+
+@pytest.mark.parametrize("rows,F,D", [(8192, 3072, 1024), (300, 256, 64), (1000, 512, 136)])
+def test_gemm_swiglu_bwd_is_gemm_then_swiglu_bwd(rows, F, D):
+    t = torch()
+    g = t.Generator(device="cuda").manual_seed(rows * 3 + F + D)
+    dy = t.randn(rows, D, device="cuda", generator=g).to(t.bfloat16)
+    w = (t.randn(D, F, device="cuda", generator=g) / math.sqrt(F)).to(t.bfloat16)
+    gu = (2 * t.randn(rows, 2 * F, device="cuda", generator=g)).to(t.bfloat16)
+    dh, dgu_ref = empty((rows, F), V.BF16), empty((rows, 2 * F), V.BF16)
+    call("veda_gemm_nn", rows, F, D, ptr(dy), D, ptr(w), F, ptr(dh), F, V.BF16, V.BF16, 1.0, 0.0,
+         stream())
+    call("veda_swiglu_bwd", ptr(gu), 2 * F, gu.data_ptr() + 2 * F, 2 * F, ptr(dh), F, ptr(dgu_ref),
+         2 * F, dgu_ref.data_ptr() + 2 * F, 2 * F, rows, F, V.BF16, stream())
+    dgu = empty((rows, 2 * F), V.BF16)
+    call("veda_gemm_swiglu_bwd", rows, F, D, ptr(dy), D, ptr(w), F, ptr(gu), 2 * F, ptr(dgu), 2 * F,
+         stream())
+    sync()
+    assert t.equal(dgu, dgu_ref)
+
+
+def test_gemm_swiglu_rejects_what_it_cannot_tile():
+    a = empty((512, 512), V.BF16)
+    L = V.lib()
+    # F not a multiple of 128 (forward) or 256 (backward), fewer than 256 rows: nothing runs
+    assert L.veda_gemm_swiglu_fwd(300, 200, 64, ptr(a), 64, ptr(a), 64, ptr(a), 400, ptr(a), 200,
+                                  stream()) == -4
+    assert L.veda_gemm_swiglu_bwd(300, 128, 64, ptr(a), 64, ptr(a), 128, ptr(a), 256, ptr(a), 256,
+                                  stream()) == -4
+    assert L.veda_gemm_swiglu_fwd(200, 128, 64, ptr(a), 64, ptr(a), 64, ptr(a), 256, ptr(a), 128,
+                                  stream()) == -4
+    sync()
+
+
 # ---------------------------------------------------------------------------------------------
 # Cross-entropy
 # ---------------------------------------------------------------------------------------------

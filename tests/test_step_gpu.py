@@ -251,6 +251,28 @@ def test_recompute_attention_is_bit_exact():
     b.close()
 
 
+def test_fused_mlp_is_bit_exact(monkeypatch):
+    """The feed-forward block with SwiGLU in the GEMM epilogues (the bf16 default) and run as its
+    three ops (VEDA_FUSED_MLP=0) give the same losses, norms, gradients and weights, bit for bit."""
+    cfg, B, T = QWEN_SMALL, 2, 128
+    flat = np.concatenate([p.ravel() for p in O.init_params(cfg, 3, bf16=True)])
+    a, b = make_trainer(cfg, 1, B, T), make_trainer(cfg, 1, B, T)
+    for t in (a, b):
+        t.set_params(flat)
+        t.set_step_graph(False)
+    for s in range(3):
+        ids, tg = O.synthetic_batch(cfg, B, T, 40 + s)
+        monkeypatch.setenv("VEDA_FUSED_MLP", "1")
+        la, na = a.step_host(ids, tg)
+        monkeypatch.setenv("VEDA_FUSED_MLP", "0")
+        lb, nb = b.step_host(ids, tg)
+        assert la == lb and na == nb, (s, la, lb, na, nb)
+    assert np.array_equal(a.get_grads(), b.get_grads())
+    assert np.array_equal(a.get_params(), b.get_params())
+    a.close()
+    b.close()
+
+
 @pytest.mark.parametrize("dtype", [0, 1])
 def test_step_graph_replay_matches_eager(dtype):
     """A trainer replaying its step from a CUDA graph (captured at the second step) gives the same

@@ -40,6 +40,8 @@ SIGNATURES = {
     "veda_gemm_nt": (_i, [_i64, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _i, _f, _f, _p]),
     "veda_gemm_nn": (_i, [_i64, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _i, _f, _f, _p]),
     "veda_gemm_tn": (_i, [_i64, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _i, _f, _f, _p]),
+    "veda_gemm_swiglu_fwd": (_i, [_i64, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _p]),
+    "veda_gemm_swiglu_bwd": (_i, [_i64, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _p]),
     "veda_gemm_batched": (_i, [_i, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p,
                                _i64, _i64, _i, _i, _f, _f, _p]),
     "veda_rmsnorm_fwd": (_i, [_p, _i64, _p, _p, _i64, _i64, _i64, _f, _i, _p]),

@@ -22,6 +22,7 @@
 // Every mbarrier wait is bounded; a wait that gives up records VEDA_ERR_TIMEOUT in the library's
 // device status word (veda_kernel_status) and the kernel runs to completion.
 #include "gemm.cuh"
+#include "swiglu_math.cuh"
 #include "tc_common.cuh"
 
 #include <cuda.h>
@@ -65,6 +66,11 @@ struct Params
     int vec_ok;       // C base and ldc allow 16-byte stores
     int out_mode;     // 0: stores from registers; 1: TMA store; 2: TMA reduce-add (fp32 C)
     int* status;
+    // SwiGLU epilogues of the paired kernel (EPI 1 and 2): the width F of gate and of up, which
+    // sit side by side in one [M, 2F] buffer; EPI 2 reads them from gu
+    int F;
+    const bf16* gu;
+    int64_t ldgu;
 };
 
 // Per-warp output staging: two 4 KB tiles of 32 rows x 128 bytes (128-byte swizzle), so the
@@ -509,6 +515,183 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
 // complete on the even CTA's stage barrier (the .cta_group::2 form of the TMA load, which may
 // signal the peer's barrier); tcgen05.commit signals stage release and tile completion to the
 // barriers of both CTAs; the odd CTA's epilogue releases an accumulator on the even CTA's barrier.
+// ---- SwiGLU epilogues of the paired kernel ----------------------------------------------------
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b)
+{
+    const __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&t);
+}
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// Writes this lane's row (64 bf16 as 32 packed words) of a 32 x 128-byte staging tile and stores
+// the tile to (x, y) of `map`; the staging buffers alternate as in epilogue_tma.
+__device__ __forceinline__ void stage_store(const CUtensorMap* map, const uint32_t (&w)[32], int x, int y,
+                                            uint8_t* staging, uint32_t& nstore, int lane)
+{
+    uint8_t* buf = staging + (nstore & 1) * kStageTile;
+    if (nstore >= 2)
+    {
+        if (lane == 0)
+        {
+            bulk_wait_group_read<1>();
+        }
+        __syncwarp();
+    }
+    uint8_t* row = buf + lane * 128;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+    {
+        *reinterpret_cast<uint4*>(row + ((k ^ (lane & 7)) << 4)) =
+            make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+    }
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0)
+    {
+        tma_store_2d(map, buf, x, y);
+        bulk_commit_group();
+    }
+    ++nstore;
+}
+
+// EPI 1, one warp's 32 rows: accumulator columns 0-127 are gate columns gcol.. of the [M, 2F]
+// output and 128-255 the up columns F + gcol..; writes both (bf16) and h = silu(gate) * up,
+// computed from the bf16-rounded gate and up as the stand-alone SwiGLU reads them, into H.
+__device__ __forceinline__ void epilogue_swiglu(const Params& p, const CUtensorMap* mc,
+                                                const CUtensorMap* mh, uint32_t taddr, int row0,
+                                                int gcol, uint8_t* staging, uint32_t& nstore, int lane)
+{
+    if (row0 >= p.M)
+    {
+        return;
+    }
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 64)
+    {
+        uint32_t gw[32], uw[32], hw[32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+        {
+            uint32_t a[32], b[32];
+            tmem_ld32(taddr + static_cast<uint32_t>(c + half * 32), a);
+            tmem_ld32(taddr + static_cast<uint32_t>(128 + c + half * 32), b);
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+            {
+                const uint32_t g2 = pack_bf16(__uint_as_float(a[2 * q]), __uint_as_float(a[2 * q + 1]));
+                const uint32_t u2 = pack_bf16(__uint_as_float(b[2 * q]), __uint_as_float(b[2 * q + 1]));
+                gw[half * 16 + q] = g2;
+                uw[half * 16 + q] = u2;
+                hw[half * 16 + q] = pack_bf16(swiglu_value(bf16_lo(g2), bf16_lo(u2)),
+                                              swiglu_value(bf16_hi(g2), bf16_hi(u2)));
+            }
+        }
+        stage_store(mc, gw, gcol + c, row0, staging, nstore, lane);
+        stage_store(mc, uw, p.F + gcol + c, row0, staging, nstore, lane);
+        stage_store(mh, hw, gcol + c, row0, staging, nstore, lane);
+    }
+}
+
+// A warp's 32 rows x 64 bf16 of `src` (row stride ld): eight 16-byte loads a lane, each
+// instruction reading four whole 128-byte rows; rows at or past M read as zero.
+__device__ __forceinline__ void fetch_rows(const bf16* src, int64_t ld, int row0, int M, int lane,
+                                           uint4 (&v)[8])
+{
+    const int seg = lane & 7;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+    {
+        const int r = row0 + 4 * k + (lane >> 3);
+        v[k] = r < M ? __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(r) * ld) + seg)
+                     : make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+// The fetched rows into a 128-byte-swizzled staging tile (row r's segment s at s ^ (r & 7)).
+__device__ __forceinline__ void stash_rows(uint8_t* buf, int lane, const uint4 (&v)[8])
+{
+    const int seg = lane & 7;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+    {
+        const int r = 4 * k + (lane >> 3);
+        *reinterpret_cast<uint4*>(buf + r * 128 + ((seg ^ (r & 7)) << 4)) = v[k];
+    }
+}
+
+// EPI 2, one warp's 32 rows: the accumulator is dh for columns col0..col0+255 of the [M, F]
+// intermediate; dh rounded to bf16 (as the stand-alone path stores it) with gate and up of the
+// same rows and columns (p.gu) gives dg and du, written into C, the [M, 2F] gradient of gate|up,
+// at col0 and F + col0. pg / pu hold gate and up of the first 64 columns on entry.
+__device__ __forceinline__ void epilogue_dswiglu(const Params& p, const CUtensorMap* mc, uint32_t taddr,
+                                                 int row0, int col0, uint8_t* staging,
+                                                 uint32_t& nstore, int lane, uint4 (&pg)[8],
+                                                 uint4 (&pu)[8])
+{
+    uint8_t* const bg = staging;
+    uint8_t* const bu = staging + kStageTile;
+    const bool rows_in = row0 < p.M;
+#pragma unroll 1
+    for (int c = 0; c < 256; c += 64)
+    {
+        if (nstore > 0)
+        {
+            if (lane == 0)
+            {
+                bulk_wait_group_read<0>();   // the last chunk's stores have read both buffers
+            }
+            __syncwarp();
+        }
+        stash_rows(bg, lane, pg);
+        stash_rows(bu, lane, pu);
+        __syncwarp();
+        if (c + 64 < 256 && rows_in)
+        {
+            // the next chunk's gate and up load while this one is computed
+            fetch_rows(p.gu + col0 + c + 64, p.ldgu, row0, p.M, lane, pg);
+            fetch_rows(p.gu + p.F + col0 + c + 64, p.ldgu, row0, p.M, lane, pu);
+        }
+        uint32_t d0[32], d1[32];
+        tmem_ld32(taddr + static_cast<uint32_t>(c), d0);
+        tmem_ld32(taddr + static_cast<uint32_t>(c + 32), d1);
+        uint8_t* const rg = bg + lane * 128;
+        uint8_t* const ru = bu + lane * 128;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+        {
+            uint4* const gk = reinterpret_cast<uint4*>(rg + ((k ^ (lane & 7)) << 4));
+            uint4* const uk = reinterpret_cast<uint4*>(ru + ((k ^ (lane & 7)) << 4));
+            const uint4 gv = *gk, uv = *uk;
+            const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+            const uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
+            const uint32_t* dsrc = k < 4 ? &d0[8 * k] : &d1[8 * (k - 4)];
+            uint32_t og[4], ou[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+            {
+                const uint32_t d2 = pack_bf16(__uint_as_float(dsrc[2 * q]), __uint_as_float(dsrc[2 * q + 1]));
+                float dg0, du0, dg1, du1;
+                swiglu_grads(bf16_lo(gw[q]), bf16_lo(uw[q]), bf16_lo(d2), dg0, du0);
+                swiglu_grads(bf16_hi(gw[q]), bf16_hi(uw[q]), bf16_hi(d2), dg1, du1);
+                og[q] = pack_bf16(dg0, dg1);
+                ou[q] = pack_bf16(du0, du1);
+            }
+            *gk = make_uint4(og[0], og[1], og[2], og[3]);
+            *uk = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0 && rows_in)
+        {
+            tma_store_2d(mc, bg, col0 + c, row0);
+            tma_store_2d(mc, bu, p.F + col0 + c, row0);
+            bulk_commit_group();
+        }
+        ++nstore;
+    }
+}
+
 struct Cfg2
 {
     static constexpr int STAGES = 6;
@@ -570,10 +753,11 @@ __device__ __forceinline__ void commit_pair(uint64_t* bar)
         : "memory");
 }
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                const __grid_constant__ CUtensorMap tma_c, const Params p)
+                const __grid_constant__ CUtensorMap tma_c, const __grid_constant__ CUtensorMap tma_h,
+                const Params p)
 {
     using C_ = Cfg2;
     extern __shared__ uint8_t smem_raw[];
@@ -640,7 +824,10 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
             const int kb0 = split * p.kb_per_split;
             const int kb1 = min(p.kblocks, kb0 + p.kb_per_split);
             const int row0 = mb * 256 + static_cast<int>(rank) * 128;
-            const int col0 = nb * 256 + static_cast<int>(rank) * 128;
+            // EPI 1: the tile's B columns are 128 gate rows of W (this CTA's half at rank 0) and
+            // the 128 matching up rows, F further on (rank 1)
+            const int col0 = EPI == 1 ? (rank == 0 ? nb * 128 : p.F + nb * 128)
+                                      : nb * 256 + static_cast<int>(rank) * 128;
             for (int kb = kb0; kb < kb1; ++kb)
             {
                 mbar_wait(&empty[stage], phase ^ 1, p.status, abort);
@@ -729,6 +916,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
     {
         const int quarter = warp & 3;
         const uint32_t release = peer_addr(&tempty[0], 0);   // the even CTA's tempty[0]
+        uint8_t* const wstage = staging + (warp - 2) * 2 * kStageTile;
         uint32_t nstore = 0;
         int it = 0;
         for (int u = cid; u < units; u += nclusters, ++it)
@@ -737,15 +925,32 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
             unit_coords(u, p, mb, nb, split);
             const int buf = it & 1;
             const uint32_t tphase = (it >> 1) & 1;
+            const int row = mb * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
+            [[maybe_unused]] uint4 pg[8], pu[8];
+            if constexpr (EPI == 2)
+            {
+                // gate and up of the first 64 columns: their loads run while the products finish
+                if (row - lane < p.M)
+                {
+                    fetch_rows(p.gu + nb * 256, p.ldgu, row - lane, p.M, lane, pg);
+                    fetch_rows(p.gu + p.F + nb * 256, p.ldgu, row - lane, p.M, lane, pu);
+                }
+            }
             mbar_wait(&tfull[buf], tphase, p.status, abort);
             fence_after();
-            const int row = mb * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
             const uint32_t base = tmem + static_cast<uint32_t>(buf * 256) +
                                   (static_cast<uint32_t>(quarter * 32) << 16);
-            if (p.out_mode != 0)
+            if constexpr (EPI == 1)
             {
-                epilogue_tma<256>(p, &tma_c, base, row - lane, nb * 256,
-                                  staging + (warp - 2) * 2 * kStageTile, nstore, lane);
+                epilogue_swiglu(p, &tma_c, &tma_h, base, row - lane, nb * 128, wstage, nstore, lane);
+            }
+            else if constexpr (EPI == 2)
+            {
+                epilogue_dswiglu(p, &tma_c, base, row - lane, nb * 256, wstage, nstore, lane, pg, pu);
+            }
+            else if (p.out_mode != 0)
+            {
+                epilogue_tma<256>(p, &tma_c, base, row - lane, nb * 256, wstage, nstore, lane);
             }
             else
             {
@@ -839,17 +1044,17 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& m
 
 // Launches the paired-CTA kernel on `clusters` clusters of two; -1 if clusters cannot be
 // scheduled (the caller then uses the single-CTA kernel).
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int EPI = 0>
 int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const Params& p,
-               int clusters, cudaStream_t s)
+               int clusters, cudaStream_t s, const CUtensorMap* mh = nullptr)
 {
-    auto kernel = tc_gemm2_kernel<A_MN, B_MN>;
+    auto kernel = tc_gemm2_kernel<A_MN, B_MN, EPI>;
     return launch("veda_gemm (tcgen05, CTA pair)", kernel, dim3(2 * clusters), dim3(kThreads),
-                  Cfg2::SMEM, s, ma, mb, mc, p);
+                  Cfg2::SMEM, s, ma, mb, mc, mh != nullptr ? *mh : mc, p);
 }
 
 // How many two-CTA clusters of the paired kernel fit on the device at once (0: none).
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int EPI = 0>
 int pair_clusters()
 {
     static int cached_device = -1, cached = 0;
@@ -857,7 +1062,7 @@ int pair_clusters()
     cudaGetDevice(&device);
     if (cached_device != device)
     {
-        auto kernel = tc_gemm2_kernel<A_MN, B_MN>;
+        auto kernel = tc_gemm2_kernel<A_MN, B_MN, EPI>;
         cached = 0;
         if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2::SMEM) ==
             cudaSuccess)
@@ -1033,6 +1238,108 @@ int tc_gemm_pair(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t
     if (op == kNT) return launch_tc2<false, false>(ma, mb, mc, p, clusters, s);
     if (op == kNN) return launch_tc2<false, true>(ma, mb, mc, p, clusters, s);
     return launch_tc2<true, true>(ma, mb, mc, p, clusters, s);
+}
+
+// bf16 store map of the epilogue: 64-column x 32-row boxes, 128-byte swizzle.
+bool make_store_map(CUtensorMap* map, void* base, int64_t inner, int64_t outer, int64_t ld)
+{
+    auto fn = encode_fn();
+    if (fn == nullptr)
+    {
+        return false;
+    }
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    const cuuint32_t box[2] = {64, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool swiglu_shapes_ok(int64_t rows, int64_t F, int64_t D, int64_t tile)
+{
+    return pair_enabled() && rows >= 256 && rows < (1ll << 31) && F >= tile && F % tile == 0 &&
+           2 * F < (1ll << 31) && D >= 16 && D % 8 == 0 && D < (1ll << 31);
+}
+
+// The gate|up projection with SwiGLU in its epilogue (paired kernel, EPI 1): gu[rows, 2F] =
+// x[rows, D] W[2F, D]^T (W's rows 0..F-1 gate, F..2F-1 up) and h[rows, F] = silu(gate) * up.
+// Each tile pairs 128 gate columns with the 128 matching up columns. -1: not for this kernel.
+int gemm_swiglu_fwd_tc(int64_t rows, int64_t F, int64_t D, const void* x, int64_t ldx, const void* w,
+                       int64_t ldw, void* gu, int64_t ldgu, void* h, int64_t ldh, cudaStream_t s)
+{
+    if (!swiglu_shapes_ok(rows, F, D, 128) || !aligned16(x) || !aligned16(w) || !aligned16(gu) ||
+        !aligned16(h) || ldx % 8 != 0 || ldw % 8 != 0 || ldgu % 8 != 0 || ldh % 8 != 0)
+    {
+        return -1;
+    }
+    const int clusters_max = std::min(pair_clusters<false, false, 1>(), compute_sms() / 2);
+    CUtensorMap ma, mb, mc, mh;
+    if (clusters_max < 1 || !make_map(&ma, x, D, rows, ldx, 64, 128) ||
+        !make_map(&mb, w, D, 2 * F, ldw, 64, 128) || !make_store_map(&mc, gu, 2 * F, rows, ldgu) ||
+        !make_store_map(&mh, h, F, rows, ldh))
+    {
+        return -1;
+    }
+    Params p{};
+    p.M = static_cast<int>(rows);
+    p.N = static_cast<int>(2 * F);
+    p.K = static_cast<int>(D);
+    p.num_m = static_cast<int>((rows + 255) / 256);
+    p.num_n = static_cast<int>(F / 128);
+    p.kblocks = static_cast<int>((D + BK - 1) / BK);
+    p.splits = 1;
+    p.kb_per_split = p.kblocks;
+    p.C = gu;
+    p.ldc = ldgu;
+    p.alpha = 1.0f;
+    p.vec_ok = 1;
+    p.out_mode = 1;
+    p.status = device_status_ptr();
+    p.F = static_cast<int>(F);
+    const int tiles = p.num_m * p.num_n;
+    return launch_tc2<false, false, 1>(ma, mb, mc, p, std::min(tiles, clusters_max), s, &mh);
+}
+
+// The down projection's input gradient with SwiGLU's backward in its epilogue (paired kernel,
+// EPI 2): dh = dy[rows, D] W[D, F] stays in TMEM; with gate and up from gu[rows, 2F] the
+// epilogue writes dgu[rows, 2F] = (dgate | dup). -1: not for this kernel.
+int gemm_swiglu_bwd_tc(int64_t rows, int64_t F, int64_t D, const void* dy, int64_t lddy, const void* w,
+                       int64_t ldw, const void* gu, int64_t ldgu, void* dgu, int64_t lddgu, cudaStream_t s)
+{
+    if (!swiglu_shapes_ok(rows, F, D, 256) || !aligned16(dy) || !aligned16(w) || !aligned16(gu) ||
+        !aligned16(dgu) || lddy % 8 != 0 || ldw % 8 != 0 || ldgu % 8 != 0 || lddgu % 8 != 0)
+    {
+        return -1;
+    }
+    const int clusters_max = std::min(pair_clusters<false, true, 2>(), compute_sms() / 2);
+    CUtensorMap ma, mb, mc;
+    if (clusters_max < 1 || !make_map(&ma, dy, D, rows, lddy, 64, 128) ||
+        !make_map(&mb, w, F, D, ldw, 64, 64) || !make_store_map(&mc, dgu, 2 * F, rows, lddgu))
+    {
+        return -1;
+    }
+    Params p{};
+    p.M = static_cast<int>(rows);
+    p.N = static_cast<int>(F);
+    p.K = static_cast<int>(D);
+    p.num_m = static_cast<int>((rows + 255) / 256);
+    p.num_n = static_cast<int>(F / 256);
+    p.kblocks = static_cast<int>((D + BK - 1) / BK);
+    p.splits = 1;
+    p.kb_per_split = p.kblocks;
+    p.C = dgu;
+    p.ldc = lddgu;
+    p.alpha = 1.0f;
+    p.vec_ok = 1;
+    p.out_mode = 1;
+    p.status = device_status_ptr();
+    p.F = static_cast<int>(F);
+    p.gu = static_cast<const bf16*>(gu);
+    p.ldgu = ldgu;
+    const int tiles = p.num_m * p.num_n;
+    return launch_tc2<false, true, 2>(ma, mb, mc, p, std::min(tiles, clusters_max), s);
 }
 
 int tc_gemm(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* B,
@@ -1214,6 +1521,41 @@ extern "C" int veda_gemm_tn(int64_t M, int64_t N, int64_t K, const void* A, int6
 {
     return gemm_dispatch(kTN, 1, M, N, K, A, lda, 0, B, ldb, 0, C, ldc, 0, dtype_ab, dtype_c,
                          alpha, beta, stream);
+}
+
+extern "C" int veda_gemm_swiglu_fwd(int64_t rows, int64_t F, int64_t D, const void* x, int64_t ldx,
+                                    const void* w_gate_up, int64_t ldw, void* gate_up, int64_t ldgu,
+                                    void* h, int64_t ldh, veda_stream_t stream)
+{
+    VEDA_REQUIRE(rows >= 0 && F > 0 && D > 0, "bad shape");
+    VEDA_REQUIRE(ldx >= D && ldw >= D && ldgu >= 2 * F && ldh >= F, "leading dimension too small");
+    if (rows == 0)
+    {
+        return VEDA_OK;
+    }
+    VEDA_REQUIRE(x && w_gate_up && gate_up && h, "null pointer");
+    const int rc = gemm_swiglu_fwd_tc(rows, F, D, x, ldx, w_gate_up, ldw, gate_up, ldgu, h, ldh, stream);
+    return rc == -1 ? fail(VEDA_ERR_UNSUPPORTED, "veda_gemm_swiglu_fwd: shape or alignment not supported "
+                                                 "(F a multiple of 128, rows >= 256, 16-byte rows)")
+                    : rc;
+}
+
+extern "C" int veda_gemm_swiglu_bwd(int64_t rows, int64_t F, int64_t D, const void* dy, int64_t lddy,
+                                    const void* w_down, int64_t ldw, const void* gate_up, int64_t ldgu,
+                                    void* dgate_up, int64_t lddgu, veda_stream_t stream)
+{
+    VEDA_REQUIRE(rows >= 0 && F > 0 && D > 0, "bad shape");
+    VEDA_REQUIRE(lddy >= D && ldw >= F && ldgu >= 2 * F && lddgu >= 2 * F, "leading dimension too small");
+    if (rows == 0)
+    {
+        return VEDA_OK;
+    }
+    VEDA_REQUIRE(dy && w_down && gate_up && dgate_up, "null pointer");
+    const int rc =
+        gemm_swiglu_bwd_tc(rows, F, D, dy, lddy, w_down, ldw, gate_up, ldgu, dgate_up, lddgu, stream);
+    return rc == -1 ? fail(VEDA_ERR_UNSUPPORTED, "veda_gemm_swiglu_bwd: shape or alignment not supported "
+                                                 "(F a multiple of 256, rows >= 256, 16-byte rows)")
+                    : rc;
 }
 
 extern "C" int veda_gemm_batched(int op, int64_t batch, int64_t M, int64_t N, int64_t K,

@@ -1641,6 +1641,105 @@ Variable swiglu(const Variable& gate_up)
     });
 }
 
+// VEDA_FUSED_MLP=0 runs the feed-forward block as its three ops even where the fused form applies
+// (read at every call, so a process can compare the two).
+bool fused_mlp_enabled()
+{
+    const char* v = std::getenv("VEDA_FUSED_MLP");
+    return !(v != nullptr && v[0] == '0');
+}
+
+Variable mlp(const Variable& x, const Variable& gate_up, const Variable& down)
+{
+    // Model.cpp:199-203: down(silu(gate(x)) * up(x)). The fused form needs bf16 throughout, F a
+    // multiple of 256 and at least 256 rows; otherwise the three ops run one by one.
+    const Tensor& xv = x.value();
+    const Tensor& wg = gate_up.value();
+    const Tensor& wd = down.value();
+    const size_t D = xv.rank() >= 1 ? xv.shape()[xv.rank() - 1] : 0;
+    const size_t rows = D > 0 ? xv.numel() / D : 0;
+    const bool fusable = xv.dtype() == DType::BF16 && wg.dtype() == DType::BF16 &&
+                         wd.dtype() == DType::BF16 && wg.rank() == 2 && wd.rank() == 2 &&
+                         wg.shape()[1] == D && wg.shape()[0] % 512 == 0 && wd.shape()[0] == D &&
+                         2 * wd.shape()[1] == wg.shape()[0] && rows >= 256 && D % 8 == 0 &&
+                         fused_mlp_enabled();
+    if (!fusable)
+    {
+        return linear(swiglu(linear(x, gate_up)), down);
+    }
+    const LinearSaved l1 = linear_setup(xv, x.node(), gate_up);
+    const size_t F = l1.out / 2;
+    Tensor gu = Tensor::empty(Shape({rows, 2 * F}), DType::BF16);
+    Tensor h = Tensor::empty(Shape({rows, F}), DType::BF16);
+    int rc = VEDA_OK;
+    {
+        profile::Scope scope("gemm_fwd", 4.0 * rows * D * F,
+                             2.0 * (static_cast<double>(rows) * D + 2.0 * F * D + 3.0 * rows * F));
+        rc = veda_gemm_swiglu_fwd(rows, F, D, l1.xs.data_ptr(), l1.ldx, l1.wc.data_ptr(), D,
+                                  gu.data_ptr(), 2 * F, h.data_ptr(), F, S());
+    }
+    if (rc == VEDA_ERR_UNSUPPORTED)
+    {
+        return linear(swiglu(linear(x, gate_up)), down);
+    }
+    check(rc, "mlp (gate|up projection and SwiGLU)");
+    LinearSaved l2 = linear_setup(h, nullptr, down);
+    Tensor value = linear_forward(l2, xv.shape());
+    return make({x, gate_up, down}, std::move(value), [l1, l2, gu, rows, F, D](const Tensor& g) {
+        // the down projection's backward: dW (+)= G^T h beside dgate|up = SwiGLU'(G W) (one GEMM
+        // whose epilogue applies SwiGLU's backward, so dh is never stored); then the gate|up
+        // projection's backward with dgate|up
+        const Tensor gc = as_dtype(g, DType::BF16);
+        Tensor dgu = Tensor::empty(Shape({rows, 2 * F}), DType::BF16);
+        const auto& win = l2.win;
+        {
+            profile::Scope scope("gemm_bwd", 4.0 * rows * D * F,
+                                 2.0 * (2.0 * static_cast<double>(rows) * D + 2.0 * D * F + 5.0 * rows * F) +
+                                     8.0 * static_cast<double>(D) * F);
+            const cudaStream_t main = reinterpret_cast<cudaStream_t>(S());
+            const bool side = win->requires_grad && gemm_overlap_enabled();
+            SideStream* ss = side ? &side_stream() : nullptr;
+            auto weight_grad = [&](cudaStream_t st) {
+                bool fresh = false;
+                Tensor& gw = grad_target(*win, &fresh, DType::F32);
+                check(veda_gemm_tn(D, F, rows, gc.data_ptr(), D, l2.xs.data_ptr(), F, gw.data_ptr(), F,
+                                   VEDA_BF16, dt(gw.dtype()), 1.0f, fresh ? 0.0f : 1.0f, st),
+                      "mlp backward (down projection weight)");
+            };
+            if (side)
+            {
+                cuda_check(cudaEventRecord(ss->fork, main), "gemm fork");
+                cuda_check(cudaStreamWaitEvent(ss->stream, ss->fork, 0), "gemm fork wait");
+                weight_grad(ss->stream);
+            }
+            int rc = veda_gemm_swiglu_bwd(rows, F, D, gc.data_ptr(), D, l2.wc.data_ptr(), F,
+                                          gu.data_ptr(), 2 * F, dgu.data_ptr(), 2 * F, S());
+            if (rc == VEDA_ERR_UNSUPPORTED)
+            {
+                Tensor dh = Tensor::empty(Shape({rows, F}), DType::BF16);
+                check(veda_gemm_nn(rows, F, D, gc.data_ptr(), D, l2.wc.data_ptr(), F, dh.data_ptr(), F,
+                                   VEDA_BF16, VEDA_BF16, 1.0f, 0.0f, S()),
+                      "mlp backward (down projection input)");
+                const char* base = static_cast<const char*>(gu.data_ptr());
+                char* db = static_cast<char*>(dgu.data_ptr());
+                rc = veda_swiglu_bwd(base, 2 * F, base + 2 * F, 2 * F, dh.data_ptr(), F, db, 2 * F,
+                                     db + 2 * F, 2 * F, rows, F, VEDA_BF16, S());
+            }
+            check(rc, "mlp backward (SwiGLU)");
+            if (side)
+            {
+                cuda_check(cudaEventRecord(ss->join, ss->stream), "gemm join");
+                cuda_check(cudaStreamWaitEvent(main, ss->join, 0), "gemm join wait");
+            }
+            else if (win->requires_grad)
+            {
+                weight_grad(main);
+            }
+        }
+        linear_backward(l1, dgu);
+    });
+}
+
 GradientCheck check_gradient(const std::function<Variable(const Variable&)>& loss_of,
                              const Tensor& at, float step, double tolerance)
 {

@@ -345,9 +345,8 @@ Variable TinyTransformer::forward_from(const Variable& x0, size_t B, size_t T)
                                                        T, H, Hk, Dh, eps),
                                    L.o);
         Variable b = autograd::add_rms_norm(x, proj, L.post_norm, eps, &x);
-        Variable h = autograd::swiglu(autograd::linear(b, L.gate_up));
         const Variable& next = l + 1 < layers_.size() ? layers_[l + 1].in_norm : final_norm_;
-        a = autograd::add_rms_norm(x, autograd::linear(h, L.down), next, eps, &x);
+        a = autograd::add_rms_norm(x, autograd::mlp(b, L.gate_up, L.down), next, eps, &x);
     }
     // tied LM head: the embedding matrix read the other way round (Model.cpp:253-254)
     return autograd::linear(a, embed_);

@@ -1,19 +1,14 @@
-// SwiGLU forward and backward — HBM-bound element-wise kernels.
-//   forward  h = silu(g) * u, silu(g) = g / (1 + exp(-g))       src/libs/ops/Activations.cpp:13-16,
-//                                                               src/libs/train/Model.cpp:201-202
-//   backward dg = (dh * u) * s * (1 + g (1 - s)), s = sigmoid(g) src/libs/autograd/NonLinear.cpp:47-63
-//            du = dh * silu(g)                                  src/libs/autograd/Variable.cpp:218-239
-// gate and up may be column slices of one [rows, 2F] buffer (the fused gate|up projection).
+// SwiGLU forward and backward — HBM-bound element-wise kernels (the math is in swiglu_math.cuh).
+// gate and up may be column slices of one [rows, 2F] buffer (the fused gate|up projection). The
+// training step runs neither: the gate|up projection's GEMM writes h as well, and the down
+// projection's input-gradient GEMM writes dg and du (gemm_sm100.cu, the same math).
 #include "common.cuh"
+#include "swiglu_math.cuh"
 
 namespace veda::cuda
 {
 namespace
 {
-
-// sigmoid(g) = 1 / (1 + e^-g) with the hardware exponential and reciprocal-divide: a few ulp,
-// far inside the fp32 tolerance, and exact at the ends (e^-g = inf gives 0, e^-g = 0 gives 1)
-__device__ __forceinline__ float sigmoid_of(float g) { return __fdividef(1.0f, 1.0f + __expf(-g)); }
 
 template <typename T, int V>
 __device__ __forceinline__ void load_vec(const T* p, float (&out)[V])
@@ -72,7 +67,7 @@ __global__ void swiglu_fwd_kernel(const T* __restrict__ gate, int64_t ldg, const
                 if (r0 + k < rows)
                 {
 #pragma unroll
-                    for (int j = 0; j < V; ++j) g[k][j] = g[k][j] * sigmoid_of(g[k][j]) * u[k][j];
+                    for (int j = 0; j < V; ++j) g[k][j] = swiglu_value(g[k][j], u[k][j]);
                     store_vec<T, V>(h + (r0 + k) * ldh + c, g[k]);
                 }
             }
@@ -115,13 +110,7 @@ __global__ void swiglu_bwd_kernel(const T* __restrict__ gate, int64_t ldg, const
                 {
                     float dg[V], du[V];
 #pragma unroll
-                    for (int j = 0; j < V; ++j)
-                    {
-                        const float sg = sigmoid_of(g[k][j]);
-                        const float through = d[k][j] * u[k][j];
-                        dg[j] = through * sg * (1.0f + g[k][j] * (1.0f - sg));
-                        du[j] = d[k][j] * (g[k][j] * sg);
-                    }
+                    for (int j = 0; j < V; ++j) swiglu_grads(g[k][j], u[k][j], d[k][j], dg[j], du[j]);
                     store_vec<T, V>(dgate + (r0 + k) * lddg + c, dg);
                     store_vec<T, V>(dup + (r0 + k) * lddu + c, du);
                 }
