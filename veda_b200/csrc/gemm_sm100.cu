@@ -593,84 +593,108 @@ __device__ __forceinline__ void epilogue_swiglu(const Params& p, const CUtensorM
     }
 }
 
-// A warp's 32 rows x 64 bf16 of `src` (row stride ld): eight 16-byte loads a lane, each
-// instruction reading four whole 128-byte rows; rows at or past M read as zero.
-__device__ __forceinline__ void fetch_rows(const bf16* src, int64_t ld, int row0, int M, int lane,
-                                           uint4 (&v)[8])
+// EPI 2 staging: per warp four 2 KB tiles of 32 rows x 64 bytes (32 bf16) with the 64-byte swizzle
+// (row r's 16-byte segment s at s ^ ((r >> 1) & 3)), gate and up of two 32-column chunks, so one
+// chunk's gate and up load while the other's are computed; dg and du overwrite them in place.
+constexpr int kChunkTile = 32 * 64;
+
+__device__ __forceinline__ uint32_t swz64(int r, int s)
 {
-    const int seg = lane & 7;
+    return static_cast<uint32_t>(r * 64 + ((s ^ ((r >> 1) & 3)) << 4));
+}
+
+// Asynchronous copy of a warp's 32 rows x 32 bf16 of `src` (row stride ld) into a staging tile:
+// four 16-byte copies a lane, each instruction eight whole 64-byte rows; rows at or past M are
+// filled with zeros.
+__device__ __forceinline__ void copy_chunk_async(uint8_t* tile, const bf16* src, int64_t ld, int row0,
+                                                 int M, int lane)
+{
+    const int seg = lane & 3;
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
+    for (int k = 0; k < 4; ++k)
     {
-        const int r = row0 + 4 * k + (lane >> 3);
-        v[k] = r < M ? __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(r) * ld) + seg)
-                     : make_uint4(0u, 0u, 0u, 0u);
+        const int r = 8 * k + (lane >> 2);
+        const bool in = row0 + r < M;
+        const int row = in ? row0 + r : M - 1;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(tile + swz64(r, seg))),
+                     "l"(src + static_cast<int64_t>(row) * ld + seg * 8), "r"(in ? 16u : 0u)
+                     : "memory");
     }
 }
 
-// The fetched rows into a 128-byte-swizzled staging tile (row r's segment s at s ^ (r & 7)).
-__device__ __forceinline__ void stash_rows(uint8_t* buf, int lane, const uint4 (&v)[8])
+// Gate and up of chunk j (columns col0 + 32 j) into the warp's tile pair j & 1, as one group.
+__device__ __forceinline__ void dswiglu_load(const Params& p, int row0, int col0, int j, uint8_t* staging,
+                                             int lane)
 {
-    const int seg = lane & 7;
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-    {
-        const int r = 4 * k + (lane >> 3);
-        *reinterpret_cast<uint4*>(buf + r * 128 + ((seg ^ (r & 7)) << 4)) = v[k];
-    }
+    uint8_t* const pair = staging + (j & 1) * 2 * kChunkTile;
+    copy_chunk_async(pair, p.gu + col0 + 32 * j, p.ldgu, row0, p.M, lane);
+    copy_chunk_async(pair + kChunkTile, p.gu + p.F + col0 + 32 * j, p.ldgu, row0, p.M, lane);
+    asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// EPI 2, one warp's 32 rows: the accumulator is dh for columns col0..col0+255 of the [M, F]
-// intermediate; dh rounded to bf16 (as the stand-alone path stores it) with gate and up of the
-// same rows and columns (p.gu) gives dg and du, written into C, the [M, 2F] gradient of gate|up,
-// at col0 and F + col0. pg / pu hold gate and up of the first 64 columns on entry.
+// EPI 2, before the unit's accumulator is ready: once the last unit's stores have read the
+// staging tiles, chunks 0 and 1 start loading.
+__device__ __forceinline__ void dswiglu_start(const Params& p, int row0, int col0, uint8_t* staging,
+                                              uint32_t nstore, int lane)
+{
+    if (row0 >= p.M)
+    {
+        return;
+    }
+    if (nstore > 0)
+    {
+        if (lane == 0)
+        {
+            bulk_wait_group_read<0>();
+        }
+        __syncwarp();
+    }
+    dswiglu_load(p, row0, col0, 0, staging, lane);
+    dswiglu_load(p, row0, col0, 1, staging, lane);
+}
+
+// EPI 2, one warp's 32 rows x 128 columns (col0..) of the [M, F] intermediate, whose dh the
+// accumulator at taddr holds, in four chunks of 32 columns: dh rounded to bf16 (as the stand-alone
+// path stores it) with gate and up of the same rows and columns (p.gu) gives dg and du, written
+// into C, the [M, 2F] gradient of gate|up, at col0 and F + col0 (C's map: 32 x 32 boxes, 64-byte
+// swizzle). Chunk j + 2 loads into the tiles of chunk j once chunk j's stores have read them.
 __device__ __forceinline__ void epilogue_dswiglu(const Params& p, const CUtensorMap* mc, uint32_t taddr,
                                                  int row0, int col0, uint8_t* staging,
-                                                 uint32_t& nstore, int lane, uint4 (&pg)[8],
-                                                 uint4 (&pu)[8])
+                                                 uint32_t& nstore, int lane)
 {
-    uint8_t* const bg = staging;
-    uint8_t* const bu = staging + kStageTile;
-    const bool rows_in = row0 < p.M;
-#pragma unroll 1
-    for (int c = 0; c < 256; c += 64)
+    if (row0 >= p.M)
     {
-        if (nstore > 0)
+        return;
+    }
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j)
+    {
+        if (j < 3)
         {
-            if (lane == 0)
-            {
-                bulk_wait_group_read<0>();   // the last chunk's stores have read both buffers
-            }
-            __syncwarp();
+            asm volatile("cp.async.wait_group 1;" ::: "memory");   // chunk j's group is complete
         }
-        stash_rows(bg, lane, pg);
-        stash_rows(bu, lane, pu);
-        __syncwarp();
-        if (c + 64 < 256 && rows_in)
+        else
         {
-            // the next chunk's gate and up load while this one is computed
-            fetch_rows(p.gu + col0 + c + 64, p.ldgu, row0, p.M, lane, pg);
-            fetch_rows(p.gu + p.F + col0 + c + 64, p.ldgu, row0, p.M, lane, pu);
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
-        uint32_t d0[32], d1[32];
-        tmem_ld32(taddr + static_cast<uint32_t>(c), d0);
-        tmem_ld32(taddr + static_cast<uint32_t>(c + 32), d1);
-        uint8_t* const rg = bg + lane * 128;
-        uint8_t* const ru = bu + lane * 128;
+        __syncwarp();   // every lane's copies (other lanes' rows) are visible to the warp
+        uint8_t* const tg = staging + (j & 1) * 2 * kChunkTile;
+        uint8_t* const tu = tg + kChunkTile;
+        uint32_t d[32];
+        tmem_ld32(taddr + static_cast<uint32_t>(32 * j), d);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
+        for (int k = 0; k < 4; ++k)
         {
-            uint4* const gk = reinterpret_cast<uint4*>(rg + ((k ^ (lane & 7)) << 4));
-            uint4* const uk = reinterpret_cast<uint4*>(ru + ((k ^ (lane & 7)) << 4));
+            uint4* const gk = reinterpret_cast<uint4*>(tg + swz64(lane, k));
+            uint4* const uk = reinterpret_cast<uint4*>(tu + swz64(lane, k));
             const uint4 gv = *gk, uv = *uk;
             const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
             const uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
-            const uint32_t* dsrc = k < 4 ? &d0[8 * k] : &d1[8 * (k - 4)];
             uint32_t og[4], ou[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q)
             {
-                const uint32_t d2 = pack_bf16(__uint_as_float(dsrc[2 * q]), __uint_as_float(dsrc[2 * q + 1]));
+                const uint32_t d2 = pack_bf16(__uint_as_float(d[8 * k + 2 * q]), __uint_as_float(d[8 * k + 2 * q + 1]));
                 float dg0, du0, dg1, du1;
                 swiglu_grads(bf16_lo(gw[q]), bf16_lo(uw[q]), bf16_lo(d2), dg0, du0);
                 swiglu_grads(bf16_hi(gw[q]), bf16_hi(uw[q]), bf16_hi(d2), dg1, du1);
@@ -682,24 +706,40 @@ __device__ __forceinline__ void epilogue_dswiglu(const Params& p, const CUtensor
         }
         fence_proxy_async();
         __syncwarp();
-        if (lane == 0 && rows_in)
+        if (lane == 0)
         {
-            tma_store_2d(mc, bg, col0 + c, row0);
-            tma_store_2d(mc, bu, p.F + col0 + c, row0);
+            tma_store_2d(mc, tg, col0 + 32 * j, row0);
+            tma_store_2d(mc, tu, p.F + col0 + 32 * j, row0);
             bulk_commit_group();
         }
         ++nstore;
+        if (j + 2 < 4)
+        {
+            if (lane == 0)
+            {
+                bulk_wait_group_read<0>();   // the stores just issued have read the pair
+            }
+            __syncwarp();
+            dswiglu_load(p, row0, col0, j + 2, staging, lane);
+        }
     }
 }
 
+// The paired kernel's shape per epilogue: EPI 2 (SwiGLU's backward, the heaviest epilogue) runs
+// eight epilogue warps, two per scheduler, each on half of the tile's columns, and one pipeline
+// stage less to stage their tiles; the others run four (eight measured slower for EPI 1).
+template <int EPI>
 struct Cfg2
 {
-    static constexpr int STAGES = 6;
+    static constexpr int EPI_WARPS = EPI == 2 ? 8 : 4;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int STAGES = EPI == 2 ? 5 : 6;
     static constexpr int A_BYTES = 128 * BK * 2;   // this CTA's 128 rows of A
     static constexpr int B_BYTES = 128 * BK * 2;   // this CTA's 128 columns of B
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 512;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + kOutStaging + 1024 + 256;
+    static constexpr int STAGING = EPI_WARPS * 2 * kStageTile;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 + 256;
 };
 
 __device__ __forceinline__ uint32_t cluster_rank()
@@ -754,19 +794,19 @@ __device__ __forceinline__ void commit_pair(uint64_t* bar)
 }
 
 template <bool A_MN, bool B_MN, int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg2<EPI>::THREADS, 1)
 tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                 const __grid_constant__ CUtensorMap tma_c, const __grid_constant__ CUtensorMap tma_h,
                 const Params p)
 {
-    using C_ = Cfg2;
+    using C_ = Cfg2<EPI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* sa = smem;
     uint8_t* sb = smem + C_::STAGES * C_::A_BYTES;
     uint8_t* staging = sb + C_::STAGES * C_::B_BYTES;   // epilogue staging tiles
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + kOutStaging);
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + C_::STAGING);
     uint64_t* empty = full + C_::STAGES;
     uint64_t* tfull = empty + C_::STAGES;
     uint64_t* tempty = tfull + 2;
@@ -790,7 +830,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
         for (int b = 0; b < 2; ++b)
         {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 8);   // 4 epilogue warps in each CTA
+            mbar_init(&tempty[b], 2 * C_::EPI_WARPS);   // the epilogue warps of both CTAs
         }
         mbar_fence_init();
     }
@@ -915,6 +955,8 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
     else if (warp >= 2)
     {
         const int quarter = warp & 3;
+        // EPI 2: warps 2-5 take the tile's columns 0-127, warps 6-9 columns 128-255
+        const int chalf = (warp - 2) >> 2;
         const uint32_t release = peer_addr(&tempty[0], 0);   // the even CTA's tempty[0]
         uint8_t* const wstage = staging + (warp - 2) * 2 * kStageTile;
         uint32_t nstore = 0;
@@ -926,15 +968,10 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
             const int buf = it & 1;
             const uint32_t tphase = (it >> 1) & 1;
             const int row = mb * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
-            [[maybe_unused]] uint4 pg[8], pu[8];
             if constexpr (EPI == 2)
             {
-                // gate and up of the first 64 columns: their loads run while the products finish
-                if (row - lane < p.M)
-                {
-                    fetch_rows(p.gu + nb * 256, p.ldgu, row - lane, p.M, lane, pg);
-                    fetch_rows(p.gu + p.F + nb * 256, p.ldgu, row - lane, p.M, lane, pu);
-                }
+                // gate and up of the first two chunks load while the products finish
+                dswiglu_start(p, row - lane, nb * 256 + chalf * 128, wstage, nstore, lane);
             }
             mbar_wait(&tfull[buf], tphase, p.status, abort);
             fence_after();
@@ -946,7 +983,8 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant
             }
             else if constexpr (EPI == 2)
             {
-                epilogue_dswiglu(p, &tma_c, base, row - lane, nb * 256, wstage, nstore, lane, pg, pu);
+                epilogue_dswiglu(p, &tma_c, base + static_cast<uint32_t>(chalf * 128), row - lane,
+                                 nb * 256 + chalf * 128, wstage, nstore, lane);
             }
             else if (p.out_mode != 0)
             {
@@ -1049,8 +1087,8 @@ int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
                int clusters, cudaStream_t s, const CUtensorMap* mh = nullptr)
 {
     auto kernel = tc_gemm2_kernel<A_MN, B_MN, EPI>;
-    return launch("veda_gemm (tcgen05, CTA pair)", kernel, dim3(2 * clusters), dim3(kThreads),
-                  Cfg2::SMEM, s, ma, mb, mc, mh != nullptr ? *mh : mc, p);
+    return launch("veda_gemm (tcgen05, CTA pair)", kernel, dim3(2 * clusters), dim3(Cfg2<EPI>::THREADS),
+                  Cfg2<EPI>::SMEM, s, ma, mb, mc, mh != nullptr ? *mh : mc, p);
 }
 
 // How many two-CTA clusters of the paired kernel fit on the device at once (0: none).
@@ -1064,13 +1102,13 @@ int pair_clusters()
     {
         auto kernel = tc_gemm2_kernel<A_MN, B_MN, EPI>;
         cached = 0;
-        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2::SMEM) ==
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2<EPI>::SMEM) ==
             cudaSuccess)
         {
             cudaLaunchConfig_t cfg{};
             cfg.gridDim = dim3(2 * (sm_count() / 2));
-            cfg.blockDim = dim3(kThreads);
-            cfg.dynamicSmemBytes = Cfg2::SMEM;
+            cfg.blockDim = dim3(Cfg2<EPI>::THREADS);
+            cfg.dynamicSmemBytes = Cfg2<EPI>::SMEM;
             cudaLaunchAttribute attr{};
             attr.id = cudaLaunchAttributeClusterDimension;
             attr.val.clusterDim.x = 2;
@@ -1240,8 +1278,10 @@ int tc_gemm_pair(int op, int64_t M, int64_t N, int64_t K, const void* A, int64_t
     return launch_tc2<true, true>(ma, mb, mc, p, clusters, s);
 }
 
-// bf16 store map of the epilogue: 64-column x 32-row boxes, 128-byte swizzle.
-bool make_store_map(CUtensorMap* map, void* base, int64_t inner, int64_t outer, int64_t ld)
+// bf16 store map of the epilogue: 64-column x 32-row boxes with the 128-byte swizzle, or (narrow)
+// 32-column boxes with the 64-byte swizzle.
+bool make_store_map(CUtensorMap* map, void* base, int64_t inner, int64_t outer, int64_t ld,
+                    bool narrow = false)
 {
     auto fn = encode_fn();
     if (fn == nullptr)
@@ -1250,10 +1290,11 @@ bool make_store_map(CUtensorMap* map, void* base, int64_t inner, int64_t outer, 
     }
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
-    const cuuint32_t box[2] = {64, 32};
+    const cuuint32_t box[2] = {narrow ? 32u : 64u, 32};
     const cuuint32_t estr[2] = {1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_INTERLEAVE_NONE,
+              narrow ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -1316,7 +1357,7 @@ int gemm_swiglu_bwd_tc(int64_t rows, int64_t F, int64_t D, const void* dy, int64
     const int clusters_max = std::min(pair_clusters<false, true, 2>(), compute_sms() / 2);
     CUtensorMap ma, mb, mc;
     if (clusters_max < 1 || !make_map(&ma, dy, D, rows, lddy, 64, 128) ||
-        !make_map(&mb, w, F, D, ldw, 64, 64) || !make_store_map(&mc, dgu, 2 * F, rows, lddgu))
+        !make_map(&mb, w, F, D, ldw, 64, 64) || !make_store_map(&mc, dgu, 2 * F, rows, lddgu, true))
     {
         return -1;
     }
