@@ -1673,7 +1673,8 @@ Variable mlp(const Variable& x, const Variable& gate_up, const Variable& down)
     Tensor h = Tensor::empty(Shape({rows, F}), DType::BF16);
     int rc = VEDA_OK;
     {
-        profile::Scope scope("gemm_fwd", 4.0 * rows * D * F,
+        // a class of its own: the GEMM with SwiGLU in its epilogue
+        profile::Scope scope("mlp_fwd", 4.0 * rows * D * F,
                              2.0 * (static_cast<double>(rows) * D + 2.0 * F * D + 3.0 * rows * F));
         rc = veda_gemm_swiglu_fwd(rows, F, D, l1.xs.data_ptr(), l1.ldx, l1.wc.data_ptr(), D,
                                   gu.data_ptr(), 2 * F, h.data_ptr(), F, S());
@@ -1693,7 +1694,7 @@ Variable mlp(const Variable& x, const Variable& gate_up, const Variable& down)
         Tensor dgu = Tensor::empty(Shape({rows, 2 * F}), DType::BF16);
         const auto& win = l2.win;
         {
-            profile::Scope scope("gemm_bwd", 4.0 * rows * D * F,
+            profile::Scope scope("mlp_bwd", 4.0 * rows * D * F,
                                  2.0 * (2.0 * static_cast<double>(rows) * D + 2.0 * D * F + 5.0 * rows * F) +
                                      8.0 * static_cast<double>(D) * F);
             const cudaStream_t main = reinterpret_cast<cudaStream_t>(S());

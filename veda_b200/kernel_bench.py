@@ -303,6 +303,85 @@ def one_gemm(op, M, N, K, reps, out=None):
           flush=True)
 
 
+def swiglu_gemms(rows, F, D, reps, profile=False):
+    """The MLP's GEMMs with SwiGLU in the epilogue (veda_gemm_swiglu_fwd / _bwd) against the GEMM
+    followed by the stand-alone SwiGLU kernel, each timed as a CUDA graph of `reps` launches
+    (median of 7 replays). With `profile`, two rounds of the fused forward and backward run once
+    each, untimed (for ncu: the second round is launches 2 and 3)."""
+    import torch
+    import veda_b200 as V
+    L = V.lib()
+    s = torch.cuda.Stream()
+    torch.cuda.set_stream(s)
+    st = s.cuda_stream
+    bf = torch.bfloat16
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn(rows, D, device="cuda", generator=g).to(bf)
+    wgu = (torch.randn(2 * F, D, device="cuda", generator=g) / math.sqrt(D)).to(bf)
+    wd = (torch.randn(D, F, device="cuda", generator=g) / math.sqrt(F)).to(bf)
+    dy = torch.randn(rows, D, device="cuda", generator=g).to(bf)
+    gu = torch.empty(rows, 2 * F, device="cuda", dtype=bf)
+    h = torch.empty(rows, F, device="cuda", dtype=bf)
+    dh = torch.empty(rows, F, device="cuda", dtype=bf)
+    dgu = torch.empty(rows, 2 * F, device="cuda", dtype=bf)
+    es = 2
+
+    def fwd_fused():
+        V.check(L.veda_gemm_swiglu_fwd(rows, F, D, x.data_ptr(), D, wgu.data_ptr(), D, gu.data_ptr(),
+                                       2 * F, h.data_ptr(), F, st))
+
+    def bwd_fused():
+        V.check(L.veda_gemm_swiglu_bwd(rows, F, D, dy.data_ptr(), D, wd.data_ptr(), F, gu.data_ptr(),
+                                       2 * F, dgu.data_ptr(), 2 * F, st))
+
+    def fwd_two():
+        V.check(L.veda_gemm_nt(rows, 2 * F, D, x.data_ptr(), D, wgu.data_ptr(), D, gu.data_ptr(),
+                               2 * F, V.BF16, V.BF16, 1.0, 0.0, st))
+        V.check(L.veda_swiglu_fwd(gu.data_ptr(), 2 * F, gu.data_ptr() + F * es, 2 * F, h.data_ptr(), F,
+                                  rows, F, V.BF16, st))
+
+    def bwd_two():
+        V.check(L.veda_gemm_nn(rows, F, D, dy.data_ptr(), D, wd.data_ptr(), F, dh.data_ptr(), F,
+                               V.BF16, V.BF16, 1.0, 0.0, st))
+        V.check(L.veda_swiglu_bwd(gu.data_ptr(), 2 * F, gu.data_ptr() + F * es, 2 * F, dh.data_ptr(),
+                                  F, dgu.data_ptr(), 2 * F, dgu.data_ptr() + F * es, 2 * F, rows, F,
+                                  V.BF16, st))
+
+    if profile:
+        for _ in range(2):
+            fwd_fused()
+            bwd_fused()
+        torch.cuda.synchronize()
+        return
+
+    def graph_us(fn):
+        fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(7):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            graph.replay()
+            b.record(s)
+            b.synchronize()
+            ts.append(a.elapsed_time(b) / reps * 1e3)
+        del graph
+        return sorted(ts)[3]
+
+    out = {"bench": "swiglu-gemms", "rows": rows, "F": F, "D": D,
+           "fwd_fused_us": graph_us(fwd_fused), "fwd_gemm_then_swiglu_us": graph_us(fwd_two),
+           "bwd_fused_us": graph_us(bwd_fused), "bwd_gemm_then_swiglu_us": graph_us(bwd_two)}
+    out["fwd_fused_tflops"] = 4.0 * rows * F * D / out["fwd_fused_us"] / 1e6
+    out["bwd_fused_tflops"] = 2.0 * rows * F * D / out["bwd_fused_us"] / 1e6
+    print(json.dumps(out), flush=True)
+
+
 def decode(prompt_len, new_tokens):
     """Greedy generation with the KV cache on the Qwen3-0.6B-shaped model (random weights, batch 1):
     decode tokens/s after the prefill, against the HBM roofline of one step (every weight read
@@ -384,12 +463,21 @@ def main():
     d.add_argument("--tokens", type=int, default=8192)
     d.add_argument("--reps", type=int, default=20)
     d.add_argument("--kernels", nargs="+", default=None)
+    f = sub.add_parser("swiglu")
+    f.add_argument("--rows", type=int, default=8192)
+    f.add_argument("--f", type=int, default=3072)
+    f.add_argument("--d", type=int, default=1024)
+    f.add_argument("--reps", type=int, default=8)
+    f.add_argument("--profile", action="store_true")
     e = sub.add_parser("decode")
     e.add_argument("--prompt", type=int, default=128)
     e.add_argument("--new-tokens", type=int, default=64)
     args = ap.parse_args()
     if args.cmd == "decode":
         decode(args.prompt, args.new_tokens)
+        return
+    if args.cmd == "swiglu":
+        swiglu_gemms(args.rows, args.f, args.d, args.reps, args.profile)
         return
     if args.cmd == "mm-sweep":
         mm_sweep(args.reps)
