@@ -695,9 +695,12 @@ __device__ __forceinline__ void epilogue_dswiglu(const Params& p, const CUtensor
             for (int q = 0; q < 4; ++q)
             {
                 const uint32_t d2 = pack_bf16(__uint_as_float(d[8 * k + 2 * q]), __uint_as_float(d[8 * k + 2 * q + 1]));
-                float dg0, du0, dg1, du1;
-                swiglu_grads(bf16_lo(gw[q]), bf16_lo(uw[q]), bf16_lo(d2), dg0, du0);
-                swiglu_grads(bf16_hi(gw[q]), bf16_hi(uw[q]), bf16_hi(d2), dg1, du1);
+                uint64_t dg2, du2;
+                swiglu_grads2(pk(bf16_lo(gw[q]), bf16_hi(gw[q])), pk(bf16_lo(uw[q]), bf16_hi(uw[q])),
+                              pk(bf16_lo(d2), bf16_hi(d2)), dg2, du2);
+                float dg0, dg1, du0, du1;
+                upk(dg2, dg0, dg1);
+                upk(du2, du0, du1);
                 og[q] = pack_bf16(dg0, dg1);
                 ou[q] = pack_bf16(du0, du1);
             }
