@@ -35,7 +35,7 @@ enum veda_status {
     VEDA_ERR_INVALID_ARGUMENT = -1, /* reference: std::invalid_argument */
     VEDA_ERR_CUDA = -2,             /* a CUDA launch or runtime failure   */
     VEDA_ERR_TIMEOUT = -3,          /* a bounded device wait gave up      */
-    VEDA_ERR_UNSUPPORTED = -4,      /* shape/alignment this build does not handle */
+    VEDA_ERR_UNSUPPORTED = -4,      /* shape/alignment the library does not handle */
     VEDA_ERR_OUT_OF_RANGE = -5      /* reference: std::out_of_range (ids) */
 };
 
